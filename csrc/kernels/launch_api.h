@@ -1,0 +1,61 @@
+// Raw-pointer launchers of the sm_100a kernels.  Compiled by nvcc without any
+// torch header; the torch-facing wrappers (shape checks, allocation) are in
+// the g++-compiled torch_ops.cpp.  Every launcher returns the launch status.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace mmltk {
+
+enum class DType : int { kF32 = 0, kBF16 = 1 };
+
+int num_sms();
+
+// ---------------------------------------------------------------- LayerNorm
+cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
+                                 float* rstd, int64_t rows, int C, float eps, cudaStream_t st);
+// part: fp32 scratch [2, nparts, C]; nparts from layernorm_bwd_parts(rows)
+int layernorm_bwd_parts(int64_t rows);
+cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
+                                 const float* rstd, void* gx, void* gw, void* gb, float* part, int64_t rows, int C,
+                                 cudaStream_t st);
+
+// ---------------------------------------------------------------- MSDeformAttn
+struct MsdaDims {
+    int B, S, Lq, H, L, P, D;
+};
+cudaError_t launch_msda_fwd(DType t, const void* value, const int* shapes, const int* starts, const void* ref,
+                            const void* off, const void* logits, void* out, MsdaDims d, cudaStream_t st);
+// gvalue_acc: fp32 [B*S*H*D], gref_acc: fp32 [B*Lq*L*4]; both zeroed by the launcher.
+cudaError_t launch_msda_bwd(DType t, const void* gout, const void* value, const int* shapes, const int* starts,
+                            const void* ref, const void* off, const void* logits, float* gvalue_acc, float* gref_acc,
+                            void* gvalue, void* gref, void* goff, void* glogits, MsdaDims d, cudaStream_t st);
+
+// ---------------------------------------------------------------- matcher
+constexpr int kMatcherMaxLayers = 8;
+struct MatcherLayers {
+    const void* logits[kMatcherMaxLayers];
+    const void* boxes[kMatcherMaxLayers];
+};
+cudaError_t launch_matcher_cost(DType lt, DType bt, MatcherLayers lp, int NL, const int64_t* labels,
+                                const float* tboxes, const int32_t* counts, float* cost, int B, int Q, int C, int T,
+                                float w_class, float w_bbox, float w_giou, float alpha, cudaStream_t st);
+size_t lsap_shared_bytes(int Qg, int T, int warps_per_block);
+int lsap_warps_per_block(int Qg, int T);
+cudaError_t launch_lsap(const float* cost, const int32_t* counts, int32_t* match, int NL, int B, int G, int Qg, int T,
+                        int* status, cudaStream_t st);
+
+// ---------------------------------------------------------------- elementwise
+cudaError_t launch_cast_f32(DType dst_t, const float* src, void* dst, int64_t n, cudaStream_t st);
+
+// ---------------------------------------------------------------- losses
+int dense_neg_blocks(int64_t n);
+// partials: fp32 [dense_neg_blocks(n)], counter: zeroed uint32 (reset by the kernel), out: fp32 [1]
+cudaError_t launch_dense_neg_fwd(DType t, const void* x, int64_t n, float coef, float* partials,
+                                 unsigned int* counter, float* out, cudaStream_t st);
+cudaError_t launch_dense_neg_bwd(DType t, const void* x, const float* g, int64_t n, float coef, void* dx,
+                                 cudaStream_t st);
+
+}  // namespace mmltk

@@ -1,0 +1,237 @@
+// LayerNorm over the last dimension, one warp per row.
+//
+// Forward: y = (x - mean) * rstd * w + b, statistics in fp32 (two passes over
+// registers, no E[x^2]-E[x]^2 cancellation).  Saves mean/rstd for backward.
+// Backward: dx per row; dgamma/dbeta accumulated per lane over the rows its
+// warp visits (each lane owns fixed columns), reduced across the CTA's warps
+// in shared memory into one fp32 partial per CTA, then summed by a second
+// kernel -- no atomics, deterministic.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace mmltk {
+
+namespace {
+
+template <typename T, typename W, int kMaxVec>
+__global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, const W* __restrict__ w,
+                                                     const W* __restrict__ b, T* __restrict__ y,
+                                                     float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                     int64_t rows, int C, float eps) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int nv = C >> 2;
+    for (int64_t r = warp; r < rows; r += nwarps) {
+        const T* xr = x + r * C;
+        float4 v[kMaxVec];
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < kMaxVec; ++k) {
+            const int i = lane + 32 * k;
+            if (i < nv) {
+                v[k] = load4(xr + 4 * i);
+                s += v[k].x + v[k].y + v[k].z + v[k].w;
+            }
+        }
+        const float mean = warp_sum(s) / C;
+        float q = 0.f;
+#pragma unroll
+        for (int k = 0; k < kMaxVec; ++k) {
+            const int i = lane + 32 * k;
+            if (i < nv) {
+                const float a = v[k].x - mean, bb = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
+                q += a * a + bb * bb + c * c + d * d;
+            }
+        }
+        const float rstd = rsqrtf(warp_sum(q) / C + eps);
+        T* yr = y + r * C;
+#pragma unroll
+        for (int k = 0; k < kMaxVec; ++k) {
+            const int i = lane + 32 * k;
+            if (i < nv) {
+                const int c0 = 4 * i;
+                float4 o;
+                o.x = (v[k].x - mean) * rstd * to_f(w[c0]) + to_f(b[c0]);
+                o.y = (v[k].y - mean) * rstd * to_f(w[c0 + 1]) + to_f(b[c0 + 1]);
+                o.z = (v[k].z - mean) * rstd * to_f(w[c0 + 2]) + to_f(b[c0 + 2]);
+                o.w = (v[k].w - mean) * rstd * to_f(w[c0 + 3]) + to_f(b[c0 + 3]);
+                store4(yr + c0, o);
+            }
+        }
+        if (lane == 0) {
+            mean_out[r] = mean;
+            rstd_out[r] = rstd;
+        }
+    }
+}
+
+template <typename T, typename W, int kMaxVec>
+__global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, const T* __restrict__ x,
+                                                     const W* __restrict__ w, const float* __restrict__ mean_in,
+                                                     const float* __restrict__ rstd_in, T* __restrict__ gx,
+                                                     float* __restrict__ part_w, float* __restrict__ part_b,
+                                                     int64_t rows, int C) {
+    extern __shared__ float smem[];  // [warps][2][C]
+    const int lane = threadIdx.x & 31;
+    const int wib = threadIdx.x >> 5;
+    const int nwib = blockDim.x >> 5;
+    const int64_t warp = static_cast<int64_t>(blockIdx.x) * nwib + wib;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * nwib;
+    const int nv = C >> 2;
+    float4 aw[kMaxVec], ab[kMaxVec];
+#pragma unroll
+    for (int k = 0; k < kMaxVec; ++k) {
+        aw[k] = make_float4(0, 0, 0, 0);
+        ab[k] = make_float4(0, 0, 0, 0);
+    }
+    for (int64_t r = warp; r < rows; r += nwarps) {
+        const float mean = mean_in[r], rstd = rstd_in[r];
+        float4 xh[kMaxVec], g[kMaxVec];
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int k = 0; k < kMaxVec; ++k) {
+            const int i = lane + 32 * k;
+            if (i < nv) {
+                const int c0 = 4 * i;
+                float4 xv = load4(x + r * C + c0);
+                float4 gv = load4(gy + r * C + c0);
+                xh[k] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd,
+                                    (xv.w - mean) * rstd);
+                aw[k].x += gv.x * xh[k].x; aw[k].y += gv.y * xh[k].y;
+                aw[k].z += gv.z * xh[k].z; aw[k].w += gv.w * xh[k].w;
+                ab[k].x += gv.x; ab[k].y += gv.y; ab[k].z += gv.z; ab[k].w += gv.w;
+                g[k] = make_float4(gv.x * to_f(w[c0]), gv.y * to_f(w[c0 + 1]), gv.z * to_f(w[c0 + 2]),
+                                   gv.w * to_f(w[c0 + 3]));
+                s1 += g[k].x + g[k].y + g[k].z + g[k].w;
+                s2 += g[k].x * xh[k].x + g[k].y * xh[k].y + g[k].z * xh[k].z + g[k].w * xh[k].w;
+            }
+        }
+        s1 = warp_sum(s1) / C;
+        s2 = warp_sum(s2) / C;
+#pragma unroll
+        for (int k = 0; k < kMaxVec; ++k) {
+            const int i = lane + 32 * k;
+            if (i < nv) {
+                float4 o;
+                o.x = (g[k].x - s1 - xh[k].x * s2) * rstd;
+                o.y = (g[k].y - s1 - xh[k].y * s2) * rstd;
+                o.z = (g[k].z - s1 - xh[k].z * s2) * rstd;
+                o.w = (g[k].w - s1 - xh[k].w * s2) * rstd;
+                store4(gx + r * C + 4 * i, o);
+            }
+        }
+    }
+    // CTA reduction of the per-lane column partials
+    float* sw = smem + wib * 2 * C;
+    float* sb = sw + C;
+#pragma unroll
+    for (int k = 0; k < kMaxVec; ++k) {
+        const int i = lane + 32 * k;
+        if (i < nv) {
+            store4(sw + 4 * i, aw[k]);
+            store4(sb + 4 * i, ab[k]);
+        }
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float a = 0.f, bb = 0.f;
+        for (int q = 0; q < nwib; ++q) {
+            a += smem[q * 2 * C + c];
+            bb += smem[q * 2 * C + C + c];
+        }
+        part_w[static_cast<int64_t>(blockIdx.x) * C + c] = a;
+        part_b[static_cast<int64_t>(blockIdx.x) * C + c] = bb;
+    }
+}
+
+template <typename W>
+__global__ void colsum_partials_kernel(const float* __restrict__ pw, const float* __restrict__ pb, int nparts, int C,
+                                       W* __restrict__ gw, W* __restrict__ gb) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    float a = 0.f, b = 0.f;
+    for (int p = 0; p < nparts; ++p) {
+        a += pw[static_cast<int64_t>(p) * C + c];
+        b += pb[static_cast<int64_t>(p) * C + c];
+    }
+    gw[c] = from_f<W>(a);
+    gb[c] = from_f<W>(b);
+}
+
+template <typename F>
+void dispatch_vec(int C, F&& f) {
+    const int nvl = (C / 4 + 31) / 32;
+    switch (nvl) {
+        case 1: return f(std::integral_constant<int, 1>{});
+        case 2: return f(std::integral_constant<int, 2>{});
+        case 3: return f(std::integral_constant<int, 3>{});
+        case 4: return f(std::integral_constant<int, 4>{});
+        case 5: case 6: return f(std::integral_constant<int, 6>{});
+        case 7: case 8: return f(std::integral_constant<int, 8>{});
+        default: return f(std::integral_constant<int, 12>{});
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
+                                 float* rstd, int64_t rows, int C, float eps, cudaStream_t st) {
+    if (rows == 0) return cudaSuccess;
+    if (C % 4 != 0 || C > 4 * 32 * 12) return cudaErrorInvalidValue;
+    const int threads = 256;
+    const int64_t blocks = std::min<int64_t>((rows + 7) / 8, static_cast<int64_t>(num_sms()) * 16);
+    return MMLTK_DISPATCH_DT(xt, [&] {
+        using T = scalar_t;
+        return MMLTK_DISPATCH_DT(wt, [&] {
+            using Wt = scalar_t;
+            dispatch_vec(C, [&](auto nvl) {
+                ln_fwd_kernel<T, Wt, decltype(nvl)::value><<<blocks, threads, 0, st>>>(
+                    static_cast<const T*>(x), static_cast<const Wt*>(w), static_cast<const Wt*>(b),
+                    static_cast<T*>(y), mean, rstd, rows, C, eps);
+            });
+            return cudaGetLastError();
+        });
+    });
+}
+
+int layernorm_bwd_parts(int64_t rows) {
+    const int nwib = 8;
+    int64_t blocks = std::min<int64_t>((rows + nwib - 1) / nwib, static_cast<int64_t>(num_sms()) * 2);
+    return static_cast<int>(std::max<int64_t>(blocks, 1));
+}
+
+cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
+                                 const float* rstd, void* gx, void* gw, void* gb, float* part, int64_t rows, int C,
+                                 cudaStream_t st) {
+    if (C % 4 != 0 || C > 4 * 32 * 12) return cudaErrorInvalidValue;
+    const int threads = 256;
+    const int nwib = threads / 32;
+    const int blocks = layernorm_bwd_parts(rows);
+    const size_t smem = static_cast<size_t>(nwib) * 2 * C * sizeof(float);
+    return MMLTK_DISPATCH_DT(xt, [&] {
+        using T = scalar_t;
+        return MMLTK_DISPATCH_DT(wt, [&] {
+            using Wt = scalar_t;
+            cudaError_t e = cudaSuccess;
+            dispatch_vec(C, [&](auto nvl) {
+                auto kern = ln_bwd_kernel<T, Wt, decltype(nvl)::value>;
+                if (smem > 48 * 1024)
+                    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+                if (e != cudaSuccess) return;
+                kern<<<blocks, threads, smem, st>>>(static_cast<const T*>(gy), static_cast<const T*>(x),
+                                                    static_cast<const Wt*>(w), mean, rstd, static_cast<T*>(gx), part,
+                                                    part + static_cast<int64_t>(blocks) * C, rows, C);
+            });
+            if (e != cudaSuccess) return e;
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+            colsum_partials_kernel<Wt><<<(C + 127) / 128, 128, 0, st>>>(
+                part, part + static_cast<int64_t>(blocks) * C, blocks, C, static_cast<Wt*>(gw), static_cast<Wt*>(gb));
+            return cudaGetLastError();
+        });
+    });
+}
+
+}  // namespace mmltk

@@ -1,0 +1,70 @@
+"""Hungarian matcher with Group-DETR groups.
+
+Reference: `compute_matcher_indices_for_layers` (`src/rfdetr/detection_ops.cpp:1167-1279`)
+- cost = set_cost_class * (a (1-p)^2 softplus(-x) - (1-a) p^2 softplus(x))[label]
+       + set_cost_bbox * L1(cxcywh) - set_cost_giou * GIoU, a = 0.25
+  (`detection_ops.cpp:967-1062`, kernel `src/rfdetr/cuda/detr_ops_cuda.cu:117-152`);
+- non-finite costs replaced by max finite + max |finite| + 1 (`detection_ops.cpp:412-459`);
+- one LSAP per (layer, image, group) over that group's queries
+  (`detection_ops.cpp:1138-1165`), indices offset by the group.
+
+Output: ``match [NL, B, G, T] int32`` -- for target slot t of image b the
+matched query index of group g in layer l (in [0, Q)), -1 if unmatched.
+
+CUDA: one cost kernel for all layers + the warp-per-problem LSAP kernel
+(nothing is copied to the host).  CPU: the same cost in torch ops + the C++
+solver on the worker pool.
+"""
+from __future__ import annotations
+
+from typing import List, Sequence
+
+import torch
+import torch.nn.functional as F
+
+from ..ops._ext import kernels, native
+from ..utils.boxes import cxcywh_to_xyxy, generalized_box_iou
+from .targets import Targets
+
+__all__ = ["matcher_cost_reference", "hungarian_match"]
+
+FOCAL_ALPHA = 0.25
+
+
+def matcher_cost_reference(logits: Sequence[torch.Tensor], boxes: Sequence[torch.Tensor], targets: Targets,
+                           w_class: float, w_bbox: float, w_giou: float) -> torch.Tensor:
+    """[NL, B, Q, T] fp32 cost with torch ops (CPU oracle)."""
+    out = []
+    T = targets.slots
+    for lg, bx in zip(logits, boxes):
+        x = lg.float()
+        B, Q, C = x.shape
+        lab = targets.labels.clamp(0, C - 1)                       # [B,T]
+        xs = torch.gather(x, 2, lab[:, None, :].expand(B, Q, T))   # [B,Q,T]
+        p = xs.sigmoid()
+        a = FOCAL_ALPHA
+        cls = a * (1 - p) ** 2 * F.softplus(-xs) - (1 - a) * p ** 2 * F.softplus(xs)
+        pb = bx.float()
+        l1 = (pb[:, :, None, :] - targets.boxes[:, None, :, :]).abs().sum(-1)
+        giou = torch.stack([generalized_box_iou(cxcywh_to_xyxy(pb[b]), cxcywh_to_xyxy(targets.boxes[b]))
+                            for b in range(B)])
+        c = w_class * cls + w_bbox * l1 - w_giou * giou
+        valid = targets.valid()[:, None, :]
+        out.append(torch.where(valid, c, torch.zeros_like(c)))
+    return torch.stack(out)
+
+
+def hungarian_match(logits: List[torch.Tensor], boxes: List[torch.Tensor], targets: Targets, groups: int,
+                    w_class: float = 2.0, w_bbox: float = 5.0, w_giou: float = 2.0) -> torch.Tensor:
+    with torch.no_grad():
+        dev = logits[0].device
+        Q = logits[0].shape[1]
+        if dev.type == "cuda" and targets.slots <= Q // groups:
+            k = kernels()
+            cost = k.matcher_cost([l.detach() for l in logits], [b.detach() for b in boxes], targets.labels,
+                                  targets.boxes, targets.counts, w_class, w_bbox, w_giou, FOCAL_ALPHA)
+            match, _status = k.lsap_batched(cost, targets.counts, groups)
+            return match
+        cost = matcher_cost_reference(logits, boxes, targets, w_class, w_bbox, w_giou)
+        m = native().match_batched(cost.cpu(), targets.counts.cpu().to(torch.int64), groups)
+        return m.to(dev)

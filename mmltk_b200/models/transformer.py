@@ -1,0 +1,401 @@
+"""Two-stage deformable transformer with Group-DETR queries.
+
+Reference: `NativeTransformerImpl` / `NativeDecoderImpl` / `NativeDecoderLayerImpl`
+/ `MSDeformAttnImpl` / `gen_encoder_output_proposals`
+(`src/rfdetr/layers/model.cpp:808-1363`).
+
+Numerics kept from the reference:
+* decoder layer: self-attn (nn.MultiheadAttention layout, 8 heads) on
+  ``q = k = tgt + query_pos, v = tgt``; in training the 13 Group-DETR groups are
+  attended independently; post-LN; MSDeformAttn; FFN (ReLU); post-LN;
+* lite refpoint refine: the reference points and the ``ref_point_head`` query
+  position are computed once from the initial refpoints;
+* two-stage proposals ``(x+0.5)/W, wh = 0.05 * 2**lvl``, validity (0.01, 0.99);
+  per-group ``enc_output`` Linear -> LN -> class Linear / bbox MLP with bbox
+  reparameterisation, top-k by max class logit.
+
+B200 design: the 13 per-group encoder heads are stacked parameters evaluated
+as batched GEMMs (one launch per head stage instead of 13); their checkpoint
+keys are still ``enc_output.<g>.weight`` etc. through state-dict hooks.  The
+proposal grid is computed once per feature shape and cached on the device.
+"""
+from __future__ import annotations
+
+import math
+from typing import List, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import ops
+from ..config import RfDetrConfig
+
+
+class Mlp(nn.Module):
+    """`RfDetrMlpImpl` (reference `src/rfdetr/layers/modules.cpp:61-83`): Linear+ReLU stack."""
+
+    def __init__(self, din: int, dh: int, dout: int, n: int):
+        super().__init__()
+        dims = [din] + [dh] * (n - 1)
+        outs = [dh] * (n - 1) + [dout]
+        self.layers = nn.ModuleList(nn.Linear(a, b) for a, b in zip(dims, outs))
+
+    def forward(self, x):
+        n = len(self.layers)
+        for i, l in enumerate(self.layers):
+            if i + 1 < n:
+                x = ops.linear(x, l.weight, l.bias, act="relu")
+            else:
+                x = ops.linear(x, l.weight, l.bias)
+        return x
+
+
+def gen_sineembed_for_position(pos: torch.Tensor, dim: int = 128) -> torch.Tensor:
+    """Sine embedding of (x, y[, w, h]) -> [..., 2*dim or 4*dim] (reference `model.cpp:234-261`)."""
+    scale = 2 * math.pi
+    dim_t = torch.arange(dim, dtype=torch.float32, device=pos.device)
+    dim_t = 10000.0 ** (2 * torch.div(dim_t, 2, rounding_mode="floor") / dim)
+
+    def enc(v):
+        x = v[..., None] * scale / dim_t
+        return torch.stack((x[..., 0::2].sin(), x[..., 1::2].cos()), -1).flatten(-2)
+
+    p = pos.float()
+    parts = [enc(p[..., 1]), enc(p[..., 0])]
+    if pos.shape[-1] == 4:
+        parts += [enc(p[..., 2]), enc(p[..., 3])]
+    return torch.cat(parts, -1)
+
+
+def reparam_boxes(delta: torch.Tensor, base: torch.Tensor) -> torch.Tensor:
+    """bbox reparameterisation: cxcy = d_xy * base_wh + base_xy, wh = exp(d_wh) * base_wh."""
+    cxcy = delta[..., :2] * base[..., 2:] + base[..., :2]
+    wh = delta[..., 2:].exp() * base[..., 2:]
+    return torch.cat([cxcy, wh], -1)
+
+
+class MSDeformAttn(nn.Module):
+    def __init__(self, d_model: int, n_levels: int, n_heads: int, n_points: int):
+        super().__init__()
+        self.d_model, self.n_levels, self.n_heads, self.n_points = d_model, n_levels, n_heads, n_points
+        self.sampling_offsets = nn.Linear(d_model, n_heads * n_levels * n_points * 2)
+        self.attention_weights = nn.Linear(d_model, n_heads * n_levels * n_points)
+        self.value_proj = nn.Linear(d_model, d_model)
+        self.output_proj = nn.Linear(d_model, d_model)
+        self.reset_parameters()
+
+    def reset_parameters(self):
+        """Grid init (reference `model.cpp:873-895`)."""
+        with torch.no_grad():
+            self.sampling_offsets.weight.zero_()
+            thetas = torch.arange(self.n_heads, dtype=torch.float32) * (2.0 * math.pi / self.n_heads)
+            grid = torch.stack([thetas.cos(), thetas.sin()], -1)
+            grid = (grid / grid.abs().max(-1, keepdim=True)[0]).view(self.n_heads, 1, 1, 2)
+            grid = grid.repeat(1, self.n_levels, self.n_points, 1)
+            for i in range(self.n_points):
+                grid[:, :, i, :] *= i + 1
+            self.sampling_offsets.bias.copy_(grid.view(-1))
+            self.attention_weights.weight.zero_()
+            self.attention_weights.bias.zero_()
+            nn.init.xavier_uniform_(self.value_proj.weight)
+            self.value_proj.bias.zero_()
+            nn.init.xavier_uniform_(self.output_proj.weight)
+            self.output_proj.bias.zero_()
+
+    def forward(self, query, ref, value_in, shapes, padding_mask=None):
+        B, Lq, _ = query.shape
+        S = value_in.shape[1]
+        H, L, P = self.n_heads, self.n_levels, self.n_points
+        value = ops.linear(value_in, self.value_proj.weight, self.value_proj.bias)
+        if padding_mask is not None:
+            value = value.masked_fill(padding_mask[..., None], 0.0)
+        value = value.view(B, S, H, self.d_model // H)
+        off = ops.linear(query, self.sampling_offsets.weight, self.sampling_offsets.bias).view(B, Lq, H, L, P, 2)
+        logits = ops.linear(query, self.attention_weights.weight, self.attention_weights.bias).view(B, Lq, H, L * P)
+        out = ops.msda(value, shapes, ref, off, logits)
+        return ops.linear(out.to(query.dtype), self.output_proj.weight, self.output_proj.bias)
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, cfg: RfDetrConfig):
+        super().__init__()
+        d = cfg.hidden_dim
+        self.group_detr = max(1, cfg.group_detr)
+        self.self_attn = nn.MultiheadAttention(d, cfg.sa_nheads, dropout=0.0)
+        self.norm1 = nn.LayerNorm(d)
+        self.cross_attn = MSDeformAttn(d, cfg.num_feature_levels, cfg.ca_nheads, cfg.dec_n_points)
+        self.linear1 = nn.Linear(d, cfg.dim_feedforward)
+        self.linear2 = nn.Linear(cfg.dim_feedforward, d)
+        self.norm2 = nn.LayerNorm(d)
+        self.norm3 = nn.LayerNorm(d)
+
+    def _self_attention(self, tgt, query_pos, groups):
+        B, Q, d = tgt.shape
+        H = self.self_attn.num_heads
+        Dh = d // H
+        w, b = self.self_attn.in_proj_weight, self.self_attn.in_proj_bias
+        qk = ops.linear(tgt + query_pos, w[:2 * d], b[:2 * d])  # [B, Q, 2d]
+        v = ops.linear(tgt, w[2 * d:], b[2 * d:])              # [B, Q, d]
+        Qg = Q // groups
+        # [B, G, Qg, H, Dh] -> [B*G, H, Qg, Dh]: attention never crosses a group
+        q = qk[..., :d].reshape(B * groups, Qg, H, Dh).transpose(1, 2)
+        k = qk[..., d:].reshape(B * groups, Qg, H, Dh).transpose(1, 2)
+        vv = v.reshape(B * groups, Qg, H, Dh).transpose(1, 2)
+        o = ops.attention(q, k, vv).transpose(1, 2).reshape(B, Q, d)
+        return ops.linear(o, self.self_attn.out_proj.weight, self.self_attn.out_proj.bias)
+
+    def forward(self, tgt, query_pos, ref, memory, shapes, padding_mask, groups):
+        sa = self._self_attention(tgt, query_pos, groups)
+        x = ops.layer_norm(tgt + sa, self.norm1.weight, self.norm1.bias, 1e-5)
+        ca = self.cross_attn(x + query_pos, ref, memory, shapes, padding_mask)
+        x = ops.layer_norm(x + ca, self.norm2.weight, self.norm2.bias, 1e-5)
+        h = ops.linear(x, self.linear1.weight, self.linear1.bias, act="relu")
+        h = ops.linear(h, self.linear2.weight, self.linear2.bias)
+        return ops.layer_norm(x + h, self.norm3.weight, self.norm3.bias, 1e-5)
+
+
+class Decoder(nn.Module):
+    def __init__(self, cfg: RfDetrConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.layers = nn.ModuleList(DecoderLayer(cfg) for _ in range(max(1, cfg.dec_layers)))
+        self.norm = nn.LayerNorm(cfg.hidden_dim)
+        self.ref_point_head = Mlp(2 * cfg.hidden_dim, cfg.hidden_dim, cfg.hidden_dim, 2)
+
+    def forward(self, tgt, memory, refpoints, shapes, padding_mask, valid_ratios, groups, bbox_embed=None):
+        cfg = self.cfg
+        L = len(shapes)
+
+        def reference(r):
+            vr = valid_ratios if valid_ratios is not None else torch.ones(r.shape[0], L, 2, device=r.device,
+                                                                           dtype=r.dtype)
+            rin = r[:, :, None, :4] * torch.cat([vr, vr], -1)[:, None].to(r.dtype)  # [B,Q,L,4]
+            sine = gen_sineembed_for_position(rin[:, :, 0], cfg.hidden_dim // 2).to(tgt.dtype)
+            return rin, self.ref_point_head(sine)
+
+        out = tgt
+        refs = refpoints
+        intermediate = []
+        hs_refs = [refpoints]
+        if cfg.lite_refpoint_refine:
+            rin, qpos = reference(refs if cfg.bbox_reparam else refs.sigmoid())
+        for li, layer in enumerate(self.layers):
+            if not cfg.lite_refpoint_refine:
+                rin, qpos = reference(refs if cfg.bbox_reparam else refs.sigmoid())
+            out = layer(out, qpos, rin, memory, shapes, padding_mask, groups)
+            if not cfg.lite_refpoint_refine and bbox_embed is not None:
+                delta = bbox_embed(out)
+                new = reparam_boxes(delta, refs) if cfg.bbox_reparam else refs + delta
+                if li != len(self.layers) - 1:
+                    hs_refs.append(new)
+                refs = new.detach()
+            intermediate.append(ops.layer_norm(out, self.norm.weight, self.norm.bias, 1e-5))
+        if bbox_embed is not None and not cfg.lite_refpoint_refine:
+            return torch.stack(intermediate), torch.stack(hs_refs)
+        return torch.stack(intermediate), refs.unsqueeze(0)
+
+
+class GroupedLinear(nn.Module):
+    """G independent Linear layers stored as one [G, out, in] parameter.
+
+    State dict keys are ``<g>.weight`` / ``<g>.bias`` (a ModuleList of Linear in
+    the reference checkpoint)."""
+
+    def __init__(self, groups: int, din: int, dout: int):
+        super().__init__()
+        self.groups = groups
+        ref = [nn.Linear(din, dout) for _ in range(groups)]
+        self.weight = nn.Parameter(torch.stack([l.weight.data for l in ref]))
+        self.bias = nn.Parameter(torch.stack([l.bias.data for l in ref]))
+
+        def save_hook(mod, state, prefix, md):
+            w = state.pop(prefix + "weight")
+            b = state.pop(prefix + "bias")
+            for g in range(w.shape[0]):
+                state[f"{prefix}{g}.weight"] = w[g]
+                state[f"{prefix}{g}.bias"] = b[g]
+
+        def load_hook(state, prefix, md, strict, missing, unexpected, errors):
+            ks = [f"{prefix}{g}.weight" for g in range(self.groups)]
+            if all(k in state for k in ks):
+                state[prefix + "weight"] = torch.stack([state.pop(k) for k in ks])
+                state[prefix + "bias"] = torch.stack([state.pop(f"{prefix}{g}.bias") for g in range(self.groups)])
+
+        self._register_state_dict_hook(save_hook)
+        self._register_load_state_dict_pre_hook(load_hook)
+
+    def forward(self, x: torch.Tensor, groups: int, act=None) -> torch.Tensor:
+        """x: [G', B, N, din] (one slice per group) or [B, N, din] (shared) -> [groups, B, N, dout]."""
+        w = self.weight[:groups].to(x.dtype)
+        b = self.bias[:groups].to(x.dtype)
+        if x.dim() == 3:
+            y = torch.einsum("bnc,goc->gbno", x, w)
+        else:
+            y = torch.einsum("gbnc,goc->gbno", x, w)
+        y = y + b[:, None, None, :]
+        if act == "relu":
+            y = F.relu(y)
+        return y
+
+
+class GroupedLayerNorm(nn.Module):
+    def __init__(self, groups: int, dim: int):
+        super().__init__()
+        self.groups = groups
+        self.weight = nn.Parameter(torch.ones(groups, dim))
+        self.bias = nn.Parameter(torch.zeros(groups, dim))
+
+        def save_hook(mod, state, prefix, md):
+            w = state.pop(prefix + "weight")
+            b = state.pop(prefix + "bias")
+            for g in range(w.shape[0]):
+                state[f"{prefix}{g}.weight"] = w[g]
+                state[f"{prefix}{g}.bias"] = b[g]
+
+        def load_hook(state, prefix, md, strict, missing, unexpected, errors):
+            ks = [f"{prefix}{g}.weight" for g in range(self.groups)]
+            if all(k in state for k in ks):
+                state[prefix + "weight"] = torch.stack([state.pop(k) for k in ks])
+                state[prefix + "bias"] = torch.stack([state.pop(f"{prefix}{g}.bias") for g in range(self.groups)])
+
+        self._register_state_dict_hook(save_hook)
+        self._register_load_state_dict_pre_hook(load_hook)
+
+    def forward(self, x, groups):
+        # x [G, B, N, C]: normalise, then per-group affine
+        y = F.layer_norm(x, (x.shape[-1],), None, None, 1e-5)
+        return y * self.weight[:groups, None, None].to(y.dtype) + self.bias[:groups, None, None].to(y.dtype)
+
+
+class GroupedMlp(nn.Module):
+    """G independent 3-layer box MLPs; keys ``<g>.layers.<i>.weight``."""
+
+    def __init__(self, groups: int, din: int, dh: int, dout: int, n: int):
+        super().__init__()
+        self.groups = groups
+        dims = [din] + [dh] * (n - 1)
+        outs = [dh] * (n - 1) + [dout]
+        self.layers = nn.ModuleList(GroupedLinear(groups, a, b) for a, b in zip(dims, outs))
+        # re-key: GroupedLinear hooks emit `layers.<i>.<g>.weight`; the checkpoint wants `<g>.layers.<i>.weight`
+
+        def save_hook(mod, state, prefix, md):
+            n_l = len(self.layers)
+            for i in range(n_l):
+                for g in range(self.groups):
+                    for t in ("weight", "bias"):
+                        k = f"{prefix}layers.{i}.{g}.{t}"
+                        if k in state:
+                            state[f"{prefix}{g}.layers.{i}.{t}"] = state.pop(k)
+
+        def load_hook(state, prefix, md, strict, missing, unexpected, errors):
+            for i in range(len(self.layers)):
+                for g in range(self.groups):
+                    for t in ("weight", "bias"):
+                        k = f"{prefix}{g}.layers.{i}.{t}"
+                        if k in state:
+                            state[f"{prefix}layers.{i}.{g}.{t}"] = state.pop(k)
+
+        self._register_state_dict_hook(save_hook)
+        self._register_load_state_dict_pre_hook(load_hook)
+
+    def forward(self, x, groups):
+        n = len(self.layers)
+        for i, l in enumerate(self.layers):
+            x = l(x, groups, act="relu" if i + 1 < n else None)
+        return x
+
+
+_proposal_cache = {}
+
+
+def encoder_proposals(shapes, batch: int, device, dtype, unsigmoid: bool):
+    """Full-valid two-stage proposals (reference `model.cpp:1076-1139`), cached per shape.
+
+    Returns (proposals [1, S, 4], valid [1, S, 1])."""
+    key = (tuple(shapes), str(device), dtype, unsigmoid)
+    hit = _proposal_cache.get(key)
+    if hit is not None:
+        return hit
+    props = []
+    for lvl, (h, w) in enumerate(shapes):
+        gy, gx = torch.meshgrid(torch.arange(h, dtype=torch.float32, device=device),
+                                torch.arange(w, dtype=torch.float32, device=device), indexing="ij")
+        grid = torch.stack([(gx + 0.5) / w, (gy + 0.5) / h], -1)
+        wh = torch.full_like(grid, 0.05 * (2.0 ** lvl))
+        props.append(torch.cat([grid, wh], -1).view(1, -1, 4))
+    p = torch.cat(props, 1)
+    valid = ((p > 0.01) & (p < 0.99)).all(-1, keepdim=True)
+    if unsigmoid:
+        p = torch.log(p / (1 - p)).masked_fill(~valid, float("inf"))
+    else:
+        p = p.masked_fill(~valid, 0.0)
+    out = (p.to(dtype), valid)
+    _proposal_cache[key] = out
+    return out
+
+
+class Transformer(nn.Module):
+    def __init__(self, cfg: RfDetrConfig):
+        super().__init__()
+        self.cfg = cfg
+        G = max(1, cfg.group_detr)
+        d = cfg.hidden_dim
+        self.decoder = Decoder(cfg)
+        self.enc_output = GroupedLinear(G, d, d)
+        self.enc_output_norm = GroupedLayerNorm(G, d)
+        self.enc_out_class_embed = GroupedLinear(G, d, max(1, cfg.num_classes))
+        self.enc_out_bbox_embed = GroupedMlp(G, d, d, 4, 3)
+        prior = -math.log((1 - 0.01) / 0.01)
+        with torch.no_grad():
+            self.enc_out_class_embed.bias.fill_(prior)
+
+    def forward(self, feats: List[torch.Tensor], refpoint_embed, query_feat, training: bool, bbox_embed=None):
+        """feats: channels-last [B, h, w, C] per level.  Returns dict with hs [Ldec,B,Q,C], refs, enc_* ."""
+        cfg = self.cfg
+        B = feats[0].shape[0]
+        shapes = [(f.shape[1], f.shape[2]) for f in feats]
+        memory = torch.cat([f.reshape(B, -1, f.shape[-1]) for f in feats], 1)  # [B, S, C]
+        groups = max(1, cfg.group_detr) if training else 1
+        out = {"shapes": shapes}
+        refpoints = refpoint_embed.unsqueeze(0).expand(B, -1, -1)
+        if cfg.two_stage:
+            props, valid = encoder_proposals(shapes, B, memory.device, memory.dtype, not cfg.bbox_reparam)
+            out_mem = memory.masked_fill(~valid, 0.0)
+            h = self.enc_output(out_mem, groups)                               # [G, B, S, C]
+            h = self.enc_output_norm(h, groups)
+            cls = self.enc_out_class_embed(h, groups)                          # [G, B, S, K]
+            delta = self.enc_out_bbox_embed(h, groups)                         # [G, B, S, 4]
+            if cfg.bbox_reparam:
+                coord = reparam_boxes(delta, props[None])
+            else:
+                coord = delta + props[None]
+            k = min(cfg.num_queries, cls.shape[2])
+            topk = cls.max(-1)[0].topk(k, dim=2)[1]                            # [G, B, k]
+            boxes = coord.gather(2, topk[..., None].expand(-1, -1, -1, 4))      # [G, B, k, 4]
+            mem_sel = h.gather(2, topk[..., None].expand(-1, -1, -1, h.shape[-1]))
+            # group-major query order [B, G*k, .]
+            enc_boxes = boxes.permute(1, 0, 2, 3).reshape(B, groups * k, 4)
+            enc_mem = mem_sel.permute(1, 0, 2, 3).reshape(B, groups * k, -1)
+            out["enc_boxes"] = enc_boxes if cfg.bbox_reparam else enc_boxes.sigmoid()
+            out["enc_memory"] = enc_mem
+            ts = enc_boxes.detach()
+            n_ts = ts.shape[1]
+            head = refpoints[:, :n_ts]
+            if cfg.bbox_reparam:
+                head = reparam_boxes(head.to(ts.dtype), ts)
+            else:
+                head = head + ts
+            refpoints = torch.cat([head, refpoints[:, n_ts:].to(head.dtype)], 1)
+        tgt = query_feat.unsqueeze(0).expand(B, -1, -1).to(memory.dtype)
+        hs, refs = self.decoder(tgt, memory, refpoints.to(memory.dtype), shapes, None, None, groups, bbox_embed)
+        out["hs"] = hs
+        out["refs"] = refs
+        out["memory"] = memory
+        return out
+
+    def encoder_class_logits(self, enc_memory: torch.Tensor, groups: int) -> torch.Tensor:
+        B, Q, C = enc_memory.shape
+        x = enc_memory.view(B, groups, Q // groups, C).permute(1, 0, 2, 3)   # [G, B, k, C]
+        logits = self.enc_out_class_embed(x, groups)                         # [G, B, k, K]
+        return logits.permute(1, 0, 2, 3).reshape(B, Q, -1)

@@ -1,0 +1,40 @@
+"""LayerNorm over the last dimension (ViT eps 1e-6, decoder eps 1e-5, LayerNorm2d
+as channels-last LN).  Reference: `torch::nn::LayerNorm` uses in
+`src/rfdetr/layers/model.cpp:267-285,535-541,873-886` (libtorch kernel).
+
+CUDA: one warp per row, fp32 statistics, bf16/fp32 I/O; backward computes dx
+per row and dgamma/dbeta through per-CTA fp32 partials reduced by a second
+kernel.  CPU: ``torch.nn.functional.layer_norm`` (the oracle).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import kernels
+
+__all__ = ["layer_norm"]
+
+
+class _LayerNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        shape = x.shape
+        x2 = x.contiguous().view(-1, shape[-1])
+        y, mean, rstd = kernels().layernorm_fwd(x2, weight, bias, float(eps))
+        ctx.save_for_backward(x2, weight, mean, rstd)
+        ctx.shape = shape
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, weight, mean, rstd = ctx.saved_tensors
+        gy2 = gy.contiguous().view(x2.shape)
+        dx, dw, db = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd)
+        return dx.view(ctx.shape), dw, db, None
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float) -> torch.Tensor:
+    if x.is_cuda and x.shape[-1] % 8 == 0 and x.dtype in (torch.bfloat16, torch.float32):
+        return _LayerNormFn.apply(x, weight, bias, eps)
+    return F.layer_norm(x, (x.shape[-1],), weight.to(x.dtype), bias.to(x.dtype), eps)

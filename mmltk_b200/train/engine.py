@@ -1,0 +1,252 @@
+"""One training step on one device: forward, matcher, losses, backward and the
+optimizer update -- eager or replayed from a CUDA graph.
+
+Reference step (`src/rfdetr/training/train.cpp:2287-2458`): autocast forward,
+`detection_loss_dict`, `backward`, `average_gradients` (NCCL), finite check,
+`clip_grad_norm_(0.1)`, fused AdamW, EMA update, with one host sync per
+optimizer step for the metrics.
+
+B200 design:
+* parameters are bf16 views into one flat buffer; fp32 master weights, Adam
+  moments and the EMA shadow are flat fp32 buffers; gradients accumulate in
+  place into one flat bf16 buffer;
+* the matcher and every loss stay on the device, so the whole step (including
+  the optimizer kernels and, for DDP, the gradient collective) is captured once
+  into a CUDA graph and replayed; the host only refreshes the per-step
+  scalars (lr scale, bias corrections, EMA decay) with one async copy and reads
+  back the loss + status flags once per step;
+* the optimizer is the fused grad-norm + AdamW + EMA kernel pair (one pass
+  over memory).  With DDP the gradient reduction is delegated to a
+  ``GradientSync`` (fused in-kernel NVSwitch reduce-scatter/all-gather, or the
+  NCCL baseline).
+"""
+from __future__ import annotations
+
+import math
+import time
+from typing import Callable, Dict, List, Optional
+
+import torch
+
+from ..config import TrainOptions, lr_scale
+from ..criterion import SetCriterion, Targets
+from ..ops._ext import kernels
+from .flat import FlatParams
+from .param_groups import build_param_groups
+
+__all__ = ["TrainEngine", "StepResult"]
+
+
+class StepResult:
+    __slots__ = ("loss", "losses", "grad_norm", "nonfinite")
+
+    def __init__(self, loss, losses, grad_norm, nonfinite):
+        self.loss, self.losses, self.grad_norm, self.nonfinite = loss, losses, grad_norm, nonfinite
+
+
+class TrainEngine:
+    def __init__(self, model: torch.nn.Module, opts: TrainOptions, device, grad_sync=None,
+                 max_targets: int = 100, steps_per_epoch: int = 1, total_steps: int = 1):
+        self.model = model
+        self.cfg = model.cfg
+        self.opts = opts
+        self.device = torch.device(device)
+        self.cuda = self.device.type == "cuda"
+        self.grad_sync = grad_sync
+        self.world = grad_sync.world_size if grad_sync is not None else 1
+        self.max_targets = max_targets
+        self.steps_per_epoch = max(1, steps_per_epoch)
+        self.total_steps = max(1, total_steps)
+        self.step_count = 0
+        if opts.freeze_encoder:
+            for n, p in model.named_parameters():
+                if "backbone.0.encoder" in n:
+                    p.requires_grad_(False)
+        named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+        nvit = getattr(self.cfg, "vit_depth", 12) + 1
+        self.groups, assign = build_param_groups(named, opts, nvit)
+        self.criterion = SetCriterion(self.cfg, self.world,
+                                      grad_sync.all_reduce_small if grad_sync is not None else None)
+        if self.cuda:
+            self._init_cuda(named, assign)
+        else:
+            self._init_cpu(named, assign)
+        self.graph = None
+        self._graph_warmup = 0
+
+    # ------------------------------------------------------------------ setup
+    def _init_cpu(self, named, assign):
+        self.model.to(self.device)
+        pgs = [{"params": [], "lr": g["lr"], "weight_decay": g["weight_decay"]} for g in self.groups]
+        for (n, p), gi in zip(named, assign):
+            pgs[gi]["params"].append(p)
+        self.optimizer = torch.optim.AdamW(pgs, betas=(0.9, 0.999), eps=1e-8)
+        self.base_lrs = [g["lr"] for g in self.groups]
+        self.ema = [p.detach().clone() for _, p in named] if self.opts.use_ema else None
+        self.ema_named = [n for n, _ in named]
+        self.params = [p for _, p in named]
+
+    def _init_cuda(self, named, assign):
+        k = kernels()
+        pad = self.grad_sync.pad_multiple if self.grad_sync is not None else 1
+        fp32 = {n: p.detach().float().clone() for n, p in named}
+        self.model.to(self.device, torch.bfloat16)
+        named_dev = [(n, p) for n, p in self.model.named_parameters() if p.requires_grad]
+        self.flat = FlatParams(named_dev, assign, self.device, torch.bfloat16, pad_to=pad)
+        master = torch.zeros(self.flat.total, dtype=torch.float32, device=self.device)
+        for i, n in enumerate(self.flat.names):
+            o, c = self.flat.offsets[i], self.flat.numels[i]
+            master[o:o + c].copy_(fp32[n].reshape(-1))
+        self.master = master
+        self.chunks = self.flat.chunk_table().to(self.device)
+        self.group_hyper = torch.tensor([[g["lr"], g["weight_decay"]] for g in self.groups], dtype=torch.float32,
+                                        device=self.device)
+        nsc = k.step_scalar_floats()
+        self.scalars_host = torch.zeros(nsc, dtype=torch.float32).pin_memory()
+        self.scalars = torch.zeros(nsc, dtype=torch.float32, device=self.device)
+        self.flags = torch.zeros(2, dtype=torch.int32, device=self.device)
+        if self.grad_sync is not None:
+            self.grad_sync.setup(self)
+        else:
+            self.m = torch.zeros_like(master)
+            self.v = torch.zeros_like(master)
+            self.ema_buf = master.clone() if self.opts.use_ema else None
+            self.scratch = torch.zeros(k.optim_num_partials(), dtype=torch.float32, device=self.device)
+        self.readback = torch.zeros(4, dtype=torch.float32).pin_memory()
+
+    # ------------------------------------------------------------------ scalars
+    def _host_scalars(self, step: int):
+        o = self.opts
+        t = step + 1
+        s = lr_scale(o, step, self.steps_per_epoch, self.total_steps)
+        d = o.ema_decay * (1 - math.exp(-(step + 1) / o.ema_tau)) if o.ema_tau > 0 else o.ema_decay
+        return [s, 0.9, 0.999, 1e-8, 1 - 0.9 ** t, 1 - 0.999 ** t, o.clip_max_norm, d,
+                1.0 if o.use_ema else 0.0, 1.0 / self.world]
+
+    # ------------------------------------------------------------------ body
+    def _forward_loss(self, images: torch.Tensor, targets: Targets):
+        out = self.model(images)
+        losses, _ = self.criterion(out, targets, training=True)
+        total = self.criterion.weighted(losses)
+        return total, losses
+
+    def _cuda_body(self, images, targets):
+        self.flags.zero_()
+        self.flat.zero_grad()
+        total, losses = self._forward_loss(images, targets)
+        total.backward()
+        if self.grad_sync is not None:
+            self.grad_sync.step(self)
+        else:
+            kernels().adamw_ema_step(self.chunks, self.group_hyper, self.scalars, self.flat.grad_buf, self.master,
+                                     self.m, self.v, self.ema_buf, self.flat.param_buf, self.scratch, self.flags)
+        return total.detach(), {k: v.detach() for k, v in losses.items()}
+
+    # ------------------------------------------------------------------ public
+    def bind_static_inputs(self, batch: int, channels: int, height: int, width: int) -> None:
+        dev = self.device
+        self.in_images = torch.zeros(batch, channels, height, width, dtype=torch.bfloat16, device=dev)
+        T = self.max_targets
+        self.in_targets = Targets(torch.full((batch, T, 4), 0.5, device=dev), torch.zeros(batch, T, dtype=torch.int64,
+                                  device=dev), torch.ones(batch, dtype=torch.int32, device=dev), [1] * batch)
+
+    def load_inputs(self, images: torch.Tensor, targets: Targets) -> None:
+        """Copy one batch (pinned host or device tensors) into the static input buffers."""
+        self.in_images.copy_(images, non_blocking=True)
+        t = self.in_targets
+        T = targets.slots
+        if T > t.slots:
+            raise ValueError(f"batch has {T} target slots, engine was built for {t.slots}")
+        t.boxes[:, :T].copy_(targets.boxes, non_blocking=True)
+        t.labels[:, :T].copy_(targets.labels, non_blocking=True)
+        if T < t.slots:
+            t.boxes[:, T:].fill_(0.5)
+            t.labels[:, T:].zero_()
+        t.counts.copy_(targets.counts, non_blocking=True)
+        t.counts_host = list(targets.counts_host)
+
+    def step(self, images: Optional[torch.Tensor] = None, targets: Optional[Targets] = None,
+             sync: bool = True) -> StepResult:
+        """One optimizer step.  On CUDA, inputs are copied into the static buffers first
+        (pass None to reuse what is already there)."""
+        if not self.cuda:
+            return self._cpu_step(images, targets)
+        if images is not None:
+            self.load_inputs(images, targets)
+        sc = self._host_scalars(self.step_count)
+        self.scalars_host[:len(sc)] = torch.tensor(sc)
+        self.scalars.copy_(self.scalars_host, non_blocking=True)
+        if self.opts.cuda_graph and self._graph_warmup >= 3:
+            if self.graph is None:
+                self._capture()
+            self.graph.replay()
+            total, losses = self.static_total, self.static_losses
+        else:
+            total, losses = self._cuda_body(self.in_images, self.in_targets)
+            self._graph_warmup += 1
+        self.step_count += 1
+        if self.grad_sync is not None:
+            self.grad_sync.after_step(self)
+        if not sync:
+            return StepResult(total, losses, None, None)
+        self.readback[0].copy_(total, non_blocking=True)
+        self.readback[1:3].copy_(self.flags.view(torch.float32), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        loss = float(self.readback[0])
+        nonfinite = int(self.flags_host_bits(self.readback[1]))
+        norm = float(self.readback[2])
+        if nonfinite or not math.isfinite(loss):
+            raise FloatingPointError(f"non-finite RF-DETR loss ({loss}) or gradients (norm {norm}) at step "
+                                     f"{self.step_count}")
+        return StepResult(loss, losses, norm, nonfinite)
+
+    @staticmethod
+    def flags_host_bits(x: torch.Tensor) -> int:
+        return int(x.view(torch.int32).item())
+
+    def release_graph(self) -> None:
+        """Drop the captured graph (required before destroying a process group it uses)."""
+        if self.graph is not None:
+            torch.cuda.synchronize()
+            self.graph.reset()
+            self.graph = None
+            self.static_total = self.static_losses = None
+            self._graph_warmup = 0
+
+    def _capture(self):
+        stream = torch.cuda.current_stream()
+        self.graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(self.graph, stream=torch.cuda.Stream()):
+            self.static_total, self.static_losses = self._cuda_body(self.in_images, self.in_targets)
+        stream.wait_stream(stream)
+
+    def _cpu_step(self, images, targets) -> StepResult:
+        o = self.opts
+        s = lr_scale(o, self.step_count, self.steps_per_epoch, self.total_steps)
+        for g, base in zip(self.optimizer.param_groups, self.base_lrs):
+            g["lr"] = base * s
+        self.optimizer.zero_grad(set_to_none=True)
+        total, losses = self._forward_loss(images, targets)
+        total.backward()
+        if self.grad_sync is not None:
+            self.grad_sync.cpu_average(self.params)
+        norm = torch.nn.utils.clip_grad_norm_(self.params, o.clip_max_norm) if o.clip_max_norm > 0 else None
+        if not torch.isfinite(total) or (norm is not None and not torch.isfinite(norm)):
+            raise FloatingPointError(f"non-finite RF-DETR loss or gradients at step {self.step_count}")
+        self.optimizer.step()
+        if self.ema is not None:
+            d = o.ema_decay * (1 - math.exp(-(self.step_count + 1) / o.ema_tau)) if o.ema_tau > 0 else o.ema_decay
+            with torch.no_grad():
+                torch._foreach_mul_(self.ema, d)
+                torch._foreach_add_(self.ema, [p.detach() for p in self.params], alpha=1 - d)
+        self.step_count += 1
+        return StepResult(float(total), {k: v.detach() for k, v in losses.items()},
+                          None if norm is None else float(norm), 0)
+
+    # ------------------------------------------------------------------ state
+    def ema_state(self) -> Optional[Dict[str, torch.Tensor]]:
+        if not self.cuda:
+            return None if self.ema is None else {n: t for n, t in zip(self.ema_named, self.ema)}
+        buf = self.grad_sync.gather_ema(self) if self.grad_sync is not None else self.ema_buf
+        return None if buf is None else self.flat.state_dict_tensors(buf)

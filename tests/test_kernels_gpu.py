@@ -1,0 +1,181 @@
+"""sm_100a kernels vs plain-PyTorch fp32 references of the same op."""
+import numpy as np
+import pytest
+import torch
+
+from mmltk_b200 import ops
+from mmltk_b200.ops import kernels, native
+from mmltk_b200.ops.msda import msda_reference
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return (a.float() - b.float()).abs().max().item() / max(1e-6, b.float().abs().max().item())
+
+
+@pytest.mark.parametrize("C", [64, 256, 384, 768])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_layernorm_fwd_bwd(cuda_device, C, dtype):
+    torch.manual_seed(0)
+    x = torch.randn(1037, C, device=cuda_device) * 3 + 1
+    w = torch.randn(C, device=cuda_device)
+    b = torch.randn(C, device=cuda_device)
+    gy = torch.randn(1037, C, device=cuda_device)
+    xr, wr, br = (t.clone().requires_grad_() for t in (x, w, b))
+    yr = torch.nn.functional.layer_norm(xr, (C,), wr, br, 1e-6)
+    yr.backward(gy)
+    xk = x.to(dtype).requires_grad_()
+    wk = w.to(dtype).requires_grad_()
+    bk = b.to(dtype).requires_grad_()
+    yk = ops.layer_norm(xk, wk, bk, 1e-6)
+    yk.backward(gy.to(dtype))
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
+    assert _rel(yk, yr) < tol
+    assert _rel(xk.grad, xr.grad) < tol
+    assert _rel(wk.grad, wr.grad) < tol * 2
+    assert _rel(bk.grad, br.grad) < tol * 2
+
+
+def _msda_inputs(B, shapes, Lq, H, D, P, device, dtype, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    S = sum(h * w for h, w in shapes)
+    L = len(shapes)
+    value = torch.randn(B, S, H, D, generator=g)
+    ref = torch.rand(B, Lq, L, 4, generator=g)
+    ref[..., 2:] = ref[..., 2:] * 0.5 + 0.05
+    off = torch.randn(B, Lq, H, L, P, 2, generator=g) * 2
+    logits = torch.randn(B, Lq, H, L * P, generator=g)
+    return [t.to(device=device, dtype=dtype) for t in (value, ref, off, logits)]
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(B=2, shapes=[(9, 11)], Lq=37, H=16, D=16, P=2),            # RF-DETR decoder (single P4 level)
+    dict(B=2, shapes=[(12, 12), (6, 6)], Lq=50, H=8, D=32, P=4),    # multi-level
+    dict(B=1, shapes=[(5, 7), (3, 3), (2, 2)], Lq=19, H=4, D=64, P=3),
+])
+def test_msda_fwd_bwd_vs_grid_sample(cuda_device, cfg):
+    shapes = cfg["shapes"]
+    v, r, o, lg = _msda_inputs(cfg["B"], shapes, cfg["Lq"], cfg["H"], cfg["D"], cfg["P"], "cpu", torch.float32)
+    # reference in fp32 on CPU (grid_sample + softmax + location arithmetic)
+    ins = [t.clone().requires_grad_() for t in (v, r, o, lg)]
+    out_ref = msda_reference(ins[0], shapes, ins[1], ins[2], ins[3])
+    gout = torch.randn_like(out_ref)
+    out_ref.backward(gout)
+    for dtype, tol in ((torch.float32, 2e-4), (torch.bfloat16, 3e-2)):
+        dins = [t.to(cuda_device, dtype).clone().requires_grad_() for t in (v, r, o, lg)]
+        out = ops.msda(dins[0], shapes, dins[1], dins[2], dins[3])
+        out.backward(gout.to(cuda_device, dtype))
+        assert _rel(out.cpu(), out_ref) < tol, dtype
+        for a, b, name in zip(dins, ins, ("value", "ref", "offsets", "logits")):
+            assert _rel(a.grad.cpu(), b.grad) < tol * (3 if dtype == torch.bfloat16 else 5), (name, dtype)
+
+
+def test_msda_out_of_range_points_are_zero(cuda_device):
+    shapes = [(4, 4)]
+    v, r, o, lg = _msda_inputs(1, shapes, 5, 2, 16, 2, cuda_device, torch.float32)
+    r[..., :2] = 5.0  # far outside the map
+    out = ops.msda(v, shapes, r, o, lg)
+    assert out.abs().max().item() == 0.0
+
+
+def test_matcher_cost_and_gpu_lsap(cuda_device):
+    from mmltk_b200.criterion.matcher import matcher_cost_reference
+    from mmltk_b200.data.synthetic import synthetic_targets
+    torch.manual_seed(0)
+    NL, B, G, Qg, C, T = 3, 4, 5, 60, 91, 10
+    Q = G * Qg
+    gen = torch.Generator().manual_seed(1)
+    tg = synthetic_targets(B, gen, kmax=T, slots=T)
+    logits = [torch.randn(B, Q, C) for _ in range(NL)]
+    boxes = [torch.cat([torch.rand(B, Q, 2) * 0.8 + 0.1, torch.rand(B, Q, 2) * 0.3 + 0.02], -1) for _ in range(NL)]
+    ref = matcher_cost_reference(logits, boxes, tg, 2.0, 5.0, 2.0)
+    tgd = tg.to(cuda_device)
+    k = kernels()
+    cost = k.matcher_cost([l.to(cuda_device) for l in logits], [b.to(cuda_device) for b in boxes], tgd.labels,
+                          tgd.boxes, tgd.counts, 2.0, 5.0, 2.0, 0.25)
+    valid = tg.valid()[None, :, None, :].expand_as(ref)
+    assert (cost.cpu()[valid] - ref[valid]).abs().max().item() < 1e-4
+    # LSAP on the same cost: GPU == host C++ solver == scipy
+    match, status = k.lsap_batched(cost, tgd.counts, G)
+    assert int(status.item()) == 0
+    host = native().match_batched(cost.cpu(), tg.counts.to(torch.int64), G)
+    assert torch.equal(match.cpu(), host)
+
+
+def test_gpu_lsap_random_sizes(cuda_device):
+    k = kernels()
+    rng = np.random.default_rng(3)
+    for (G, Qg, T) in [(1, 7, 7), (3, 100, 40), (13, 300, 10), (2, 33, 1)]:
+        B = 3
+        cost = torch.from_numpy(rng.normal(size=(2, B, G * Qg, T)).astype(np.float32))
+        counts = torch.from_numpy(rng.integers(0, T + 1, size=B).astype(np.int32))
+        m, st = k.lsap_batched(cost.to(cuda_device), counts.to(cuda_device), G)
+        h = native().match_batched(cost, counts.to(torch.int64), G)
+        assert int(st.item()) == 0
+        assert torch.equal(m.cpu(), h)
+
+
+def test_dense_focal_neg(cuda_device):
+    x = torch.randn(3, 50, 91) * 3
+    xr = x.clone().requires_grad_()
+    ref = (torch.sigmoid(xr) ** 2 * torch.nn.functional.softplus(xr)).sum() * 0.75
+    ref.backward()
+    xd = x.to(cuda_device, torch.bfloat16).requires_grad_()
+    out = ops.dense_focal_neg(xd, 0.75)
+    out.backward()
+    xb = x.to(torch.bfloat16).float().requires_grad_()
+    refb = (torch.sigmoid(xb) ** 2 * torch.nn.functional.softplus(xb)).sum() * 0.75
+    refb.backward()
+    assert abs(out.item() - refb.item()) / refb.item() < 1e-3
+    assert _rel(xd.grad.cpu(), xb.grad) < 2e-2
+
+
+def test_fused_adamw_ema_matches_torch(cuda_device):
+    from mmltk_b200.train.flat import FlatParams
+    torch.manual_seed(0)
+    shapes = [(64, 33), (91,), (3, 5, 7)]
+    ps = [torch.nn.Parameter(torch.randn(s)) for s in shapes]
+    ref = [torch.nn.Parameter(p.detach().clone()) for p in ps]
+    groups = [0, 1, 0]
+    hyper = [(1e-3, 0.05), (2e-3, 0.0)]
+    opt = torch.optim.AdamW([{"params": [ref[0], ref[2]], "lr": 1e-3, "weight_decay": 0.05},
+                             {"params": [ref[1]], "lr": 2e-3, "weight_decay": 0.0}], betas=(0.9, 0.999), eps=1e-8)
+    dev_ps = [torch.nn.Parameter(p.detach().to(cuda_device, torch.bfloat16)) for p in ps]
+    flat = FlatParams([(f"p{i}", p) for i, p in enumerate(dev_ps)], groups, cuda_device)
+    master = torch.zeros(flat.total, device=cuda_device)
+    for i, p in enumerate(ps):
+        master[flat.offsets[i]:flat.offsets[i] + p.numel()] = p.detach().reshape(-1).to(cuda_device)
+    m = torch.zeros_like(master)
+    v = torch.zeros_like(master)
+    ema = master.clone()
+    emar = [p.detach().clone() for p in ref]
+    k = kernels()
+    scratch = torch.zeros(k.optim_num_partials(), device=cuda_device)
+    flags = torch.zeros(2, dtype=torch.int32, device=cuda_device)
+    chunks = flat.chunk_table().to(cuda_device)
+    gh = torch.tensor(hyper, device=cuda_device)
+    max_norm = 0.1
+    for step in range(3):
+        grads = [torch.randn(s) for s in shapes]
+        grads_b = [g.to(torch.bfloat16).float() for g in grads]
+        for p, g in zip(ref, grads_b):
+            p.grad = g.clone()
+        torch.nn.utils.clip_grad_norm_(ref, max_norm)
+        opt.step()
+        d = 0.993 * (1 - np.exp(-(step + 1) / 100))
+        for e, p in zip(emar, ref):
+            e.mul_(d).add_(p.detach(), alpha=1 - d)
+        for i, g in enumerate(grads):
+            flat.view(flat.grad_buf, i).copy_(g.to(cuda_device, torch.bfloat16).view(shapes[i]))
+        t = step + 1
+        sc = torch.zeros(k.step_scalar_floats())
+        sc[:10] = torch.tensor([1.0, 0.9, 0.999, 1e-8, 1 - 0.9 ** t, 1 - 0.999 ** t, max_norm, d, 1.0, 1.0])
+        k.adamw_ema_step(chunks, gh, sc.to(cuda_device), flat.grad_buf, master, m, v, ema, flat.param_buf, scratch,
+                         flags)
+    for i, p in enumerate(ref):
+        got = master[flat.offsets[i]:flat.offsets[i] + p.numel()].cpu().view(p.shape)
+        assert torch.allclose(got, p.detach(), atol=1e-5, rtol=1e-4)
+        got_e = ema[flat.offsets[i]:flat.offsets[i] + p.numel()].cpu().view(p.shape)
+        assert torch.allclose(got_e, emar[i], atol=1e-5, rtol=1e-4)
+    assert int(flags[0].item()) == 0

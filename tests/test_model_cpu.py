@@ -1,0 +1,147 @@
+"""Model structure, checkpoint key layout and numerics of the CPU (oracle) path."""
+import math
+
+import pytest
+import torch
+
+from mmltk_b200.config import config_from_preset, infer_preset_from_path, find_preset
+from mmltk_b200.models import RFDETR, build_model
+from mmltk_b200.models.transformer import encoder_proposals, gen_sineembed_for_position
+
+
+def tiny(**kw):
+    return build_model("rf-detr-tiny-test", **kw)
+
+
+def test_state_dict_uses_reference_key_layout():
+    m = build_model("rf-detr-nano")
+    keys = set(m.state_dict().keys())
+    must = [
+        "backbone.0.encoder.encoder.embeddings.cls_token",
+        "backbone.0.encoder.encoder.embeddings.position_embeddings",
+        "backbone.0.encoder.encoder.embeddings.patch_embeddings.projection.weight",
+        "backbone.0.encoder.encoder.encoder.layer.0.norm1.weight",
+        "backbone.0.encoder.encoder.encoder.layer.0.attention.attention.query.weight",
+        "backbone.0.encoder.encoder.encoder.layer.11.attention.attention.value.bias",
+        "backbone.0.encoder.encoder.encoder.layer.3.attention.output.dense.weight",
+        "backbone.0.encoder.encoder.encoder.layer.5.layer_scale1.lambda1",
+        "backbone.0.encoder.encoder.encoder.layer.5.mlp.fc1.weight",
+        "backbone.0.encoder.encoder.layernorm.weight",
+        "backbone.0.projector.stages.0.0.cv1.conv.weight",
+        "backbone.0.projector.stages.0.0.cv1.bn.weight",
+        "backbone.0.projector.stages.0.0.m.2.cv2.conv.weight",
+        "backbone.0.projector.stages.0.1.weight",
+        "transformer.decoder.layers.0.self_attn.in_proj_weight",
+        "transformer.decoder.layers.1.cross_attn.sampling_offsets.weight",
+        "transformer.decoder.layers.1.cross_attn.value_proj.bias",
+        "transformer.decoder.ref_point_head.layers.1.weight",
+        "transformer.decoder.norm.weight",
+        "transformer.enc_output.0.weight",
+        "transformer.enc_output.12.bias",
+        "transformer.enc_output_norm.7.weight",
+        "transformer.enc_out_class_embed.3.weight",
+        "transformer.enc_out_bbox_embed.12.layers.2.bias",
+        "class_embed.weight", "bbox_embed.layers.2.weight", "refpoint_embed.weight", "query_feat.weight",
+    ]
+    for k in must:
+        assert k in keys, k
+    assert not any("qkv" in k for k in keys)
+    assert m.state_dict()["refpoint_embed.weight"].shape == (3900, 4)
+
+
+def test_state_dict_roundtrip_and_qkv_split():
+    torch.manual_seed(0)
+    a = tiny()
+    b = tiny()
+    sd = a.state_dict()
+    b.load_state_dict(sd, strict=True)
+    for k, v in b.state_dict().items():
+        assert torch.equal(v, sd[k]), k
+    layer = a.backbone[0].encoder.encoder.encoder.layer[0].attention.attention
+    C = layer.width
+    assert torch.equal(sd["backbone.0.encoder.encoder.encoder.layer.0.attention.attention.key.weight"],
+                       layer.qkv_weight[C:2 * C])
+
+
+def test_init_matches_reference_conventions():
+    m = build_model("rf-detr-nano")
+    prior = -math.log((1 - 0.01) / 0.01)
+    assert torch.allclose(m.class_embed.bias, torch.full_like(m.class_embed.bias, prior))
+    assert torch.allclose(m.transformer.enc_out_class_embed.bias, torch.full_like(m.transformer.enc_out_class_embed.bias,
+                                                                                  prior))
+    assert m.refpoint_embed.weight.abs().max() == 0
+    assert m.bbox_embed.layers[2].weight.abs().max() == 0
+    ca = m.transformer.decoder.layers[0].cross_attn
+    assert ca.attention_weights.weight.abs().max() == 0
+    # grid init: head 0 points along +x with magnitude (point index + 1)
+    b = ca.sampling_offsets.bias.view(ca.n_heads, ca.n_levels, ca.n_points, 2)
+    assert torch.allclose(b[0, 0, :, 0], torch.arange(1, ca.n_points + 1, dtype=torch.float32))
+
+
+def test_forward_shapes_train_and_eval():
+    torch.manual_seed(0)
+    m = tiny(resolution=64)
+    x = torch.randn(2, 3, 64, 64)
+    m.train()
+    o = m(x)
+    Q = m.cfg.num_queries * m.cfg.group_detr
+    assert o["pred_logits"].shape == (2, Q, m.cfg.num_classes)
+    assert o["pred_boxes"].shape == (2, Q, 4)
+    assert len(o["aux_outputs"]) == m.cfg.dec_layers - 1
+    assert o["enc_outputs"]["pred_logits"].shape == (2, Q, m.cfg.num_classes)
+    m.eval()
+    with torch.no_grad():
+        o = m(x)
+    assert o["pred_logits"].shape == (2, m.cfg.num_queries, m.cfg.num_classes)
+
+
+def test_windowing_is_a_permutation_of_tokens():
+    """With identity layers the windowed backbone must return the un-windowed grid."""
+    cfg = config_from_preset("rf-detr-tiny-test", num_windows=2, resolution=64, positional_encoding_size=4)
+    m = RFDETR(cfg)
+    enc = m.backbone[0].encoder.encoder
+    for layer in enc.encoder.layer:
+        layer.layer_scale1.lambda1.data.zero_()
+        layer.layer_scale2.lambda1.data.zero_()
+    enc.layernorm.weight.data.fill_(1.0)
+    enc.layernorm.bias.data.zero_()
+    x = torch.randn(2, 3, 64, 64)
+    feats = enc(x)
+    tokens = enc.embeddings.patch_embeddings(x) + enc.embeddings.position_embeddings[:, 1:]
+    expect = torch.nn.functional.layer_norm(tokens, (cfg.vit_width,), eps=1e-6).view(2, 4, 4, -1)
+    assert torch.allclose(feats[0], expect, atol=1e-5)
+
+
+def test_proposals_and_sine_embedding():
+    p, valid = encoder_proposals([(4, 5)], 1, "cpu", torch.float32, False)
+    assert p.shape == (1, 20, 4)
+    assert torch.allclose(p[0, 0], torch.tensor([0.1, 0.125, 0.05, 0.05]))
+    e = gen_sineembed_for_position(torch.rand(3, 7, 4), 64)
+    assert e.shape == (3, 7, 256)
+
+
+def test_preset_inference_from_paths():
+    assert infer_preset_from_path("/w/rf-detr-medium.pth").name == "rf-detr-medium"
+    assert infer_preset_from_path("/x/my_seg-2xl_run/checkpoint.pth").name == "rf-detr-seg-xxlarge"
+    assert infer_preset_from_path("models/rf-detr-seg-m-ft.pth").name == "rf-detr-seg-medium"
+    assert infer_preset_from_path("/tmp/large/weights.pth").name == "rf-detr-large"
+    assert infer_preset_from_path("/tmp/nothing.pth") is None
+    assert find_preset("rf-detr-base").patch_size == 14
+
+
+def test_class_head_resize_repeats_rows():
+    m = tiny()
+    w = m.class_embed.weight.detach().clone()
+    m.reinitialize_detection_head(w.shape[0] + 3)
+    assert m.class_embed.weight.shape[0] == w.shape[0] + 3
+    assert torch.equal(m.class_embed.weight[w.shape[0]:], w[:3])
+
+
+def test_large_vitb_p3p5_builds():
+    cfg = config_from_preset("rf-detr-large-vitb", resolution=128, positional_encoding_size=8, group_detr=1,
+                             num_queries=20, num_select=20)
+    m = RFDETR(cfg)
+    m.eval()
+    with torch.no_grad():
+        o = m(torch.randn(1, 3, 128, 128))
+    assert o["pred_boxes"].shape == (1, 20, 4)

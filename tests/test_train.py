@@ -1,0 +1,141 @@
+"""Training step: CPU oracle path (BASELINE config 1 shape, reduced) and the CUDA engine."""
+import copy
+import math
+
+import pytest
+import torch
+
+from mmltk_b200.config import TrainOptions, config_from_preset
+from mmltk_b200.criterion import SetCriterion, pad_targets
+from mmltk_b200.data.synthetic import synthetic_batch
+from mmltk_b200.models import RFDETR
+from mmltk_b200.train.engine import TrainEngine
+from mmltk_b200.train.param_groups import build_param_groups, parameter_lr
+
+
+def test_param_group_lrs_follow_reference_formula():
+    o = TrainOptions()
+    lr = parameter_lr("backbone.0.encoder.encoder.encoder.layer.3.mlp.fc1.weight", o)
+    assert math.isclose(lr, o.lr_encoder * o.encoder_layer_decay ** (13 + 1 - 4) * o.lr_component_decay ** 2)
+    assert math.isclose(parameter_lr("backbone.0.encoder.encoder.embeddings.cls_token", o),
+                        o.lr_encoder * o.encoder_layer_decay ** 14 * o.lr_component_decay ** 2)
+    assert math.isclose(parameter_lr("transformer.decoder.layers.0.linear1.weight", o), o.lr * o.lr_component_decay)
+    assert math.isclose(parameter_lr("class_embed.weight", o), o.lr)
+    m = RFDETR(config_from_preset("rf-detr-nano"))
+    groups, assign = build_param_groups(list(m.named_parameters()), o)
+    wd0 = [g for g in groups if g["weight_decay"] == 0.0]
+    assert all("backbone.0.encoder" in n for g in wd0 for n in g["names"])
+    assert len(assign) == len(list(m.parameters()))
+
+
+def _ia_bce_reference(logits, match_q, labels, src_iou, valid, num_boxes, alpha=0.25):
+    """Literal reference formula with dense pos/neg weight tensors (`detection_ops.cpp:1324-1342`)."""
+    prob = logits.sigmoid()
+    pos_w = torch.zeros_like(logits)
+    neg_w = prob ** 2
+    B = logits.shape[0]
+    for b in range(B):
+        for (q, lab, iou) in zip(match_q[b][valid[b]], labels[b][valid[b]], src_iou[b][valid[b]]):
+            t = (prob[b, q, lab].detach() ** alpha * iou ** (1 - alpha)).clamp(min=0.01)
+            pos_w[b, q, lab] = t
+            neg_w[b, q, lab] = 1 - t
+    return (neg_w * logits - torch.nn.functional.logsigmoid(logits) * (pos_w + neg_w)).sum() / num_boxes
+
+
+def test_ia_bce_decomposition_matches_dense_formula():
+    from mmltk_b200.utils.boxes import aligned_iou, cxcywh_to_xyxy
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-tiny-test", resolution=64)
+    crit = SetCriterion(cfg)
+    B, Q, C, T = 2, 10, 91, 4
+    logits = torch.randn(B, Q, C, requires_grad=True)
+    boxes = torch.cat([torch.rand(B, Q, 2) * 0.6 + 0.2, torch.rand(B, Q, 2) * 0.3 + 0.05], -1)
+    tg = pad_targets([{"boxes": torch.tensor([[0.3, 0.3, 0.2, 0.2], [0.6, 0.5, 0.1, 0.3]]), "labels": torch.tensor([3, 7])},
+                      {"boxes": torch.tensor([[0.5, 0.5, 0.4, 0.4]]), "labels": torch.tensor([1])}], slots=T)
+    match = torch.tensor([[[4, 1, -1, -1]], [[7, -1, -1, -1]]], dtype=torch.int32)  # [B,G=1,T]
+    layer = {"pred_logits": logits, "pred_boxes": boxes}
+    m = crit._gather(layer, match, tg)
+    nb = torch.tensor(3.0)
+    out = crit.loss_labels(layer, m, nb, log=False)["loss_ce"]
+    iou = aligned_iou(cxcywh_to_xyxy(m["src_boxes"]), cxcywh_to_xyxy(m["tgt_boxes"]))
+    ref = _ia_bce_reference(logits, m["q"][:, 0], m["labels"][:, 0], iou[:, 0], m["valid"][:, 0], nb)
+    assert torch.allclose(out, ref, rtol=1e-5, atol=1e-6)
+    g1 = torch.autograd.grad(out, logits)[0]
+    g2 = torch.autograd.grad(ref, logits)[0]
+    assert torch.allclose(g1, g2, rtol=1e-4, atol=1e-7)
+
+
+@pytest.mark.parametrize("branch", ["focal", "varifocal", "position"])
+def test_other_classification_branches_run(branch):
+    torch.manual_seed(0)
+    kw = {"ia_bce_loss": False}
+    if branch == "varifocal":
+        kw["use_varifocal_loss"] = True
+    if branch == "position":
+        kw["use_position_supervised_loss"] = True
+    cfg = config_from_preset("rf-detr-tiny-test", resolution=64, **kw)
+    m = RFDETR(cfg)
+    imgs, tg = synthetic_batch(2, 64, seed=0, kmax=5, slots=5)
+    losses, _ = SetCriterion(cfg)(m(imgs), tg)
+    total = SetCriterion(cfg).weighted(losses)
+    total.backward()
+    assert torch.isfinite(total)
+
+
+def test_cpu_train_steps_reduce_loss():
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-tiny-test", resolution=64)
+    model = RFDETR(cfg)
+    opts = TrainOptions(lr=1e-3, lr_encoder=1e-3, use_ema=True)
+    eng = TrainEngine(model, opts, "cpu", max_targets=5)
+    imgs, tg = synthetic_batch(2, 64, seed=0, kmax=5, slots=5)
+    first = eng.step(imgs, tg).loss
+    for _ in range(15):
+        last = eng.step(imgs, tg).loss
+    assert last < first
+    assert eng.ema_state() is not None
+
+
+@pytest.mark.slow
+def test_nano_cpu_step_baseline_config1():
+    """RF-DETR-Nano, batch 2 @384, fp32 on CPU, seed 0 (one full step)."""
+    torch.manual_seed(0)
+    model = RFDETR(config_from_preset("rf-detr-nano"))
+    eng = TrainEngine(model, TrainOptions(), "cpu", max_targets=10)
+    imgs, tg = synthetic_batch(2, 384, seed=0, kmax=10, slots=10)
+    r = eng.step(imgs, tg)
+    assert math.isfinite(r.loss)
+
+
+@pytest.mark.gpu
+def test_cuda_engine_eager_and_graph(cuda_device):
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-medium", group_detr=3, dec_layers=2, resolution=256,
+                             positional_encoding_size=16)
+    model = RFDETR(cfg)
+    eng = TrainEngine(model, TrainOptions(use_ema=True, cuda_graph=True), cuda_device, max_targets=10)
+    eng.bind_static_inputs(2, 3, 256, 256)
+    imgs, tg = synthetic_batch(2, 256, seed=0, kmax=10, slots=10, dtype=torch.bfloat16)
+    imgs, tg = imgs.to(cuda_device), tg.to(cuda_device)
+    losses = [eng.step(imgs, tg).loss for _ in range(8)]  # steps 4.. replay the captured graph
+    assert eng.graph is not None
+    assert all(math.isfinite(l) for l in losses)
+    assert losses[-1] < losses[0]
+    eng.release_graph()
+
+
+@pytest.mark.gpu
+def test_cuda_losses_match_cpu_oracle(cuda_device):
+    """Same weights and batch: CUDA bf16 forward + losses vs the CPU fp32 oracle."""
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-medium", group_detr=2, dec_layers=2, resolution=256,
+                             positional_encoding_size=16)
+    model = RFDETR(cfg).train()
+    gpu = copy.deepcopy(model).to(cuda_device, torch.bfloat16).train()
+    imgs, tg = synthetic_batch(2, 256, seed=1, kmax=8, slots=8)
+    crit = SetCriterion(cfg)
+    lc, _ = crit(model(imgs), tg)
+    lg, _ = crit(gpu(imgs.to(cuda_device, torch.bfloat16)), tg.to(cuda_device))
+    for k in ("loss_bbox", "loss_giou", "loss_ce"):
+        a, b = float(lc[k]), float(lg[k])
+        assert abs(a - b) / max(abs(a), 1e-3) < 0.1, (k, a, b)
