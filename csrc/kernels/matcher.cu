@@ -56,7 +56,10 @@ __global__ void __launch_bounds__(128) matcher_cost_kernel(MatcherLayers lp, con
     const int l = blockIdx.x / (qtiles * B);
     const int nt = min(counts[b], T);
     for (int i = threadIdx.x; i < nt * 4; i += blockDim.x) sbox[i] = tboxes[static_cast<int64_t>(b) * T * 4 + i];
-    for (int i = threadIdx.x; i < nt; i += blockDim.x) slab[i] = static_cast<int>(labels[static_cast<int64_t>(b) * T + i]);
+    for (int i = threadIdx.x; i < nt; i += blockDim.x) {
+        const int64_t lab = labels[static_cast<int64_t>(b) * T + i];
+        slab[i] = static_cast<int>(lab < 0 ? 0 : (lab >= C ? C - 1 : lab));  // labels are validated on the host
+    }
     __syncthreads();
     const int q = tile * blockDim.x + threadIdx.x;
     if (q >= Q) return;
@@ -161,9 +164,14 @@ __global__ void __launch_bounds__(128) lsap_kernel(const float* __restrict__ cos
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-        fmax = fmax > __shfl_xor_sync(0xffffffffu, fmax, o) ? fmax : __shfl_xor_sync(0xffffffffu, fmax, o);
-        amax = amax > __shfl_xor_sync(0xffffffffu, amax, o) ? amax : __shfl_xor_sync(0xffffffffu, amax, o);
-        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+        // every lane executes every shuffle exactly once (a shuffle inside a
+        // conditional expression would desynchronise the warp)
+        const double of = __shfl_xor_sync(0xffffffffu, fmax, o);
+        const double oa = __shfl_xor_sync(0xffffffffu, amax, o);
+        const int ob = __shfl_xor_sync(0xffffffffu, bad, o);
+        fmax = fmax > of ? fmax : of;
+        amax = amax > oa ? amax : oa;
+        bad |= ob;
     }
     const double flt_max = 3.4028234663852886e38;
     double rep = flt_max;
@@ -245,11 +253,23 @@ __global__ void __launch_bounds__(128) lsap_kernel(const float* __restrict__ cos
                 if (lane == 0) atomicExch(status, 2);
                 return;
             }
+            if (best_it < 0 || best_it >= n_rem) {  // self-check: record and stop, never touch memory
+                if (lane == 0) atomicExch(status, 3);
+                return;
+            }
             const int j = s.rem[best_it];
+            if (j < 0 || j >= Qg) {
+                if (lane == 0) atomicExch(status, 4);
+                return;
+            }
             if (s.row4col[j] < 0) {
                 sink = j;
             } else {
                 i = s.row4col[j];
+                if (i < 0 || i >= nt) {
+                    if (lane == 0) atomicExch(status, 5);
+                    return;
+                }
             }
             __syncwarp();
             if (lane == 0) {
@@ -262,14 +282,29 @@ __global__ void __launch_bounds__(128) lsap_kernel(const float* __restrict__ cos
         // dual updates
         if (lane == 0) s.u[cur] += min_val;
         for (int t = lane; t < nt; t += 32)
-            if (s.sr[t] && t != cur) s.u[t] += min_val - s.spc[s.col4row[t]];
+            if (s.sr[t] && t != cur) {
+                const int c4 = s.col4row[t];
+                if (c4 < 0 || c4 >= Qg) {
+                    atomicExch(status, 8);
+                    continue;
+                }
+                s.u[t] += min_val - s.spc[c4];
+            }
         for (int q = lane; q < Qg; q += 32)
             if (s.sc[q]) s.v[q] -= min_val - s.spc[q];
         __syncwarp();
         if (lane == 0) {
             int j = sink;
             for (int guard = 0; guard <= nt; ++guard) {
+                if (j < 0 || j >= Qg) {
+                    atomicExch(status, 6);
+                    break;
+                }
                 const int r = s.path[j];
+                if (r < 0 || r >= nt) {
+                    atomicExch(status, 7);
+                    break;
+                }
                 s.row4col[j] = r;
                 const int prev = s.col4row[r];
                 s.col4row[r] = j;
