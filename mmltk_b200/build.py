@@ -48,8 +48,8 @@ def _cutlass_include():
 def extensions():
     from torch.utils.cpp_extension import CppExtension, CUDAExtension
 
-    kern_src = sorted(glob.glob(os.path.join("csrc", "kernels", "*.cu")) +
-                      glob.glob(os.path.join("csrc", "kernels", "*.cpp")))
+    kern_src = sorted(p for p in glob.glob(os.path.join("csrc", "kernels", "*.cu")) +
+                      glob.glob(os.path.join("csrc", "kernels", "*.cpp")) if "noalloc" not in p)
     host_src = sorted(glob.glob(os.path.join("csrc", "host", "*.cpp")))
     inc = [os.path.join(ROOT, "csrc", "include"), os.path.join(ROOT, "csrc", "kernels")]
     return [
@@ -59,6 +59,32 @@ def extensions():
                       extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
                       libraries=["cuda"] if False else []),
     ]
+
+
+NOALLOC_LIB = os.path.join(ROOT, "mmltk_b200", "libmmltk_noalloc.so")
+
+
+def build_noalloc(verbose: bool = False) -> str:
+    """Plain C-ABI library with the allocation-free MSDeformAttn backward
+    (``mmltk_msda_bwd_noalloc``, see csrc/kernels/msda_noalloc.h).  It is kept
+    out of the torch extension so its fixed scratch array is only reserved by
+    processes that load it."""
+    import subprocess
+
+    srcs = [os.path.join(ROOT, "csrc", "kernels", f) for f in ("msda.cu", "msda_noalloc.cu")]
+    newest = max(os.path.getmtime(p) for p in srcs + [os.path.join(ROOT, "csrc", "kernels", "launch_api.h"),
+                                                       os.path.join(ROOT, "csrc", "kernels", "common.cuh"),
+                                                       os.path.join(ROOT, "csrc", "kernels", "msda_noalloc.h")])
+    if os.path.exists(NOALLOC_LIB) and os.path.getmtime(NOALLOC_LIB) >= newest:
+        return NOALLOC_LIB
+    nvcc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+    cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17", "-shared",
+           "-Xcompiler", "-fPIC", "-cudart", "shared", "-I", os.path.join(ROOT, "csrc", "kernels"), *srcs,
+           "-o", NOALLOC_LIB]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    return NOALLOC_LIB
 
 
 def build(verbose: bool = False, jobs: int | None = None) -> None:
@@ -77,6 +103,7 @@ def build(verbose: bool = False, jobs: int | None = None) -> None:
               script_args=args)
     finally:
         os.chdir(cwd)
+    build_noalloc(verbose)
 
 
 if __name__ == "__main__":
