@@ -50,6 +50,15 @@ cudaError_t launch_lsap(const float* cost, const int32_t* counts, int32_t* match
 // ---------------------------------------------------------------- elementwise
 cudaError_t launch_cast_f32(DType dst_t, const float* src, void* dst, int64_t n, cudaStream_t st);
 
+// mode 0: out = colsum(x); mode 1: gout = x * gamma (row-broadcast) and out = colsum(x * pre).
+// part: fp32 scratch [colsum_parts(M, N), N]; N % 8 == 0.
+int colsum_parts(int64_t M, int N);
+cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const void* pre, const void* gamma,
+                          void* gout, int64_t M, int N, float* part, void* out, cudaStream_t st);
+cudaError_t launch_reduce_partials(DType out_t, const float* part, int nparts, int N, void* out, cudaStream_t st);
+// act: 1 = GELU(erf), 2 = ReLU.  n % 8 == 0.
+cudaError_t launch_act_bwd(DType t, const void* gy, const void* pre, void* gx, int64_t n, int act, cudaStream_t st);
+
 // ---------------------------------------------------------------- losses
 int dense_neg_blocks(int64_t n);
 // partials: fp32 [dense_neg_blocks(n)], counter: zeroed uint32 (reset by the kernel), out: fp32 [1]

@@ -227,9 +227,9 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
             if (e != cudaSuccess) return e;
             e = cudaGetLastError();
             if (e != cudaSuccess) return e;
-            colsum_partials_kernel<Wt><<<(C + 127) / 128, 128, 0, st>>>(
-                part, part + static_cast<int64_t>(blocks) * C, blocks, C, static_cast<Wt*>(gw), static_cast<Wt*>(gb));
-            return cudaGetLastError();
+            e = launch_reduce_partials(wt, part, blocks, C, gw, st);
+            if (e != cudaSuccess) return e;
+            return launch_reduce_partials(wt, part + static_cast<int64_t>(blocks) * C, blocks, C, gb, st);
         });
     });
 }

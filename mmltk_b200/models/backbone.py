@@ -135,8 +135,8 @@ class SelfAttention(nn.Module):
         N, L, C = x.shape
         H = self.heads
         qkv = ops.linear(x, self.qkv_weight, self.qkv_bias)  # [N, L, 3C]
-        qkv = qkv.view(N, L, 3, H, C // H).permute(2, 0, 3, 1, 4)  # [3, N, H, L, D]
-        o = ops.attention(qkv[0], qkv[1], qkv[2])  # [N, H, L, D]
+        q, k, v = qkv.view(N, L, 3, H, C // H).permute(2, 0, 3, 1, 4).unbind(0)  # [N, H, L, D] each
+        o = ops.attention(q, k, v)  # [N, H, L, D]
         return o.transpose(1, 2).reshape(N, L, C)
 
 

@@ -114,8 +114,9 @@ class RFDETR(nn.Module):
         else:
             boxes = (delta + refs).sigmoid()
         L = hs.shape[0]
-        out = {"pred_logits": logits[L - 1], "pred_boxes": boxes[L - 1],
-               "aux_outputs": [{"pred_logits": logits[i], "pred_boxes": boxes[i]} for i in range(L - 1)]}
+        lg, bx = logits.unbind(0), boxes.unbind(0)   # one backward node per tensor (no per-layer zero fill)
+        out = {"pred_logits": lg[L - 1], "pred_boxes": bx[L - 1],
+               "aux_outputs": [{"pred_logits": lg[i], "pred_boxes": bx[i]} for i in range(L - 1)]}
         groups = max(1, cfg.group_detr) if training else 1
         if cfg.two_stage and "enc_memory" in t:
             enc_logits = self.transformer.encoder_class_logits(t["enc_memory"], groups)

@@ -1,11 +1,17 @@
 """Dense layers with fused epilogues.
 
-``linear(x, w, b, act)``            y = act(x W^T + b)            act in {None, "gelu", "relu"}
-``linear_scale_residual(x, w, b, gamma, res)``  y = res + gamma * (x W^T + b)   (ViT LayerScale + residual)
+``linear(x, w, b, act)``                       y = act(x W^T + b)       act in {None, "gelu", "relu"}
+``linear_scale_residual(x, w, b, gamma, res)`` y = res + gamma * (x W^T + b)   (ViT LayerScale + residual)
 
-On CUDA with bf16 operands these run the framework's tcgen05/TMEM GEMM
-(``gemm_tc``: TMA-fed shared-memory tiles, accumulators in tensor memory, the
-epilogue applied on the tcgen05.ld read-back).  The CPU path is the fp32 oracle.
+CUDA (bf16): one autograd node per layer.  The products run on the tensor
+cores through ``gemm`` (``mmltk_b200.ops.gemm``: the framework's tcgen05/TMEM
+kernel where the shape qualifies, cuBLAS otherwise); the memory-bound parts
+are framework kernels: the bias gradient is a single-pass column sum
+(``colsum``), the activation backward and the LayerScale backward
+(``g_pre = gy * gamma`` together with ``g_gamma = colsum(gy * pre)``) are one
+pass each.  This replaces autograd's generic ``AddmmBackward`` whose
+bias-gradient reduction and zero-filled select/slice backwards dominated the
+step profile.  CPU: the plain fp32 definition (the oracle).
 Reference: every `torch::nn::Linear` of `src/rfdetr/layers/model.cpp` (cuBLAS).
 """
 from __future__ import annotations
@@ -16,86 +22,67 @@ import torch
 import torch.nn.functional as F
 
 from ._ext import kernels
+from .gemm import gemm_nt, gemm_nn, gemm_tn
 
-__all__ = ["linear", "linear_scale_residual", "gemm_enabled", "set_gemm_enabled"]
+__all__ = ["linear", "linear_scale_residual", "set_fused_linear"]
 
 _ACTS = {None: 0, "none": 0, "gelu": 1, "relu": 2}
-_state = {"enabled": os.environ.get("MMLTK_TC_GEMM", "1") != "0"}
+_state = {"enabled": os.environ.get("MMLTK_FUSED_LINEAR", "1") != "0"}
 
 
-def gemm_enabled() -> bool:
-    return _state["enabled"]
-
-
-def set_gemm_enabled(flag: bool) -> None:
+def set_fused_linear(flag: bool) -> None:
     _state["enabled"] = bool(flag)
 
 
-def _act(y, act):
-    if act == "gelu":
+def _act(y, act_id):
+    if act_id == 1:
         return F.gelu(y)
-    if act == "relu":
+    if act_id == 2:
         return F.relu(y)
     return y
 
 
-def _tc_ok(x, w):
+def _ok(x, w):
     return (_state["enabled"] and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
-            and x.shape[-1] % 64 == 0 and w.shape[0] % 64 == 0 and hasattr(kernels(), "gemm_tc"))
+            and x.shape[-1] % 8 == 0 and w.shape[0] % 8 == 0)
 
 
-class _LinearTC(torch.autograd.Function):
-    """y = act(x W^T + b) on the tcgen05 GEMM; backward uses the same GEMM with
-    transposed operand descriptors (dX = dY' W, dW = dY'^T X)."""
+def _2d(t, n):
+    t2 = t.reshape(-1, n)
+    return t2 if t2.is_contiguous() else t2.contiguous()
 
+
+class _Linear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, act_id):
         shp = x.shape
-        x2 = x.reshape(-1, shp[-1])
-        if not x2.is_contiguous():
-            x2 = x2.contiguous()
-        k = kernels()
-        if act_id == 0:
-            y = k.gemm_tc(x2, w, b, 0, None, None)
-            pre = None
-        else:
-            # keep the pre-activation for the backward of the activation
-            pre = k.gemm_tc(x2, w, b, 0, None, None)
-            y = k.bias_act(pre, None, act_id)
-        ctx.save_for_backward(x2, w, pre)
-        ctx.act_id = act_id
-        ctx.has_bias = b is not None
-        ctx.shp = shp
+        x2 = _2d(x, shp[-1])
+        pre = gemm_nt(x2, w, b)                   # x W^T + b
+        y = _act(pre, act_id) if act_id else pre
+        ctx.save_for_backward(x2, w, pre if act_id else None)
+        ctx.act_id, ctx.has_bias, ctx.shp = act_id, b is not None, shp
         return y.view(*shp[:-1], w.shape[0])
 
     @staticmethod
     def backward(ctx, gy):
         x2, w, pre = ctx.saved_tensors
         k = kernels()
-        gy2 = gy.reshape(-1, w.shape[0])
-        if not gy2.is_contiguous():
-            gy2 = gy2.contiguous()
-        if ctx.act_id != 0:
-            gy2 = k.act_bwd(gy2, pre, ctx.act_id)
-        gx = k.gemm_tc_nn(gy2, w)              # [M,N] x [N,K] -> [M,K]
-        gw = k.gemm_tc_tn(gy2, x2)             # [M,N]^T x [M,K] -> [N,K]
-        gb = k.colsum(gy2) if ctx.has_bias else None
-        return gx.view(ctx.shp), gw, gb, None
+        g = _2d(gy, w.shape[0])
+        if ctx.act_id:
+            g = k.act_bwd(g, pre, ctx.act_id)
+        gx = gemm_nn(g, w) if ctx.needs_input_grad[0] else None
+        gw = gemm_tn(g, x2) if ctx.needs_input_grad[1] else None
+        gb = k.colsum(g) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        return (None if gx is None else gx.view(ctx.shp)), gw, gb, None
 
 
-class _LinearScaleResidualTC(torch.autograd.Function):
+class _LinearScaleResidual(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, gamma, res):
         shp = x.shape
-        x2 = x.reshape(-1, shp[-1])
-        if not x2.is_contiguous():
-            x2 = x2.contiguous()
-        r2 = res.reshape(-1, w.shape[0])
-        if not r2.is_contiguous():
-            r2 = r2.contiguous()
-        k = kernels()
-        pre = k.gemm_tc(x2, w, b, 0, None, None)
-        y = k.scale_residual(pre, gamma, r2)
+        x2 = _2d(x, shp[-1])
+        pre = gemm_nt(x2, w, b)
+        y = torch.addcmul(res.reshape(pre.shape), pre, gamma.to(pre.dtype))
         ctx.save_for_backward(x2, w, gamma, pre)
         ctx.shp = shp
         return y.view(*shp[:-1], w.shape[0])
@@ -104,23 +91,21 @@ class _LinearScaleResidualTC(torch.autograd.Function):
     def backward(ctx, gy):
         x2, w, gamma, pre = ctx.saved_tensors
         k = kernels()
-        gy2 = gy.reshape(-1, w.shape[0])
-        if not gy2.is_contiguous():
-            gy2 = gy2.contiguous()
-        g_pre, g_gamma = k.scale_bwd(gy2, pre, gamma)
-        gx = k.gemm_tc_nn(g_pre, w)
-        gw = k.gemm_tc_tn(g_pre, x2)
+        g = _2d(gy, w.shape[0])
+        g_pre, g_gamma = k.scale_bwd(g, pre, gamma)
+        gx = gemm_nn(g_pre, w)
+        gw = gemm_tn(g_pre, x2)
         gb = k.colsum(g_pre)
         return gx.view(ctx.shp), gw, gb, g_gamma, gy
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, b=None, act=None) -> torch.Tensor:
-    if _tc_ok(x, w):
-        return _LinearTC.apply(x, w, b, _ACTS[act])
-    return _act(F.linear(x, w.to(x.dtype), None if b is None else b.to(x.dtype)), act)
+    if _ok(x, w):
+        return _Linear.apply(x, w, b, _ACTS[act])
+    return _act(F.linear(x, w.to(x.dtype), None if b is None else b.to(x.dtype)), _ACTS[act])
 
 
 def linear_scale_residual(x, w, b, gamma, res):
-    if _tc_ok(x, w):
-        return _LinearScaleResidualTC.apply(x, w, b, gamma, res)
+    if _ok(x, w) and gamma.dtype == x.dtype:
+        return _LinearScaleResidual.apply(x, w, b, gamma, res)
     return res + gamma.to(x.dtype) * F.linear(x, w.to(x.dtype), b.to(x.dtype))

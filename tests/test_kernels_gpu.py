@@ -183,3 +183,49 @@ def test_fused_adamw_ema_matches_torch(cuda_device):
         got_e = ema[off[i]:off[i] + p.numel()].cpu().view(p.shape)
         assert torch.allclose(got_e, emar[i], atol=1e-5, rtol=1e-4)
     assert int(flags[0].item()) == 0
+
+
+@pytest.mark.parametrize("act", [None, "gelu", "relu"])
+def test_fused_linear_matches_fp32(cuda_device, act):
+    torch.manual_seed(0)
+    M, K, N = 300, 384, 256
+    bf = lambda t: t.to(torch.bfloat16).float()  # reference sees the same rounded inputs
+    x = bf(torch.randn(M, K) * 0.5)
+    w = bf(torch.randn(N, K) * 0.05)
+    b = bf(torch.randn(N) * 0.1)
+    gy = bf(torch.randn(M, N))
+    xr, wr, br = (t.clone().requires_grad_() for t in (x, w, b))
+    yr = torch.nn.functional.linear(xr, wr, br)
+    yr = {None: yr, "gelu": torch.nn.functional.gelu(yr), "relu": torch.relu(yr)}[act]
+    yr.backward(gy)
+    xd, wd, bd = (t.to(cuda_device, torch.bfloat16).requires_grad_() for t in (x, w, b))
+    yd = ops.linear(xd, wd, bd, act=act)
+    yd.backward(gy.to(cuda_device, torch.bfloat16))
+    assert _rel(yd.cpu(), yr) < 2e-2
+    for a, r in ((xd, xr), (wd, wr), (bd, br)):
+        assert _rel(a.grad.cpu(), r.grad) < 3e-2
+
+
+def test_linear_scale_residual_matches_fp32(cuda_device):
+    torch.manual_seed(0)
+    M, K, N = 257 * 4, 384, 384
+    x, res = torch.randn(M, K), torch.randn(M, N)
+    w, b, gamma = torch.randn(N, K) * 0.05, torch.randn(N) * 0.1, torch.rand(N) + 0.5
+    gy = torch.randn(M, N)
+    ins = [t.clone().requires_grad_() for t in (x, w, b, gamma, res)]
+    yr = ins[4] + ins[3] * torch.nn.functional.linear(ins[0], ins[1], ins[2])
+    yr.backward(gy)
+    dins = [t.to(cuda_device, torch.bfloat16).requires_grad_() for t in (x, w, b, gamma, res)]
+    yd = ops.linear_scale_residual(*dins)
+    yd.backward(gy.to(cuda_device, torch.bfloat16))
+    assert _rel(yd.cpu(), yr) < 2e-2
+    for a, r in zip(dins, ins):
+        assert _rel(a.grad.cpu(), r.grad) < 3e-2
+
+
+def test_colsum(cuda_device):
+    for (M, N) in [(1, 8), (10400, 384), (777, 1536), (31200, 256), (5, 4096)]:
+        x = torch.randn(M, N, device=cuda_device).to(torch.bfloat16)
+        got = kernels().colsum(x, torch.float32)
+        ref = x.float().sum(0)
+        assert (got - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
