@@ -1,0 +1,336 @@
+// Fused data-parallel gradient step over NVSwitch peer memory.
+//
+// Replaces the reference's `allreduce_coalesced` of every fp32 gradient after
+// backward followed by a replicated `clip_grad_norm_` + fused AdamW + EMA
+// (`src/rfdetr/training/train.cpp:876-887,1389-1410,2287-2344`).
+//
+// Every rank owns one contiguous shard of the flat parameter space.  Two
+// kernels per step, both reading and writing other GPUs' memory directly
+// (CUDA IPC mappings, 16-byte P2P loads and 8-byte P2P stores; no TMA and no
+// multicast):
+//
+//   ddp_rs_kernel      barrier "gradients ready" -> reduce-scatter: sum the
+//                      shard of every rank's bf16 gradient buffer in fp32
+//                      (fixed rank order) into a local fp32 shard, plus the
+//                      shard's sum of squares, published to every peer;
+//   ddp_update_kernel  wait for every rank's sum of squares -> global L2 norm
+//                      of the averaged gradient -> clip -> AdamW on the fp32
+//                      master shard -> EMA shard update -> all-gather: write
+//                      the new bf16 parameters into every rank's parameter
+//                      buffer -> barrier "parameters delivered".
+//
+// Flags carry a per-step epoch (incremented on the device at the end of the
+// update kernel), so the two kernels can be replayed from a CUDA graph
+// without any host involvement.  Every wait is bounded: after
+// `spin_limit` polls a wait records an error code in `status` (device memory
+// the host reads once per step) and the kernel returns instead of hanging.
+#include "common.cuh"
+#include "ddp_fused.h"
+#include "optim.cuh"
+
+namespace mmltk {
+
+namespace {
+
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// 16-byte load of another GPU's memory, coherent at system scope (never served
+// from a stale cache line of an earlier step)
+__device__ __forceinline__ uint4 ld_peer16(const void* p) {
+    uint4 r;
+    asm volatile("ld.relaxed.sys.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(uint4 raw, float* f) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 t = __bfloat1622float2(h[i]);
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+
+// Bounded wait until *flag >= want (epochs only grow).  Returns false on timeout.
+__device__ bool wait_u32(const uint32_t* flag, uint32_t want, long long spin_limit) {
+    for (long long it = 0; it < spin_limit; ++it) {
+        if (static_cast<int32_t>(ld_acquire_u32(flag) - want) >= 0) return true;
+        __nanosleep(it < 64 ? 32 : 256);
+    }
+    return false;
+}
+
+__device__ void record_error(int* status, int code) { atomicCAS(status, 0, code); }
+
+// Grid-wide "last CTA" election with a self-resetting ticket.
+__device__ bool last_cta(unsigned int* ticket) {
+    __shared__ bool is_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned int t = atomicAdd(ticket, 1u);
+        is_last = (t == gridDim.x - 1);
+        if (is_last) *ticket = 0u;
+    }
+    __syncthreads();
+    return is_last;
+}
+
+__global__ void __launch_bounds__(256) ddp_rs_kernel(DdpPeers peers, DdpState st, int64_t shard_off, int64_t shard_len,
+                                                     float* __restrict__ gshard, float* __restrict__ partials) {
+    const uint32_t epoch = *st.epoch;
+    const int world = peers.world, rank = peers.rank;
+    // ---- barrier: my gradients are complete; wait for everybody's
+    if (blockIdx.x == 0 && threadIdx.x < world) {
+        __threadfence_system();
+        st_release_u32(peers.flags[threadIdx.x] + kFlagReady + rank, epoch);
+    }
+    __shared__ int ok;
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    if (threadIdx.x < world) {
+        if (!wait_u32(st.flags_local + kFlagReady + threadIdx.x, epoch, st.spin_limit)) {
+            record_error(st.status, kErrTimeoutReady);
+            ok = 0;
+        }
+    }
+    __syncthreads();
+    if (!ok) return;
+    // ---- reduce-scatter of this rank's shard, fp32 accumulation in rank order
+    float ss = 0.f;
+    const int64_t nvec = shard_len / 8;
+    for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
+         v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        const int64_t e = shard_off + 8 * v;
+        for (int j = 0; j < world; ++j) {
+            float f[8];
+            bf16x8_to_f32(ld_peer16(peers.grad[j] + e), f);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[c] += f[c];
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) ss += acc[c] * acc[c];
+        store8(gshard + 8 * v, acc);
+    }
+    __shared__ float red[8];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < (blockDim.x >> 5); ++w) t += red[w];
+        partials[blockIdx.x] = t;
+    }
+    // ---- the last CTA publishes the shard's sum of squares to every rank
+    if (last_cta(st.ticket)) {
+        if (threadIdx.x < 32) {
+            float t = 0.f;
+            for (int i = threadIdx.x; i < static_cast<int>(gridDim.x); i += 32) t += partials[i];
+            t = warp_sum(t);
+            if (threadIdx.x < world) {
+                const unsigned long long packed =
+                    (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(t);
+                st_release_u64(reinterpret_cast<unsigned long long*>(peers.flags[threadIdx.x] + kFlagNorm) + rank,
+                               packed);
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) ddp_update_kernel(DdpPeers peers, DdpState st, int64_t shard_off,
+                                                         const ChunkDesc* __restrict__ chunks, int nchunks,
+                                                         const float* __restrict__ gshard,
+                                                         float* __restrict__ master, float* __restrict__ m,
+                                                         float* __restrict__ v, float* __restrict__ ema,
+                                                         const GroupHyper* __restrict__ groups,
+                                                         const StepScalars* __restrict__ sc, int* __restrict__ flags) {
+    const uint32_t epoch = *st.epoch;
+    const int world = peers.world, rank = peers.rank;
+    __shared__ float s_sumsq;
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        ok = 1;
+        s_sumsq = 0.f;
+    }
+    __syncthreads();
+    // ---- every rank's shard sum of squares (fixed order -> same norm on every rank)
+    if (threadIdx.x == 0) {
+        float tot = 0.f;
+        for (int j = 0; j < world; ++j) {
+            const unsigned long long* slot =
+                reinterpret_cast<const unsigned long long*>(st.flags_local + kFlagNorm) + j;
+            unsigned long long val = 0;
+            bool got = false;
+            for (long long it = 0; it < st.spin_limit; ++it) {
+                val = ld_acquire_u64(slot);
+                if (static_cast<uint32_t>(val >> 32) == epoch) {
+                    got = true;
+                    break;
+                }
+                __nanosleep(it < 64 ? 32 : 256);
+            }
+            if (!got) {
+                record_error(st.status, kErrTimeoutNorm);
+                ok = 0;
+                break;
+            }
+            tot += __uint_as_float(static_cast<uint32_t>(val & 0xffffffffu));
+        }
+        s_sumsq = tot;
+    }
+    __syncthreads();
+    if (!ok) return;
+    const float inv_world = sc->inv_world > 0.f ? sc->inv_world : 1.f;
+    const float norm = sqrtf(s_sumsq) * inv_world;
+    const bool finite = isfinite(norm);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        if (!finite) flags[0] = 1;
+        reinterpret_cast<float*>(flags)[1] = norm;
+    }
+    float clip = 1.f;
+    if (sc->max_norm > 0.f && finite) clip = fminf(1.f, sc->max_norm / (norm + 1e-6f));
+    const float gs = clip * inv_world;
+    const float b1 = sc->beta1, b2 = sc->beta2, eps = sc->eps;
+    const float inv_bc1 = 1.f / sc->bias_corr1, inv_sqrt_bc2 = rsqrtf(sc->bias_corr2);
+    const float ema_d = sc->ema_decay;
+    const bool do_ema = ema != nullptr && sc->ema_enabled != 0.f;
+    // ---- sharded AdamW + EMA, then all-gather of the bf16 parameters
+    for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        const ChunkDesc cd = chunks[c];  // offsets are shard-local
+        const GroupHyper gh = groups[cd.group];
+        const float lr = gh.lr * sc->lr_scale;
+        const float decay = 1.f - lr * gh.weight_decay;
+        for (int64_t i = cd.offset + 4 * threadIdx.x; i < cd.offset + cd.length; i += 4 * blockDim.x) {
+            float4 p = *reinterpret_cast<float4*>(master + i);
+            if (finite) {
+                const float4 g4 = *reinterpret_cast<const float4*>(gshard + i);
+                float4 mm = *reinterpret_cast<float4*>(m + i);
+                float4 vv = *reinterpret_cast<float4*>(v + i);
+                const float gv[4] = {g4.x * gs, g4.y * gs, g4.z * gs, g4.w * gs};
+                float* pp = &p.x;
+                float* mp = &mm.x;
+                float* vp = &vv.x;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    mp[k] = b1 * mp[k] + (1.f - b1) * gv[k];
+                    vp[k] = b2 * vp[k] + (1.f - b2) * gv[k] * gv[k];
+                    const float denom = sqrtf(vp[k]) * inv_sqrt_bc2 + eps;
+                    pp[k] = pp[k] * decay - lr * inv_bc1 * mp[k] / denom;
+                }
+                *reinterpret_cast<float4*>(master + i) = p;
+                *reinterpret_cast<float4*>(m + i) = mm;
+                *reinterpret_cast<float4*>(v + i) = vv;
+                if (do_ema) {
+                    float4 e = *reinterpret_cast<float4*>(ema + i);
+                    e.x = ema_d * e.x + (1.f - ema_d) * p.x;
+                    e.y = ema_d * e.y + (1.f - ema_d) * p.y;
+                    e.z = ema_d * e.z + (1.f - ema_d) * p.z;
+                    e.w = ema_d * e.w + (1.f - ema_d) * p.w;
+                    *reinterpret_cast<float4*>(ema + i) = e;
+                }
+            }
+            // all-gather: the same 8 bytes to every rank's parameter buffer
+            __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
+            uint2 raw;
+            raw.x = *reinterpret_cast<uint32_t*>(&lo);
+            raw.y = *reinterpret_cast<uint32_t*>(&hi);
+            for (int j = 0; j < world; ++j)
+                *reinterpret_cast<uint2*>(peers.param[j] + shard_off + i) = raw;
+        }
+    }
+    // ---- completion: once every CTA's stores are out, tell every rank, wait for all
+    __threadfence_system();
+    if (last_cta(st.ticket)) {
+        __threadfence_system();
+        if (threadIdx.x < world) st_release_u32(peers.flags[threadIdx.x] + kFlagDone + rank, epoch);
+        __syncthreads();
+        if (threadIdx.x < world) {
+            if (!wait_u32(st.flags_local + kFlagDone + threadIdx.x, epoch, st.spin_limit))
+                record_error(st.status, kErrTimeoutDone);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) *st.epoch = epoch + 1;  // next step (stream order publishes it)
+    }
+}
+
+// Sum of a small fp32 vector over all ranks (num_boxes and other per-step
+// scalars), one CTA, no host involvement.  Uses its own flag region.
+__global__ void small_allreduce_kernel(DdpPeers peers, DdpState st, float* __restrict__ data, int n) {
+    const uint32_t epoch = *st.small_epoch;
+    const int world = peers.world, rank = peers.rank;
+    // slots are double-buffered by epoch parity: a rank can only write the
+    // buffer of epoch e+2 after every rank signalled e+1, i.e. finished reading e
+    const int base = (epoch & 1u) * kDdpMaxWorld * kSmallMax;
+    // publish my values to every rank's slot [rank]
+    for (int i = threadIdx.x; i < n * world; i += blockDim.x) {
+        const int j = i / n, k = i % n;
+        peers.small[j][base + rank * kSmallMax + k] = data[k];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < world) st_release_u32(peers.flags[threadIdx.x] + kFlagSmall + rank, epoch);
+    __shared__ int ok;
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    if (threadIdx.x < world && !wait_u32(st.flags_local + kFlagSmall + threadIdx.x, epoch, st.spin_limit)) {
+        record_error(st.status, kErrTimeoutSmall);
+        ok = 0;
+    }
+    __syncthreads();
+    if (ok) {
+        for (int k = threadIdx.x; k < n; k += blockDim.x) {
+            float s = 0.f;
+            for (int j = 0; j < world; ++j) s += st.small_local[base + j * kSmallMax + k];
+            data[k] = s;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *st.small_epoch = epoch + 1;
+}
+
+}  // namespace
+
+int ddp_rs_blocks() { return num_sms() * 2; }
+
+cudaError_t launch_ddp_rs(const DdpPeers& peers, const DdpState& st, int64_t shard_off, int64_t shard_len,
+                          float* gshard, float* partials, cudaStream_t s) {
+    if (shard_len % 8 != 0 || peers.world < 1 || peers.world > kDdpMaxWorld) return cudaErrorInvalidValue;
+    ddp_rs_kernel<<<ddp_rs_blocks(), 256, 0, s>>>(peers, st, shard_off, shard_len, gshard, partials);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ddp_update(const DdpPeers& peers, const DdpState& st, int64_t shard_off, const ChunkDesc* chunks,
+                              int nchunks, const float* gshard, float* master, float* m, float* v, float* ema,
+                              const GroupHyper* groups, const StepScalars* sc, int* flags, cudaStream_t s) {
+    const int blocks = std::max(1, std::min(nchunks, num_sms() * 4));
+    ddp_update_kernel<<<blocks, 256, 0, s>>>(peers, st, shard_off, chunks, nchunks, gshard, master, m, v, ema, groups,
+                                             sc, flags);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_small_allreduce(const DdpPeers& peers, const DdpState& st, float* data, int n, cudaStream_t s) {
+    if (n < 1 || n > kSmallMax) return cudaErrorInvalidValue;
+    small_allreduce_kernel<<<1, 128, 0, s>>>(peers, st, data, n);
+    return cudaGetLastError();
+}
+
+}  // namespace mmltk

@@ -1,0 +1,58 @@
+// Shared layout of the fused data-parallel step (kernels + host wrappers).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "optim.cuh"
+
+namespace mmltk {
+
+constexpr int kDdpMaxWorld = 16;
+constexpr int kSmallMax = 16;  // floats per rank in the small all-reduce
+
+// Flag words (uint32) inside each rank's peer-visible flag buffer.
+constexpr int kFlagReady = 0;                       // [world] gradients ready (epoch)
+constexpr int kFlagDone = kFlagReady + kDdpMaxWorld;  // [world] parameters delivered (epoch)
+constexpr int kFlagSmall = kFlagDone + kDdpMaxWorld;  // [world] small all-reduce (epoch)
+constexpr int kFlagNorm = 64;                        // [world] u64 (epoch << 32 | sumsq bits), 8-byte aligned
+constexpr int kFlagWords = kFlagNorm + 2 * kDdpMaxWorld;
+
+// Error codes written into DdpState::status.
+constexpr int kErrTimeoutReady = 1;
+constexpr int kErrTimeoutNorm = 2;
+constexpr int kErrTimeoutDone = 3;
+constexpr int kErrTimeoutSmall = 4;
+
+// Pointers into every rank's peer-visible buffers (index = rank).
+struct DdpPeers {
+    const __nv_bfloat16* grad[kDdpMaxWorld];
+    __nv_bfloat16* param[kDdpMaxWorld];
+    uint32_t* flags[kDdpMaxWorld];
+    float* small[kDdpMaxWorld];
+    int world;
+    int rank;
+};
+
+// This rank's local control words.
+struct DdpState {
+    uint32_t* flags_local;       // my flag buffer (peers write into it)
+    float* small_local;          // my small all-reduce slots [world * kSmallMax]
+    uint32_t* epoch;             // step epoch (device), starts at 1
+    uint32_t* small_epoch;       // small all-reduce epoch (device), starts at 1
+    unsigned int* ticket;        // zeroed grid ticket
+    int* status;                 // 0 = ok, else kErrTimeout*
+    long long spin_limit;        // polls before a wait gives up
+};
+
+int ddp_rs_blocks();
+cudaError_t launch_ddp_rs(const DdpPeers& peers, const DdpState& st, int64_t shard_off, int64_t shard_len,
+                          float* gshard, float* partials, cudaStream_t s);
+cudaError_t launch_ddp_update(const DdpPeers& peers, const DdpState& st, int64_t shard_off, const ChunkDesc* chunks,
+                              int nchunks, const float* gshard, float* master, float* m, float* v, float* ema,
+                              const GroupHyper* groups, const StepScalars* sc, int* flags, cudaStream_t s);
+cudaError_t launch_small_allreduce(const DdpPeers& peers, const DdpState& st, float* data, int n, cudaStream_t s);
+
+}  // namespace mmltk

@@ -93,6 +93,7 @@ void register_more_ops(pybind11::module& m) {
     m.def("colsum", &colsum, py::arg("x"), py::arg("out_dtype") = py::none());
     m.def("scale_bwd", &scale_bwd);
     m.def("act_bwd", &act_bwd);
+    register_ddp_ops(m);
 }
 
 }  // namespace mmltk

@@ -92,7 +92,8 @@ class TrainEngine:
         fp32 = {n: p.detach().float().clone() for n, p in named}
         self.model.to(self.device, torch.bfloat16)
         named_dev = [(n, p) for n, p in self.model.named_parameters() if p.requires_grad]
-        self.flat = FlatParams(named_dev, assign, self.device, torch.bfloat16, pad_to=pad)
+        alloc = getattr(self.grad_sync, "alloc", None) if self.grad_sync is not None else None
+        self.flat = FlatParams(named_dev, assign, self.device, torch.bfloat16, pad_to=pad, alloc=alloc)
         master = torch.zeros(self.flat.total, dtype=torch.float32, device=self.device)
         for i, n in enumerate(self.flat.names):
             o, c = self.flat.offsets[i], self.flat.numels[i]
@@ -191,7 +192,12 @@ class TrainEngine:
             return StepResult(total, losses, None, None)
         self.readback[0].copy_(total, non_blocking=True)
         self.readback[1:3].copy_(self.flags.view(torch.float32), non_blocking=True)
+        sync_status = getattr(self.grad_sync, "status_tensor", None)
+        if sync_status is not None:
+            self.readback[3:4].copy_(sync_status().view(torch.float32), non_blocking=True)
         torch.cuda.current_stream().synchronize()
+        if sync_status is not None:
+            self.grad_sync.check(self.flags_host_bits(self.readback[3]))
         loss = float(self.readback[0])
         nonfinite = int(self.flags_host_bits(self.readback[1]))
         norm = float(self.readback[2])

@@ -27,7 +27,7 @@ def _round(n: int, a: int = ALIGN) -> int:
 
 class FlatParams:
     def __init__(self, named_params: Sequence[Tuple[str, torch.nn.Parameter]], group_of: Sequence[int],
-                 device, dtype=torch.bfloat16, pad_to: int = 1):
+                 device, dtype=torch.bfloat16, pad_to: int = 1, alloc=None):
         # order parameters by group so every group is one contiguous range
         order = sorted(range(len(named_params)), key=lambda i: (group_of[i], i))
         self.names: List[str] = []
@@ -47,8 +47,12 @@ class FlatParams:
         self.total = _round(off, max(ALIGN, pad_to))
         self.device = torch.device(device)
         self.dtype = dtype
-        self.param_buf = torch.zeros(self.total, dtype=dtype, device=self.device)
-        self.grad_buf = torch.zeros(self.total, dtype=dtype, device=self.device)
+        # `alloc(numel, dtype)` lets a gradient-sync backend place both buffers in
+        # peer-visible memory (zero-initialised)
+        if alloc is None:
+            alloc = lambda n, dt: torch.zeros(n, dtype=dt, device=self.device)  # noqa: E731
+        self.param_buf = alloc(self.total, dtype)
+        self.grad_buf = alloc(self.total, dtype)
         with torch.no_grad():
             for p, o, n in zip(self.params, self.offsets, self.numels):
                 self.param_buf[o:o + n].copy_(p.detach().reshape(-1))

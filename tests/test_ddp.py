@@ -1,0 +1,176 @@
+"""Data-parallel paths.
+
+CPU (gloo, 2 ranks): the reference semantics of averaging gradients after
+backward, host-side shard tables.  GPU (1 device): the fused kernels' bounded
+waits time out into an error status instead of hanging when a peer never
+arrives (the "peer" flag is a local buffer nothing writes).  Multi-GPU
+(2 devices): the fused NVSwitch step matches the NCCL baseline.
+"""
+import math
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from mmltk_b200.parallel.fused import shard_chunks
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_shard_chunks_cover_each_element_once():
+    chunks = torch.tensor([[0, 128, 0], [128, 64, 1], [192, 256, 0], [448, 64, 2]])
+    total, world = 512, 4
+    S = total // world
+    seen = torch.zeros(total, dtype=torch.int32)
+    for r in range(world):
+        t = shard_chunks(chunks, r * S, S)
+        for o, n, g in t.tolist():
+            seen[r * S + o:r * S + o + n] += 1
+            # group of every element is preserved
+            for e in range(r * S + o, r * S + o + n):
+                gg = [c[2] for c in chunks.tolist() if c[0] <= e < c[0] + c[1]]
+                assert gg == [g]
+    assert (seen == 1).all()
+
+
+def _cpu_ddp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    sys.path.insert(0, ROOT)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from mmltk_b200.config import TrainOptions, config_from_preset
+    from mmltk_b200.data.synthetic import synthetic_batch
+    from mmltk_b200.models import RFDETR
+    from mmltk_b200.parallel.ddp import NcclGradSync
+    from mmltk_b200.train.engine import TrainEngine
+    torch.manual_seed(0)
+    model = RFDETR(config_from_preset("rf-detr-tiny-test", resolution=64))
+    eng = TrainEngine(model, TrainOptions(lr=1e-3), "cpu", grad_sync=NcclGradSync(), max_targets=4)
+    imgs, tg = synthetic_batch(2, 64, seed=100 + rank, kmax=4, slots=4)  # different data per rank
+    for _ in range(2):
+        eng.step(imgs, tg)
+    flat = torch.cat([p.detach().reshape(-1) for p in model.parameters()])
+    out = [torch.zeros_like(flat) for _ in range(world)]
+    dist.all_gather(out, flat)
+    q.put((rank, float((out[0] - out[1]).abs().max())))
+    dist.destroy_process_group()
+
+
+def test_cpu_gloo_ddp_keeps_ranks_identical():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cpu_ddp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(d == 0.0 for _, d in res)
+
+
+@pytest.mark.gpu
+def test_fused_wait_times_out_into_status(cuda_device):
+    """A peer that never signals: the kernel gives up after spin_limit polls and reports it."""
+    from mmltk_b200.ops import kernels
+    k = kernels()
+    n = 4096
+    own = [k.ipc_alloc(n * 2, 0)[0] for _ in range(2)]          # param, grad
+    fake = [k.ipc_alloc(n * 2, 0)[0] for _ in range(2)]          # the "peer's" buffers (local, never signalled)
+    flags, _ = k.ipc_alloc(k.ddp_flag_words() * 4, 0)
+    fake_flags, _ = k.ipc_alloc(k.ddp_flag_words() * 4, 0)
+    small, _ = k.ipc_alloc(k.ddp_small_floats() * 4, 0)
+    fake_small, _ = k.ipc_alloc(k.ddp_small_floats() * 4, 0)
+    ctrl = torch.zeros(8, dtype=torch.int32, device=cuda_device)
+    ctrl[0] = 1
+    ctrl[1] = 1
+    comm = k.DdpComm([own[1].data_ptr(), fake[1].data_ptr()], [own[0].data_ptr(), fake[0].data_ptr()],
+                     [flags.data_ptr(), fake_flags.data_ptr()], [small.data_ptr(), fake_small.data_ptr()],
+                     0, 2, flags.view(torch.int32), small.view(torch.float32), ctrl, 2000)
+    gshard = torch.zeros(n // 2, device=cuda_device)
+    partials = torch.zeros(k.ddp_rs_blocks(), device=cuda_device)
+    comm.rs(0, n // 2, gshard, partials)
+    torch.cuda.synchronize()
+    assert int(ctrl[3]) == 1  # timed out waiting for 'gradients ready'
+    # our own 'ready' flag was delivered to the fake peer
+    assert int(fake_flags.view(torch.int32)[0]) == 1
+    ctrl[3] = 0
+    data = torch.ones(3, device=cuda_device)
+    comm.small_allreduce(data)
+    torch.cuda.synchronize()
+    assert int(ctrl[3]) == 4
+
+
+def _gpu_ddp_worker(rank, world, port, backend, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    sys.path.insert(0, ROOT)
+    import datetime
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    from mmltk_b200.config import TrainOptions, config_from_preset
+    from mmltk_b200.data.synthetic import synthetic_batch
+    from mmltk_b200.models import RFDETR
+    from mmltk_b200.parallel.ddp import NcclGradSync
+    from mmltk_b200.parallel.fused import FusedGradSync
+    from mmltk_b200.train.engine import TrainEngine
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-medium", group_detr=2, dec_layers=2, resolution=256,
+                             positional_encoding_size=16)
+    sync = FusedGradSync() if backend == "fused" else NcclGradSync()
+    eng = TrainEngine(RFDETR(cfg), TrainOptions(use_ema=True, cuda_graph=True), "cuda", grad_sync=sync,
+                      max_targets=6)
+    eng.bind_static_inputs(2, 3, 256, 256)
+    imgs, tg = synthetic_batch(2, 256, seed=10 + rank, kmax=6, slots=6, dtype=torch.bfloat16)
+    losses = [eng.step(imgs.cuda(), tg.to("cuda")).loss for _ in range(6)]
+    params = eng.flat.param_buf.float()
+    other = [torch.zeros_like(params) for _ in range(world)]
+    dist.all_gather(other, params)
+    same = float((other[0] - other[1]).abs().max())
+    q.put((rank, losses, same, params.cpu() if rank == 0 else None))
+    eng.release_graph()
+    if backend == "fused":
+        sync.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _run_gpu_ddp(backend):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gpu_ddp_worker, args=(r, 2, port, backend, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=600) for _ in procs], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return res
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_fused_ddp_matches_nccl_baseline():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    fused = _run_gpu_ddp("fused")
+    nccl = _run_gpu_ddp("nccl")
+    assert fused[0][2] == 0.0 and fused[1][2] == 0.0  # ranks hold identical parameters
+    for a, b in zip(fused[0][1], nccl[0][1]):
+        assert math.isfinite(a) and abs(a - b) / max(1e-3, abs(b)) < 0.05
+    n = min(fused[0][3].numel(), nccl[0][3].numel())  # the fused layout pads to a multiple of world * 64
+    diff = (fused[0][3][:n] - nccl[0][3][:n]).abs().max().item()
+    assert diff < 0.05
