@@ -41,26 +41,35 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// 8 x bf16 <-> 8 x float through one 16-byte vector.
-struct alignas(16) Bf16x8 {
-    __nv_bfloat162 h[4];
-};
+// 8 x bf16 <-> 8 x float through one 16-byte vector.  The data moves as raw
+// uint4 / uint2 words: assigning __nv_bfloat162 structs member-wise would split
+// every 16-byte access into four 4-byte ones.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+}
 
 __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
-    Bf16x8 v = *reinterpret_cast<const Bf16x8*>(p);
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        float2 t = __bfloat1622float2(v.h[i]);
+        const float2 t = unpack_bf16x2(w[i]);
         f[2 * i] = t.x;
         f[2 * i + 1] = t.y;
     }
 }
 
 __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* f) {
-    Bf16x8 v;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v.h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-    *reinterpret_cast<Bf16x8*>(p) = v;
+    uint4 raw;
+    raw.x = pack_bf16x2(f[0], f[1]);
+    raw.y = pack_bf16x2(f[2], f[3]);
+    raw.z = pack_bf16x2(f[4], f[5]);
+    raw.w = pack_bf16x2(f[6], f[7]);
+    *reinterpret_cast<uint4*>(p) = raw;
 }
 
 __device__ __forceinline__ void load8(const float* p, float* f) {
@@ -77,18 +86,15 @@ __device__ __forceinline__ void store8(float* p, const float* f) {
 
 // 4 elements <-> float4
 __device__ __forceinline__ float4 load4(const __nv_bfloat16* p) {
-    uint2 raw = *reinterpret_cast<const uint2*>(p);
-    __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&raw.x);
-    __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&raw.y);
-    float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
-    return make_float4(fa.x, fa.y, fb.x, fb.y);
+    const uint2 raw = *reinterpret_cast<const uint2*>(p);
+    const float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
+    return make_float4(a.x, a.y, b.x, b.y);
 }
 __device__ __forceinline__ float4 load4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ void store4(__nv_bfloat16* p, float4 v) {
-    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
     uint2 raw;
-    raw.x = *reinterpret_cast<uint32_t*>(&a);
-    raw.y = *reinterpret_cast<uint32_t*>(&b);
+    raw.x = pack_bf16x2(v.x, v.y);
+    raw.y = pack_bf16x2(v.z, v.w);
     *reinterpret_cast<uint2*>(p) = raw;
 }
 __device__ __forceinline__ void store4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }

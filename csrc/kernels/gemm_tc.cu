@@ -1,0 +1,574 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05) with the accumulator
+// in tensor memory.
+//
+//   C[M,N] = opA(A) . opB(B)  (+ bias, + activation / LayerScale-residual epilogue)
+//
+// Persistent kernel, one CTA per SM, 128x256 output tiles, six warps:
+//   warp 0    TMA producer: 128B-swizzled A (128x64) and B (256x64) tiles into a
+//             4-stage ring (cp.async.bulk.tensor with mbarrier transaction
+//             counts); also owns the TMEM allocation (all 512 columns);
+//   warp 1    MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16,
+//             bf16 x bf16 -> fp32), 4 per K tile, into one of two TMEM
+//             accumulators, and hands each smem stage back with tcgen05.commit;
+//   warps 2-5 epilogue: tcgen05.ld (32 lanes x 16 columns per instruction),
+//             fused bias / GELU / ReLU / LayerScale + residual, bf16 stores.
+// The two accumulators let the epilogue of tile i run while tile i+1 is being
+// multiplied.  Work units are (tile, K split); GEMMs with few output tiles and
+// a long reduction (weight gradients reduce over all tokens) are split along K
+// and the partial tiles are summed with 16-byte fp32 vector atomics into a
+// workspace, then converted.  Operands may be K-major ([rows, K] row-major)
+// or MN-major ([K, rows] row-major), so x.W^T, dY.W and dY^T.X all run without
+// materialising a transpose.  M/N/K tails: TMA zero fill + masked stores.
+//
+// Every mbarrier wait is bounded; on timeout the kernel records an error code
+// in a status word and leaves (after releasing its TMEM) instead of spinning.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+
+#include "common.cuh"
+#include "gemm_tc.h"
+
+namespace mmltk {
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+constexpr int kATile = BM * BK * 2;                // 16 KB
+constexpr int kThreads = 320;                      // 2 producer/MMA warps + 8 epilogue warps
+constexpr int kEpiWarps = 8;
+constexpr int kStageWords = 32 * 17;               // per-warp epilogue staging tile, padded rows
+constexpr int kStagingBytes = kEpiWarps * kStageWords * 4;
+constexpr int kMaxStages = 6;
+constexpr long long kWaitLimit = 1ll << 22;
+constexpr int kSmemLimit = 227 * 1024;
+
+// Tile configuration for a tile width BN (128, 192 or 256 output columns).
+template <int BN_>
+struct Tile {
+    static constexpr int BN = BN_;
+    static constexpr int kBTile = BN * BK * 2;
+    static constexpr int kStageBytes = kATile + kBTile;
+    static constexpr int kStages =
+        (kSmemLimit - kStagingBytes - 2048) / kStageBytes < kMaxStages ? (kSmemLimit - kStagingBytes - 2048) / kStageBytes
+                                                                         : kMaxStages;
+    static constexpr int kAccCols = BN;            // fp32 accumulator columns per buffer
+    static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
+    static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + kStagingBytes + 1024 + 256;
+};
+
+struct __align__(8) SmemCtl {
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint32_t tmem_base;
+    int abort;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; false on timeout or when another role has aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+    for (long long i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 255 && *abort) return false;
+    }
+    return false;
+}
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field = 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3fff);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3fff) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3fff) << 32;
+    d |= 1ull << 46;  // version
+    d |= 2ull << 61;  // SWIZZLE_128B
+    return d;
+}
+// Instruction descriptor: bf16 x bf16 -> f32, M=128, N=n, operand majors.
+__host__ __device__ constexpr uint32_t instr_desc(bool a_mn, bool b_mn, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+}
+// Descriptor of the 16-wide K slice kk (0..3) of an operand tile.
+//   K-major : rows x 128 B, 8-row groups 1024 B apart; K advances 32 B inside the swizzled row.
+//   MN-major: 64-wide MN groups (64 K-rows x 128 B = 8 KB) side by side; K advances 16 rows = 2 KB.
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t tile, int kk) {
+    if (MN) return smem_desc(tile + kk * 2048, 8192, 1024);
+    return smem_desc(tile + kk * 32, 16, 1024);
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ float gelu_f(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
+
+// 32 consecutive accumulator columns of this thread's row: two loads, one wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr + 16));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Warp-cooperative row-block copy through the padded staging tile (32 rows x 16
+// words, row stride 17 words: conflict-free when every lane writes its own row).
+// Each lane owns one row in registers; global memory is touched in 64-byte row
+// segments (8 rows per instruction) instead of one 16-byte piece per row.
+__device__ __forceinline__ void stage_store(uint32_t* stg, int lane, const float* x, __nv_bfloat16* base, int64_t ld,
+                                            int rows_valid, int ncols) {
+#pragma unroll
+    for (int w = 0; w < 16; ++w) stg[lane * 17 + w] = pack_bf16x2(x[2 * w], x[2 * w + 1]);
+    __syncwarp();
+    const int seg = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = 8 * i + (lane >> 2);
+        if (r < rows_valid && seg * 8 < ncols) {
+            const uint32_t* src = stg + r * 17 + seg * 4;
+            *reinterpret_cast<uint4*>(base + r * ld + seg * 8) = make_uint4(src[0], src[1], src[2], src[3]);
+        }
+    }
+    __syncwarp();
+}
+
+__device__ __forceinline__ void stage_load(uint32_t* stg, int lane, float* x, const __nv_bfloat16* base, int64_t ld,
+                                           int rows_valid, int ncols) {
+    const int seg = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = 8 * i + (lane >> 2);
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (r < rows_valid && seg * 8 < ncols) w = *reinterpret_cast<const uint4*>(base + r * ld + seg * 8);
+        uint32_t* dst = stg + r * 17 + seg * 4;
+        dst[0] = w.x; dst[1] = w.y; dst[2] = w.z; dst[3] = w.w;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int w = 0; w < 16; ++w) {
+        const float2 t = unpack_bf16x2(stg[lane * 17 + w]);
+        x[2 * w] = t.x;
+        x[2 * w + 1] = t.y;
+    }
+    __syncwarp();
+}
+
+// Epilogue of one warp's 32 rows x `ncols` (16 or 32) columns; lane = row.
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg, int lane, int row0, int col,
+                                               int ncols, float* v) {
+    const int rows_valid = min(32, g.M - row0);
+    const int row = row0 + lane;
+    if (g.ws) {  // split-K partial: fp32 vector atomics into the workspace
+        if (row < g.M) {
+            float4* w = reinterpret_cast<float4*>(g.ws + static_cast<int64_t>(row) * g.ldc + col);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (4 * i < ncols)
+                    atomicAdd(w + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+        }
+        return;
+    }
+    if (g.bias) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (8 * j < ncols) {
+                float b[8];
+                load8(g.bias + col + 8 * j, b);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[8 * j + i] += b[i];
+            }
+        }
+    }
+    const int64_t base = static_cast<int64_t>(row0) * g.ldc + col;
+    if (g.aux) stage_store(stg, lane, v, g.aux + base, g.ldc, rows_valid, ncols);  // pre-activation for backward
+    if (g.epi == 1) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = gelu_f(v[i]);
+    } else if (g.epi == 2) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.f);
+    } else if (g.epi == 3) {
+        float r[32];
+        stage_load(stg, lane, r, g.res + base, g.ldc, rows_valid, ncols);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (8 * j < ncols) {
+                float gm[8];
+                load8(g.gamma + col + 8 * j, gm);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[8 * j + i] = r[8 * j + i] + gm[i] * v[8 * j + i];
+            }
+        }
+    }
+    stage_store(stg, lane, v, g.C + base, g.ldc, rows_valid, ncols);
+}
+
+struct Sched {
+    int m_tiles, n_tiles, splits, ktiles, kt_per_split, bn;
+    __device__ void unit(int u, int& m0, int& n0, int& kt0, int& kt1) const {
+        const int tile = u / splits, s = u % splits;
+        m0 = (tile / n_tiles) * BM;
+        n0 = (tile % n_tiles) * bn;
+        kt0 = s * kt_per_split;
+        kt1 = min(ktiles, kt0 + kt_per_split);
+    }
+};
+
+template <bool A_MN, bool B_MN, int BN_>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                              const __grid_constant__ CUtensorMap tmB, GemmArgs g,
+                                                              Sched sch) {
+    using T = Tile<BN_>;
+    constexpr int BN = T::BN, kStages = T::kStages, kBTile = T::kBTile, kAccCols = T::kAccCols;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* tilesA = smem;
+    unsigned char* tilesB = smem + kStages * kATile;
+    uint32_t* staging = reinterpret_cast<uint32_t*>(smem + kStages * (kATile + kBTile));
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(reinterpret_cast<unsigned char*>(staging) + kStagingBytes);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int units = sch.m_tiles * sch.n_tiles * sch.splits;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&ctl->full[s], 1);
+            mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->acc_full[b], 1);
+            mbar_init(&ctl->acc_empty[b], kEpiWarps);  // one arrival per epilogue warp
+        }
+        ctl->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&ctl->tmem_base)),
+                     "r"(T::kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;  // global k-tile counter across units -> ring position
+            for (int u = blockIdx.x; u < units; u += gridDim.x) {
+                int m0, n0, kt0, kt1;
+                sch.unit(u, m0, n0, kt0, kt1);
+                // MN-major operands are loaded as 64-wide boxes; boxes entirely past the
+                // extent are skipped (they only feed output rows/columns that are masked)
+                const int a_boxes = A_MN ? min(BM / 64, (g.M - m0 + 63) / 64) : 1;
+                const int b_boxes = B_MN ? min(BN / 64, (g.N - n0 + 63) / 64) : 1;
+                const uint32_t bytes = (A_MN ? a_boxes * 8192 : kATile) + (B_MN ? b_boxes * 8192 : kBTile);
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1;
+                    if (!mbar_wait(&ctl->empty[s], ph ^ 1, &ctl->abort)) {
+                        ctl->abort = 1;
+                        atomicCAS(g.status, 0, 1);
+                        goto producer_done;
+                    }
+                    mbar_expect_tx(&ctl->full[s], bytes);
+                    unsigned char* a = tilesA + s * kATile;
+                    unsigned char* b = tilesB + s * kBTile;
+                    const int k0 = kt * BK;
+                    if (A_MN) {
+                        for (int q = 0; q < a_boxes; ++q) tma_load_2d(&tmA, &ctl->full[s], a + q * 8192, m0 + 64 * q, k0);
+                    } else {
+                        tma_load_2d(&tmA, &ctl->full[s], a, k0, m0);
+                    }
+                    if (B_MN) {
+                        for (int q = 0; q < b_boxes; ++q) tma_load_2d(&tmB, &ctl->full[s], b + q * 8192, n0 + 64 * q, k0);
+                    } else {
+                        tma_load_2d(&tmB, &ctl->full[s], b, k0, n0);
+                    }
+                }
+            }
+        producer_done:;
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(A_MN, B_MN, BN);
+            int it = 0, local = 0;
+            for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+                int m0, n0, kt0, kt1;
+                sch.unit(u, m0, n0, kt0, kt1);
+                const int buf = local & 1;
+                const uint32_t acc_ph = (local >> 1) & 1;
+                if (!mbar_wait(&ctl->acc_empty[buf], acc_ph ^ 1, &ctl->abort)) {
+                    ctl->abort = 1;
+                    atomicCAS(g.status, 0, 2);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t acc = tmem + buf * kAccCols;
+                bool ok = true;
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1;
+                    if (!mbar_wait(&ctl->full[s], ph, &ctl->abort)) {
+                        ctl->abort = 1;
+                        atomicCAS(g.status, 0, 2);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(tilesA + s * kATile);
+                    const uint32_t b = smem_u32(tilesB + s * kBTile);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        tc_mma(acc, operand_desc<A_MN>(a, kk), operand_desc<B_MN>(b, kk), idesc,
+                               (kt > kt0 || kk > 0) ? 1u : 0u);
+                    tc_commit(&ctl->empty[s]);
+                }
+                if (!ok) break;
+                tc_commit(&ctl->acc_full[buf]);
+            }
+        }
+    } else {
+        // epilogue: 8 warps; warp w reads TMEM lanes 32*(w%4) .. +31 (its quarter of the
+        // tile's rows) and half of the tile's columns, 32 columns per tcgen05.wait
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        uint32_t* stg = staging + (warp - 2) * kStageWords;
+        int local = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+            int m0, n0, kt0, kt1;
+            sch.unit(u, m0, n0, kt0, kt1);
+            const int buf = local & 1;
+            const uint32_t acc_ph = (local >> 1) & 1;
+            if (!mbar_wait(&ctl->acc_full[buf], acc_ph, &ctl->abort)) {
+                if (lane == 0) atomicCAS(g.status, 0, 3);
+                ctl->abort = 1;
+                break;
+            }
+            tc_fence_after();
+            const int row0 = m0 + 32 * q;
+            const uint32_t acc = tmem + buf * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
+            constexpr int kHalfCols = BN / 2;
+            for (int c = half * kHalfCols; c < (half + 1) * kHalfCols; c += 32) {
+                if (n0 + c >= g.N || row0 >= g.M) break;  // warp-uniform
+                const int ncols = min(min(32, (half + 1) * kHalfCols - c), g.N - n0 - c);
+                float v[32];
+                if (ncols > 16) {
+                    tmem_ld32(acc + c, v);
+                } else {
+                    tmem_ld16(acc + c, v);
+                }
+                epilogue_chunk(g, stg, lane, row0, n0 + c, ncols, v);
+            }
+            // accumulator buffer free again
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->acc_empty[buf]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(T::kTmemCols));
+    }
+}
+
+__global__ void ws_to_bf16_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ c, int64_t n) {
+    for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x * 8) {
+        float v[8];
+        load8(ws + i, v);
+        store8(c + i, v);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D bf16 tensor [outer, inner] (row pitch in elements), box {64, box_rows}, 128B swizzle, zero OOB fill.
+bool make_map(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, int64_t pitch, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch * 2)};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        std::fprintf(stderr, "gemm_tc: cuTensorMapEncodeTiled failed (%d): inner %lld outer %lld pitch %lld box %d\n",
+                     static_cast<int>(r), static_cast<long long>(inner), static_cast<long long>(outer),
+                     static_cast<long long>(pitch), box_rows);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+// Tile width for an M x N output: maximise (useful columns) x (wave occupancy of the
+// persistent grid) x (per-tile efficiency of the width), e.g. N = 1536 -> 192,
+// N = 384 with 82 row tiles -> 128 (246 tiles fill 2 waves of 148 SMs better than 164).
+int pick_bn(int M, int N) {
+    const int sms = num_sms();
+    const int widths[3] = {256, 192, 128};
+    const double tile_eff[3] = {1.0, 0.96, 0.88};
+    int best = 256;
+    double best_score = -1.0;
+    for (int i = 0; i < 3; ++i) {
+        const int bn = widths[i];
+        const int tn = (N + bn - 1) / bn;
+        const double col_eff = static_cast<double>(N) / (static_cast<double>(tn) * bn);
+        const long long units = static_cast<long long>((M + BM - 1) / BM) * tn;
+        const long long waves = (units + sms - 1) / sms;
+        const double wave_eff = static_cast<double>(units) / static_cast<double>(waves * sms);
+        const double score = col_eff * wave_eff * tile_eff[i];
+        if (score > best_score + 1e-9) {
+            best_score = score;
+            best = bn;
+        }
+    }
+    return best;
+}
+
+size_t gemm_tc_smem_bytes() { return Tile<256>::kSmemBytes; }
+
+int gemm_tc_splits(int M, int N, int K) {
+    const int bn = pick_bn(M, N);
+    const int tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+    const int ktiles = (K + BK - 1) / BK;
+    const int sms = num_sms();
+    if (tiles >= sms / 2 || ktiles < 8) return 1;
+    int s = std::min((sms + tiles - 1) / tiles, ktiles / 4);
+    return std::max(1, s);
+}
+
+cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t lda, int64_t ldb, cudaStream_t st) {
+    GemmArgs g = g_in;
+    // The tensor maps are encoded through the driver API, which needs a current
+    // context; threads that only used the runtime lazily (e.g. the autograd
+    // worker thread) may not have one yet.
+    int dev = 0;
+    cudaError_t de = cudaGetDevice(&dev);
+    if (de == cudaSuccess) de = cudaSetDevice(dev);
+    if (de != cudaSuccess) return de;
+    const int bn = pick_bn(g.M, g.N);
+    CUtensorMap ta, tb;
+    bool ok = a_mn ? make_map(&ta, g.A, g.M, g.K, lda, 64) : make_map(&ta, g.A, g.K, g.M, lda, BM);
+    ok = ok && (b_mn ? make_map(&tb, g.B, g.N, g.K, ldb, 64) : make_map(&tb, g.B, g.K, g.N, ldb, bn));
+    if (!ok) return cudaErrorInvalidValue;
+    Sched sch;
+    sch.bn = bn;
+    sch.m_tiles = (g.M + BM - 1) / BM;
+    sch.n_tiles = (g.N + bn - 1) / bn;
+    sch.ktiles = (g.K + BK - 1) / BK;
+    sch.splits = g.ws ? std::max(1, g.splits) : 1;
+    sch.kt_per_split = (sch.ktiles + sch.splits - 1) / sch.splits;
+    sch.splits = (sch.ktiles + sch.kt_per_split - 1) / sch.kt_per_split;
+    const int units = sch.m_tiles * sch.n_tiles * sch.splits;
+    const int grid = std::min(units, num_sms());
+    cudaError_t e = cudaSuccess;
+    if (g.ws) {
+        e = cudaMemsetAsync(g.ws, 0, static_cast<size_t>(g.M) * g.ldc * sizeof(float), st);
+        if (e != cudaSuccess) return e;
+    }
+    auto launch = [&](auto kern, size_t smem) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) {
+            std::fprintf(stderr, "gemm_tc: cudaFuncSetAttribute(%zu bytes) failed: %s\n", smem, cudaGetErrorString(e));
+            return;
+        }
+        kern<<<grid, kThreads, smem, st>>>(ta, tb, g, sch);
+        e = cudaGetLastError();
+    };
+    auto by_major = [&](auto bnc) {
+        constexpr int BNv = decltype(bnc)::value;
+        const size_t smem = Tile<BNv>::kSmemBytes;
+        if (!a_mn && !b_mn) launch(gemm_tc_kernel<false, false, BNv>, smem);
+        else if (!a_mn && b_mn) launch(gemm_tc_kernel<false, true, BNv>, smem);
+        else if (a_mn && b_mn) launch(gemm_tc_kernel<true, true, BNv>, smem);
+        else launch(gemm_tc_kernel<true, false, BNv>, smem);
+    };
+    if (bn == 256) by_major(std::integral_constant<int, 256>{});
+    else if (bn == 192) by_major(std::integral_constant<int, 192>{});
+    else by_major(std::integral_constant<int, 128>{});
+    if (e != cudaSuccess || !g.ws) return e;
+    const int64_t n = static_cast<int64_t>(g.M) * g.ldc;
+    ws_to_bf16_kernel<<<std::min<int64_t>((n / 8 + 255) / 256, num_sms() * 8), 256, 0, st>>>(g.ws, g.C, n);
+    return cudaGetLastError();
+}
+
+}  // namespace mmltk

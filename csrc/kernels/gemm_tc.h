@@ -1,0 +1,33 @@
+// Arguments of the tcgen05 GEMM (see gemm_tc.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace mmltk {
+
+struct GemmArgs {
+    const __nv_bfloat16* A;
+    const __nv_bfloat16* B;
+    __nv_bfloat16* C;           // [M, N], row pitch ldc
+    __nv_bfloat16* aux;         // optional: pre-activation (acc + bias), same layout as C
+    const __nv_bfloat16* bias;  // optional [N]
+    const __nv_bfloat16* res;   // epi 3: residual [M, N] (pitch ldc)
+    const __nv_bfloat16* gamma; // epi 3: LayerScale [N]
+    int* status;                // 0 ok, else a bounded wait gave up (1 producer, 2 MMA, 3 epilogue)
+    float* ws;                  // split-K: fp32 [M, N] workspace (zeroed by the launcher); nullptr = no split
+    int splits;                 // K splits when ws != nullptr
+    int M, N, K;
+    int64_t ldc;
+    int epi;                    // 0 none, 1 GELU(erf), 2 ReLU, 3 res + gamma * (acc + bias)
+};
+
+size_t gemm_tc_smem_bytes();
+// K splits worth using for this shape (1 = none); only for plain products (no bias / epilogue).
+int gemm_tc_splits(int M, int N, int K);
+// a_mn: A stored [K, M] (else [M, K]); b_mn: B stored [K, N] (else [N, K]); lda/ldb: row pitch in elements.
+cudaError_t launch_gemm_tc(const GemmArgs& g, bool a_mn, bool b_mn, int64_t lda, int64_t ldb, cudaStream_t st);
+
+}  // namespace mmltk

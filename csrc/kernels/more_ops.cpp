@@ -94,6 +94,7 @@ void register_more_ops(pybind11::module& m) {
     m.def("scale_bwd", &scale_bwd);
     m.def("act_bwd", &act_bwd);
     register_ddp_ops(m);
+    register_gemm_ops(m);
 }
 
 }  // namespace mmltk

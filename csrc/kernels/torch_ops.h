@@ -14,5 +14,6 @@ cudaStream_t cur_stream();
 // Ops defined in other wrapper files (GEMM, attention, DDP, ...) register here.
 void register_more_ops(pybind11::module& m);
 void register_ddp_ops(pybind11::module& m);
+void register_gemm_ops(pybind11::module& m);
 
 }  // namespace mmltk

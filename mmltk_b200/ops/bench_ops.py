@@ -1,0 +1,131 @@
+"""Kernel micro-benchmarks: the framework's sm_100a kernels against the
+library baseline of the same op, timed with CUDA events after warm-up.
+
+    python -m mmltk_b200.ops.bench_ops gemm      # tcgen05 GEMM vs cuBLAS on the RF-DETR-M shapes
+    python -m mmltk_b200.ops.bench_ops msda      # MSDeformAttn fwd+bwd vs fp32 reference path
+
+Inputs are larger than L2 where the op allows; each timing is the median of
+several event-timed runs.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+
+import torch
+
+__all__ = ["time_ms", "bench_gemm", "bench_msda"]
+
+
+def time_ms(fn, warmup: int = 5, iters: int = 20, reps: int = 5) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        out.append(s.elapsed_time(e) / iters)
+    return statistics.median(out)
+
+
+# (name, M, N, K, mode): mode nt = x W^T, nn = dY W, tn = dY^T X
+GEMM_SHAPES = [
+    ("vit.qkv.fwd", 10400, 1152, 384, "nt"), ("vit.proj.fwd", 10400, 384, 384, "nt"),
+    ("vit.fc1.fwd", 10400, 1536, 384, "nt"), ("vit.fc2.fwd", 10400, 384, 1536, "nt"),
+    ("vit.fc1.dgrad", 10400, 384, 1536, "nn"), ("vit.fc2.dgrad", 10400, 1536, 384, "nn"),
+    ("vit.fc1.wgrad", 1536, 384, 10400, "tn"), ("vit.fc2.wgrad", 384, 1536, 10400, "tn"),
+    ("dec.ffn1.fwd", 31200, 2048, 256, "nt"), ("dec.ffn2.fwd", 31200, 256, 2048, "nt"),
+    ("dec.ffn1.wgrad", 2048, 256, 31200, "tn"), ("dec.ffn2.dgrad", 31200, 2048, 256, "nn"),
+]
+
+
+def bench_gemm(device="cuda", only=None, quick=False):
+    from ._ext import kernels
+    k = kernels()
+    rows = []
+    for name, M, N, K, mode in GEMM_SHAPES:
+        if only and name != only:
+            continue
+        g = torch.Generator(device=device).manual_seed(0)
+        if mode == "nt":
+            a = torch.randn(M, K, device=device, generator=g).bfloat16()
+            b = torch.randn(N, K, device=device, generator=g).bfloat16()
+            ours = lambda: k.gemm_tc(a, b, None, False, False)  # noqa: E731
+            lib = lambda: torch.mm(a, b.t())  # noqa: E731
+        elif mode == "nn":
+            a = torch.randn(M, K, device=device, generator=g).bfloat16()
+            b = torch.randn(K, N, device=device, generator=g).bfloat16()
+            ours = lambda: k.gemm_tc(a, b, None, False, True)  # noqa: E731
+            lib = lambda: torch.mm(a, b)  # noqa: E731
+        else:
+            a = torch.randn(K, M, device=device, generator=g).bfloat16()
+            b = torch.randn(K, N, device=device, generator=g).bfloat16()
+            ours = lambda: k.gemm_tc(a, b, None, True, True)  # noqa: E731
+            lib = lambda: torch.mm(a.t(), b)  # noqa: E731
+        ref = lib().float()
+        got = ours()[0].float()
+        err = ((got - ref).abs().max() / ref.abs().max()).item()
+        if quick:  # a few launches only (for profiler captures)
+            for _ in range(3):
+                ours()
+            torch.cuda.synchronize()
+            continue
+        t_ours, t_lib = time_ms(ours), time_ms(lib)
+        fl = 2.0 * M * N * K
+        rows.append({"shape": name, "M": M, "N": N, "K": K, "mode": mode, "ms_tc": round(t_ours, 4),
+                     "ms_cublas": round(t_lib, 4), "tflops_tc": round(fl / t_ours / 1e9, 1),
+                     "tflops_cublas": round(fl / t_lib / 1e9, 1), "speedup": round(t_lib / t_ours, 3),
+                     "rel_err": err, "status": k.gemm_tc_status(torch.cuda.current_device())})
+    return rows
+
+
+def bench_msda(device="cuda"):
+    """value [16, 6480, 16, 16] bf16, Lq 3900, 2 levels (72x72, 36x36), 4 points."""
+    from .msda import msda, msda_reference
+    B, H, D, Lq, P = 16, 16, 16, 3900, 4
+    shapes = [(72, 72), (36, 36)]
+    S = sum(h * w for h, w in shapes)
+    L = len(shapes)
+    g = torch.Generator(device=device).manual_seed(0)
+    value = torch.randn(B, S, H, D, device=device, generator=g).bfloat16().requires_grad_()
+    ref = torch.rand(B, Lq, L, 4, device=device, generator=g).bfloat16()
+    ref[..., 2:] = ref[..., 2:] * 0.3 + 0.02
+    ref.requires_grad_()
+    off = torch.randn(B, Lq, H, L, P, 2, device=device, generator=g).bfloat16().requires_grad_()
+    logits = torch.randn(B, Lq, H, L * P, device=device, generator=g).bfloat16().requires_grad_()
+    gout = torch.randn(B, Lq, H * D, device=device, generator=g).bfloat16()
+
+    def ours():
+        out = msda(value, shapes, ref, off, logits)
+        out.backward(gout)
+
+    def baseline():  # fp32 grid_sample path incl. the bf16 -> fp32 casts
+        out = msda_reference(value, shapes, ref, off, logits)
+        out.backward(gout.float())
+
+    t_ours = time_ms(ours, warmup=3, iters=5)
+    t_base = time_ms(baseline, warmup=2, iters=3, reps=3)
+    return [{"op": "msda_fwd_bwd", "B": B, "S": S, "H": H, "D": D, "Lq": Lq, "levels": L, "points": P,
+             "ms_ours": round(t_ours, 3), "ms_fp32_grid_sample": round(t_base, 3),
+             "speedup": round(t_base / t_ours, 2)}]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["gemm", "msda"])
+    ap.add_argument("--shape", default=None, help="run one GEMM shape (see GEMM_SHAPES)")
+    ap.add_argument("--quick", action="store_true", help="launch a few times without timing (profiler runs)")
+    args = ap.parse_args()
+    rows = bench_gemm(only=args.shape, quick=args.quick) if args.what == "gemm" else bench_msda()
+    for r in rows:
+        print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()

@@ -3,11 +3,12 @@
 ``gemm_nt(a [M,K], b [N,K], bias)`` -> a b^T (+ bias)   (forward)
 ``gemm_nn(a [M,N], b [N,K])``        -> a b               (input gradient)
 ``gemm_tn(a [M,N], b [M,K])``        -> a^T b             (weight gradient)
+``gemm_nt_epilogue(...)``            forward with a fused GELU / ReLU / LayerScale+residual epilogue
 
 Shapes that fit the framework's sm_100a kernel (``gemm_tc``: TMA loads into
 128B-swizzled shared memory, ``tcgen05.mma`` with the accumulator in tensor
-memory, epilogue through ``tcgen05.ld``) run on it; everything else runs on
-cuBLAS through torch.
+memory, epilogue through ``tcgen05.ld``; K-major and MN-major operands, so no
+transposes are materialised) run on it; anything else runs on cuBLAS.
 """
 from __future__ import annotations
 
@@ -17,13 +18,21 @@ import torch
 
 from ._ext import kernels
 
-__all__ = ["gemm_nt", "gemm_nn", "gemm_tn", "set_tc_gemm", "tc_gemm_enabled"]
+__all__ = ["gemm_nt", "gemm_nn", "gemm_tn", "gemm_nt_epilogue", "set_tc_gemm", "tc_gemm_enabled"]
 
-_state = {"enabled": os.environ.get("MMLTK_TC_GEMM", "1") != "0", "checked": False, "have": False}
+# The fused-epilogue forward products always run on the tcgen05 kernel (that is
+# where fusing saves whole passes over memory); plain products (backward dgrad /
+# wgrad) use cuBLAS unless MMLTK_TC_GEMM_ALL=1.
+_state = {"enabled": os.environ.get("MMLTK_TC_GEMM", "1") != "0", "checked": False, "have": False,
+          "all": os.environ.get("MMLTK_TC_GEMM_ALL", "0") == "1"}
+
+EPI = {"gelu": 1, "relu": 2, "scale_residual": 3}
 
 
-def set_tc_gemm(flag: bool) -> None:
+def set_tc_gemm(flag: bool, plain_products: bool = None) -> None:
     _state["enabled"] = bool(flag)
+    if plain_products is not None:
+        _state["all"] = bool(plain_products)
 
 
 def tc_gemm_enabled() -> bool:
@@ -33,31 +42,40 @@ def tc_gemm_enabled() -> bool:
     return _state["enabled"] and _state["have"]
 
 
-def _tc_fits(M, N, K):
-    return M % 128 == 0 and N % 64 == 0 and K % 64 == 0
+def _rowmajor(t):
+    return t.stride(-1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
+
+
+def _fits_nt(a, b):
+    return tc_gemm_enabled() and a.shape[1] % 8 == 0 and b.shape[0] % 16 == 0 and _rowmajor(a) and _rowmajor(b)
 
 
 def gemm_nt(a: torch.Tensor, b: torch.Tensor, bias=None) -> torch.Tensor:
-    M, K = a.shape
-    N = b.shape[0]
-    if tc_gemm_enabled() and _tc_fits(M, N, K):
-        return kernels().gemm_tc(a, b, bias, False, False)
+    if _state["all"] and _fits_nt(a, b):
+        return kernels().gemm_tc(a, b, bias, False, False)[0]
     if bias is None:
         return torch.mm(a, b.t())
     return torch.addmm(bias, a, b.t())
 
 
+def gemm_nt_epilogue(a, b, bias, epi: str, res=None, gamma=None):
+    """(out, pre) with out = act(a b^T + bias) or res + gamma * (a b^T + bias); pre = a b^T + bias.
+    Returns None when the shape does not fit the tensor-core kernel."""
+    if not _fits_nt(a, b):
+        return None
+    out, pre = kernels().gemm_tc(a, b, bias, False, False, EPI[epi], True, res, gamma)
+    return out, pre
+
+
 def gemm_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    M, N = a.shape
-    K = b.shape[1]
-    if tc_gemm_enabled() and _tc_fits(M, K, N):
-        return kernels().gemm_tc(a, b, None, False, True)
+    if (_state["all"] and tc_gemm_enabled() and a.shape[1] % 8 == 0 and b.shape[1] % 128 == 0 and _rowmajor(a)
+            and _rowmajor(b)):
+        return kernels().gemm_tc(a, b, None, False, True)[0]
     return torch.mm(a, b)
 
 
 def gemm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    M, N = a.shape
-    K = b.shape[1]
-    if tc_gemm_enabled() and _tc_fits(N, K, M):
-        return kernels().gemm_tc(a, b, None, True, True)
+    if (_state["all"] and tc_gemm_enabled() and a.shape[1] % 128 == 0 and b.shape[1] % 128 == 0 and _rowmajor(a)
+            and _rowmajor(b)):
+        return kernels().gemm_tc(a, b, None, True, True)[0]
     return torch.mm(a.t(), b)

@@ -22,7 +22,7 @@ import torch
 import torch.nn.functional as F
 
 from ._ext import kernels
-from .gemm import gemm_nt, gemm_nn, gemm_tn
+from .gemm import gemm_nn, gemm_nt, gemm_nt_epilogue, gemm_tn
 
 __all__ = ["linear", "linear_scale_residual", "set_fused_linear"]
 
@@ -57,8 +57,12 @@ class _Linear(torch.autograd.Function):
     def forward(ctx, x, w, b, act_id):
         shp = x.shape
         x2 = _2d(x, shp[-1])
-        pre = gemm_nt(x2, w, b)                   # x W^T + b
-        y = _act(pre, act_id) if act_id else pre
+        fused = gemm_nt_epilogue(x2, w, b, "gelu" if act_id == 1 else "relu") if act_id else None
+        if fused is not None:
+            y, pre = fused                        # activation applied in the GEMM epilogue
+        else:
+            pre = gemm_nt(x2, w, b)               # x W^T + b
+            y = _act(pre, act_id) if act_id else pre
         ctx.save_for_backward(x2, w, pre if act_id else None)
         ctx.act_id, ctx.has_bias, ctx.shp = act_id, b is not None, shp
         return y.view(*shp[:-1], w.shape[0])
@@ -81,8 +85,13 @@ class _LinearScaleResidual(torch.autograd.Function):
     def forward(ctx, x, w, b, gamma, res):
         shp = x.shape
         x2 = _2d(x, shp[-1])
-        pre = gemm_nt(x2, w, b)
-        y = torch.addcmul(res.reshape(pre.shape), pre, gamma.to(pre.dtype))
+        r2 = _2d(res, w.shape[0])
+        fused = gemm_nt_epilogue(x2, w, b, "scale_residual", r2, gamma)
+        if fused is not None:
+            y, pre = fused                        # res + gamma * (x W^T + b) in the GEMM epilogue
+        else:
+            pre = gemm_nt(x2, w, b)
+            y = torch.addcmul(r2, pre, gamma.to(pre.dtype))
         ctx.save_for_backward(x2, w, gamma, pre)
         ctx.shp = shp
         return y.view(*shp[:-1], w.shape[0])

@@ -229,3 +229,64 @@ def test_colsum(cuda_device):
         got = kernels().colsum(x, torch.float32)
         ref = x.float().sum(0)
         assert (got - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 384), (10400 // 8, 256, 96), (384, 1152, 1536)])
+def test_gemm_tc_all_operand_majors(cuda_device, a_mn, b_mn, M, N, K):
+    """tcgen05 GEMM vs fp32 matmul for K-major / MN-major operands, with M and K tails."""
+    if (a_mn and M % 128) or (b_mn and N % 128):
+        pytest.skip("MN-major extents must be multiples of 128")
+    k = kernels()
+    g = torch.Generator().manual_seed(M + N + K)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, generator=g).to(torch.bfloat16)
+    ref = A.float() @ B.float().t()
+    a = (A.t().contiguous() if a_mn else A).to(cuda_device)
+    b = (B.t().contiguous() if b_mn else B).to(cuda_device)
+    out = k.gemm_tc(a, b, None, a_mn, b_mn)[0]
+    torch.cuda.synchronize()
+    assert k.gemm_tc_status(0) == 0
+    err = (out.float().cpu() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, err
+
+
+@pytest.mark.parametrize("epi", ["gelu", "relu", "scale_residual"])
+def test_gemm_tc_fused_epilogues(cuda_device, epi):
+    from mmltk_b200.ops.gemm import gemm_nt_epilogue
+    g = torch.Generator().manual_seed(3)
+    M, N, K = 333, 384, 384
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    B = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16)
+    bias = torch.randn(N, generator=g).to(torch.bfloat16)
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    gamma = torch.rand(N, generator=g).to(torch.bfloat16)
+    pre = A.float() @ B.float().t() + bias.float()
+    ref = {"gelu": torch.nn.functional.gelu(pre), "relu": torch.relu(pre),
+           "scale_residual": res.float() + gamma.float() * pre}[epi]
+    d = lambda t: t.to(cuda_device)
+    out, pre_d = gemm_nt_epilogue(d(A), d(B), d(bias), epi, d(res), d(gamma))
+    assert (pre_d.float().cpu() - pre).abs().max().item() < 2e-2 * pre.abs().max().item()
+    assert (out.float().cpu() - ref).abs().max().item() < 2e-2 * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("N", [128, 192, 384, 1152, 272])
+def test_gemm_tc_tile_widths(cuda_device, N):
+    """Tile widths 128 / 192 / 256 and a ragged N (272 = 256 + 16) with every epilogue."""
+    from mmltk_b200.ops.gemm import gemm_nt_epilogue
+    g = torch.Generator().manual_seed(N)
+    M, K = 200, 320
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    B = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16)
+    bias = torch.randn(N, generator=g).to(torch.bfloat16)
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    gamma = torch.rand(N, generator=g).to(torch.bfloat16)
+    pre = A.float() @ B.float().t() + bias.float()
+    d = lambda t: t.to(cuda_device)
+    plain = kernels().gemm_tc(d(A), d(B), None, False, False)[0]
+    ref0 = A.float() @ B.float().t()
+    assert (plain.float().cpu() - ref0).abs().max().item() < 1e-2 * ref0.abs().max().item()
+    out, pre_d = gemm_nt_epilogue(d(A), d(B), d(bias), "scale_residual", d(res), d(gamma))
+    ref = res.float() + gamma.float() * pre
+    assert (pre_d.float().cpu() - pre).abs().max().item() < 2e-2 * pre.abs().max().item()
+    assert (out.float().cpu() - ref).abs().max().item() < 2e-2 * ref.abs().max().item()
