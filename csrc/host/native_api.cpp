@@ -1,5 +1,13 @@
 #include "native_api.h"
 
 namespace mmltk {
-void register_native_api(pybind11::module& m) { (void)m; }
+
+void register_data_api(pybind11::module& m);
+void register_eval_api(pybind11::module& m);
+
+void register_native_api(pybind11::module& m) {
+    register_data_api(m);
+    register_eval_api(m);
+}
+
 }  // namespace mmltk

@@ -54,7 +54,7 @@ def extensions():
     inc = [os.path.join(ROOT, "csrc", "include"), os.path.join(ROOT, "csrc", "kernels")]
     return [
         CppExtension("mmltk_b200._native", host_src, include_dirs=inc + [os.path.join(ROOT, "csrc", "host")],
-                     extra_compile_args={"cxx": CXX_FLAGS}, extra_link_args=["-lpthread"]),
+                     extra_compile_args={"cxx": CXX_FLAGS}, extra_link_args=["-lpthread", "-lz"]),
         CUDAExtension("mmltk_b200._kernels", kern_src, include_dirs=inc,
                       extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
                       libraries=["cuda"] if False else []),
