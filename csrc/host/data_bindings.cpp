@@ -17,6 +17,7 @@ namespace {
 
 using data::Loader;
 using data::Reader;
+using data::PackedInstance;
 
 template <typename T>
 std::vector<T> to_vec(const torch::Tensor& t) {
@@ -95,7 +96,7 @@ py::tuple instances_py(const Reader& r, uint32_t i) {
 }
 
 // Padded targets of a batch: boxes [B,T,4] normalised cxcywh (pad box (0.5,0.5,0.25,0.25)),
-// labels [B,T] int64, counts [B] int32, areas [B,T] (mask area or box area, normalised).
+// labels [B,T] int64, counts [B] int32, areas [B,T] (mask area or box area, pixels).
 py::tuple targets_py(const Reader& r, std::vector<uint32_t> idx, int T) {
     const int B = int(idx.size());
     const float W = float(r.header().width), H = float(r.header().height);
@@ -127,10 +128,25 @@ py::tuple targets_py(const Reader& r, std::vector<uint32_t> idx, int T) {
                 area = 0;
                 for (int q = 0; q < p[k].rle_pairs; ++q) area += r.rle()[p[k].rle_offset + q].length;
             }
-            areas.data_ptr<float>()[int64_t(b) * T + k] = float(area / (W * H));
+            areas.data_ptr<float>()[int64_t(b) * T + k] = float(area);
         }
     }
     return py::make_tuple(boxes, labels, counts, areas);
+}
+
+// One instance's binary mask (runs, or the box when it has none) into m [H, W] (zeroed by the caller).
+void fill_mask(const Reader& r, const PackedInstance& p, uint8_t* m) {
+    const int W = int(r.header().width), H = int(r.header().height);
+    if (!p.rle_pairs) {
+        for (int y = std::max<int>(0, p.y1); y < std::min<int>(H, p.y2); ++y)
+            std::fill(m + int64_t(y) * W + std::max<int>(0, p.x1), m + int64_t(y) * W + std::min<int>(W, p.x2), 1);
+        return;
+    }
+    for (int q = 0; q < p.rle_pairs; ++q) {
+        const auto& rp = r.rle()[p.rle_offset + q];
+        const uint64_t s = rp.start, l = rp.length, lim = uint64_t(W) * H;
+        std::fill(m + std::min(s, lim), m + std::min(s + l, lim), 1);
+    }
 }
 
 // Binary masks of the first T instances of each image, concatenated image-major: [sum(counts), H, W] uint8.
@@ -142,23 +158,27 @@ torch::Tensor masks_py(const Reader& r, std::vector<uint32_t> idx, int T) {
     uint8_t* o = out.data_ptr<uint8_t>();
     int64_t row = 0;
     for (auto i : idx) {
-        const auto& e = r.entry(i);
         const auto* p = r.instances(i);
-        for (int k = 0; k < std::min<int>(e.num_instances, T); ++k, ++row) {
-            uint8_t* m = o + row * int64_t(H) * W;
-            if (!p[k].rle_pairs) {  // no mask: the box
-                for (int y = std::max<int>(0, p[k].y1); y < std::min<int>(H, p[k].y2); ++y)
-                    std::fill(m + int64_t(y) * W + std::max<int>(0, p[k].x1), m + int64_t(y) * W + std::min<int>(W, p[k].x2), 1);
-                continue;
-            }
-            for (int q = 0; q < p[k].rle_pairs; ++q) {
-                const auto& rp = r.rle()[p[k].rle_offset + q];
-                const uint64_t s = rp.start, l = rp.length, lim = uint64_t(W) * H;
-                std::fill(m + std::min(s, lim), m + std::min(s + l, lim), 1);
-            }
-        }
+        for (int k = 0; k < std::min<int>(r.entry(i).num_instances, T); ++k, ++row)
+            fill_mask(r, p[k], o + row * int64_t(H) * W);
     }
     return out;
+}
+
+// Masks of (image, instance) pairs into a caller-owned [>= n, H, W] uint8 host tensor (pinned for upload).
+void instance_masks_py(const Reader& r, const std::vector<std::pair<uint32_t, uint32_t>>& pairs, torch::Tensor out) {
+    const int W = int(r.header().width), H = int(r.header().height);
+    TORCH_CHECK(!out.is_cuda() && out.is_contiguous() && out.scalar_type() == torch::kUInt8 &&
+                    out.numel() >= int64_t(pairs.size()) * H * W,
+                "instance_masks: contiguous host uint8 [n, H, W] expected");
+    uint8_t* o = out.data_ptr<uint8_t>();
+    const int64_t plane = int64_t(H) * W;
+    std::memset(o, 0, size_t(pairs.size()) * size_t(plane));
+    for (size_t n = 0; n < pairs.size(); ++n) {
+        const auto [img, k] = pairs[n];
+        if (img >= r.num_images() || k >= r.entry(img).num_instances) throw std::out_of_range("instance_masks");
+        fill_mask(r, r.instances(img)[k], o + int64_t(n) * plane);
+    }
 }
 
 torch::Tensor image_py(const Reader& r, uint32_t i) {
@@ -195,10 +215,11 @@ void register_data_api(pybind11::module& m) {
         .def("image", &image_py)
         .def("instances", &instances_py)
         .def("targets", &targets_py)
-        .def("masks", &masks_py);
+        .def("masks", &masks_py)
+        .def("instance_masks", &instance_masks_py);
     py::class_<Loader>(m, "DatasetLoader")
         .def(py::init([](const std::string& path, int batch, bool shuffle, uint64_t seed, int rank, int count,
-                         bool drop_last, int workers, bool bf16, std::vector<int64_t> slot_ptrs, size_t slot_bytes) {
+                         bool drop_last, int workers, int format, std::vector<int64_t> slot_ptrs, size_t slot_bytes) {
                  Loader::Config c;
                  c.path = path;
                  c.batch = batch;
@@ -208,7 +229,7 @@ void register_data_api(pybind11::module& m) {
                  c.shard_count = count;
                  c.drop_last = drop_last;
                  c.workers = workers;
-                 c.bf16 = bf16;
+                 c.format = format;
                  std::vector<void*> slots;
                  for (auto p : slot_ptrs) slots.push_back(reinterpret_cast<void*>(p));
                  return std::make_unique<Loader>(c, slots, slot_bytes);

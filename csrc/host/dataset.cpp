@@ -244,7 +244,7 @@ Reader::~Reader() {
 // ---------------------------------------------------------------- loader
 Loader::Loader(const Config& cfg, std::vector<void*> slots, size_t slot_bytes)
     : cfg_(cfg), reader_(cfg.path), slots_(std::move(slots)), slot_bytes_(slot_bytes) {
-    const size_t need = size_t(cfg_.batch) * reader_.header().image_stride / (cfg_.bf16 ? 2 : 1);
+    const size_t need = size_t(cfg_.batch) * reader_.header().image_stride / (cfg_.format == 1 ? 2 : cfg_.format == 2 ? 4 : 1);
     if (slot_bytes_ < need) throw std::runtime_error("loader: slot buffers are too small for one batch");
     if (slots_.empty()) throw std::runtime_error("loader: at least one slot buffer is needed");
     if (cfg_.shard_count < 1 || cfg_.shard_rank < 0 || cfg_.shard_rank >= cfg_.shard_count)
@@ -299,9 +299,12 @@ void Loader::fill(int slot, const std::vector<uint32_t>& idx) {
     // images of one batch are gathered in parallel on the shared worker pool
     WorkerPool::global().parallel_for(int64_t(idx.size()), [&](int64_t k) {
         const float* src = reader_.pixels(idx[k]);
-        if (cfg_.bf16) {
+        if (cfg_.format == 1) {
             uint16_t* dst = static_cast<uint16_t*>(slots_[slot]) + k * floats;
             for (size_t i = 0; i < floats; ++i) dst[i] = f2bf(src[i]);
+        } else if (cfg_.format == 2) {
+            uint8_t* dst = static_cast<uint8_t*>(slots_[slot]) + k * floats;
+            for (size_t i = 0; i < floats; ++i) dst[i] = uint8_t(std::lrintf(std::min(1.f, std::max(0.f, src[i])) * 255.f));
         } else {
             std::memcpy(static_cast<uint8_t*>(slots_[slot]) + k * stride, src, stride);
         }

@@ -78,7 +78,8 @@ class Reader {
 
 // Prefetching batch loader.  Slots are caller-owned host buffers (pinned by
 // the caller) of `slot_bytes` each, filled with `batch` images as float32 or
-// bf16 planar RGB.
+// bf16 planar RGB, or as uint8 (round(255 x)): the compiled pixels are k/255,
+// so uint8 is exact and moves a quarter of the fp32 bytes host -> device.
 class Loader {
    public:
     struct Config {
@@ -89,7 +90,7 @@ class Loader {
         int shard_rank = 0, shard_count = 1;
         bool drop_last = false;
         int workers = 4;
-        bool bf16 = false;
+        int format = 0;  // 0 fp32, 1 bf16, 2 uint8
     };
     Loader(const Config& cfg, std::vector<void*> slots, size_t slot_bytes);
     ~Loader();

@@ -4,10 +4,12 @@ namespace mmltk {
 
 void register_data_api(pybind11::module& m);
 void register_eval_api(pybind11::module& m);
+void register_aug_api(pybind11::module& m);
 
 void register_native_api(pybind11::module& m) {
     register_data_api(m);
     register_eval_api(m);
+    register_aug_api(m);
 }
 
 }  // namespace mmltk

@@ -67,4 +67,12 @@ cudaError_t launch_dense_neg_fwd(DType t, const void* x, int64_t n, float coef, 
 cudaError_t launch_dense_neg_bwd(DType t, const void* x, const float* g, int64_t n, float coef, void* dx,
                                  cudaStream_t st);
 
+// ---------------------------------------------------------------- augmentation
+// in: [B,3,H,W] uint8 (k/255) or fp32 in [0,1]; out: normalised bf16 / fp32; rec: [B,64] host-drawn
+// records or null (normalise only); donors: [slots,3,H,W] like `in`; donor_masks: [slots,H,W] uint8.
+cudaError_t launch_augment(DType out_t, bool in_u8, const void* in, void* out, const float* rec, const void* donors,
+                           const uint8_t* donor_masks, int B, int H, int W, cudaStream_t st);
+cudaError_t launch_warp_masks(const uint8_t* src, const uint8_t* donor_masks, const int32_t* rows, const float* rec,
+                              uint8_t* out, int N, int H, int W, cudaStream_t st);
+
 }  // namespace mmltk

@@ -95,6 +95,7 @@ void register_more_ops(pybind11::module& m) {
     m.def("act_bwd", &act_bwd);
     register_ddp_ops(m);
     register_gemm_ops(m);
+    register_aug_ops(m);
 }
 
 }  // namespace mmltk

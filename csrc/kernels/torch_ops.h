@@ -15,5 +15,6 @@ cudaStream_t cur_stream();
 void register_more_ops(pybind11::module& m);
 void register_ddp_ops(pybind11::module& m);
 void register_gemm_ops(pybind11::module& m);
+void register_aug_ops(pybind11::module& m);
 
 }  // namespace mmltk

@@ -19,6 +19,9 @@ from ..ops._ext import native
 
 __all__ = ["CompiledDataset", "BatchLoader"]
 
+# host slot formats: the compiled pixels are k/255, so uint8 is exact and the cheapest to upload
+_FORMATS = {"float32": (0, torch.float32), "bfloat16": (1, torch.bfloat16), "uint8": (2, torch.uint8)}
+
 
 class CompiledDataset:
     """Random access to a compiled ``.bin`` (memory-mapped)."""
@@ -62,21 +65,23 @@ class CompiledDataset:
 class BatchLoader:
     def __init__(self, path: str, batch_size: int, shuffle: bool = True, seed: int = 42, shard_rank: int = 0,
                  shard_count: int = 1, drop_last: bool = False, workers: int = 4, prefetch: int = 3,
-                 bf16: bool = True, max_targets: int = 100, device: Optional[torch.device] = None,
+                 pixels: str = "uint8", max_targets: int = 100, device: Optional[torch.device] = None,
                  with_masks: bool = False):
         self.dataset = CompiledDataset(path)
         w, h = self.dataset.size
         self.batch_size = batch_size
-        self.bf16 = bf16
+        if pixels not in _FORMATS:
+            raise ValueError(f"pixels must be one of {sorted(_FORMATS)}")
+        self.pixels = pixels
         self.max_targets = max_targets
         self.with_masks = with_masks
         self.device = device
-        dtype = torch.bfloat16 if bf16 else torch.float32
+        code, dtype = _FORMATS[pixels]
         pin = torch.cuda.is_available()
         self.slots = [torch.empty(batch_size, 3, h, w, dtype=dtype, pin_memory=pin) for _ in range(max(2, prefetch))]
         nbytes = self.slots[0].numel() * self.slots[0].element_size()
         self.loader = native().DatasetLoader(path, batch_size, shuffle, seed, shard_rank, shard_count, drop_last,
-                                             workers, bf16, [s.data_ptr() for s in self.slots], nbytes)
+                                             workers, code, [s.data_ptr() for s in self.slots], nbytes)
         self.copy_stream = torch.cuda.Stream(device) if (device is not None and torch.device(device).type == "cuda") else None
         self.epoch = 0
 

@@ -71,7 +71,7 @@ def test_loader_epoch_shard_and_targets(compiled):
     seen = []
     for rank in range(2):
         bl = BatchLoader(stats["path"], batch_size=2, shuffle=True, seed=3, shard_rank=rank, shard_count=2,
-                         bf16=False, max_targets=6)
+                         pixels="float32", max_targets=6)
         assert len(bl) == 2  # 5 batches -> 2 per rank
         for images, targets, idx in bl:
             assert images.shape == (2, 3, 64, 64)
@@ -87,7 +87,7 @@ def test_loader_epoch_shard_and_targets(compiled):
 
 def test_loader_bf16_and_masks(compiled):
     _, stats = compiled
-    bl = BatchLoader(stats["path"], batch_size=3, shuffle=False, bf16=True, max_targets=8, with_masks=True)
+    bl = BatchLoader(stats["path"], batch_size=3, shuffle=False, pixels="bfloat16", max_targets=8, with_masks=True)
     images, targets, idx = next(iter(bl))
     assert images.dtype == torch.bfloat16
     assert (images.float() - torch.stack([bl.dataset.image(i) for i in idx])).abs().max() < 4e-3
