@@ -1,0 +1,4 @@
+"""Evaluation: COCO-style AP over compiled splits."""
+from .coco import CocoEvaluator
+
+__all__ = ["CocoEvaluator"]
