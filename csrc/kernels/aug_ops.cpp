@@ -68,9 +68,44 @@ torch::Tensor warp_masks(torch::Tensor src, torch::Tensor donor_masks, torch::Te
     return out;
 }
 
+// logits [B,Q,C], boxes [B,Q,4] -> (scores [B,K], labels [B,K] int64, boxes [B,K,4] xyxy px, queries [B,K] int32)
+std::vector<torch::Tensor> topk_postprocess(torch::Tensor logits, torch::Tensor boxes, int64_t K,
+                                            c10::optional<torch::Tensor> sizes, double fixed_h, double fixed_w) {
+    TORCH_CHECK(logits.is_cuda() && logits.dim() == 3 && boxes.dim() == 3 && boxes.size(2) == 4 &&
+                    boxes.size(0) == logits.size(0) && boxes.size(1) == logits.size(1),
+                "topk_postprocess: logits [B,Q,C], boxes [B,Q,4] on CUDA");
+    at::cuda::CUDAGuard guard(logits.device());
+    auto l = logits.contiguous();
+    auto b = boxes.contiguous();
+    TORCH_CHECK(l.scalar_type() == torch::kBFloat16 || l.scalar_type() == torch::kFloat32, "logits bf16/fp32");
+    TORCH_CHECK(b.scalar_type() == torch::kBFloat16 || b.scalar_type() == torch::kFloat32, "boxes bf16/fp32");
+    const int64_t B = l.size(0), Q = l.size(1), C = l.size(2);
+    TORCH_CHECK(K > 0 && K <= 1024 && K <= Q * C, "topk_postprocess: 0 < K <= min(1024, Q*C)");
+    const float* sp = nullptr;
+    torch::Tensor sz;
+    if (sizes && sizes->defined()) {
+        sz = sizes->to(l.device(), torch::kFloat32).contiguous();
+        TORCH_CHECK(sz.dim() == 2 && sz.size(0) == B && sz.size(1) == 2, "sizes [B,2] (h, w)");
+        sp = sz.data_ptr<float>();
+    }
+    auto fo = l.options().dtype(torch::kFloat32);
+    auto scores = torch::empty({B, K}, fo);
+    auto labels = torch::empty({B, K}, l.options().dtype(torch::kInt64));
+    auto ob = torch::empty({B, K, 4}, fo);
+    auto qs = torch::empty({B, K}, l.options().dtype(torch::kInt32));
+    check_cuda(launch_topk_postprocess(dtype_of(l), dtype_of(b), l.data_ptr(), b.data_ptr(), sp, int(B), int(Q),
+                                       int(C), int(K), float(fixed_h), float(fixed_w), scores.data_ptr<float>(),
+                                       labels.data_ptr<int64_t>(), ob.data_ptr<float>(), qs.data_ptr<int32_t>(),
+                                       cur_stream()),
+               "topk_postprocess");
+    return {scores, labels, ob, qs};
+}
+
 }  // namespace
 
 void register_aug_ops(pybind11::module& m) {
+    m.def("topk_postprocess", &topk_postprocess, py::arg("logits"), py::arg("boxes"), py::arg("k"),
+          py::arg("sizes") = py::none(), py::arg("fixed_h") = 1.0, py::arg("fixed_w") = 1.0);
     m.def("augment_images", &augment_images, py::arg("images"), py::arg("out"), py::arg("records") = py::none(),
           py::arg("donors") = py::none(), py::arg("donor_masks") = py::none());
     m.def("warp_masks", &warp_masks);

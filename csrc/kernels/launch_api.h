@@ -75,4 +75,11 @@ cudaError_t launch_augment(DType out_t, bool in_u8, const void* in, void* out, c
 cudaError_t launch_warp_masks(const uint8_t* src, const uint8_t* donor_masks, const int32_t* rows, const float* rec,
                               uint8_t* out, int N, int H, int W, cudaStream_t st);
 
+// ---------------------------------------------------------------- detection post-process
+// logits [B,Q,C], boxes [B,Q,4] cxcywh (normalised); sizes [B,2] (h, w) fp32 or null (fixed_h/w).
+// K <= 1024.  Outputs: scores [B,K] f32, labels [B,K] i64, boxes [B,K,4] xyxy pixels, queries [B,K] i32.
+cudaError_t launch_topk_postprocess(DType lt, DType bt, const void* logits, const void* boxes, const float* sizes,
+                                    int B, int Q, int C, int K, float fixed_h, float fixed_w, float* scores,
+                                    int64_t* labels, float* out_boxes, int32_t* queries, cudaStream_t st);
+
 }  // namespace mmltk
