@@ -216,7 +216,12 @@ void register_data_api(pybind11::module& m) {
         .def("instances", &instances_py)
         .def("targets", &targets_py)
         .def("masks", &masks_py)
-        .def("instance_masks", &instance_masks_py);
+        .def("instance_masks", &instance_masks_py)
+        .def("instance_counts", [](const Reader& r) {
+            auto t = torch::empty({int64_t(r.num_images())}, torch::kInt32);
+            for (uint32_t i = 0; i < r.num_images(); ++i) t.data_ptr<int32_t>()[i] = r.entry(i).num_instances;
+            return t;
+        });
     py::class_<Loader>(m, "DatasetLoader")
         .def(py::init([](const std::string& path, int batch, bool shuffle, uint64_t seed, int rank, int count,
                          bool drop_last, int workers, int format, std::vector<int64_t> slot_ptrs, size_t slot_bytes) {

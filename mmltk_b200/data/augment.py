@@ -22,17 +22,19 @@ CPU path and the oracle of the kernel tests.
 """
 from __future__ import annotations
 
-import dataclasses
 from typing import List, Optional, Sequence, Tuple
 
 import torch
 
+from ..config.train_options import AugGroup as AugmentGroup
+from ..config.train_options import AugmentationConfig as AugmentConfig
 from ..criterion.targets import Targets
 from ..ops._ext import kernels, native
 
-__all__ = ["AugmentGroup", "AugmentConfig", "GpuAugmenter", "augment_reference", "normalize_images",
+__all__ = ["AugmentGroup", "AugmentConfig", "config_to_native", "GpuAugmenter", "augment_reference", "normalize_images",
            "IMAGENET_MEAN", "IMAGENET_STD", "REC"]
 
+_GROUPS = ("geometry", "resize", "color", "noise", "blur", "occlusion")
 IMAGENET_MEAN = (0.485, 0.456, 0.406)
 IMAGENET_STD = (0.229, 0.224, 0.225)
 
@@ -42,47 +44,19 @@ REC = dict(inv=0, fwd=6, color=12, color_off=21, noise_mode=24, noise_str=25, bl
            paste_box=45, floats=64)
 
 
-@dataclasses.dataclass
-class AugmentGroup:
-    probability: float = 0.5
-    min_strength: float = 0.05
-    max_strength: float = 0.5
+def config_to_native(cfg: AugmentConfig) -> dict:
+    if not cfg.valid():
+        raise ValueError("augmentation: every group needs 0 <= probability <= 1 and "
+                         "0 <= min_strength <= max_strength <= 1, and copy-paste probability in [0, 1]")
+    d = {g: (getattr(cfg, g).probability, getattr(cfg, g).min_strength, getattr(cfg, g).max_strength)
+         for g in _GROUPS}
+    d["enabled"] = bool(cfg.enabled)
+    d["copy_paste"] = float(cfg.copy_paste_probability)
+    return d
 
-    def valid(self) -> bool:
-        return 0 <= self.probability <= 1 and 0 <= self.min_strength <= self.max_strength <= 1
 
-
-@dataclasses.dataclass
-class AugmentConfig:
-    enabled: bool = False
-    geometry: AugmentGroup = dataclasses.field(default_factory=AugmentGroup)
-    resize: AugmentGroup = dataclasses.field(default_factory=AugmentGroup)
-    color: AugmentGroup = dataclasses.field(default_factory=AugmentGroup)
-    noise: AugmentGroup = dataclasses.field(default_factory=AugmentGroup)
-    blur: AugmentGroup = dataclasses.field(default_factory=AugmentGroup)
-    occlusion: AugmentGroup = dataclasses.field(default_factory=AugmentGroup)
-    copy_paste_probability: float = 0.5
-
-    GROUPS = ("geometry", "resize", "color", "noise", "blur", "occlusion")
-
-    def validate(self) -> None:
-        for g in self.GROUPS:
-            if not getattr(self, g).valid():
-                raise ValueError(f"augmentation group {g}: need 0 <= probability <= 1 and "
-                                 f"0 <= min_strength <= max_strength <= 1")
-        if not 0 <= self.copy_paste_probability <= 1:
-            raise ValueError("copy-paste probability must lie in [0, 1]")
-
-    def to_native(self) -> dict:
-        d = {g: (getattr(self, g).probability, getattr(self, g).min_strength, getattr(self, g).max_strength)
-             for g in self.GROUPS}
-        d["enabled"] = bool(self.enabled)
-        d["copy_paste"] = float(self.copy_paste_probability)
-        return d
-
-    @property
-    def copy_paste(self) -> bool:
-        return self.enabled and self.copy_paste_probability > 0
+def _copy_paste_on(cfg: AugmentConfig) -> bool:
+    return cfg.enabled and cfg.copy_paste_probability > 0
 
 
 # ------------------------------------------------------------------ torch restatement (CPU path / oracle)
@@ -258,7 +232,6 @@ class GpuAugmenter:
     def __init__(self, config: AugmentConfig, capacity: int, height: int, width: int, slots: int,
                  device: Optional[torch.device] = None, masks: bool = False, seed: int = 42, rank: int = 0,
                  out_dtype: torch.dtype = torch.bfloat16):
-        config.validate()
         self.config = config
         self.capacity, self.H, self.W, self.T = capacity, height, width, slots
         self.device = torch.device(device) if device is not None else torch.device("cpu")
@@ -266,7 +239,7 @@ class GpuAugmenter:
         self.masks = masks
         self.seed, self.rank = seed, rank
         self.out_dtype = out_dtype
-        self.planner = native().AugmentPlanner(config.to_native(), capacity, width, height, masks)
+        self.planner = native().AugmentPlanner(config_to_native(config), capacity, width, height, masks)
         pin = self.cuda
         self._ring = [self._staging(pin) for _ in range(2)]
         self._turn = 0
@@ -274,9 +247,9 @@ class GpuAugmenter:
         self.records = torch.empty(capacity, REC["floats"], device=dev)
         self.out = torch.empty(capacity, 3, height, width, dtype=out_dtype, device=dev)
         self.donors = (torch.zeros(capacity, 3, height, width, dtype=torch.uint8, device=dev)
-                       if config.copy_paste else None)
+                       if _copy_paste_on(config) else None)
         self.donor_masks = (torch.zeros(capacity, height, width, dtype=torch.uint8, device=dev)
-                            if (config.copy_paste and masks) else torch.zeros(0, height, width, dtype=torch.uint8,
+                            if (_copy_paste_on(config) and masks) else torch.zeros(0, height, width, dtype=torch.uint8,
                                                                                   device=dev))
 
     def _staging(self, pin: bool) -> dict:

@@ -73,6 +73,9 @@ class TrainEngine:
             self._init_cpu(named, assign)
         self.graph = None
         self._graph_warmup = 0
+        # gradient accumulation: micro-batches before one optimizer step (eager; the graph path needs 1)
+        self.accum = max(1, int(opts.grad_accum_steps))
+        self._micro = 0
 
     # ------------------------------------------------------------------ setup
     def _init_cpu(self, named, assign):
@@ -131,11 +134,14 @@ class TrainEngine:
         total = self.criterion.weighted(losses)
         return total, losses
 
-    def _cuda_body(self, images, targets):
-        self.flags.zero_()
-        self.flat.zero_grad()
+    def _cuda_body(self, images, targets, first: bool = True, last: bool = True):
+        if first:
+            self.flags.zero_()
+            self.flat.zero_grad()
         total, losses = self._forward_loss(images, targets)
-        total.backward()
+        (total / self.accum if self.accum > 1 else total).backward()
+        if not last:
+            return total.detach(), {k: v.detach() for k, v in losses.items()}
         if self.grad_sync is not None:
             self.grad_sync.step(self)
         else:
@@ -165,6 +171,10 @@ class TrainEngine:
             t.labels[:, T:].zero_()
         t.counts.copy_(targets.counts, non_blocking=True)
         t.counts_host = list(targets.counts_host)
+        # segmentation targets: the mask rows change size with every batch, so they are
+        # passed through (and such steps run eagerly, outside the captured graph)
+        t.masks = None if targets.masks is None else targets.masks.to(self.device, non_blocking=True)
+        t.mask_offsets = targets.mask_offsets
 
     def step(self, images: Optional[torch.Tensor] = None, targets: Optional[Targets] = None,
              sync: bool = True) -> StepResult:
@@ -174,10 +184,22 @@ class TrainEngine:
             return self._cpu_step(images, targets)
         if images is not None:
             self.load_inputs(images, targets)
+        if self.accum > 1:
+            # micro-batch: forward + backward into the flat gradient, optimizer on the last one
+            first, last = self._micro == 0, self._micro == self.accum - 1
+            self._micro = 0 if last else self._micro + 1
+            if not last:
+                total, losses = self._cuda_body(self.in_images, self.in_targets, first=first, last=False)
+                return StepResult(total, losses, None, None)
+            sc = self._host_scalars(self.step_count)
+            self.scalars_host[:len(sc)] = torch.tensor(sc)
+            self.scalars.copy_(self.scalars_host, non_blocking=True)
+            total, losses = self._cuda_body(self.in_images, self.in_targets, first=first, last=True)
+            return self._finish(total, losses, sync)
         sc = self._host_scalars(self.step_count)
         self.scalars_host[:len(sc)] = torch.tensor(sc)
         self.scalars.copy_(self.scalars_host, non_blocking=True)
-        if self.opts.cuda_graph and self._graph_warmup >= 3:
+        if self.opts.cuda_graph and self._graph_warmup >= 3 and self.in_targets.masks is None:
             if self.graph is None:
                 self._capture()
             self.graph.replay()
@@ -185,6 +207,9 @@ class TrainEngine:
         else:
             total, losses = self._cuda_body(self.in_images, self.in_targets)
             self._graph_warmup += 1
+        return self._finish(total, losses, sync)
+
+    def _finish(self, total, losses, sync: bool) -> StepResult:
         self.step_count += 1
         if self.grad_sync is not None:
             self.grad_sync.after_step(self)
@@ -232,9 +257,14 @@ class TrainEngine:
         s = lr_scale(o, self.step_count, self.steps_per_epoch, self.total_steps)
         for g, base in zip(self.optimizer.param_groups, self.base_lrs):
             g["lr"] = base * s
-        self.optimizer.zero_grad(set_to_none=True)
+        first, last = self._micro == 0, self._micro == self.accum - 1
+        self._micro = 0 if last else self._micro + 1
+        if first:
+            self.optimizer.zero_grad(set_to_none=True)
         total, losses = self._forward_loss(images, targets)
-        total.backward()
+        (total / self.accum if self.accum > 1 else total).backward()
+        if not last:
+            return StepResult(float(total.detach()),{k: v.detach() for k, v in losses.items()}, None, 0)
         if self.grad_sync is not None:
             self.grad_sync.cpu_average(self.params)
         norm = torch.nn.utils.clip_grad_norm_(self.params, o.clip_max_norm) if o.clip_max_norm > 0 else None
@@ -247,7 +277,7 @@ class TrainEngine:
                 torch._foreach_mul_(self.ema, d)
                 torch._foreach_add_(self.ema, [p.detach() for p in self.params], alpha=1 - d)
         self.step_count += 1
-        return StepResult(float(total), {k: v.detach() for k, v in losses.items()},
+        return StepResult(float(total.detach()),{k: v.detach() for k, v in losses.items()},
                           None if norm is None else float(norm), 0)
 
     # ------------------------------------------------------------------ state
@@ -256,3 +286,112 @@ class TrainEngine:
             return None if self.ema is None else {n: t for n, t in zip(self.ema_named, self.ema)}
         buf = self.grad_sync.gather_ema(self) if self.grad_sync is not None else self.ema_buf
         return None if buf is None else self.flat.state_dict_tensors(buf)
+
+    # flat fp32 buffers, full length, on this device ("master", "m", "v", "ema"); sharded copies are gathered
+    def _full(self, which: str) -> Optional[torch.Tensor]:
+        sharded = getattr(self, "master_shard", None) is not None and self.master is None
+        local = {"master": self.master_shard if sharded else self.master, "m": self.m, "v": self.v,
+                 "ema": self.ema_buf}[which]
+        if local is None:
+            return None
+        return self.grad_sync.gather_full(local) if sharded else local
+
+    def export_model(self, which: str = "master") -> torch.nn.Module:
+        """An fp32 CPU copy of the model holding the master (or EMA) weights -- for checkpoints
+        and evaluation; its ``state_dict()`` has the checkpoint key layout."""
+        import copy
+        if not self.cuda:
+            m = copy.deepcopy(self.model).float()
+            if which == "ema" and self.ema is not None:
+                named = dict(m.named_parameters())
+                with torch.no_grad():
+                    for n, t in zip(self.ema_named, self.ema):
+                        named[n].copy_(t)
+            return m
+        buf = self._full("ema" if which == "ema" else "master")
+        if buf is None:
+            raise ValueError(f"no {which} weights (EMA disabled?)")
+        host = buf.float().cpu()
+        m = copy.deepcopy(self.model).to("cpu", torch.float32)
+        named = dict(m.named_parameters())
+        with torch.no_grad():
+            for i, n in enumerate(self.flat.names):
+                o, c = self.flat.offsets[i], self.flat.numels[i]
+                named[n].copy_(host[o:o + c].view_as(named[n]))
+        return m
+
+    def optimizer_state(self) -> dict:
+        """Per-parameter AdamW state in a world-size independent layout (archive-ready dict)."""
+        d = {"kind": "adamw", "step": int(self.step_count)}
+        if not self.cuda:
+            names = [n for n, _ in zip(self.ema_named, self.params)]
+            for i, (n, p) in enumerate(zip(names, self.params)):
+                st = self.optimizer.state.get(p, {})
+                e = {"name": n}
+                if st:
+                    e["exp_avg"] = st["exp_avg"].detach().cpu()
+                    e["exp_avg_sq"] = st["exp_avg_sq"].detach().cpu()
+                d[f"entry_{i:06d}"] = e
+            d["entry_count"] = len(names)
+            return d
+        m, v = self._full("m").cpu(), self._full("v").cpu()
+        for i, n in enumerate(self.flat.names):
+            o, c = self.flat.offsets[i], self.flat.numels[i]
+            d[f"entry_{i:06d}"] = {"name": n, "exp_avg": m[o:o + c].clone(), "exp_avg_sq": v[o:o + c].clone()}
+        d["entry_count"] = len(self.flat.names)
+        return d
+
+    def load_optimizer_state(self, d: dict) -> None:
+        if d.get("kind") != "adamw":
+            raise ValueError(f"resume: optimizer kind {d.get('kind')!r} does not match 'adamw'")
+        entries = {d[f"entry_{i:06d}"]["name"]: d[f"entry_{i:06d}"] for i in range(int(d["entry_count"]))}
+        self.step_count = int(d["step"])
+        if not self.cuda:
+            for n, p in zip(self.ema_named, self.params):
+                e = entries.get(n)
+                if e is None or "exp_avg" not in e:
+                    continue
+                self.optimizer.state[p] = {"step": torch.tensor(float(self.step_count)),
+                                           "exp_avg": e["exp_avg"].to(p.device).view_as(p).clone(),
+                                           "exp_avg_sq": e["exp_avg_sq"].to(p.device).view_as(p).clone()}
+            return
+        full_m = torch.zeros(self.flat.total, dtype=torch.float32)
+        full_v = torch.zeros(self.flat.total, dtype=torch.float32)
+        for i, n in enumerate(self.flat.names):
+            e = entries.get(n)
+            if e is None:
+                raise ValueError(f"resume: optimizer state has no entry for {n}")
+            o, c = self.flat.offsets[i], self.flat.numels[i]
+            full_m[o:o + c] = e["exp_avg"].reshape(-1)
+            full_v[o:o + c] = e["exp_avg_sq"].reshape(-1)
+        sharded = getattr(self, "master_shard", None) is not None and self.master is None
+        if sharded:
+            off, size = self.grad_sync.off, self.grad_sync.size
+            self.m.copy_(full_m[off:off + size])
+            self.v.copy_(full_v[off:off + size])
+        else:
+            self.m.copy_(full_m)
+            self.v.copy_(full_v)
+
+    def load_ema_state(self, state: Dict[str, torch.Tensor]) -> None:
+        """EMA shadow from a name -> tensor dict keyed by parameter names."""
+        if not self.cuda:
+            if self.ema is None:
+                return
+            with torch.no_grad():
+                for n, t in zip(self.ema_named, self.ema):
+                    if n in state:
+                        t.copy_(state[n].view_as(t))
+            return
+        if self.ema_buf is None:
+            return
+        full = torch.zeros(self.flat.total, dtype=torch.float32)
+        for i, n in enumerate(self.flat.names):
+            o, c = self.flat.offsets[i], self.flat.numels[i]
+            if n in state:
+                full[o:o + c] = state[n].reshape(-1).float()
+        sharded = getattr(self, "master_shard", None) is not None and self.master is None
+        if sharded:
+            self.ema_buf.copy_(full[self.grad_sync.off:self.grad_sync.off + self.grad_sync.size])
+        else:
+            self.ema_buf.copy_(full)

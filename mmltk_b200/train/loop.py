@@ -1,0 +1,335 @@
+"""``run_training``: the epoch loop around :class:`TrainEngine`.
+
+Reference: `src/rfdetr/training/train.cpp:1870-2730` -- option validation,
+distributed context, loaders (rank-sharded, ``drop_last``), artifact
+resolution with ``num_classes`` from the dataset, weights / resume, the epoch
+loop, per-epoch validation of the regular and (optionally) EMA weights,
+checkpoints (``checkpoint.pt`` for resume, ``checkpoint_epoch_<n>.pt``,
+``checkpoint_best_regular.pt``, ``checkpoint_best_ema.pt``), ``progress.json``
+(throttled, atomic), ``log.txt`` (one JSON line per epoch) and
+``results.json``.
+
+Differences by design:
+* augmentation and target building run through :class:`GpuAugmenter`
+  (host plan + one fused kernel), and the step through the CUDA-graph engine
+  with the fused NVSwitch gradient step when more than one GPU is used;
+* validation is distributed: every rank evaluates a shard of the validation
+  split and the match records are all-gathered, instead of rank 0 alone.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import threading
+import time
+from typing import Dict, Optional
+
+import torch
+
+from ..ckpt import CheckpointMetadata, load_native_checkpoint, save_native_checkpoint
+from ..ckpt.native import state_from_archive, state_to_archive
+from ..config import TrainOptions
+from ..data.augment import GpuAugmenter
+from ..data.loader import BatchLoader, CompiledDataset
+from ..infer.predictor import Predictor, resolve_model
+from ..parallel.launch import DistContext, init_distributed
+
+__all__ = ["run_training", "ProgressWriter", "checkpoint_metric"]
+
+
+class ProgressWriter:
+    """Latest-state JSON file: throttled writes, atomic replace, ``phase: "error"`` on failure
+    (reference `LatestJsonWriter`, `train.cpp:606-768`)."""
+
+    def __init__(self, path: str, min_interval_s: float = 0.25):
+        self.path = path
+        self.min_interval = min_interval_s
+        self.last = 0.0
+        self.state: Dict = {}
+        self.lock = threading.Lock()
+
+    def submit(self, update: Dict, force: bool = False) -> None:
+        with self.lock:
+            self.state.update(update)
+            now = time.monotonic()
+            if not force and now - self.last < self.min_interval:
+                return
+            self.last = now
+            tmp = self.path + ".tmp"
+            with open(tmp, "w") as f:
+                json.dump(self.state, f, indent=1)
+            os.replace(tmp, self.path)
+
+    def error(self, message: str) -> None:
+        self.submit({"phase": "error", "error": message}, force=True)
+
+
+def checkpoint_metric(summary: Dict, masks: bool) -> float:
+    key = "segm" if masks and "segm" in summary else "bbox"
+    return float(summary[key]["ap"])
+
+
+def _summary_json(s: Optional[Dict]) -> Dict:
+    if not s:
+        return {}
+    out = {"bbox": {k: s["bbox"][k] for k in ("ap", "ap50", "ap75")}}
+    if "segm" in s:
+        out["mask"] = {k: s["segm"][k] for k in ("ap", "ap50", "ap75")}
+    return out
+
+
+def _augmentation_json(a) -> Dict:
+    g = lambda x: {"probability": x.probability, "min_strength": x.min_strength, "max_strength": x.max_strength}
+    return {"enabled": a.enabled, "geometry": g(a.geometry), "resize": g(a.resize), "color": g(a.color),
+            "noise": g(a.noise), "blur": g(a.blur), "occlusion": g(a.occlusion),
+            "copy_paste_probability": a.copy_paste_probability}
+
+
+def _resume_extra(opts: TrainOptions, engine, epoch: int, best_regular: float, best_ema: float) -> Dict:
+    d = {"optimizer_kind": "adamw", "optimizer": engine.optimizer_state(), "epoch": int(epoch),
+         "lr_scheduler": opts.lr_scheduler, "lr_drop": int(opts.lr_drop), "warmup_epochs": float(opts.warmup_epochs),
+         "warmup_momentum": float(opts.warmup_momentum), "lr_min_factor": float(opts.lr_min_factor),
+         "gpu_augment_enabled": bool(opts.augmentation.enabled), "best_regular_metric": float(best_regular),
+         "best_ema_metric": float(best_ema), "grad_scaler_scale": 1.0, "grad_scaler_growth_tracker": 0}
+    a = opts.augmentation
+    for name in ("geometry", "resize", "color", "noise", "blur", "occlusion"):
+        g = getattr(a, name)
+        d[f"gpu_augment_{name}_probability"] = float(g.probability)
+        d[f"gpu_augment_{name}_min_strength"] = float(g.min_strength)
+        d[f"gpu_augment_{name}_max_strength"] = float(g.max_strength)
+    d["gpu_augment_copy_paste_probability"] = float(a.copy_paste_probability)
+    ema = engine.ema_state()
+    if ema is not None:
+        d["ema_state"] = state_to_archive({k: v.float().cpu() for k, v in ema.items()})
+    return d
+
+
+def _check_resume(extra: Dict, opts: TrainOptions) -> None:
+    for key, cur in (("lr_scheduler", opts.lr_scheduler), ("lr_drop", opts.lr_drop),
+                     ("warmup_epochs", opts.warmup_epochs), ("warmup_momentum", opts.warmup_momentum),
+                     ("lr_min_factor", opts.lr_min_factor)):
+        if key in extra and extra[key] != cur:
+            raise ValueError(f"resume checkpoint {key} ({extra[key]!r}) does not match the current options ({cur!r})")
+    if extra.get("optimizer_kind", "adamw") != "adamw":
+        raise ValueError("resume checkpoint optimizer_kind does not match the current options")
+    if "optimizer" not in extra:
+        raise ValueError("resume checkpoint is missing the optimizer state")
+
+
+def evaluate(model_fp32: torch.nn.Module, compiled: str, ctx: DistContext, batch_size: int, max_dets: int,
+             masks: bool, shard: bool = True) -> Dict:
+    """COCO AP of a model over a compiled split; each rank takes every world-th batch."""
+    from ..eval import CocoEvaluator
+    pred = Predictor(model_fp32, device=ctx.device, cuda_graph=ctx.device.type == "cuda", with_masks=masks)
+    ev = CocoEvaluator(compiled, masks=masks, max_dets=max_dets)
+    bl = BatchLoader(compiled, batch_size, shuffle=False, pixels="uint8", max_targets=1,
+                     shard_rank=ctx.rank if shard else 0, shard_count=ctx.world_size if shard else 1,
+                     device=ctx.device if ctx.device.type == "cuda" else None)
+    for images, _t, idx in bl:
+        if images.shape[0] != batch_size and pred.use_graph:
+            pad = torch.zeros(batch_size - images.shape[0], *images.shape[1:], dtype=images.dtype,
+                              device=images.device)
+            res = {k: v[:len(idx)] for k, v in pred(torch.cat([images, pad])).items()}
+        else:
+            res = pred(images)
+        ev.add(idx, res["scores"], res["labels"], res["boxes"], res.get("masks"))
+    # images left over by the per-rank sharding (fewer than one batch per rank) go to rank 0
+    n = len(bl.dataset)
+    covered = len(bl) * batch_size * (ctx.world_size if shard else 1)
+    if ctx.main and covered < n:
+        rest = list(range(covered, n))
+        for s in range(0, len(rest), batch_size):
+            ids = rest[s:s + batch_size]
+            x = torch.stack([(bl.dataset.image(i) * 255).round().to(torch.uint8) for i in ids]).to(ctx.device)
+            res = pred._step(x)
+            ev.add(ids, res["scores"], res["labels"], res["boxes"], res.get("masks"))
+    pred.release()
+    if shard and ctx.enabled:
+        ev.reduce()
+    return ev.summarize()
+
+
+def run_training(opts: TrainOptions, ctx: Optional[DistContext] = None) -> Dict:
+    opts.validate()
+    if not opts.train_compiled or not opts.val_compiled or not opts.output_dir:
+        raise ValueError("train needs --train-compiled, --val-compiled and --output-dir")
+    if bool(opts.weights) == bool(opts.resume) and (opts.weights or opts.resume):
+        raise ValueError("pass exactly one of --weights / --resume")
+    own_ctx = ctx is None
+    if ctx is None:
+        ctx = init_distributed(opts.dist_rank if opts.dist_worker else None,
+                               opts.dist_world_size if opts.dist_worker else None, opts.device_id,
+                               opts.dist_store_file)
+    torch.manual_seed(opts.seed + ctx.rank)
+    out_dir = opts.output_dir
+    paths = {k: os.path.join(out_dir, v) for k, v in dict(
+        progress="progress.json", log="log.txt", results="results.json", ckpt="checkpoint.pt",
+        best_regular="checkpoint_best_regular.pt", best_ema="checkpoint_best_ema.pt").items()}
+    progress = None
+    if ctx.main:
+        os.makedirs(out_dir, exist_ok=True)
+        for k in ("progress", "log", "results"):
+            if os.path.exists(paths[k]):
+                os.remove(paths[k])
+        progress = ProgressWriter(paths["progress"])
+    try:
+        result = _train(opts, ctx, paths, progress)
+    except BaseException as e:
+        if progress is not None:
+            progress.error(f"{type(e).__name__}: {e}")
+        raise
+    finally:
+        if own_ctx:
+            ctx.close()
+    return result
+
+
+def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress: Optional[ProgressWriter]) -> Dict:
+    from .engine import TrainEngine
+    train_ds = CompiledDataset(opts.train_compiled)
+    W, H = train_ds.size
+    if W != H:
+        raise ValueError(f"compiled train images must be square (got {W}x{H})")
+    if opts.resolution and opts.resolution != W:
+        raise ValueError(f"--resolution {opts.resolution} differs from the compiled image size {W}")
+    num_classes = train_ds.num_classes
+    resume = load_native_checkpoint(opts.resume) if opts.resume else None
+    if resume is not None:
+        _check_resume(resume.extra, opts)
+    model, info = resolve_model(opts.weights or opts.resume or None, preset=opts.preset or None, resolution=W,
+                                num_classes=num_classes, strict=False)
+    cfg = model.cfg
+    masks = bool(cfg.segmentation)
+    counts = train_ds.reader.instance_counts()
+    slots = int(counts.max()) + 1 if counts.numel() else 1
+    slots = max(1, min(slots, 256))
+    loader = BatchLoader(opts.train_compiled, opts.batch_size, shuffle=True, seed=opts.seed, shard_rank=ctx.rank,
+                         shard_count=ctx.world_size, drop_last=True, pixels="uint8", workers=max(1, opts.workers or 4),
+                         prefetch=max(2, opts.prefetch_factor), max_targets=1,
+                         device=ctx.device if ctx.device.type == "cuda" else None)
+    batches = len(loader)
+    steps_per_epoch = batches // opts.grad_accum_steps
+    if steps_per_epoch == 0:
+        raise ValueError("the compiled train split is too small for one effective batch per rank; reduce "
+                         "--batch-size, --grad-accum-steps or the world size")
+    total_steps = max(1, steps_per_epoch * opts.epochs)
+    grad_sync = None
+    if ctx.enabled:
+        if ctx.device.type == "cuda" and opts.ddp_backend == "fused":
+            from ..parallel.fused import FusedGradSync
+            grad_sync = FusedGradSync()
+        else:
+            from ..parallel.ddp import NcclGradSync
+            grad_sync = NcclGradSync()
+    engine = TrainEngine(model, opts, ctx.device, grad_sync, max_targets=slots, steps_per_epoch=steps_per_epoch,
+                         total_steps=total_steps)
+    if ctx.device.type == "cuda":
+        engine.bind_static_inputs(opts.batch_size, 3, H, W)
+    start_epoch, best_regular, best_ema = 0, -math.inf, -math.inf
+    if resume is not None:
+        engine.load_optimizer_state(resume.extra["optimizer"])
+        if "ema_state" in resume.extra:
+            engine.load_ema_state(state_from_archive(resume.extra["ema_state"]))
+        start_epoch = int(resume.extra.get("epoch", -1)) + 1
+        best_regular = float(resume.extra.get("best_regular_metric", -math.inf))
+        best_ema = float(resume.extra.get("best_ema_metric", -math.inf))
+    augmenter = GpuAugmenter(opts.augmentation, opts.batch_size, H, W, slots, device=ctx.device, masks=masks,
+                             seed=opts.seed, rank=ctx.rank)
+    meta = CheckpointMetadata.from_config(cfg, "native", info.get("weights_path", ""))
+    val_bs = opts.val_batch_size or opts.batch_size
+    best_path, best_is_ema = None, False
+    if ctx.main:
+        if math.isfinite(best_regular) and os.path.exists(paths["best_regular"]):
+            best_path = paths["best_regular"]
+        if math.isfinite(best_ema) and os.path.exists(paths["best_ema"]) and best_ema >= best_regular:
+            best_path, best_is_ema = paths["best_ema"], True
+        progress.submit({"phase": "starting", "epoch": start_epoch, "total_epochs": opts.epochs,
+                         "completed_batches": 0, "total_batches": batches, "optimizer_steps": 0,
+                         "steps_per_epoch": steps_per_epoch, "train_loss": 0.0, "step_loss": 0.0,
+                         "batches_per_second": 0.0, "images_per_second": 0.0, "elapsed_seconds": 0.0,
+                         "checkpoint_path": "", "val_loss": None, "val": {}}, force=True)
+    history = []
+    t_start = time.monotonic()
+    seq = 0
+    last_epoch = start_epoch - 1
+    for epoch in range(start_epoch, opts.epochs):
+        loader.set_epoch(epoch)
+        loss_sum, n_loss, t_epoch = 0.0, 0, time.monotonic()
+        for b, (images, _plain, idx) in enumerate(loader):
+            if b >= steps_per_epoch * opts.grad_accum_steps:
+                break
+            st = augmenter.prepare(idx, loader.dataset.reader, epoch, seq)
+            seq += 1
+            x, targets = augmenter.apply(images, st)
+            r = engine.step(x, targets)
+            if r.grad_norm is not None or not ctx.device.type == "cuda":
+                loss_sum += float(r.loss)
+                n_loss += 1
+            if progress is not None:
+                el = time.monotonic() - t_epoch
+                progress.submit({"phase": "train", "epoch": epoch, "completed_batches": b + 1,
+                                 "optimizer_steps": engine.step_count, "train_loss": loss_sum / max(1, n_loss),
+                                 "step_loss": float(r.loss), "batches_per_second": (b + 1) / max(el, 1e-9),
+                                 "images_per_second": (b + 1) * opts.batch_size * ctx.world_size / max(el, 1e-9),
+                                 "elapsed_seconds": time.monotonic() - t_start})
+        train_loss = loss_sum / max(1, n_loss)
+        # validation: regular weights, then EMA
+        if progress is not None:
+            progress.submit({"phase": "validate", "epoch": epoch}, force=True)
+        regular = engine.export_model("master")
+        val = evaluate(regular, opts.val_compiled, ctx, val_bs, opts.eval_max_dets, masks)
+        ema_val = None
+        ema_model = engine.export_model("ema") if opts.use_ema else None
+        if ema_model is not None:
+            ema_val = evaluate(ema_model, opts.val_compiled, ctx, val_bs, opts.eval_max_dets, masks)
+        if ctx.main:
+            state = regular.state_dict()
+            save_native_checkpoint(os.path.join(os.path.dirname(paths["ckpt"]), f"checkpoint_epoch_{epoch + 1}.pt"),
+                                   state, meta)
+            m = checkpoint_metric(val, masks)
+            if m > best_regular:
+                best_regular = m
+                save_native_checkpoint(paths["best_regular"], state, meta)
+                best_path, best_is_ema = paths["best_regular"], False
+            if ema_val is not None:
+                me = checkpoint_metric(ema_val, masks)
+                if me > best_ema:
+                    best_ema = me
+                    save_native_checkpoint(paths["best_ema"], ema_model.state_dict(), meta)
+                    best_path, best_is_ema = paths["best_ema"], True
+        extra = _resume_extra(opts, engine, epoch, best_regular, best_ema)   # collective when sharded
+        if ctx.main:
+            save_native_checkpoint(paths["ckpt"], regular.state_dict(), meta, extra)
+            rec = {"epoch": epoch, "train_lanes": 1, "eval_lanes": 1,
+                   "effective_batch_per_rank": opts.batch_size * opts.grad_accum_steps,
+                   "effective_batch_global": opts.batch_size * opts.grad_accum_steps * ctx.world_size,
+                   "train_loss": train_loss, "val_loss": None, "val": _summary_json(val),
+                   "ema_val_loss": None, "ema_val": _summary_json(ema_val)}
+            with open(paths["log"], "a") as f:
+                f.write(json.dumps(rec) + "\n")
+            history.append(rec)
+            progress.submit({"phase": "epoch_complete", "epoch": epoch, "val": _summary_json(val),
+                             "checkpoint_path": best_path or paths["ckpt"]}, force=True)
+        last_epoch = epoch
+        ctx.barrier()
+    engine.release_graph()
+    result = {"preset_name": cfg.preset_name, "output_dir": opts.output_dir, "checkpoint": paths["ckpt"],
+              "best_checkpoint": best_path or paths["ckpt"], "best_is_ema": best_is_ema,
+              "best_regular_metric": best_regular, "best_ema_metric": best_ema, "last_epoch": last_epoch,
+              "history_size": len(history), "train_lanes": 1, "eval_lanes": 1,
+              "effective_batch_per_rank": opts.batch_size * opts.grad_accum_steps,
+              "effective_batch_global": opts.batch_size * opts.grad_accum_steps * ctx.world_size,
+              "gpu_augmentation": _augmentation_json(opts.augmentation), "test": {}}
+    if opts.test_compiled:
+        best = resolve_model(result["best_checkpoint"], preset=cfg.preset_name, num_classes=num_classes,
+                             strict=False)[0]
+        result["test"] = _summary_json(evaluate(best, opts.test_compiled, ctx, val_bs, opts.eval_max_dets, masks))
+    if ctx.main:
+        with open(paths["results"], "w") as f:
+            json.dump(result, f, indent=1)
+        progress.submit({"phase": "complete"}, force=True)
+    if grad_sync is not None and hasattr(grad_sync, "close"):
+        ctx.barrier()
+        grad_sync.close()
+    return result
