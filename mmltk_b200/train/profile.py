@@ -1,0 +1,85 @@
+"""Kernel-time breakdown of one training step (``torch.profiler``, CUDA activity).
+
+    python -m mmltk_b200.train.profile --preset rf-detr-medium --batch-size 8 --steps 2
+
+Runs warm-up steps, then profiles ``--steps`` eager steps of the same engine the
+bench uses (eager, so every kernel is attributed; the bench replays the
+captured graph) and prints a markdown table of CUDA time per kernel, grouped
+by kernel name, plus the graph-replay step time measured with CUDA events.
+"""
+from __future__ import annotations
+
+import argparse
+import collections
+import sys
+
+import torch
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--preset", default="rf-detr-medium")
+    ap.add_argument("--batch-size", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--top", type=int, default=30)
+    a = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        print("profile: needs a GPU", file=sys.stderr)
+        return 2
+    from ..config import TrainOptions
+    from ..data.synthetic import synthetic_batch
+    from ..models.rfdetr import build_model
+    from .engine import TrainEngine
+    torch.manual_seed(0)
+    model = build_model(a.preset)
+    cfg = model.cfg
+    opts = TrainOptions(batch_size=a.batch_size, use_ema=True, cuda_graph=False)
+    dev = torch.device("cuda", 0)
+    images, targets = synthetic_batch(a.batch_size, cfg.resolution, seed=0, kmax=10, slots=10, dtype=torch.bfloat16)
+    images, targets = images.to(dev), targets.to(dev)
+    eng = TrainEngine(model, opts, dev, max_targets=targets.slots, steps_per_epoch=1000, total_steps=1000)
+    eng.bind_static_inputs(a.batch_size, 3, cfg.resolution, cfg.resolution)
+    for _ in range(a.warmup):
+        eng.step(images, targets)
+    torch.cuda.synchronize()
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(a.steps):
+            eng.step()
+        torch.cuda.synchronize()
+    per = collections.Counter()
+    count = collections.Counter()
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            per[ev.name] += ev.device_time
+            count[ev.name] += 1
+    total = sum(per.values())
+    print(f"# {a.preset} train step, batch {a.batch_size}, {cfg.resolution}x{cfg.resolution}, bf16\n")
+    print(f"CUDA time {total / 1e3 / a.steps:.2f} ms/step over {a.steps} eager steps "
+          f"({sum(count.values()) // a.steps} kernels/step)\n")
+    print("| share | ms/step | launches/step | kernel |\n|---|---|---|---|")
+    for name, t in per.most_common(a.top):
+        print(f"| {100 * t / total:.1f}% | {t / 1e3 / a.steps:.3f} | {count[name] // a.steps} | "
+              f"`{name[:110]}` |")
+    # graph replay for comparison
+    opts.cuda_graph = True
+    eng2 = eng
+    eng2.opts.cuda_graph = True
+    for _ in range(4):
+        eng2.step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        eng2.step(sync=False)
+    e1.record()
+    e1.synchronize()
+    print(f"\nCUDA-graph replay: {e0.elapsed_time(e1) / 10:.3f} ms/step "
+          f"({a.batch_size * 10000 / e0.elapsed_time(e1):.1f} img/s)")
+    eng2.release_graph()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
