@@ -85,6 +85,11 @@ class TrainEngine:
             pgs[gi]["params"].append(p)
         self.optimizer = torch.optim.AdamW(pgs, betas=(0.9, 0.999), eps=1e-8)
         self.base_lrs = [g["lr"] for g in self.groups]
+        self.muon = None
+        if self.opts.optimizer == "muon":
+            from .muon import MuonAux
+            self.muon = MuonAux([n for n, _ in named], [p.data for _, p in named], assign, self.groups,
+                                self.opts.momentum)
         self.ema = [p.detach().clone() for _, p in named] if self.opts.use_ema else None
         self.ema_named = [n for n, _ in named]
         self.params = [p for _, p in named]
@@ -109,6 +114,22 @@ class TrainEngine:
         self.scalars_host = torch.zeros(nsc, dtype=torch.float32).pin_memory()
         self.scalars = torch.zeros(nsc, dtype=torch.float32, device=self.device)
         self.flags = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.muon = None
+        if self.opts.optimizer == "muon":
+            # Muon runs eagerly on the master weights (fp32 views into the flat buffer)
+            from .muon import MuonAux
+            if self.grad_sync is not None and type(self.grad_sync).__name__ != "NcclGradSync":
+                raise ValueError("muon runs with the NCCL all-reduce gradient sync (--ddp-backend nccl)")
+            shapes = dict((n, p.shape) for n, p in named_dev)
+            self.muon = MuonAux(self.flat.names, [self.flat.view(master, i).view(shapes[n])
+                                                  for i, n in enumerate(self.flat.names)],
+                                self.flat.group_of, self.groups, self.opts.momentum)
+            self.m = self.v = None
+            self.ema_buf = master.clone() if self.opts.use_ema else None
+            self.readback = torch.zeros(4, dtype=torch.float32).pin_memory()
+            if self.grad_sync is not None:
+                self.grad_sync.muon_mode = True
+            return
         if self.grad_sync is not None:
             self.grad_sync.setup(self)
         else:
@@ -142,12 +163,39 @@ class TrainEngine:
         (total / self.accum if self.accum > 1 else total).backward()
         if not last:
             return total.detach(), {k: v.detach() for k, v in losses.items()}
-        if self.grad_sync is not None:
+        if self.muon is not None:
+            self._muon_update()
+        elif self.grad_sync is not None:
             self.grad_sync.step(self)
         else:
             kernels().adamw_ema_step(self.chunks, self.group_hyper, self.scalars, self.flat.grad_buf, self.master,
                                      self.m, self.v, self.ema_buf, self.flat.param_buf, self.scratch, self.flags)
         return total.detach(), {k: v.detach() for k, v in losses.items()}
+
+    def _muon_update(self) -> None:
+        """Eager Muon step on the flat buffers: all-reduce, clip, Muon/AdamW on the fp32
+        master, bf16 parameter refresh, EMA."""
+        from ..config import warmup_momentum
+        o = self.opts
+        g = self.flat.grad_buf
+        if self.grad_sync is not None:
+            torch.distributed.all_reduce(g, group=self.grad_sync.group)
+        gf = g.float()
+        if self.world > 1:
+            gf.div_(self.world)
+        norm = gf.norm()
+        self.flags[0:1].copy_((~torch.isfinite(norm)).to(torch.int32).reshape(1))
+        self.flags[1:2].copy_(norm.reshape(1).view(torch.int32))
+        if o.clip_max_norm > 0:
+            gf.mul_((o.clip_max_norm / (norm + 1e-6)).clamp(max=1.0))
+        grads = [self.flat.view(gf, i) for i in range(len(self.flat.names))]
+        s = lr_scale(o, self.step_count, self.steps_per_epoch, self.total_steps)
+        mom = warmup_momentum(o, self.step_count, self.steps_per_epoch, o.momentum)
+        self.muon.step(grads, s, mom)
+        self.flat.param_buf.copy_(self.master)
+        if self.ema_buf is not None:
+            d = o.ema_decay * (1 - math.exp(-(self.step_count + 1) / o.ema_tau)) if o.ema_tau > 0 else o.ema_decay
+            self.ema_buf.mul_(d).add_(self.master, alpha=1 - d)
 
     # ------------------------------------------------------------------ public
     def bind_static_inputs(self, batch: int, channels: int, height: int, width: int) -> None:
@@ -199,7 +247,8 @@ class TrainEngine:
         sc = self._host_scalars(self.step_count)
         self.scalars_host[:len(sc)] = torch.tensor(sc)
         self.scalars.copy_(self.scalars_host, non_blocking=True)
-        if self.opts.cuda_graph and self._graph_warmup >= 3 and self.in_targets.masks is None:
+        if (self.opts.cuda_graph and self._graph_warmup >= 3 and self.in_targets.masks is None
+                and self.muon is None):
             if self.graph is None:
                 self._capture()
             self.graph.replay()
@@ -270,7 +319,13 @@ class TrainEngine:
         norm = torch.nn.utils.clip_grad_norm_(self.params, o.clip_max_norm) if o.clip_max_norm > 0 else None
         if not torch.isfinite(total) or (norm is not None and not torch.isfinite(norm)):
             raise FloatingPointError(f"non-finite RF-DETR loss or gradients at step {self.step_count}")
-        self.optimizer.step()
+        if self.muon is not None:
+            from ..config import warmup_momentum
+            zeros = [torch.zeros_like(p) for p in self.params]
+            self.muon.step([p.grad if p.grad is not None else z for p, z in zip(self.params, zeros)], s,
+                           warmup_momentum(o, self.step_count, self.steps_per_epoch, o.momentum))
+        else:
+            self.optimizer.step()
         if self.ema is not None:
             d = o.ema_decay * (1 - math.exp(-(self.step_count + 1) / o.ema_tau)) if o.ema_tau > 0 else o.ema_decay
             with torch.no_grad():
@@ -321,7 +376,11 @@ class TrainEngine:
         return m
 
     def optimizer_state(self) -> dict:
-        """Per-parameter AdamW state in a world-size independent layout (archive-ready dict)."""
+        """Per-parameter optimizer state in a world-size independent layout (archive-ready dict)."""
+        if self.muon is not None:
+            d = self.muon.state_dict()
+            d["step"] = int(self.step_count)
+            return d
         d = {"kind": "adamw", "step": int(self.step_count)}
         if not self.cuda:
             names = [n for n, _ in zip(self.ema_named, self.params)]
@@ -342,6 +401,10 @@ class TrainEngine:
         return d
 
     def load_optimizer_state(self, d: dict) -> None:
+        if self.muon is not None:
+            self.muon.load_state_dict(d)
+            self.step_count = int(d["step"])
+            return
         if d.get("kind") != "adamw":
             raise ValueError(f"resume: optimizer kind {d.get('kind')!r} does not match 'adamw'")
         entries = {d[f"entry_{i:06d}"]["name"]: d[f"entry_{i:06d}"] for i in range(int(d["entry_count"]))}

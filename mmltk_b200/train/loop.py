@@ -87,7 +87,7 @@ def _augmentation_json(a) -> Dict:
 
 
 def _resume_extra(opts: TrainOptions, engine, epoch: int, best_regular: float, best_ema: float) -> Dict:
-    d = {"optimizer_kind": "adamw", "optimizer": engine.optimizer_state(), "epoch": int(epoch),
+    d = {"optimizer_kind": opts.optimizer, "optimizer": engine.optimizer_state(), "epoch": int(epoch),
          "lr_scheduler": opts.lr_scheduler, "lr_drop": int(opts.lr_drop), "warmup_epochs": float(opts.warmup_epochs),
          "warmup_momentum": float(opts.warmup_momentum), "lr_min_factor": float(opts.lr_min_factor),
          "gpu_augment_enabled": bool(opts.augmentation.enabled), "best_regular_metric": float(best_regular),
@@ -111,7 +111,7 @@ def _check_resume(extra: Dict, opts: TrainOptions) -> None:
                      ("lr_min_factor", opts.lr_min_factor)):
         if key in extra and extra[key] != cur:
             raise ValueError(f"resume checkpoint {key} ({extra[key]!r}) does not match the current options ({cur!r})")
-    if extra.get("optimizer_kind", "adamw") != "adamw":
+    if extra.get("optimizer_kind", "adamw") != opts.optimizer:
         raise ValueError("resume checkpoint optimizer_kind does not match the current options")
     if "optimizer" not in extra:
         raise ValueError("resume checkpoint is missing the optimizer state")
@@ -216,7 +216,7 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
     total_steps = max(1, steps_per_epoch * opts.epochs)
     grad_sync = None
     if ctx.enabled:
-        if ctx.device.type == "cuda" and opts.ddp_backend == "fused":
+        if ctx.device.type == "cuda" and opts.ddp_backend == "fused" and opts.optimizer == "adamw":
             from ..parallel.fused import FusedGradSync
             grad_sync = FusedGradSync()
         else:
