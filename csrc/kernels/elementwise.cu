@@ -1,10 +1,20 @@
-// Memory-bound helpers of the dense layers:
-//   colsum        out[n] = sum_m x[m, n]                       (bias gradients)
-//   scale_bwd     g_pre = gy * gamma ; g_gamma[n] = sum_m gy*pre (LayerScale backward)
-//   act_bwd       g_pre = gy * act'(pre)  for GELU(erf) / ReLU
-// Column reductions run in two levels with no atomics: a row-chunk per CTA
-// writes one fp32 partial row, then a reduce kernel with one warp per 32
-// columns sums the partials with 8 loads in flight per lane.
+// Memory-bound helpers of the dense layers, each ONE launch:
+//   colsum        out[n] (+)= sum_m x[m, n]                              (bias gradients)
+//   scale_bwd     g_pre = gy * gamma ; g_gamma[n] (+)= sum_m gy * pre     (LayerScale backward)
+//   act_bwd       g_pre = gy * act'(pre) ; optionally gb[n] (+)= sum_m g_pre   (GELU(erf) / ReLU + bias grad)
+//
+// Column reductions: the columns are cut into 256-wide slabs (grid.y) and the
+// rows into chunks (grid.x).  Each CTA (32 column lanes x 8 row lanes, 8
+// columns per thread) reduces its rows in shared memory and adds its partial
+// row into a per-device fp32 accumulator with vector atomics (the sum happens
+// in L2, spread over all slices); the last CTA of a slab to arrive (counter)
+// writes -- or, for gradient accumulation, adds into -- the output and clears
+// the accumulator and counter for the next launch.  No second reduction
+// launch, and a parameter's gradient accumulates in place in the flat
+// gradient buffer (no AccumulateGrad add).  Float atomics make the summation
+// order, and so the last bits of the result, run dependent.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace mmltk {
@@ -12,96 +22,102 @@ namespace mmltk {
 namespace {
 
 constexpr int kColThreads = 256;
-
-// Block = 256 threads = (256 / (N/8)) row lanes x (N/8) column lanes when N/8 <= 256,
-// otherwise the block covers a 2048-column slab.  Each thread owns 8 columns.
-template <typename T, int MODE>  // MODE 0: colsum(x) ; 1: colsum(gy*pre) + g_pre = gy*gamma
-__global__ void __launch_bounds__(kColThreads) colsum_partial_kernel(const T* __restrict__ x,
-                                                                     const T* __restrict__ pre,
-                                                                     const T* __restrict__ gamma,
-                                                                     T* __restrict__ gout, int64_t M, int N,
-                                                                     int rows_per_cta, float* __restrict__ part) {
-    const int vec_cols = N / 8;
-    const int col_lanes = vec_cols < kColThreads ? vec_cols : kColThreads;
-    const int row_lanes = kColThreads / col_lanes;
-    const int tid = threadIdx.x;
-    const int cl = tid % col_lanes, rl = tid / col_lanes;
-    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
-    const int64_t r1 = r0 + rows_per_cta < M ? r0 + rows_per_cta : M;
-    __shared__ float red[kColThreads * 8];
-    const int vc = cl + blockIdx.y * kColThreads;
-    // every thread reaches both barriers; idle threads just contribute nothing
-    const bool active = tid < col_lanes * row_lanes && vc < vec_cols;
-    {
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        float gm[8];
-        if (MODE == 1 && active) load8(gamma + 8 * vc, gm);
-        for (int64_t r = r0 + rl; active && r < r1; r += row_lanes) {
-            float a[8];
-            load8(x + r * N + 8 * vc, a);
-            if (MODE == 1) {
-                float p[8], o[8];
-                load8(pre + r * N + 8 * vc, p);
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    acc[c] += a[c] * p[c];
-                    o[c] = a[c] * gm[c];
-                }
-                store8(gout + r * N + 8 * vc, o);
-            } else {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) acc[c] += a[c];
-            }
-        }
-        // reduce over the row lanes through shared memory
-        if (tid < col_lanes * row_lanes) {
-#pragma unroll
-            for (int c = 0; c < 8; ++c) red[(rl * col_lanes + cl) * 8 + c] = acc[c];
-        }
-        __syncthreads();
-        if (active && rl == 0) {
-            for (int q = 1; q < row_lanes; ++q)
-#pragma unroll
-                for (int c = 0; c < 8; ++c) acc[c] += red[(q * col_lanes + cl) * 8 + c];
-            store8(part + static_cast<int64_t>(blockIdx.x) * N + 8 * vc, acc);
-        }
-    }
-}
-
-template <typename TO>
-__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ part, int nparts, int N,
-                                                              TO* __restrict__ out) {
-    // 8 warps x 32 lanes: lane -> column, warp -> strided subset of partial rows
-    __shared__ float red[8][33];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int col = blockIdx.x * 32 + lane;
-    float s = 0.f;
-    if (col < N) {
-        int p = w;
-        for (; p + 24 < nparts; p += 32) {
-            const float a = part[static_cast<int64_t>(p) * N + col];
-            const float b = part[static_cast<int64_t>(p + 8) * N + col];
-            const float c = part[static_cast<int64_t>(p + 16) * N + col];
-            const float d = part[static_cast<int64_t>(p + 24) * N + col];
-            s += (a + b) + (c + d);
-        }
-        for (; p < nparts; p += 8) s += part[static_cast<int64_t>(p) * N + col];
-    }
-    red[w][lane] = s;
-    __syncthreads();
-    if (w == 0 && col < N) {
-        float t = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) t += red[q][lane];
-        out[col] = from_f<TO>(t);
-    }
-}
+constexpr int kSlabCols = 256;     // columns per slab = 32 lanes x 8
 
 __device__ __forceinline__ float gelu_grad(float x) {
     // d/dx [x * Phi(x)] = Phi(x) + x * phi(x)
     const float cdf = 0.5f * (1.f + erff(x * 0.70710678118654752f));
     const float pdf = 0.39894228040143268f * __expf(-0.5f * x * x);
     return cdf + x * pdf;
+}
+
+__device__ __forceinline__ void ldcg8(const float* p, float* f) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(p + 4));
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+template <typename TO>
+__device__ __forceinline__ void write_out8(TO* out, const float* s, int n_valid, bool accumulate) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        if (c < n_valid) {
+            const float base = accumulate ? to_f(out[c]) : 0.f;
+            out[c] = from_f<TO>(base + s[c]);
+        }
+    }
+}
+
+// MODE 0: colsum(x) ; 1: gout = x * gamma, colsum(x * pre) ; 2: gout = x * act'(pre), colsum(gout)
+template <typename T, int MODE, typename TO>
+__global__ void __launch_bounds__(kColThreads) colreduce_kernel(const T* __restrict__ x, const T* __restrict__ pre,
+                                                                const T* __restrict__ gamma, T* __restrict__ gout,
+                                                                int64_t M, int N, int rows_per_cta, int act,
+                                                                float* acc_buf, unsigned* counters,
+                                                                TO* __restrict__ out, int accumulate) {
+    __shared__ float red[kColThreads * 8];
+    __shared__ unsigned s_last;
+    const int tid = threadIdx.x, cl = tid & 31, rl = tid >> 5;
+    const int col = blockIdx.y * kSlabCols + 8 * cl;   // first of this thread's 8 columns
+    const bool cols_ok = col < N;                       // N % 8 == 0, so all 8 or none
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
+    const int64_t r1 = r0 + rows_per_cta < M ? r0 + rows_per_cta : M;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float gm[8];
+    if (MODE == 1 && cols_ok) load8(gamma + col, gm);
+    for (int64_t r = r0 + rl; cols_ok && r < r1; r += 8) {
+        float a[8];
+        load8(x + r * N + col, a);
+        if (MODE == 0) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[c] += a[c];
+        } else {
+            float p[8], o[8];
+            load8(pre + r * N + col, p);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                if (MODE == 1) {
+                    acc[c] += a[c] * p[c];
+                    o[c] = a[c] * gm[c];
+                } else {
+                    o[c] = act == 1 ? a[c] * gelu_grad(p[c]) : (p[c] > 0.f ? a[c] : 0.f);
+                }
+            }
+            if (MODE == 2) {
+                // the bias gradient sums g_pre as stored (rounded to T), i.e. what the GEMMs consume
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc[c] += to_f(from_f<T>(o[c]));
+            }
+            store8(gout + r * N + col, o);
+        }
+    }
+    if (acc_buf == nullptr) return;   // act_bwd without a bias gradient
+#pragma unroll
+    for (int c = 0; c < 8; ++c) red[tid * 8 + c] = acc[c];
+    __syncthreads();
+    if (rl == 0 && cols_ok) {
+        for (int q = 1; q < 8; ++q)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[c] += red[(q * 32 + cl) * 8 + c];
+        atomicAdd(reinterpret_cast<float4*>(acc_buf + col), make_float4(acc[0], acc[1], acc[2], acc[3]));
+        atomicAdd(reinterpret_cast<float4*>(acc_buf + col + 4), make_float4(acc[4], acc[5], acc[6], acc[7]));
+    }
+    // arrival: the last CTA of this slab writes the result and clears the scratch
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&counters[blockIdx.y], 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (rl == 0 && cols_ok) {
+        float s[8];
+        ldcg8(acc_buf + col, s);
+        write_out8(out + col, s, 8, accumulate != 0);
+        *reinterpret_cast<float4*>(acc_buf + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(acc_buf + col + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (tid == 0) counters[blockIdx.y] = 0u;   // ready for the next launch (and graph replay)
 }
 
 template <typename T>
@@ -118,37 +134,99 @@ __global__ void __launch_bounds__(256) act_bwd_kernel(const T* __restrict__ gy, 
     }
 }
 
+template <typename TO>
+__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ part, int nparts, int N,
+                                                              TO* __restrict__ out) {
+    __shared__ float red[8][33];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int col = blockIdx.x * 32 + lane;
+    float s = 0.f;
+    if (col < N)
+        for (int p = w; p < nparts; p += 8) s += part[static_cast<int64_t>(p) * N + col];
+    red[w][lane] = s;
+    __syncthreads();
+    if (w == 0 && col < N) {
+        float t = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t += red[q][lane];
+        out[col] = from_f<TO>(t);
+    }
+}
+
+std::mutex g_scratch_mu;
+void* g_scratch[64] = {nullptr};
+
 }  // namespace
 
+// Per-device zero-initialised scratch of the single-launch reductions: kMaxCounters arrival
+// counters followed by kReduceAccFloats fp32 accumulators.  Every launch leaves it zeroed.
+ReduceScratch reduce_scratch() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return {nullptr, nullptr};
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (g_scratch[dev] == nullptr) {
+        const size_t bytes = kMaxCounters * sizeof(unsigned) + kReduceAccFloats * sizeof(float);
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) return {nullptr, nullptr};
+        if (cudaMemset(p, 0, bytes) != cudaSuccess) return {nullptr, nullptr};
+        g_scratch[dev] = p;
+    }
+    unsigned* c = static_cast<unsigned*>(g_scratch[dev]);
+    return {c, reinterpret_cast<float*>(c + kMaxCounters)};
+}
+
 int colsum_parts(int64_t M, int N) {
-    const int64_t slabs = (N / 8 + kColThreads - 1) / kColThreads;
+    const int64_t slabs = (N + kSlabCols - 1) / kSlabCols;
     int64_t want = static_cast<int64_t>(num_sms()) * 2 / slabs;
-    want = std::max<int64_t>(1, std::min<int64_t>(want, (M + 63) / 64));
+    want = std::max<int64_t>(1, std::min<int64_t>(want, (M + 31) / 32));
     return static_cast<int>(want);
 }
 
-cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const void* pre, const void* gamma,
-                          void* gout, int64_t M, int N, float* part, void* out, cudaStream_t st) {
+static cudaError_t launch_colreduce(DType t, DType out_t, int mode, const void* x, const void* pre,
+                                    const void* gamma, void* gout, int64_t M, int N, int act, float* part,
+                                    void* out, bool accumulate, cudaStream_t st) {
     if (N % 8 != 0) return cudaErrorInvalidValue;
+    const int slabs = (N + kSlabCols - 1) / kSlabCols;
+    if (slabs > kMaxCounters || (part != nullptr && N > kReduceAccFloats)) return cudaErrorInvalidValue;
+    const ReduceScratch rs = reduce_scratch();
+    if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
+    unsigned* counters = rs.counters;
+    float* acc_buf = part != nullptr ? rs.acc : nullptr;   // null: no column sum wanted
     const int parts = colsum_parts(M, N);
     const int rows_per_cta = static_cast<int>((M + parts - 1) / parts);
-    dim3 grid(parts, (N / 8 + kColThreads - 1) / kColThreads);
-    cudaError_t e = MMLTK_DISPATCH_DT(t, [&] {
+    const dim3 grid(parts, slabs);
+    return MMLTK_DISPATCH_DT(t, [&] {
         using T = scalar_t;
-        if (mode == 0)
-            colsum_partial_kernel<T, 0><<<grid, kColThreads, 0, st>>>(static_cast<const T*>(x), nullptr, nullptr,
-                                                                      nullptr, M, N, rows_per_cta, part);
-        else
-            colsum_partial_kernel<T, 1><<<grid, kColThreads, 0, st>>>(
-                static_cast<const T*>(x), static_cast<const T*>(pre), static_cast<const T*>(gamma),
-                static_cast<T*>(gout), M, N, rows_per_cta, part);
-        return cudaGetLastError();
+        return MMLTK_DISPATCH_DT(out_t, [&] {
+            using TO = scalar_t;
+            const T* xx = static_cast<const T*>(x);
+            const T* pp = static_cast<const T*>(pre);
+            const T* gg = static_cast<const T*>(gamma);
+            T* go = static_cast<T*>(gout);
+            TO* oo = static_cast<TO*>(out);
+            if (mode == 0)
+                colreduce_kernel<T, 0, TO><<<grid, kColThreads, 0, st>>>(xx, pp, gg, go, M, N, rows_per_cta, act,
+                                                                        acc_buf, counters, oo, accumulate);
+            else if (mode == 1)
+                colreduce_kernel<T, 1, TO><<<grid, kColThreads, 0, st>>>(xx, pp, gg, go, M, N, rows_per_cta, act,
+                                                                        acc_buf, counters, oo, accumulate);
+            else
+                colreduce_kernel<T, 2, TO><<<grid, kColThreads, 0, st>>>(xx, pp, gg, go, M, N, rows_per_cta, act,
+                                                                        acc_buf, counters, oo, accumulate);
+            return cudaGetLastError();
+        });
     });
-    if (e != cudaSuccess) return e;
-    return MMLTK_DISPATCH_DT(out_t, [&] {
-        reduce_partials_kernel<scalar_t><<<(N + 31) / 32, 256, 0, st>>>(part, parts, N, static_cast<scalar_t*>(out));
-        return cudaGetLastError();
-    });
+}
+
+cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const void* pre, const void* gamma,
+                          void* gout, int64_t M, int N, float* part, void* out, cudaStream_t st, bool accumulate) {
+    return launch_colreduce(t, out_t, mode, x, pre, gamma, gout, M, N, 0, part, out, accumulate, st);
+}
+
+cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,
+                                int act, float* part, void* gb, bool accumulate, cudaStream_t st) {
+    return launch_colreduce(t, out_t, 2, gy, pre, nullptr, gx, M, N, act, part, gb, accumulate, st);
 }
 
 cudaError_t launch_reduce_partials(DType out_t, const float* part, int nparts, int N, void* out, cudaStream_t st) {

@@ -16,11 +16,11 @@ int num_sms();
 // ---------------------------------------------------------------- LayerNorm
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st);
-// part: fp32 scratch [2, nparts, C]; nparts from layernorm_bwd_parts(rows)
+// One launch: gx, and gw / gb written (or added into, `accumulate`) by the last CTA.
 int layernorm_bwd_parts(int64_t rows);
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
-                                 const float* rstd, void* gx, void* gw, void* gb, float* part, int64_t rows, int C,
-                                 cudaStream_t st);
+                                 const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
+                                 bool accumulate, cudaStream_t st);
 
 // ---------------------------------------------------------------- MSDeformAttn
 struct MsdaDims {
@@ -50,11 +50,24 @@ cudaError_t launch_lsap(const float* cost, const int32_t* counts, int32_t* match
 // ---------------------------------------------------------------- elementwise
 cudaError_t launch_cast_f32(DType dst_t, const float* src, void* dst, int64_t n, cudaStream_t st);
 
-// mode 0: out = colsum(x); mode 1: gout = x * gamma (row-broadcast) and out = colsum(x * pre).
-// part: fp32 scratch [colsum_parts(M, N), N]; N % 8 == 0.
+// mode 0: out (+)= colsum(x); mode 1: gout = x * gamma (row-broadcast) and out (+)= colsum(x * pre).
+// part: fp32 scratch [colsum_parts(M, N), N]; N % 8 == 0.  One launch (the last CTA of each column
+// slab finishes the reduction); launches that share the per-device arrival counters must be
+// stream-ordered.  accumulate: add into `out` instead of overwriting it.
 int colsum_parts(int64_t M, int N);
+constexpr int kMaxCounters = 4096;
+constexpr int kReduceAccFloats = 16384;
+struct ReduceScratch {
+    unsigned* counters;
+    float* acc;
+};
+ReduceScratch reduce_scratch();
 cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const void* pre, const void* gamma,
-                          void* gout, int64_t M, int N, float* part, void* out, cudaStream_t st);
+                          void* gout, int64_t M, int N, float* part, void* out, cudaStream_t st,
+                          bool accumulate = false);
+// gx = gy * act'(pre) and, when part/gb are given, gb (+)= colsum(gx) in the same pass.
+cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,
+                                int act, float* part, void* gb, bool accumulate, cudaStream_t st);
 cudaError_t launch_reduce_partials(DType out_t, const float* part, int nparts, int N, void* out, cudaStream_t st);
 // act: 1 = GELU(erf), 2 = ReLU.  n % 8 == 0.
 cudaError_t launch_act_bwd(DType t, const void* gy, const void* pre, void* gx, int64_t n, int act, cudaStream_t st);
@@ -66,6 +79,21 @@ cudaError_t launch_dense_neg_fwd(DType t, const void* x, int64_t n, float coef, 
                                  unsigned int* counter, float* out, cudaStream_t st);
 cudaError_t launch_dense_neg_bwd(DType t, const void* x, const float* g, int64_t n, float coef, void* dx,
                                  cudaStream_t st);
+
+// ---------------------------------------------------------------- matched-pair losses
+constexpr int kMatchedMaxLayers = 16;
+struct MatchedLayers {
+    const void* logits[kMatchedMaxLayers];   // [B, Q, C] per layer
+    const void* boxes[kMatchedMaxLayers];    // [B, Q, 4] cxcywh
+    void* glogits[kMatchedMaxLayers];        // backward: dense-term gradients, matched terms added in place
+    void* gboxes[kMatchedMaxLayers];         // backward: box gradients, written (arrive zeroed)
+};
+// forward: out [NL, 3] (zeroed by the caller) += per-layer sums (correction, L1, 1 - GIoU);
+// backward: out_or_gout = upstream gradient [NL, 3].  match [NL, B, G, T] query or -1;
+// tgt [B, T, 4] fp32 cxcywh; labels [B, T]; mode 0 IA-BCE, 1 sigmoid focal.
+cudaError_t launch_matched_loss(bool backward, DType lt, DType bt, const MatchedLayers& L, int NL, int B, int Q,
+                                int C, int G, int T, const int32_t* match, const float* tgt, const int64_t* labels,
+                                int mode, float alpha, float* out_or_gout, cudaStream_t st);
 
 // ---------------------------------------------------------------- augmentation
 // in: [B,3,H,W] uint8 (k/255) or fp32 in [0,1]; out: normalised bf16 / fp32; rec: [B,64] host-drawn

@@ -71,7 +71,8 @@ template <typename T, typename W, int kMaxVec>
 __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, const T* __restrict__ x,
                                                      const W* __restrict__ w, const float* __restrict__ mean_in,
                                                      const float* __restrict__ rstd_in, T* __restrict__ gx,
-                                                     float* __restrict__ part_w, float* __restrict__ part_b,
+                                                     float* acc_w, float* acc_b, unsigned* counter,
+                                                     W* __restrict__ gw, W* __restrict__ gb, int accumulate,
                                                      int64_t rows, int C) {
     extern __shared__ float smem[];  // [warps][2][C]
     const int lane = threadIdx.x & 31;
@@ -135,15 +136,32 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
         }
     }
     __syncthreads();
+    // CTA partials go to the fp32 accumulators (atomics resolve in L2); the last CTA to
+    // arrive writes (or adds into) gw / gb and clears the scratch for the next launch
     for (int c = threadIdx.x; c < C; c += blockDim.x) {
         float a = 0.f, bb = 0.f;
         for (int q = 0; q < nwib; ++q) {
             a += smem[q * 2 * C + c];
             bb += smem[q * 2 * C + C + c];
         }
-        part_w[static_cast<int64_t>(blockIdx.x) * C + c] = a;
-        part_b[static_cast<int64_t>(blockIdx.x) * C + c] = bb;
+        atomicAdd(acc_w + c, a);
+        atomicAdd(acc_b + c, bb);
     }
+    __shared__ unsigned s_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float a = __ldcg(acc_w + c), bb = __ldcg(acc_b + c);
+        gw[c] = from_f<W>((accumulate ? to_f(gw[c]) : 0.f) + a);
+        gb[c] = from_f<W>((accumulate ? to_f(gb[c]) : 0.f) + bb);
+        acc_w[c] = 0.f;
+        acc_b[c] = 0.f;
+    }
+    if (threadIdx.x == 0) *counter = 0u;
 }
 
 template <typename W>
@@ -203,9 +221,11 @@ int layernorm_bwd_parts(int64_t rows) {
 }
 
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
-                                 const float* rstd, void* gx, void* gw, void* gb, float* part, int64_t rows, int C,
-                                 cudaStream_t st) {
-    if (C % 4 != 0 || C > 4 * 32 * 12) return cudaErrorInvalidValue;
+                                 const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
+                                 bool accumulate, cudaStream_t st) {
+    if (C % 4 != 0 || C > 4 * 32 * 12 || 2 * C > kReduceAccFloats) return cudaErrorInvalidValue;
+    const ReduceScratch rs = reduce_scratch();
+    if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
     const int threads = 256;
     const int nwib = threads / 32;
     const int blocks = layernorm_bwd_parts(rows);
@@ -221,15 +241,12 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
                     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
                 if (e != cudaSuccess) return;
                 kern<<<blocks, threads, smem, st>>>(static_cast<const T*>(gy), static_cast<const T*>(x),
-                                                    static_cast<const Wt*>(w), mean, rstd, static_cast<T*>(gx), part,
-                                                    part + static_cast<int64_t>(blocks) * C, rows, C);
+                                                    static_cast<const Wt*>(w), mean, rstd, static_cast<T*>(gx), rs.acc,
+                                                    rs.acc + C, rs.counters, static_cast<Wt*>(gw),
+                                                    static_cast<Wt*>(gb), accumulate ? 1 : 0, rows, C);
             });
             if (e != cudaSuccess) return e;
-            e = cudaGetLastError();
-            if (e != cudaSuccess) return e;
-            e = launch_reduce_partials(wt, part, blocks, C, gw, st);
-            if (e != cudaSuccess) return e;
-            return launch_reduce_partials(wt, part + static_cast<int64_t>(blocks) * C, blocks, C, gb, st);
+            return cudaGetLastError();
         });
     });
 }

@@ -41,24 +41,35 @@ torch::Tensor dense_focal_neg_bwd(torch::Tensor x, torch::Tensor g, double coef)
     return dx.view(x.sizes());
 }
 
-// sum over rows of a [M, N] tensor -> [N] in out_dtype
-torch::Tensor colsum(torch::Tensor x, c10::optional<at::ScalarType> out_dtype) {
+// Destination of a column reduction: `acc` (accumulated into, e.g. a parameter's .grad view) or a new tensor.
+torch::Tensor reduce_target(const c10::optional<torch::Tensor>& acc, int64_t N, const torch::TensorOptions& o) {
+    if (acc && acc->defined()) {
+        TORCH_CHECK(acc->is_cuda() && acc->is_contiguous() && acc->numel() == N, "reduction target: [N] contiguous");
+        return *acc;
+    }
+    return torch::empty({N}, o);
+}
+
+// sum over rows of a [M, N] tensor -> [N] in out_dtype, or added into `out`
+torch::Tensor colsum(torch::Tensor x, c10::optional<at::ScalarType> out_dtype, c10::optional<torch::Tensor> out) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 2, "colsum: CUDA [M,N] expected");
     at::cuda::CUDAGuard guard(x.device());
     auto xc = aligned16(x);
     const int64_t M = xc.size(0);
     const int N = static_cast<int>(xc.size(1));
     auto ot = out_dtype.has_value() ? *out_dtype : xc.scalar_type();
-    auto out = torch::empty({N}, xc.options().dtype(ot));
+    const bool acc = out && out->defined();
+    auto o = reduce_target(out, N, xc.options().dtype(ot));
     auto part = torch::empty({colsum_parts(M, N), N}, xc.options().dtype(torch::kFloat32));
-    check_cuda(launch_colsum(dtype_of(xc), dtype_of(out), 0, xc.data_ptr(), nullptr, nullptr, nullptr, M, N,
-                             part.data_ptr<float>(), out.data_ptr(), cur_stream()),
+    check_cuda(launch_colsum(dtype_of(xc), dtype_of(o), 0, xc.data_ptr(), nullptr, nullptr, nullptr, M, N,
+                             part.data_ptr<float>(), o.data_ptr(), cur_stream(), acc),
                "colsum");
-    return out;
+    return o;
 }
 
-// LayerScale backward: g_pre = gy * gamma, g_gamma = colsum(gy * pre)
-std::vector<torch::Tensor> scale_bwd(torch::Tensor gy, torch::Tensor pre, torch::Tensor gamma) {
+// LayerScale backward: g_pre = gy * gamma, g_gamma (+)= colsum(gy * pre)
+std::vector<torch::Tensor> scale_bwd(torch::Tensor gy, torch::Tensor pre, torch::Tensor gamma,
+                                     c10::optional<torch::Tensor> gamma_grad) {
     TORCH_CHECK(gy.sizes() == pre.sizes() && gy.dim() == 2, "scale_bwd: shape mismatch");
     TORCH_CHECK(gamma.scalar_type() == gy.scalar_type(), "scale_bwd: gamma dtype must match");
     at::cuda::CUDAGuard guard(gy.device());
@@ -66,12 +77,32 @@ std::vector<torch::Tensor> scale_bwd(torch::Tensor gy, torch::Tensor pre, torch:
     const int64_t M = g.size(0);
     const int N = static_cast<int>(g.size(1));
     auto gpre = torch::empty_like(g);
-    auto ggamma = torch::empty({N}, gamma.options());
+    const bool acc = gamma_grad && gamma_grad->defined();
+    auto ggamma = reduce_target(gamma_grad, N, gamma.options());
     auto part = torch::empty({colsum_parts(M, N), N}, g.options().dtype(torch::kFloat32));
-    check_cuda(launch_colsum(dtype_of(g), dtype_of(gamma), 1, g.data_ptr(), p.data_ptr(), gm.data_ptr(),
-                             gpre.data_ptr(), M, N, part.data_ptr<float>(), ggamma.data_ptr(), cur_stream()),
+    check_cuda(launch_colsum(dtype_of(g), dtype_of(ggamma), 1, g.data_ptr(), p.data_ptr(), gm.data_ptr(),
+                             gpre.data_ptr(), M, N, part.data_ptr<float>(), ggamma.data_ptr(), cur_stream(), acc),
                "scale_bwd");
     return {gpre, ggamma};
+}
+
+// g_pre = gy * act'(pre) and the bias gradient colsum(g_pre) in one pass (added into bias_grad if given)
+std::vector<torch::Tensor> act_bwd_bias(torch::Tensor gy, torch::Tensor pre, int64_t act,
+                                        c10::optional<torch::Tensor> bias_grad, c10::optional<at::ScalarType> dt) {
+    TORCH_CHECK(gy.sizes() == pre.sizes() && gy.scalar_type() == pre.scalar_type() && gy.dim() == 2,
+                "act_bwd_bias: mismatch");
+    at::cuda::CUDAGuard guard(gy.device());
+    auto g = aligned16(gy), p = aligned16(pre);
+    const int64_t M = g.size(0);
+    const int N = static_cast<int>(g.size(1));
+    auto gpre = torch::empty_like(g);
+    const bool acc = bias_grad && bias_grad->defined();
+    auto gb = reduce_target(bias_grad, N, g.options().dtype(dt.has_value() ? *dt : g.scalar_type()));
+    auto part = torch::empty({colsum_parts(M, N), N}, g.options().dtype(torch::kFloat32));
+    check_cuda(launch_act_bwd_bias(dtype_of(g), dtype_of(gb), g.data_ptr(), p.data_ptr(), gpre.data_ptr(), M, N,
+                                   static_cast<int>(act), part.data_ptr<float>(), gb.data_ptr(), acc, cur_stream()),
+               "act_bwd_bias");
+    return {gpre, gb};
 }
 
 torch::Tensor act_bwd(torch::Tensor gy, torch::Tensor pre, int64_t act) {
@@ -90,12 +121,16 @@ torch::Tensor act_bwd(torch::Tensor gy, torch::Tensor pre, int64_t act) {
 void register_more_ops(pybind11::module& m) {
     m.def("dense_focal_neg_fwd", &dense_focal_neg_fwd);
     m.def("dense_focal_neg_bwd", &dense_focal_neg_bwd);
-    m.def("colsum", &colsum, py::arg("x"), py::arg("out_dtype") = py::none());
-    m.def("scale_bwd", &scale_bwd);
+    m.def("colsum", &colsum, py::arg("x"), py::arg("out_dtype") = py::none(), py::arg("out") = py::none());
+    m.def("scale_bwd", &scale_bwd, py::arg("gy"), py::arg("pre"), py::arg("gamma"),
+          py::arg("gamma_grad") = py::none());
+    m.def("act_bwd_bias", &act_bwd_bias, py::arg("gy"), py::arg("pre"), py::arg("act"),
+          py::arg("bias_grad") = py::none(), py::arg("dtype") = py::none());
     m.def("act_bwd", &act_bwd);
     register_ddp_ops(m);
     register_gemm_ops(m);
     register_aug_ops(m);
+    register_loss_ops(m);
 }
 
 }  // namespace mmltk

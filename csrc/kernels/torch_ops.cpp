@@ -64,8 +64,10 @@ std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch
     return {y, mean, rstd};
 }
 
+// gw_acc / gb_acc: when given (a parameter's .grad view), the weight / bias gradients are added into them
 std::vector<torch::Tensor> layernorm_bwd(torch::Tensor gy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
-                                         torch::Tensor rstd) {
+                                         torch::Tensor rstd, c10::optional<torch::Tensor> gw_acc,
+                                         c10::optional<torch::Tensor> gb_acc) {
     TORCH_CHECK(gy.sizes() == x.sizes() && gy.is_contiguous() && x.is_contiguous() &&
                     gy.scalar_type() == x.scalar_type(),
                 "layernorm_bwd: grad/x mismatch");
@@ -74,13 +76,18 @@ std::vector<torch::Tensor> layernorm_bwd(torch::Tensor gy, torch::Tensor x, torc
     const int C = static_cast<int>(x.size(1));
     auto gx = torch::empty_like(x);
     auto wc = w.contiguous();
-    auto gw = torch::empty_like(wc);
-    auto gb = torch::empty_like(wc);
-    const int parts = layernorm_bwd_parts(rows);
-    auto part = torch::empty({2, parts, C}, x.options().dtype(torch::kFloat32));
+    const bool acc = gw_acc && gw_acc->defined() && gb_acc && gb_acc->defined();
+    if (acc) {
+        TORCH_CHECK(gw_acc->is_contiguous() && gb_acc->is_contiguous() && gw_acc->numel() == C &&
+                        gb_acc->numel() == C && gw_acc->scalar_type() == w.scalar_type() &&
+                        gb_acc->scalar_type() == w.scalar_type(),
+                    "layernorm_bwd: accumulation targets must be contiguous [C] of the weight dtype");
+    }
+    auto gw = acc ? *gw_acc : torch::empty_like(wc);
+    auto gb = acc ? *gb_acc : torch::empty_like(wc);
     check_cuda(launch_layernorm_bwd(dtype_of(x), dtype_of(w), gy.data_ptr(), x.data_ptr(), wc.data_ptr(),
                                     mean.data_ptr<float>(), rstd.data_ptr<float>(), gx.data_ptr(), gw.data_ptr(),
-                                    gb.data_ptr(), part.data_ptr<float>(), rows, C, cur_stream()),
+                                    gb.data_ptr(), rows, C, acc, cur_stream()),
                "layernorm_bwd");
     return {gx, gw, gb};
 }
@@ -251,7 +258,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "mmltk_b200 sm_100a CUDA kernels";
     m.def("num_sms", &mmltk::num_sms);
     m.def("layernorm_fwd", &mmltk::layernorm_fwd);
-    m.def("layernorm_bwd", &mmltk::layernorm_bwd);
+    m.def("layernorm_bwd", &mmltk::layernorm_bwd, py::arg("gy"), py::arg("x"), py::arg("w"), py::arg("mean"),
+          py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none());
     m.def("msda_fwd", &mmltk::msda_fwd);
     m.def("msda_bwd", &mmltk::msda_bwd);
     m.def("matcher_cost", &mmltk::matcher_cost);

@@ -16,5 +16,6 @@ void register_more_ops(pybind11::module& m);
 void register_ddp_ops(pybind11::module& m);
 void register_gemm_ops(pybind11::module& m);
 void register_aug_ops(pybind11::module& m);
+void register_loss_ops(pybind11::module& m);
 
 }  // namespace mmltk

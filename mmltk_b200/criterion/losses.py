@@ -14,6 +14,7 @@ materialising the [B, Q, C] weight tensors.
 """
 from __future__ import annotations
 
+import os
 from typing import Callable, Dict, List, Optional
 
 import torch
@@ -36,6 +37,43 @@ def _dense_neg(x: torch.Tensor, coef: float) -> torch.Tensor:
     return dense_focal_neg(x, coef)
 
 
+class _DetLossFn(torch.autograd.Function):
+    """Dense negative term + fused matched-pair terms of every layer: [NL, 4] =
+    (dense, correction, L1, 1 - GIoU) sums.  Backward writes the logits gradients
+    once (dense kernel, then the matched entries adjusted in place) and the box
+    gradients by scatter -- no per-layer index / zero-fill / add chains."""
+
+    @staticmethod
+    def forward(ctx, match, tgt_boxes, labels, mode, alpha, coef, *tensors):
+        from ..ops import kernels
+        k = kernels()
+        nl = len(tensors) // 2
+        logits = [t.contiguous() for t in tensors[:nl]]
+        boxes = [t.contiguous() for t in tensors[nl:]]
+        dense = torch.stack([k.dense_focal_neg_fwd(x, coef) for x in logits])
+        sums = k.matched_loss_fwd(logits, boxes, match, tgt_boxes, labels, mode, alpha)
+        ctx.save_for_backward(match, tgt_boxes, labels, *logits, *boxes)
+        ctx.cfg = (mode, alpha, coef, nl)
+        return torch.cat([dense[:, None], sums], 1)
+
+    @staticmethod
+    def backward(ctx, g):
+        from ..ops import kernels
+        k = kernels()
+        match, tgt, labels, *rest = ctx.saved_tensors
+        mode, alpha, coef, nl = ctx.cfg
+        logits, boxes = list(rest[:nl]), list(rest[nl:])
+        g = g.float().contiguous()
+        glog = [k.dense_focal_neg_bwd(x, g[i, 0], coef) for i, x in enumerate(logits)]
+        gbox = [torch.zeros_like(b) for b in boxes]
+        k.matched_loss_bwd(logits, boxes, match, tgt, labels, g[:, 1:].contiguous(), glog, gbox, mode, alpha)
+        return (None,) * 6 + tuple(glog) + tuple(gbox)
+
+
+# (dense, correction, L1, 1-GIoU) sums -> (loss_ce, loss_bbox, loss_giou) numerators
+_COMBINE = [[1.0, 0.0, 0.0], [1.0, 0.0, 0.0], [0.0, 1.0, 0.0], [0.0, 0.0, 1.0]]
+
+
 class SetCriterion:
     def __init__(self, cfg: RfDetrConfig, world_size: int = 1,
                  all_reduce: Optional[Callable[[torch.Tensor], torch.Tensor]] = None):
@@ -43,6 +81,9 @@ class SetCriterion:
         self.world_size = max(1, world_size)
         self.all_reduce = all_reduce
         self.weight_dict = cfg.loss_weight_dict()
+        # fused CUDA path for the detection terms (the per-layer torch statement is the oracle)
+        self.fused = os.environ.get("MMLTK_FUSED_LOSS", "1") != "0"
+        self._match_full = None
 
     # ---------------------------------------------------------------- helpers
     def num_boxes(self, targets: Targets, groups: int) -> torch.Tensor:
@@ -146,14 +187,19 @@ class SetCriterion:
         by_q: Dict[int, List[int]] = {}
         for i, l in enumerate(layers):
             by_q.setdefault(l["pred_logits"].shape[1], []).append(i)
+        self._match_full = None
         for q, idx in by_q.items():
             g = groups if q % groups == 0 else 1
             mm = hungarian_match([layers[i]["pred_logits"] for i in idx], [layers[i]["pred_boxes"] for i in idx],
                                  targets, g, cfg.set_cost_class, cfg.set_cost_bbox, cfg.set_cost_giou)
             for j, i in enumerate(idx):
                 match[i] = mm[j]
+            if len(by_q) == 1:
+                self._match_full = mm          # [NL, B, G, T], layers in order
         num_boxes = self.num_boxes(targets, groups)
         n_dec = 1 + len(outputs.get("aux_outputs", []))
+        if self._fused_ok(layers, by_q):
+            return self._fused(layers, match, targets, num_boxes, n_dec), match
         losses: Dict[str, torch.Tensor] = {}
         for li, layer in enumerate(layers):
             if li == 0:
@@ -175,10 +221,76 @@ class SetCriterion:
                 losses[k + suffix] = v
         return losses, match
 
+    # ---------------------------------------------------------------- fused path
+    def _fused_ok(self, layers, by_q) -> bool:
+        cfg = self.cfg
+        if not self.fused or cfg.use_varifocal_loss or cfg.use_position_supervised_loss or len(by_q) != 1:
+            return False
+        x = layers[0]["pred_logits"]
+        if not x.is_cuda or len(layers) > 16:
+            return False
+        from ..ops import kernels
+        if not hasattr(kernels(), "matched_loss_fwd"):
+            return False
+        return all(l["pred_logits"].shape == x.shape and l["pred_logits"].dtype == x.dtype and
+                   l["pred_boxes"].dtype == layers[0]["pred_boxes"].dtype for l in layers)
+
+    def _fused(self, layers, match, targets, num_boxes, n_dec) -> Dict[str, torch.Tensor]:
+        cfg = self.cfg
+        if cfg.ia_bce_loss:
+            mode, coef = 0, 1.0
+        else:
+            mode, coef = 1, 1.0 - cfg.focal_alpha
+        nl = len(layers) if cfg.aux_loss else 1
+        full = self._match_full
+        mt = full[:nl] if full is not None and full.shape[0] >= nl else torch.stack(match[:nl])
+        mt = mt.to(torch.int32).contiguous()
+        out = _DetLossFn.apply(mt, targets.boxes.float().contiguous(), targets.labels.contiguous(), mode,
+                               float(cfg.focal_alpha), coef, *[l["pred_logits"] for l in layers[:nl]],
+                               *[l["pred_boxes"] for l in layers[:nl]])
+        if getattr(self, "_comb_dev", None) is None or self._comb_dev.device != out.device:
+            self._comb_dev = torch.tensor(_COMBINE, device=out.device, dtype=out.dtype)   # once, before capture
+        per = (out @ self._comb_dev) / num_boxes                                 # [NL, 3]
+        losses: Dict[str, torch.Tensor] = {"_det_per_layer": per}
+        names = ("loss_ce", "loss_bbox", "loss_giou")
+        suffixes = []
+        for li in range(nl):
+            suffix = "" if li == 0 else (f"_{li - 1}" if li < n_dec else "_enc")
+            suffixes.append(suffix)
+            for j, n in enumerate(names):
+                losses[n + suffix] = per[li, j]
+        self._fused_suffixes = suffixes
+        with torch.no_grad():   # logging terms of the main layer (reference logs them per step)
+            main = layers[0]
+            m = self._gather(main, match[0], targets)
+            rows = main["pred_logits"][m["bidx"], m["q"]]
+            valid = m["valid"]
+            n = valid.sum().clamp(min=1)
+            losses["class_error"] = 100.0 - ((rows.argmax(-1) == m["labels"]) & valid).sum() * 100.0 / n
+            losses.update(self.loss_cardinality(main, targets))
+        if cfg.segmentation and targets.masks is not None:
+            for li in range(nl):
+                m = self._gather(layers[li], match[li], targets)
+                for k, v in mask_losses(layers[li], m, targets, cfg, num_boxes).items():
+                    losses[k + suffixes[li]] = v
+        return losses
+
     def weighted(self, losses: Dict[str, torch.Tensor]) -> torch.Tensor:
         total = None
+        covered = set()
+        per = losses.get("_det_per_layer")
+        if per is not None:
+            # detection terms of every layer in one multiply-reduce
+            key = (per.shape[0], per.device)
+            if getattr(self, "_wmat_key", None) != key:
+                w = [[self.weight_dict.get(n + s, 0.0) for n in ("loss_ce", "loss_bbox", "loss_giou")]
+                     for s in self._fused_suffixes]
+                self._wmat = torch.tensor(w, device=per.device, dtype=per.dtype)
+                self._wmat_key = key
+            total = (per * self._wmat).sum()
+            covered = {n + s for s in self._fused_suffixes for n in ("loss_ce", "loss_bbox", "loss_giou")}
         for k, w in self.weight_dict.items():
-            if k in losses:
+            if k in losses and k not in covered:
                 total = losses[k] * w if total is None else total + losses[k] * w
         if total is None:
             raise RuntimeError("criterion returned no weighted losses")

@@ -135,9 +135,7 @@ class SelfAttention(nn.Module):
         N, L, C = x.shape
         H = self.heads
         qkv = ops.linear(x, self.qkv_weight, self.qkv_bias)  # [N, L, 3C]
-        q, k, v = qkv.view(N, L, 3, H, C // H).permute(2, 0, 3, 1, 4).unbind(0)  # [N, H, L, D] each
-        o = ops.attention(q, k, v)  # [N, H, L, D]
-        return o.transpose(1, 2).reshape(N, L, C)
+        return ops.qkv_attention(qkv, H)                      # [N, L, C]
 
 
 class SelfOutput(nn.Module):

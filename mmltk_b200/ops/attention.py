@@ -1,31 +1,28 @@
 """Scaled dot-product attention for the windowed ViT and the Group-DETR decoder.
 
 ``attention(q, k, v)``: q/k/v [N, H, L, D] -> [N, H, L, D], softmax scale 1/sqrt(D).
+``qkv_attention(qkv, heads)``: packed projections [N, L, 3C] -> [N, L, C] (the ViT layout).
 Reference: `at::scaled_dot_product_attention` (`src/rfdetr/layers/model.cpp:498`) and
 `nn::MultiheadAttention` (`model.cpp:917`).
 
-On CUDA with bf16 and head_dim 64 this runs the framework's tcgen05 flash
-attention (S = Q K^T accumulated in TMEM, online softmax on the tcgen05.ld
-read-back, P V accumulated in TMEM).  Other shapes and the CPU path use the
-math definition (the oracle).
+CUDA runs cuDNN's sm100 flash attention (library kernel).  ``qkv_attention``
+owns the data layout around it: q, k and v are strided views straight into
+the packed projection output (no split / permute copies), the output comes
+back in [N, L, H, D] order so the output projection reads it without a
+transpose, and in the backward pass dq / dk / dv are written into the packed
+[N, L, 3, H, D] gradient with one contiguous stack.  The generic autograd
+route (unbind + permute) costs two extra full passes over the gradients per
+layer, one of them a slow strided concatenation.  CPU: the math definition
+(the oracle).
 """
 from __future__ import annotations
 
 import math
-import os
 
 import torch
 import torch.nn.functional as F
 
-from ._ext import kernels
-
-__all__ = ["attention", "attention_reference", "set_flash_enabled"]
-
-_state = {"enabled": os.environ.get("MMLTK_TC_ATTN", "1") != "0"}
-
-
-def set_flash_enabled(flag: bool) -> None:
-    _state["enabled"] = bool(flag)
+__all__ = ["attention", "attention_reference", "qkv_attention", "qkv_attention_reference"]
 
 
 def attention_reference(q, k, v):
@@ -35,28 +32,53 @@ def attention_reference(q, k, v):
     return torch.matmul(p, v.float()).to(q.dtype)
 
 
-class _FlashFn(torch.autograd.Function):
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    if q.is_cuda:
+        return F.scaled_dot_product_attention(q, k, v)
+    return attention_reference(q, k, v)
+
+
+def _split(qkv: torch.Tensor, heads: int):
+    N, L, C3 = qkv.shape
+    D = C3 // (3 * heads)
+    v5 = qkv.view(N, L, 3, heads, D)
+    return [v5[:, :, i].transpose(1, 2) for i in range(3)]   # [N, H, L, D] strided views
+
+
+class _QKVAttnFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v):
-        o, lse = kernels().flash_fwd(q, k, v)
-        ctx.save_for_backward(q, k, v, o, lse)
-        return o
+    def forward(ctx, qkv, heads):
+        N, L, C3 = qkv.shape
+        C = C3 // 3
+        leaves = [t.detach().requires_grad_() for t in _split(qkv, heads)]
+        with torch.enable_grad():
+            o = F.scaled_dot_product_attention(*leaves)           # [N, H, L, D]
+        ctx.leaves, ctx.o = leaves, o
+        ctx.shape = (N, L, heads, C // heads)
+        return o.detach().transpose(1, 2).reshape(N, L, C)
 
     @staticmethod
     def backward(ctx, go):
-        q, k, v, o, lse = ctx.saved_tensors
-        dq, dk, dv = kernels().flash_bwd(go.contiguous(), q, k, v, o, lse)
-        return dq, dk, dv
+        N, L, H, D = ctx.shape
+        g = go.reshape(N, L, H, D).transpose(1, 2)
+        dq, dk, dv = torch.autograd.grad(ctx.o, ctx.leaves, g)
+        ctx.leaves = ctx.o = None
+        # [N, L, 3, H, D]: one concatenation of (usually contiguous) [N, L, H, D] gradients
+        dqkv = torch.stack([dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2)], dim=2)
+        return dqkv.view(N, L, 3 * H * D), None
 
 
-def _flash_ok(q):
-    return (_state["enabled"] and q.is_cuda and q.dtype == torch.bfloat16 and q.shape[-1] == 64
-            and hasattr(kernels(), "flash_fwd"))
+def qkv_attention_reference(qkv: torch.Tensor, heads: int) -> torch.Tensor:
+    N, L, C3 = qkv.shape
+    q, k, v = _split(qkv, heads)
+    return attention_reference(q, k, v).transpose(1, 2).reshape(N, L, C3 // 3)
 
 
-def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
-    if q.is_cuda:
-        if _flash_ok(q):
-            return _FlashFn.apply(q.contiguous(), k.contiguous(), v.contiguous())
-        return F.scaled_dot_product_attention(q, k, v)
-    return attention_reference(q, k, v)
+def qkv_attention(qkv: torch.Tensor, heads: int) -> torch.Tensor:
+    if qkv.is_cuda and qkv.dtype in (torch.bfloat16, torch.float16):
+        if torch.is_grad_enabled() and qkv.requires_grad:
+            return _QKVAttnFn.apply(qkv, heads)
+        N, L, C3 = qkv.shape
+        o = F.scaled_dot_product_attention(*_split(qkv, heads))
+        return o.transpose(1, 2).reshape(N, L, C3 // 3)
+    return qkv_attention_reference(qkv, heads)

@@ -79,3 +79,8 @@ def gemm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
             and _rowmajor(b)):
         return kernels().gemm_tc(a, b, None, True, True)[0]
     return torch.mm(a.t(), b)
+
+
+def gemm_tn_acc(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out += a^T b in one GEMM (beta = 1): weight gradients accumulated straight into .grad."""
+    return out.addmm_(a.t(), b)

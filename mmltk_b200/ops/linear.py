@@ -22,7 +22,8 @@ import torch
 import torch.nn.functional as F
 
 from ._ext import kernels
-from .gemm import gemm_nn, gemm_nt, gemm_nt_epilogue, gemm_tn
+from .gemm import gemm_nn, gemm_nt, gemm_nt_epilogue, gemm_tn, gemm_tn_acc
+from .gradacc import grad_target
 
 __all__ = ["linear", "linear_scale_residual", "set_fused_linear"]
 
@@ -65,6 +66,7 @@ class _Linear(torch.autograd.Function):
             y = _act(pre, act_id) if act_id else pre
         ctx.save_for_backward(x2, w, pre if act_id else None)
         ctx.act_id, ctx.has_bias, ctx.shp = act_id, b is not None, shp
+        ctx.params = (w, b)                       # the Parameter objects (their .grad may be flat views)
         return y.view(*shp[:-1], w.shape[0])
 
     @staticmethod
@@ -72,12 +74,22 @@ class _Linear(torch.autograd.Function):
         x2, w, pre = ctx.saved_tensors
         k = kernels()
         g = _2d(gy, w.shape[0])
+        wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
+        want_b = ctx.has_bias and ctx.needs_input_grad[2]
+        gb = None
         if ctx.act_id:
-            g = k.act_bwd(g, pre, ctx.act_id)
+            if want_b:   # activation backward and bias gradient in one pass
+                g, gb = k.act_bwd_bias(g, pre, ctx.act_id, bt)
+            else:
+                g = k.act_bwd(g, pre, ctx.act_id)
+        elif want_b:
+            gb = k.colsum(g, None, bt)
         gx = gemm_nn(g, w) if ctx.needs_input_grad[0] else None
-        gw = gemm_tn(g, x2) if ctx.needs_input_grad[1] else None
-        gb = k.colsum(g) if ctx.has_bias and ctx.needs_input_grad[2] else None
-        return (None if gx is None else gx.view(ctx.shp)), gw, gb, None
+        gw = None
+        if ctx.needs_input_grad[1]:
+            gw = gemm_tn(g, x2) if wt is None else gemm_tn_acc(g, x2, wt)
+        return ((None if gx is None else gx.view(ctx.shp)), None if wt is not None else gw,
+                None if bt is not None else gb, None)
 
 
 class _LinearScaleResidual(torch.autograd.Function):
@@ -94,6 +106,7 @@ class _LinearScaleResidual(torch.autograd.Function):
             y = torch.addcmul(r2, pre, gamma.to(pre.dtype))
         ctx.save_for_backward(x2, w, gamma, pre)
         ctx.shp = shp
+        ctx.params = (w, b, gamma)
         return y.view(*shp[:-1], w.shape[0])
 
     @staticmethod
@@ -101,16 +114,27 @@ class _LinearScaleResidual(torch.autograd.Function):
         x2, w, gamma, pre = ctx.saved_tensors
         k = kernels()
         g = _2d(gy, w.shape[0])
-        g_pre, g_gamma = k.scale_bwd(g, pre, gamma)
+        wt, bt, gt = (grad_target(p) for p in ctx.params)
+        g_pre, g_gamma = k.scale_bwd(g, pre, gamma, gt)
         gx = gemm_nn(g_pre, w)
-        gw = gemm_tn(g_pre, x2)
-        gb = k.colsum(g_pre)
-        return gx.view(ctx.shp), gw, gb, g_gamma, gy
+        gw = gemm_tn(g_pre, x2) if wt is None else gemm_tn_acc(g_pre, x2, wt)
+        gb = k.colsum(g_pre, None, bt)
+        return (gx.view(ctx.shp), None if wt is not None else gw, None if bt is not None else gb,
+                None if gt is not None else g_gamma, gy)
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, b=None, act=None) -> torch.Tensor:
     if _ok(x, w):
         return _Linear.apply(x, w, b, _ACTS[act])
+    n = w.shape[0]
+    if n % 8 and n > 8 and _ok(x, w.new_empty(8, w.shape[1])):
+        # Output widths that are not a multiple of 8 (the 91-class heads) make cuBLAS fall back to
+        # its 1-byte-aligned kernels, ~10x slower for the [B*Q, 91] logits and their weight gradient.
+        # Padding the weight rows to a multiple of 8 keeps every product on the aligned path.
+        pad = (-n) % 8
+        wp = F.pad(w, (0, 0, 0, pad))
+        bp = None if b is None else F.pad(b, (0, pad))
+        return _Linear.apply(x, wp, bp, _ACTS[act])[..., :n].contiguous()
     return _act(F.linear(x, w.to(x.dtype), None if b is None else b.to(x.dtype)), _ACTS[act])
 
 

@@ -12,6 +12,7 @@ import torch
 import torch.nn.functional as F
 
 from ._ext import kernels
+from .gradacc import grad_target
 
 __all__ = ["layer_norm"]
 
@@ -24,12 +25,17 @@ class _LayerNormFn(torch.autograd.Function):
         y, mean, rstd = kernels().layernorm_fwd(x2, weight, bias, float(eps))
         ctx.save_for_backward(x2, weight, mean, rstd)
         ctx.shape = shape
+        ctx.params = (weight, bias)
         return y.view(shape)
 
     @staticmethod
     def backward(ctx, gy):
         x2, weight, mean, rstd = ctx.saved_tensors
         gy2 = gy.contiguous().view(x2.shape)
+        wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
+        if wt is not None and bt is not None:   # weight / bias gradients added straight into .grad
+            dx, _, _ = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd, wt, bt)
+            return dx.view(ctx.shape), None, None, None
         dx, dw, db = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd)
         return dx.view(ctx.shape), dw, db, None
 
