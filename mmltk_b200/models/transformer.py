@@ -229,11 +229,20 @@ class GroupedLinear(nn.Module):
         """x: [G', B, N, din] (one slice per group) or [B, N, din] (shared) -> [groups, B, N, dout]."""
         w = self.weight[:groups].to(x.dtype)
         b = self.bias[:groups].to(x.dtype)
+        dout = w.shape[1]
+        pad = (-dout) % 8 if (x.is_cuda and dout > 8) else 0
+        if pad:   # odd widths (91 classes) would put cuBLAS on its unaligned kernels
+            w = F.pad(w, (0, 0, 0, pad))
+            b = F.pad(b, (0, pad))
+        G = w.shape[0]
         if x.dim() == 3:
-            y = torch.einsum("bnc,goc->gbno", x, w)
-        else:
-            y = torch.einsum("gbnc,goc->gbno", x, w)
-        y = y + b[:, None, None, :]
+            B, N, C = x.shape
+            x = x.unsqueeze(0).expand(G, B, N, C)
+        Gx, B, N, C = x.shape
+        # batched GEMM with the bias folded in (beta = 1 on a broadcast bias)
+        y = torch.baddbmm(b[:, None, :], x.reshape(G, B * N, C), w.transpose(1, 2)).view(G, B, N, -1)
+        if pad:
+            y = y[..., :dout]
         if act == "relu":
             y = F.relu(y)
         return y
@@ -362,18 +371,27 @@ class Transformer(nn.Module):
         if cfg.two_stage:
             props, valid = encoder_proposals(shapes, B, memory.device, memory.dtype, not cfg.bbox_reparam)
             out_mem = memory.masked_fill(~valid, 0.0)
-            h = self.enc_output(out_mem, groups)                               # [G, B, S, C]
-            h = self.enc_output_norm(h, groups)
-            cls = self.enc_out_class_embed(h, groups)                          # [G, B, S, K]
-            delta = self.enc_out_bbox_embed(h, groups)                         # [G, B, S, 4]
+            # Selection pass over every token, without autograd: only the top-k indices leave it.
+            with torch.no_grad():
+                h_all = self.enc_output_norm(self.enc_output(out_mem, groups), groups)   # [G, B, S, C]
+                cls = self.enc_out_class_embed(h_all, groups)                          # [G, B, S, K]
+                k = min(cfg.num_queries, cls.shape[2])
+                topk = cls.max(-1)[0].topk(k, dim=2)[1]                                # [G, B, k]
+                del h_all, cls
+            # Differentiable pass on the selected tokens only: the head is per token, so recomputing
+            # enc_output + norm + box MLP on the k chosen rows gives the same values (and gradients)
+            # as gathering them from the full pass, at k / S of the cost.
+            S, C = out_mem.shape[1], out_mem.shape[2]
+            mem_in = out_mem.unsqueeze(0).expand(groups, B, S, C).gather(
+                2, topk[..., None].expand(-1, -1, -1, C))                              # [G, B, k, C]
+            mem_sel = self.enc_output_norm(self.enc_output(mem_in, groups), groups)    # [G, B, k, C]
+            delta = self.enc_out_bbox_embed(mem_sel, groups)                            # [G, B, k, 4]
+            props_sel = props.expand(B, -1, -1).unsqueeze(0).expand(groups, -1, -1, -1).gather(
+                2, topk[..., None].expand(-1, -1, -1, 4))                               # [G, B, k, 4]
             if cfg.bbox_reparam:
-                coord = reparam_boxes(delta, props[None])
+                boxes = reparam_boxes(delta, props_sel)
             else:
-                coord = delta + props[None]
-            k = min(cfg.num_queries, cls.shape[2])
-            topk = cls.max(-1)[0].topk(k, dim=2)[1]                            # [G, B, k]
-            boxes = coord.gather(2, topk[..., None].expand(-1, -1, -1, 4))      # [G, B, k, 4]
-            mem_sel = h.gather(2, topk[..., None].expand(-1, -1, -1, h.shape[-1]))
+                boxes = delta + props_sel
             # group-major query order [B, G*k, .]
             enc_boxes = boxes.permute(1, 0, 2, 3).reshape(B, groups * k, 4)
             enc_mem = mem_sel.permute(1, 0, 2, 3).reshape(B, groups * k, -1)
