@@ -153,6 +153,16 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
     }
 }
 
+// out (+)= acc, then acc = 0 (finishes a column sum accumulated by another kernel's atomics)
+template <typename TO>
+__global__ void colacc_finalize_kernel(float* acc, TO* out, int N, int accumulate) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= N) return;
+    const float s = acc[c];
+    out[c] = from_f<TO>((accumulate ? to_f(out[c]) : 0.f) + s);
+    acc[c] = 0.f;
+}
+
 std::mutex g_scratch_mu;
 void* g_scratch[64] = {nullptr};
 
@@ -227,6 +237,14 @@ cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const v
 cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,
                                 int act, float* part, void* gb, bool accumulate, cudaStream_t st) {
     return launch_colreduce(t, out_t, 2, gy, pre, nullptr, gx, M, N, act, part, gb, accumulate, st);
+}
+
+cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bool accumulate, cudaStream_t st) {
+    return MMLTK_DISPATCH_DT(out_t, [&] {
+        colacc_finalize_kernel<scalar_t><<<(N + 255) / 256, 256, 0, st>>>(acc, static_cast<scalar_t*>(out), N,
+                                                                          accumulate ? 1 : 0);
+        return cudaGetLastError();
+    });
 }
 
 cudaError_t launch_reduce_partials(DType out_t, const float* part, int nparts, int N, void* out, cudaStream_t st) {

@@ -27,9 +27,12 @@ bool aligned16(const torch::Tensor& t) { return reinterpret_cast<uintptr_t>(t.da
 // C = opA(a) opB(b) (+ bias) with an optional fused epilogue.
 //   a_mn=false: a is [M, K]; a_mn=true: a is [K, M].   b_mn=false: b is [N, K]; b_mn=true: b is [K, N].
 //   epi: 0 none, 1 GELU, 2 ReLU, 3 res + gamma * (acc + bias).  want_aux: also return acc + bias.
+//   epi 4 / 5 (activation backward: C = acc * GELU'(res) / acc * [res > 0]): res = pre-activation [M, N].
+//   colsum: optional [N] output that receives (or, colsum_acc, accumulates) the column sums of C.
 std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> bias, bool a_mn,
                                    bool b_mn, int64_t epi, bool want_aux, c10::optional<torch::Tensor> res,
-                                   c10::optional<torch::Tensor> gamma) {
+                                   c10::optional<torch::Tensor> gamma, c10::optional<torch::Tensor> colsum,
+                                   bool colsum_acc) {
     TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.dim() == 2 && b.dim() == 2, "gemm_tc: 2-D CUDA tensors expected");
     TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16, "gemm_tc: bf16 only");
     TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm_tc: operands must be row-major");
@@ -73,6 +76,25 @@ std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::option
         g.res = reinterpret_cast<const __nv_bfloat16*>(res_c.data_ptr());
         g.gamma = reinterpret_cast<const __nv_bfloat16*>(gamma_c.data_ptr());
     }
+    if (epi == 4 || epi == 5) {
+        TORCH_CHECK(res.has_value() && res->defined(), "gemm_tc: epilogues 4/5 need the pre-activation (res)");
+        res_c = res->contiguous();
+        TORCH_CHECK(res_c.numel() == M * N && res_c.scalar_type() == torch::kBFloat16 && aligned16(res_c),
+                    "gemm_tc: pre-activation must be bf16 [M, N]");
+        g.res = reinterpret_cast<const __nv_bfloat16*>(res_c.data_ptr());
+    }
+    TORCH_CHECK(epi >= 0 && epi <= 5, "gemm_tc: unknown epilogue");
+    torch::Tensor colsum_t;
+    if (colsum.has_value() && colsum->defined()) {
+        colsum_t = *colsum;
+        TORCH_CHECK(colsum_t.is_cuda() && colsum_t.is_contiguous() && colsum_t.numel() == N &&
+                        (colsum_t.scalar_type() == torch::kBFloat16 || colsum_t.scalar_type() == torch::kFloat32),
+                    "gemm_tc: colsum must be a contiguous bf16/fp32 [N] tensor");
+        TORCH_CHECK(N <= kReduceAccFloats, "gemm_tc: colsum supports N <= ", kReduceAccFloats);
+        const ReduceScratch rs = reduce_scratch();
+        TORCH_CHECK(rs.acc != nullptr, "gemm_tc: reduction scratch unavailable");
+        g.colacc = rs.acc;   // zero on entry; the finalize below writes the result and clears it
+    }
     g.status = status_word(a.device()).data_ptr<int>();
     g.M = static_cast<int>(M);
     g.N = static_cast<int>(N);
@@ -80,7 +102,7 @@ std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::option
     g.ldc = N;
     g.epi = static_cast<int>(epi);
     torch::Tensor ws;
-    if (epi == 0 && !want_aux && g.bias == nullptr) {
+    if (epi == 0 && !want_aux && g.bias == nullptr && g.colacc == nullptr) {
         const int splits = gemm_tc_splits(g.M, g.N, g.K);
         if (splits > 1) {  // few output tiles, long reduction: split K, sum partials in fp32
             ws = torch::empty({M, N}, a.options().dtype(torch::kFloat32));
@@ -89,6 +111,10 @@ std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::option
         }
     }
     check_cuda(launch_gemm_tc(g, a_mn, b_mn, a.stride(0), b.stride(0), cur_stream()), "gemm_tc");
+    if (g.colacc != nullptr)
+        check_cuda(launch_colacc_finalize(g.colacc, dtype_of(colsum_t), colsum_t.data_ptr(), static_cast<int>(N),
+                                          colsum_acc, cur_stream()),
+                   "gemm_tc colsum");
     if (want_aux) return {C, aux};
     return {C};
 }
@@ -103,7 +129,7 @@ int64_t gemm_tc_status(int64_t device) {
 void register_gemm_ops(pybind11::module& m) {
     m.def("gemm_tc", &gemm_tc, py::arg("a"), py::arg("b"), py::arg("bias") = py::none(), py::arg("a_mn") = false,
           py::arg("b_mn") = false, py::arg("epi") = 0, py::arg("want_aux") = false, py::arg("res") = py::none(),
-          py::arg("gamma") = py::none());
+          py::arg("gamma") = py::none(), py::arg("colsum") = py::none(), py::arg("colsum_acc") = false);
     m.def("gemm_tc_status", &gemm_tc_status);
     m.def("gemm_tc_smem_bytes", &gemm_tc_smem_bytes);
 }

@@ -154,6 +154,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ float gelu_f(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
+// d/dx [x * Phi(x)] = Phi(x) + x * phi(x)
+__device__ __forceinline__ float gelu_grad_f(float x) {
+    return 0.5f * (1.f + erff(x * 0.70710678118654752f)) + x * 0.39894228040143268f * __expf(-0.5f * x * x);
+}
 
 // 32 consecutive accumulator columns of this thread's row: two loads, one wait.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
@@ -261,8 +265,31 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg,
                 for (int i = 0; i < 8; ++i) v[8 * j + i] = r[8 * j + i] + gm[i] * v[8 * j + i];
             }
         }
+    } else if (g.epi == 4 || g.epi == 5) {
+        // activation backward: the product is the gradient w.r.t. the activation output
+        float p[32];
+        stage_load(stg, lane, p, g.res + base, g.ldc, rows_valid, ncols);
+        if (g.epi == 4) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= gelu_grad_f(p[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = p[i] > 0.f ? v[i] : 0.f;
+        }
     }
     stage_store(stg, lane, v, g.C + base, g.ldc, rows_valid, ncols);
+    if (g.colacc) {
+        // column sums of the stored tile (the staging buffer still holds it): lane = column
+        if (lane < ncols) {
+            float s = 0.f;
+            for (int r = 0; r < rows_valid; ++r) {
+                const float2 t = unpack_bf16x2(stg[r * 17 + (lane >> 1)]);
+                s += (lane & 1) ? t.y : t.x;
+            }
+            atomicAdd(g.colacc + col + lane, s);
+        }
+        __syncwarp();
+    }
 }
 
 struct Sched {

@@ -21,7 +21,9 @@ struct GemmArgs {
     int splits;                 // K splits when ws != nullptr
     int M, N, K;
     int64_t ldc;
-    int epi;                    // 0 none, 1 GELU(erf), 2 ReLU, 3 res + gamma * (acc + bias)
+    int epi;                    // 0 none, 1 GELU(erf), 2 ReLU, 3 res + gamma * (acc + bias),
+                                // 4 acc * GELU'(res), 5 acc * [res > 0]   (res = pre-activation, backward)
+    float* colacc;              // optional fp32 [N]: += column sums of the stored (bf16-rounded) output
 };
 
 size_t gemm_tc_smem_bytes();

@@ -185,8 +185,8 @@ class ViTLayer(nn.Module):
         d = self.attention.output.dense
         x = ops.linear_scale_residual(a, d.weight, d.bias, self.layer_scale1.lambda1, x)
         h = ops.layer_norm(x, self.norm2.weight, self.norm2.bias, 1e-6)
-        h = ops.linear(h, self.mlp.fc1.weight, self.mlp.fc1.bias, act="gelu")
-        return ops.linear_scale_residual(h, self.mlp.fc2.weight, self.mlp.fc2.bias, self.layer_scale2.lambda1, x)
+        return ops.mlp_scale_residual(h, self.mlp.fc1.weight, self.mlp.fc1.bias, self.mlp.fc2.weight,
+                                      self.mlp.fc2.bias, self.layer_scale2.lambda1, x)
 
 
 class Encoder(nn.Module):

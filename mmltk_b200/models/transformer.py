@@ -227,25 +227,30 @@ class GroupedLinear(nn.Module):
 
     def forward(self, x: torch.Tensor, groups: int, act=None) -> torch.Tensor:
         """x: [G', B, N, din] (one slice per group) or [B, N, din] (shared) -> [groups, B, N, dout]."""
-        w = self.weight[:groups].to(x.dtype)
-        b = self.bias[:groups].to(x.dtype)
-        dout = w.shape[1]
-        pad = (-dout) % 8 if (x.is_cuda and dout > 8) else 0
-        if pad:   # odd widths (91 classes) would put cuBLAS on its unaligned kernels
-            w = F.pad(w, (0, 0, 0, pad))
-            b = F.pad(b, (0, pad))
-        G = w.shape[0]
-        if x.dim() == 3:
-            B, N, C = x.shape
-            x = x.unsqueeze(0).expand(G, B, N, C)
-        Gx, B, N, C = x.shape
-        # batched GEMM with the bias folded in (beta = 1 on a broadcast bias)
-        y = torch.baddbmm(b[:, None, :], x.reshape(G, B * N, C), w.transpose(1, 2)).view(G, B, N, -1)
-        if pad:
-            y = y[..., :dout]
-        if act == "relu":
-            y = F.relu(y)
-        return y
+        return grouped_linear(x, self.weight[:groups], self.bias[:groups], act)
+
+
+def grouped_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, act=None) -> torch.Tensor:
+    """Per-group affine maps: x [G, B, N, din] or [B, N, din] (shared), w [G, dout, din], b [G, dout]."""
+    w = w.to(x.dtype)
+    b = b.to(x.dtype)
+    dout = w.shape[1]
+    pad = (-dout) % 8 if (x.is_cuda and dout > 8) else 0
+    if pad:   # odd widths (91 classes) would put cuBLAS on its unaligned kernels
+        w = F.pad(w, (0, 0, 0, pad))
+        b = F.pad(b, (0, pad))
+    G = w.shape[0]
+    if x.dim() == 3:
+        B, N, C = x.shape
+        x = x.unsqueeze(0).expand(G, B, N, C)
+    _, B, N, C = x.shape
+    # batched GEMM with the bias folded in (beta = 1 on a broadcast bias)
+    y = torch.baddbmm(b[:, None, :], x.reshape(G, B * N, C), w.transpose(1, 2)).view(G, B, N, -1)
+    if pad:
+        y = y[..., :dout]
+    if act == "relu":
+        y = F.relu(y)
+    return y
 
 
 class GroupedLayerNorm(nn.Module):
@@ -373,11 +378,20 @@ class Transformer(nn.Module):
             out_mem = memory.masked_fill(~valid, 0.0)
             # Selection pass over every token, without autograd: only the top-k indices leave it.
             with torch.no_grad():
-                h_all = self.enc_output_norm(self.enc_output(out_mem, groups), groups)   # [G, B, S, C]
-                cls = self.enc_out_class_embed(h_all, groups)                          # [G, B, S, K]
+                # the norm's per-group affine is folded into the class head: W' = W diag(gamma),
+                # b' = W beta + b, so the selection pass runs GEMM -> LN -> GEMM with no affine passes
+                h_all = self.enc_output(out_mem, groups)                               # [G, B, S, C]
+                hn = F.layer_norm(h_all, (h_all.shape[-1],), None, None, 1e-5)
+                del h_all
+                wc = self.enc_out_class_embed.weight[:groups].float()
+                gam = self.enc_output_norm.weight[:groups].float()
+                bet = self.enc_output_norm.bias[:groups].float()
+                w_f = wc * gam[:, None, :]
+                b_f = self.enc_out_class_embed.bias[:groups].float() + torch.einsum("gkc,gc->gk", wc, bet)
+                cls = grouped_linear(hn, w_f, b_f)                                     # [G, B, S, K]
                 k = min(cfg.num_queries, cls.shape[2])
                 topk = cls.max(-1)[0].topk(k, dim=2)[1]                                # [G, B, k]
-                del h_all, cls
+                del hn, cls
             # Differentiable pass on the selected tokens only: the head is per token, so recomputing
             # enc_output + norm + box MLP on the k chosen rows gives the same values (and gradients)
             # as gathering them from the full pass, at k / S of the cost.

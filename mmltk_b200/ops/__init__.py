@@ -2,7 +2,7 @@
 CPU tensors run the plain-PyTorch fp32 definitions that serve as test oracles."""
 from ._ext import has_kernels, has_native, kernels, native
 from .attention import attention, attention_reference, qkv_attention, qkv_attention_reference
-from .linear import linear, linear_scale_residual
+from .linear import linear, linear_scale_residual, mlp_scale_residual
 from .msda import msda, msda_reference
 from .norm import layer_norm
 from .losses import dense_focal_neg

@@ -22,10 +22,10 @@ import torch
 import torch.nn.functional as F
 
 from ._ext import kernels
-from .gemm import gemm_nn, gemm_nt, gemm_nt_epilogue, gemm_tn, gemm_tn_acc
+from .gemm import _fits_nt, gemm_nn, gemm_nt, gemm_nt_epilogue, gemm_tn, gemm_tn_acc, tc_gemm_enabled
 from .gradacc import grad_target
 
-__all__ = ["linear", "linear_scale_residual", "set_fused_linear"]
+__all__ = ["linear", "linear_scale_residual", "mlp_scale_residual", "set_fused_linear"]
 
 _ACTS = {None: 0, "none": 0, "gelu": 1, "relu": 2}
 _state = {"enabled": os.environ.get("MMLTK_FUSED_LINEAR", "1") != "0"}
@@ -142,3 +142,51 @@ def linear_scale_residual(x, w, b, gamma, res):
     if _ok(x, w) and gamma.dtype == x.dtype:
         return _LinearScaleResidual.apply(x, w, b, gamma, res)
     return res + gamma.to(x.dtype) * F.linear(x, w.to(x.dtype), b.to(x.dtype))
+
+
+class _MlpScaleResidual(torch.autograd.Function):
+    """y = res + gamma * (fc2(GELU(fc1(x)))) -- the ViT MLP sub-block as one autograd node, so that
+    the backward can fuse across the two layers: the fc2 input-gradient GEMM applies GELU' of the
+    saved fc1 pre-activation in its epilogue and accumulates the fc1 bias gradient from the same
+    tile (no separate activation-backward pass over the [tokens, 4C] gradient)."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2, gamma, res):
+        shp = x.shape
+        x2 = _2d(x, shp[-1])
+        r2 = _2d(res, w2.shape[0])
+        h, pre1 = gemm_nt_epilogue(x2, w1, b1, "gelu")
+        y, pre2 = gemm_nt_epilogue(h, w2, b2, "scale_residual", r2, gamma)
+        ctx.save_for_backward(x2, w1, pre1, h, w2, gamma, pre2)
+        ctx.params = (w1, b1, w2, b2, gamma)
+        ctx.shp = shp
+        return y.view(*shp[:-1], w2.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, w1, pre1, h, w2, gamma, pre2 = ctx.saved_tensors
+        k = kernels()
+        wt1, bt1, wt2, bt2, gt = (grad_target(p) for p in ctx.params)
+        g = _2d(gy, w2.shape[0])
+        g_pre2, g_gamma = k.scale_bwd(g, pre2, gamma, gt)
+        gb2 = k.colsum(g_pre2, None, bt2)
+        gw2 = gemm_tn(g_pre2, h) if wt2 is None else gemm_tn_acc(g_pre2, h, wt2)
+        gb1 = bt1 if bt1 is not None else torch.empty(w1.shape[0], device=g.device, dtype=w1.dtype)
+        # fc2 input gradient, GELU backward and the fc1 bias gradient in one GEMM launch
+        g_pre1 = k.gemm_tc(g_pre2, w2, None, False, True, 4, False, pre1, None, gb1, bt1 is not None)[0]
+        gw1 = gemm_tn(g_pre1, x2) if wt1 is None else gemm_tn_acc(g_pre1, x2, wt1)
+        gx = gemm_nn(g_pre1, w1)
+        none_if = lambda t, v: None if t is not None else v
+        return (gx.view(ctx.shp), none_if(wt1, gw1), none_if(bt1, gb1), none_if(wt2, gw2), none_if(bt2, gb2),
+                none_if(gt, g_gamma), gy)
+
+
+def mlp_scale_residual(x, w1, b1, w2, b2, gamma, res):
+    """res + gamma * (GELU(x W1^T + b1) W2^T + b2)."""
+    if (_ok(x, w1) and _ok(x, w2.new_empty(8, w2.shape[1])) and gamma.dtype == x.dtype and w1.shape[0] % 128 == 0
+            and tc_gemm_enabled()):
+        x2 = x.reshape(-1, x.shape[-1])
+        if _fits_nt(x2 if x2.is_contiguous() else x2.contiguous(), w1):
+            return _MlpScaleResidual.apply(x, w1, b1, w2, b2, gamma, res)
+    h = linear(x, w1, b1, act="gelu")
+    return linear_scale_residual(h, w2, b2, gamma, res)

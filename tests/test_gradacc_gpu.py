@@ -141,3 +141,29 @@ def test_fused_detection_losses_match_per_layer_statement(ia_bce):
         assert torch.allclose(l1[k], l0[k], rtol=5e-3, atol=1e-3), (k, l1[k], l0[k])
     assert torch.allclose(g1, g0, rtol=2e-2, atol=2e-5), (g1 - g0).abs().max()
     assert torch.allclose(b1, b0, rtol=2e-2, atol=1e-4), (b1 - b0).abs().max()
+
+
+def test_mlp_block_fused_backward_matches_unfused():
+    from mmltk_b200.ops.linear import linear, linear_scale_residual, mlp_scale_residual
+    torch.manual_seed(0)
+    C = 384
+    x = (torch.randn(2, 650, C, device="cuda") * 0.5).bfloat16()
+    res = torch.randn(2, 650, C, device="cuda").bfloat16()
+    ps = [torch.nn.Parameter((torch.randn(*s, device="cuda") * 0.05).bfloat16())
+          for s in [(4 * C, C), (4 * C,), (C, 4 * C), (C,), (C,)]]
+    go = torch.randn(2, 650, C, device="cuda").bfloat16()
+    grads = {}
+    for fused in (True, False):
+        xi = x.clone().requires_grad_()
+        ri = res.clone().requires_grad_()
+        for p in ps:
+            p.grad = None
+        if fused:
+            y = mlp_scale_residual(xi, *ps, ri)
+        else:
+            h = linear(xi, ps[0], ps[1], act="gelu")
+            y = linear_scale_residual(h, ps[2], ps[3], ps[4], ri)
+        y.backward(go)
+        grads[fused] = [y.detach().float(), xi.grad.float(), ri.grad.float()] + [p.grad.float() for p in ps]
+    for a, b in zip(grads[True], grads[False]):
+        assert torch.allclose(a, b, rtol=3e-2, atol=3e-2 * (1 + b.abs().max().item() * 0.02)), (a - b).abs().max()
