@@ -237,7 +237,8 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
             cudaError_t e = cudaSuccess;
             dispatch_vec(C, [&](auto nvl) {
                 auto kern = ln_bwd_kernel<T, Wt, decltype(nvl)::value>;
-                if (smem > 48 * 1024)
+                // the kernel also has a few bytes of static shared memory, so opt in at 48 KB already
+                if (smem >= 40 * 1024)
                     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
                 if (e != cudaSuccess) return;
                 kern<<<blocks, threads, smem, st>>>(static_cast<const T*>(gy), static_cast<const T*>(x),

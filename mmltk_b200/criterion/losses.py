@@ -22,7 +22,7 @@ import torch.nn.functional as F
 
 from ..config import RfDetrConfig
 from ..utils.boxes import aligned_giou, aligned_iou, cxcywh_to_xyxy
-from .matcher import hungarian_match
+from .matcher import hungarian_match, mask_cost
 from .masks import mask_losses
 from .targets import Targets
 
@@ -190,8 +190,13 @@ class SetCriterion:
         self._match_full = None
         for q, idx in by_q.items():
             g = groups if q % groups == 0 else 1
+            mcost = None
+            if cfg.segmentation and targets.masks is not None and all(
+                    ("sparse_masks" in layers[i] or "pred_masks" in layers[i]) for i in idx):
+                mcost = [mask_cost(layers[i], targets, cfg.mask_ce_loss_coef, cfg.mask_dice_loss_coef,
+                                   cfg.mask_point_sample_ratio) for i in idx]
             mm = hungarian_match([layers[i]["pred_logits"] for i in idx], [layers[i]["pred_boxes"] for i in idx],
-                                 targets, g, cfg.set_cost_class, cfg.set_cost_bbox, cfg.set_cost_giou)
+                                 targets, g, cfg.set_cost_class, cfg.set_cost_bbox, cfg.set_cost_giou, mcost)
             for j, i in enumerate(idx):
                 match[i] = mm[j]
             if len(by_q) == 1:

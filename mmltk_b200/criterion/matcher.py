@@ -26,7 +26,7 @@ from ..ops._ext import kernels, native
 from ..utils.boxes import cxcywh_to_xyxy, generalized_box_iou
 from .targets import Targets
 
-__all__ = ["matcher_cost_reference", "hungarian_match"]
+__all__ = ["matcher_cost_reference", "hungarian_match", "mask_cost"]
 
 FOCAL_ALPHA = 0.25
 
@@ -54,8 +54,43 @@ def matcher_cost_reference(logits: Sequence[torch.Tensor], boxes: Sequence[torch
     return torch.stack(out)
 
 
+def mask_cost(layer: dict, targets: Targets, ce_coef: float, dice_coef: float, ratio: int) -> torch.Tensor:
+    """[B, Q, T] mask matching cost (reference `detection_ops.cpp:1085-1136`): one random point set
+    per call, shared by every query; predicted logits sampled at the points (bilinear, from the
+    sparse head form: sampled spatial features x query features + bias), target masks sampled
+    nearest; sigmoid-CE and dice costs as GEMMs over the point axis (K5 in GEMM form)."""
+    from .masks import point_sample
+    with torch.no_grad():
+        if "sparse_masks" in layer:
+            spatial, query, bias = layer["sparse_masks"]                # [B,C,h,w], [B,Q,C], [1]
+            B, Cf, h, w = spatial.shape
+            P = max(1, h * w // ratio)
+            pts = torch.rand(1, P, 2, device=spatial.device)
+            feat = point_sample(spatial.float(), pts.expand(B, P, 2))   # [B, C, P]
+            x = torch.bmm(query.float(), feat) + bias.float()            # [B, Q, P]
+        else:
+            pm = layer["pred_masks"]                                     # [B, Q, h, w]
+            B, Q, h, w = pm.shape
+            P = max(1, h * w // ratio)
+            pts = torch.rand(1, P, 2, device=pm.device)
+            x = point_sample(pm.float().flatten(0, 1)[:, None], pts.expand(B * Q, P, 2))[:, 0].view(B, Q, P)
+        T = targets.slots
+        offs = torch.as_tensor(targets.mask_offsets, device=x.device)
+        rows = (offs[:, None] + torch.arange(T, device=x.device)[None]).clamp(max=max(0, targets.masks.shape[0] - 1))
+        tm = targets.masks[rows.reshape(-1)].float()[:, None]           # [B*T, 1, Hm, Wm]
+        t = point_sample(tm, pts.expand(B * T, P, 2), mode="nearest")[:, 0].view(B, T, P)
+        pos, neg = F.softplus(-x), F.softplus(x)
+        ce = (torch.bmm(pos, t.transpose(1, 2)) + torch.bmm(neg, (1 - t).transpose(1, 2))) / P
+        sig = x.sigmoid()
+        num = 2 * torch.bmm(sig, t.transpose(1, 2))
+        den = sig.sum(-1)[:, :, None] + t.sum(-1)[:, None, :]
+        dice = 1 - (num + 1) / (den + 1)
+        return ce_coef * ce + dice_coef * dice
+
+
 def hungarian_match(logits: List[torch.Tensor], boxes: List[torch.Tensor], targets: Targets, groups: int,
-                    w_class: float = 2.0, w_bbox: float = 5.0, w_giou: float = 2.0) -> torch.Tensor:
+                    w_class: float = 2.0, w_bbox: float = 5.0, w_giou: float = 2.0, mask_costs=None) -> torch.Tensor:
+    """mask_costs: optional list (one per layer) of [B, Q, T] costs added before the assignment."""
     with torch.no_grad():
         dev = logits[0].device
         Q = logits[0].shape[1]
@@ -63,8 +98,12 @@ def hungarian_match(logits: List[torch.Tensor], boxes: List[torch.Tensor], targe
             k = kernels()
             cost = k.matcher_cost([l.detach() for l in logits], [b.detach() for b in boxes], targets.labels,
                                   targets.boxes, targets.counts, w_class, w_bbox, w_giou, FOCAL_ALPHA)
+            if mask_costs is not None:
+                cost += torch.stack(mask_costs).to(cost.dtype)
             match, _status = k.lsap_batched(cost, targets.counts, groups)
             return match
         cost = matcher_cost_reference(logits, boxes, targets, w_class, w_bbox, w_giou)
+        if mask_costs is not None:
+            cost = cost + torch.stack(mask_costs).float()
         m = native().match_batched(cost.cpu(), targets.counts.cpu().to(torch.int64), groups)
         return m.to(dev)

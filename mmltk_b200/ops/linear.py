@@ -28,7 +28,8 @@ from .gradacc import grad_target
 __all__ = ["linear", "linear_scale_residual", "mlp_scale_residual", "set_fused_linear"]
 
 _ACTS = {None: 0, "none": 0, "gelu": 1, "relu": 2}
-_state = {"enabled": os.environ.get("MMLTK_FUSED_LINEAR", "1") != "0"}
+_state = {"enabled": os.environ.get("MMLTK_FUSED_LINEAR", "1") != "0",
+          "fused_mlp": os.environ.get("MMLTK_FUSED_MLP", "0") == "1"}
 
 
 def set_fused_linear(flag: bool) -> None:
@@ -182,9 +183,14 @@ class _MlpScaleResidual(torch.autograd.Function):
 
 
 def mlp_scale_residual(x, w1, b1, w2, b2, gamma, res):
-    """res + gamma * (GELU(x W1^T + b1) W2^T + b2)."""
-    if (_ok(x, w1) and _ok(x, w2.new_empty(8, w2.shape[1])) and gamma.dtype == x.dtype and w1.shape[0] % 128 == 0
-            and tc_gemm_enabled()):
+    """res + gamma * (GELU(x W1^T + b1) W2^T + b2).
+
+    The cross-layer fused backward is opt-in (``MMLTK_FUSED_MLP=1``): measured on B200 for the
+    RF-DETR-M ViT (10.4k tokens x 384 -> 1536) the GELU' epilogue leaves the tcgen05 GEMM
+    epilogue-bound (~75 us per layer) and the step ~0.1 ms slower than cuBLAS + the separate
+    single-pass activation/bias kernel."""
+    if (_state["fused_mlp"] and _ok(x, w1) and _ok(x, w2.new_empty(8, w2.shape[1])) and gamma.dtype == x.dtype
+            and w1.shape[0] % 128 == 0 and tc_gemm_enabled()):
         x2 = x.reshape(-1, x.shape[-1])
         if _fits_nt(x2 if x2.is_contiguous() else x2.contiguous(), w1):
             return _MlpScaleResidual.apply(x, w1, b1, w2, b2, gamma, res)

@@ -19,6 +19,7 @@ Differences by design:
 from __future__ import annotations
 
 import json
+import logging
 import math
 import os
 import threading
@@ -35,7 +36,9 @@ from ..data.loader import BatchLoader, CompiledDataset
 from ..infer.predictor import Predictor, resolve_model
 from ..parallel.launch import DistContext, init_distributed
 
-__all__ = ["run_training", "ProgressWriter", "checkpoint_metric"]
+__all__ = ["run_training", "ProgressWriter", "checkpoint_metric", "evaluate", "validation_loss"]
+
+log = logging.getLogger("mmltk.train")
 
 
 class ProgressWriter:
@@ -63,6 +66,19 @@ class ProgressWriter:
 
     def error(self, message: str) -> None:
         self.submit({"phase": "error", "error": message}, force=True)
+
+
+def _validation_record(opts, paths, ctx, epoch: int, source: str, summary: Dict, seconds: float) -> None:
+    """``--validation-profile``: one JSON line per validation pass (reference
+    `validation_profile.jsonl`, `src/rfdetr/inference/evaluator.cpp:1490-1560`)."""
+    if not (opts.validation_profile and ctx.main):
+        return
+    rec = {"event": "rfdetr.validation.pass", "event_source": "train", "epoch": epoch, "validation_pass": epoch,
+           "model_source": source, "world_size": ctx.world_size, "total_wall_seconds": seconds,
+           "metric_mode": "bbox_and_mask" if "segm" in summary else "bbox", **_summary_json(summary),
+           "val_loss": summary.get("loss")}
+    with open(os.path.join(os.path.dirname(paths["log"]), "validation_profile.jsonl"), "a") as f:
+        f.write(json.dumps(rec) + "\n")
 
 
 def checkpoint_metric(summary: Dict, masks: bool) -> float:
@@ -118,7 +134,7 @@ def _check_resume(extra: Dict, opts: TrainOptions) -> None:
 
 
 def evaluate(model_fp32: torch.nn.Module, compiled: str, ctx: DistContext, batch_size: int, max_dets: int,
-             masks: bool, shard: bool = True) -> Dict:
+             masks: bool, shard: bool = True, with_loss: bool = False) -> Dict:
     """COCO AP of a model over a compiled split; each rank takes every world-th batch."""
     from ..eval import CocoEvaluator
     pred = Predictor(model_fp32, device=ctx.device, cuda_graph=ctx.device.type == "cuda", with_masks=masks)
@@ -147,7 +163,44 @@ def evaluate(model_fp32: torch.nn.Module, compiled: str, ctx: DistContext, batch
     pred.release()
     if shard and ctx.enabled:
         ev.reduce()
-    return ev.summarize()
+    out = ev.summarize()
+    if with_loss:
+        out["loss"] = validation_loss(pred.model, compiled, ctx, batch_size, shard)
+    return out
+
+
+@torch.no_grad()
+def validation_loss(model, compiled: str, ctx: DistContext, batch_size: int, shard: bool = True) -> float:
+    """Mean weighted criterion loss over a compiled split, eval-mode outputs (one query group),
+    averaged across ranks (reference `--validation-loss`, `train.cpp:1513-1868`)."""
+    from ..criterion import SetCriterion
+    from ..data.augment import normalize_images
+    ds = CompiledDataset(compiled)
+    counts = ds.reader.instance_counts()
+    slots = max(1, int(counts.max()) if counts.numel() else 1)
+    crit = SetCriterion(model.cfg)
+    dev = ctx.device
+    bl = BatchLoader(compiled, batch_size, shuffle=False, pixels="uint8", max_targets=slots,
+                     shard_rank=ctx.rank if shard else 0, shard_count=ctx.world_size if shard else 1,
+                     device=dev if dev.type == "cuda" else None)
+    was_training = model.training
+    model.eval()
+    dtype = next(model.parameters()).dtype
+    total = torch.zeros((), dtype=torch.float64, device=dev)
+    n = torch.zeros((), dtype=torch.float64, device=dev)
+    for images, targets, idx in bl:
+        x = normalize_images(images.to(dev), dtype if dev.type == "cuda" else torch.float32)
+        out = model(x, include_masks=bool(model.cfg.segmentation))
+        losses, _ = crit(out, targets.to(dev), training=False)
+        total += crit.weighted(losses).double() * len(idx)
+        n += len(idx)
+    if ctx.enabled:
+        import torch.distributed as dist
+        both = torch.stack([total, n]).to(dev)
+        dist.all_reduce(both)
+        total, n = both[0], both[1]
+    model.train(was_training)
+    return float(total / n.clamp(min=1))
 
 
 def run_training(opts: TrainOptions, ctx: Optional[DistContext] = None) -> Dict:
@@ -266,6 +319,12 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
             if r.grad_norm is not None or not ctx.device.type == "cuda":
                 loss_sum += float(r.loss)
                 n_loss += 1
+            if ctx.main and opts.print_freq > 0 and (b + 1) % opts.print_freq == 0:
+                el = time.monotonic() - t_epoch
+                log.info("epoch %d step %d/%d loss %.4f (mean %.4f) grad_norm %s %.1f img/s", epoch, b + 1,
+                         steps_per_epoch * opts.grad_accum_steps, float(r.loss), loss_sum / max(1, n_loss),
+                         "-" if r.grad_norm is None else f"{r.grad_norm:.3f}",
+                         (b + 1) * opts.batch_size * ctx.world_size / max(el, 1e-9))
             if progress is not None:
                 el = time.monotonic() - t_epoch
                 progress.submit({"phase": "train", "epoch": epoch, "completed_batches": b + 1,
@@ -278,11 +337,17 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
         if progress is not None:
             progress.submit({"phase": "validate", "epoch": epoch}, force=True)
         regular = engine.export_model("master")
-        val = evaluate(regular, opts.val_compiled, ctx, val_bs, opts.eval_max_dets, masks)
+        t_val = time.monotonic()
+        val = evaluate(regular, opts.val_compiled, ctx, val_bs, opts.eval_max_dets, masks,
+                       with_loss=opts.validation_loss)
+        _validation_record(opts, paths, ctx, epoch, "regular", val, time.monotonic() - t_val)
         ema_val = None
         ema_model = engine.export_model("ema") if opts.use_ema else None
         if ema_model is not None:
-            ema_val = evaluate(ema_model, opts.val_compiled, ctx, val_bs, opts.eval_max_dets, masks)
+            t_val = time.monotonic()
+            ema_val = evaluate(ema_model, opts.val_compiled, ctx, val_bs, opts.eval_max_dets, masks,
+                               with_loss=opts.validation_loss)
+            _validation_record(opts, paths, ctx, epoch, "ema", ema_val, time.monotonic() - t_val)
         if ctx.main:
             state = regular.state_dict()
             save_native_checkpoint(os.path.join(os.path.dirname(paths["ckpt"]), f"checkpoint_epoch_{epoch + 1}.pt"),
@@ -304,8 +369,9 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
             rec = {"epoch": epoch, "train_lanes": 1, "eval_lanes": 1,
                    "effective_batch_per_rank": opts.batch_size * opts.grad_accum_steps,
                    "effective_batch_global": opts.batch_size * opts.grad_accum_steps * ctx.world_size,
-                   "train_loss": train_loss, "val_loss": None, "val": _summary_json(val),
-                   "ema_val_loss": None, "ema_val": _summary_json(ema_val)}
+                   "train_loss": train_loss, "val_loss": val.get("loss"), "val": _summary_json(val),
+                   "ema_val_loss": None if ema_val is None else ema_val.get("loss"),
+                   "ema_val": _summary_json(ema_val)}
             with open(paths["log"], "a") as f:
                 f.write(json.dumps(rec) + "\n")
             history.append(rec)

@@ -24,6 +24,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--top", type=int, default=30)
     ap.add_argument("--by-op", action="store_true", help="rank aten ops (with input shapes) instead of kernels")
+    ap.add_argument("--no-shapes", action="store_true", help="with --by-op: group by op name only")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         print("profile: needs a GPU", file=sys.stderr)
@@ -51,9 +52,8 @@ def main(argv=None) -> int:
             for _ in range(a.steps):
                 eng.step()
             torch.cuda.synchronize()
-        print(prof.key_averages(group_by_input_shape=True).table(sort_by="self_cuda_time_total",
-                                                                  row_limit=a.top, max_name_column_width=60,
-                                                                  max_shapes_column_width=90))
+        print(prof.key_averages(group_by_input_shape=not a.no_shapes).table(
+            sort_by="self_cuda_time_total", row_limit=a.top, max_name_column_width=60, max_shapes_column_width=90))
         return 0
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         for _ in range(a.steps):

@@ -74,3 +74,14 @@ def test_grad_accumulation_counts_optimizer_steps(splits, tmp_path):
     run_training(_opts(tr, va, out, epochs=1, grad_accum_steps=3, use_ema=False))
     ck = load_native_checkpoint(str(out / "checkpoint.pt"))
     assert ck.extra["optimizer"]["step"] == 1
+
+
+def test_validation_loss_and_profile(splits, tmp_path):
+    tr, va = splits
+    out = tmp_path / "vl"
+    run_training(_opts(tr, va, out, epochs=1, use_ema=False, validation_loss=True, validation_profile=True,
+                       print_freq=1))
+    log = [json.loads(l) for l in open(out / "log.txt")]
+    assert log[0]["val_loss"] is not None and log[0]["val_loss"] > 0
+    prof = [json.loads(l) for l in open(out / "validation_profile.jsonl")]
+    assert prof[0]["event"] == "rfdetr.validation.pass" and prof[0]["model_source"] == "regular"

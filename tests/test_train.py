@@ -139,3 +139,20 @@ def test_cuda_losses_match_cpu_oracle(cuda_device):
     for k in ("loss_bbox", "loss_giou", "loss_ce"):
         a, b = float(lc[k]), float(lg[k])
         assert abs(a - b) / max(abs(a), 1e-3) < 0.1, (k, a, b)
+
+
+def test_mask_matching_cost_prefers_the_right_mask():
+    """The mask term of the matcher cost is lowest for the query whose mask logits agree with the target."""
+    from mmltk_b200.criterion.matcher import mask_cost
+    from mmltk_b200.criterion.targets import pad_targets
+    torch.manual_seed(0)
+    H = W = 16
+    m1 = torch.zeros(H, W, dtype=torch.bool)
+    m1[:8] = True
+    m2 = ~m1
+    tg = pad_targets([{"boxes": torch.tensor([[0.5, 0.25, 1.0, 0.5], [0.5, 0.75, 1.0, 0.5]]),
+                       "labels": torch.tensor([1, 2]), "masks": torch.stack([m1, m2])}], slots=3)
+    logits = torch.stack([(m1.float() * 2 - 1) * 8, (m2.float() * 2 - 1) * 8])[None]   # [1, Q=2, H, W]
+    c = mask_cost({"pred_masks": logits}, tg, 5.0, 5.0, 1)
+    assert c.shape == (1, 2, 3)
+    assert c[0, 0, 0] < c[0, 0, 1] and c[0, 1, 1] < c[0, 1, 0]
