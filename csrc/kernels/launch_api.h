@@ -105,6 +105,22 @@ cudaError_t launch_augment(DType out_t, bool in_u8, const void* in, void* out, c
 cudaError_t launch_warp_masks(const uint8_t* src, const uint8_t* donor_masks, const int32_t* rows, const float* rec,
                               uint8_t* out, int N, int H, int W, cudaStream_t st);
 
+// ---------------------------------------------------------------- image ops (imaging.cu)
+// src: pitched 8-bit 3-channel frame; dst: [3, dh, dw] fp32 in [0,1] or normalised bf16
+cudaError_t launch_letterbox(const uint8_t* src, int64_t pitch, int sw, int sh, bool bgr, void* dst, int dw, int dh,
+                             bool normalize_bf16, cudaStream_t st);
+cudaError_t launch_vflip(uint8_t* buf, int64_t pitch, int width, int height, cudaStream_t st);
+cudaError_t launch_draw(uint8_t* img, int64_t pitch, int W, int H, const float* boxes, const uint8_t* colors,
+                        const uint8_t* masks, const char* text, int text_len, int n, int thickness, float mask_alpha,
+                        int scale, cudaStream_t st);
+cudaError_t launch_composite(uint8_t* dst, int64_t dpitch, const uint8_t* rgba, int64_t spitch, int W, int H,
+                             bool swap_rb, cudaStream_t st);
+cudaError_t launch_resize_masks(const uint8_t* src, int n, int sh, int sw, uint8_t* dst, int dh, int dw,
+                                cudaStream_t st);
+cudaError_t launch_pack_masks(const uint8_t* m, int n, int64_t pixels, uint64_t* out, cudaStream_t st);
+cudaError_t launch_sample_packed(const uint64_t* bits, int n, int H, int W, const float* pts, int P, float* out,
+                                 cudaStream_t st);
+
 // ---------------------------------------------------------------- detection post-process
 // logits [B,Q,C], boxes [B,Q,4] cxcywh (normalised); sizes [B,2] (h, w) fp32 or null (fixed_h/w).
 // K <= 1024.  Outputs: scores [B,K] f32, labels [B,K] i64, boxes [B,K,4] xyxy pixels, queries [B,K] i32.

@@ -131,6 +131,7 @@ void register_more_ops(pybind11::module& m) {
     register_gemm_ops(m);
     register_aug_ops(m);
     register_loss_ops(m);
+    register_image_ops(m);
 }
 
 }  // namespace mmltk

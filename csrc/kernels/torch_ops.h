@@ -17,5 +17,6 @@ void register_ddp_ops(pybind11::module& m);
 void register_gemm_ops(pybind11::module& m);
 void register_aug_ops(pybind11::module& m);
 void register_loss_ops(pybind11::module& m);
+void register_image_ops(pybind11::module& m);
 
 }  // namespace mmltk
