@@ -155,6 +155,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--output", required=True)
     p.add_argument("--threshold", type=float, default=0.5)
     p.add_argument("--backend", choices=("auto", "weights", "onnx", "tensorrt"), default="auto")
+    p.add_argument("--draw-dir", default=None, help="write annotated PNGs (drawn on the GPU) here")
     _add_model_inputs(p)
     _add_execution(p)
     p = rf.add_parser("evaluate")
@@ -184,6 +185,16 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--output", default=None)
     _add_model_inputs(p)
     _add_execution(p)
+    p = rf.add_parser("live", help="headless live analysis of a frame source (synthetic: no capture device)")
+    _add_model_inputs(p)
+    p.add_argument("--synthetic", action="store_true", default=True)
+    p.add_argument("--frames", type=int, default=300)
+    p.add_argument("--width", type=int, default=1280)
+    p.add_argument("--height", type=int, default=720)
+    p.add_argument("--threshold", type=float, default=0.5)
+    p.add_argument("--output", default=None, help="directory for annotated PNG frames")
+    p.add_argument("--save-every", type=int, default=0)
+    p.add_argument("--device-id", type=int, default=0)
     p = rf.add_parser("latency", help="batch-1 (or --batch-size) latency of the CUDA-graph predictor")
     _add_model_inputs(p)
     p.add_argument("--batch-size", type=int, default=1)
@@ -319,7 +330,8 @@ def _predict(a) -> int:
         raise SystemExit("predict takes --compiled or image paths (exactly one source)")
     pred, info = _predictor(a)
     if a.compiled:
-        recs, timing = predict_compiled(pred, a.compiled, a.batch_size, a.threshold, a.workers)
+        recs, timing = predict_compiled(pred, a.compiled, a.batch_size, a.threshold, a.workers,
+                                        draw_dir=a.draw_dir)
         write_predictions_json(a.output, recs, info, "compiled_dataset", compiled_path=a.compiled)
     else:
         recs = predict_images(pred, a.images, a.threshold)
@@ -370,6 +382,18 @@ def _train(a) -> int:
     return 0
 
 
+def _live(a) -> int:
+    from ..live import FrameAnalyzer, SyntheticFrameSource, run_live
+    pred, info = _predictor(a)
+    src = SyntheticFrameSource(a.width, a.height, frames=a.frames)
+    an = FrameAnalyzer(pred, [], threshold=a.threshold)
+    st = run_live(src, an, out_dir=a.output, save_every=a.save_every)
+    print(json.dumps({"preset_name": info["preset_name"], "frames_in": st.frames_in,
+                      "frames_analyzed": st.frames_analyzed, "dropped": st.dropped, "fps": st.fps,
+                      "latency_ms_p50": st.latency_ms_p50}))
+    return 0
+
+
 def _latency(a) -> int:
     pred, info = _predictor(a)
     print(json.dumps({"preset_name": info["preset_name"], **pred.latency(a.iters, 20, a.batch_size)}))
@@ -412,6 +436,8 @@ def run(argv: Optional[List[str]] = None) -> int:
                           "environment")
     if r == "latency":
         return _latency(a)
+    if r == "live":
+        return _live(a)
     raise SystemExit(f"unknown command {r}")
 
 

@@ -183,8 +183,25 @@ def _records(results: Dict[str, torch.Tensor], indices: Sequence[int], names: Se
     return recs
 
 
+def _draw_batch(images, res, idx, class_names, threshold, out_dir) -> None:
+    """Annotated PNGs (masks, boxes, label bars drawn on the device) for one batch."""
+    from ..ops._ext import native
+    from .visualize import draw_detections
+    os.makedirs(out_dir, exist_ok=True)
+    for j, di in enumerate(idx):
+        img = images[j]
+        if img.dtype != torch.uint8:
+            img = (img.float() * 255).round().clamp(0, 255).to(torch.uint8)
+        hwc = img.permute(1, 2, 0).contiguous()
+        one = {k: v[j] for k, v in res.items()}
+        hwc = draw_detections(hwc, one, class_names, threshold)
+        with open(os.path.join(out_dir, f"{int(di):06d}.png"), "wb") as f:
+            f.write(native().encode_png(hwc.cpu()))
+
+
 def predict_compiled(predictor: Predictor, compiled: str, batch_size: int = 1, threshold: float = 0.5,
-                     workers: int = 4, limit: Optional[int] = None, evaluator=None) -> Tuple[List[dict], dict]:
+                     workers: int = 4, limit: Optional[int] = None, evaluator=None,
+                     draw_dir: Optional[str] = None) -> Tuple[List[dict], dict]:
     from ..data.loader import BatchLoader
     bl = BatchLoader(compiled, batch_size, shuffle=False, pixels="uint8", workers=workers, max_targets=1,
                      device=predictor.device if predictor.cuda else None)
@@ -202,6 +219,8 @@ def predict_compiled(predictor: Predictor, compiled: str, batch_size: int = 1, t
             res = predictor(images)
         if evaluator is not None:
             evaluator.add(idx, res["scores"], res["labels"], res["boxes"], res.get("masks"))
+        if draw_dir:
+            _draw_batch(images, res, idx, class_names, threshold, draw_dir)
         records += _records(res, idx, [], class_names, threshold)
         n += len(idx)
         if limit and n >= limit:

@@ -66,3 +66,15 @@ def test_train_two_rank_gloo(data, tmp_path):
 def test_train_requires_inputs(data, tmp_path):
     with pytest.raises(SystemExit):
         main(["rfdetr", "train", "--train-compiled", str(data / "train.bin"), "--output-dir", str(tmp_path)])
+
+
+def test_predict_draw_and_live(data, tmp_path, capsys):
+    out = tmp_path / "draw"
+    assert main(["rfdetr", "predict", "--compiled", str(data / "val.bin"), "--preset", "rf-detr-tiny-test",
+                 "--output", str(tmp_path / "p.json"), "--threshold", "0.0", "--draw-dir", str(out)]) == 0
+    assert len(list(out.glob("*.png"))) == 8
+    capsys.readouterr()
+    assert main(["rfdetr", "live", "--preset", "rf-detr-tiny-test", "--frames", "4", "--width", "64",
+                 "--height", "48", "--threshold", "0.0"]) == 0
+    st = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert st["frames_in"] == 4 and st["frames_analyzed"] >= 1
