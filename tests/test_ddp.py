@@ -174,3 +174,35 @@ def test_fused_ddp_matches_nccl_baseline():
     n = min(fused[0][3].numel(), nccl[0][3].numel())  # the fused layout pads to a multiple of world * 64
     diff = (fused[0][3][:n] - nccl[0][3][:n]).abs().max().item()
     assert diff < 0.05
+
+
+def test_launcher_fails_fast_when_a_rank_dies(tmp_path):
+    """Host-side failure injection: rank 1 exits with an error before the first collective; the
+    launcher returns its code and terminates rank 0, which is blocked in a gloo barrier."""
+    import sys
+    import time
+    from mmltk_b200.parallel.launch import launch_workers
+    script = tmp_path / "worker.py"
+    script.write_text(
+        "import sys, datetime, torch.distributed as dist\n"
+        "a = sys.argv\n"
+        "rank = int(a[a.index('--dist-rank') + 1]); world = int(a[a.index('--dist-world-size') + 1])\n"
+        "store = a[a.index('--dist-store-file') + 1]\n"
+        "if rank == 1:\n"
+        "    sys.exit(3)\n"
+        "dist.init_process_group('gloo', store=dist.FileStore(store, world), rank=rank, world_size=world,\n"
+        "                        timeout=datetime.timedelta(seconds=120))\n"
+        "dist.barrier()\n")
+    t0 = time.time()
+    code = launch_workers(["--workers", "2"], [0, 1], entry=[sys.executable, str(script)])
+    assert code == 3
+    assert time.time() - t0 < 60
+
+
+def test_worker_argv_rewrite():
+    from mmltk_b200.parallel.launch import rewrite_worker_argv
+    argv = ["rfdetr", "train", "--device-ids", "0,1", "--workers", "8", "--epochs", "2", "--dist-worker"]
+    out = rewrite_worker_argv(argv, 1, 2, 1, "/tmp/s", 4)
+    assert out[:4] == ["rfdetr", "train", "--epochs", "2"]
+    assert out[out.index("--dist-rank") + 1] == "1" and out[out.index("--device-id") + 1] == "1"
+    assert out.count("--workers") == 1 and out[out.index("--workers") + 1] == "4"
