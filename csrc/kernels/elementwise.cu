@@ -23,6 +23,9 @@ namespace {
 
 constexpr int kColThreads = 256;
 constexpr int kSlabCols = 256;     // columns per slab = 32 lanes x 8
+constexpr int kColCtasPerSm = 4;   // resident CTAs per SM (64 registers per thread)
+// rows per row lane with loads in flight together (the GELU derivative needs the registers of two)
+__host__ __device__ constexpr int col_unroll(int mode) { return mode == 2 ? 2 : 4; }
 
 __device__ __forceinline__ float gelu_grad(float x) {
     // d/dx [x * Phi(x)] = Phi(x) + x * phi(x)
@@ -49,13 +52,74 @@ __device__ __forceinline__ void write_out8(TO* out, const float* s, int n_valid,
     }
 }
 
+// 8 elements as loaded (not yet widened): loads of several rows can be in flight while only
+// their raw registers are live
+template <typename T>
+struct Raw8;
+template <>
+struct Raw8<__nv_bfloat16> {
+    uint4 v;
+    __device__ __forceinline__ void load(const __nv_bfloat16* p) { v = *reinterpret_cast<const uint4*>(p); }
+    __device__ __forceinline__ void widen(float* f) const {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 t = unpack_bf16x2(w[i]);
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        }
+    }
+};
+template <>
+struct Raw8<float> {
+    float4 a, b;
+    __device__ __forceinline__ void load(const float* p) {
+        a = reinterpret_cast<const float4*>(p)[0];
+        b = reinterpret_cast<const float4*>(p)[1];
+    }
+    __device__ __forceinline__ void widen(float* f) const {
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    }
+};
+
+template <typename T, int MODE>
+__device__ __forceinline__ void colreduce_row(const T* __restrict__ x, const T* __restrict__ pre,
+                                              T* __restrict__ gout, const float* a, const float* p,
+                                              const float* gm, float* acc, int act, int64_t off) {
+    if constexpr (MODE == 0) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] += a[c];
+    } else {
+        float o[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            if (MODE == 1) {
+                acc[c] += a[c] * p[c];
+                o[c] = a[c] * gm[c];
+            } else {
+                o[c] = act == 1 ? a[c] * gelu_grad(p[c]) : (p[c] > 0.f ? a[c] : 0.f);
+            }
+        }
+        if (MODE == 2) {
+            // the bias gradient sums g_pre as stored (rounded to T), i.e. what the GEMMs consume
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[c] += to_f(from_f<T>(o[c]));
+        }
+        store8(gout + off, o);
+    }
+}
+
 // MODE 0: colsum(x) ; 1: gout = x * gamma, colsum(x * pre) ; 2: gout = x * act'(pre), colsum(gout)
+// Each row lane keeps col_unroll(MODE) rows' loads in flight (issued before any is consumed) and
+// four CTAs share an SM: a memory-bound pass needs tens of KB in flight per SM to cover DRAM
+// latency, which one 16-byte load per thread per iteration does not give.
 template <typename T, int MODE, typename TO>
-__global__ void __launch_bounds__(kColThreads) colreduce_kernel(const T* __restrict__ x, const T* __restrict__ pre,
-                                                                const T* __restrict__ gamma, T* __restrict__ gout,
-                                                                int64_t M, int N, int rows_per_cta, int act,
-                                                                float* acc_buf, unsigned* counters,
-                                                                TO* __restrict__ out, int accumulate) {
+__global__ void __launch_bounds__(kColThreads, kColCtasPerSm) colreduce_kernel(const T* __restrict__ x, const T* __restrict__ pre,
+                                                                   const T* __restrict__ gamma, T* __restrict__ gout,
+                                                                   int64_t M, int N, int rows_per_cta, int act,
+                                                                   float* acc_buf, unsigned* counters,
+                                                                   TO* __restrict__ out, int accumulate) {
     __shared__ float red[kColThreads * 8];
     __shared__ unsigned s_last;
     const int tid = threadIdx.x, cl = tid & 31, rl = tid >> 5;
@@ -64,32 +128,31 @@ __global__ void __launch_bounds__(kColThreads) colreduce_kernel(const T* __restr
     const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
     const int64_t r1 = r0 + rows_per_cta < M ? r0 + rows_per_cta : M;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    float gm[8];
+    float gm[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (MODE == 1 && cols_ok) load8(gamma + col, gm);
-    for (int64_t r = r0 + rl; cols_ok && r < r1; r += 8) {
-        float a[8];
-        load8(x + r * N + col, a);
-        if (MODE == 0) {
+    int64_t r = r0 + rl;
+    if (cols_ok) {
+        constexpr int U = col_unroll(MODE);
+        for (; r + 8 * (U - 1) < r1; r += 8 * U) {
+            Raw8<T> ra[U], rp[U];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) acc[c] += a[c];
-        } else {
-            float p[8], o[8];
-            load8(pre + r * N + col, p);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                if (MODE == 1) {
-                    acc[c] += a[c] * p[c];
-                    o[c] = a[c] * gm[c];
-                } else {
-                    o[c] = act == 1 ? a[c] * gelu_grad(p[c]) : (p[c] > 0.f ? a[c] : 0.f);
-                }
+            for (int u = 0; u < U; ++u) {
+                ra[u].load(x + (r + 8 * u) * N + col);
+                if (MODE != 0) rp[u].load(pre + (r + 8 * u) * N + col);
             }
-            if (MODE == 2) {
-                // the bias gradient sums g_pre as stored (rounded to T), i.e. what the GEMMs consume
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[c] += to_f(from_f<T>(o[c]));
+            for (int u = 0; u < U; ++u) {
+                float a[8], p[8];
+                ra[u].widen(a);
+                if (MODE != 0) rp[u].widen(p);
+                colreduce_row<T, MODE>(x, pre, gout, a, p, gm, acc, act, (r + 8 * u) * N + col);
             }
-            store8(gout + r * N + col, o);
+        }
+        for (; r < r1; r += 8) {
+            float a[8], p[8];
+            load8(x + r * N + col, a);
+            if (MODE != 0) load8(pre + r * N + col, p);
+            colreduce_row<T, MODE>(x, pre, gout, a, p, gm, acc, act, r * N + col);
         }
     }
     if (acc_buf == nullptr) return;   // act_bwd without a bias gradient
@@ -186,24 +249,24 @@ ReduceScratch reduce_scratch() {
     return {c, reinterpret_cast<float*>(c + kMaxCounters)};
 }
 
-int colsum_parts(int64_t M, int N) {
+static int colsum_parts(int64_t M, int N, int mode) {
     const int64_t slabs = (N + kSlabCols - 1) / kSlabCols;
-    int64_t want = static_cast<int64_t>(num_sms()) * 2 / slabs;
-    want = std::max<int64_t>(1, std::min<int64_t>(want, (M + 31) / 32));
+    int64_t want = static_cast<int64_t>(num_sms()) * kColCtasPerSm / slabs;
+    want = std::max<int64_t>(1, std::min<int64_t>(want, (M + 8 * col_unroll(mode) - 1) / (8 * col_unroll(mode))));
     return static_cast<int>(want);
 }
 
 static cudaError_t launch_colreduce(DType t, DType out_t, int mode, const void* x, const void* pre,
-                                    const void* gamma, void* gout, int64_t M, int N, int act, float* part,
-                                    void* out, bool accumulate, cudaStream_t st) {
+                                    const void* gamma, void* gout, int64_t M, int N, int act, void* out,
+                                    bool accumulate, cudaStream_t st) {
     if (N % 8 != 0) return cudaErrorInvalidValue;
     const int slabs = (N + kSlabCols - 1) / kSlabCols;
-    if (slabs > kMaxCounters || (part != nullptr && N > kReduceAccFloats)) return cudaErrorInvalidValue;
+    if (slabs > kMaxCounters || (out != nullptr && N > kReduceAccFloats)) return cudaErrorInvalidValue;
     const ReduceScratch rs = reduce_scratch();
     if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
     unsigned* counters = rs.counters;
-    float* acc_buf = part != nullptr ? rs.acc : nullptr;   // null: no column sum wanted
-    const int parts = colsum_parts(M, N);
+    float* acc_buf = out != nullptr ? rs.acc : nullptr;   // null: no column sum wanted
+    const int parts = colsum_parts(M, N, mode);
     const int rows_per_cta = static_cast<int>((M + parts - 1) / parts);
     const dim3 grid(parts, slabs);
     return MMLTK_DISPATCH_DT(t, [&] {
@@ -230,13 +293,14 @@ static cudaError_t launch_colreduce(DType t, DType out_t, int mode, const void* 
 }
 
 cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const void* pre, const void* gamma,
-                          void* gout, int64_t M, int N, float* part, void* out, cudaStream_t st, bool accumulate) {
-    return launch_colreduce(t, out_t, mode, x, pre, gamma, gout, M, N, 0, part, out, accumulate, st);
+                          void* gout, int64_t M, int N, void* out, cudaStream_t st, bool accumulate) {
+    if (out == nullptr) return cudaErrorInvalidValue;
+    return launch_colreduce(t, out_t, mode, x, pre, gamma, gout, M, N, 0, out, accumulate, st);
 }
 
 cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,
-                                int act, float* part, void* gb, bool accumulate, cudaStream_t st) {
-    return launch_colreduce(t, out_t, 2, gy, pre, nullptr, gx, M, N, act, part, gb, accumulate, st);
+                                int act, void* gb, bool accumulate, cudaStream_t st) {
+    return launch_colreduce(t, out_t, 2, gy, pre, nullptr, gx, M, N, act, gb, accumulate, st);
 }
 
 cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bool accumulate, cudaStream_t st) {

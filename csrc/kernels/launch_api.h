@@ -17,7 +17,6 @@ int num_sms();
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st);
 // One launch: gx, and gw / gb written (or added into, `accumulate`) by the last CTA.
-int layernorm_bwd_parts(int64_t rows);
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
                                  bool accumulate, cudaStream_t st);
@@ -51,10 +50,9 @@ cudaError_t launch_lsap(const float* cost, const int32_t* counts, int32_t* match
 cudaError_t launch_cast_f32(DType dst_t, const float* src, void* dst, int64_t n, cudaStream_t st);
 
 // mode 0: out (+)= colsum(x); mode 1: gout = x * gamma (row-broadcast) and out (+)= colsum(x * pre).
-// part: fp32 scratch [colsum_parts(M, N), N]; N % 8 == 0.  One launch (the last CTA of each column
+// N % 8 == 0.  One launch (the last CTA of each column
 // slab finishes the reduction); launches that share the per-device arrival counters must be
 // stream-ordered.  accumulate: add into `out` instead of overwriting it.
-int colsum_parts(int64_t M, int N);
 constexpr int kMaxCounters = 4096;
 constexpr int kReduceAccFloats = 16384;
 struct ReduceScratch {
@@ -63,11 +61,10 @@ struct ReduceScratch {
 };
 ReduceScratch reduce_scratch();
 cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const void* pre, const void* gamma,
-                          void* gout, int64_t M, int N, float* part, void* out, cudaStream_t st,
-                          bool accumulate = false);
-// gx = gy * act'(pre) and, when part/gb are given, gb (+)= colsum(gx) in the same pass.
+                          void* gout, int64_t M, int N, void* out, cudaStream_t st, bool accumulate = false);
+// gx = gy * act'(pre) and, when gb is given, gb (+)= colsum(gx) in the same pass.
 cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,
-                                int act, float* part, void* gb, bool accumulate, cudaStream_t st);
+                                int act, void* gb, bool accumulate, cudaStream_t st);
 cudaError_t launch_reduce_partials(DType out_t, const float* part, int nparts, int N, void* out, cudaStream_t st);
 // out (+)= acc; acc = 0 (acc: a column sum accumulated by atomics, e.g. in the GEMM epilogue)
 cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bool accumulate, cudaStream_t st);

@@ -4,8 +4,9 @@
 // registers, no E[x^2]-E[x]^2 cancellation).  Saves mean/rstd for backward.
 // Backward: dx per row; dgamma/dbeta accumulated per lane over the rows its
 // warp visits (each lane owns fixed columns), reduced across the CTA's warps
-// in shared memory into one fp32 partial per CTA, then summed by a second
-// kernel -- no atomics, deterministic.
+// in shared memory, added into per-device fp32 accumulators with vector
+// atomics; the last CTA to arrive writes (or accumulates into) dgamma/dbeta.
+// One launch; float atomics make the last bits run dependent.
 #include <algorithm>
 
 #include "common.cuh"
@@ -67,6 +68,64 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, co
     }
 }
 
+// 4 elements as loaded, widened only when used (keeps the next row's loads in few registers)
+template <typename T>
+struct Raw4;
+template <>
+struct Raw4<__nv_bfloat16> {
+    uint2 v;
+    __device__ __forceinline__ void load(const __nv_bfloat16* p) { v = *reinterpret_cast<const uint2*>(p); }
+    __device__ __forceinline__ float4 widen() const {
+        const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y);
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+};
+template <>
+struct Raw4<float> {
+    float4 v;
+    __device__ __forceinline__ void load(const float* p) { v = *reinterpret_cast<const float4*>(p); }
+    __device__ __forceinline__ float4 widen() const { return v; }
+};
+
+// one row of the backward pass: xv / gv hold this lane's x and gy columns (fp32)
+template <typename T, typename W, int kMaxVec>
+__device__ __forceinline__ void ln_bwd_row(float4 (&xh)[kMaxVec], float4 (&g)[kMaxVec], float mean, float rstd,
+                                           const W* __restrict__ w, float4 (&aw)[kMaxVec], float4 (&ab)[kMaxVec],
+                                           T* __restrict__ gxr, int lane, int nv, int C) {
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxVec; ++k) {
+        const int i = lane + 32 * k;
+        if (i < nv) {
+            const int c0 = 4 * i;
+            const float4 xv = xh[k], gv = g[k];
+            xh[k] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd,
+                                (xv.w - mean) * rstd);
+            aw[k].x += gv.x * xh[k].x; aw[k].y += gv.y * xh[k].y;
+            aw[k].z += gv.z * xh[k].z; aw[k].w += gv.w * xh[k].w;
+            ab[k].x += gv.x; ab[k].y += gv.y; ab[k].z += gv.z; ab[k].w += gv.w;
+            g[k] = make_float4(gv.x * to_f(w[c0]), gv.y * to_f(w[c0 + 1]), gv.z * to_f(w[c0 + 2]),
+                               gv.w * to_f(w[c0 + 3]));
+            s1 += g[k].x + g[k].y + g[k].z + g[k].w;
+            s2 += g[k].x * xh[k].x + g[k].y * xh[k].y + g[k].z * xh[k].z + g[k].w * xh[k].w;
+        }
+    }
+    s1 = warp_sum(s1) / C;
+    s2 = warp_sum(s2) / C;
+#pragma unroll
+    for (int k = 0; k < kMaxVec; ++k) {
+        const int i = lane + 32 * k;
+        if (i < nv) {
+            float4 o;
+            o.x = (g[k].x - s1 - xh[k].x * s2) * rstd;
+            o.y = (g[k].y - s1 - xh[k].y * s2) * rstd;
+            o.z = (g[k].z - s1 - xh[k].z * s2) * rstd;
+            o.w = (g[k].w - s1 - xh[k].w * s2) * rstd;
+            store4(gxr + 4 * i, o);
+        }
+    }
+}
+
 template <typename T, typename W, int kMaxVec>
 __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, const T* __restrict__ x,
                                                      const W* __restrict__ w, const float* __restrict__ mean_in,
@@ -87,41 +146,60 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
         aw[k] = make_float4(0, 0, 0, 0);
         ab[k] = make_float4(0, 0, 0, 0);
     }
-    for (int64_t r = warp; r < rows; r += nwarps) {
-        const float mean = mean_in[r], rstd = rstd_in[r];
-        float4 xh[kMaxVec], g[kMaxVec];
-        float s1 = 0.f, s2 = 0.f;
+    if constexpr (kMaxVec <= 6) {
+        // the next row's x / gy / statistics are loaded while the current row is reduced and
+        // written, so each warp keeps two rows of loads in flight
+        Raw4<T> nx[kMaxVec], ng[kMaxVec];
+        float nmean = 0.f, nrstd = 0.f;
+        int64_t r = warp;
+        if (r < rows) {
+            nmean = mean_in[r];
+            nrstd = rstd_in[r];
 #pragma unroll
-        for (int k = 0; k < kMaxVec; ++k) {
-            const int i = lane + 32 * k;
-            if (i < nv) {
-                const int c0 = 4 * i;
-                float4 xv = load4(x + r * C + c0);
-                float4 gv = load4(gy + r * C + c0);
-                xh[k] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd,
-                                    (xv.w - mean) * rstd);
-                aw[k].x += gv.x * xh[k].x; aw[k].y += gv.y * xh[k].y;
-                aw[k].z += gv.z * xh[k].z; aw[k].w += gv.w * xh[k].w;
-                ab[k].x += gv.x; ab[k].y += gv.y; ab[k].z += gv.z; ab[k].w += gv.w;
-                g[k] = make_float4(gv.x * to_f(w[c0]), gv.y * to_f(w[c0 + 1]), gv.z * to_f(w[c0 + 2]),
-                                   gv.w * to_f(w[c0 + 3]));
-                s1 += g[k].x + g[k].y + g[k].z + g[k].w;
-                s2 += g[k].x * xh[k].x + g[k].y * xh[k].y + g[k].z * xh[k].z + g[k].w * xh[k].w;
+            for (int k = 0; k < kMaxVec; ++k) {
+                const int i = lane + 32 * k;
+                if (i < nv) {
+                    nx[k].load(x + r * C + 4 * i);
+                    ng[k].load(gy + r * C + 4 * i);
+                }
             }
         }
-        s1 = warp_sum(s1) / C;
-        s2 = warp_sum(s2) / C;
+        for (; r < rows; r += nwarps) {
+            const float mean = nmean, rstd = nrstd;
+            float4 xv[kMaxVec], gv[kMaxVec];
 #pragma unroll
-        for (int k = 0; k < kMaxVec; ++k) {
-            const int i = lane + 32 * k;
-            if (i < nv) {
-                float4 o;
-                o.x = (g[k].x - s1 - xh[k].x * s2) * rstd;
-                o.y = (g[k].y - s1 - xh[k].y * s2) * rstd;
-                o.z = (g[k].z - s1 - xh[k].z * s2) * rstd;
-                o.w = (g[k].w - s1 - xh[k].w * s2) * rstd;
-                store4(gx + r * C + 4 * i, o);
+            for (int k = 0; k < kMaxVec; ++k) {
+                xv[k] = nx[k].widen();
+                gv[k] = ng[k].widen();
             }
+            const int64_t rn = r + nwarps;
+            if (rn < rows) {
+                nmean = mean_in[rn];
+                nrstd = rstd_in[rn];
+#pragma unroll
+                for (int k = 0; k < kMaxVec; ++k) {
+                    const int i = lane + 32 * k;
+                    if (i < nv) {
+                        nx[k].load(x + rn * C + 4 * i);
+                        ng[k].load(gy + rn * C + 4 * i);
+                    }
+                }
+            }
+            ln_bwd_row<T, W, kMaxVec>(xv, gv, mean, rstd, w, aw, ab, gx + r * C, lane, nv, C);
+        }
+    } else {
+        // wide rows have no registers to spare for a second row
+        for (int64_t r = warp; r < rows; r += nwarps) {
+            float4 xv[kMaxVec], gv[kMaxVec];
+#pragma unroll
+            for (int k = 0; k < kMaxVec; ++k) {
+                const int i = lane + 32 * k;
+                if (i < nv) {
+                    xv[k] = load4(x + r * C + 4 * i);
+                    gv[k] = load4(gy + r * C + 4 * i);
+                }
+            }
+            ln_bwd_row<T, W, kMaxVec>(xv, gv, mean_in[r], rstd_in[r], w, aw, ab, gx + r * C, lane, nv, C);
         }
     }
     // CTA reduction of the per-lane column partials
@@ -136,16 +214,18 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
         }
     }
     __syncthreads();
-    // CTA partials go to the fp32 accumulators (atomics resolve in L2); the last CTA to
-    // arrive writes (or adds into) gw / gb and clears the scratch for the next launch
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float a = 0.f, bb = 0.f;
+    // CTA partials go to the fp32 accumulators with 16-byte atomics (resolved in L2); the last
+    // CTA to arrive writes (or adds into) gw / gb and clears the scratch for the next launch
+    for (int c4 = threadIdx.x; c4 < nv; c4 += blockDim.x) {
+        float4 a = make_float4(0, 0, 0, 0), bb = make_float4(0, 0, 0, 0);
         for (int q = 0; q < nwib; ++q) {
-            a += smem[q * 2 * C + c];
-            bb += smem[q * 2 * C + C + c];
+            const float4 pa = *reinterpret_cast<const float4*>(smem + q * 2 * C + 4 * c4);
+            const float4 pb = *reinterpret_cast<const float4*>(smem + q * 2 * C + C + 4 * c4);
+            a.x += pa.x; a.y += pa.y; a.z += pa.z; a.w += pa.w;
+            bb.x += pb.x; bb.y += pb.y; bb.z += pb.z; bb.w += pb.w;
         }
-        atomicAdd(acc_w + c, a);
-        atomicAdd(acc_b + c, bb);
+        atomicAdd(reinterpret_cast<float4*>(acc_w + 4 * c4), a);
+        atomicAdd(reinterpret_cast<float4*>(acc_b + 4 * c4), bb);
     }
     __shared__ unsigned s_last;
     __threadfence();
@@ -214,11 +294,18 @@ cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* 
     });
 }
 
-int layernorm_bwd_parts(int64_t rows) {
-    const int nwib = 8;
-    int64_t blocks = std::min<int64_t>((rows + nwib - 1) / nwib, static_cast<int64_t>(num_sms()) * 2);
-    return static_cast<int>(std::max<int64_t>(blocks, 1));
+namespace {
+// one resident wave: as many CTAs as fit on every SM (registers / shared memory of this
+// instantiation), each warp then strides over rows
+template <typename K>
+int ln_bwd_blocks(K kern, int threads, size_t smem, int64_t rows) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    const int64_t want = static_cast<int64_t>(num_sms()) * per_sm;
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, (rows + threads / 32 - 1) / (threads / 32))));
 }
+}  // namespace
 
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
@@ -228,7 +315,6 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
     if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
     const int threads = 256;
     const int nwib = threads / 32;
-    const int blocks = layernorm_bwd_parts(rows);
     const size_t smem = static_cast<size_t>(nwib) * 2 * C * sizeof(float);
     return MMLTK_DISPATCH_DT(xt, [&] {
         using T = scalar_t;
@@ -241,6 +327,7 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
                 if (smem >= 40 * 1024)
                     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
                 if (e != cudaSuccess) return;
+                const int blocks = ln_bwd_blocks(kern, threads, smem, rows);
                 kern<<<blocks, threads, smem, st>>>(static_cast<const T*>(gy), static_cast<const T*>(x),
                                                     static_cast<const Wt*>(w), mean, rstd, static_cast<T*>(gx), rs.acc,
                                                     rs.acc + C, rs.counters, static_cast<Wt*>(gw),

@@ -60,9 +60,8 @@ torch::Tensor colsum(torch::Tensor x, c10::optional<at::ScalarType> out_dtype, c
     auto ot = out_dtype.has_value() ? *out_dtype : xc.scalar_type();
     const bool acc = out && out->defined();
     auto o = reduce_target(out, N, xc.options().dtype(ot));
-    auto part = torch::empty({colsum_parts(M, N), N}, xc.options().dtype(torch::kFloat32));
     check_cuda(launch_colsum(dtype_of(xc), dtype_of(o), 0, xc.data_ptr(), nullptr, nullptr, nullptr, M, N,
-                             part.data_ptr<float>(), o.data_ptr(), cur_stream(), acc),
+                             o.data_ptr(), cur_stream(), acc),
                "colsum");
     return o;
 }
@@ -79,9 +78,8 @@ std::vector<torch::Tensor> scale_bwd(torch::Tensor gy, torch::Tensor pre, torch:
     auto gpre = torch::empty_like(g);
     const bool acc = gamma_grad && gamma_grad->defined();
     auto ggamma = reduce_target(gamma_grad, N, gamma.options());
-    auto part = torch::empty({colsum_parts(M, N), N}, g.options().dtype(torch::kFloat32));
     check_cuda(launch_colsum(dtype_of(g), dtype_of(ggamma), 1, g.data_ptr(), p.data_ptr(), gm.data_ptr(),
-                             gpre.data_ptr(), M, N, part.data_ptr<float>(), ggamma.data_ptr(), cur_stream(), acc),
+                             gpre.data_ptr(), M, N, ggamma.data_ptr(), cur_stream(), acc),
                "scale_bwd");
     return {gpre, ggamma};
 }
@@ -98,9 +96,8 @@ std::vector<torch::Tensor> act_bwd_bias(torch::Tensor gy, torch::Tensor pre, int
     auto gpre = torch::empty_like(g);
     const bool acc = bias_grad && bias_grad->defined();
     auto gb = reduce_target(bias_grad, N, g.options().dtype(dt.has_value() ? *dt : g.scalar_type()));
-    auto part = torch::empty({colsum_parts(M, N), N}, g.options().dtype(torch::kFloat32));
     check_cuda(launch_act_bwd_bias(dtype_of(g), dtype_of(gb), g.data_ptr(), p.data_ptr(), gpre.data_ptr(), M, N,
-                                   static_cast<int>(act), part.data_ptr<float>(), gb.data_ptr(), acc, cur_stream()),
+                                   static_cast<int>(act), gb.data_ptr(), acc, cur_stream()),
                "act_bwd_bias");
     return {gpre, gb};
 }

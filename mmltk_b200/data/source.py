@@ -50,7 +50,7 @@ def write_synthetic_source(root: str, splits=("train", "val"), images: int = 8, 
                     m = torch.zeros(h, w, dtype=torch.bool)
                     m[y1:y2, x1:x2] = True
                     rec["mask_rle"] = _rle(m)
-                img[y1:y2, x1:x2] = torch.tensor([40 * c, 255 - 40 * c, 128], dtype=torch.uint8)
+                img[y1:y2, x1:x2] = torch.tensor([(40 * c) % 256, 255 - (40 * c) % 256, 128], dtype=torch.uint8)
                 lines.append(json.dumps(rec))
             with open(os.path.join(d, f"{k:06d}.png"), "wb") as f:
                 f.write(native().encode_png(img))

@@ -34,7 +34,7 @@ from ..ops._ext import kernels
 from .flat import FlatParams
 from .param_groups import build_param_groups
 
-__all__ = ["TrainEngine", "StepResult"]
+__all__ = ["TrainEngine", "StepResult", "PendingStep"]
 
 
 class StepResult:
@@ -42,6 +42,25 @@ class StepResult:
 
     def __init__(self, loss, losses, grad_norm, nonfinite):
         self.loss, self.losses, self.grad_norm, self.nonfinite = loss, losses, grad_norm, nonfinite
+
+
+class PendingStep:
+    """Handle of a step queued by ``TrainEngine.step_async``."""
+    __slots__ = ("engine", "rb", "event", "partial", "step", "_done")
+
+    def __init__(self, engine, rb, event, partial: StepResult):
+        self.engine, self.rb, self.event, self.partial = engine, rb, event, partial
+        self.step = engine.step_count
+        self._done = partial if rb is None else None
+
+    def ready(self) -> bool:
+        return self._done is not None or self.event.query()
+
+    def result(self) -> StepResult:
+        if self._done is None:
+            self.event.synchronize()
+            self._done = self.engine._read_result(self.rb, self.partial.losses, self.step)
+        return self._done
 
 
 class TrainEngine:
@@ -126,7 +145,7 @@ class TrainEngine:
                                 self.flat.group_of, self.groups, self.opts.momentum)
             self.m = self.v = None
             self.ema_buf = master.clone() if self.opts.use_ema else None
-            self.readback = torch.zeros(4, dtype=torch.float32).pin_memory()
+            self._alloc_readback()
             if self.grad_sync is not None:
                 self.grad_sync.muon_mode = True
             return
@@ -137,7 +156,14 @@ class TrainEngine:
             self.v = torch.zeros_like(master)
             self.ema_buf = master.clone() if self.opts.use_ema else None
             self.scratch = torch.zeros(k.optim_num_partials(), dtype=torch.float32, device=self.device)
-        self.readback = torch.zeros(4, dtype=torch.float32).pin_memory()
+        self._alloc_readback()
+
+    def _alloc_readback(self) -> None:
+        # a ring of pinned readback slots: a deferred step's values stay readable while up to
+        # three more steps are queued behind it
+        self._readbacks = [torch.zeros(4, dtype=torch.float32).pin_memory() for _ in range(4)]
+        self._rb_turn = 0
+        self.readback = self._readbacks[0]
 
     # ------------------------------------------------------------------ scalars
     def _host_scalars(self, step: int):
@@ -258,27 +284,49 @@ class TrainEngine:
             self._graph_warmup += 1
         return self._finish(total, losses, sync)
 
+    def step_async(self, images: Optional[torch.Tensor] = None, targets: Optional[Targets] = None) -> "PendingStep":
+        """Queue one optimizer step and its loss/flag readback without waiting; ``.result()`` on the
+        returned handle waits for that step only.  The host can prepare the next batch meanwhile.
+        (The reference trainer reads its loss synchronously every step: rfdetr/src/engine.cpp.)"""
+        if not self.cuda:
+            return PendingStep(self, None, None, self.step(images, targets))
+        r = self.step(images, targets, sync=False)
+        if self.accum > 1 and self._micro != 0:
+            return PendingStep(self, None, None, r)        # a micro-batch: nothing to read yet
+        rb = self._queue_readback(r.loss)
+        ev = torch.cuda.Event()
+        ev.record()
+        return PendingStep(self, rb, ev, StepResult(None, r.losses, None, None))
+
+    def _queue_readback(self, total) -> torch.Tensor:
+        rb = self._readbacks[self._rb_turn]
+        self._rb_turn = (self._rb_turn + 1) % len(self._readbacks)
+        rb[0:1].copy_(total.reshape(1), non_blocking=True)
+        rb[1:3].copy_(self.flags.view(torch.float32), non_blocking=True)
+        sync_status = getattr(self.grad_sync, "status_tensor", None)
+        if sync_status is not None:
+            rb[3:4].copy_(sync_status().view(torch.float32), non_blocking=True)
+        return rb
+
+    def _read_result(self, rb: torch.Tensor, losses, step: int) -> StepResult:
+        if getattr(self.grad_sync, "status_tensor", None) is not None:
+            self.grad_sync.check(self.flags_host_bits(rb[3]))
+        loss = float(rb[0])
+        nonfinite = int(self.flags_host_bits(rb[1]))
+        norm = float(rb[2])
+        if nonfinite or not math.isfinite(loss):
+            raise FloatingPointError(f"non-finite RF-DETR loss ({loss}) or gradients (norm {norm}) at step {step}")
+        return StepResult(loss, losses, norm, nonfinite)
+
     def _finish(self, total, losses, sync: bool) -> StepResult:
         self.step_count += 1
         if self.grad_sync is not None:
             self.grad_sync.after_step(self)
         if not sync:
             return StepResult(total, losses, None, None)
-        self.readback[0].copy_(total, non_blocking=True)
-        self.readback[1:3].copy_(self.flags.view(torch.float32), non_blocking=True)
-        sync_status = getattr(self.grad_sync, "status_tensor", None)
-        if sync_status is not None:
-            self.readback[3:4].copy_(sync_status().view(torch.float32), non_blocking=True)
+        rb = self._queue_readback(total)
         torch.cuda.current_stream().synchronize()
-        if sync_status is not None:
-            self.grad_sync.check(self.flags_host_bits(self.readback[3]))
-        loss = float(self.readback[0])
-        nonfinite = int(self.flags_host_bits(self.readback[1]))
-        norm = float(self.readback[2])
-        if nonfinite or not math.isfinite(loss):
-            raise FloatingPointError(f"non-finite RF-DETR loss ({loss}) or gradients (norm {norm}) at step "
-                                     f"{self.step_count}")
-        return StepResult(loss, losses, norm, nonfinite)
+        return self._read_result(rb, losses, self.step_count)
 
     @staticmethod
     def flags_host_bits(x: torch.Tensor) -> int:

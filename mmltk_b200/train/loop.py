@@ -309,13 +309,11 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
     for epoch in range(start_epoch, opts.epochs):
         loader.set_epoch(epoch)
         loss_sum, n_loss, t_epoch = 0.0, 0, time.monotonic()
-        for b, (images, _plain, idx) in enumerate(loader):
-            if b >= steps_per_epoch * opts.grad_accum_steps:
-                break
-            st = augmenter.prepare(idx, loader.dataset.reader, epoch, seq)
-            seq += 1
-            x, targets = augmenter.apply(images, st)
-            r = engine.step(x, targets)
+
+        def consume(b, pending):
+            # read step b's loss once it has finished; the next batch was queued meanwhile
+            nonlocal loss_sum, n_loss
+            r = pending.result()
             if r.grad_norm is not None or not ctx.device.type == "cuda":
                 loss_sum += float(r.loss)
                 n_loss += 1
@@ -332,6 +330,20 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
                                  "step_loss": float(r.loss), "batches_per_second": (b + 1) / max(el, 1e-9),
                                  "images_per_second": (b + 1) * opts.batch_size * ctx.world_size / max(el, 1e-9),
                                  "elapsed_seconds": time.monotonic() - t_start})
+
+        prev = None
+        for b, (images, _plain, idx) in enumerate(loader):
+            if b >= steps_per_epoch * opts.grad_accum_steps:
+                break
+            st = augmenter.prepare(idx, loader.dataset.reader, epoch, seq)
+            seq += 1
+            x, targets = augmenter.apply(images, st)
+            pending = engine.step_async(x, targets)
+            if prev is not None:
+                consume(*prev)
+            prev = (b, pending)
+        if prev is not None:
+            consume(*prev)
         train_loss = loss_sum / max(1, n_loss)
         # validation: regular weights, then EMA
         if progress is not None:

@@ -16,6 +16,40 @@ import sys
 import torch
 
 
+def _origin(ev) -> str:
+    """Nearest enclosing autograd node (backward) or autograd Function / module-level op (forward)."""
+    p = ev.cpu_parent
+    while p is not None:
+        n = p.name
+        if n.startswith("autograd::engine::evaluate_function: "):
+            return n.split(": ", 1)[1]
+        if not n.startswith("aten::") and not n.startswith("cuda") and not n.startswith("ProfilerStep"):
+            return n
+        p = p.cpu_parent
+    return "-"
+
+
+def origin_table(events, steps: int, top: int) -> str:
+    """CUDA time of each aten op's own kernels, keyed by (op, origin)."""
+    per = collections.Counter()
+    count = collections.Counter()
+    for ev in events:
+        if ev.device_type != torch.autograd.DeviceType.CPU or not ev.name.startswith("aten::"):
+            continue
+        t = sum(k.device_time for k in ev.kernels)
+        if not ev.kernels:
+            continue
+        key = (ev.name, _origin(ev))
+        per[key] += t
+        count[key] += len(ev.kernels)
+    total = sum(per.values()) or 1.0
+    lines = ["| share | ms/step | kernels/step | aten op | origin |", "|---|---|---|---|---|"]
+    for (name, org), t in per.most_common(top):
+        lines.append(f"| {100 * t / total:.1f}% | {t / 1e3 / steps:.3f} | {count[(name, org)] // steps} | "
+                     f"`{name}` | `{org[:80]}` |")
+    return "\n".join(lines)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--preset", default="rf-detr-medium")
@@ -25,6 +59,8 @@ def main(argv=None) -> int:
     ap.add_argument("--top", type=int, default=30)
     ap.add_argument("--by-op", action="store_true", help="rank aten ops (with input shapes) instead of kernels")
     ap.add_argument("--no-shapes", action="store_true", help="with --by-op: group by op name only")
+    ap.add_argument("--by-origin", action="store_true",
+                    help="rank (aten op, enclosing autograd node or autograd Function) pairs by CUDA time")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         print("profile: needs a GPU", file=sys.stderr)
@@ -46,6 +82,13 @@ def main(argv=None) -> int:
         eng.step(images, targets)
     torch.cuda.synchronize()
     from torch.profiler import ProfilerActivity, profile
+    if a.by_origin:
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+            for _ in range(a.steps):
+                eng.step()
+            torch.cuda.synchronize()
+        print(origin_table(prof.events(), a.steps, a.top))
+        return 0
     if a.by_op:
         # aten ops with input shapes, ranked by the CUDA time of the kernels they launched
         with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:

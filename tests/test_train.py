@@ -124,6 +124,43 @@ def test_cuda_engine_eager_and_graph(cuda_device):
     eng.release_graph()
 
 
+def test_step_async_cpu_returns_the_step_result():
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-tiny-test", resolution=64)
+    eng = TrainEngine(RFDETR(cfg), TrainOptions(lr=1e-3), "cpu", max_targets=5)
+    imgs, tg = synthetic_batch(2, 64, seed=0, kmax=5, slots=5)
+    p = eng.step_async(imgs, tg)
+    assert p.ready()
+    r = p.result()
+    assert math.isfinite(r.loss) and r.grad_norm is not None
+
+
+@pytest.mark.gpu
+def test_cuda_step_async_matches_step(cuda_device):
+    """Deferred readback: the same losses as synchronous steps, read one step late."""
+    cfg = config_from_preset("rf-detr-medium", group_detr=2, dec_layers=2, resolution=256,
+                             positional_encoding_size=16)
+    imgs, tg = synthetic_batch(2, 256, seed=3, kmax=8, slots=8, dtype=torch.bfloat16)
+    imgs, tg = imgs.to(cuda_device), tg.to(cuda_device)
+    runs = []
+    for mode in ("sync", "async"):
+        torch.manual_seed(0)
+        eng = TrainEngine(RFDETR(cfg), TrainOptions(cuda_graph=True), cuda_device, max_targets=8)
+        eng.bind_static_inputs(2, 3, 256, 256)
+        if mode == "sync":
+            runs.append([eng.step(imgs, tg).loss for _ in range(6)])
+        else:
+            pend = [eng.step_async(imgs, tg) for _ in range(3)]
+            out = [p.result().loss for p in pend]
+            for _ in range(3):
+                q = eng.step_async(imgs, tg)
+                out.append(q.result().loss)
+            runs.append(out)
+        eng.release_graph()
+    for a, b in zip(*runs):
+        assert abs(a - b) <= 2e-2 * max(1.0, abs(a)), runs
+
+
 @pytest.mark.gpu
 def test_cuda_losses_match_cpu_oracle(cuda_device):
     """Same weights and batch: CUDA bf16 forward + losses vs the CPU fp32 oracle."""
