@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--ddp", default=os.environ.get("MMLTK_DDP", "fused"), choices=["fused", "nccl"])
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-infer", action="store_true", help="skip the batch-1 inference latency")
     ap.add_argument("--profile-launches", action="store_true", default=True)
     return ap.parse_args()
 
@@ -239,6 +240,18 @@ def main():
     if args.profile_launches:
         launches = count_launches(engine, dev_batches[0], args.steps)
 
+    # second half of the metric: batch-1 inference latency (same architecture, eval mode, CUDA-graph
+    # Predictor, pinned uint8 input -> preprocess -> model -> top-k post-process -> D2H), rank 0 only
+    infer = None
+    if rank == 0 and not args.no_infer:
+        from mmltk_b200.infer import Predictor
+        torch.manual_seed(0)
+        pred = Predictor(RFDETR(cfg).eval(), device=dev)
+        infer = {"model": args.preset, "batch": 1, "resolution": cfg.resolution, "dtype": "bf16",
+                 **{k: (round(v, 4) if isinstance(v, float) else v) for k, v in pred.latency(200, 20, 1).items()}}
+        pred.release()
+        del pred
+
     if world > 1:
         barrier()
     if rank == 0:
@@ -262,6 +275,7 @@ def main():
                     "ms_per_step": round(ms_e2e / args.steps, 3)},
             "wall_s": {"value_region": round(wall_dev, 3), "e2e_region": round(wall_e2e, 3)},
             "gpu_launches": launches,
+            "infer_b1": infer,
             "clocks": clocks,
             "final_loss": losses[-1] if losses else None,
         }

@@ -224,8 +224,10 @@ void register_data_api(pybind11::module& m) {
         });
     py::class_<Loader>(m, "DatasetLoader")
         .def(py::init([](const std::string& path, int batch, bool shuffle, uint64_t seed, int rank, int count,
-                         bool drop_last, int workers, int format, std::vector<int64_t> slot_ptrs, size_t slot_bytes) {
+                         bool drop_last, int workers, int format, std::vector<int64_t> slot_ptrs, size_t slot_bytes,
+                         std::vector<int> cpus) {
                  Loader::Config c;
+                 c.cpus = std::move(cpus);
                  c.path = path;
                  c.batch = batch;
                  c.shuffle = shuffle;
@@ -238,7 +240,10 @@ void register_data_api(pybind11::module& m) {
                  std::vector<void*> slots;
                  for (auto p : slot_ptrs) slots.push_back(reinterpret_cast<void*>(p));
                  return std::make_unique<Loader>(c, slots, slot_bytes);
-             }))
+             }),
+             py::arg("path"), py::arg("batch"), py::arg("shuffle"), py::arg("seed"), py::arg("rank"), py::arg("count"),
+             py::arg("drop_last"), py::arg("workers"), py::arg("format"), py::arg("slot_ptrs"), py::arg("slot_bytes"),
+             py::arg("cpus") = std::vector<int>{})
         .def("begin_epoch", &Loader::begin_epoch)
         .def("num_batches", &Loader::num_batches)
         .def("next", [](Loader& l) -> py::object {

@@ -12,6 +12,7 @@
 #include <stdexcept>
 
 #include "image_io.h"
+#include "exec_policy.h"
 #include "worker_pool.h"
 
 namespace mmltk::data {
@@ -312,6 +313,7 @@ void Loader::fill(int slot, const std::vector<uint32_t>& idx) {
 }
 
 void Loader::producer() {
+    if (!cfg_.cpus.empty()) set_thread_affinity(cfg_.cpus);
     while (true) {
         int slot = -1;
         std::vector<uint32_t> idx;

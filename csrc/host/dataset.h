@@ -91,6 +91,7 @@ class Loader {
         bool drop_last = false;
         int workers = 4;
         int format = 0;  // 0 fp32, 1 bf16, 2 uint8
+        std::vector<int> cpus;   // CPUs of the producer thread (empty: not pinned)
     };
     Loader(const Config& cfg, std::vector<void*> slots, size_t slot_bytes);
     ~Loader();

@@ -71,7 +71,14 @@ WorkerPool::~WorkerPool() {
 
 void WorkerPool::loop(int index) {
     t_in_worker = true;
-    if (!cpus_.empty()) pin_current_thread(cpus_[static_cast<size_t>(index) % cpus_.size()]);
+    uint64_t pinned = 0;   // generation of cpus_ this thread is pinned to (0: never pinned)
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        if (!cpus_.empty()) {
+            pin_current_thread(cpus_[static_cast<size_t>(index) % cpus_.size()]);
+            pinned = pin_gen_;
+        }
+    }
     while (true) {
         std::packaged_task<void()> task;
         {
@@ -80,9 +87,19 @@ void WorkerPool::loop(int index) {
             if (stop_ && tasks_.empty()) return;
             task = std::move(tasks_.front());
             tasks_.pop();
+            if (pinned != pin_gen_ && !cpus_.empty()) {
+                pin_current_thread(cpus_[static_cast<size_t>(index) % cpus_.size()]);
+                pinned = pin_gen_;
+            }
         }
         task();
     }
+}
+
+void WorkerPool::set_affinity(std::vector<int> cpus) {
+    std::lock_guard<std::mutex> lk(mu_);
+    cpus_ = std::move(cpus);
+    ++pin_gen_;
 }
 
 std::future<void> WorkerPool::enqueue(std::function<void()> fn) {
@@ -114,9 +131,26 @@ void WorkerPool::parallel_for(int64_t n, const std::function<void(int64_t)>& fn)
     for (auto& f : futs) f.get();
 }
 
+namespace {
+std::mutex g_pool_mu;
+WorkerPool* g_pool = nullptr;   // created once, never destroyed (lives until process exit)
+}  // namespace
+
 WorkerPool& WorkerPool::global() {
-    static WorkerPool pool(std::max(1u, std::min(16u, std::thread::hardware_concurrency())));
-    return pool;
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if (g_pool == nullptr) g_pool = new WorkerPool(std::max(1u, std::min(16u, std::thread::hardware_concurrency())));
+    return *g_pool;
+}
+
+int WorkerPool::configure_global(int threads, std::vector<int> cpus) {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if (g_pool == nullptr) {
+        const int n = threads > 0 ? threads : static_cast<int>(std::max(1u, std::min(16u, std::thread::hardware_concurrency())));
+        g_pool = new WorkerPool(n, std::move(cpus));
+    } else if (!cpus.empty()) {
+        g_pool->set_affinity(std::move(cpus));
+    }
+    return g_pool->size();
 }
 
 }  // namespace mmltk

@@ -34,12 +34,20 @@ class WorkerPool {
     // worker it runs inline.
     void parallel_for(int64_t n, const std::function<void(int64_t)>& fn);
 
+    // Re-pins the workers (each before its next task): worker i -> cpus[i % size].
+    void set_affinity(std::vector<int> cpus);
+
+    // The process-wide pool (the loader's gather threads, the batch LSAP, the evaluator).
     static WorkerPool& global();
+    // Size and CPUs of the global pool: the size applies only if the pool does not exist
+    // yet, the CPUs always.  Returns the pool's size.
+    static int configure_global(int threads, std::vector<int> cpus);
 
    private:
     void loop(int index);
     std::vector<std::thread> workers_;
     std::vector<int> cpus_;
+    uint64_t pin_gen_ = 0;
     std::queue<std::packaged_task<void()>> tasks_;
     std::mutex mu_;
     std::condition_variable cv_;

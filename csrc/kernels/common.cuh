@@ -29,6 +29,33 @@ __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return
 template <>
 __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
 
+// Standard normal CDF Phi(x) and density phi(x), for GELU(erf) forward and backward.
+// Phi comes from erf(|x|/sqrt 2) by Abramowitz & Stegun, Handbook of Mathematical
+// Functions, formula 7.1.26 (|erf error| <= 1.5e-7): 1 - t(a1 + t(a2 + ...)) exp(-z^2) with
+// t = 1/(1 + p z).  exp(-z^2) = exp(-x^2/2) is the exponential phi needs anyway, so one
+// exponential and one reciprocal replace the erf evaluation.
+struct NormalCdfPdf {
+    float cdf, pdf;
+};
+__device__ __forceinline__ NormalCdfPdf normal_cdf_pdf(float x) {
+    const float e = __expf(-0.5f * x * x);
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = __fdividef(1.f, fmaf(0.3275911f, z, 1.f));   // approximate reciprocal; 1 <= divisor
+    const float poly =
+        t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
+    const float half_erf = 0.5f - 0.5f * poly * e;   // erf(z) / 2, z >= 0
+    NormalCdfPdf r;
+    r.cdf = 0.5f + copysignf(half_erf, x);
+    r.pdf = 0.39894228040143268f * e;
+    return r;
+}
+// GELU(x) = x Phi(x);  GELU'(x) = Phi(x) + x phi(x)
+__device__ __forceinline__ float gelu_fwd(float x) { return x * normal_cdf_pdf(x).cdf; }
+__device__ __forceinline__ float gelu_bwd(float x) {
+    const NormalCdfPdf n = normal_cdf_pdf(x);
+    return fmaf(x, n.pdf, n.cdf);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -24,15 +24,10 @@ namespace {
 constexpr int kColThreads = 256;
 constexpr int kSlabCols = 256;     // columns per slab = 32 lanes x 8
 constexpr int kColCtasPerSm = 4;   // resident CTAs per SM (64 registers per thread)
-// rows per row lane with loads in flight together (the GELU derivative needs the registers of two)
+// rows per row lane with loads in flight together (with the GELU derivative, two fit in 64 registers)
 __host__ __device__ constexpr int col_unroll(int mode) { return mode == 2 ? 2 : 4; }
 
-__device__ __forceinline__ float gelu_grad(float x) {
-    // d/dx [x * Phi(x)] = Phi(x) + x * phi(x)
-    const float cdf = 0.5f * (1.f + erff(x * 0.70710678118654752f));
-    const float pdf = 0.39894228040143268f * __expf(-0.5f * x * x);
-    return cdf + x * pdf;
-}
+__device__ __forceinline__ float gelu_grad(float x) { return gelu_bwd(x); }
 
 __device__ __forceinline__ void ldcg8(const float* p, float* f) {
     const float4 a = __ldcg(reinterpret_cast<const float4*>(p));

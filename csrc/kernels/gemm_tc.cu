@@ -153,11 +153,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
-__device__ __forceinline__ float gelu_f(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
-// d/dx [x * Phi(x)] = Phi(x) + x * phi(x)
-__device__ __forceinline__ float gelu_grad_f(float x) {
-    return 0.5f * (1.f + erff(x * 0.70710678118654752f)) + x * 0.39894228040143268f * __expf(-0.5f * x * x);
-}
+__device__ __forceinline__ float gelu_f(float x) { return gelu_fwd(x); }
+__device__ __forceinline__ float gelu_grad_f(float x) { return gelu_bwd(x); }
 
 // 32 consecutive accumulator columns of this thread's row: two loads, one wait.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {

@@ -115,7 +115,9 @@ def _add_train(p):
     g.add_argument("--device-ids", default="")
     g.add_argument("--workers", type=int, default=0)
     g.add_argument("--lanes", type=int, default=0)
-    g.add_argument("--cpu-affinity", default="")
+    g.add_argument("--cpu-affinity", default="", help="CPU list for this run, e.g. 0-15,32-47 (ranks get shards)")
+    _bool_flag(g, "high-priority", "high_priority", None,
+               "lowest permitted nice value and realtime I/O priority (best effort)")
     g.add_argument("--prefetch-factor", type=int, default=None)
     g.add_argument("--print-freq", type=int, default=None)
     g.add_argument("--seed", type=int, default=None)
@@ -215,7 +217,7 @@ _SIMPLE = {"batch_size": "batch_size", "val_batch_size": "val_batch_size", "epoc
            "fused_optimizer": "fused_optimizer", "use_ema": "use_ema", "validation_loss": "validation_loss",
            "validation_profile": "validation_profile", "prefetch_factor": "prefetch_factor",
            "print_freq": "print_freq", "seed": "seed", "amp": "amp", "compile_mode": "compile_mode",
-           "ddp_backend": "ddp_backend"}
+           "ddp_backend": "ddp_backend", "high_priority": "high_priority"}
 
 
 def train_options_from_args(a) -> "TrainOptions":
@@ -374,7 +376,7 @@ def _train(a) -> int:
     from ..train.loop import run_training
     o = train_options_from_args(a)
     if len(o.device_ids) > 1 and not o.dist_worker:
-        return launch_workers(a.raw_argv, o.device_ids, workers=o.workers)
+        return launch_workers(a.raw_argv, o.device_ids, workers=o.workers, cpu_affinity=o.cpu_affinity)
     if len(o.device_ids) == 1:
         o.device_id = o.device_ids[0]
     res = run_training(o)

@@ -96,6 +96,7 @@ class TrainOptions:
     workers: int = 0
     lanes: int = 0
     cpu_affinity: str = ""
+    high_priority: bool = False   # lowest permitted nice value and realtime I/O priority for this process
     prefetch_factor: int = 2
     print_freq: int = 100
     seed: int = 42

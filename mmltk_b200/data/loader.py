@@ -66,7 +66,7 @@ class BatchLoader:
     def __init__(self, path: str, batch_size: int, shuffle: bool = True, seed: int = 42, shard_rank: int = 0,
                  shard_count: int = 1, drop_last: bool = False, workers: int = 4, prefetch: int = 3,
                  pixels: str = "uint8", max_targets: int = 100, device: Optional[torch.device] = None,
-                 with_masks: bool = False):
+                 with_masks: bool = False, cpus: Optional[List[int]] = None):
         self.dataset = CompiledDataset(path)
         w, h = self.dataset.size
         self.batch_size = batch_size
@@ -81,7 +81,8 @@ class BatchLoader:
         self.slots = [torch.empty(batch_size, 3, h, w, dtype=dtype, pin_memory=pin) for _ in range(max(2, prefetch))]
         nbytes = self.slots[0].numel() * self.slots[0].element_size()
         self.loader = native().DatasetLoader(path, batch_size, shuffle, seed, shard_rank, shard_count, drop_last,
-                                             workers, code, [s.data_ptr() for s in self.slots], nbytes)
+                                             workers, code, [s.data_ptr() for s in self.slots], nbytes,
+                                             list(cpus or []))
         self.copy_stream = torch.cuda.Stream(device) if (device is not None and torch.device(device).type == "cuda") else None
         self.epoch = 0
 

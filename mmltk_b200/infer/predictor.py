@@ -147,8 +147,9 @@ class Predictor:
                 self(x)
                 times.append((time.perf_counter() - t0) * 1e3)
         t = torch.tensor(times)
-        return {"p50_ms": float(t.median()), "p90_ms": float(t.quantile(0.9)), "mean_ms": float(t.mean()),
-                "iters": iters, "batch": batch}
+        return {"p50_ms": float(t.median()), "p90_ms": float(t.quantile(0.9)), "p99_ms": float(t.quantile(0.99)),
+                "mean_ms": float(t.mean()), "images_per_s": float(batch * 1e3 / t.mean()), "iters": iters,
+                "batch": batch}
 
 
 def encode_mask_rle(mask: torch.Tensor) -> str:

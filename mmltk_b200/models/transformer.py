@@ -139,8 +139,11 @@ class DecoderLayer(nn.Module):
         v = ops.linear(tgt, w[2 * d:], b[2 * d:])              # [B, Q, d]
         Qg = Q // groups
         # [B, G, Qg, H, Dh] -> [B*G, H, Qg, Dh]: attention never crosses a group
-        q = qk[..., :d].reshape(B * groups, Qg, H, Dh).transpose(1, 2)
-        k = qk[..., d:].reshape(B * groups, Qg, H, Dh).transpose(1, 2)
+        # split (not two slices): its backward is one concatenation instead of two
+        # zero-filled full-width buffers, two copies and an add
+        qh, kh = qk.split(d, dim=-1)
+        q = qh.reshape(B * groups, Qg, H, Dh).transpose(1, 2)
+        k = kh.reshape(B * groups, Qg, H, Dh).transpose(1, 2)
         vv = v.reshape(B * groups, Qg, H, Dh).transpose(1, 2)
         o = ops.attention(q, k, vv).transpose(1, 2).reshape(B, Q, d)
         return ops.linear(o, self.self_attn.out_proj.weight, self.self_attn.out_proj.bias)
@@ -378,20 +381,8 @@ class Transformer(nn.Module):
             out_mem = memory.masked_fill(~valid, 0.0)
             # Selection pass over every token, without autograd: only the top-k indices leave it.
             with torch.no_grad():
-                # the norm's per-group affine is folded into the class head: W' = W diag(gamma),
-                # b' = W beta + b, so the selection pass runs GEMM -> LN -> GEMM with no affine passes
-                h_all = self.enc_output(out_mem, groups)                               # [G, B, S, C]
-                hn = F.layer_norm(h_all, (h_all.shape[-1],), None, None, 1e-5)
-                del h_all
-                wc = self.enc_out_class_embed.weight[:groups].float()
-                gam = self.enc_output_norm.weight[:groups].float()
-                bet = self.enc_output_norm.bias[:groups].float()
-                w_f = wc * gam[:, None, :]
-                b_f = self.enc_out_class_embed.bias[:groups].float() + torch.einsum("gkc,gc->gk", wc, bet)
-                cls = grouped_linear(hn, w_f, b_f)                                     # [G, B, S, K]
-                k = min(cfg.num_queries, cls.shape[2])
-                topk = cls.max(-1)[0].topk(k, dim=2)[1]                                # [G, B, k]
-                del hn, cls
+                topk = self._select(out_mem, groups)                                   # [G, B, k]
+                k = topk.shape[2]
             # Differentiable pass on the selected tokens only: the head is per token, so recomputing
             # enc_output + norm + box MLP on the k chosen rows gives the same values (and gradients)
             # as gathering them from the full pass, at k / S of the cost.
@@ -425,6 +416,42 @@ class Transformer(nn.Module):
         out["refs"] = refs
         out["memory"] = memory
         return out
+
+    def _select(self, out_mem: torch.Tensor, groups: int) -> torch.Tensor:
+        """Top-k token indices per group by the best class logit of the two-stage head.
+
+        * every group's ``enc_output`` in ONE GEMM over the shared memory tokens:
+          [B*S, C] x [C, G*C] (no per-group copy of the input);
+        * LayerNorm without affine over each C-wide slice; the norm's per-group affine is
+          folded into the class head: W' = W diag(gamma), b' = W beta + b;
+        * class logits as a strided batched GEMM over the groups; the class dimension is
+          padded to a multiple of 8 with zero weights and -inf bias, so the max over the
+          padded, contiguous rows equals the max over the real classes.
+        """
+        B, S, C = out_mem.shape
+        G = groups
+        dt = out_mem.dtype
+        w_all = self.enc_output.weight[:G].to(dt).reshape(G * C, C)
+        b_all = self.enc_output.bias[:G].to(dt).reshape(G * C)
+        h = ops.linear(out_mem, w_all, b_all)                                  # [B, S, G*C]
+        unit = h.new_ones(C)
+        hn = ops.layer_norm(h.view(B, S, G, C), unit, torch.zeros_like(unit), 1e-5)
+        del h
+        wc = self.enc_out_class_embed.weight[:G].float()
+        gam = self.enc_output_norm.weight[:G].float()
+        bet = self.enc_output_norm.bias[:G].float()
+        w_f = wc * gam[:, None, :]
+        b_f = self.enc_out_class_embed.bias[:G].float() + torch.einsum("gkc,gc->gk", wc, bet)
+        K = w_f.shape[1]
+        pad = (-K) % 8
+        if pad:
+            w_f = F.pad(w_f, (0, 0, 0, pad))
+            b_f = F.pad(b_f, (0, pad), value=float("-inf"))
+        x = hn.view(B * S, G, C).transpose(0, 1)                               # [G, B*S, C], row stride G*C
+        cls = torch.baddbmm(b_f.to(dt)[:, None, :], x, w_f.to(dt).transpose(1, 2))   # [G, B*S, K+pad]
+        best = cls.amax(-1).view(G, B, S)
+        k = min(self.cfg.num_queries, S)
+        return best.topk(k, dim=2)[1]
 
     def encoder_class_logits(self, enc_memory: torch.Tensor, groups: int) -> torch.Tensor:
         B, Q, C = enc_memory.shape

@@ -3,8 +3,9 @@ as channels-last LN).  Reference: `torch::nn::LayerNorm` uses in
 `src/rfdetr/layers/model.cpp:267-285,535-541,873-886` (libtorch kernel).
 
 CUDA: one warp per row, fp32 statistics, bf16/fp32 I/O; backward computes dx
-per row and dgamma/dbeta through per-CTA fp32 partials reduced by a second
-kernel.  CPU: ``torch.nn.functional.layer_norm`` (the oracle).
+per row and dgamma/dbeta in the same launch (per-CTA partials added into fp32
+accumulators, the last CTA writes or accumulates into ``.grad``).  CPU:
+``torch.nn.functional.layer_norm`` (the oracle).
 """
 from __future__ import annotations
 

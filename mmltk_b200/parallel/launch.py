@@ -24,12 +24,12 @@ import subprocess
 import sys
 import tempfile
 import time
-from typing import List, Optional, Sequence
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
 
-__all__ = ["DistContext", "init_distributed", "launch_workers", "rewrite_worker_argv"]
+__all__ = ["DistContext", "init_distributed", "launch_workers", "rank_plan", "rewrite_worker_argv"]
 
 
 @dataclasses.dataclass
@@ -112,19 +112,39 @@ def rewrite_worker_argv(argv: Sequence[str], rank: int, world: int, device: int,
     return out
 
 
+def rank_plan(world: int, workers: int = 0, cpu_affinity: str = "") -> List[Tuple[Optional[int], str]]:
+    """(worker budget, CPU list) per rank: contiguous CPU shards of ``cpu_affinity`` (or of
+    the allowed set), the worker budget split evenly and clamped to the shard (>= 3)."""
+    from ..ops._ext import native
+    from ..utils.runtime import rank_cpu_shards
+    n = native()
+    shards = rank_cpu_shards(world, cpu_affinity)
+    out = []
+    for r in range(world):
+        per = max(1, workers // world + (1 if r < workers % world else 0)) if workers else None
+        shard = shards[r]
+        if len(shard) >= 3:
+            per = n.clamp_workers(per or 0, len(shard), 0, 3)
+        out.append((per, n.format_cpuset(shard) if shard else ""))
+    return out
+
+
 def launch_workers(argv: Sequence[str], device_ids: Sequence[int], workers: int = 0, python: Optional[str] = None,
-                   entry: Optional[Sequence[str]] = None, poll_s: float = 0.2) -> int:
+                   entry: Optional[Sequence[str]] = None, poll_s: float = 0.2, cpu_affinity: str = "") -> int:
     """Run one child per device and wait.  Returns 0, or the first failing child's exit code
-    (the others are terminated).  SIGINT / SIGTERM received by the parent go to every child."""
+    (the others are terminated).  SIGINT / SIGTERM received by the parent go to every child.
+    Each child gets a contiguous shard of the CPUs and its share of ``--workers``
+    (``rank_plan``)."""
     world = len(device_ids)
     store = os.path.join(tempfile.gettempdir(), f"mmltk_rfdetr_train_{os.getpid()}.store")
     if os.path.exists(store):
         os.remove(store)
     base = list(entry) if entry is not None else [python or sys.executable, "-m", "mmltk_b200.cli"]
-    per = max(1, workers // world) if workers else None
+    plan = rank_plan(world, workers, cpu_affinity)
     children: List[subprocess.Popen] = []
     for r, d in enumerate(device_ids):
-        cmd = base + rewrite_worker_argv(argv, r, world, int(d), store, per)
+        per, cpus = plan[r]
+        cmd = base + rewrite_worker_argv(argv, r, world, int(d), store, per, cpus or None)
         children.append(subprocess.Popen(cmd))
 
     def forward(sig, _frame):

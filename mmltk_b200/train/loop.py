@@ -35,6 +35,7 @@ from ..data.augment import GpuAugmenter
 from ..data.loader import BatchLoader, CompiledDataset
 from ..infer.predictor import Predictor, resolve_model
 from ..parallel.launch import DistContext, init_distributed
+from ..utils.runtime import setup_host_runtime
 
 __all__ = ["run_training", "ProgressWriter", "checkpoint_metric", "evaluate", "validation_loss"]
 
@@ -257,10 +258,15 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
     counts = train_ds.reader.instance_counts()
     slots = int(counts.max()) + 1 if counts.numel() else 1
     slots = max(1, min(slots, 256))
+    rt = setup_host_runtime(opts.workers, 1, max(2, opts.prefetch_factor), opts.cpu_affinity,
+                            pin=ctx.device.type == "cuda", high_priority=opts.high_priority)
+    if ctx.main:
+        log.info("host runtime: %s", rt.describe())
     loader = BatchLoader(opts.train_compiled, opts.batch_size, shuffle=True, seed=opts.seed, shard_rank=ctx.rank,
-                         shard_count=ctx.world_size, drop_last=True, pixels="uint8", workers=max(1, opts.workers or 4),
+                         shard_count=ctx.world_size, drop_last=True, pixels="uint8", workers=max(1, rt.split["gather"]),
                          prefetch=max(2, opts.prefetch_factor), max_targets=1,
-                         device=ctx.device if ctx.device.type == "cuda" else None)
+                         device=ctx.device if ctx.device.type == "cuda" else None,
+                         cpus=rt.loader_cpus[:1] if ctx.device.type == "cuda" else None)
     batches = len(loader)
     steps_per_epoch = batches // opts.grad_accum_steps
     if steps_per_epoch == 0:

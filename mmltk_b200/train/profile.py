@@ -16,8 +16,13 @@ import sys
 import torch
 
 
-def _origin(ev) -> str:
-    """Nearest enclosing autograd node (backward) or autograd Function / module-level op (forward)."""
+def _origin(ev, stack: bool = False) -> str:
+    """Nearest enclosing autograd node (backward) or autograd Function / module-level op (forward);
+    with ``stack``, forward ops outside an autograd Function name their innermost frame in this package."""
+    if stack and ev.stack:
+        for fr in ev.stack:
+            if "mmltk_b200" in fr and "profile.py" not in fr:
+                return fr.split("mmltk_b200/")[-1]
     p = ev.cpu_parent
     while p is not None:
         n = p.name
@@ -29,24 +34,27 @@ def _origin(ev) -> str:
     return "-"
 
 
-def origin_table(events, steps: int, top: int) -> str:
-    """CUDA time of each aten op's own kernels, keyed by (op, origin)."""
+def origin_table(events, steps: int, top: int, shapes: bool = False, stack: bool = False) -> str:
+    """CUDA time of each aten op's own kernels, keyed by (op, origin[, input shapes])."""
     per = collections.Counter()
     count = collections.Counter()
     for ev in events:
         if ev.device_type != torch.autograd.DeviceType.CPU or not ev.name.startswith("aten::"):
             continue
-        t = sum(k.device_time for k in ev.kernels)
+        t = sum(k.duration for k in ev.kernels)
         if not ev.kernels:
             continue
-        key = (ev.name, _origin(ev))
+        org = _origin(ev, stack)
+        if shapes:
+            org = f"{org} {str(ev.input_shapes)[:70]}"
+        key = (ev.name, org)
         per[key] += t
         count[key] += len(ev.kernels)
     total = sum(per.values()) or 1.0
     lines = ["| share | ms/step | kernels/step | aten op | origin |", "|---|---|---|---|---|"]
     for (name, org), t in per.most_common(top):
         lines.append(f"| {100 * t / total:.1f}% | {t / 1e3 / steps:.3f} | {count[(name, org)] // steps} | "
-                     f"`{name}` | `{org[:80]}` |")
+                     f"`{name}` | `{org[:150]}` |")
     return "\n".join(lines)
 
 
@@ -58,9 +66,10 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--top", type=int, default=30)
     ap.add_argument("--by-op", action="store_true", help="rank aten ops (with input shapes) instead of kernels")
-    ap.add_argument("--no-shapes", action="store_true", help="with --by-op: group by op name only")
+    ap.add_argument("--no-shapes", action="store_true", help="with --by-op / --by-origin: leave input shapes out")
     ap.add_argument("--by-origin", action="store_true",
                     help="rank (aten op, enclosing autograd node or autograd Function) pairs by CUDA time")
+    ap.add_argument("--stack", action="store_true", help="with --by-origin: name forward ops by source line")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         print("profile: needs a GPU", file=sys.stderr)
@@ -83,11 +92,12 @@ def main(argv=None) -> int:
     torch.cuda.synchronize()
     from torch.profiler import ProfilerActivity, profile
     if a.by_origin:
-        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=not a.no_shapes,
+                     with_stack=a.stack) as prof:
             for _ in range(a.steps):
                 eng.step()
             torch.cuda.synchronize()
-        print(origin_table(prof.events(), a.steps, a.top))
+        print(origin_table(prof.events(), a.steps, a.top, shapes=not a.no_shapes, stack=a.stack))
         return 0
     if a.by_op:
         # aten ops with input shapes, ranked by the CUDA time of the kernels they launched

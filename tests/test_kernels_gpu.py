@@ -290,3 +290,19 @@ def test_gemm_tc_tile_widths(cuda_device, N):
     ref = res.float() + gamma.float() * pre
     assert (pre_d.float().cpu() - pre).abs().max().item() < 2e-2 * pre.abs().max().item()
     assert (out.float().cpu() - ref).abs().max().item() < 2e-2 * ref.abs().max().item()
+
+
+@pytest.mark.gpu
+def test_gelu_derivative_accuracy_fp32(cuda_device):
+    """GELU'(x) = Phi(x) + x phi(x) (Abramowitz & Stegun 7.1.26 erf) against a float64 oracle,
+    through the act_bwd kernel and the fused act_bwd + bias-gradient reduction."""
+    x = torch.linspace(-14.0, 14.0, 64 * 1024, dtype=torch.float64)
+    ref = torch.special.ndtr(x) + x * torch.exp(-0.5 * x * x) / np.sqrt(2 * np.pi)
+    pre = x.float().to(cuda_device).reshape(-1, 256)
+    gy = torch.ones_like(pre)
+    out = kernels().act_bwd(gy, pre, 1).double().cpu().reshape(-1)
+    err = (out - ref).abs()
+    assert float(err.max()) < 2e-6, float(err.max())
+    gpre, gb = kernels().act_bwd_bias(gy, pre, 1, None, None)
+    assert float((gpre.double().cpu().reshape(-1) - ref).abs().max()) < 2e-6
+    assert torch.allclose(gb.double().cpu(), ref.reshape(-1, 256).sum(0), atol=1e-3, rtol=1e-5)

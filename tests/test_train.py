@@ -124,6 +124,22 @@ def test_cuda_engine_eager_and_graph(cuda_device):
     eng.release_graph()
 
 
+def test_two_stage_selection_matches_the_unfolded_head():
+    """One-GEMM selection pass (folded norm affine, -inf padded classes) picks the same tokens as
+    enc_output -> grouped LayerNorm -> class head per group."""
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-tiny-test", resolution=64, group_detr=3, num_classes=13)
+    tr = [m for m in RFDETR(cfg).modules() if hasattr(m, "_select")][0]
+    with torch.no_grad():
+        for p in list(tr.enc_output_norm.parameters()) + list(tr.enc_out_class_embed.parameters()):
+            p.normal_()
+        mem = torch.randn(2, 50, cfg.hidden_dim)
+        sel = tr._select(mem, 3)
+        cls = tr.enc_out_class_embed(tr.enc_output_norm(tr.enc_output(mem, 3), 3), 3)
+        ref = cls.max(-1)[0].topk(sel.shape[2], dim=2)[1]
+    assert torch.equal(sel.sort(-1)[0], ref.sort(-1)[0])
+
+
 def test_step_async_cpu_returns_the_step_result():
     torch.manual_seed(0)
     cfg = config_from_preset("rf-detr-tiny-test", resolution=64)
