@@ -161,13 +161,16 @@ __global__ void __launch_bounds__(kColThreads, kColCtasPerSm) colreduce_kernel(c
         atomicAdd(reinterpret_cast<float4*>(acc_buf + col), make_float4(acc[0], acc[1], acc[2], acc[3]));
         atomicAdd(reinterpret_cast<float4*>(acc_buf + col + 4), make_float4(acc[4], acc[5], acc[6], acc[7]));
     }
-    // arrival: the last CTA of this slab writes the result and clears the scratch
-    __threadfence();
+    // arrival: the last CTA of this slab writes the result and clears the scratch.  One thread
+    // fences after the barrier (the barrier orders the CTA's atomics before it), as in a grid sync.
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&counters[blockIdx.y], 1u) == gridDim.x - 1;
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(&counters[blockIdx.y], 1u) == gridDim.x - 1;
+        if (s_last) __threadfence();
+    }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     if (rl == 0 && cols_ok) {
         float s[8];
         ldcg8(acc_buf + col, s);

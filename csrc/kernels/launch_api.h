@@ -14,12 +14,25 @@ enum class DType : int { kF32 = 0, kBF16 = 1 };
 int num_sms();
 
 // ---------------------------------------------------------------- LayerNorm
+// res/sum (both or neither): normalise x + res and store the sum to `sum`; pos/y2 (both or
+// neither): also store y + pos to y2.  All [rows, C] of the x dtype.
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
-                                 float* rstd, int64_t rows, int C, float eps, cudaStream_t st);
+                                 float* rstd, int64_t rows, int C, float eps, cudaStream_t st,
+                                 const void* res = nullptr, void* sum = nullptr, const void* pos = nullptr,
+                                 void* y2 = nullptr);
 // One launch: gx, and gw / gb written (or added into, `accumulate`) by the last CTA.
+// gy2 (optional): a second output gradient added to gy (the y + pos output of the forward).
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
-                                 bool accumulate, cudaStream_t st);
+                                 bool accumulate, cudaStream_t st, const void* gy2 = nullptr);
+
+// ---------------------------------------------------------------- sine position embedding
+// pos [rows, n] fp32 (n = 2 or 4: x, y[, w, h]); out [rows, n * dim] bf16 in block order y, x[, w, h];
+// freq [dim / 2] fp32.  n * dim / 32 must be 8, 16 or 32 and divide dim.
+cudaError_t launch_sine_embed_fwd(const float* pos, int64_t rows, int n, int dim, const float* freq, void* out,
+                                  cudaStream_t st);
+cudaError_t launch_sine_embed_bwd(const float* pos, int64_t rows, int n, int dim, const float* freq, const void* gout,
+                                  float* gpos, cudaStream_t st);
 
 // ---------------------------------------------------------------- MSDeformAttn
 struct MsdaDims {

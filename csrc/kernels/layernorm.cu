@@ -15,11 +15,21 @@ namespace mmltk {
 
 namespace {
 
+// Optional fusions of the forward: res -> normalise x + res and store the sum; pos -> also
+// store y + pos.
+template <typename T>
+struct LnFwdExtra {
+    const T* res;
+    T* sum;
+    const T* pos;
+    T* y2;
+};
+
 template <typename T, typename W, int kMaxVec>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, const W* __restrict__ w,
                                                      const W* __restrict__ b, T* __restrict__ y,
                                                      float* __restrict__ mean_out, float* __restrict__ rstd_out,
-                                                     int64_t rows, int C, float eps) {
+                                                     int64_t rows, int C, float eps, LnFwdExtra<T> ex) {
     const int lane = threadIdx.x & 31;
     const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -33,6 +43,11 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, co
             const int i = lane + 32 * k;
             if (i < nv) {
                 v[k] = load4(xr + 4 * i);
+                if (ex.res != nullptr) {   // fused residual add: the norm's input is x + res
+                    const float4 r4 = load4(ex.res + r * C + 4 * i);
+                    v[k].x += r4.x; v[k].y += r4.y; v[k].z += r4.z; v[k].w += r4.w;
+                    store4(ex.sum + r * C + 4 * i, v[k]);
+                }
                 s += v[k].x + v[k].y + v[k].z + v[k].w;
             }
         }
@@ -59,6 +74,10 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, co
                 o.z = (v[k].z - mean) * rstd * to_f(w[c0 + 2]) + to_f(b[c0 + 2]);
                 o.w = (v[k].w - mean) * rstd * to_f(w[c0 + 3]) + to_f(b[c0 + 3]);
                 store4(yr + c0, o);
+                if (ex.pos != nullptr) {   // second output y + pos (e.g. a query with its position embedding)
+                    const float4 p4 = load4(ex.pos + r * C + c0);
+                    store4(ex.y2 + r * C + c0, make_float4(o.x + p4.x, o.y + p4.y, o.z + p4.z, o.w + p4.w));
+                }
             }
         }
         if (lane == 0) {
@@ -132,7 +151,7 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                                                      const float* __restrict__ rstd_in, T* __restrict__ gx,
                                                      float* acc_w, float* acc_b, unsigned* counter,
                                                      W* __restrict__ gw, W* __restrict__ gb, int accumulate,
-                                                     int64_t rows, int C) {
+                                                     int64_t rows, int C, const T* __restrict__ gy2) {
     extern __shared__ float smem[];  // [warps][2][C]
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
@@ -171,6 +190,10 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
             for (int k = 0; k < kMaxVec; ++k) {
                 xv[k] = nx[k].widen();
                 gv[k] = ng[k].widen();
+                if (gy2 != nullptr && lane + 32 * k < nv) {   // gradient of the fused y + pos output
+                    const float4 g2 = load4(gy2 + r * C + 4 * (lane + 32 * k));
+                    gv[k].x += g2.x; gv[k].y += g2.y; gv[k].z += g2.z; gv[k].w += g2.w;
+                }
             }
             const int64_t rn = r + nwarps;
             if (rn < rows) {
@@ -197,6 +220,10 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                 if (i < nv) {
                     xv[k] = load4(x + r * C + 4 * i);
                     gv[k] = load4(gy + r * C + 4 * i);
+                    if (gy2 != nullptr) {
+                        const float4 g2 = load4(gy2 + r * C + 4 * i);
+                        gv[k].x += g2.x; gv[k].y += g2.y; gv[k].z += g2.z; gv[k].w += g2.w;
+                    }
                 }
             }
             ln_bwd_row<T, W, kMaxVec>(xv, gv, mean_in[r], rstd_in[r], w, aw, ab, gx + r * C, lane, nv, C);
@@ -227,13 +254,16 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
         atomicAdd(reinterpret_cast<float4*>(acc_w + 4 * c4), a);
         atomicAdd(reinterpret_cast<float4*>(acc_b + 4 * c4), bb);
     }
+    // arrival (one thread fences after the barrier, as in a grid sync)
     __shared__ unsigned s_last;
-    __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+        if (s_last) __threadfence();
+    }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     for (int c = threadIdx.x; c < C; c += blockDim.x) {
         const float a = __ldcg(acc_w + c), bb = __ldcg(acc_b + c);
         gw[c] = from_f<W>((accumulate ? to_f(gw[c]) : 0.f) + a);
@@ -275,7 +305,9 @@ void dispatch_vec(int C, F&& f) {
 }  // namespace
 
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
-                                 float* rstd, int64_t rows, int C, float eps, cudaStream_t st) {
+                                 float* rstd, int64_t rows, int C, float eps, cudaStream_t st, const void* res,
+                                 void* sum, const void* pos, void* y2) {
+    if ((res == nullptr) != (sum == nullptr) || (pos == nullptr) != (y2 == nullptr)) return cudaErrorInvalidValue;
     if (rows == 0) return cudaSuccess;
     if (C % 4 != 0 || C > 4 * 32 * 12) return cudaErrorInvalidValue;
     const int threads = 256;
@@ -287,7 +319,9 @@ cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* 
             dispatch_vec(C, [&](auto nvl) {
                 ln_fwd_kernel<T, Wt, decltype(nvl)::value><<<blocks, threads, 0, st>>>(
                     static_cast<const T*>(x), static_cast<const Wt*>(w), static_cast<const Wt*>(b),
-                    static_cast<T*>(y), mean, rstd, rows, C, eps);
+                    static_cast<T*>(y), mean, rstd, rows, C, eps,
+                    LnFwdExtra<T>{static_cast<const T*>(res), static_cast<T*>(sum), static_cast<const T*>(pos),
+                                  static_cast<T*>(y2)});
             });
             return cudaGetLastError();
         });
@@ -309,7 +343,7 @@ int ln_bwd_blocks(K kern, int threads, size_t smem, int64_t rows) {
 
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
-                                 bool accumulate, cudaStream_t st) {
+                                 bool accumulate, cudaStream_t st, const void* gy2) {
     if (C % 4 != 0 || C > 4 * 32 * 12 || 2 * C > kReduceAccFloats) return cudaErrorInvalidValue;
     const ReduceScratch rs = reduce_scratch();
     if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
@@ -331,7 +365,8 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
                 kern<<<blocks, threads, smem, st>>>(static_cast<const T*>(gy), static_cast<const T*>(x),
                                                     static_cast<const Wt*>(w), mean, rstd, static_cast<T*>(gx), rs.acc,
                                                     rs.acc + C, rs.counters, static_cast<Wt*>(gw),
-                                                    static_cast<Wt*>(gb), accumulate ? 1 : 0, rows, C);
+                                                    static_cast<Wt*>(gb), accumulate ? 1 : 0, rows, C,
+                                                    static_cast<const T*>(gy2));
             });
             if (e != cudaSuccess) return e;
             return cudaGetLastError();

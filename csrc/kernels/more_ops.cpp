@@ -113,9 +113,41 @@ torch::Tensor act_bwd(torch::Tensor gy, torch::Tensor pre, int64_t act) {
     return out;
 }
 
+torch::Tensor sine_embed_fwd(torch::Tensor pos, int64_t dim, torch::Tensor freq) {
+    TORCH_CHECK(pos.is_cuda() && pos.scalar_type() == torch::kFloat32 && freq.scalar_type() == torch::kFloat32,
+                "sine_embed_fwd: CUDA fp32 pos / freq expected");
+    at::cuda::CUDAGuard guard(pos.device());
+    auto p = pos.contiguous();
+    const int n = static_cast<int>(p.size(-1));
+    const int64_t rows = p.numel() / n;
+    auto sizes = p.sizes().vec();
+    sizes.back() = n * dim;
+    auto out = torch::empty(sizes, p.options().dtype(torch::kBFloat16));
+    check_cuda(launch_sine_embed_fwd(p.data_ptr<float>(), rows, n, static_cast<int>(dim),
+                                     freq.contiguous().data_ptr<float>(), out.data_ptr(), cur_stream()),
+               "sine_embed_fwd");
+    return out;
+}
+
+torch::Tensor sine_embed_bwd(torch::Tensor pos, int64_t dim, torch::Tensor freq, torch::Tensor gout) {
+    at::cuda::CUDAGuard guard(pos.device());
+    auto p = pos.contiguous();
+    auto g = aligned16(gout.to(torch::kBFloat16));
+    const int n = static_cast<int>(p.size(-1));
+    const int64_t rows = p.numel() / n;
+    auto gpos = torch::empty_like(p);
+    check_cuda(launch_sine_embed_bwd(p.data_ptr<float>(), rows, n, static_cast<int>(dim),
+                                     freq.contiguous().data_ptr<float>(), g.data_ptr(), gpos.data_ptr<float>(),
+                                     cur_stream()),
+               "sine_embed_bwd");
+    return gpos;
+}
+
 }  // namespace
 
 void register_more_ops(pybind11::module& m) {
+    m.def("sine_embed_fwd", &sine_embed_fwd, py::arg("pos"), py::arg("dim"), py::arg("freq"));
+    m.def("sine_embed_bwd", &sine_embed_bwd, py::arg("pos"), py::arg("dim"), py::arg("freq"), py::arg("gout"));
     m.def("dense_focal_neg_fwd", &dense_focal_neg_fwd);
     m.def("dense_focal_neg_bwd", &dense_focal_neg_bwd);
     m.def("colsum", &colsum, py::arg("x"), py::arg("out_dtype") = py::none(), py::arg("out") = py::none());

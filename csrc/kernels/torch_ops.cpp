@@ -45,10 +45,20 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 namespace {
 
 // ---------------------------------------------------------------- LayerNorm
-std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps) {
+// res: normalise x + res (the sum is returned too); pos: also return y + pos.
+// Returns {y, mean, rstd, sum (or undefined), y + pos (or undefined)}.
+std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps,
+                                         c10::optional<torch::Tensor> res, c10::optional<torch::Tensor> pos) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "layernorm_fwd: x must be contiguous [rows, C]");
     TORCH_CHECK(w.scalar_type() == b.scalar_type() && w.numel() == x.size(1) && b.numel() == x.size(1),
                 "layernorm_fwd: weight/bias must match C and share a dtype");
+    const bool has_res = res && res->defined(), has_pos = pos && pos->defined();
+    if (has_res)
+        TORCH_CHECK(res->sizes() == x.sizes() && res->is_contiguous() && res->scalar_type() == x.scalar_type(),
+                    "layernorm_fwd: res must match x");
+    if (has_pos)
+        TORCH_CHECK(pos->sizes() == x.sizes() && pos->is_contiguous() && pos->scalar_type() == x.scalar_type(),
+                    "layernorm_fwd: pos must match x");
     at::cuda::CUDAGuard guard(x.device());
     const int64_t rows = x.size(0);
     const int C = static_cast<int>(x.size(1));
@@ -57,17 +67,27 @@ std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch
     auto mean = torch::empty({rows}, opts);
     auto rstd = torch::empty({rows}, opts);
     auto wc = w.contiguous(), bc = b.contiguous();
+    torch::Tensor sum, y2;
+    if (has_res) sum = torch::empty_like(x);
+    if (has_pos) y2 = torch::empty_like(x);
     check_cuda(launch_layernorm_fwd(dtype_of(x), dtype_of(w), x.data_ptr(), wc.data_ptr(), bc.data_ptr(), y.data_ptr(),
                                     mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C, static_cast<float>(eps),
-                                    cur_stream()),
+                                    cur_stream(), has_res ? res->data_ptr() : nullptr,
+                                    has_res ? sum.data_ptr() : nullptr, has_pos ? pos->data_ptr() : nullptr,
+                                    has_pos ? y2.data_ptr() : nullptr),
                "layernorm_fwd");
-    return {y, mean, rstd};
+    return {y, mean, rstd, sum, y2};
 }
 
 // gw_acc / gb_acc: when given (a parameter's .grad view), the weight / bias gradients are added into them
+// gy2: gradient of the forward's y + pos output, added to gy inside the kernel
 std::vector<torch::Tensor> layernorm_bwd(torch::Tensor gy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
                                          torch::Tensor rstd, c10::optional<torch::Tensor> gw_acc,
-                                         c10::optional<torch::Tensor> gb_acc) {
+                                         c10::optional<torch::Tensor> gb_acc, c10::optional<torch::Tensor> gy2) {
+    const bool has_g2 = gy2 && gy2->defined();
+    if (has_g2)
+        TORCH_CHECK(gy2->sizes() == x.sizes() && gy2->is_contiguous() && gy2->scalar_type() == x.scalar_type(),
+                    "layernorm_bwd: gy2 must match x");
     TORCH_CHECK(gy.sizes() == x.sizes() && gy.is_contiguous() && x.is_contiguous() &&
                     gy.scalar_type() == x.scalar_type(),
                 "layernorm_bwd: grad/x mismatch");
@@ -87,7 +107,7 @@ std::vector<torch::Tensor> layernorm_bwd(torch::Tensor gy, torch::Tensor x, torc
     auto gb = acc ? *gb_acc : torch::empty_like(wc);
     check_cuda(launch_layernorm_bwd(dtype_of(x), dtype_of(w), gy.data_ptr(), x.data_ptr(), wc.data_ptr(),
                                     mean.data_ptr<float>(), rstd.data_ptr<float>(), gx.data_ptr(), gw.data_ptr(),
-                                    gb.data_ptr(), rows, C, acc, cur_stream()),
+                                    gb.data_ptr(), rows, C, acc, cur_stream(), has_g2 ? gy2->data_ptr() : nullptr),
                "layernorm_bwd");
     return {gx, gw, gb};
 }
@@ -257,9 +277,10 @@ void adamw_ema_step(torch::Tensor chunks, torch::Tensor groups, torch::Tensor sc
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "mmltk_b200 sm_100a CUDA kernels";
     m.def("num_sms", &mmltk::num_sms);
-    m.def("layernorm_fwd", &mmltk::layernorm_fwd);
+    m.def("layernorm_fwd", &mmltk::layernorm_fwd, py::arg("x"), py::arg("w"), py::arg("b"), py::arg("eps"),
+          py::arg("res") = py::none(), py::arg("pos") = py::none());
     m.def("layernorm_bwd", &mmltk::layernorm_bwd, py::arg("gy"), py::arg("x"), py::arg("w"), py::arg("mean"),
-          py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none());
+          py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none(), py::arg("gy2") = py::none());
     m.def("msda_fwd", &mmltk::msda_fwd);
     m.def("msda_bwd", &mmltk::msda_bwd);
     m.def("matcher_cost", &mmltk::matcher_cost);

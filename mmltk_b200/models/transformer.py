@@ -52,20 +52,10 @@ class Mlp(nn.Module):
 
 
 def gen_sineembed_for_position(pos: torch.Tensor, dim: int = 128) -> torch.Tensor:
-    """Sine embedding of (x, y[, w, h]) -> [..., 2*dim or 4*dim] (reference `model.cpp:234-261`)."""
-    scale = 2 * math.pi
-    dim_t = torch.arange(dim, dtype=torch.float32, device=pos.device)
-    dim_t = 10000.0 ** (2 * torch.div(dim_t, 2, rounding_mode="floor") / dim)
-
-    def enc(v):
-        x = v[..., None] * scale / dim_t
-        return torch.stack((x[..., 0::2].sin(), x[..., 1::2].cos()), -1).flatten(-2)
-
-    p = pos.float()
-    parts = [enc(p[..., 1]), enc(p[..., 0])]
-    if pos.shape[-1] == 4:
-        parts += [enc(p[..., 2]), enc(p[..., 3])]
-    return torch.cat(parts, -1)
+    """Sine embedding of (x, y[, w, h]) -> [..., 2*dim or 4*dim] (reference `model.cpp:234-261`):
+    blocks y, x[, w, h], entries sin / cos of v * 2 pi / 10000^(2i/dim).  One fused kernel each
+    way on CUDA (bf16 out); the fp32 torch expression on CPU."""
+    return ops.sine_embed(pos, dim)
 
 
 def reparam_boxes(delta: torch.Tensor, base: torch.Tensor) -> torch.Tensor:
@@ -130,12 +120,12 @@ class DecoderLayer(nn.Module):
         self.norm2 = nn.LayerNorm(d)
         self.norm3 = nn.LayerNorm(d)
 
-    def _self_attention(self, tgt, query_pos, groups):
+    def _self_attention(self, tgt, query_pos, groups, tgt_pos=None):
         B, Q, d = tgt.shape
         H = self.self_attn.num_heads
         Dh = d // H
         w, b = self.self_attn.in_proj_weight, self.self_attn.in_proj_bias
-        qk = ops.linear(tgt + query_pos, w[:2 * d], b[:2 * d])  # [B, Q, 2d]
+        qk = ops.linear(tgt_pos if tgt_pos is not None else tgt + query_pos, w[:2 * d], b[:2 * d])  # [B, Q, 2d]
         v = ops.linear(tgt, w[2 * d:], b[2 * d:])              # [B, Q, d]
         Qg = Q // groups
         # [B, G, Qg, H, Dh] -> [B*G, H, Qg, Dh]: attention never crosses a group
@@ -148,14 +138,19 @@ class DecoderLayer(nn.Module):
         o = ops.attention(q, k, vv).transpose(1, 2).reshape(B, Q, d)
         return ops.linear(o, self.self_attn.out_proj.weight, self.self_attn.out_proj.bias)
 
-    def forward(self, tgt, query_pos, ref, memory, shapes, padding_mask, groups):
-        sa = self._self_attention(tgt, query_pos, groups)
-        x = ops.layer_norm(tgt + sa, self.norm1.weight, self.norm1.bias, 1e-5)
-        ca = self.cross_attn(x + query_pos, ref, memory, shapes, padding_mask)
-        x = ops.layer_norm(x + ca, self.norm2.weight, self.norm2.bias, 1e-5)
+    def forward(self, tgt, query_pos, ref, memory, shapes, padding_mask, groups, tgt_pos=None, want_pos=False):
+        """Post-norm layer.  ``tgt_pos`` = tgt + query_pos when the caller has it already;
+        ``want_pos`` also returns out + query_pos (the next layer's self-attention input), made by
+        the last norm's kernel.  Residual adds are fused into the norms."""
+        sa = self._self_attention(tgt, query_pos, groups, tgt_pos)
+        x, x_pos = ops.add_layer_norm(tgt, sa, self.norm1.weight, self.norm1.bias, 1e-5, pos=query_pos)
+        ca = self.cross_attn(x_pos, ref, memory, shapes, padding_mask)
+        x = ops.add_layer_norm(x, ca, self.norm2.weight, self.norm2.bias, 1e-5)
         h = ops.linear(x, self.linear1.weight, self.linear1.bias, act="relu")
         h = ops.linear(h, self.linear2.weight, self.linear2.bias)
-        return ops.layer_norm(x + h, self.norm3.weight, self.norm3.bias, 1e-5)
+        if want_pos:
+            return ops.add_layer_norm(x, h, self.norm3.weight, self.norm3.bias, 1e-5, pos=query_pos)
+        return ops.add_layer_norm(x, h, self.norm3.weight, self.norm3.bias, 1e-5)
 
 
 class Decoder(nn.Module):
@@ -183,10 +178,15 @@ class Decoder(nn.Module):
         hs_refs = [refpoints]
         if cfg.lite_refpoint_refine:
             rin, qpos = reference(refs if cfg.bbox_reparam else refs.sigmoid())
+        out_pos = None   # out + qpos, from the previous layer's last norm
         for li, layer in enumerate(self.layers):
             if not cfg.lite_refpoint_refine:
                 rin, qpos = reference(refs if cfg.bbox_reparam else refs.sigmoid())
-            out = layer(out, qpos, rin, memory, shapes, padding_mask, groups)
+                out_pos = None
+            # the next layer reuses this layer's qpos only under lite refinement
+            chain = cfg.lite_refpoint_refine and li + 1 < len(self.layers)
+            res = layer(out, qpos, rin, memory, shapes, padding_mask, groups, tgt_pos=out_pos, want_pos=chain)
+            out, out_pos = res if chain else (res, None)
             if not cfg.lite_refpoint_refine and bbox_embed is not None:
                 delta = bbox_embed(out)
                 new = reparam_boxes(delta, refs) if cfg.bbox_reparam else refs + delta

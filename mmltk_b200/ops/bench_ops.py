@@ -3,6 +3,7 @@ library baseline of the same op, timed with CUDA events after warm-up.
 
     python -m mmltk_b200.ops.bench_ops gemm      # tcgen05 GEMM vs cuBLAS on the RF-DETR-M shapes
     python -m mmltk_b200.ops.bench_ops msda      # MSDeformAttn fwd+bwd vs fp32 reference path
+    python -m mmltk_b200.ops.bench_ops attn      # attention fwd+bwd of the RF-DETR-M shapes per SDPA backend
 
 Inputs are larger than L2 where the op allows; each timing is the median of
 several event-timed runs.
@@ -15,7 +16,7 @@ import statistics
 
 import torch
 
-__all__ = ["time_ms", "bench_gemm", "bench_msda"]
+__all__ = ["time_ms", "bench_gemm", "bench_msda", "bench_attn"]
 
 
 def time_ms(fn, warmup: int = 5, iters: int = 20, reps: int = 5) -> float:
@@ -116,13 +117,48 @@ def bench_msda(device="cuda"):
              "speedup": round(t_base / t_ours, 2)}]
 
 
+# (name, batch*windows or batch*groups, heads, length, head dim): RF-DETR-M batch 8
+ATTN_SHAPES = [("dec.self_attn", 104, 8, 300, 32), ("vit.window", 32, 6, 325, 64), ("vit.global", 8, 6, 1300, 64)]
+
+
+def bench_attn(device="cuda"):
+    """Forward + backward of the step's attention shapes under each SDPA backend."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    import torch.nn.functional as F
+    rows = []
+    for name, N, H, L, D in ATTN_SHAPES:
+        g = torch.Generator(device=device).manual_seed(0)
+        q, k, v = (torch.randn(N, H, L, D, device=device, generator=g).bfloat16().requires_grad_() for _ in range(3))
+        go = torch.randn(N, H, L, D, device=device, generator=g).bfloat16()
+        row = {"op": "attention", "shape": name, "N": N, "H": H, "L": L, "D": D}
+        for be in (SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION):
+            def fwd():
+                with sdpa_kernel([be]):
+                    return F.scaled_dot_product_attention(q, k, v)
+
+            def both():
+                fwd().backward(go)
+            try:
+                row[be.name.lower() + "_fwd_ms"] = round(time_ms(fwd, warmup=3, iters=10), 4)
+                row[be.name.lower() + "_fwd_bwd_ms"] = round(time_ms(both, warmup=3, iters=10), 4)
+            except RuntimeError as e:   # backend unavailable for this shape / arch
+                row[be.name.lower()] = f"unavailable: {str(e).splitlines()[0][:80]}"
+        rows.append(row)
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "msda"])
+    ap.add_argument("what", choices=["gemm", "msda", "attn"])
     ap.add_argument("--shape", default=None, help="run one GEMM shape (see GEMM_SHAPES)")
     ap.add_argument("--quick", action="store_true", help="launch a few times without timing (profiler runs)")
     args = ap.parse_args()
-    rows = bench_gemm(only=args.shape, quick=args.quick) if args.what == "gemm" else bench_msda()
+    if args.what == "gemm":
+        rows = bench_gemm(only=args.shape, quick=args.quick)
+    elif args.what == "msda":
+        rows = bench_msda()
+    else:
+        rows = bench_attn()
     for r in rows:
         print(json.dumps(r))
 

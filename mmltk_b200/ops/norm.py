@@ -15,7 +15,7 @@ import torch.nn.functional as F
 from ._ext import kernels
 from .gradacc import grad_target
 
-__all__ = ["layer_norm"]
+__all__ = ["layer_norm", "add_layer_norm"]
 
 
 class _LayerNormFn(torch.autograd.Function):
@@ -23,7 +23,7 @@ class _LayerNormFn(torch.autograd.Function):
     def forward(ctx, x, weight, bias, eps):
         shape = x.shape
         x2 = x.contiguous().view(-1, shape[-1])
-        y, mean, rstd = kernels().layernorm_fwd(x2, weight, bias, float(eps))
+        y, mean, rstd = kernels().layernorm_fwd(x2, weight, bias, float(eps))[:3]
         ctx.save_for_backward(x2, weight, mean, rstd)
         ctx.shape = shape
         ctx.params = (weight, bias)
@@ -45,3 +45,50 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: f
     if x.is_cuda and x.shape[-1] % 8 == 0 and x.dtype in (torch.bfloat16, torch.float32):
         return _LayerNormFn.apply(x, weight, bias, eps)
     return F.layer_norm(x, (x.shape[-1],), weight.to(x.dtype), bias.to(x.dtype), eps)
+
+
+class _AddLayerNormFn(torch.autograd.Function):
+    """y = LN(a + b) [, y + pos] in one kernel; the sum is stored for the backward."""
+
+    @staticmethod
+    def forward(ctx, a, b, weight, bias, pos, eps):
+        shape = a.shape
+        C = shape[-1]
+        a2 = a.contiguous().view(-1, C)
+        b2 = b.contiguous().view(-1, C)
+        p2 = pos.contiguous().view(-1, C) if pos is not None else None
+        y, mean, rstd, s, y2 = kernels().layernorm_fwd(a2, weight, bias, float(eps), b2, p2)
+        ctx.save_for_backward(s, weight, mean, rstd)
+        ctx.shape = shape
+        ctx.params = (weight, bias)
+        ctx.has_pos = pos is not None
+        if ctx.has_pos:
+            return y.view(shape), y2.view(shape)
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, gy, gy2=None):
+        s, weight, mean, rstd = ctx.saved_tensors
+        gy = gy.contiguous().view(s.shape) if gy is not None else torch.zeros_like(s)
+        g2 = gy2.contiguous().view(s.shape) if (ctx.has_pos and gy2 is not None) else None
+        wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
+        if wt is not None and bt is not None:
+            dx, dw, db = kernels().layernorm_bwd(gy, s, weight, mean, rstd, wt, bt, g2)
+            dw = db = None
+        else:
+            dx, dw, db = kernels().layernorm_bwd(gy, s, weight, mean, rstd, None, None, g2)
+        dx = dx.view(ctx.shape)
+        gpos = gy2.view(ctx.shape) if g2 is not None else None
+        return dx, dx, dw, db, gpos, None
+
+
+def add_layer_norm(a: torch.Tensor, b: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float,
+                   pos: torch.Tensor = None):
+    """LN(a + b), and with ``pos`` also LN(a + b) + pos -- the post-norm residual of a decoder
+    layer and the next query (with its position embedding) in one pass."""
+    if (a.is_cuda and a.shape[-1] % 8 == 0 and a.dtype in (torch.bfloat16, torch.float32)
+            and b.dtype == a.dtype and b.shape == a.shape and (pos is None or (pos.dtype == a.dtype
+                                                                             and pos.shape == a.shape))):
+        return _AddLayerNormFn.apply(a, b, weight, bias, pos, eps)
+    y = F.layer_norm(a + b, (a.shape[-1],), weight.to(a.dtype), bias.to(a.dtype), eps)
+    return (y, y + pos) if pos is not None else y

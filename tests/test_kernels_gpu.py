@@ -306,3 +306,53 @@ def test_gelu_derivative_accuracy_fp32(cuda_device):
     gpre, gb = kernels().act_bwd_bias(gy, pre, 1, None, None)
     assert float((gpre.double().cpu().reshape(-1) - ref).abs().max()) < 2e-6
     assert torch.allclose(gb.double().cpu(), ref.reshape(-1, 256).sum(0), atol=1e-3, rtol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [2, 4])
+def test_sine_embed_fwd_bwd(cuda_device, n):
+    from mmltk_b200.ops.posembed import sine_embed, sine_embed_reference
+    pos = torch.rand(3, 777, n, device=cuda_device, requires_grad=True)
+    out = sine_embed(pos, 128)
+    assert out.dtype == torch.bfloat16 and out.shape == (3, 777, n * 128)
+    pos64 = pos.detach().double().cpu().requires_grad_()
+    ref = sine_embed_reference(pos64, 128)
+    assert (out.double().cpu() - ref).abs().max() < 4e-3          # bf16 output rounding
+    g = torch.randn(3, 777, n * 128, device=cuda_device).bfloat16()
+    out.backward(g)
+    ref.backward(g.double().cpu())
+    err = (pos.grad.double().cpu() - pos64.grad).abs().max() / pos64.grad.abs().max()
+    assert err < 1e-4, float(err)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("with_pos", [False, True])
+def test_add_layer_norm_fused(cuda_device, with_pos):
+    """LN(a + b) [and LN(a + b) + pos] in one kernel, fwd and bwd against fp32 autograd."""
+    from mmltk_b200.ops import add_layer_norm
+    torch.manual_seed(0)
+    R, C = 2051, 256
+    a = torch.randn(R, C, device=cuda_device)
+    b = torch.randn(R, C, device=cuda_device)
+    p = torch.randn(R, C, device=cuda_device)
+    w = torch.randn(C, device=cuda_device)
+    bias = torch.randn(C, device=cuda_device)
+    leaves = [t.clone().requires_grad_() for t in (a, b, p, w, bias)]
+    a1, b1, p1, w1, bias1 = leaves
+    out = add_layer_norm(a1.bfloat16(), b1.bfloat16(), w1, bias1, 1e-5, pos=p1.bfloat16() if with_pos else None)
+    refs = [t.clone().requires_grad_() for t in (a, b, p, w, bias)]
+    a2, b2, p2, w2, bias2 = refs
+    y_ref = torch.nn.functional.layer_norm(a2 + b2, (C,), w2, bias2, 1e-5)
+    outs_ref = (y_ref, y_ref + p2) if with_pos else (y_ref,)
+    outs = out if with_pos else (out,)
+    for o, r in zip(outs, outs_ref):
+        assert (o.float() - r).abs().max() < 0.06
+    gs = [torch.randn(R, C, device=cuda_device) for _ in outs]
+    torch.autograd.backward([o.float() for o in outs], gs)
+    torch.autograd.backward(list(outs_ref), gs)
+    names = ["a", "b", "pos", "w", "bias"]
+    for n, l, r in zip(names, leaves, refs):
+        if n == "pos" and not with_pos:
+            continue
+        rel = (l.grad - r.grad).abs().max() / r.grad.abs().max()
+        assert rel < 0.03, (n, float(rel))

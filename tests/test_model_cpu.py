@@ -120,6 +120,21 @@ def test_proposals_and_sine_embedding():
     assert e.shape == (3, 7, 256)
 
 
+def test_sine_embedding_matches_interleaved_sin_cos():
+    """sin(v f + phase) form == the reference's interleaved sin / cos of (y, x, w, h)."""
+    import math
+    pos = torch.rand(2, 9, 4, dtype=torch.float64)
+    dim = 64
+    t = 10000.0 ** (2 * (torch.arange(dim, dtype=torch.float64) // 2) / dim)
+    ref = []
+    for c in (1, 0, 2, 3):
+        x = pos[..., c, None] * 2 * math.pi / t
+        ref.append(torch.stack((x[..., 0::2].sin(), x[..., 1::2].cos()), -1).flatten(-2))
+    ref = torch.cat(ref, -1)
+    got = gen_sineembed_for_position(pos, dim).double()
+    assert torch.allclose(got, ref, atol=2e-6)
+
+
 def test_preset_inference_from_paths():
     assert infer_preset_from_path("/w/rf-detr-medium.pth").name == "rf-detr-medium"
     assert infer_preset_from_path("/x/my_seg-2xl_run/checkpoint.pth").name == "rf-detr-seg-xxlarge"
