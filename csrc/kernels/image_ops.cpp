@@ -108,9 +108,41 @@ torch::Tensor sample_packed_masks(torch::Tensor bits, int64_t h, int64_t w, torc
     return out;
 }
 
+// inp [N, C, H, W] (fp32 / bf16), pts [N or 1, P, 2] in [0, 1] (x, y) -> [N, C, P]
+torch::Tensor point_sample(torch::Tensor inp, torch::Tensor pts) {
+    TORCH_CHECK(inp.is_cuda() && inp.dim() == 4, "point_sample: CUDA [N, C, H, W] input");
+    at::cuda::CUDAGuard guard(inp.device());
+    auto x = inp.contiguous();
+    auto p = pts.to(inp.device(), torch::kFloat32).contiguous();
+    const int N = int(x.size(0)), C = int(x.size(1));
+    TORCH_CHECK(p.dim() == 3 && p.size(2) == 2 && (p.size(0) == N || p.size(0) == 1), "point_sample: pts [N|1, P, 2]");
+    const int P = int(p.size(1));
+    auto out = torch::empty({N, C, P}, x.options());
+    check_cuda(launch_point_sample_fwd(dtype_of(x), x.data_ptr(), N, C, int(x.size(2)), int(x.size(3)),
+                                       p.data_ptr<float>(), P, p.size(0) == 1 && N != 1, out.data_ptr(), cur_stream()),
+               "point_sample");
+    return out;
+}
+
+// gradient w.r.t. the input map (fp32 [N, C, H, W])
+torch::Tensor point_sample_bwd(torch::Tensor gout, torch::Tensor pts, int64_t H, int64_t W) {
+    TORCH_CHECK(gout.is_cuda() && gout.dim() == 3, "point_sample_bwd: CUDA [N, C, P] gradient");
+    at::cuda::CUDAGuard guard(gout.device());
+    auto g = gout.contiguous();
+    auto p = pts.to(g.device(), torch::kFloat32).contiguous();
+    const int N = int(g.size(0)), C = int(g.size(1)), P = int(g.size(2));
+    auto gin = torch::zeros({N, C, H, W}, g.options().dtype(torch::kFloat32));
+    check_cuda(launch_point_sample_bwd(dtype_of(g), g.data_ptr(), N, C, int(H), int(W), p.data_ptr<float>(), P,
+                                       p.size(0) == 1 && N != 1, gin.data_ptr<float>(), cur_stream()),
+               "point_sample_bwd");
+    return gin;
+}
+
 }  // namespace
 
 void register_image_ops(pybind11::module& m) {
+    m.def("point_sample", &point_sample, py::arg("inp"), py::arg("pts"));
+    m.def("point_sample_bwd", &point_sample_bwd, py::arg("gout"), py::arg("pts"), py::arg("h"), py::arg("w"));
     m.def("letterbox", &letterbox, py::arg("frame"), py::arg("h"), py::arg("w"), py::arg("bgr") = true,
           py::arg("normalize_bf16") = true);
     m.def("vflip_", &vflip_);

@@ -13,7 +13,10 @@
 //  * resize_masks: batched nearest resize of binary masks (the compiler's mask resize, K16);
 //  * pack_masks / sample_packed: bool masks <-> 64-bit words, and nearest sampling of
 //    packed masks at normalised points (`mask_pack_cuda.cu:11-31`,
-//    `training_mask_ops_cuda.cu:75-159`).
+//    `training_mask_ops_cuda.cu:75-159`);
+//  * point_sample: bilinear sampling of [N, C, H, W] maps at normalised points with zero
+//    padding, align_corners = false (grid_sample semantics), and its input gradient
+//    (`training_mask_ops_cuda.cu:34-73`, K6).
 #include "common.cuh"
 
 namespace mmltk {
@@ -235,6 +238,59 @@ __global__ void sample_packed_kernel(const unsigned long long* __restrict__ bits
     out[i] = v;
 }
 
+
+// ---------------------------------------------------------------- bilinear point sampling
+// Corner (k = 0..3) of point (px, py) in an H x W map: index (or -1 outside) and weight.
+__device__ __forceinline__ void ps_corner(float px, float py, int H, int W, int k, int& idx, float& w) {
+    const float ix = px * W - 0.5f, iy = py * H - 0.5f;
+    const float fx = floorf(ix), fy = floorf(iy);
+    const int x = int(fx) + (k & 1), y = int(fy) + (k >> 1);
+    const float ax = ix - fx, ay = iy - fy;
+    w = ((k & 1) ? ax : 1.f - ax) * ((k >> 1) ? ay : 1.f - ay);
+    idx = (x >= 0 && x < W && y >= 0 && y < H) ? y * W + x : -1;
+}
+
+template <typename T>
+__global__ void point_sample_fwd_kernel(const T* __restrict__ inp, int C, int H, int W, const float* __restrict__ pts,
+                                        int P, int pts_shared, T* __restrict__ out, int64_t total) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int p = int(i % P);
+    const int64_t nc = i / P;
+    const int64_t n = nc / C;
+    const float* q = pts + 2 * ((pts_shared ? 0 : n) * P + p);
+    const T* m = inp + nc * int64_t(H) * W;
+    float v = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        int idx;
+        float w;
+        ps_corner(q[0], q[1], H, W, k, idx, w);
+        if (idx >= 0) v += w * to_f(m[idx]);
+    }
+    out[i] = from_f<T>(v);
+}
+
+template <typename T>
+__global__ void point_sample_bwd_kernel(const T* __restrict__ gout, int C, int H, int W, const float* __restrict__ pts,
+                                        int P, int pts_shared, float* __restrict__ gin, int64_t total) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int p = int(i % P);
+    const int64_t nc = i / P;
+    const int64_t n = nc / C;
+    const float* q = pts + 2 * ((pts_shared ? 0 : n) * P + p);
+    float* g = gin + nc * int64_t(H) * W;
+    const float go = to_f(gout[i]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        int idx;
+        float w;
+        ps_corner(q[0], q[1], H, W, k, idx, w);
+        if (idx >= 0 && w != 0.f) atomicAdd(g + idx, w * go);
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_letterbox(const uint8_t* src, int64_t pitch, int sw, int sh, bool bgr, void* dst, int dw, int dh,
@@ -300,6 +356,28 @@ cudaError_t launch_sample_packed(const uint64_t* bits, int n, int H, int W, cons
     sample_packed_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(
         reinterpret_cast<const unsigned long long*>(bits), words, H, W, pts, P, out, total);
     return cudaGetLastError();
+}
+
+cudaError_t launch_point_sample_fwd(DType t, const void* inp, int N, int C, int H, int W, const float* pts, int P,
+                                    bool pts_shared, void* out, cudaStream_t st) {
+    const int64_t total = int64_t(N) * C * P;
+    if (total == 0) return cudaSuccess;
+    return MMLTK_DISPATCH_DT(t, [&] {
+        point_sample_fwd_kernel<scalar_t><<<unsigned((total + 255) / 256), 256, 0, st>>>(
+            static_cast<const scalar_t*>(inp), C, H, W, pts, P, pts_shared ? 1 : 0, static_cast<scalar_t*>(out), total);
+        return cudaGetLastError();
+    });
+}
+
+cudaError_t launch_point_sample_bwd(DType t, const void* gout, int N, int C, int H, int W, const float* pts, int P,
+                                    bool pts_shared, float* gin, cudaStream_t st) {
+    const int64_t total = int64_t(N) * C * P;
+    if (total == 0) return cudaSuccess;
+    return MMLTK_DISPATCH_DT(t, [&] {
+        point_sample_bwd_kernel<scalar_t><<<unsigned((total + 255) / 256), 256, 0, st>>>(
+            static_cast<const scalar_t*>(gout), C, H, W, pts, P, pts_shared ? 1 : 0, gin, total);
+        return cudaGetLastError();
+    });
 }
 
 }  // namespace mmltk

@@ -22,9 +22,11 @@ cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* 
                                  void* y2 = nullptr);
 // One launch: gx, and gw / gb written (or added into, `accumulate`) by the last CTA.
 // gy2 (optional): a second output gradient added to gy (the y + pos output of the forward).
+// gres (optional): added to gx (the gradient x receives through a residual branch).
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
-                                 bool accumulate, cudaStream_t st, const void* gy2 = nullptr);
+                                 bool accumulate, cudaStream_t st, const void* gy2 = nullptr,
+                                 const void* gres = nullptr);
 
 // ---------------------------------------------------------------- sine position embedding
 // pos [rows, n] fp32 (n = 2 or 4: x, y[, w, h]); out [rows, n * dim] bf16 in block order y, x[, w, h];
@@ -128,6 +130,12 @@ cudaError_t launch_composite(uint8_t* dst, int64_t dpitch, const uint8_t* rgba, 
 cudaError_t launch_resize_masks(const uint8_t* src, int n, int sh, int sw, uint8_t* dst, int dh, int dw,
                                 cudaStream_t st);
 cudaError_t launch_pack_masks(const uint8_t* m, int n, int64_t pixels, uint64_t* out, cudaStream_t st);
+// bilinear, zero padding, align_corners = false; pts [N or 1, P, 2] normalised (x, y); gin fp32 [N, C, H, W]
+// (accumulated: zero it first)
+cudaError_t launch_point_sample_fwd(DType t, const void* inp, int N, int C, int H, int W, const float* pts, int P,
+                                    bool pts_shared, void* out, cudaStream_t st);
+cudaError_t launch_point_sample_bwd(DType t, const void* gout, int N, int C, int H, int W, const float* pts, int P,
+                                    bool pts_shared, float* gin, cudaStream_t st);
 cudaError_t launch_sample_packed(const uint64_t* bits, int n, int H, int W, const float* pts, int P, float* out,
                                  cudaStream_t st);
 

@@ -110,7 +110,15 @@ struct Raw4<float> {
 template <typename T, typename W, int kMaxVec>
 __device__ __forceinline__ void ln_bwd_row(float4 (&xh)[kMaxVec], float4 (&g)[kMaxVec], float mean, float rstd,
                                            const W* __restrict__ w, float4 (&aw)[kMaxVec], float4 (&ab)[kMaxVec],
-                                           T* __restrict__ gxr, int lane, int nv, int C) {
+                                           T* __restrict__ gxr, int lane, int nv, int C,
+                                           const T* __restrict__ gresr) {
+    // the residual gradient is loaded first so its latency hides behind the reductions below
+    Raw4<T> gr[kMaxVec];
+    if (gresr != nullptr) {
+#pragma unroll
+        for (int k = 0; k < kMaxVec; ++k)
+            if (lane + 32 * k < nv) gr[k].load(gresr + 4 * (lane + 32 * k));
+    }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int k = 0; k < kMaxVec; ++k) {
@@ -140,6 +148,10 @@ __device__ __forceinline__ void ln_bwd_row(float4 (&xh)[kMaxVec], float4 (&g)[kM
             o.y = (g[k].y - s1 - xh[k].y * s2) * rstd;
             o.z = (g[k].z - s1 - xh[k].z * s2) * rstd;
             o.w = (g[k].w - s1 - xh[k].w * s2) * rstd;
+            if (gresr != nullptr) {   // gradient reaching x through a residual branch, added here
+                const float4 r4 = gr[k].widen();
+                o.x += r4.x; o.y += r4.y; o.z += r4.z; o.w += r4.w;
+            }
             store4(gxr + 4 * i, o);
         }
     }
@@ -151,7 +163,8 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                                                      const float* __restrict__ rstd_in, T* __restrict__ gx,
                                                      float* acc_w, float* acc_b, unsigned* counter,
                                                      W* __restrict__ gw, W* __restrict__ gb, int accumulate,
-                                                     int64_t rows, int C, const T* __restrict__ gy2) {
+                                                     int64_t rows, int C, const T* __restrict__ gy2,
+                                                     const T* __restrict__ gres) {
     extern __shared__ float smem[];  // [warps][2][C]
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
@@ -208,7 +221,8 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                     }
                 }
             }
-            ln_bwd_row<T, W, kMaxVec>(xv, gv, mean, rstd, w, aw, ab, gx + r * C, lane, nv, C);
+            ln_bwd_row<T, W, kMaxVec>(xv, gv, mean, rstd, w, aw, ab, gx + r * C, lane, nv, C,
+                                      gres != nullptr ? gres + r * C : nullptr);
         }
     } else {
         // wide rows have no registers to spare for a second row
@@ -226,7 +240,8 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                     }
                 }
             }
-            ln_bwd_row<T, W, kMaxVec>(xv, gv, mean_in[r], rstd_in[r], w, aw, ab, gx + r * C, lane, nv, C);
+            ln_bwd_row<T, W, kMaxVec>(xv, gv, mean_in[r], rstd_in[r], w, aw, ab, gx + r * C, lane, nv, C,
+                                      gres != nullptr ? gres + r * C : nullptr);
         }
     }
     // CTA reduction of the per-lane column partials
@@ -343,7 +358,7 @@ int ln_bwd_blocks(K kern, int threads, size_t smem, int64_t rows) {
 
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
-                                 bool accumulate, cudaStream_t st, const void* gy2) {
+                                 bool accumulate, cudaStream_t st, const void* gy2, const void* gres) {
     if (C % 4 != 0 || C > 4 * 32 * 12 || 2 * C > kReduceAccFloats) return cudaErrorInvalidValue;
     const ReduceScratch rs = reduce_scratch();
     if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
@@ -366,7 +381,7 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
                                                     static_cast<const Wt*>(w), mean, rstd, static_cast<T*>(gx), rs.acc,
                                                     rs.acc + C, rs.counters, static_cast<Wt*>(gw),
                                                     static_cast<Wt*>(gb), accumulate ? 1 : 0, rows, C,
-                                                    static_cast<const T*>(gy2));
+                                                    static_cast<const T*>(gy2), static_cast<const T*>(gres));
             });
             if (e != cudaSuccess) return e;
             return cudaGetLastError();

@@ -83,19 +83,20 @@ __global__ void __launch_bounds__(128) matcher_cost_kernel(MatcherLayers lp, con
 }
 
 // ---------------------------------------------------------------- LSAP
-// Problem (l, b, g): rows = the nt targets of image b (nt <= Qg), columns =
-// the Qg queries of group g.  The cost of (row t, column q) is
-// cost[l, b, g*Qg + q, t].  All state lives in shared memory.
+// Problem (l, b, g) over the nt targets of image b and the Qg queries of group g, cost
+// cost[l, b, g*Qg + q, t].  Rows are the shorter side: the targets when nt <= Qg, the queries
+// otherwise (scipy's rectangular_lsap transposes the same way).  All state lives in shared
+// memory; the kernel carves every array with max(Qg, T) entries.
 struct LsapSmem {
-    double* u;     // [T]
-    double* v;     // [Qg]
-    double* spc;   // [Qg]
-    int* path;     // [Qg]
-    int* row4col;  // [Qg]
-    int* rem;      // [Qg]
-    int* col4row;  // [T]
-    unsigned char* sr;  // [T]
-    unsigned char* sc;  // [Qg]
+    double* u;     // [rows]
+    double* v;     // [cols]
+    double* spc;   // [cols]
+    int* path;     // [cols]
+    int* row4col;  // [cols]
+    int* rem;      // [cols]
+    int* col4row;  // [rows]
+    unsigned char* sr;  // [rows]
+    unsigned char* sc;  // [cols]
 };
 
 __host__ __device__ inline size_t lsap_smem_bytes(int Qg, int T) {
@@ -143,11 +144,16 @@ __global__ void __launch_bounds__(128) lsap_kernel(const float* __restrict__ cos
     const int b = (prob / G) % B;
     const int l = prob / (G * B);
     const int Q = Qg * G;
-    LsapSmem s = lsap_carve(lsm + static_cast<size_t>(wib) * lsap_smem_bytes(Qg, T), Qg, T);
+    const int M = Qg > T ? Qg : T;   // every per-row / per-column array holds max(Qg, T) entries
+    LsapSmem s = lsap_carve(lsm + static_cast<size_t>(wib) * lsap_smem_bytes(M, M), M, M);
     int32_t* out = match + ((static_cast<int64_t>(l) * B + b) * G + g) * T;
     for (int t = lane; t < T; t += 32) out[t] = -1;
-    const int nt = min(min(counts[b], T), Qg);
+    const int nt = min(counts[b], T);
     if (nt <= 0) return;
+    // rows are the shorter side (scipy's rectangular LSAP): targets when nt <= Qg (each target gets a
+    // query), queries otherwise (each query gets a target, nt - Qg targets stay unmatched)
+    const bool tr = nt > Qg;
+    const int nr = tr ? Qg : nt, nc = tr ? nt : Qg;
     const float* cbase = cost + ((static_cast<int64_t>(l) * B + b) * Q + static_cast<int64_t>(g) * Qg) * T;
     // sanitize: non-finite -> max finite + max |finite| + 1 (as the host solver)
     double fmax = -INFINITY, amax = 0.0;
@@ -179,31 +185,32 @@ __global__ void __launch_bounds__(128) lsap_kernel(const float* __restrict__ cos
         const double cand = fmax + amax + 1.0;
         if (isfinite(cand)) rep = cand < rep ? cand : rep;
     }
-    auto C = [&](int t, int q) -> double {
+    auto C = [&](int r, int col) -> double {
+        const int q = tr ? r : col, t = tr ? col : r;
         const double c = cbase[static_cast<int64_t>(q) * T + t];
         return (bad && !isfinite(c)) ? rep : c;
     };
 
-    for (int t = lane; t < nt; t += 32) {
-        s.u[t] = 0.0;
-        s.col4row[t] = -1;
+    for (int r = lane; r < nr; r += 32) {
+        s.u[r] = 0.0;
+        s.col4row[r] = -1;
     }
-    for (int q = lane; q < Qg; q += 32) {
-        s.v[q] = 0.0;
-        s.row4col[q] = -1;
-        s.path[q] = -1;
+    for (int c = lane; c < nc; c += 32) {
+        s.v[c] = 0.0;
+        s.row4col[c] = -1;
+        s.path[c] = -1;
     }
     __syncwarp();
     constexpr int kMaxSteps = 1 << 20;  // bound on the inner search (never reached by a valid problem)
-    for (int cur = 0; cur < nt; ++cur) {
-        for (int t = lane; t < nt; t += 32) s.sr[t] = 0;
-        for (int q = lane; q < Qg; q += 32) {
-            s.sc[q] = 0;
-            s.spc[q] = INFINITY;
-            s.rem[q] = Qg - 1 - q;
+    for (int cur = 0; cur < nr; ++cur) {
+        for (int r = lane; r < nr; r += 32) s.sr[r] = 0;
+        for (int c = lane; c < nc; c += 32) {
+            s.sc[c] = 0;
+            s.spc[c] = INFINITY;
+            s.rem[c] = nc - 1 - c;
         }
         __syncwarp();
-        int n_rem = Qg;
+        int n_rem = nc;
         double min_val = 0.0;
         int i = cur;
         int sink = -1;
@@ -258,7 +265,7 @@ __global__ void __launch_bounds__(128) lsap_kernel(const float* __restrict__ cos
                 return;
             }
             const int j = s.rem[best_it];
-            if (j < 0 || j >= Qg) {
+            if (j < 0 || j >= nc) {
                 if (lane == 0) atomicExch(status, 4);
                 return;
             }
@@ -266,7 +273,7 @@ __global__ void __launch_bounds__(128) lsap_kernel(const float* __restrict__ cos
                 sink = j;
             } else {
                 i = s.row4col[j];
-                if (i < 0 || i >= nt) {
+                if (i < 0 || i >= nr) {
                     if (lane == 0) atomicExch(status, 5);
                     return;
                 }
@@ -281,27 +288,27 @@ __global__ void __launch_bounds__(128) lsap_kernel(const float* __restrict__ cos
         }
         // dual updates
         if (lane == 0) s.u[cur] += min_val;
-        for (int t = lane; t < nt; t += 32)
-            if (s.sr[t] && t != cur) {
-                const int c4 = s.col4row[t];
-                if (c4 < 0 || c4 >= Qg) {
+        for (int r = lane; r < nr; r += 32)
+            if (s.sr[r] && r != cur) {
+                const int c4 = s.col4row[r];
+                if (c4 < 0 || c4 >= nc) {
                     atomicExch(status, 8);
                     continue;
                 }
-                s.u[t] += min_val - s.spc[c4];
+                s.u[r] += min_val - s.spc[c4];
             }
-        for (int q = lane; q < Qg; q += 32)
-            if (s.sc[q]) s.v[q] -= min_val - s.spc[q];
+        for (int c = lane; c < nc; c += 32)
+            if (s.sc[c]) s.v[c] -= min_val - s.spc[c];
         __syncwarp();
         if (lane == 0) {
             int j = sink;
-            for (int guard = 0; guard <= nt; ++guard) {
-                if (j < 0 || j >= Qg) {
+            for (int guard = 0; guard <= nr; ++guard) {
+                if (j < 0 || j >= nc) {
                     atomicExch(status, 6);
                     break;
                 }
                 const int r = s.path[j];
-                if (r < 0 || r >= nt) {
+                if (r < 0 || r >= nr) {
                     atomicExch(status, 7);
                     break;
                 }
@@ -314,9 +321,16 @@ __global__ void __launch_bounds__(128) lsap_kernel(const float* __restrict__ cos
         }
         __syncwarp();
     }
-    for (int t = lane; t < nt; t += 32) {
-        const int q = s.col4row[t];
-        out[t] = q >= 0 ? g * Qg + q : -1;
+    if (!tr) {
+        for (int t = lane; t < nt; t += 32) {
+            const int q = s.col4row[t];
+            out[t] = q >= 0 ? g * Qg + q : -1;
+        }
+    } else {
+        for (int q = lane; q < nr; q += 32) {
+            const int t = s.col4row[q];
+            if (t >= 0 && t < nt) out[t] = g * Qg + q;
+        }
     }
 }
 
@@ -341,11 +355,16 @@ cudaError_t launch_matcher_cost(DType lt, DType bt, MatcherLayers lp, int NL, co
     });
 }
 
-size_t lsap_shared_bytes(int Qg, int T, int warps_per_block) { return lsap_smem_bytes(Qg, T) * warps_per_block; }
+// every array of a problem is sized max(Qg, T): rows and columns swap when T > Qg
+size_t lsap_shared_bytes(int Qg, int T, int warps_per_block) {
+    const int M = std::max(Qg, T);
+    return lsap_smem_bytes(M, M) * warps_per_block;
+}
 
 int lsap_warps_per_block(int Qg, int T) {
+    const int M = std::max(Qg, T);
     int wpb = 4;
-    while (wpb > 1 && lsap_smem_bytes(Qg, T) * wpb > 200 * 1024) wpb >>= 1;
+    while (wpb > 1 && lsap_smem_bytes(M, M) * wpb > 200 * 1024) wpb >>= 1;
     return wpb;
 }
 

@@ -83,8 +83,13 @@ std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch
 // gy2: gradient of the forward's y + pos output, added to gy inside the kernel
 std::vector<torch::Tensor> layernorm_bwd(torch::Tensor gy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
                                          torch::Tensor rstd, c10::optional<torch::Tensor> gw_acc,
-                                         c10::optional<torch::Tensor> gb_acc, c10::optional<torch::Tensor> gy2) {
+                                         c10::optional<torch::Tensor> gb_acc, c10::optional<torch::Tensor> gy2,
+                                         c10::optional<torch::Tensor> gres) {
     const bool has_g2 = gy2 && gy2->defined();
+    const bool has_res = gres && gres->defined();
+    if (has_res)
+        TORCH_CHECK(gres->sizes() == x.sizes() && gres->is_contiguous() && gres->scalar_type() == x.scalar_type(),
+                    "layernorm_bwd: gres must match x");
     if (has_g2)
         TORCH_CHECK(gy2->sizes() == x.sizes() && gy2->is_contiguous() && gy2->scalar_type() == x.scalar_type(),
                     "layernorm_bwd: gy2 must match x");
@@ -107,7 +112,8 @@ std::vector<torch::Tensor> layernorm_bwd(torch::Tensor gy, torch::Tensor x, torc
     auto gb = acc ? *gb_acc : torch::empty_like(wc);
     check_cuda(launch_layernorm_bwd(dtype_of(x), dtype_of(w), gy.data_ptr(), x.data_ptr(), wc.data_ptr(),
                                     mean.data_ptr<float>(), rstd.data_ptr<float>(), gx.data_ptr(), gw.data_ptr(),
-                                    gb.data_ptr(), rows, C, acc, cur_stream(), has_g2 ? gy2->data_ptr() : nullptr),
+                                    gb.data_ptr(), rows, C, acc, cur_stream(), has_g2 ? gy2->data_ptr() : nullptr,
+                                    has_res ? gres->data_ptr() : nullptr),
                "layernorm_bwd");
     return {gx, gw, gb};
 }
@@ -223,7 +229,6 @@ std::vector<torch::Tensor> lsap_batched(torch::Tensor cost, torch::Tensor counts
     const int G = static_cast<int>(groups);
     TORCH_CHECK(G >= 1 && Q % G == 0, "lsap_batched: Q must be divisible by groups");
     const int Qg = Q / G;
-    TORCH_CHECK(T <= Qg, "lsap_batched: more target slots than queries per group; use the host solver");
     TORCH_CHECK(lsap_shared_bytes(Qg, T, lsap_warps_per_block(Qg, T)) <= 227 * 1024, "lsap_batched: too large");
     at::cuda::CUDAGuard guard(cost.device());
     auto match = torch::full({NL, B, G, T}, -1, cost.options().dtype(torch::kInt32));
@@ -280,7 +285,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("layernorm_fwd", &mmltk::layernorm_fwd, py::arg("x"), py::arg("w"), py::arg("b"), py::arg("eps"),
           py::arg("res") = py::none(), py::arg("pos") = py::none());
     m.def("layernorm_bwd", &mmltk::layernorm_bwd, py::arg("gy"), py::arg("x"), py::arg("w"), py::arg("mean"),
-          py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none(), py::arg("gy2") = py::none());
+          py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none(), py::arg("gy2") = py::none(),
+          py::arg("gres") = py::none());
     m.def("msda_fwd", &mmltk::msda_fwd);
     m.def("msda_bwd", &mmltk::msda_bwd);
     m.def("matcher_cost", &mmltk::matcher_cost);

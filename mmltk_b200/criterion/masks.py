@@ -15,13 +15,38 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-__all__ = ["point_sample", "uncertain_point_coords", "mask_losses"]
+from ..ops._ext import kernels
+
+__all__ = ["point_sample", "point_sample_reference", "uncertain_point_coords", "mask_losses"]
+
+
+def point_sample_reference(inp: torch.Tensor, coords: torch.Tensor, mode: str = "bilinear") -> torch.Tensor:
+    """``grid_sample`` form (zero padding, align_corners=False): the CPU path and test oracle."""
+    grid = 2.0 * coords[:, :, None, :] - 1.0
+    return F.grid_sample(inp, grid.to(inp.dtype), mode=mode, padding_mode="zeros", align_corners=False)[..., 0]
+
+
+class _PointSampleFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, inp, coords):
+        ctx.save_for_backward(coords)
+        ctx.hw = (inp.shape[-2], inp.shape[-1])
+        ctx.dtype = inp.dtype
+        return kernels().point_sample(inp, coords)
+
+    @staticmethod
+    def backward(ctx, g):
+        (coords,) = ctx.saved_tensors
+        gin = kernels().point_sample_bwd(g, coords, ctx.hw[0], ctx.hw[1])
+        return gin.to(ctx.dtype), None
 
 
 def point_sample(inp: torch.Tensor, coords: torch.Tensor, mode: str = "bilinear") -> torch.Tensor:
-    """inp [N,C,H,W], coords [N,P,2] in [0,1] (x, y) -> [N,C,P]."""
-    grid = 2.0 * coords[:, :, None, :] - 1.0
-    return F.grid_sample(inp, grid.to(inp.dtype), mode=mode, padding_mode="zeros", align_corners=False)[..., 0]
+    """inp [N,C,H,W], coords [N,P,2] in [0,1] (x, y) -> [N,C,P].  Bilinear on CUDA runs the
+    point-sample kernel (one thread per output, 4-corner atomics in backward)."""
+    if mode == "bilinear" and inp.is_cuda and inp.dtype in (torch.float32, torch.bfloat16):
+        return _PointSampleFn.apply(inp, coords)
+    return point_sample_reference(inp, coords, mode)
 
 
 def uncertain_point_coords(logits: torch.Tensor, num_points: int, oversample: int = 3,
@@ -69,8 +94,14 @@ def mask_losses(layer, m, targets, cfg, num_boxes):
         B, G, T = m["valid"].shape
         t_idx = torch.arange(T, device=src.device)[None, None, :].expand(B, G, T)
         rows = (offs[:, None, None] + t_idx).reshape(-1).clamp(max=max(0, targets.masks.shape[0] - 1))
-        tm = targets.masks[rows].float()[:, None]               # [N,1,Hm,Wm]
-        labels = point_sample(tm, coords, mode="nearest")[:, 0]
+        Hm, Wm = targets.masks.shape[-2:]
+        if src.is_cuda:
+            # target masks bit-packed once, then sampled (nearest) at the points: no dense float copies
+            bits = kernels().pack_masks(targets.masks)[rows]
+            labels = kernels().sample_packed_masks(bits, Hm, Wm, coords)
+        else:
+            tm = targets.masks[rows].float()[:, None]           # [N,1,Hm,Wm]
+            labels = point_sample_reference(tm, coords, mode="nearest")[:, 0]
     zero = torch.zeros((), device=src.device)
     ce = F.binary_cross_entropy_with_logits(logits, labels, reduction="none").mean(1)
     p = logits.sigmoid()

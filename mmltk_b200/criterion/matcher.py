@@ -93,8 +93,7 @@ def hungarian_match(logits: List[torch.Tensor], boxes: List[torch.Tensor], targe
     """mask_costs: optional list (one per layer) of [B, Q, T] costs added before the assignment."""
     with torch.no_grad():
         dev = logits[0].device
-        Q = logits[0].shape[1]
-        if dev.type == "cuda" and targets.slots <= Q // groups:
+        if dev.type == "cuda":   # cost build + batched LSAP on the device (any target / query ratio)
             k = kernels()
             cost = k.matcher_cost([l.detach() for l in logits], [b.detach() for b in boxes], targets.labels,
                                   targets.boxes, targets.counts, w_class, w_bbox, w_giou, FOCAL_ALPHA)

@@ -177,14 +177,16 @@ class ViTLayer(nn.Module):
 
     def forward(self, x: torch.Tensor, full_attention: bool) -> torch.Tensor:
         NW, L, C = x.shape
-        h = ops.layer_norm(x, self.norm1.weight, self.norm1.bias, 1e-6)
+        # (LN(x), x) as one node: the residual and the normalised branch's gradients meet in the
+        # LayerNorm backward kernel
+        h, x = ops.layer_norm_with_residual(x, self.norm1.weight, self.norm1.bias, 1e-6)
         if full_attention and self.num_windows > 1:
             w2 = self.num_windows ** 2
             h = h.view(NW // w2, w2 * L, C)
         a = self.attention.attention(h).view(NW, L, C)
         d = self.attention.output.dense
         x = ops.linear_scale_residual(a, d.weight, d.bias, self.layer_scale1.lambda1, x)
-        h = ops.layer_norm(x, self.norm2.weight, self.norm2.bias, 1e-6)
+        h, x = ops.layer_norm_with_residual(x, self.norm2.weight, self.norm2.bias, 1e-6)
         return ops.mlp_scale_residual(h, self.mlp.fc1.weight, self.mlp.fc1.bias, self.mlp.fc2.weight,
                                       self.mlp.fc2.bias, self.layer_scale2.lambda1, x)
 

@@ -15,7 +15,7 @@ import torch.nn.functional as F
 from ._ext import kernels
 from .gradacc import grad_target
 
-__all__ = ["layer_norm", "add_layer_norm"]
+__all__ = ["layer_norm", "add_layer_norm", "layer_norm_with_residual"]
 
 
 class _LayerNormFn(torch.autograd.Function):
@@ -92,3 +92,40 @@ def add_layer_norm(a: torch.Tensor, b: torch.Tensor, weight: torch.Tensor, bias:
         return _AddLayerNormFn.apply(a, b, weight, bias, pos, eps)
     y = F.layer_norm(a + b, (a.shape[-1],), weight.to(a.dtype), bias.to(a.dtype), eps)
     return (y, y + pos) if pos is not None else y
+
+
+class _LayerNormResidualFn(torch.autograd.Function):
+    """(LN(x), x): the pre-norm block's normalised input and its residual stream as ONE node, so
+    the two gradients that reach x are summed inside the LayerNorm backward kernel instead of
+    by a separate add."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        shape = x.shape
+        x2 = x.contiguous().view(-1, shape[-1])
+        y, mean, rstd = kernels().layernorm_fwd(x2, weight, bias, float(eps))[:3]
+        ctx.save_for_backward(x2, weight, mean, rstd)
+        ctx.shape = shape
+        ctx.params = (weight, bias)
+        return y.view(shape), x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, gy, gres):
+        x2, weight, mean, rstd = ctx.saved_tensors
+        gr = gres.contiguous().view(x2.shape) if gres is not None else None
+        if gy is None:
+            return (gres, None, None, None)
+        gy2 = gy.contiguous().view(x2.shape)
+        wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
+        if wt is not None and bt is not None:
+            dx, _, _ = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd, wt, bt, None, gr)
+            return dx.view(ctx.shape), None, None, None
+        dx, dw, db = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd, None, None, None, gr)
+        return dx.view(ctx.shape), dw, db, None
+
+
+def layer_norm_with_residual(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float):
+    """Returns (LN(x), x); use the second output as the block's residual input."""
+    if x.is_cuda and x.shape[-1] % 8 == 0 and x.dtype in (torch.bfloat16, torch.float32) and x.requires_grad:
+        return _LayerNormResidualFn.apply(x, weight, bias, eps)
+    return layer_norm(x, weight, bias, eps), x

@@ -30,6 +30,7 @@ import torch
 
 from ..ckpt import CheckpointMetadata, load_native_checkpoint, save_native_checkpoint
 from ..ckpt.native import state_from_archive, state_to_archive
+from ..ops._ext import native
 from ..config import TrainOptions
 from ..data.augment import GpuAugmenter
 from ..data.loader import BatchLoader, CompiledDataset
@@ -135,8 +136,10 @@ def _check_resume(extra: Dict, opts: TrainOptions) -> None:
 
 
 def evaluate(model_fp32: torch.nn.Module, compiled: str, ctx: DistContext, batch_size: int, max_dets: int,
-             masks: bool, shard: bool = True, with_loss: bool = False) -> Dict:
-    """COCO AP of a model over a compiled split; each rank takes every world-th batch."""
+             masks: bool, shard: bool = True, with_loss: bool = False, sample_png: Optional[str] = None) -> Dict:
+    """COCO AP of a model over a compiled split; each rank takes every world-th batch.
+    ``sample_png``: the main rank also writes its first validation image with the predictions drawn
+    on the GPU (reference: the eval sample image of `train.cpp:158-265`)."""
     from ..eval import CocoEvaluator
     pred = Predictor(model_fp32, device=ctx.device, cuda_graph=ctx.device.type == "cuda", with_masks=masks)
     ev = CocoEvaluator(compiled, masks=masks, max_dets=max_dets)
@@ -151,6 +154,9 @@ def evaluate(model_fp32: torch.nn.Module, compiled: str, ctx: DistContext, batch
         else:
             res = pred(images)
         ev.add(idx, res["scores"], res["labels"], res["boxes"], res.get("masks"))
+        if sample_png and ctx.main:
+            _write_eval_sample(images[0], {k: v[:1] for k, v in res.items()}, bl.dataset.class_names, sample_png)
+            sample_png = None
     # images left over by the per-rank sharding (fewer than one batch per rank) go to rank 0
     n = len(bl.dataset)
     covered = len(bl) * batch_size * (ctx.world_size if shard else 1)
@@ -168,6 +174,15 @@ def evaluate(model_fp32: torch.nn.Module, compiled: str, ctx: DistContext, batch
     if with_loss:
         out["loss"] = validation_loss(pred.model, compiled, ctx, batch_size, shard)
     return out
+
+
+def _write_eval_sample(image_u8, res, class_names, path: str, threshold: float = 0.3) -> None:
+    from ..infer.visualize import draw_detections
+    os.makedirs(os.path.dirname(path) or ".", exist_ok=True)
+    hwc = image_u8.permute(1, 2, 0).contiguous()
+    hwc = draw_detections(hwc, {k: v[0] for k, v in res.items()}, class_names, threshold)
+    with open(path, "wb") as f:
+        f.write(native().encode_png(hwc.cpu()))
 
 
 @torch.no_grad()
@@ -357,7 +372,8 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
         regular = engine.export_model("master")
         t_val = time.monotonic()
         val = evaluate(regular, opts.val_compiled, ctx, val_bs, opts.eval_max_dets, masks,
-                       with_loss=opts.validation_loss)
+                       with_loss=opts.validation_loss,
+                       sample_png=os.path.join(opts.output_dir, "eval_samples", f"epoch_{epoch:04d}.png"))
         _validation_record(opts, paths, ctx, epoch, "regular", val, time.monotonic() - t_val)
         ema_val = None
         ema_model = engine.export_model("ema") if opts.use_ema else None

@@ -52,7 +52,9 @@ def test_train_predict_evaluate_export(data, tmp_path, capsys):
                  str(tmp_path / "x.json")]) == 2
 
 
-def test_train_two_rank_gloo(data, tmp_path):
+def test_train_two_rank_gloo(data, tmp_path, monkeypatch):
+    # CPU ranks over gloo, also on a machine with fewer GPUs than ranks: the children see no GPU
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "")
     out = tmp_path / "ddp"
     argv = ["rfdetr", "train", "--train-compiled", str(data / "train.bin"), "--val-compiled", str(data / "val.bin"),
             "--output-dir", str(out), "--preset", "rf-detr-tiny-test", "--batch-size", "2", "--epochs", "1",

@@ -108,7 +108,8 @@ def test_matcher_cost_and_gpu_lsap(cuda_device):
 def test_gpu_lsap_random_sizes(cuda_device):
     k = kernels()
     rng = np.random.default_rng(3)
-    for (G, Qg, T) in [(1, 7, 7), (3, 100, 40), (13, 300, 10), (2, 33, 1)]:
+    # the last three have more target slots than queries per group (the transposed problem)
+    for (G, Qg, T) in [(1, 7, 7), (3, 100, 40), (13, 300, 10), (2, 33, 1), (2, 5, 12), (1, 3, 40), (4, 10, 11)]:
         B = 3
         cost = torch.from_numpy(rng.normal(size=(2, B, G * Qg, T)).astype(np.float32))
         counts = torch.from_numpy(rng.integers(0, T + 1, size=B).astype(np.int32))
@@ -356,3 +357,52 @@ def test_add_layer_norm_fused(cuda_device, with_pos):
             continue
         rel = (l.grad - r.grad).abs().max() / r.grad.abs().max()
         assert rel < 0.03, (n, float(rel))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_point_sample_matches_grid_sample(cuda_device, dtype):
+    from mmltk_b200.criterion.masks import point_sample, point_sample_reference
+    torch.manual_seed(0)
+    inp = torch.randn(37, 2, 27, 31, device=cuda_device).to(dtype)
+    pts = torch.rand(37, 211, 2, device=cuda_device) * 1.2 - 0.1          # some points outside
+    a = inp.clone().requires_grad_()
+    b = inp.float().clone().requires_grad_()
+    out = point_sample(a, pts)
+    ref = point_sample_reference(b, pts)
+    tol = 1e-5 if dtype == torch.float32 else 3e-2
+    assert (out.float() - ref).abs().max() < tol
+    g = torch.randn_like(ref)
+    out.backward(g.to(dtype))
+    ref.backward(g)
+    assert (a.grad.float() - b.grad).abs().max() < (1e-4 if dtype == torch.float32 else 5e-2)
+
+
+@pytest.mark.gpu
+def test_packed_mask_sampling_matches_nearest_grid_sample(cuda_device):
+    from mmltk_b200.criterion.masks import point_sample_reference
+    from mmltk_b200.ops import kernels
+    torch.manual_seed(0)
+    masks = torch.rand(9, 45, 61, device=cuda_device) > 0.5
+    pts = torch.rand(9, 300, 2, device=cuda_device)
+    got = kernels().sample_packed_masks(kernels().pack_masks(masks), 45, 61, pts)
+    ref = point_sample_reference(masks.float()[:, None], pts, mode="nearest")[:, 0]
+    assert torch.equal(got, ref)
+
+
+@pytest.mark.gpu
+def test_layer_norm_with_residual_sums_both_gradients(cuda_device):
+    """(LN(x), x): dx = LN backward + the residual branch's gradient, in one kernel."""
+    from mmltk_b200.ops import layer_norm_with_residual
+    torch.manual_seed(0)
+    x = torch.randn(1037, 384, device=cuda_device)
+    w, b = torch.randn(384, device=cuda_device), torch.randn(384, device=cuda_device)
+    x1 = x.clone().bfloat16().requires_grad_()
+    h, xr = layer_norm_with_residual(x1, w, b, 1e-6)
+    g1, g2 = torch.randn_like(x), torch.randn_like(x)
+    ((h.float() * g1).sum() + (xr.float() * g2).sum()).backward()
+    x2 = x.clone().requires_grad_()
+    h2 = torch.nn.functional.layer_norm(x2, (384,), w, b, 1e-6)
+    ((h2 * g1).sum() + (x2 * g2).sum()).backward()
+    rel = (x1.grad.float() - x2.grad).abs().max() / x2.grad.abs().max()
+    assert rel < 0.03, float(rel)

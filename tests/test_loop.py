@@ -36,8 +36,10 @@ def test_train_outputs_and_resume(splits, tmp_path):
     out = tmp_path / "run"
     res = run_training(_opts(tr, va, out))
     for f in ("checkpoint.pt", "checkpoint_epoch_1.pt", "checkpoint_epoch_2.pt", "checkpoint_best_regular.pt",
-              "results.json", "log.txt", "progress.json"):
+              "results.json", "log.txt", "progress.json", "eval_samples/epoch_0000.png",
+              "eval_samples/epoch_0001.png"):
         assert os.path.exists(out / f), f
+    assert open(out / "eval_samples" / "epoch_0000.png", "rb").read(8) == b"\x89PNG\r\n\x1a\n"
     assert is_native_checkpoint(str(out / "checkpoint.pt"))
     log = [json.loads(l) for l in open(out / "log.txt")]
     assert [r["epoch"] for r in log] == [0, 1]
