@@ -83,6 +83,8 @@ cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void
 cudaError_t launch_reduce_partials(DType out_t, const float* part, int nparts, int N, void* out, cudaStream_t st);
 // out (+)= acc; acc = 0 (acc: a column sum accumulated by atomics, e.g. in the GEMM epilogue)
 cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bool accumulate, cudaStream_t st);
+// y = GELU(x), erf form.  n % 8 == 0.
+cudaError_t launch_gelu_fwd(DType t, const void* x, void* y, int64_t n, cudaStream_t st);
 // act: 1 = GELU(erf), 2 = ReLU.  n % 8 == 0.
 cudaError_t launch_act_bwd(DType t, const void* gy, const void* pre, void* gx, int64_t n, int act, cudaStream_t st);
 

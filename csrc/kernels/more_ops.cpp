@@ -102,6 +102,15 @@ std::vector<torch::Tensor> act_bwd_bias(torch::Tensor gy, torch::Tensor pre, int
     return {gpre, gb};
 }
 
+torch::Tensor gelu_fwd(torch::Tensor x) {
+    TORCH_CHECK(x.is_cuda(), "gelu_fwd: CUDA tensor expected");
+    at::cuda::CUDAGuard guard(x.device());
+    auto xc = aligned16(x);
+    auto y = torch::empty_like(xc);
+    check_cuda(launch_gelu_fwd(dtype_of(xc), xc.data_ptr(), y.data_ptr(), xc.numel(), cur_stream()), "gelu_fwd");
+    return y;
+}
+
 torch::Tensor act_bwd(torch::Tensor gy, torch::Tensor pre, int64_t act) {
     TORCH_CHECK(gy.sizes() == pre.sizes() && gy.scalar_type() == pre.scalar_type(), "act_bwd: mismatch");
     at::cuda::CUDAGuard guard(gy.device());
@@ -156,6 +165,7 @@ void register_more_ops(pybind11::module& m) {
     m.def("act_bwd_bias", &act_bwd_bias, py::arg("gy"), py::arg("pre"), py::arg("act"),
           py::arg("bias_grad") = py::none(), py::arg("dtype") = py::none());
     m.def("act_bwd", &act_bwd);
+    m.def("gelu_fwd", &gelu_fwd);
     register_ddp_ops(m);
     register_gemm_ops(m);
     register_aug_ops(m);

