@@ -222,9 +222,11 @@ __global__ void __launch_bounds__(256) ddp_update_kernel(DdpPeers peers, DdpStat
         for (int64_t i = cd.offset + 4 * threadIdx.x; i < cd.offset + cd.length; i += 4 * blockDim.x) {
             float4 p = *reinterpret_cast<float4*>(master + i);
             if (finite) {
+                // all operands loaded before use: one memory round trip per iteration
                 const float4 g4 = *reinterpret_cast<const float4*>(gshard + i);
                 float4 mm = *reinterpret_cast<float4*>(m + i);
                 float4 vv = *reinterpret_cast<float4*>(v + i);
+                float4 e = do_ema ? *reinterpret_cast<const float4*>(ema + i) : make_float4(0.f, 0.f, 0.f, 0.f);
                 const float gv[4] = {g4.x * gs, g4.y * gs, g4.z * gs, g4.w * gs};
                 float* pp = &p.x;
                 float* mp = &mm.x;
@@ -240,7 +242,6 @@ __global__ void __launch_bounds__(256) ddp_update_kernel(DdpPeers peers, DdpStat
                 *reinterpret_cast<float4*>(m + i) = mm;
                 *reinterpret_cast<float4*>(v + i) = vv;
                 if (do_ema) {
-                    float4 e = *reinterpret_cast<float4*>(ema + i);
                     e.x = ema_d * e.x + (1.f - ema_d) * p.x;
                     e.y = ema_d * e.y + (1.f - ema_d) * p.y;
                     e.z = ema_d * e.z + (1.f - ema_d) * p.z;

@@ -98,10 +98,13 @@ __global__ void __launch_bounds__(256) adamw_ema_kernel(const ChunkDesc* __restr
         const float lr = gh.lr * sc->lr_scale;
         const float decay = 1.f - lr * gh.weight_decay;
         for (int64_t i = cd.offset + 4 * threadIdx.x; i < cd.offset + cd.length; i += 4 * blockDim.x) {
+            // every operand of this element group is loaded before any is used (one memory
+            // round trip per iteration, the EMA included)
             const float4 gg = load4(grad + i);
             float4 p = *reinterpret_cast<float4*>(master + i);
             float4 mm = *reinterpret_cast<float4*>(m + i);
             float4 vv = *reinterpret_cast<float4*>(v + i);
+            float4 e = do_ema ? *reinterpret_cast<const float4*>(ema + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             const float gs = clip * inv_world;
             float gv[4] = {gg.x * gs, gg.y * gs, gg.z * gs, gg.w * gs};
             float* pp = &p.x;
@@ -119,7 +122,6 @@ __global__ void __launch_bounds__(256) adamw_ema_kernel(const ChunkDesc* __restr
             *reinterpret_cast<float4*>(v + i) = vv;
             store4(param + i, p);
             if (do_ema) {
-                float4 e = *reinterpret_cast<float4*>(ema + i);
                 e.x = ema_d * e.x + (1.f - ema_d) * p.x;
                 e.y = ema_d * e.y + (1.f - ema_d) * p.y;
                 e.z = ema_d * e.z + (1.f - ema_d) * p.z;
@@ -141,7 +143,12 @@ void launch_grad_sumsq(const __nv_bfloat16* grad, int64_t n, float* partials, in
 void launch_adamw_ema(const ChunkDesc* chunks, int nchunks, const __nv_bfloat16* grad, float* master, float* m,
                       float* v, float* ema, __nv_bfloat16* param, const GroupHyper* groups, const StepScalars* sc,
                       const float* partials, int nparts, int* flags, cudaStream_t st) {
-    const int blocks = std::min(nchunks, num_sms() * 4);
+    // one resident wave; blocks stride over the (small) chunks, which balances the work
+    static int per_sm = 0;
+    if (per_sm == 0 && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_ema_kernel, 256, 0) !=
+                            cudaSuccess || per_sm < 1))
+        per_sm = 2;
+    const int blocks = std::min(nchunks, num_sms() * per_sm);
     if (blocks <= 0) return;
     adamw_ema_kernel<<<blocks, 256, 0, st>>>(chunks, nchunks, grad, master, m, v, ema, param, groups, sc, partials,
                                              nparts, flags);

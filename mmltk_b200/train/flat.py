@@ -18,7 +18,8 @@ import torch
 __all__ = ["FlatParams", "ALIGN"]
 
 ALIGN = 64          # elements (128 bytes of bf16)
-CHUNK = 1 << 16     # max elements per chunk-table entry
+CHUNK = 1 << 13     # max elements per chunk-table entry (small: the optimizer's blocks stride over
+                    # chunks, so large tensors split into many chunks keep the blocks balanced)
 
 
 def _round(n: int, a: int = ALIGN) -> int:
