@@ -24,8 +24,9 @@ namespace {
 constexpr int kColThreads = 256;
 constexpr int kSlabCols = 256;     // columns per slab = 32 lanes x 8
 constexpr int kColCtasPerSm = 4;   // resident CTAs per SM (64 registers per thread)
-// rows per row lane with loads in flight together (with the GELU derivative, two fit in 64 registers)
-__host__ __device__ constexpr int col_unroll(int mode) { return mode == 2 ? 2 : 4; }
+// rows per row lane with loads in flight together (two with the GELU derivative or a second sum, to
+// fit 64 registers)
+__host__ __device__ constexpr int col_unroll(int mode) { return mode >= 2 ? 2 : 4; }
 
 __device__ __forceinline__ float gelu_grad(float x) { return gelu_bwd(x); }
 
@@ -81,7 +82,7 @@ struct Raw8<float> {
 template <typename T, int MODE>
 __device__ __forceinline__ void colreduce_row(const T* __restrict__ x, const T* __restrict__ pre,
                                               T* __restrict__ gout, const float* a, const float* p,
-                                              const float* gm, float* acc, int act, int64_t off) {
+                                              const float* gm, float* acc, float* acc2, int act, int64_t off) {
     if constexpr (MODE == 0) {
 #pragma unroll
         for (int c = 0; c < 8; ++c) acc[c] += a[c];
@@ -89,12 +90,17 @@ __device__ __forceinline__ void colreduce_row(const T* __restrict__ x, const T* 
         float o[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            if (MODE == 1) {
+            if (MODE == 1 || MODE == 3) {
                 acc[c] += a[c] * p[c];
                 o[c] = a[c] * gm[c];
             } else {
                 o[c] = act == 1 ? a[c] * gelu_grad(p[c]) : (p[c] > 0.f ? a[c] : 0.f);
             }
+        }
+        if (MODE == 3) {
+            // second column sum: the bias gradient of the scaled product, as stored
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc2[c] += to_f(from_f<T>(o[c]));
         }
         if (MODE == 2) {
             // the bias gradient sums g_pre as stored (rounded to T), i.e. what the GEMMs consume
@@ -105,7 +111,8 @@ __device__ __forceinline__ void colreduce_row(const T* __restrict__ x, const T* 
     }
 }
 
-// MODE 0: colsum(x) ; 1: gout = x * gamma, colsum(x * pre) ; 2: gout = x * act'(pre), colsum(gout)
+// MODE 0: colsum(x) ; 1: gout = x * gamma, colsum(x * pre) ; 2: gout = x * act'(pre), colsum(gout) ;
+// 3: MODE 1 plus a second column sum colsum(gout) into out2 (LayerScale and bias gradients in one pass)
 // Each row lane keeps col_unroll(MODE) rows' loads in flight (issued before any is consumed) and
 // four CTAs share an SM: a memory-bound pass needs tens of KB in flight per SM to cover DRAM
 // latency, which one 16-byte load per thread per iteration does not give.
@@ -114,7 +121,8 @@ __global__ void __launch_bounds__(kColThreads, kColCtasPerSm) colreduce_kernel(c
                                                                    const T* __restrict__ gamma, T* __restrict__ gout,
                                                                    int64_t M, int N, int rows_per_cta, int act,
                                                                    float* acc_buf, unsigned* counters,
-                                                                   TO* __restrict__ out, int accumulate) {
+                                                                   TO* __restrict__ out, int accumulate,
+                                                                   TO* __restrict__ out2, int accumulate2) {
     __shared__ float red[kColThreads * 8];
     __shared__ unsigned s_last;
     const int tid = threadIdx.x, cl = tid & 31, rl = tid >> 5;
@@ -123,8 +131,9 @@ __global__ void __launch_bounds__(kColThreads, kColCtasPerSm) colreduce_kernel(c
     const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
     const int64_t r1 = r0 + rows_per_cta < M ? r0 + rows_per_cta : M;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float acc2[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     float gm[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (MODE == 1 && cols_ok) load8(gamma + col, gm);
+    if ((MODE == 1 || MODE == 3) && cols_ok) load8(gamma + col, gm);
     int64_t r = r0 + rl;
     if (cols_ok) {
         constexpr int U = col_unroll(MODE);
@@ -140,14 +149,14 @@ __global__ void __launch_bounds__(kColThreads, kColCtasPerSm) colreduce_kernel(c
                 float a[8], p[8];
                 ra[u].widen(a);
                 if (MODE != 0) rp[u].widen(p);
-                colreduce_row<T, MODE>(x, pre, gout, a, p, gm, acc, act, (r + 8 * u) * N + col);
+                colreduce_row<T, MODE>(x, pre, gout, a, p, gm, acc, acc2, act, (r + 8 * u) * N + col);
             }
         }
         for (; r < r1; r += 8) {
             float a[8], p[8];
             load8(x + r * N + col, a);
             if (MODE != 0) load8(pre + r * N + col, p);
-            colreduce_row<T, MODE>(x, pre, gout, a, p, gm, acc, act, r * N + col);
+            colreduce_row<T, MODE>(x, pre, gout, a, p, gm, acc, acc2, act, r * N + col);
         }
     }
     if (acc_buf == nullptr) return;   // act_bwd without a bias gradient
@@ -160,6 +169,20 @@ __global__ void __launch_bounds__(kColThreads, kColCtasPerSm) colreduce_kernel(c
             for (int c = 0; c < 8; ++c) acc[c] += red[(q * 32 + cl) * 8 + c];
         atomicAdd(reinterpret_cast<float4*>(acc_buf + col), make_float4(acc[0], acc[1], acc[2], acc[3]));
         atomicAdd(reinterpret_cast<float4*>(acc_buf + col + 4), make_float4(acc[4], acc[5], acc[6], acc[7]));
+    }
+    if constexpr (MODE == 3) {   // the second sum through the same shared buffer, into acc_buf + N
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < 8; ++c) red[tid * 8 + c] = acc2[c];
+        __syncthreads();
+        if (rl == 0 && cols_ok) {
+            for (int q = 1; q < 8; ++q)
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc2[c] += red[(q * 32 + cl) * 8 + c];
+            float* a2 = acc_buf + N;
+            atomicAdd(reinterpret_cast<float4*>(a2 + col), make_float4(acc2[0], acc2[1], acc2[2], acc2[3]));
+            atomicAdd(reinterpret_cast<float4*>(a2 + col + 4), make_float4(acc2[4], acc2[5], acc2[6], acc2[7]));
+        }
     }
     // arrival: the last CTA of this slab writes the result and clears the scratch.  One thread
     // fences after the barrier (the barrier orders the CTA's atomics before it), as in a grid sync.
@@ -177,6 +200,13 @@ __global__ void __launch_bounds__(kColThreads, kColCtasPerSm) colreduce_kernel(c
         write_out8(out + col, s, 8, accumulate != 0);
         *reinterpret_cast<float4*>(acc_buf + col) = make_float4(0.f, 0.f, 0.f, 0.f);
         *reinterpret_cast<float4*>(acc_buf + col + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        if constexpr (MODE == 3) {
+            float* a2 = acc_buf + N;
+            ldcg8(a2 + col, s);
+            write_out8(out2 + col, s, 8, accumulate2 != 0);
+            *reinterpret_cast<float4*>(a2 + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(a2 + col + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
     if (tid == 0) counters[blockIdx.y] = 0u;   // ready for the next launch (and graph replay)
 }
@@ -279,10 +309,11 @@ static int colsum_parts(int64_t M, int N, int mode) {
 
 static cudaError_t launch_colreduce(DType t, DType out_t, int mode, const void* x, const void* pre,
                                     const void* gamma, void* gout, int64_t M, int N, int act, void* out,
-                                    bool accumulate, cudaStream_t st) {
+                                    bool accumulate, cudaStream_t st, void* out2 = nullptr, bool accumulate2 = false) {
     if (N % 8 != 0) return cudaErrorInvalidValue;
     const int slabs = (N + kSlabCols - 1) / kSlabCols;
     if (slabs > kMaxCounters || (out != nullptr && N > kReduceAccFloats)) return cudaErrorInvalidValue;
+    if (mode == 3 && (out2 == nullptr || out == nullptr || 2 * N > kReduceAccFloats)) return cudaErrorInvalidValue;
     const ReduceScratch rs = reduce_scratch();
     if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
     unsigned* counters = rs.counters;
@@ -299,15 +330,20 @@ static cudaError_t launch_colreduce(DType t, DType out_t, int mode, const void* 
             const T* gg = static_cast<const T*>(gamma);
             T* go = static_cast<T*>(gout);
             TO* oo = static_cast<TO*>(out);
+            TO* o2 = static_cast<TO*>(out2);
+            const int a1 = accumulate ? 1 : 0, a2 = accumulate2 ? 1 : 0;
             if (mode == 0)
                 colreduce_kernel<T, 0, TO><<<grid, kColThreads, 0, st>>>(xx, pp, gg, go, M, N, rows_per_cta, act,
-                                                                        acc_buf, counters, oo, accumulate);
+                                                                        acc_buf, counters, oo, a1, o2, a2);
             else if (mode == 1)
                 colreduce_kernel<T, 1, TO><<<grid, kColThreads, 0, st>>>(xx, pp, gg, go, M, N, rows_per_cta, act,
-                                                                        acc_buf, counters, oo, accumulate);
-            else
+                                                                        acc_buf, counters, oo, a1, o2, a2);
+            else if (mode == 2)
                 colreduce_kernel<T, 2, TO><<<grid, kColThreads, 0, st>>>(xx, pp, gg, go, M, N, rows_per_cta, act,
-                                                                        acc_buf, counters, oo, accumulate);
+                                                                        acc_buf, counters, oo, a1, o2, a2);
+            else
+                colreduce_kernel<T, 3, TO><<<grid, kColThreads, 0, st>>>(xx, pp, gg, go, M, N, rows_per_cta, act,
+                                                                        acc_buf, counters, oo, a1, o2, a2);
             return cudaGetLastError();
         });
     });
@@ -317,6 +353,12 @@ cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const v
                           void* gout, int64_t M, int N, void* out, cudaStream_t st, bool accumulate) {
     if (out == nullptr) return cudaErrorInvalidValue;
     return launch_colreduce(t, out_t, mode, x, pre, gamma, gout, M, N, 0, out, accumulate, st);
+}
+
+cudaError_t launch_scale_bias_bwd(DType t, DType out_t, const void* gy, const void* pre, const void* gamma, void* gpre,
+                                  int64_t M, int N, void* ggamma, bool acc_gamma, void* gbias, bool acc_bias,
+                                  cudaStream_t st) {
+    return launch_colreduce(t, out_t, 3, gy, pre, gamma, gpre, M, N, 0, ggamma, acc_gamma, st, gbias, acc_bias);
 }
 
 cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,

@@ -77,6 +77,11 @@ struct ReduceScratch {
 ReduceScratch reduce_scratch();
 cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const void* pre, const void* gamma,
                           void* gout, int64_t M, int N, void* out, cudaStream_t st, bool accumulate = false);
+// LayerScale + bias backward in one pass: gpre = gy * gamma, ggamma (+)= colsum(gy * pre),
+// gbias (+)= colsum(gpre).  2 N <= kReduceAccFloats.
+cudaError_t launch_scale_bias_bwd(DType t, DType out_t, const void* gy, const void* pre, const void* gamma, void* gpre,
+                                  int64_t M, int N, void* ggamma, bool acc_gamma, void* gbias, bool acc_bias,
+                                  cudaStream_t st);
 // gx = gy * act'(pre) and, when gb is given, gb (+)= colsum(gx) in the same pass.
 cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,
                                 int act, void* gb, bool accumulate, cudaStream_t st);

@@ -66,6 +66,30 @@ torch::Tensor colsum(torch::Tensor x, c10::optional<at::ScalarType> out_dtype, c
     return o;
 }
 
+// LayerScale + bias backward in one pass: g_pre = gy * gamma, g_gamma (+)= colsum(gy * pre),
+// g_bias (+)= colsum(g_pre) (bias_grad: accumulation target; bias_dtype: output dtype otherwise)
+std::vector<torch::Tensor> scale_bias_bwd(torch::Tensor gy, torch::Tensor pre, torch::Tensor gamma,
+                                          c10::optional<torch::Tensor> gamma_grad, c10::optional<torch::Tensor> bias_grad,
+                                          c10::optional<at::ScalarType> bias_dtype) {
+    TORCH_CHECK(gy.sizes() == pre.sizes() && gy.dim() == 2, "scale_bias_bwd: shape mismatch");
+    TORCH_CHECK(gamma.scalar_type() == gy.scalar_type(), "scale_bias_bwd: gamma dtype must match");
+    at::cuda::CUDAGuard guard(gy.device());
+    auto g = aligned16(gy), p = aligned16(pre), gm = aligned16(gamma);
+    const int64_t M = g.size(0);
+    const int N = static_cast<int>(g.size(1));
+    auto gpre = torch::empty_like(g);
+    const bool acc_g = gamma_grad && gamma_grad->defined();
+    const bool acc_b = bias_grad && bias_grad->defined();
+    auto ggamma = reduce_target(gamma_grad, N, gamma.options());
+    auto gbias = reduce_target(bias_grad, N, g.options().dtype(bias_dtype.has_value() ? *bias_dtype : g.scalar_type()));
+    TORCH_CHECK(ggamma.scalar_type() == gbias.scalar_type(), "scale_bias_bwd: gamma / bias gradients share a dtype");
+    check_cuda(launch_scale_bias_bwd(dtype_of(g), dtype_of(ggamma), g.data_ptr(), p.data_ptr(), gm.data_ptr(),
+                                     gpre.data_ptr(), M, N, ggamma.data_ptr(), acc_g, gbias.data_ptr(), acc_b,
+                                     cur_stream()),
+               "scale_bias_bwd");
+    return {gpre, ggamma, gbias};
+}
+
 // LayerScale backward: g_pre = gy * gamma, g_gamma (+)= colsum(gy * pre)
 std::vector<torch::Tensor> scale_bwd(torch::Tensor gy, torch::Tensor pre, torch::Tensor gamma,
                                      c10::optional<torch::Tensor> gamma_grad) {
@@ -162,6 +186,8 @@ void register_more_ops(pybind11::module& m) {
     m.def("colsum", &colsum, py::arg("x"), py::arg("out_dtype") = py::none(), py::arg("out") = py::none());
     m.def("scale_bwd", &scale_bwd, py::arg("gy"), py::arg("pre"), py::arg("gamma"),
           py::arg("gamma_grad") = py::none());
+    m.def("scale_bias_bwd", &scale_bias_bwd, py::arg("gy"), py::arg("pre"), py::arg("gamma"),
+          py::arg("gamma_grad") = py::none(), py::arg("bias_grad") = py::none(), py::arg("bias_dtype") = py::none());
     m.def("act_bwd_bias", &act_bwd_bias, py::arg("gy"), py::arg("pre"), py::arg("act"),
           py::arg("bias_grad") = py::none(), py::arg("dtype") = py::none());
     m.def("act_bwd", &act_bwd);

@@ -126,10 +126,14 @@ class _LinearScaleResidual(torch.autograd.Function):
         k = kernels()
         g = _2d(gy, w.shape[0])
         wt, bt, gt = (grad_target(p) for p in ctx.params)
-        g_pre, g_gamma = k.scale_bwd(g, pre, gamma, gt)
+        # LayerScale and bias gradients in the same pass that makes g_pre
+        if (gt is None) == (bt is None) and (bt is None or bt.dtype == gt.dtype):
+            g_pre, g_gamma, gb = k.scale_bias_bwd(g, pre, gamma, gt, bt, gamma.dtype)
+        else:
+            g_pre, g_gamma = k.scale_bwd(g, pre, gamma, gt)
+            gb = k.colsum(g_pre, None, bt)
         gx = gemm_nn(g_pre, w)
         gw = gemm_tn(g_pre, x2) if wt is None else gemm_tn_acc(g_pre, x2, wt)
-        gb = k.colsum(g_pre, None, bt)
         return (gx.view(ctx.shp), None if wt is not None else gw, None if bt is not None else gb,
                 None if gt is not None else g_gamma, gy)
 
@@ -179,8 +183,11 @@ class _MlpScaleResidual(torch.autograd.Function):
         k = kernels()
         wt1, bt1, wt2, bt2, gt = (grad_target(p) for p in ctx.params)
         g = _2d(gy, w2.shape[0])
-        g_pre2, g_gamma = k.scale_bwd(g, pre2, gamma, gt)
-        gb2 = k.colsum(g_pre2, None, bt2)
+        if (gt is None) == (bt2 is None) and (bt2 is None or bt2.dtype == gt.dtype):
+            g_pre2, g_gamma, gb2 = k.scale_bias_bwd(g, pre2, gamma, gt, bt2, gamma.dtype)
+        else:
+            g_pre2, g_gamma = k.scale_bwd(g, pre2, gamma, gt)
+            gb2 = k.colsum(g_pre2, None, bt2)
         gw2 = gemm_tn(g_pre2, h) if wt2 is None else gemm_tn_acc(g_pre2, h, wt2)
         gb1 = bt1 if bt1 is not None else torch.empty(w1.shape[0], device=g.device, dtype=w1.dtype)
         # fc2 input gradient, GELU backward and the fc1 bias gradient in one GEMM launch

@@ -171,3 +171,28 @@ def test_mlp_block_fused_backward_matches_unfused():
         # the fused form applies GELU to the fp32 accumulator, the unfused one to the stored bf16
         # pre-activation: compare at the scale of each tensor
         assert (a - b).abs().max() <= 3e-2 * b.abs().max() + 1e-2, (a - b).abs().max()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_scale_bias_bwd_one_pass(cuda_device, accumulate):
+    """g_pre = gy * gamma, g_gamma = sum(gy * pre), g_bias = sum(g_pre) from one launch."""
+    from mmltk_b200.ops import kernels
+    torch.manual_seed(0)
+    M, N = 5003, 384
+    gy = torch.randn(M, N, device=cuda_device).bfloat16()
+    pre = torch.randn(M, N, device=cuda_device).bfloat16()
+    gamma = torch.randn(N, device=cuda_device).bfloat16()
+    base_g = torch.randn(N, device=cuda_device).bfloat16() if accumulate else None
+    base_b = torch.randn(N, device=cuda_device).bfloat16() if accumulate else None
+    gt = base_g.clone() if accumulate else None
+    bt = base_b.clone() if accumulate else None
+    g_pre, g_gamma, g_bias = kernels().scale_bias_bwd(gy, pre, gamma, gt, bt, gamma.dtype)
+    ref_pre = gy.float() * gamma.float()
+    ref_gamma = (gy.float() * pre.float()).sum(0) + (base_g.float() if accumulate else 0)
+    ref_bias = ref_pre.bfloat16().float().sum(0) + (base_b.float() if accumulate else 0)
+    assert (g_pre.float() - ref_pre).abs().max() < 0.05
+    assert (g_gamma.float() - ref_gamma).abs().max() < 0.02 * ref_gamma.abs().max() + 0.5
+    assert (g_bias.float() - ref_bias).abs().max() < 0.02 * ref_bias.abs().max() + 0.5
+    if accumulate:
+        assert g_gamma.data_ptr() == gt.data_ptr() and g_bias.data_ptr() == bt.data_ptr()
