@@ -248,24 +248,6 @@ __global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, 
     }
 }
 
-template <typename TO>
-__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ part, int nparts, int N,
-                                                              TO* __restrict__ out) {
-    __shared__ float red[8][33];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int col = blockIdx.x * 32 + lane;
-    float s = 0.f;
-    if (col < N)
-        for (int p = w; p < nparts; p += 8) s += part[static_cast<int64_t>(p) * N + col];
-    red[w][lane] = s;
-    __syncthreads();
-    if (w == 0 && col < N) {
-        float t = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) t += red[q][lane];
-        out[col] = from_f<TO>(t);
-    }
-}
 
 // out (+)= acc, then acc = 0 (finishes a column sum accumulated by another kernel's atomics)
 template <typename TO>
@@ -374,12 +356,6 @@ cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bo
     });
 }
 
-cudaError_t launch_reduce_partials(DType out_t, const float* part, int nparts, int N, void* out, cudaStream_t st) {
-    return MMLTK_DISPATCH_DT(out_t, [&] {
-        reduce_partials_kernel<scalar_t><<<(N + 31) / 32, 256, 0, st>>>(part, nparts, N, static_cast<scalar_t*>(out));
-        return cudaGetLastError();
-    });
-}
 
 cudaError_t launch_act_bwd(DType t, const void* gy, const void* pre, void* gx, int64_t n, int act, cudaStream_t st) {
     if (n % 8 != 0) return cudaErrorInvalidValue;

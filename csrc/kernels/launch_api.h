@@ -19,14 +19,16 @@ int num_sms();
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st,
                                  const void* res = nullptr, void* sum = nullptr, const void* pos = nullptr,
-                                 void* y2 = nullptr);
+                                 void* y2 = nullptr, const void* rbias = nullptr);
 // One launch: gx, and gw / gb written (or added into, `accumulate`) by the last CTA.
 // gy2 (optional): a second output gradient added to gy (the y + pos output of the forward).
 // gres (optional): added to gx (the gradient x receives through a residual branch).
+// gbias2 (optional, weight dtype [C]): column sums of gx (before gres) written / added
+// (accumulate2) -- the gradient of a bias fused into the forward's residual input.
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
                                  bool accumulate, cudaStream_t st, const void* gy2 = nullptr,
-                                 const void* gres = nullptr);
+                                 const void* gres = nullptr, void* gbias2 = nullptr, bool accumulate2 = false);
 
 // ---------------------------------------------------------------- sine position embedding
 // pos [rows, n] fp32 (n = 2 or 4: x, y[, w, h]); out [rows, n * dim] bf16 in block order y, x[, w, h];
@@ -85,7 +87,6 @@ cudaError_t launch_scale_bias_bwd(DType t, DType out_t, const void* gy, const vo
 // gx = gy * act'(pre) and, when gb is given, gb (+)= colsum(gx) in the same pass.
 cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,
                                 int act, void* gb, bool accumulate, cudaStream_t st);
-cudaError_t launch_reduce_partials(DType out_t, const float* part, int nparts, int N, void* out, cudaStream_t st);
 // out (+)= acc; acc = 0 (acc: a column sum accumulated by atomics, e.g. in the GEMM epilogue)
 cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bool accumulate, cudaStream_t st);
 // y = GELU(x), erf form.  n % 8 == 0.

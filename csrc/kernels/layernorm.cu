@@ -15,21 +15,22 @@ namespace mmltk {
 
 namespace {
 
-// Optional fusions of the forward: res -> normalise x + res and store the sum; pos -> also
-// store y + pos.
-template <typename T>
+// Optional fusions of the forward: res -> normalise x + res (+ rbias, a bias row vector of the
+// residual branch) and store the sum; pos -> also store y + pos.
+template <typename T, typename W>
 struct LnFwdExtra {
     const T* res;
     T* sum;
     const T* pos;
     T* y2;
+    const W* rbias;
 };
 
 template <typename T, typename W, int kMaxVec>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, const W* __restrict__ w,
                                                      const W* __restrict__ b, T* __restrict__ y,
                                                      float* __restrict__ mean_out, float* __restrict__ rstd_out,
-                                                     int64_t rows, int C, float eps, LnFwdExtra<T> ex) {
+                                                     int64_t rows, int C, float eps, LnFwdExtra<T, W> ex) {
     const int lane = threadIdx.x & 31;
     const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -43,9 +44,14 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, co
             const int i = lane + 32 * k;
             if (i < nv) {
                 v[k] = load4(xr + 4 * i);
-                if (ex.res != nullptr) {   // fused residual add: the norm's input is x + res
+                if (ex.res != nullptr) {   // fused residual add: the norm's input is x + res (+ rbias)
                     const float4 r4 = load4(ex.res + r * C + 4 * i);
                     v[k].x += r4.x; v[k].y += r4.y; v[k].z += r4.z; v[k].w += r4.w;
+                    if (ex.rbias != nullptr) {
+                        const int c0 = 4 * i;
+                        v[k].x += to_f(ex.rbias[c0]); v[k].y += to_f(ex.rbias[c0 + 1]);
+                        v[k].z += to_f(ex.rbias[c0 + 2]); v[k].w += to_f(ex.rbias[c0 + 3]);
+                    }
                     store4(ex.sum + r * C + 4 * i, v[k]);
                 }
                 s += v[k].x + v[k].y + v[k].z + v[k].w;
@@ -107,11 +113,11 @@ struct Raw4<float> {
 };
 
 // one row of the backward pass: xv / gv hold this lane's x and gy columns (fp32)
-template <typename T, typename W, int kMaxVec>
+template <typename T, typename W, int kMaxVec, bool kBias2>
 __device__ __forceinline__ void ln_bwd_row(float4 (&xh)[kMaxVec], float4 (&g)[kMaxVec], float mean, float rstd,
                                            const W* __restrict__ w, float4 (&aw)[kMaxVec], float4 (&ab)[kMaxVec],
-                                           T* __restrict__ gxr, int lane, int nv, int C,
-                                           const T* __restrict__ gresr) {
+                                           float4 (&ad)[kMaxVec], T* __restrict__ gxr, int lane,
+                                           int nv, int C, const T* __restrict__ gresr) {
     // the residual gradient is loaded first so its latency hides behind the reductions below
     Raw4<T> gr[kMaxVec];
     if (gresr != nullptr) {
@@ -148,6 +154,9 @@ __device__ __forceinline__ void ln_bwd_row(float4 (&xh)[kMaxVec], float4 (&g)[kM
             o.y = (g[k].y - s1 - xh[k].y * s2) * rstd;
             o.z = (g[k].z - s1 - xh[k].z * s2) * rstd;
             o.w = (g[k].w - s1 - xh[k].w * s2) * rstd;
+            if constexpr (kBias2) {   // column sums of the input gradient: the fused residual branch's bias gradient
+                ad[k].x += o.x; ad[k].y += o.y; ad[k].z += o.z; ad[k].w += o.w;
+            }
             if (gresr != nullptr) {   // gradient reaching x through a residual branch, added here
                 const float4 r4 = gr[k].widen();
                 o.x += r4.x; o.y += r4.y; o.z += r4.z; o.w += r4.w;
@@ -157,14 +166,15 @@ __device__ __forceinline__ void ln_bwd_row(float4 (&xh)[kMaxVec], float4 (&g)[kM
     }
 }
 
-template <typename T, typename W, int kMaxVec>
+template <typename T, typename W, int kMaxVec, bool kBias2>
 __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, const T* __restrict__ x,
                                                      const W* __restrict__ w, const float* __restrict__ mean_in,
                                                      const float* __restrict__ rstd_in, T* __restrict__ gx,
                                                      float* acc_w, float* acc_b, unsigned* counter,
                                                      W* __restrict__ gw, W* __restrict__ gb, int accumulate,
                                                      int64_t rows, int C, const T* __restrict__ gy2,
-                                                     const T* __restrict__ gres) {
+                                                     const T* __restrict__ gres, W* __restrict__ gbias2,
+                                                     int accumulate2) {
     extern __shared__ float smem[];  // [warps][2][C]
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
@@ -172,11 +182,12 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
     const int64_t warp = static_cast<int64_t>(blockIdx.x) * nwib + wib;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * nwib;
     const int nv = C >> 2;
-    float4 aw[kMaxVec], ab[kMaxVec];
+    float4 aw[kMaxVec], ab[kMaxVec], ad[kMaxVec];
 #pragma unroll
     for (int k = 0; k < kMaxVec; ++k) {
         aw[k] = make_float4(0, 0, 0, 0);
         ab[k] = make_float4(0, 0, 0, 0);
+        ad[k] = make_float4(0, 0, 0, 0);
     }
     if constexpr (kMaxVec <= 6) {
         // the next row's x / gy / statistics are loaded while the current row is reduced and
@@ -221,7 +232,7 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                     }
                 }
             }
-            ln_bwd_row<T, W, kMaxVec>(xv, gv, mean, rstd, w, aw, ab, gx + r * C, lane, nv, C,
+            ln_bwd_row<T, W, kMaxVec, kBias2>(xv, gv, mean, rstd, w, aw, ab, ad, gx + r * C, lane, nv, C,
                                       gres != nullptr ? gres + r * C : nullptr);
         }
     } else {
@@ -240,12 +251,14 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                     }
                 }
             }
-            ln_bwd_row<T, W, kMaxVec>(xv, gv, mean_in[r], rstd_in[r], w, aw, ab, gx + r * C, lane, nv, C,
+            ln_bwd_row<T, W, kMaxVec, kBias2>(xv, gv, mean_in[r], rstd_in[r], w, aw, ab, ad, gx + r * C, lane, nv,
+                                              C,
                                       gres != nullptr ? gres + r * C : nullptr);
         }
     }
-    // CTA reduction of the per-lane column partials
-    float* sw = smem + wib * 2 * C;
+    // CTA reduction of the per-lane column partials ([warps][nacc][C]: gamma, beta[, input])
+    constexpr int nacc = kBias2 ? 3 : 2;
+    float* sw = smem + wib * nacc * C;
     float* sb = sw + C;
 #pragma unroll
     for (int k = 0; k < kMaxVec; ++k) {
@@ -253,21 +266,27 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
         if (i < nv) {
             store4(sw + 4 * i, aw[k]);
             store4(sb + 4 * i, ab[k]);
+            if constexpr (kBias2) store4(sb + C + 4 * i, ad[k]);
         }
     }
     __syncthreads();
     // CTA partials go to the fp32 accumulators with 16-byte atomics (resolved in L2); the last
     // CTA to arrive writes (or adds into) gw / gb and clears the scratch for the next launch
     for (int c4 = threadIdx.x; c4 < nv; c4 += blockDim.x) {
-        float4 a = make_float4(0, 0, 0, 0), bb = make_float4(0, 0, 0, 0);
+        float4 a = make_float4(0, 0, 0, 0), bb = make_float4(0, 0, 0, 0), dd = make_float4(0, 0, 0, 0);
         for (int q = 0; q < nwib; ++q) {
-            const float4 pa = *reinterpret_cast<const float4*>(smem + q * 2 * C + 4 * c4);
-            const float4 pb = *reinterpret_cast<const float4*>(smem + q * 2 * C + C + 4 * c4);
+            const float4 pa = *reinterpret_cast<const float4*>(smem + q * nacc * C + 4 * c4);
+            const float4 pb = *reinterpret_cast<const float4*>(smem + q * nacc * C + C + 4 * c4);
             a.x += pa.x; a.y += pa.y; a.z += pa.z; a.w += pa.w;
             bb.x += pb.x; bb.y += pb.y; bb.z += pb.z; bb.w += pb.w;
+            if constexpr (kBias2) {
+                const float4 pd = *reinterpret_cast<const float4*>(smem + q * nacc * C + 2 * C + 4 * c4);
+                dd.x += pd.x; dd.y += pd.y; dd.z += pd.z; dd.w += pd.w;
+            }
         }
         atomicAdd(reinterpret_cast<float4*>(acc_w + 4 * c4), a);
         atomicAdd(reinterpret_cast<float4*>(acc_b + 4 * c4), bb);
+        if constexpr (kBias2) atomicAdd(reinterpret_cast<float4*>(acc_b + C + 4 * c4), dd);
     }
     // arrival (one thread fences after the barrier, as in a grid sync)
     __shared__ unsigned s_last;
@@ -285,22 +304,13 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
         gb[c] = from_f<W>((accumulate ? to_f(gb[c]) : 0.f) + bb);
         acc_w[c] = 0.f;
         acc_b[c] = 0.f;
+        if constexpr (kBias2) {
+            const float d = __ldcg(acc_b + C + c);
+            gbias2[c] = from_f<W>((accumulate2 ? to_f(gbias2[c]) : 0.f) + d);
+            acc_b[C + c] = 0.f;
+        }
     }
     if (threadIdx.x == 0) *counter = 0u;
-}
-
-template <typename W>
-__global__ void colsum_partials_kernel(const float* __restrict__ pw, const float* __restrict__ pb, int nparts, int C,
-                                       W* __restrict__ gw, W* __restrict__ gb) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= C) return;
-    float a = 0.f, b = 0.f;
-    for (int p = 0; p < nparts; ++p) {
-        a += pw[static_cast<int64_t>(p) * C + c];
-        b += pb[static_cast<int64_t>(p) * C + c];
-    }
-    gw[c] = from_f<W>(a);
-    gb[c] = from_f<W>(b);
 }
 
 template <typename F>
@@ -321,7 +331,8 @@ void dispatch_vec(int C, F&& f) {
 
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st, const void* res,
-                                 void* sum, const void* pos, void* y2) {
+                                 void* sum, const void* pos, void* y2, const void* rbias) {
+    if (rbias != nullptr && res == nullptr) return cudaErrorInvalidValue;
     if ((res == nullptr) != (sum == nullptr) || (pos == nullptr) != (y2 == nullptr)) return cudaErrorInvalidValue;
     if (rows == 0) return cudaSuccess;
     if (C % 4 != 0 || C > 4 * 32 * 12) return cudaErrorInvalidValue;
@@ -335,8 +346,8 @@ cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* 
                 ln_fwd_kernel<T, Wt, decltype(nvl)::value><<<blocks, threads, 0, st>>>(
                     static_cast<const T*>(x), static_cast<const Wt*>(w), static_cast<const Wt*>(b),
                     static_cast<T*>(y), mean, rstd, rows, C, eps,
-                    LnFwdExtra<T>{static_cast<const T*>(res), static_cast<T*>(sum), static_cast<const T*>(pos),
-                                  static_cast<T*>(y2)});
+                    LnFwdExtra<T, Wt>{static_cast<const T*>(res), static_cast<T*>(sum), static_cast<const T*>(pos),
+                                      static_cast<T*>(y2), static_cast<const Wt*>(rbias)});
             });
             return cudaGetLastError();
         });
@@ -358,20 +369,21 @@ int ln_bwd_blocks(K kern, int threads, size_t smem, int64_t rows) {
 
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
-                                 bool accumulate, cudaStream_t st, const void* gy2, const void* gres) {
-    if (C % 4 != 0 || C > 4 * 32 * 12 || 2 * C > kReduceAccFloats) return cudaErrorInvalidValue;
+                                 bool accumulate, cudaStream_t st, const void* gy2, const void* gres, void* gbias2,
+                                 bool accumulate2) {
+    if (C % 4 != 0 || C > 4 * 32 * 12 || 3 * C > kReduceAccFloats) return cudaErrorInvalidValue;
     const ReduceScratch rs = reduce_scratch();
     if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
     const int threads = 256;
     const int nwib = threads / 32;
-    const size_t smem = static_cast<size_t>(nwib) * 2 * C * sizeof(float);
+    const size_t smem = static_cast<size_t>(nwib) * (gbias2 != nullptr ? 3 : 2) * C * sizeof(float);
     return MMLTK_DISPATCH_DT(xt, [&] {
         using T = scalar_t;
         return MMLTK_DISPATCH_DT(wt, [&] {
             using Wt = scalar_t;
             cudaError_t e = cudaSuccess;
-            dispatch_vec(C, [&](auto nvl) {
-                auto kern = ln_bwd_kernel<T, Wt, decltype(nvl)::value>;
+            auto run = [&](auto nvl, auto b2) {
+                auto kern = ln_bwd_kernel<T, Wt, decltype(nvl)::value, decltype(b2)::value>;
                 // the kernel also has a few bytes of static shared memory, so opt in at 48 KB already
                 if (smem >= 40 * 1024)
                     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -381,7 +393,12 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
                                                     static_cast<const Wt*>(w), mean, rstd, static_cast<T*>(gx), rs.acc,
                                                     rs.acc + C, rs.counters, static_cast<Wt*>(gw),
                                                     static_cast<Wt*>(gb), accumulate ? 1 : 0, rows, C,
-                                                    static_cast<const T*>(gy2), static_cast<const T*>(gres));
+                                                    static_cast<const T*>(gy2), static_cast<const T*>(gres),
+                                                    static_cast<Wt*>(gbias2), accumulate2 ? 1 : 0);
+            };
+            dispatch_vec(C, [&](auto nvl) {
+                if (gbias2 != nullptr) run(nvl, std::true_type{});
+                else run(nvl, std::false_type{});
             });
             if (e != cudaSuccess) return e;
             return cudaGetLastError();

@@ -48,11 +48,17 @@ namespace {
 // res: normalise x + res (the sum is returned too); pos: also return y + pos.
 // Returns {y, mean, rstd, sum (or undefined), y + pos (or undefined)}.
 std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps,
-                                         c10::optional<torch::Tensor> res, c10::optional<torch::Tensor> pos) {
+                                         c10::optional<torch::Tensor> res, c10::optional<torch::Tensor> pos,
+                                         c10::optional<torch::Tensor> rbias) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "layernorm_fwd: x must be contiguous [rows, C]");
     TORCH_CHECK(w.scalar_type() == b.scalar_type() && w.numel() == x.size(1) && b.numel() == x.size(1),
                 "layernorm_fwd: weight/bias must match C and share a dtype");
     const bool has_res = res && res->defined(), has_pos = pos && pos->defined();
+    const bool has_rb = rbias && rbias->defined();
+    if (has_rb)
+        TORCH_CHECK(has_res && rbias->numel() == x.size(1) && rbias->is_contiguous() &&
+                        rbias->scalar_type() == w.scalar_type(),
+                    "layernorm_fwd: rbias needs res and must be a contiguous [C] vector of the weight dtype");
     if (has_res)
         TORCH_CHECK(res->sizes() == x.sizes() && res->is_contiguous() && res->scalar_type() == x.scalar_type(),
                     "layernorm_fwd: res must match x");
@@ -74,7 +80,7 @@ std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch
                                     mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C, static_cast<float>(eps),
                                     cur_stream(), has_res ? res->data_ptr() : nullptr,
                                     has_res ? sum.data_ptr() : nullptr, has_pos ? pos->data_ptr() : nullptr,
-                                    has_pos ? y2.data_ptr() : nullptr),
+                                    has_pos ? y2.data_ptr() : nullptr, has_rb ? rbias->data_ptr() : nullptr),
                "layernorm_fwd");
     return {y, mean, rstd, sum, y2};
 }
@@ -84,7 +90,8 @@ std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch
 std::vector<torch::Tensor> layernorm_bwd(torch::Tensor gy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
                                          torch::Tensor rstd, c10::optional<torch::Tensor> gw_acc,
                                          c10::optional<torch::Tensor> gb_acc, c10::optional<torch::Tensor> gy2,
-                                         c10::optional<torch::Tensor> gres) {
+                                         c10::optional<torch::Tensor> gres, bool want_gbias2,
+                                         c10::optional<torch::Tensor> gbias2_acc) {
     const bool has_g2 = gy2 && gy2->defined();
     const bool has_res = gres && gres->defined();
     if (has_res)
@@ -110,12 +117,18 @@ std::vector<torch::Tensor> layernorm_bwd(torch::Tensor gy, torch::Tensor x, torc
     }
     auto gw = acc ? *gw_acc : torch::empty_like(wc);
     auto gb = acc ? *gb_acc : torch::empty_like(wc);
+    const bool acc2 = gbias2_acc && gbias2_acc->defined();
+    if (acc2)
+        TORCH_CHECK(gbias2_acc->is_contiguous() && gbias2_acc->numel() == C && gbias2_acc->scalar_type() == w.scalar_type(),
+                    "layernorm_bwd: gbias2 target must be a contiguous [C] of the weight dtype");
+    torch::Tensor gb2;
+    if (want_gbias2 || acc2) gb2 = acc2 ? *gbias2_acc : torch::empty_like(wc);
     check_cuda(launch_layernorm_bwd(dtype_of(x), dtype_of(w), gy.data_ptr(), x.data_ptr(), wc.data_ptr(),
                                     mean.data_ptr<float>(), rstd.data_ptr<float>(), gx.data_ptr(), gw.data_ptr(),
                                     gb.data_ptr(), rows, C, acc, cur_stream(), has_g2 ? gy2->data_ptr() : nullptr,
-                                    has_res ? gres->data_ptr() : nullptr),
+                                    has_res ? gres->data_ptr() : nullptr, gb2.defined() ? gb2.data_ptr() : nullptr, acc2),
                "layernorm_bwd");
-    return {gx, gw, gb};
+    return {gx, gw, gb, gb2};
 }
 
 // ---------------------------------------------------------------- MSDeformAttn
@@ -283,10 +296,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "mmltk_b200 sm_100a CUDA kernels";
     m.def("num_sms", &mmltk::num_sms);
     m.def("layernorm_fwd", &mmltk::layernorm_fwd, py::arg("x"), py::arg("w"), py::arg("b"), py::arg("eps"),
-          py::arg("res") = py::none(), py::arg("pos") = py::none());
+          py::arg("res") = py::none(), py::arg("pos") = py::none(), py::arg("rbias") = py::none());
     m.def("layernorm_bwd", &mmltk::layernorm_bwd, py::arg("gy"), py::arg("x"), py::arg("w"), py::arg("mean"),
           py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none(), py::arg("gy2") = py::none(),
-          py::arg("gres") = py::none());
+          py::arg("gres") = py::none(), py::arg("want_gbias2") = false, py::arg("gbias2_acc") = py::none());
     m.def("msda_fwd", &mmltk::msda_fwd);
     m.def("msda_bwd", &mmltk::msda_bwd);
     m.def("matcher_cost", &mmltk::matcher_cost);

@@ -93,7 +93,9 @@ class MSDeformAttn(nn.Module):
             nn.init.xavier_uniform_(self.output_proj.weight)
             self.output_proj.bias.zero_()
 
-    def forward(self, query, ref, value_in, shapes, padding_mask=None):
+    def forward(self, query, ref, value_in, shapes, padding_mask=None, defer_bias: bool = False):
+        """``defer_bias``: return (output without the output projection's bias, that bias) for a
+        consumer that adds it itself (the decoder's fused residual + norm)."""
         B, Lq, _ = query.shape
         S = value_in.shape[1]
         H, L, P = self.n_heads, self.n_levels, self.n_points
@@ -104,6 +106,8 @@ class MSDeformAttn(nn.Module):
         off = ops.linear(query, self.sampling_offsets.weight, self.sampling_offsets.bias).view(B, Lq, H, L, P, 2)
         logits = ops.linear(query, self.attention_weights.weight, self.attention_weights.bias).view(B, Lq, H, L * P)
         out = ops.msda(value, shapes, ref, off, logits)
+        if defer_bias:
+            return ops.linear(out.to(query.dtype), self.output_proj.weight, None), self.output_proj.bias
         return ops.linear(out.to(query.dtype), self.output_proj.weight, self.output_proj.bias)
 
 
@@ -136,21 +140,25 @@ class DecoderLayer(nn.Module):
         k = kh.reshape(B * groups, Qg, H, Dh).transpose(1, 2)
         vv = v.reshape(B * groups, Qg, H, Dh).transpose(1, 2)
         o = ops.attention(q, k, vv).transpose(1, 2).reshape(B, Q, d)
-        return ops.linear(o, self.self_attn.out_proj.weight, self.self_attn.out_proj.bias)
+        # the output projection's bias is added (and its gradient reduced) by the following norm
+        return ops.linear(o, self.self_attn.out_proj.weight, None), self.self_attn.out_proj.bias
 
     def forward(self, tgt, query_pos, ref, memory, shapes, padding_mask, groups, tgt_pos=None, want_pos=False):
         """Post-norm layer.  ``tgt_pos`` = tgt + query_pos when the caller has it already;
         ``want_pos`` also returns out + query_pos (the next layer's self-attention input), made by
         the last norm's kernel.  Residual adds are fused into the norms."""
-        sa = self._self_attention(tgt, query_pos, groups, tgt_pos)
-        x, x_pos = ops.add_layer_norm(tgt, sa, self.norm1.weight, self.norm1.bias, 1e-5, pos=query_pos)
-        ca = self.cross_attn(x_pos, ref, memory, shapes, padding_mask)
-        x = ops.add_layer_norm(x, ca, self.norm2.weight, self.norm2.bias, 1e-5)
+        # each branch's last linear runs without its bias; the fused add + norm adds it and reduces
+        # its gradient in the norm's backward kernel
+        sa, sa_b = self._self_attention(tgt, query_pos, groups, tgt_pos)
+        x, x_pos = ops.add_layer_norm(tgt, sa, self.norm1.weight, self.norm1.bias, 1e-5, pos=query_pos, rbias=sa_b)
+        ca, ca_b = self.cross_attn(x_pos, ref, memory, shapes, padding_mask, defer_bias=True)
+        x = ops.add_layer_norm(x, ca, self.norm2.weight, self.norm2.bias, 1e-5, rbias=ca_b)
         h = ops.linear(x, self.linear1.weight, self.linear1.bias, act="relu")
-        h = ops.linear(h, self.linear2.weight, self.linear2.bias)
+        h = ops.linear(h, self.linear2.weight, None)
         if want_pos:
-            return ops.add_layer_norm(x, h, self.norm3.weight, self.norm3.bias, 1e-5, pos=query_pos)
-        return ops.add_layer_norm(x, h, self.norm3.weight, self.norm3.bias, 1e-5)
+            return ops.add_layer_norm(x, h, self.norm3.weight, self.norm3.bias, 1e-5, pos=query_pos,
+                                      rbias=self.linear2.bias)
+        return ops.add_layer_norm(x, h, self.norm3.weight, self.norm3.bias, 1e-5, rbias=self.linear2.bias)
 
 
 class Decoder(nn.Module):

@@ -35,9 +35,9 @@ class _LayerNormFn(torch.autograd.Function):
         gy2 = gy.contiguous().view(x2.shape)
         wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
         if wt is not None and bt is not None:   # weight / bias gradients added straight into .grad
-            dx, _, _ = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd, wt, bt)
+            dx = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd, wt, bt)[0]
             return dx.view(ctx.shape), None, None, None
-        dx, dw, db = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd)
+        dx, dw, db = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd)[:3]
         return dx.view(ctx.shape), dw, db, None
 
 
@@ -48,19 +48,23 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: f
 
 
 class _AddLayerNormFn(torch.autograd.Function):
-    """y = LN(a + b) [, y + pos] in one kernel; the sum is stored for the backward."""
+    """y = LN(a + b [+ rbias]) [, y + pos] in one kernel; the sum is stored for the backward.
+    ``rbias`` is the bias of the linear that produced ``b`` (that linear runs without it): its
+    gradient, the column sums of the norm's input gradient, comes out of the same backward
+    kernel instead of a separate reduction."""
 
     @staticmethod
-    def forward(ctx, a, b, weight, bias, pos, eps):
+    def forward(ctx, a, b, weight, bias, pos, rbias, eps):
         shape = a.shape
         C = shape[-1]
         a2 = a.contiguous().view(-1, C)
         b2 = b.contiguous().view(-1, C)
         p2 = pos.contiguous().view(-1, C) if pos is not None else None
-        y, mean, rstd, s, y2 = kernels().layernorm_fwd(a2, weight, bias, float(eps), b2, p2)
+        rb = rbias.to(weight.dtype).contiguous() if rbias is not None else None
+        y, mean, rstd, s, y2 = kernels().layernorm_fwd(a2, weight, bias, float(eps), b2, p2, rb)
         ctx.save_for_backward(s, weight, mean, rstd)
         ctx.shape = shape
-        ctx.params = (weight, bias)
+        ctx.params = (weight, bias, rbias)
         ctx.has_pos = pos is not None
         if ctx.has_pos:
             return y.view(shape), y2.view(shape)
@@ -71,26 +75,39 @@ class _AddLayerNormFn(torch.autograd.Function):
         s, weight, mean, rstd = ctx.saved_tensors
         gy = gy.contiguous().view(s.shape) if gy is not None else torch.zeros_like(s)
         g2 = gy2.contiguous().view(s.shape) if (ctx.has_pos and gy2 is not None) else None
-        wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
-        if wt is not None and bt is not None:
-            dx, dw, db = kernels().layernorm_bwd(gy, s, weight, mean, rstd, wt, bt, g2)
+        w_p, b_p, rb_p = ctx.params
+        wt, bt = grad_target(w_p), grad_target(b_p)
+        rbt = grad_target(rb_p) if rb_p is not None else None
+        want_rb = rb_p is not None and ctx.needs_input_grad[5]
+        rb_ok = rbt is None or rbt.dtype == weight.dtype
+        accumulate = wt is not None and bt is not None
+        dx, dw, db, drb = kernels().layernorm_bwd(gy, s, weight, mean, rstd, wt if accumulate else None,
+                                                  bt if accumulate else None, g2, None, want_rb,
+                                                  rbt if (want_rb and rb_ok) else None)
+        if accumulate:
             dw = db = None
+        if want_rb and rbt is not None and rb_ok:
+            drb = None                                # added into the bias' .grad by the kernel
+        elif want_rb and drb is not None:
+            drb = drb.to(rb_p.dtype)
         else:
-            dx, dw, db = kernels().layernorm_bwd(gy, s, weight, mean, rstd, None, None, g2)
+            drb = None
         dx = dx.view(ctx.shape)
         gpos = gy2.view(ctx.shape) if g2 is not None else None
-        return dx, dx, dw, db, gpos, None
+        return dx, dx, dw, db, gpos, drb, None
 
 
 def add_layer_norm(a: torch.Tensor, b: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float,
-                   pos: torch.Tensor = None):
-    """LN(a + b), and with ``pos`` also LN(a + b) + pos -- the post-norm residual of a decoder
-    layer and the next query (with its position embedding) in one pass."""
+                   pos: torch.Tensor = None, rbias: torch.Tensor = None):
+    """LN(a + b [+ rbias]), and with ``pos`` also that + pos -- the post-norm residual of a decoder
+    layer and the next query (with its position embedding) in one pass.  ``rbias``: the bias of
+    the linear that produced ``b``, when that linear was run without it."""
     if (a.is_cuda and a.shape[-1] % 8 == 0 and a.dtype in (torch.bfloat16, torch.float32)
             and b.dtype == a.dtype and b.shape == a.shape and (pos is None or (pos.dtype == a.dtype
                                                                              and pos.shape == a.shape))):
-        return _AddLayerNormFn.apply(a, b, weight, bias, pos, eps)
-    y = F.layer_norm(a + b, (a.shape[-1],), weight.to(a.dtype), bias.to(a.dtype), eps)
+        return _AddLayerNormFn.apply(a, b, weight, bias, pos, rbias, eps)
+    x = a + b if rbias is None else a + b + rbias.to(a.dtype)
+    y = F.layer_norm(x, (a.shape[-1],), weight.to(a.dtype), bias.to(a.dtype), eps)
     return (y, y + pos) if pos is not None else y
 
 
@@ -118,9 +135,9 @@ class _LayerNormResidualFn(torch.autograd.Function):
         gy2 = gy.contiguous().view(x2.shape)
         wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
         if wt is not None and bt is not None:
-            dx, _, _ = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd, wt, bt, None, gr)
+            dx = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd, wt, bt, None, gr)[0]
             return dx.view(ctx.shape), None, None, None
-        dx, dw, db = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd, None, None, None, gr)
+        dx, dw, db = kernels().layernorm_bwd(gy2, x2, weight, mean, rstd, None, None, None, gr)[:3]
         return dx.view(ctx.shape), dw, db, None
 
 

@@ -329,9 +329,9 @@ def test_sine_embed_fwd_bwd(cuda_device, n):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("with_pos", [False, True])
-def test_add_layer_norm_fused(cuda_device, with_pos):
-    """LN(a + b) [and LN(a + b) + pos] in one kernel, fwd and bwd against fp32 autograd."""
+@pytest.mark.parametrize("with_pos,with_rbias", [(False, False), (True, False), (True, True), (False, True)])
+def test_add_layer_norm_fused(cuda_device, with_pos, with_rbias):
+    """LN(a + b [+ rbias]) [and that + pos] in one kernel, fwd and bwd against fp32 autograd."""
     from mmltk_b200.ops import add_layer_norm
     torch.manual_seed(0)
     R, C = 2051, 256
@@ -340,12 +340,14 @@ def test_add_layer_norm_fused(cuda_device, with_pos):
     p = torch.randn(R, C, device=cuda_device)
     w = torch.randn(C, device=cuda_device)
     bias = torch.randn(C, device=cuda_device)
-    leaves = [t.clone().requires_grad_() for t in (a, b, p, w, bias)]
-    a1, b1, p1, w1, bias1 = leaves
-    out = add_layer_norm(a1.bfloat16(), b1.bfloat16(), w1, bias1, 1e-5, pos=p1.bfloat16() if with_pos else None)
-    refs = [t.clone().requires_grad_() for t in (a, b, p, w, bias)]
-    a2, b2, p2, w2, bias2 = refs
-    y_ref = torch.nn.functional.layer_norm(a2 + b2, (C,), w2, bias2, 1e-5)
+    rb = torch.randn(C, device=cuda_device)
+    leaves = [t.clone().requires_grad_() for t in (a, b, p, w, bias, rb)]
+    a1, b1, p1, w1, bias1, rb1 = leaves
+    out = add_layer_norm(a1.bfloat16(), b1.bfloat16(), w1, bias1, 1e-5, pos=p1.bfloat16() if with_pos else None,
+                         rbias=rb1 if with_rbias else None)
+    refs = [t.clone().requires_grad_() for t in (a, b, p, w, bias, rb)]
+    a2, b2, p2, w2, bias2, rb2 = refs
+    y_ref = torch.nn.functional.layer_norm(a2 + b2 + (rb2 if with_rbias else 0), (C,), w2, bias2, 1e-5)
     outs_ref = (y_ref, y_ref + p2) if with_pos else (y_ref,)
     outs = out if with_pos else (out,)
     for o, r in zip(outs, outs_ref):
@@ -353,9 +355,9 @@ def test_add_layer_norm_fused(cuda_device, with_pos):
     gs = [torch.randn(R, C, device=cuda_device) for _ in outs]
     torch.autograd.backward([o.float() for o in outs], gs)
     torch.autograd.backward(list(outs_ref), gs)
-    names = ["a", "b", "pos", "w", "bias"]
+    names = ["a", "b", "pos", "w", "bias", "rbias"]
     for n, l, r in zip(names, leaves, refs):
-        if n == "pos" and not with_pos:
+        if (n == "pos" and not with_pos) or (n == "rbias" and not with_rbias):
             continue
         rel = (l.grad - r.grad).abs().max() / r.grad.abs().max()
         assert rel < 0.03, (n, float(rel))
