@@ -58,10 +58,31 @@ def gemm_nt(a: torch.Tensor, b: torch.Tensor, bias=None) -> torch.Tensor:
     return torch.addmm(bias, a, b.t())
 
 
-def gemm_nt_epilogue(a, b, bias, epi: str, res=None, gamma=None, want_pre: bool = True):
+_SMS = {}
+
+
+def num_sms() -> int:
+    """Multiprocessors of the current device (cached per device)."""
+    d = torch.cuda.current_device()
+    if d not in _SMS:
+        _SMS[d] = torch.cuda.get_device_properties(d).multi_processor_count
+    return _SMS[d]
+
+
+def _fills_gpu(M: int, N: int) -> bool:
+    """True when a 128 x 128 tiling of the output gives at least half a wave of CTAs: below that
+    (batch-1 inference shapes) the persistent one-tile-per-CTA GEMM leaves most SMs idle, and the
+    library GEMM plus one elementwise pass is faster."""
+    tiles = ((M + 127) // 128) * ((N + 127) // 128)
+    return tiles * 2 >= num_sms()
+
+
+def gemm_nt_epilogue(a, b, bias, epi: str, res=None, gamma=None, want_pre: bool = True, force: bool = False):
     """(out, pre) with out = act(a b^T + bias) or res + gamma * (a b^T + bias); pre = a b^T + bias
-    (None unless ``want_pre``).  Returns None when the shape does not fit the tensor-core kernel."""
-    if not _fits_nt(a, b):
+    (None unless ``want_pre``).  Returns None when the shape does not fit the tensor-core kernel
+    (or, unless ``force``, is too small to fill the GPU with it); the caller then runs the library
+    GEMM."""
+    if not _fits_nt(a, b) or not (force or _fills_gpu(a.shape[0], b.shape[0])):
         return None
     r = kernels().gemm_tc(a, b, bias, False, False, EPI[epi], want_pre, res, gamma)
     return r[0], (r[1] if want_pre else None)

@@ -170,8 +170,8 @@ class _MlpScaleResidual(torch.autograd.Function):
         shp = x.shape
         x2 = _2d(x, shp[-1])
         r2 = _2d(res, w2.shape[0])
-        h, pre1 = gemm_nt_epilogue(x2, w1, b1, "gelu")
-        y, pre2 = gemm_nt_epilogue(h, w2, b2, "scale_residual", r2, gamma)
+        h, pre1 = gemm_nt_epilogue(x2, w1, b1, "gelu", force=True)
+        y, pre2 = gemm_nt_epilogue(h, w2, b2, "scale_residual", r2, gamma, force=True)
         ctx.save_for_backward(x2, w1, pre1, h, w2, gamma, pre2)
         ctx.params = (w1, b1, w2, b2, gamma)
         ctx.shp = shp

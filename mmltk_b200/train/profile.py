@@ -58,6 +58,47 @@ def origin_table(events, steps: int, top: int, shapes: bool = False, stack: bool
     return "\n".join(lines)
 
 
+def _kernel_table(events, steps: int, top: int) -> str:
+    per = collections.Counter()
+    count = collections.Counter()
+    for ev in events:
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            per[ev.name] += ev.device_time
+            count[ev.name] += 1
+    total = sum(per.values()) or 1.0
+    lines = [f"CUDA time {total / 1e3 / steps:.3f} ms/step over {steps} eager steps "
+             f"({sum(count.values()) // steps} kernels/step)\n",
+             "| share | ms/step | launches/step | kernel |", "|---|---|---|---|"]
+    for name, t in per.most_common(top):
+        lines.append(f"| {100 * t / total:.1f}% | {t / 1e3 / steps:.4f} | {count[name] // steps} | `{name[:110]}` |")
+    return "\n".join(lines)
+
+
+def _profile_infer(a) -> int:
+    """Eager forward of the inference Predictor (kernel table), then its CUDA-graph latency."""
+    from torch.profiler import ProfilerActivity, profile
+
+    from ..infer import Predictor
+    from ..models.rfdetr import build_model
+    torch.manual_seed(0)
+    model = build_model(a.preset).eval()
+    dev = torch.device("cuda", 0)
+    pred = Predictor(model, device=dev, cuda_graph=False)
+    x = torch.randint(0, 256, (a.batch_size, 3, *pred.size), dtype=torch.uint8, device=dev)
+    for _ in range(a.warmup):
+        pred(x)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(a.steps):
+            pred(x)
+        torch.cuda.synchronize()
+    print(f"# {a.preset} inference, batch {a.batch_size}, {pred.size[0]}x{pred.size[1]}, bf16\n")
+    print(_kernel_table(prof.events(), a.steps, a.top))
+    g = Predictor(model, device=dev, cuda_graph=True)
+    print(f"\nCUDA-graph latency: {g.latency(200, 20, a.batch_size)}")
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--preset", default="rf-detr-medium")
@@ -70,10 +111,14 @@ def main(argv=None) -> int:
     ap.add_argument("--by-origin", action="store_true",
                     help="rank (aten op, enclosing autograd node or autograd Function) pairs by CUDA time")
     ap.add_argument("--stack", action="store_true", help="with --by-origin: name forward ops by source line")
+    ap.add_argument("--infer", action="store_true",
+                    help="profile the inference Predictor (eval model, uint8 input -> top-k results) instead")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         print("profile: needs a GPU", file=sys.stderr)
         return 2
+    if a.infer:
+        return _profile_infer(a)
     from ..config import TrainOptions
     from ..data.synthetic import synthetic_batch
     from ..models.rfdetr import build_model
