@@ -299,7 +299,10 @@ class E2EPipeline:
         from mmltk_b200.data.loader import BatchLoader
         from mmltk_b200.data.source import write_synthetic_source
         res = cfg.resolution
+        import atexit
+        import shutil
         root = tempfile.mkdtemp(prefix=f"mmltk_bench_r{rank}_")
+        atexit.register(shutil.rmtree, root, True)     # the synthetic dataset is scratch
         write_synthetic_source(os.path.join(root, "src"), splits=("train",), images=images_per_rank,
                                size=(res, res), classes=min(80, cfg.num_classes - 1), max_instances=slots - 1,
                                seed=1000 + rank)

@@ -225,25 +225,25 @@ __global__ void __launch_bounds__(256) act_bwd_kernel(const T* __restrict__ gy, 
     }
 }
 
-// y = GELU(x) (erf form), 8 elements per vector, two vectors in flight per thread
+// y = GELU(x) (erf form), 8 elements per vector, four vectors in flight per thread
 template <typename T>
 __global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n8) {
+    constexpr int U = 4;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += 2 * stride) {
-        const int64_t j = i + stride;
-        Raw8<T> ra, rb;
-        ra.load(x + 8 * i);
-        if (j < n8) rb.load(x + 8 * j);
-        float a[8], o[8];
-        ra.widen(a);
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += U * stride) {
+        Raw8<T> r[U];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) o[c] = gelu_fwd(a[c]);
-        store8(y + 8 * i, o);
-        if (j < n8) {
-            rb.widen(a);
+        for (int u = 0; u < U; ++u)
+            if (i + u * stride < n8) r[u].load(x + 8 * (i + u * stride));
 #pragma unroll
-            for (int c = 0; c < 8; ++c) o[c] = gelu_fwd(a[c]);
-            store8(y + 8 * j, o);
+        for (int u = 0; u < U; ++u) {
+            if (i + u * stride < n8) {
+                float a[8], o[8];
+                r[u].widen(a);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) o[c] = gelu_fwd(a[c]);
+                store8(y + 8 * (i + u * stride), o);
+            }
         }
     }
 }
@@ -373,7 +373,7 @@ cudaError_t launch_gelu_fwd(DType t, const void* x, void* y, int64_t n, cudaStre
     if (n % 8 != 0) return cudaErrorInvalidValue;
     const int64_t n8 = n / 8;
     if (n8 == 0) return cudaSuccess;
-    const int blocks = static_cast<int>(std::min<int64_t>((n8 + 511) / 512, static_cast<int64_t>(num_sms()) * 8));
+    const int blocks = static_cast<int>(std::min<int64_t>((n8 + 1023) / 1024, static_cast<int64_t>(num_sms()) * 8));
     return MMLTK_DISPATCH_DT(t, [&] {
         using T = scalar_t;
         gelu_fwd_kernel<T><<<std::max(blocks, 1), 256, 0, st>>>(static_cast<const T*>(x), static_cast<T*>(y), n8);

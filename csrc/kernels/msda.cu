@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(256) msda_fwd_kernel(const T* __restrict__ val
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(256) msda_bwd_kernel(const T* __restrict__ gout, const T* __restrict__ value,
+__global__ void __launch_bounds__(256, 3) msda_bwd_kernel(const T* __restrict__ gout, const T* __restrict__ value,
                                                        const int* __restrict__ shapes, const int* __restrict__ starts,
                                                        const T* __restrict__ ref, const T* __restrict__ off,
                                                        const T* __restrict__ logits, float* __restrict__ gvalue,
