@@ -22,6 +22,9 @@ CPU path and the oracle of the kernel tests.
 """
 from __future__ import annotations
 
+import json
+import os
+
 from typing import List, Optional, Sequence, Tuple
 
 import torch
@@ -39,6 +42,8 @@ IMAGENET_MEAN = (0.485, 0.456, 0.406)
 IMAGENET_STD = (0.229, 0.224, 0.225)
 
 # record offsets (csrc/host/augment.h)
+_TRACE_FILE = os.environ.get("MMLTK_AUGMENT_TRACE_FILE", "")
+
 REC = dict(inv=0, fwd=6, color=12, color_off=21, noise_mode=24, noise_str=25, blur=26, occ_mode=27, occ_str=28,
            occ_chan=29, erase=30, area_scale=34, flags=35, paste_slot=36, paste_mode=37, paste_inv=38, noise_key=44,
            paste_box=45, floats=64)
@@ -277,7 +282,27 @@ class GpuAugmenter:
         st["n"] = n
         st["pairs"] = len(pairs)
         st["replace"] = list(self.planner.replacements())
+        if _TRACE_FILE:
+            self._trace(indices, epoch, sequence, st)
         return st
+
+    def _trace(self, indices, epoch: int, sequence: int, st: dict) -> None:
+        """One JSONL record per batch (env ``MMLTK_AUGMENT_TRACE_FILE``; reference
+        `src/rfdetr/gpu_augment.cpp:268-273`): the planned parameters of every image."""
+        rec = st["rec"][:st["n"]]
+        imgs = []
+        for j, idx in enumerate(indices):
+            r = rec[j]
+            imgs.append({"index": int(idx), "augmented": bool(r[REC["flags"]] != 0),
+                         "forward_affine": [round(float(v), 6) for v in r[REC["fwd"]:REC["fwd"] + 6]],
+                         "color": [round(float(v), 6) for v in r[REC["color"]:REC["color"] + 9]],
+                         "noise_mode": int(r[REC["noise_mode"]]), "noise_strength": round(float(r[REC["noise_str"]]), 6),
+                         "blur": round(float(r[REC["blur"]]), 6), "occlusion_mode": int(r[REC["occ_mode"]]),
+                         "paste_slot": int(r[REC["paste_slot"]]),
+                         "targets": int(st["counts"][j])})
+        line = {"rank": self.rank, "epoch": int(epoch), "sequence": int(sequence), "images": imgs}
+        with open(_TRACE_FILE, "a") as f:
+            f.write(json.dumps(line) + "\n")
 
     def apply(self, images: torch.Tensor, st: dict) -> Tuple[torch.Tensor, Targets]:
         n = st["n"]

@@ -277,6 +277,13 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
                             pin=ctx.device.type == "cuda", high_priority=opts.high_priority)
     if ctx.main:
         log.info("host runtime: %s", rt.describe())
+        log.info("training: torch %s, bf16, optimizer %s, gradient step %s, cuda graph %s, world %d, "
+                 "batch %d per rank x %d accumulation = %d per rank, %d global", torch.__version__,
+                 opts.optimizer, ("fused-nvswitch" if opts.ddp_backend == "fused" and opts.optimizer == "adamw"
+                                  else "nccl") if ctx.enabled else "single-gpu",
+                 opts.cuda_graph and ctx.device.type == "cuda", ctx.world_size, opts.batch_size,
+                 opts.grad_accum_steps, opts.batch_size * opts.grad_accum_steps,
+                 opts.batch_size * opts.grad_accum_steps * ctx.world_size)
     loader = BatchLoader(opts.train_compiled, opts.batch_size, shuffle=True, seed=opts.seed, shard_rank=ctx.rank,
                          shard_count=ctx.world_size, drop_last=True, pixels="uint8", workers=max(1, rt.split["gather"]),
                          prefetch=max(2, opts.prefetch_factor), max_targets=1,

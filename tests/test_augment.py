@@ -198,3 +198,27 @@ def test_normalize_kernel_fp32_input():
     out = normalize_images(x, torch.float32)
     ref = (x.cpu() - MEAN) / STD
     assert (out.cpu() - ref).abs().max() < 1e-5
+
+
+def test_augment_trace_file(tmp_path, monkeypatch):
+    """MMLTK_AUGMENT_TRACE_FILE: one JSONL record per prepared batch with each image's plan."""
+    import json
+
+    import mmltk_b200.data.augment as A
+    from mmltk_b200.config.train_options import AugGroup, AugmentationConfig
+    from mmltk_b200.data.compiler import compile_split
+    from mmltk_b200.data.loader import CompiledDataset
+    from mmltk_b200.data.source import write_synthetic_source
+    trace = tmp_path / "aug.jsonl"
+    monkeypatch.setattr(A, "_TRACE_FILE", str(trace))
+    write_synthetic_source(str(tmp_path / "src"), splits=("train",), images=4, size=(48, 40))
+    path = compile_split(str(tmp_path / "src"), str(tmp_path / "bin"), "train", 48, 48)["path"]
+    ds = CompiledDataset(path)
+    cfg = AugmentationConfig(enabled=True, geometry=AugGroup(probability=1.0, min_strength=0.5, max_strength=1.0))
+    aug = A.GpuAugmenter(cfg, 2, 48, 48, 8, seed=3)
+    aug.prepare([0, 1], ds.reader, 0, 0)
+    aug.prepare([2, 3], ds.reader, 0, 1)
+    lines = [json.loads(l) for l in open(trace)]
+    assert [l["sequence"] for l in lines] == [0, 1]
+    assert [i["index"] for i in lines[1]["images"]] == [2, 3]
+    assert all(len(i["forward_affine"]) == 6 for i in lines[0]["images"])
