@@ -94,7 +94,8 @@ __device__ __forceinline__ void colreduce_row(const T* __restrict__ x, const T* 
                 acc[c] += a[c] * p[c];
                 o[c] = a[c] * gm[c];
             } else {
-                o[c] = act == 1 ? a[c] * gelu_grad(p[c]) : (p[c] > 0.f ? a[c] : 0.f);
+                // act 1: GELU' from the pre-activation; 3: p is the stored GELU'; 2: ReLU (p's sign)
+                o[c] = act == 3 ? a[c] * p[c] : act == 1 ? a[c] * gelu_grad(p[c]) : (p[c] > 0.f ? a[c] : 0.f);
             }
         }
         if (MODE == 3) {
@@ -220,14 +221,18 @@ __global__ void __launch_bounds__(256) act_bwd_kernel(const T* __restrict__ gy, 
         load8(gy + 8 * i, g);
         load8(pre + 8 * i, p);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) o[c] = act == 1 ? g[c] * gelu_grad(p[c]) : (p[c] > 0.f ? g[c] : 0.f);
+        for (int c = 0; c < 8; ++c)
+            o[c] = act == 3 ? g[c] * p[c] : act == 1 ? g[c] * gelu_grad(p[c]) : (p[c] > 0.f ? g[c] : 0.f);
         store8(gx + 8 * i, o);
     }
 }
 
-// y = GELU(x) (erf form), 8 elements per vector, four vectors in flight per thread
+// y = GELU(x) (erf form) and, when d != nullptr, d = GELU'(x) -- the forward already evaluates the
+// normal cdf / density, so storing the derivative (instead of x) leaves the backward a multiply.
+// 8 elements per vector, four vectors in flight per thread.
 template <typename T>
-__global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n8) {
+__global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, T* __restrict__ d,
+                                                       int64_t n8) {
     constexpr int U = 4;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += U * stride) {
@@ -238,11 +243,16 @@ __global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, 
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             if (i + u * stride < n8) {
-                float a[8], o[8];
+                float a[8], o[8], g[8];
                 r[u].widen(a);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) o[c] = gelu_fwd(a[c]);
+                for (int c = 0; c < 8; ++c) {
+                    const NormalCdfPdf n = normal_cdf_pdf(a[c]);
+                    o[c] = a[c] * n.cdf;
+                    g[c] = fmaf(a[c], n.pdf, n.cdf);
+                }
                 store8(y + 8 * (i + u * stride), o);
+                if (d != nullptr) store8(d + 8 * (i + u * stride), g);
             }
         }
     }
@@ -369,14 +379,15 @@ cudaError_t launch_act_bwd(DType t, const void* gy, const void* pre, void* gx, i
     });
 }
 
-cudaError_t launch_gelu_fwd(DType t, const void* x, void* y, int64_t n, cudaStream_t st) {
+cudaError_t launch_gelu_fwd(DType t, const void* x, void* y, int64_t n, cudaStream_t st, void* deriv) {
     if (n % 8 != 0) return cudaErrorInvalidValue;
     const int64_t n8 = n / 8;
     if (n8 == 0) return cudaSuccess;
     const int blocks = static_cast<int>(std::min<int64_t>((n8 + 1023) / 1024, static_cast<int64_t>(num_sms()) * 8));
     return MMLTK_DISPATCH_DT(t, [&] {
         using T = scalar_t;
-        gelu_fwd_kernel<T><<<std::max(blocks, 1), 256, 0, st>>>(static_cast<const T*>(x), static_cast<T*>(y), n8);
+        gelu_fwd_kernel<T><<<std::max(blocks, 1), 256, 0, st>>>(static_cast<const T*>(x), static_cast<T*>(y),
+                                                                static_cast<T*>(deriv), n8);
         return cudaGetLastError();
     });
 }

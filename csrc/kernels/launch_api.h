@@ -89,9 +89,9 @@ cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void
                                 int act, void* gb, bool accumulate, cudaStream_t st);
 // out (+)= acc; acc = 0 (acc: a column sum accumulated by atomics, e.g. in the GEMM epilogue)
 cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bool accumulate, cudaStream_t st);
-// y = GELU(x), erf form.  n % 8 == 0.
-cudaError_t launch_gelu_fwd(DType t, const void* x, void* y, int64_t n, cudaStream_t st);
-// act: 1 = GELU(erf), 2 = ReLU.  n % 8 == 0.
+// y = GELU(x), erf form; deriv (optional) = GELU'(x).  n % 8 == 0.
+cudaError_t launch_gelu_fwd(DType t, const void* x, void* y, int64_t n, cudaStream_t st, void* deriv = nullptr);
+// act: 1 = GELU(erf) from the pre-activation, 2 = ReLU, 3 = `pre` holds the stored GELU'.  n % 8 == 0.
 cudaError_t launch_act_bwd(DType t, const void* gy, const void* pre, void* gx, int64_t n, int act, cudaStream_t st);
 
 // ---------------------------------------------------------------- losses

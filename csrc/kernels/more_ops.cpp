@@ -135,6 +135,18 @@ torch::Tensor gelu_fwd(torch::Tensor x) {
     return y;
 }
 
+// (GELU(x), GELU'(x)) in one pass
+std::vector<torch::Tensor> gelu_fwd_deriv(torch::Tensor x) {
+    TORCH_CHECK(x.is_cuda(), "gelu_fwd_deriv: CUDA tensor expected");
+    at::cuda::CUDAGuard guard(x.device());
+    auto xc = aligned16(x);
+    auto y = torch::empty_like(xc);
+    auto d = torch::empty_like(xc);
+    check_cuda(launch_gelu_fwd(dtype_of(xc), xc.data_ptr(), y.data_ptr(), xc.numel(), cur_stream(), d.data_ptr()),
+               "gelu_fwd_deriv");
+    return {y, d};
+}
+
 torch::Tensor act_bwd(torch::Tensor gy, torch::Tensor pre, int64_t act) {
     TORCH_CHECK(gy.sizes() == pre.sizes() && gy.scalar_type() == pre.scalar_type(), "act_bwd: mismatch");
     at::cuda::CUDAGuard guard(gy.device());
@@ -192,6 +204,7 @@ void register_more_ops(pybind11::module& m) {
           py::arg("bias_grad") = py::none(), py::arg("dtype") = py::none());
     m.def("act_bwd", &act_bwd);
     m.def("gelu_fwd", &gelu_fwd);
+    m.def("gelu_fwd_deriv", &gelu_fwd_deriv);
     register_ddp_ops(m);
     register_gemm_ops(m);
     register_aug_ops(m);

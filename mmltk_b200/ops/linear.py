@@ -65,18 +65,22 @@ class _Linear(torch.autograd.Function):
         # makes y -- measured faster than the epilogue form, whose erf work stalls the 8 epilogue
         # warps of the persistent GEMM.
         fused = gemm_nt_epilogue(x2, w, b, "relu", want_pre=False) if act_id == 2 else None
+        bwd_act = act_id
         if fused is not None:
             y, pre = fused
         else:
             pre = gemm_nt(x2, w, b)               # x W^T + b
             if act_id == 1:
-                y = kernels().gelu_fwd(pre)
+                # the GELU pass also writes GELU'(pre), saved instead of pre: the backward is
+                # then a multiply (act 3) rather than a second erf evaluation
+                y, pre = kernels().gelu_fwd_deriv(pre)
+                bwd_act = 3
             else:
                 y = _act(pre, act_id) if act_id else pre
         if act_id == 2:
             pre = y
         ctx.save_for_backward(x2, w, pre if act_id else None)
-        ctx.act_id, ctx.has_bias, ctx.shp = act_id, b is not None, shp
+        ctx.act_id, ctx.has_bias, ctx.shp = bwd_act, b is not None, shp
         ctx.params = (w, b)                       # the Parameter objects (their .grad may be flat views)
         return y.view(*shp[:-1], w.shape[0])
 

@@ -306,6 +306,12 @@ def test_gelu_derivative_accuracy_fp32(cuda_device):
     assert float(err.max()) < 2e-6, float(err.max())
     fwd = kernels().gelu_fwd(pre).double().cpu().reshape(-1)
     assert float((fwd - x * torch.special.ndtr(x)).abs().max()) < 4e-6
+    y2, d2 = kernels().gelu_fwd_deriv(pre)
+    assert torch.equal(y2, kernels().gelu_fwd(pre))
+    assert float((d2.double().cpu().reshape(-1) - ref).abs().max()) < 2e-6
+    # act 3: the backward multiplies by the stored derivative
+    g3, gb3 = kernels().act_bwd_bias(gy, d2, 3, None, None)
+    assert float((g3.double().cpu().reshape(-1) - ref).abs().max()) < 2e-6
     gpre, gb = kernels().act_bwd_bias(gy, pre, 1, None, None)
     assert float((gpre.double().cpu().reshape(-1) - ref).abs().max()) < 2e-6
     assert torch.allclose(gb.double().cpu(), ref.reshape(-1, 256).sum(0), atol=1e-3, rtol=1e-5)
