@@ -307,8 +307,14 @@ class E2EPipeline:
                                size=(res, res), classes=min(80, cfg.num_classes - 1), max_instances=slots - 1,
                                seed=1000 + rank)
         path = compile_split(os.path.join(root, "src"), os.path.join(root, "bin"), "train", res, res)["path"]
+        # the host runtime a training run sets up: this rank's CPU shard, pinned loader / pool / lane
+        from mmltk_b200.ops._ext import native
+        from mmltk_b200.utils.runtime import rank_cpu_shards, setup_host_runtime
+        shard = rank_cpu_shards(world)[rank]
+        rt = setup_host_runtime(0, 1, 4, native().format_cpuset(shard) if shard else "", pin=True)
         self.loader = BatchLoader(path, args.batch, shuffle=True, seed=rank, drop_last=True, pixels="uint8",
-                                  workers=8, prefetch=4, max_targets=1, device=dev)
+                                  workers=max(1, rt.split["gather"]), prefetch=4, max_targets=1, device=dev,
+                                  cpus=rt.loader_cpus[:1])
         self.aug = GpuAugmenter(AugmentationConfig(enabled=False), args.batch, res, res, slots, device=dev,
                                 seed=rank, rank=rank)
         self.reader = self.loader.dataset.reader

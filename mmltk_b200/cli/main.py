@@ -202,6 +202,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--batch-size", type=int, default=1)
     p.add_argument("--iters", type=int, default=200)
     p.add_argument("--device-id", type=int, default=0)
+    p.add_argument("--device-ids", default="", help="e.g. 0,1,...,7: one replica per GPU, concurrent throughput")
     return ap
 
 
@@ -397,9 +398,44 @@ def _live(a) -> int:
 
 
 def _latency(a) -> int:
+    ids = [int(x) for x in a.device_ids.split(",") if x.strip()] if a.device_ids else []
+    if len(ids) > 1:
+        return _latency_replicas(a, ids)
     pred, info = _predictor(a)
     print(json.dumps({"preset_name": info["preset_name"], **pred.latency(a.iters, 20, a.batch_size)}))
     return 0
+
+
+def _latency_worker(rank, a, ids, barrier, queue):
+    import torch
+    a.device_id = ids[rank]
+    torch.cuda.set_device(a.device_id)
+    pred, info = _predictor(a)
+    pred.latency(5, 20, a.batch_size)          # graph capture and warm-up before the common start
+    barrier.wait()
+    r = pred.latency(a.iters, 5, a.batch_size)
+    queue.put((rank, info["preset_name"], r))
+
+
+def _latency_replicas(a, ids) -> int:
+    """Data-parallel inference throughput: one model replica per GPU, one process each, all timed
+    concurrently; reports the per-replica latencies and the summed images/s."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    barrier, queue = ctx.Barrier(len(ids)), ctx.Queue()
+    procs = [ctx.Process(target=_latency_worker, args=(r, a, ids, barrier, queue)) for r in range(len(ids))]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=900) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    results.sort()
+    per = [r for _, _, r in results]
+    print(json.dumps({"preset_name": results[0][1], "replicas": len(ids), "batch": a.batch_size,
+                      "images_per_s_total": round(sum(r["images_per_s"] for r in per), 1),
+                      "p50_ms_max": round(max(r["p50_ms"] for r in per), 4),
+                      "p99_ms_max": round(max(r["p99_ms"] for r in per), 4), "per_replica": per}))
+    return 0 if all(p.exitcode == 0 for p in procs) else 1
 
 
 def run(argv: Optional[List[str]] = None) -> int:
