@@ -1,0 +1,327 @@
+// Scaled dot-product attention forward on the 5th-generation tensor cores (tcgen05), head dim 64,
+// reading q / k / v straight out of the packed ViT projection [N, L, 3, H, 64]
+// (reference: `at::scaled_dot_product_attention`, `src/rfdetr/layers/model.cpp:498`).
+//
+// One CTA per (128-query tile, head, sequence), six warps:
+//   warp 4   TMA producer (one thread): the Q tile once, then 128-key K tiles into a two-stage
+//            ring and V tiles into one stage, all 128-byte swizzled 64-wide boxes of the packed
+//            projection (the column offset picks q / k / v and the head); also owns TMEM;
+//   warp 5   MMA issuer (one thread): S = Q.K^T (M=128, N=128, K=64) into TMEM columns 0-127,
+//            then O_j = P.V (M=128, N=64, K=128; P from shared memory, V MN-major) into
+//            columns 128-191;
+//   warps 0-3 softmax: thread = query row = TMEM lane.  Two passes over the S row (tcgen05.ld):
+//            the row maximum, then p = 2^(s*scale*log2e - m) written as bf16 into the
+//            swizzled K-major P tile the next MMA reads; the running output is kept in
+//            registers and rescaled at each new maximum (O = O*alpha + O_j).
+// Keys past the sequence length are masked by index, so the 128-row boxes may run into the
+// next sequence (or past the tensor, where TMA zero-fills).  Shared memory (Q 16 KB, K 2x16 KB,
+// V 16 KB, P 32 KB) and TMEM (256 columns) allow two CTAs per SM.  Every mbarrier wait is
+// bounded; on timeout the kernel records a code in the status word and leaves.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+
+#include "common.cuh"
+#include "launch_api.h"
+#include "tcgen05.cuh"
+
+namespace mmltk {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kRows = 128;                  // queries per CTA, keys per tile
+constexpr int kHd = 64;                     // head dim (one 128-byte swizzle row)
+constexpr int kTile = kRows * kHd * 2;      // 16 KB: one Q / K / V box
+constexpr int kKStages = 2;
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 256;
+constexpr int kSCol = 0, kOCol = 128;
+constexpr size_t kSmemBytes = 1024 + kTile * (1 + kKStages + 1 + 2) + 256;
+
+struct __align__(8) AttnCtl {
+    uint64_t q_full;
+    uint64_t k_full[kKStages];
+    uint64_t k_empty[kKStages];
+    uint64_t v_full, v_empty;
+    uint64_t s_full, pv_full;
+    uint64_t p_full, o_empty;      // 4 arrivals: one per softmax warp
+    uint32_t tmem_base;
+    int abort;
+};
+
+struct AttnArgs {
+    __nv_bfloat16* o;     // [N*L, C] (row pitch ldo)
+    float* lse;           // optional [N, H, L] natural-log row log-sum-exp
+    int* status;
+    int L, H, C;
+    int64_t ldo;
+    float scale_log2;     // softmax scale * log2(e)
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* sQ = smem;
+    unsigned char* sK = sQ + kTile;
+    unsigned char* sV = sK + kKStages * kTile;
+    unsigned char* sP = sV + kTile;                 // two 64-key K-major tiles
+    AttnCtl* ctl = reinterpret_cast<AttnCtl*>(sP + 2 * kTile);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * kRows, h = blockIdx.y, n = blockIdx.z;
+    const int L = a.L;
+    const int tiles = (L + kRows - 1) / kRows;
+    const int row_base = n * L;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&ctl->q_full, 1);
+        for (int s = 0; s < kKStages; ++s) {
+            mbar_init(&ctl->k_full[s], 1);
+            mbar_init(&ctl->k_empty[s], 1);
+        }
+        mbar_init(&ctl->v_full, 1);
+        mbar_init(&ctl->v_empty, 1);
+        mbar_init(&ctl->s_full, 1);
+        mbar_init(&ctl->pv_full, 1);
+        mbar_init(&ctl->p_full, 4);
+        mbar_init(&ctl->o_empty, 4);
+        ctl->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&ctl->tmem_base)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            const int cq = h * kHd, ck = a.C + h * kHd, cv = 2 * a.C + h * kHd;
+            mbar_expect_tx(&ctl->q_full, kTile);
+            tma_load_2d(&tm, &ctl->q_full, sQ, cq, row_base + q0);
+            for (int j = 0; j < tiles; ++j) {
+                const int s = j % kKStages;
+                if (!mbar_wait(&ctl->k_empty[s], ((j / kKStages) & 1) ^ 1, &ctl->abort)) goto fail_producer;
+                mbar_expect_tx(&ctl->k_full[s], kTile);
+                tma_load_2d(&tm, &ctl->k_full[s], sK + s * kTile, ck, row_base + j * kRows);
+                if (!mbar_wait(&ctl->v_empty, (j & 1) ^ 1, &ctl->abort)) goto fail_producer;
+                mbar_expect_tx(&ctl->v_full, kTile);
+                tma_load_2d(&tm, &ctl->v_full, sV, cv, row_base + j * kRows);
+            }
+            goto done_producer;
+        fail_producer:
+            ctl->abort = 1;
+            atomicCAS(a.status, 0, 1);
+        done_producer:;
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = instr_desc(false, false, kRows);
+            constexpr uint32_t idesc_o = instr_desc(false, true, kHd);
+            const uint32_t q = smem_u32(sQ), v = smem_u32(sV), p = smem_u32(sP);
+            const uint32_t tS = tmem + kSCol, tO = tmem + kOCol;
+            bool ok = mbar_wait(&ctl->q_full, 0, &ctl->abort) && mbar_wait(&ctl->k_full[0], 0, &ctl->abort);
+            if (ok) {
+                tc_fence_after();
+                const uint32_t k = smem_u32(sK);
+#pragma unroll
+                for (int kk = 0; kk < kHd / 16; ++kk)
+                    tc_mma(tS, operand_desc<false>(q, kk), operand_desc<false>(k, kk), idesc_s, kk > 0);
+                tc_commit(&ctl->k_empty[0]);
+                tc_commit(&ctl->s_full);
+            }
+            for (int j = 0; ok && j < tiles; ++j) {
+                // P_j written (so S is free again), V_j landed, the previous O_j read out
+                ok = mbar_wait(&ctl->p_full, j & 1, &ctl->abort) && mbar_wait(&ctl->v_full, j & 1, &ctl->abort) &&
+                     (j == 0 || mbar_wait(&ctl->o_empty, (j - 1) & 1, &ctl->abort));
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < kRows / 16; ++kk)
+                    tc_mma(tO, operand_desc<false>(p + (kk >> 2) * kTile, kk & 3), operand_desc<true>(v, kk), idesc_o,
+                           kk > 0);
+                tc_commit(&ctl->v_empty);
+                tc_commit(&ctl->pv_full);
+                if (j + 1 < tiles) {
+                    const int s = (j + 1) % kKStages;
+                    ok = mbar_wait(&ctl->k_full[s], ((j + 1) / kKStages) & 1, &ctl->abort);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t k = smem_u32(sK + s * kTile);
+#pragma unroll
+                    for (int kk = 0; kk < kHd / 16; ++kk)
+                        tc_mma(tS, operand_desc<false>(q, kk), operand_desc<false>(k, kk), idesc_s, kk > 0);
+                    tc_commit(&ctl->k_empty[s]);
+                    tc_commit(&ctl->s_full);
+                }
+            }
+            if (!ok) {
+                ctl->abort = 1;
+                atomicCAS(a.status, 0, 2);
+            }
+        }
+    } else {
+        // softmax warps: thread = query row r = TMEM lane r
+        const int r = threadIdx.x;
+        const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+        const uint32_t tS = tmem + kSCol + lane_off, tO = tmem + kOCol + lane_off;
+        float o[kHd];
+#pragma unroll
+        for (int i = 0; i < kHd; ++i) o[i] = 0.f;
+        float m = -1e30f, l = 0.f;
+        bool ok = true;
+        unsigned char* prow = sP + r * 128;
+        const int sw = r & 7;
+        for (int j = 0; j < tiles; ++j) {
+            if (!mbar_wait(&ctl->s_full, j & 1, &ctl->abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int valid = min(kRows, L - j * kRows);   // keys of this tile inside the sequence
+            float v[16];
+            float mx = -1e30f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                tmem_ld16(tS + 16 * c, v);
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    if (16 * c + i < valid) mx = fmaxf(mx, v[i]);
+            }
+            const float m_new = fmaxf(m, mx * a.scale_log2);
+            const float alpha = ex2(m - m_new);
+            float sum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                tmem_ld16(tS + 16 * c, v);
+                uint32_t w[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float p0 = (16 * c + 2 * i < valid) ? ex2(v[2 * i] * a.scale_log2 - m_new) : 0.f;
+                    const float p1 = (16 * c + 2 * i + 1 < valid) ? ex2(v[2 * i + 1] * a.scale_log2 - m_new) : 0.f;
+                    sum += p0 + p1;
+                    w[i] = pack_bf16x2(p0, p1);
+                }
+                // keys 16c..16c+15 -> tile c/4, 16-byte chunks 2*(c%4), +1 of this row (128B swizzle)
+                unsigned char* base = prow + (c >> 2) * kTile;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int ch = 2 * (c & 3) + q;
+                    *reinterpret_cast<uint4*>(base + ((ch ^ sw) << 4)) =
+                        make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+                }
+            }
+            l = l * alpha + sum;
+            m = m_new;
+            // P visible to the tensor core; S may be overwritten
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->p_full);
+            if (!mbar_wait(&ctl->pv_full, j & 1, &ctl->abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                tmem_ld16(tO + 16 * c, v);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[16 * c + i] = o[16 * c + i] * alpha + v[i];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->o_empty);
+        }
+        if (!ok) {
+            ctl->abort = 1;
+            if (lane == 0) atomicCAS(a.status, 0, 3);
+        } else if (q0 + r < L) {
+            const float inv = 1.f / l;
+            uint4* dst = reinterpret_cast<uint4*>(a.o + static_cast<int64_t>(row_base + q0 + r) * a.ldo + h * kHd);
+#pragma unroll
+            for (int q = 0; q < kHd / 8; ++q)
+                dst[q] = make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv),
+                                    pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
+                                    pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
+                                    pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
+            if (a.lse)
+                a.lse[(static_cast<int64_t>(n) * a.H + h) * L + q0 + r] = (m + __log2f(l)) * 0.69314718055994531f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+}  // namespace
+
+size_t attn_fwd_tc_smem_bytes() { return kSmemBytes; }
+
+cudaError_t launch_attn_fwd_tc(const void* qkv, int64_t ld, int nseq, int L, int H, void* o, int64_t ldo, float* lse,
+                               float scale, int* status, cudaStream_t st) {
+    if (nseq == 0 || L == 0) return cudaSuccess;
+    const int C = H * kHd;
+    // TMA: 16-byte aligned base and row pitch; the q / k / v column offsets are multiples of 64 elements
+    if (reinterpret_cast<uintptr_t>(qkv) % 16 != 0 || ld % 8 != 0 || ld < 3 * C) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(o) % 16 != 0 || ldo % 8 != 0) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);   // the driver-API encode needs a current context
+    if (e != cudaSuccess) return e;
+    auto fn = attn_encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    CUtensorMap tm;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(3 * C), static_cast<cuuint64_t>(static_cast<int64_t>(nseq) * L)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+    cuuint32_t box[2] = {kHd, kRows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(qkv), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::fprintf(stderr, "attn_fwd_tc: cuTensorMapEncodeTiled failed (%d)\n", static_cast<int>(r));
+        return cudaErrorInvalidValue;
+    }
+    static bool attr_set[64] = {};
+    if (!attr_set[dev & 63]) {
+        e = cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kSmemBytes));
+        if (e != cudaSuccess) return e;
+        attr_set[dev & 63] = true;
+    }
+    AttnArgs a{static_cast<__nv_bfloat16*>(o), lse, status, L, H, C, ldo, scale * 1.4426950408889634f};
+    dim3 grid((L + kRows - 1) / kRows, H, nseq);
+    attn_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(tm, a);
+    return cudaGetLastError();
+}
+
+}  // namespace mmltk

@@ -30,6 +30,14 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
                                  bool accumulate, cudaStream_t st, const void* gy2 = nullptr,
                                  const void* gres = nullptr, void* gbias2 = nullptr, bool accumulate2 = false);
 
+// ---------------------------------------------------------------- attention (tcgen05)
+// Softmax attention, head dim 64, from the packed projection qkv [nseq * L rows, >= 3 * H * 64]
+// (row pitch ld; q / k / v of head h at columns h*64, C + h*64, 2C + h*64, C = H * 64) into
+// o [nseq * L, >= C] (row pitch ldo).  lse (optional): [nseq, H, L] natural-log row log-sum-exp.
+// status: set non-zero when a bounded wait gave up (the output is then invalid).
+cudaError_t launch_attn_fwd_tc(const void* qkv, int64_t ld, int nseq, int L, int H, void* o, int64_t ldo, float* lse,
+                               float scale, int* status, cudaStream_t st);
+
 // ---------------------------------------------------------------- sine position embedding
 // pos [rows, n] fp32 (n = 2 or 4: x, y[, w, h]); out [rows, n * dim] bf16 in block order y, x[, w, h];
 // freq [dim / 2] fp32.  n * dim / 32 must be 8, 16 or 32 and divide dim.

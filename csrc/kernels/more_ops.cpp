@@ -210,6 +210,7 @@ void register_more_ops(pybind11::module& m) {
     register_aug_ops(m);
     register_loss_ops(m);
     register_image_ops(m);
+    register_attn_ops(m);
 }
 
 }  // namespace mmltk

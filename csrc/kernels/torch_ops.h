@@ -18,5 +18,6 @@ void register_gemm_ops(pybind11::module& m);
 void register_aug_ops(pybind11::module& m);
 void register_loss_ops(pybind11::module& m);
 void register_image_ops(pybind11::module& m);
+void register_attn_ops(pybind11::module& m);
 
 }  // namespace mmltk

@@ -5,7 +5,11 @@
 Reference: `at::scaled_dot_product_attention` (`src/rfdetr/layers/model.cpp:498`) and
 `nn::MultiheadAttention` (`model.cpp:917`).
 
-CUDA runs cuDNN's sm100 flash attention (library kernel).  ``qkv_attention``
+Without autograd (inference), head dim 64 runs the framework's tcgen05 kernel
+(``attn_tc.cu``: q / k / v read by TMA straight out of the packed projection, S and
+P.V accumulated in tensor memory, online softmax in registers); set
+``MMLTK_ATTN_TC=0`` to use cuDNN there too.  Training runs cuDNN's sm100 flash
+attention (library kernel) forward and backward.  ``qkv_attention``
 owns the data layout around it: q, k and v are strided views straight into
 the packed projection output (no split / permute copies), the output comes
 back in [N, L, H, D] order so the output projection reads it without a
@@ -18,11 +22,14 @@ layer, one of them a slow strided concatenation.  CPU: the math definition
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.nn.functional as F
 
-__all__ = ["attention", "attention_reference", "qkv_attention", "qkv_attention_reference"]
+__all__ = ["attention", "attention_reference", "qkv_attention", "qkv_attention_reference", "qkv_attention_tc"]
+
+_USE_TC = os.environ.get("MMLTK_ATTN_TC", "1") != "0"
 
 
 def attention_reference(q, k, v):
@@ -74,10 +81,20 @@ def qkv_attention_reference(qkv: torch.Tensor, heads: int) -> torch.Tensor:
     return attention_reference(q, k, v).transpose(1, 2).reshape(N, L, C3 // 3)
 
 
+def qkv_attention_tc(qkv: torch.Tensor, heads: int, want_lse: bool = False):
+    """tcgen05 forward: qkv [N, L, 3 * heads * 64] bf16 -> o [N, L, heads * 64]
+    (and, with ``want_lse``, the natural-log row log-sum-exp [N, heads, L] fp32)."""
+    from ._ext import kernels
+    o, lse = kernels().attn_fwd_tc(qkv, heads, want_lse)
+    return (o, lse) if want_lse else o
+
+
 def qkv_attention(qkv: torch.Tensor, heads: int) -> torch.Tensor:
     if qkv.is_cuda and qkv.dtype in (torch.bfloat16, torch.float16):
         if torch.is_grad_enabled() and qkv.requires_grad:
             return _QKVAttnFn.apply(qkv, heads)
+        if _USE_TC and qkv.dtype == torch.bfloat16 and qkv.shape[-1] == 3 * 64 * heads:
+            return qkv_attention_tc(qkv, heads)
         N, L, C3 = qkv.shape
         o = F.scaled_dot_product_attention(*_split(qkv, heads))
         return o.transpose(1, 2).reshape(N, L, C3 // 3)

@@ -137,7 +137,8 @@ def bench_msda(device="cuda", quick=False):
 
 
 # (name, batch*windows or batch*groups, heads, length, head dim): RF-DETR-M batch 8
-ATTN_SHAPES = [("dec.self_attn", 104, 8, 300, 32), ("vit.window", 32, 6, 325, 64), ("vit.global", 8, 6, 1300, 64)]
+ATTN_SHAPES = [("dec.self_attn", 104, 8, 300, 32), ("vit.window", 32, 6, 325, 64), ("vit.global", 8, 6, 1300, 64),
+               ("vit.window.b1", 4, 6, 325, 64), ("vit.global.b1", 1, 6, 1300, 64)]
 
 
 def bench_attn(device="cuda"):
@@ -162,6 +163,15 @@ def bench_attn(device="cuda"):
                 row[be.name.lower() + "_fwd_bwd_ms"] = round(time_ms(both, warmup=3, iters=10), 4)
             except RuntimeError as e:   # backend unavailable for this shape / arch
                 row[be.name.lower()] = f"unavailable: {str(e).splitlines()[0][:80]}"
+        if D == 64:
+            # forward on the packed projection layout: the tcgen05 kernel vs cuDNN on strided views
+            from .attention import _split, qkv_attention_tc
+            qkv = torch.randn(N, L, 3 * H * D, device=device, generator=g).bfloat16()
+            with torch.no_grad():
+                with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+                    row["packed_cudnn_fwd_ms"] = round(time_ms(
+                        lambda: F.scaled_dot_product_attention(*_split(qkv, H)), warmup=3, iters=20), 4)
+                row["packed_tc_fwd_ms"] = round(time_ms(lambda: qkv_attention_tc(qkv, H), warmup=3, iters=20), 4)
         rows.append(row)
     return rows
 

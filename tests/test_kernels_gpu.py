@@ -416,3 +416,25 @@ def test_layer_norm_with_residual_sums_both_gradients(cuda_device):
     ((h2 * g1).sum() + (x2 * g2).sum()).backward()
     rel = (x1.grad.float() - x2.grad).abs().max() / x2.grad.abs().max()
     assert rel < 0.03, float(rel)
+
+
+@pytest.mark.parametrize("N,L,H,pad", [(4, 325, 6, 0), (1, 1300, 6, 0), (3, 100, 2, 0), (2, 128, 6, 64),
+                                       (2, 129, 4, 0), (5, 300, 6, 8)])
+def test_attention_tc_matches_fp32(cuda_device, N, L, H, pad):
+    """tcgen05 attention forward (packed q/k/v, head dim 64) vs the fp32 math definition,
+    including partial key tiles, sequences shorter than one tile and a row pitch wider than 3C."""
+    from mmltk_b200.ops.attention import qkv_attention_reference, qkv_attention_tc
+    torch.manual_seed(0)
+    C = 64 * H
+    full = (torch.randn(N, L, 3 * C + pad, device=cuda_device) * 1.5).bfloat16()
+    qkv = full[:, :, :3 * C]
+    o, lse = qkv_attention_tc(qkv, H, want_lse=True)
+    assert kernels().attn_tc_status(torch.cuda.current_device()) == 0
+    ref = qkv_attention_reference(qkv.float(), H)
+    assert torch.allclose(o.float(), ref, atol=2e-2, rtol=2e-2), (o.float() - ref).abs().max().item()
+    q, k, _ = (t.float() for t in qkv.view(N, L, 3, H, 64).permute(2, 0, 3, 1, 4))
+    lse_ref = torch.logsumexp(q @ k.transpose(-1, -2) * 0.125, -1)
+    assert torch.allclose(lse, lse_ref, atol=2e-2, rtol=1e-3), (lse - lse_ref).abs().max().item()
+    with torch.no_grad():
+        from mmltk_b200.ops.attention import qkv_attention
+        assert torch.equal(qkv_attention(qkv, H), o)       # the inference path takes this kernel
