@@ -7,12 +7,14 @@
 //            ring and V tiles into one stage, all 128-byte swizzled 64-wide boxes of the packed
 //            projection (the column offset picks q / k / v and the head); also owns TMEM;
 //   warp 5   MMA issuer (one thread): S = Q.K^T (M=128, N=128, K=64) into TMEM columns 0-127,
-//            then O_j = P.V (M=128, N=64, K=128; P from shared memory, V MN-major) into
+//            then O += P.V (M=128, N=64, K=128; P from shared memory, V MN-major) into
 //            columns 128-191;
-//   warps 0-3 softmax: thread = query row = TMEM lane.  Two passes over the S row (tcgen05.ld):
-//            the row maximum, then p = 2^(s*scale*log2e - m) written as bf16 into the
-//            swizzled K-major P tile the next MMA reads; the running output is kept in
-//            registers and rescaled at each new maximum (O = O*alpha + O_j).
+//   warps 0-3 softmax: thread = query row = TMEM lane.  The S row (128 columns) is read from
+//            TMEM into registers in one round; p = 2^(s*scale*log2e - m) is written as bf16
+//            into the swizzled K-major P tile the next MMA reads.  O accumulates across key
+//            tiles in TMEM; it is rescaled (tcgen05.ld / st) only when a row maximum grows by
+//            more than 2^8 over the reference maximum in use (lazy rescaling), and normalised
+//            by the row sum at the end.
 // Keys past the sequence length are masked by index, so the 128-row boxes may run into the
 // next sequence (or past the tensor, where TMA zero-fills).  Shared memory (Q 16 KB, K 2x16 KB,
 // V 16 KB, P 32 KB) and TMEM (256 columns) allow two CTAs per SM.  Every mbarrier wait is
@@ -46,7 +48,7 @@ struct __align__(8) AttnCtl {
     uint64_t k_empty[kKStages];
     uint64_t v_full, v_empty;
     uint64_t s_full, pv_full;
-    uint64_t p_full, o_empty;      // 4 arrivals: one per softmax warp
+    uint64_t p_full;               // 4 arrivals: one per softmax warp
     uint32_t tmem_base;
     int abort;
 };
@@ -92,7 +94,6 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
         mbar_init(&ctl->s_full, 1);
         mbar_init(&ctl->pv_full, 1);
         mbar_init(&ctl->p_full, 4);
-        mbar_init(&ctl->o_empty, 4);
         ctl->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -144,15 +145,14 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
                 tc_commit(&ctl->s_full);
             }
             for (int j = 0; ok && j < tiles; ++j) {
-                // P_j written (so S is free again), V_j landed, the previous O_j read out
-                ok = mbar_wait(&ctl->p_full, j & 1, &ctl->abort) && mbar_wait(&ctl->v_full, j & 1, &ctl->abort) &&
-                     (j == 0 || mbar_wait(&ctl->o_empty, (j - 1) & 1, &ctl->abort));
+                // P_j written and O rescaled (so S is free again), V_j landed
+                ok = mbar_wait(&ctl->p_full, j & 1, &ctl->abort) && mbar_wait(&ctl->v_full, j & 1, &ctl->abort);
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < kRows / 16; ++kk)
                     tc_mma(tO, operand_desc<false>(p + (kk >> 2) * kTile, kk & 3), operand_desc<true>(v, kk), idesc_o,
-                           kk > 0);
+                           (j > 0 || kk > 0) ? 1u : 0u);
                 tc_commit(&ctl->v_empty);
                 tc_commit(&ctl->pv_full);
                 if (j + 1 < tiles) {
@@ -178,40 +178,53 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
         const int r = threadIdx.x;
         const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
         const uint32_t tS = tmem + kSCol + lane_off, tO = tmem + kOCol + lane_off;
-        float o[kHd];
-#pragma unroll
-        for (int i = 0; i < kHd; ++i) o[i] = 0.f;
-        float m = -1e30f, l = 0.f;
+        float m = -1e30f, l = 0.f;   // reference maximum (log2 units) and row sum
         bool ok = true;
         unsigned char* prow = sP + r * 128;
         const int sw = r & 7;
         for (int j = 0; j < tiles; ++j) {
+            // S_j landed; its commit also covers O_{j-1} = P_{j-1}.V_{j-1}, so P and O are free
             if (!mbar_wait(&ctl->s_full, j & 1, &ctl->abort)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int valid = min(kRows, L - j * kRows);   // keys of this tile inside the sequence
-            float v[16];
+            float sv[kRows];
+            tmem_ld128(tS, sv);
             float mx = -1e30f;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                tmem_ld16(tS + 16 * c, v);
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    if (16 * c + i < valid) mx = fmaxf(mx, v[i]);
+            for (int i = 0; i < kRows; ++i)
+                if (i < valid) mx = fmaxf(mx, sv[i]);
+            const float m_new = mx * a.scale_log2;
+            // lazy rescale: keep the old reference maximum unless the row maximum grew by more than
+            // 2^8 (p stays <= 256, exact enough in fp32 / bf16); the tensor-memory O is rescaled
+            // only by warps with a row that moved
+            float alpha = 1.f;
+            if (m_new > m + 8.f) {
+                alpha = ex2(m - m_new);
+                m = m_new;
             }
-            const float m_new = fmaxf(m, mx * a.scale_log2);
-            const float alpha = ex2(m - m_new);
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                for (int c = 0; c < kHd / 16; ++c) {
+                    float ov[16];
+                    tmem_ld16(tO + 16 * c, ov);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) ov[i] *= alpha;
+                    tmem_st16(tO + 16 * c, ov);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            }
             float sum = 0.f;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                tmem_ld16(tS + 16 * c, v);
+            for (int c = 0; c < kRows / 16; ++c) {
                 uint32_t w[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const float p0 = (16 * c + 2 * i < valid) ? ex2(v[2 * i] * a.scale_log2 - m_new) : 0.f;
-                    const float p1 = (16 * c + 2 * i + 1 < valid) ? ex2(v[2 * i + 1] * a.scale_log2 - m_new) : 0.f;
+                    const int k0 = 16 * c + 2 * i;
+                    const float p0 = k0 < valid ? ex2(sv[k0] * a.scale_log2 - m) : 0.f;
+                    const float p1 = k0 + 1 < valid ? ex2(sv[k0 + 1] * a.scale_log2 - m) : 0.f;
                     sum += p0 + p1;
                     w[i] = pack_bf16x2(p0, p1);
                 }
@@ -225,41 +238,33 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
                 }
             }
             l = l * alpha + sum;
-            m = m_new;
-            // P visible to the tensor core; S may be overwritten
+            // P visible to the tensor core; S and O may be overwritten / accumulated into
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctl->p_full);
-            if (!mbar_wait(&ctl->pv_full, j & 1, &ctl->abort)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                tmem_ld16(tO + 16 * c, v);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) o[16 * c + i] = o[16 * c + i] * alpha + v[i];
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ctl->o_empty);
         }
+        if (ok && !mbar_wait(&ctl->pv_full, (tiles - 1) & 1, &ctl->abort)) ok = false;
         if (!ok) {
             ctl->abort = 1;
             if (lane == 0) atomicCAS(a.status, 0, 3);
-        } else if (q0 + r < L) {
-            const float inv = 1.f / l;
-            uint4* dst = reinterpret_cast<uint4*>(a.o + static_cast<int64_t>(row_base + q0 + r) * a.ldo + h * kHd);
+        } else {
+            tc_fence_after();
+            float o[kHd];
 #pragma unroll
-            for (int q = 0; q < kHd / 8; ++q)
-                dst[q] = make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv),
-                                    pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
-                                    pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
-                                    pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
-            if (a.lse)
-                a.lse[(static_cast<int64_t>(n) * a.H + h) * L + q0 + r] = (m + __log2f(l)) * 0.69314718055994531f;
+            for (int c = 0; c < kHd / 32; ++c) tmem_ld32(tO + 32 * c, o + 32 * c);
+            if (q0 + r < L) {
+                const float inv = 1.f / l;
+                uint4* dst = reinterpret_cast<uint4*>(a.o + static_cast<int64_t>(row_base + q0 + r) * a.ldo + h * kHd);
+#pragma unroll
+                for (int q = 0; q < kHd / 8; ++q)
+                    dst[q] = make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv),
+                                        pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
+                                        pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
+                                        pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
+                if (a.lse)
+                    a.lse[(static_cast<int64_t>(n) * a.H + h) * L + q0 + r] = (m + __log2f(l)) * 0.69314718055994531f;
+            }
         }
     }
     tc_fence_before();

@@ -4,7 +4,7 @@
 //     so a kernel can record an error and leave instead of spinning forever);
 //   * 2-D TMA tile loads (no multicast);
 //   * tcgen05.mma kind::f16 (bf16 x bf16 -> fp32 in tensor memory), commit to an mbarrier,
-//     shared-memory matrix descriptors for 128-byte swizzled tiles, tcgen05.ld of 32 lanes.
+//     shared-memory matrix descriptors for 128-byte swizzled tiles, tcgen05.ld / st of 32 lanes.
 #pragma once
 
 #include <cuda.h>
@@ -122,6 +122,35 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 128 consecutive accumulator columns of this thread's row: eight loads, one wait.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float* v) {
+    uint32_t r[128];
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(r[16 * c + 0]), "=r"(r[16 * c + 1]), "=r"(r[16 * c + 2]), "=r"(r[16 * c + 3]), "=r"(r[16 * c + 4]),
+              "=r"(r[16 * c + 5]), "=r"(r[16 * c + 6]), "=r"(r[16 * c + 7]), "=r"(r[16 * c + 8]), "=r"(r[16 * c + 9]),
+              "=r"(r[16 * c + 10]), "=r"(r[16 * c + 11]), "=r"(r[16 * c + 12]), "=r"(r[16 * c + 13]),
+              "=r"(r[16 * c + 14]), "=r"(r[16 * c + 15])
+            : "r"(taddr + 16 * c));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Store 16 consecutive accumulator columns of this thread's row (caller issues tcgen05.wait::st).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+        : "memory");
+}
 
 }  // namespace tc
 }  // namespace mmltk

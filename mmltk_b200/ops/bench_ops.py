@@ -16,7 +16,7 @@ import statistics
 
 import torch
 
-__all__ = ["time_ms", "bench_gemm", "bench_msda", "bench_attn"]
+__all__ = ["time_ms", "time_graph_ms", "bench_gemm", "bench_msda", "bench_attn"]
 
 
 def time_ms(fn, warmup: int = 5, iters: int = 20, reps: int = 5) -> float:
@@ -33,6 +33,22 @@ def time_ms(fn, warmup: int = 5, iters: int = 20, reps: int = 5) -> float:
         torch.cuda.synchronize()
         out.append(s.elapsed_time(e) / iters)
     return statistics.median(out)
+
+
+def time_graph_ms(fn, iters: int = 20, reps: int = 5) -> float:
+    """Device time per call of ``fn`` with the host out of the loop: ``iters`` calls are
+    captured in one CUDA graph and the replays are event-timed (median of ``reps``)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    return time_ms(g.replay, warmup=2, iters=1, reps=reps) / iters
 
 
 # (name, M, N, K, mode): mode nt = x W^T, nn = dY W, tn = dY^T X
@@ -167,11 +183,11 @@ def bench_attn(device="cuda"):
             # forward on the packed projection layout: the tcgen05 kernel vs cuDNN on strided views
             from .attention import _split, qkv_attention_tc
             qkv = torch.randn(N, L, 3 * H * D, device=device, generator=g).bfloat16()
-            with torch.no_grad():
+            with torch.no_grad():     # device time: CUDA-graph replays (the host is out of the loop)
                 with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
-                    row["packed_cudnn_fwd_ms"] = round(time_ms(
-                        lambda: F.scaled_dot_product_attention(*_split(qkv, H)), warmup=3, iters=20), 4)
-                row["packed_tc_fwd_ms"] = round(time_ms(lambda: qkv_attention_tc(qkv, H), warmup=3, iters=20), 4)
+                    row["packed_cudnn_fwd_ms"] = round(time_graph_ms(
+                        lambda: F.scaled_dot_product_attention(*_split(qkv, H))), 4)
+                row["packed_tc_fwd_ms"] = round(time_graph_ms(lambda: qkv_attention_tc(qkv, H)), 4)
         rows.append(row)
     return rows
 
