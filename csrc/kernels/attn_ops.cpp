@@ -55,6 +55,7 @@ int64_t attn_tc_status(int64_t device) {
 void register_attn_ops(pybind11::module& m) {
     m.def("attn_fwd_tc", &attn_fwd_tc, py::arg("qkv"), py::arg("heads"), py::arg("want_lse") = false);
     m.def("attn_tc_status", &attn_tc_status, py::arg("device") = 0);
+    m.def("attn_tc_blocks_per_sm", &attn_fwd_tc_blocks_per_sm);
 }
 
 }  // namespace mmltk

@@ -2,11 +2,11 @@
 // reading q / k / v straight out of the packed ViT projection [N, L, 3, H, 64]
 // (reference: `at::scaled_dot_product_attention`, `src/rfdetr/layers/model.cpp:498`).
 //
-// One CTA per (128-query tile, head, sequence), six warps:
-//   warp 4   TMA producer (one thread): the Q tile once, then 128-key K tiles into a two-stage
-//            ring and V tiles into one stage, all 128-byte swizzled 64-wide boxes of the packed
+// One CTA per (128-query tile, head, sequence), five warps:
+//   warp 4   lane 0: TMA producer: the Q tile once, then 128-key K tiles into a two-stage
+//            ring and V tiles into another, all 128-byte swizzled 64-wide boxes of the packed
 //            projection (the column offset picks q / k / v and the head); also owns TMEM;
-//   warp 5   MMA issuer (one thread): S = Q.K^T (M=128, N=128, K=64) into TMEM columns 0-127,
+//   warp 4   lane 1: MMA issuer: S = Q.K^T (M=128, N=128, K=64) into TMEM columns 0-127,
 //            then O += P.V (M=128, N=64, K=128; P from shared memory, V MN-major) into
 //            columns 128-191;
 //   warps 0-3 softmax: thread = query row = TMEM lane.  The S row (128 columns) is read from
@@ -17,7 +17,7 @@
 //            by the row sum at the end.
 // Keys past the sequence length are masked by index, so the 128-row boxes may run into the
 // next sequence (or past the tensor, where TMA zero-fills).  Shared memory (Q 16 KB, K 2x16 KB,
-// V 16 KB, P 32 KB) and TMEM (256 columns) allow two CTAs per SM.  Every mbarrier wait is
+// V 2x16 KB, P 32 KB) and TMEM (256 columns) allow two CTAs per SM.  Every mbarrier wait is
 // bounded; on timeout the kernel records a code in the status word and leaves.
 #include <cudaTypedefs.h>
 
@@ -37,21 +37,26 @@ constexpr int kRows = 128;                  // queries per CTA, keys per tile
 constexpr int kHd = 64;                     // head dim (one 128-byte swizzle row)
 constexpr int kTile = kRows * kHd * 2;      // 16 KB: one Q / K / V box
 constexpr int kKStages = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 160;
 constexpr int kTmemCols = 256;
 constexpr int kSCol = 0, kOCol = 128;
-constexpr size_t kSmemBytes = 1024 + kTile * (1 + kKStages + 1 + 2) + 256;
+constexpr int kVStages = 2;
+// tiles + 1 KB: the control block sits in the alignment slack below the 1024-aligned tiles, so two
+// CTAs (2 x (115712 + 1024 reserved) bytes) fit the SM's 228 KB
+constexpr size_t kSmemBytes = 1024 + kTile * (1 + kKStages + kVStages + 2);
 
 struct __align__(8) AttnCtl {
     uint64_t q_full;
     uint64_t k_full[kKStages];
     uint64_t k_empty[kKStages];
-    uint64_t v_full, v_empty;
+    uint64_t v_full[kVStages], v_empty[kVStages];
     uint64_t s_full, pv_full;
     uint64_t p_full;               // 4 arrivals: one per softmax warp
     uint32_t tmem_base;
     int abort;
 };
+
+static_assert(sizeof(AttnCtl) <= 128, "control block must fit the alignment slack");
 
 struct AttnArgs {
     __nv_bfloat16* o;     // [N*L, C] (row pitch ldo)
@@ -68,15 +73,23 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-__global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+// (194 registers: ten warps of two CTAs still fit the register file)
+__global__ void __launch_bounds__(kThreads, 1) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    AttnCtl* ctl = reinterpret_cast<AttnCtl*>(smem_raw);
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + sizeof(AttnCtl) + 1023) & ~uintptr_t(1023));
     unsigned char* sQ = smem;
     unsigned char* sK = sQ + kTile;
     unsigned char* sV = sK + kKStages * kTile;
-    unsigned char* sP = sV + kTile;                 // two 64-key K-major tiles
-    AttnCtl* ctl = reinterpret_cast<AttnCtl*>(sP + 2 * kTile);
+    unsigned char* sP = sV + kVStages * kTile;      // two 64-key K-major tiles
 
+    // the layout above fits kSmemBytes when the dynamic window is 128-byte aligned; anything
+    // else is reported instead of overrunning (uniform across the CTA, before any barrier)
+    if (smem - smem_raw + kTile * (1 + kKStages + kVStages + 2) > kSmemBytes) {
+        if (threadIdx.x == 0) atomicCAS(a.status, 0, 4);
+        return;
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q0 = blockIdx.x * kRows, h = blockIdx.y, n = blockIdx.z;
     const int L = a.L;
@@ -89,8 +102,10 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
             mbar_init(&ctl->k_full[s], 1);
             mbar_init(&ctl->k_empty[s], 1);
         }
-        mbar_init(&ctl->v_full, 1);
-        mbar_init(&ctl->v_empty, 1);
+        for (int s = 0; s < kVStages; ++s) {
+            mbar_init(&ctl->v_full[s], 1);
+            mbar_init(&ctl->v_empty[s], 1);
+        }
         mbar_init(&ctl->s_full, 1);
         mbar_init(&ctl->pv_full, 1);
         mbar_init(&ctl->p_full, 4);
@@ -108,8 +123,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
 
-    if (warp == 4) {
-        if (lane == 0) {
+    if (warp == 4 && lane == 0) {
+        {
             const int cq = h * kHd, ck = a.C + h * kHd, cv = 2 * a.C + h * kHd;
             mbar_expect_tx(&ctl->q_full, kTile);
             tma_load_2d(&tm, &ctl->q_full, sQ, cq, row_base + q0);
@@ -118,9 +133,10 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
                 if (!mbar_wait(&ctl->k_empty[s], ((j / kKStages) & 1) ^ 1, &ctl->abort)) goto fail_producer;
                 mbar_expect_tx(&ctl->k_full[s], kTile);
                 tma_load_2d(&tm, &ctl->k_full[s], sK + s * kTile, ck, row_base + j * kRows);
-                if (!mbar_wait(&ctl->v_empty, (j & 1) ^ 1, &ctl->abort)) goto fail_producer;
-                mbar_expect_tx(&ctl->v_full, kTile);
-                tma_load_2d(&tm, &ctl->v_full, sV, cv, row_base + j * kRows);
+                const int sv = j % kVStages;
+                if (!mbar_wait(&ctl->v_empty[sv], ((j / kVStages) & 1) ^ 1, &ctl->abort)) goto fail_producer;
+                mbar_expect_tx(&ctl->v_full[sv], kTile);
+                tma_load_2d(&tm, &ctl->v_full[sv], sV + sv * kTile, cv, row_base + j * kRows);
             }
             goto done_producer;
         fail_producer:
@@ -128,11 +144,11 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
             atomicCAS(a.status, 0, 1);
         done_producer:;
         }
-    } else if (warp == 5) {
-        if (lane == 0) {
+    } else if (warp == 4 && lane == 1) {
+        {
             constexpr uint32_t idesc_s = instr_desc(false, false, kRows);
             constexpr uint32_t idesc_o = instr_desc(false, true, kHd);
-            const uint32_t q = smem_u32(sQ), v = smem_u32(sV), p = smem_u32(sP);
+            const uint32_t q = smem_u32(sQ), p = smem_u32(sP);
             const uint32_t tS = tmem + kSCol, tO = tmem + kOCol;
             bool ok = mbar_wait(&ctl->q_full, 0, &ctl->abort) && mbar_wait(&ctl->k_full[0], 0, &ctl->abort);
             if (ok) {
@@ -146,14 +162,16 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
             }
             for (int j = 0; ok && j < tiles; ++j) {
                 // P_j written and O rescaled (so S is free again), V_j landed
-                ok = mbar_wait(&ctl->p_full, j & 1, &ctl->abort) && mbar_wait(&ctl->v_full, j & 1, &ctl->abort);
+                ok = mbar_wait(&ctl->p_full, j & 1, &ctl->abort) &&
+                     mbar_wait(&ctl->v_full[j % kVStages], (j / kVStages) & 1, &ctl->abort);
                 if (!ok) break;
                 tc_fence_after();
+                const uint32_t v = smem_u32(sV + (j % kVStages) * kTile);
 #pragma unroll
                 for (int kk = 0; kk < kRows / 16; ++kk)
                     tc_mma(tO, operand_desc<false>(p + (kk >> 2) * kTile, kk & 3), operand_desc<true>(v, kk), idesc_o,
                            (j > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(&ctl->v_empty);
+                tc_commit(&ctl->v_empty[j % kVStages]);
                 tc_commit(&ctl->pv_full);
                 if (j + 1 < tiles) {
                     const int s = (j + 1) % kKStages;
@@ -173,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_fwd_tc_kernel(const __grid_c
                 atomicCAS(a.status, 0, 2);
             }
         }
-    } else {
+    } else if (warp < 4) {
         // softmax warps: thread = query row r = TMEM lane r
         const int r = threadIdx.x;
         const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
@@ -290,6 +308,17 @@ PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
 }  // namespace
 
 size_t attn_fwd_tc_smem_bytes() { return kSmemBytes; }
+
+int attn_fwd_tc_blocks_per_sm() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess)
+        return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_fwd_tc_kernel, kThreads, kSmemBytes) != cudaSuccess)
+        return 0;
+    return n;
+}
 
 cudaError_t launch_attn_fwd_tc(const void* qkv, int64_t ld, int nseq, int L, int H, void* o, int64_t ldo, float* lse,
                                float scale, int* status, cudaStream_t st) {

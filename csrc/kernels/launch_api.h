@@ -37,6 +37,7 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
 // status: set non-zero when a bounded wait gave up (the output is then invalid).
 cudaError_t launch_attn_fwd_tc(const void* qkv, int64_t ld, int nseq, int L, int H, void* o, int64_t ldo, float* lse,
                                float scale, int* status, cudaStream_t st);
+int attn_fwd_tc_blocks_per_sm();   // resident CTAs per SM (registers, shared memory)
 
 // ---------------------------------------------------------------- sine position embedding
 // pos [rows, n] fp32 (n = 2 or 4: x, y[, w, h]); out [rows, n * dim] bf16 in block order y, x[, w, h];
