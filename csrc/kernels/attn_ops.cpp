@@ -56,6 +56,7 @@ void register_attn_ops(pybind11::module& m) {
     m.def("attn_fwd_tc", &attn_fwd_tc, py::arg("qkv"), py::arg("heads"), py::arg("want_lse") = false);
     m.def("attn_tc_status", &attn_tc_status, py::arg("device") = 0);
     m.def("attn_tc_blocks_per_sm", &attn_fwd_tc_blocks_per_sm);
+    m.def("attn_tc_set_variant", &attn_fwd_tc_set_variant, py::arg("min_blocks"));
 }
 
 }  // namespace mmltk

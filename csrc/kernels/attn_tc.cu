@@ -73,8 +73,11 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// (194 registers: ten warps of two CTAs still fit the register file)
-__global__ void __launch_bounds__(kThreads, 1) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+// kMinBlocks = 2 caps the kernel at 168 registers (each SM sub-partition holds 16384: three
+// warps of two co-resident CTAs), with a few spilled; kMinBlocks = 1 uses 194 without spills,
+// one CTA per SM.
+template <int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     AttnCtl* ctl = reinterpret_cast<AttnCtl*>(smem_raw);
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -309,15 +312,28 @@ PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
 
 size_t attn_fwd_tc_smem_bytes() { return kSmemBytes; }
 
+namespace {
+int g_attn_variant = 2;   // kMinBlocks of the launched instantiation
+
+template <typename F>
+auto attn_kernel_ptr(F&& f) {
+    return g_attn_variant == 1 ? f(attn_fwd_tc_kernel<1>) : f(attn_fwd_tc_kernel<2>);
+}
+}  // namespace
+
+void attn_fwd_tc_set_variant(int min_blocks) { g_attn_variant = min_blocks == 1 ? 1 : 2; }
+
 int attn_fwd_tc_blocks_per_sm() {
-    int dev = 0, n = 0;
+    int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-    if (cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes)) != cudaSuccess)
-        return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_fwd_tc_kernel, kThreads, kSmemBytes) != cudaSuccess)
-        return 0;
-    return n;
+    return attn_kernel_ptr([](auto kern) {
+        int n = 0;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) !=
+            cudaSuccess)
+            return 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, kSmemBytes) != cudaSuccess) return 0;
+        return n;
+    });
 }
 
 cudaError_t launch_attn_fwd_tc(const void* qkv, int64_t ld, int nseq, int L, int H, void* o, int64_t ldo, float* lse,
@@ -345,17 +361,20 @@ cudaError_t launch_attn_fwd_tc(const void* qkv, int64_t ld, int nseq, int L, int
         std::fprintf(stderr, "attn_fwd_tc: cuTensorMapEncodeTiled failed (%d)\n", static_cast<int>(r));
         return cudaErrorInvalidValue;
     }
-    static bool attr_set[64] = {};
-    if (!attr_set[dev & 63]) {
-        e = cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kSmemBytes));
-        if (e != cudaSuccess) return e;
-        attr_set[dev & 63] = true;
-    }
+    static bool attr_set[2][64] = {};
     AttnArgs a{static_cast<__nv_bfloat16*>(o), lse, status, L, H, C, ldo, scale * 1.4426950408889634f};
     dim3 grid((L + kRows - 1) / kRows, H, nseq);
-    attn_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(tm, a);
-    return cudaGetLastError();
+    return attn_kernel_ptr([&](auto kern) {
+        bool& set = attr_set[g_attn_variant - 1][dev & 63];
+        if (!set) {
+            cudaError_t ea = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(kSmemBytes));
+            if (ea != cudaSuccess) return ea;
+            set = true;
+        }
+        kern<<<grid, kThreads, kSmemBytes, st>>>(tm, a);
+        return cudaGetLastError();
+    });
 }
 
 }  // namespace mmltk

@@ -38,6 +38,8 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
 cudaError_t launch_attn_fwd_tc(const void* qkv, int64_t ld, int nseq, int L, int H, void* o, int64_t ldo, float* lse,
                                float scale, int* status, cudaStream_t st);
 int attn_fwd_tc_blocks_per_sm();   // resident CTAs per SM (registers, shared memory)
+// 2 (default): two CTAs per SM at 168 registers; 1: one CTA per SM, no register cap.
+void attn_fwd_tc_set_variant(int min_blocks);
 
 // ---------------------------------------------------------------- sine position embedding
 // pos [rows, n] fp32 (n = 2 or 4: x, y[, w, h]); out [rows, n * dim] bf16 in block order y, x[, w, h];

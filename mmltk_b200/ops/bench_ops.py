@@ -187,7 +187,11 @@ def bench_attn(device="cuda"):
                 with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
                     row["packed_cudnn_fwd_ms"] = round(time_graph_ms(
                         lambda: F.scaled_dot_product_attention(*_split(qkv, H))), 4)
-                row["packed_tc_fwd_ms"] = round(time_graph_ms(lambda: qkv_attention_tc(qkv, H)), 4)
+                from ._ext import kernels
+                for variant in (2, 1):     # two CTAs per SM (168 registers) / one CTA per SM
+                    kernels().attn_tc_set_variant(variant)
+                    row[f"packed_tc{variant}_fwd_ms"] = round(time_graph_ms(lambda: qkv_attention_tc(qkv, H)), 4)
+                kernels().attn_tc_set_variant(2)
         rows.append(row)
     return rows
 
