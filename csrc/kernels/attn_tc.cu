@@ -329,7 +329,8 @@ int attn_fwd_tc_blocks_per_sm() {
     return attn_kernel_ptr([](auto kern) {
         int n = 0;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) !=
-            cudaSuccess)
+                cudaSuccess ||
+            cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
             return 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, kSmemBytes) != cudaSuccess) return 0;
         return n;
@@ -369,6 +370,8 @@ cudaError_t launch_attn_fwd_tc(const void* qkv, int64_t ld, int nseq, int L, int
         if (!set) {
             cudaError_t ea = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   static_cast<int>(kSmemBytes));
+            // all of the unified L1 / shared storage as shared memory (a property of this kernel)
+            if (ea == cudaSuccess) ea = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
             if (ea != cudaSuccess) return ea;
             set = true;
         }

@@ -191,6 +191,7 @@ def bench_attn(device="cuda"):
                 for variant in (2, 1):     # two CTAs per SM (168 registers) / one CTA per SM
                     kernels().attn_tc_set_variant(variant)
                     row[f"packed_tc{variant}_fwd_ms"] = round(time_graph_ms(lambda: qkv_attention_tc(qkv, H)), 4)
+                    row[f"tc{variant}_blocks_per_sm"] = kernels().attn_tc_blocks_per_sm()
                 kernels().attn_tc_set_variant(2)
         rows.append(row)
     return rows
