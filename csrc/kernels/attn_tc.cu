@@ -4,7 +4,7 @@
 //
 // One CTA per (128-query tile, head, sequence), five warps:
 //   warp 4   lane 0: TMA producer: the Q tile once, then 128-key K tiles into a two-stage
-//            ring and V tiles into another, all 128-byte swizzled 64-wide boxes of the packed
+//            ring and V tiles into one stage, all 128-byte swizzled 64-wide boxes of the packed
 //            projection (the column offset picks q / k / v and the head); also owns TMEM;
 //   warp 4   lane 1: MMA issuer: S = Q.K^T (M=128, N=128, K=64) into TMEM columns 0-127,
 //            then O += P.V (M=128, N=64, K=128; P from shared memory, V MN-major) into
@@ -17,7 +17,7 @@
 //            by the row sum at the end.
 // Keys past the sequence length are masked by index, so the 128-row boxes may run into the
 // next sequence (or past the tensor, where TMA zero-fills).  Shared memory (Q 16 KB, K 2x16 KB,
-// V 2x16 KB, P 32 KB) and TMEM (256 columns) allow two CTAs per SM.  Every mbarrier wait is
+// V 16 KB, P 32 KB) and TMEM (256 columns) allow two CTAs per SM.  Every mbarrier wait is
 // bounded; on timeout the kernel records a code in the status word and leaves.
 #include <cudaTypedefs.h>
 
@@ -40,9 +40,8 @@ constexpr int kKStages = 2;
 constexpr int kThreads = 160;
 constexpr int kTmemCols = 256;
 constexpr int kSCol = 0, kOCol = 128;
-constexpr int kVStages = 2;
-// tiles + 1 KB: the control block sits in the alignment slack below the 1024-aligned tiles, so two
-// CTAs (2 x (115712 + 1024 reserved) bytes) fit the SM's 228 KB
+constexpr int kVStages = 1;   // two V stages (112 KB) measured slower: the SM then holds one CTA
+// tiles + 1 KB: the control block sits in the alignment slack below the 1024-aligned tiles
 constexpr size_t kSmemBytes = 1024 + kTile * (1 + kKStages + kVStages + 2);
 
 struct __align__(8) AttnCtl {
