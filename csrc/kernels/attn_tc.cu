@@ -17,7 +17,7 @@
 //            by the row sum at the end.
 // Keys past the sequence length are masked by index, so the 128-row boxes may run into the
 // next sequence (or past the tensor, where TMA zero-fills).  Shared memory (Q 16 KB, K 2x16 KB,
-// V 16 KB, P 32 KB) and TMEM (256 columns) allow two CTAs per SM.  Every mbarrier wait is
+// V 16 KB, P 32 KB) and TMEM (256 columns) are sized for two CTAs per SM.  Every mbarrier wait is
 // bounded; on timeout the kernel records a code in the status word and leaves.
 #include <cudaTypedefs.h>
 
