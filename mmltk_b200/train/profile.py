@@ -88,12 +88,17 @@ def _profile_infer(a) -> int:
     for _ in range(a.warmup):
         pred(x)
     torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+    acts = [ProfilerActivity.CPU, ProfilerActivity.CUDA] if a.by_origin else [ProfilerActivity.CUDA]
+    with profile(activities=acts, record_shapes=a.by_origin and not a.no_shapes,
+                 with_stack=a.by_origin and a.stack) as prof:
         for _ in range(a.steps):
             pred(x)
         torch.cuda.synchronize()
     print(f"# {a.preset} inference, batch {a.batch_size}, {pred.size[0]}x{pred.size[1]}, bf16\n")
-    print(_kernel_table(prof.events(), a.steps, a.top))
+    if a.by_origin:
+        print(origin_table(prof.events(), a.steps, a.top, shapes=not a.no_shapes, stack=a.stack))
+    else:
+        print(_kernel_table(prof.events(), a.steps, a.top))
     g = Predictor(model, device=dev, cuda_graph=True)
     print(f"\nCUDA-graph latency: {g.latency(200, 20, a.batch_size)}")
     return 0
