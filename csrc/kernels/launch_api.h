@@ -15,11 +15,12 @@ int num_sms();
 
 // ---------------------------------------------------------------- LayerNorm
 // res/sum (both or neither): normalise x + res and store the sum to `sum`; pos/y2 (both or
-// neither): also store y + pos to y2.  All [rows, C] of the x dtype.
+// neither): also store y + pos to y2.  All [rows, C] of the x dtype.  rscale (weight dtype [C], needs
+// res): the normalised input is res + rscale * (x + rbias) instead.
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st,
                                  const void* res = nullptr, void* sum = nullptr, const void* pos = nullptr,
-                                 void* y2 = nullptr, const void* rbias = nullptr);
+                                 void* y2 = nullptr, const void* rbias = nullptr, const void* rscale = nullptr);
 // One launch: gx, and gw / gb written (or added into, `accumulate`) by the last CTA.
 // gy2 (optional): a second output gradient added to gy (the y + pos output of the forward).
 // gres (optional): added to gx (the gradient x receives through a residual branch).

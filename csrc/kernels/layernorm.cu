@@ -16,7 +16,8 @@ namespace mmltk {
 namespace {
 
 // Optional fusions of the forward: res -> normalise x + res (+ rbias, a bias row vector of the
-// residual branch) and store the sum; pos -> also store y + pos.
+// residual branch) and store the sum -- or, with rscale, res + rscale * (x + rbias), a LayerScale
+// residual; pos -> also store y + pos.
 template <typename T, typename W>
 struct LnFwdExtra {
     const T* res;
@@ -24,6 +25,7 @@ struct LnFwdExtra {
     const T* pos;
     T* y2;
     const W* rbias;
+    const W* rscale;   // with res: normalise res + rscale * (x + rbias) (a LayerScale residual)
 };
 
 template <typename T, typename W, int kMaxVec>
@@ -46,11 +48,22 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, co
                 v[k] = load4(xr + 4 * i);
                 if (ex.res != nullptr) {   // fused residual add: the norm's input is x + res (+ rbias)
                     const float4 r4 = load4(ex.res + r * C + 4 * i);
-                    v[k].x += r4.x; v[k].y += r4.y; v[k].z += r4.z; v[k].w += r4.w;
-                    if (ex.rbias != nullptr) {
-                        const int c0 = 4 * i;
-                        v[k].x += to_f(ex.rbias[c0]); v[k].y += to_f(ex.rbias[c0 + 1]);
-                        v[k].z += to_f(ex.rbias[c0 + 2]); v[k].w += to_f(ex.rbias[c0 + 3]);
+                    const int c0 = 4 * i;
+                    if (ex.rscale != nullptr) {   // res + gamma * (x + rbias)
+                        if (ex.rbias != nullptr) {
+                            v[k].x += to_f(ex.rbias[c0]); v[k].y += to_f(ex.rbias[c0 + 1]);
+                            v[k].z += to_f(ex.rbias[c0 + 2]); v[k].w += to_f(ex.rbias[c0 + 3]);
+                        }
+                        v[k].x = r4.x + to_f(ex.rscale[c0]) * v[k].x;
+                        v[k].y = r4.y + to_f(ex.rscale[c0 + 1]) * v[k].y;
+                        v[k].z = r4.z + to_f(ex.rscale[c0 + 2]) * v[k].z;
+                        v[k].w = r4.w + to_f(ex.rscale[c0 + 3]) * v[k].w;
+                    } else {
+                        v[k].x += r4.x; v[k].y += r4.y; v[k].z += r4.z; v[k].w += r4.w;
+                        if (ex.rbias != nullptr) {
+                            v[k].x += to_f(ex.rbias[c0]); v[k].y += to_f(ex.rbias[c0 + 1]);
+                            v[k].z += to_f(ex.rbias[c0 + 2]); v[k].w += to_f(ex.rbias[c0 + 3]);
+                        }
                     }
                     store4(ex.sum + r * C + 4 * i, v[k]);
                 }
@@ -331,8 +344,8 @@ void dispatch_vec(int C, F&& f) {
 
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st, const void* res,
-                                 void* sum, const void* pos, void* y2, const void* rbias) {
-    if (rbias != nullptr && res == nullptr) return cudaErrorInvalidValue;
+                                 void* sum, const void* pos, void* y2, const void* rbias, const void* rscale) {
+    if ((rbias != nullptr || rscale != nullptr) && res == nullptr) return cudaErrorInvalidValue;
     if ((res == nullptr) != (sum == nullptr) || (pos == nullptr) != (y2 == nullptr)) return cudaErrorInvalidValue;
     if (rows == 0) return cudaSuccess;
     if (C % 4 != 0 || C > 4 * 32 * 12) return cudaErrorInvalidValue;
@@ -347,7 +360,8 @@ cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* 
                     static_cast<const T*>(x), static_cast<const Wt*>(w), static_cast<const Wt*>(b),
                     static_cast<T*>(y), mean, rstd, rows, C, eps,
                     LnFwdExtra<T, Wt>{static_cast<const T*>(res), static_cast<T*>(sum), static_cast<const T*>(pos),
-                                      static_cast<T*>(y2), static_cast<const Wt*>(rbias)});
+                                      static_cast<T*>(y2), static_cast<const Wt*>(rbias),
+                                      static_cast<const Wt*>(rscale)});
             });
             return cudaGetLastError();
         });

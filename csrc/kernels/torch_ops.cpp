@@ -49,7 +49,7 @@ namespace {
 // Returns {y, mean, rstd, sum (or undefined), y + pos (or undefined)}.
 std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps,
                                          c10::optional<torch::Tensor> res, c10::optional<torch::Tensor> pos,
-                                         c10::optional<torch::Tensor> rbias) {
+                                         c10::optional<torch::Tensor> rbias, c10::optional<torch::Tensor> rscale) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "layernorm_fwd: x must be contiguous [rows, C]");
     TORCH_CHECK(w.scalar_type() == b.scalar_type() && w.numel() == x.size(1) && b.numel() == x.size(1),
                 "layernorm_fwd: weight/bias must match C and share a dtype");
@@ -59,6 +59,11 @@ std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch
         TORCH_CHECK(has_res && rbias->numel() == x.size(1) && rbias->is_contiguous() &&
                         rbias->scalar_type() == w.scalar_type(),
                     "layernorm_fwd: rbias needs res and must be a contiguous [C] vector of the weight dtype");
+    const bool has_rs = rscale && rscale->defined();
+    if (has_rs)
+        TORCH_CHECK(has_res && rscale->numel() == x.size(1) && rscale->is_contiguous() &&
+                        rscale->scalar_type() == w.scalar_type(),
+                    "layernorm_fwd: rscale needs res and must be a contiguous [C] vector of the weight dtype");
     if (has_res)
         TORCH_CHECK(res->sizes() == x.sizes() && res->is_contiguous() && res->scalar_type() == x.scalar_type(),
                     "layernorm_fwd: res must match x");
@@ -80,7 +85,8 @@ std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch
                                     mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C, static_cast<float>(eps),
                                     cur_stream(), has_res ? res->data_ptr() : nullptr,
                                     has_res ? sum.data_ptr() : nullptr, has_pos ? pos->data_ptr() : nullptr,
-                                    has_pos ? y2.data_ptr() : nullptr, has_rb ? rbias->data_ptr() : nullptr),
+                                    has_pos ? y2.data_ptr() : nullptr, has_rb ? rbias->data_ptr() : nullptr,
+                                    has_rs ? rscale->data_ptr() : nullptr),
                "layernorm_fwd");
     return {y, mean, rstd, sum, y2};
 }
@@ -296,7 +302,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "mmltk_b200 sm_100a CUDA kernels";
     m.def("num_sms", &mmltk::num_sms);
     m.def("layernorm_fwd", &mmltk::layernorm_fwd, py::arg("x"), py::arg("w"), py::arg("b"), py::arg("eps"),
-          py::arg("res") = py::none(), py::arg("pos") = py::none(), py::arg("rbias") = py::none());
+          py::arg("res") = py::none(), py::arg("pos") = py::none(), py::arg("rbias") = py::none(),
+          py::arg("rscale") = py::none());
     m.def("layernorm_bwd", &mmltk::layernorm_bwd, py::arg("gy"), py::arg("x"), py::arg("w"), py::arg("mean"),
           py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none(), py::arg("gy2") = py::none(),
           py::arg("gres") = py::none(), py::arg("want_gbias2") = false, py::arg("gbias2_acc") = py::none());

@@ -78,6 +78,13 @@ class Predictor:
         self.cuda = self.device.type == "cuda"
         self.dtype = dtype if self.cuda else torch.float32
         self.model = model.eval().to(device=self.device, dtype=self.dtype)
+        if self.cuda:
+            # the convolutions run on channels-last activations; weights in the same layout spare
+            # cuDNN a per-call weight transform (one copy kernel per 3x3 conv and forward)
+            for mod in self.model.modules():
+                if isinstance(mod, (torch.nn.Conv2d, torch.nn.ConvTranspose2d)) and mod.weight.dim() == 4 \
+                        and mod.weight.shape[-1] * mod.weight.shape[-2] > 1:
+                    mod.weight.data = mod.weight.data.contiguous(memory_format=torch.channels_last)
         self.cfg = model.cfg
         self.size = (self.cfg.resolution, self.cfg.resolution)
         self.k = int(num_select or self.cfg.num_select)

@@ -190,6 +190,23 @@ class ViTLayer(nn.Module):
         return ops.mlp_scale_residual(h, self.mlp.fc1.weight, self.mlp.fc1.bias, self.mlp.fc2.weight,
                                       self.mlp.fc2.bias, self.layer_scale2.lambda1, x)
 
+    def forward_inference(self, x: torch.Tensor, h: torch.Tensor, full_attention: bool):
+        """The layer body without autograd, from its input x and h = norm1(x).  Returns (x1, y)
+        with the layer output x1 + lambda2 * y left unformed: the next pre-norm (or the caller)
+        forms it in the same pass as its LayerNorm, and the post-attention residual is formed
+        by norm2 the same way -- no separate LayerScale-residual pass over the tokens."""
+        NW, L, C = x.shape
+        if full_attention and self.num_windows > 1:
+            w2 = self.num_windows ** 2
+            h = h.view(NW // w2, w2 * L, C)
+        a = self.attention.attention(h).view(NW, L, C)
+        d = self.attention.output.dense
+        a = ops.linear(a, d.weight, d.bias)
+        h, x1 = ops.scaled_residual_layer_norm(a, x, self.layer_scale1.lambda1, self.norm2.weight,
+                                               self.norm2.bias, 1e-6)
+        m = ops.linear(h, self.mlp.fc1.weight, self.mlp.fc1.bias, act="gelu")
+        return x1, ops.linear(m, self.mlp.fc2.weight, self.mlp.fc2.bias)
+
 
 class Encoder(nn.Module):
     def __init__(self, cfg: RfDetrConfig):
@@ -216,10 +233,26 @@ class WindowedDinov2(nn.Module):
         x = self.embeddings(pixels)
         states = {}
         full_stages = set(self.taps)
-        for i, layer in enumerate(self.encoder.layer):
-            if i in full_stages:
-                states[i] = x
-            x = layer(x, i in full_stages)
+        if torch.is_grad_enabled():
+            for i, layer in enumerate(self.encoder.layer):
+                if i in full_stages:
+                    states[i] = x
+                x = layer(x, i in full_stages)
+        else:
+            # inference: each layer's output x + lambda2 * y is formed by the next layer's norm1
+            y = gamma = None
+            for i, layer in enumerate(self.encoder.layer):
+                n1 = layer.norm1
+                if y is None:
+                    h = ops.layer_norm(x, n1.weight, n1.bias, 1e-6)
+                else:
+                    h, x = ops.scaled_residual_layer_norm(y, x, gamma, n1.weight, n1.bias, 1e-6)
+                if i in full_stages:
+                    states[i] = x
+                x, y = layer.forward_inference(x, h, i in full_stages)
+                gamma = layer.layer_scale2.lambda1
+            if y is not None:
+                x = torch.addcmul(x, y, gamma.to(y.dtype))
         states[len(self.encoder.layer)] = x
         hp, wp = H // p, W // p
         hpw, wpw = hp // nw, wp // nw

@@ -15,7 +15,7 @@ import torch.nn.functional as F
 from ._ext import kernels
 from .gradacc import grad_target
 
-__all__ = ["layer_norm", "add_layer_norm", "layer_norm_with_residual"]
+__all__ = ["scaled_residual_layer_norm", "layer_norm", "add_layer_norm", "layer_norm_with_residual"]
 
 
 class _LayerNormFn(torch.autograd.Function):
@@ -109,6 +109,24 @@ def add_layer_norm(a: torch.Tensor, b: torch.Tensor, weight: torch.Tensor, bias:
     x = a + b if rbias is None else a + b + rbias.to(a.dtype)
     y = F.layer_norm(x, (a.shape[-1],), weight.to(a.dtype), bias.to(a.dtype), eps)
     return (y, y + pos) if pos is not None else y
+
+
+def scaled_residual_layer_norm(y: torch.Tensor, res: torch.Tensor, gamma: torch.Tensor, weight: torch.Tensor,
+                               bias: torch.Tensor, eps: float):
+    """(LN(res + gamma * y), res + gamma * y) without autograd: a LayerScale residual and the next
+    pre-norm in one pass (inference).  On CUDA one LayerNorm kernel reads y and res, stores the
+    sum and the normalised rows; elsewhere (or with autograd) the plain expression."""
+    C = y.shape[-1]
+    if (y.is_cuda and not torch.is_grad_enabled() and C % 8 == 0 and y.dtype in (torch.bfloat16, torch.float32)
+            and res.dtype == y.dtype and res.shape == y.shape and gamma.dtype == weight.dtype
+            and gamma.numel() == C):
+        y2 = y.contiguous().view(-1, C)
+        r2 = res.contiguous().view(-1, C)
+        out, _m, _r, s = kernels().layernorm_fwd(y2, weight, bias, float(eps), r2, None, None,
+                                                 gamma.contiguous())[:4]
+        return out.view(y.shape), s.view(y.shape)
+    x = res + gamma.to(y.dtype) * y
+    return F.layer_norm(x, (C,), weight.to(y.dtype), bias.to(y.dtype), eps), x
 
 
 class _LayerNormResidualFn(torch.autograd.Function):

@@ -445,3 +445,20 @@ def test_attention_tc_matches_fp32(cuda_device, N, L, H, pad):
             assert torch.equal(attn_mod.qkv_attention(qkv, H), o)   # the opt-in inference path takes this kernel
         finally:
             attn_mod._USE_TC = old
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_scaled_residual_layer_norm_kernel(cuda_device, dtype):
+    """LayerNorm kernel with the fused LayerScale residual res + gamma * y vs fp32 PyTorch."""
+    from mmltk_b200.ops import scaled_residual_layer_norm
+    torch.manual_seed(0)
+    y = torch.randn(1300, 384, device=cuda_device)
+    res = torch.randn(1300, 384, device=cuda_device) * 2
+    g, w, b = (torch.rand(384, device=cuda_device) + 0.1, torch.randn(384, device=cuda_device),
+               torch.randn(384, device=cuda_device))
+    with torch.no_grad():
+        out, s = scaled_residual_layer_norm(y.to(dtype), res.to(dtype), g.to(dtype), w.to(dtype), b.to(dtype), 1e-6)
+    ref_s = res.to(dtype).float() + g.to(dtype).float() * y.to(dtype).float()
+    ref = torch.nn.functional.layer_norm(ref_s, (384,), w.to(dtype).float(), b.to(dtype).float(), 1e-6)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
+    assert _rel(s, ref_s) < tol and _rel(out, ref) < tol

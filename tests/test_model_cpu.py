@@ -160,3 +160,33 @@ def test_large_vitb_p3p5_builds():
     with torch.no_grad():
         o = m(torch.randn(1, 3, 128, 128))
     assert o["pred_boxes"].shape == (1, 20, 4)
+
+
+def test_inference_encoder_path_matches_training_path():
+    """Without autograd the ViT forms each LayerScale residual inside the next LayerNorm; the
+    features must equal the autograd path's (random, non-trivial layer scales)."""
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-tiny-test", num_windows=2, resolution=64, positional_encoding_size=4)
+    m = RFDETR(cfg)
+    enc = m.backbone[0].encoder.encoder
+    for layer in enc.encoder.layer:
+        layer.layer_scale1.lambda1.data.uniform_(0.2, 1.0)
+        layer.layer_scale2.lambda1.data.uniform_(0.2, 1.0)
+    x = torch.randn(2, 3, 64, 64)
+    with torch.enable_grad():
+        ref = [f.detach() for f in enc(x)]
+    with torch.no_grad():
+        got = enc(x)
+    assert len(got) == len(ref)
+    for g, r in zip(got, ref):
+        assert torch.allclose(g, r, atol=1e-5, rtol=1e-5)
+
+
+def test_scaled_residual_layer_norm_reference():
+    from mmltk_b200.ops import scaled_residual_layer_norm
+    torch.manual_seed(0)
+    y, res = torch.randn(5, 7, 16), torch.randn(5, 7, 16)
+    g, w, b = torch.rand(16), torch.randn(16), torch.randn(16)
+    out, s = scaled_residual_layer_norm(y, res, g, w, b, 1e-6)
+    assert torch.allclose(s, res + g * y)
+    assert torch.allclose(out, torch.nn.functional.layer_norm(res + g * y, (16,), w, b, 1e-6), atol=1e-6)
