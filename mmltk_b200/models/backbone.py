@@ -24,6 +24,7 @@ separate ``query``/``key``/``value`` tensors through state-dict hooks.
 from __future__ import annotations
 
 import math
+import os
 from typing import List
 
 import torch
@@ -32,6 +33,9 @@ import torch.nn.functional as F
 
 from .. import ops
 from ..config import RfDetrConfig
+
+# MMLTK_INFER_FUSED_RESIDUAL=0: inference runs the per-layer autograd-path ops (A/B timing)
+_FUSED_RESIDUAL_INFERENCE = os.environ.get("MMLTK_INFER_FUSED_RESIDUAL", "1") != "0"
 
 
 class PatchEmbeddings(nn.Module):
@@ -233,7 +237,7 @@ class WindowedDinov2(nn.Module):
         x = self.embeddings(pixels)
         states = {}
         full_stages = set(self.taps)
-        if torch.is_grad_enabled():
+        if torch.is_grad_enabled() or not _FUSED_RESIDUAL_INFERENCE:
             for i, layer in enumerate(self.encoder.layer):
                 if i in full_stages:
                     states[i] = x
