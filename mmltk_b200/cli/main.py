@@ -203,6 +203,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--iters", type=int, default=200)
     p.add_argument("--device-id", type=int, default=0)
     p.add_argument("--device-ids", default="", help="e.g. 0,1,...,7: one replica per GPU, concurrent throughput")
+    p.add_argument("--no-pin-cpus", action="store_true",
+                   help="do not run the measuring thread on the GPU's NUMA-local CPUs")
     return ap
 
 
@@ -402,7 +404,8 @@ def _latency(a) -> int:
     if len(ids) > 1:
         return _latency_replicas(a, ids)
     pred, info = _predictor(a)
-    print(json.dumps({"preset_name": info["preset_name"], **pred.latency(a.iters, 20, a.batch_size)}))
+    r = pred.latency(a.iters, 20, a.batch_size, pin_cpus=not a.no_pin_cpus)
+    print(json.dumps({"preset_name": info["preset_name"], **r}))
     return 0
 
 
@@ -411,9 +414,9 @@ def _latency_worker(rank, a, ids, barrier, queue):
     a.device_id = ids[rank]
     torch.cuda.set_device(a.device_id)
     pred, info = _predictor(a)
-    pred.latency(5, 20, a.batch_size)          # graph capture and warm-up before the common start
+    pred.latency(5, 20, a.batch_size, pin_cpus=not a.no_pin_cpus)   # capture and warm-up before the start
     barrier.wait()
-    r = pred.latency(a.iters, 5, a.batch_size)
+    r = pred.latency(a.iters, 5, a.batch_size, pin_cpus=not a.no_pin_cpus)
     queue.put((rank, info["preset_name"], r))
 
 

@@ -78,7 +78,7 @@ class Predictor:
         self.cuda = self.device.type == "cuda"
         self.dtype = dtype if self.cuda else torch.float32
         self.model = model.eval().to(device=self.device, dtype=self.dtype)
-        if self.cuda:
+        if self.cuda and os.environ.get("MMLTK_CL_CONV_WEIGHTS", "1") != "0":
             # the convolutions run on channels-last activations; weights in the same layout spare
             # cuDNN a per-call weight transform (one copy kernel per 3x3 conv and forward)
             for mod in self.model.modules():
@@ -114,7 +114,18 @@ class Predictor:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 outs = self._step(static)
-            g = {"graph": graph, "input": static, "outputs": outs}
+                # the host-bound results packed into one byte buffer inside the graph, so that
+                # fetching them is one device-to-host copy (largest element size first: every
+                # segment then starts aligned for its dtype)
+                keys = sorted((k for k in outs if k != "masks"), key=lambda k: -outs[k].element_size())
+                packed = torch.cat([outs[k].contiguous().view(torch.uint8).reshape(-1) for k in keys])
+            layout, off = [], 0
+            for k in keys:
+                nb = outs[k].numel() * outs[k].element_size()
+                layout.append((k, off, nb, outs[k].dtype, tuple(outs[k].shape)))
+                off += nb
+            host = torch.empty(packed.numel(), dtype=torch.uint8, pin_memory=True)
+            g = {"graph": graph, "input": static, "outputs": outs, "packed": packed, "host": host, "layout": layout}
             self._graphs[key] = g
         return g
 
@@ -128,31 +139,64 @@ class Predictor:
         g["graph"].replay()
         return g["outputs"]
 
+    @torch.no_grad()
+    def predict_host(self, images: torch.Tensor) -> Dict[str, torch.Tensor]:
+        """Results in host memory (masks excluded).  Graph path: one asynchronous copy of the
+        packed results into a pinned buffer; the returned tensors are views of that buffer,
+        valid until the next call."""
+        if not self.use_graph:
+            r = self(images)
+            return {k: v.cpu() for k, v in r.items() if k != "masks"}
+        self(images)
+        g = self._graphs[(tuple(images.shape), images.dtype)]
+        host = g["host"]
+        host.copy_(g["packed"], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return {k: host[o:o + nb].view(dt).view(shape) for k, o, nb, dt, shape in g["layout"]}
+
     def release(self) -> None:
         self._graphs.clear()
 
     @torch.no_grad()
-    def latency(self, iters: int = 100, warmup: int = 10, batch: int = 1) -> Dict[str, float]:
-        """Batch-``batch`` latency percentiles (ms) of the device-side step, CUDA events, host uint8 input."""
+    def latency(self, iters: int = 100, warmup: int = 10, batch: int = 1, pin_cpus: bool = True) -> Dict[str, float]:
+        """Batch-``batch`` latency percentiles (ms): pinned host uint8 input -> results in pinned
+        host memory, bracketed by CUDA events.  ``pin_cpus``: run the calling thread on the GPU's
+        own NUMA node while measuring (the host enqueues the copies and the graph replay, so its
+        placement is on the critical path)."""
         x = torch.randint(0, 256, (batch, 3, *self.size), dtype=torch.uint8).pin_memory() if self.cuda else \
             torch.randint(0, 256, (batch, 3, *self.size), dtype=torch.uint8)
-        for _ in range(warmup):
-            r = self(x)
-        times = []
-        for _ in range(iters):
-            if self.cuda:
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                torch.cuda.synchronize(self.device)
-                a.record()
-                r = self(x)
-                host = {k: v.to("cpu", non_blocking=True) for k, v in r.items() if k != "masks"}
-                b.record()
-                b.synchronize()
-                times.append(a.elapsed_time(b))
-            else:
-                t0 = time.perf_counter()
-                self(x)
-                times.append((time.perf_counter() - t0) * 1e3)
+        saved = None
+        if self.cuda and pin_cpus:
+            from ..utils.runtime import gpu_local_cpus
+            local = gpu_local_cpus(self.device)
+            if local:
+                saved = os.sched_getaffinity(0)
+                os.sched_setaffinity(0, local)
+        try:
+            for _ in range(warmup):
+                self.predict_host(x) if self.cuda else self(x)
+            times = []
+            for _ in range(iters):
+                if self.cuda:
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    torch.cuda.synchronize(self.device)
+                    a.record()
+                    r = self(x)
+                    if self.use_graph:
+                        g = self._graphs[(tuple(x.shape), x.dtype)]
+                        g["host"].copy_(g["packed"], non_blocking=True)
+                    else:
+                        r = {k: v.to("cpu", non_blocking=True) for k, v in r.items() if k != "masks"}
+                    b.record()
+                    b.synchronize()
+                    times.append(a.elapsed_time(b))
+                else:
+                    t0 = time.perf_counter()
+                    self(x)
+                    times.append((time.perf_counter() - t0) * 1e3)
+        finally:
+            if saved is not None:
+                os.sched_setaffinity(0, saved)
         t = torch.tensor(times)
         return {"p50_ms": float(t.median()), "p90_ms": float(t.quantile(0.9)), "p99_ms": float(t.quantile(0.99)),
                 "mean_ms": float(t.mean()), "images_per_s": float(batch * 1e3 / t.mean()), "iters": iters,

@@ -27,7 +27,7 @@ from ..ops._ext import native
 
 log = logging.getLogger("mmltk.runtime")
 
-__all__ = ["HostRuntime", "setup_host_runtime", "rank_cpu_shards"]
+__all__ = ["HostRuntime", "setup_host_runtime", "rank_cpu_shards", "gpu_local_cpus"]
 
 
 @dataclasses.dataclass
@@ -91,3 +91,25 @@ def rank_cpu_shards(world: int, cpu_affinity: str = "") -> List[List[int]]:
     n = native()
     cpus = [int(c) for c in n.resolve_cpu_affinity(cpu_affinity or "")]
     return [list(n.shard_cpus(cpus, r, world)) for r in range(world)]
+
+
+def gpu_local_cpus(device) -> List[int]:
+    """CPUs of the GPU's own NUMA node (NVML's CPU affinity of the device, found by PCI bus id)
+    that this process may run on; empty when NVML or the bus id is unavailable."""
+    import torch
+    try:
+        import pynvml
+        props = torch.cuda.get_device_properties(device)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = (os.cpu_count() + 63) // 64
+            mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception as e:   # no NVML, no such attribute, not a physical GPU
+        log.debug("gpu_local_cpus: %s", e)
+        return []
+    local = {64 * w + b for w, m in enumerate(mask) for b in range(64) if (int(m) >> b) & 1}
+    return sorted(local & set(os.sched_getaffinity(0)))

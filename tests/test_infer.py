@@ -100,6 +100,11 @@ def test_graph_predictor_matches_eager(compiled32):
     torch.cuda.synchronize()
     assert torch.equal(a["queries"], g["queries"])
     assert torch.allclose(a["boxes"], g["boxes"], atol=1e-3)
+    host = graph.predict_host(x)                  # one packed device-to-host copy
+    for k, v in g.items():
+        if k != "masks":
+            assert not host[k].is_cuda and host[k].dtype == v.dtype and torch.equal(host[k], v.cpu()), k
     lat = graph.latency(iters=20, warmup=3, batch=1)
     assert lat["p50_ms"] > 0
+    assert graph.latency(iters=5, warmup=1, batch=1, pin_cpus=False)["p50_ms"] > 0
     graph.release()
