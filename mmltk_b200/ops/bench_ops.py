@@ -157,8 +157,18 @@ ATTN_SHAPES = [("dec.self_attn", 104, 8, 300, 32), ("vit.window", 32, 6, 325, 64
                ("vit.window.b1", 4, 6, 325, 64), ("vit.global.b1", 1, 6, 1300, 64)]
 
 
-def bench_attn(device="cuda"):
-    """Forward + backward of the step's attention shapes under each SDPA backend."""
+def bench_attn(device="cuda", quick=False):
+    """Forward + backward of the step's attention shapes under each SDPA backend.  ``quick``:
+    three launches of the tcgen05 forward on the ViT global shape, untimed (profiler runs)."""
+    if quick:
+        from .attention import qkv_attention_tc
+        g = torch.Generator(device=device).manual_seed(0)
+        qkv = torch.randn(8, 1300, 3 * 384, device=device, generator=g).bfloat16()
+        with torch.no_grad():
+            for _ in range(3):
+                qkv_attention_tc(qkv, 6)
+        torch.cuda.synchronize()
+        return [{"op": "attention", "shape": "vit.global", "quick": True}]
     from torch.nn.attention import SDPBackend, sdpa_kernel
     import torch.nn.functional as F
     rows = []
@@ -208,7 +218,7 @@ def main():
     elif args.what == "msda":
         rows = bench_msda(quick=args.quick)
     else:
-        rows = bench_attn()
+        rows = bench_attn(quick=args.quick)
     for r in rows:
         print(json.dumps(r))
 
