@@ -50,10 +50,14 @@ def newton_schulz5(g: torch.Tensor, steps: int = NS_STEPS) -> torch.Tensor:
     if t:
         x = x.transpose(-2, -1)
     x = x / (x.flatten(-2).norm(dim=-1)[..., None, None] + NORM_EPS)
+    lead = x.shape[:-2]
+    x = x.reshape(-1, *x.shape[-2:])
     for _ in range(steps):
-        gram = x @ x.transpose(-2, -1)
-        poly = b * gram + c * (gram @ gram)
-        x = a * x + poly @ x
+        # three GEMMs per step, the polynomial's scaling and sums in their alpha / beta epilogues
+        gram = torch.bmm(x, x.transpose(-2, -1))
+        poly = torch.baddbmm(gram, gram, gram, beta=b, alpha=c)       # b*G + c*G.G
+        x = torch.baddbmm(x, poly, x, beta=a, alpha=1.0)              # a*X + P.X
+    x = x.reshape(*lead, *x.shape[-2:])
     if t:
         x = x.transpose(-2, -1)
     return x
