@@ -38,14 +38,17 @@ METRIC = "RF-DETR-M train img/s @1/2/4/8 B200 (max over ranks); b1 infer p50 ms"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--preset", default="rf-detr-medium")
     ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--kmax", type=int, default=10, help="boxes per image K ~ U{1..kmax} (config 4: 40)")
     ap.add_argument("--ddp", default=os.environ.get("MMLTK_DDP", "fused"), choices=["fused", "nccl"])
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--no-infer", action="store_true", help="skip the batch-1 inference latency")
+    ap.add_argument("--no-infer", action="store_true", help="skip the inference half of the metric")
+    ap.add_argument("--infer-preset", default="rf-detr-base")
+    ap.add_argument("--infer-select", type=int, default=100, help="post-process top-k (config 5: top-100)")
     ap.add_argument("--profile-launches", action="store_true", default=True)
     return ap.parse_args()
 
@@ -106,16 +109,215 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_DIR = os.path.join(HERE, "baseline", "_ref")
+
+
+def _load_reference():
+    """The reference built from its unmodified sources (baseline/build_reference.py), or None + why."""
+    import glob
+    import importlib.util
+    so = sorted(glob.glob(os.path.join(REF_DIR, "mmltk_ref*.so")))
+    if not so:
+        return None, ("reference not built in baseline/_ref (python baseline/build_reference.py compiles the "
+                      "unmodified rlewkowicz/mmltk libtorch sources; pip cannot install it: no setup.py/pyproject)")
+    import torch  # noqa: F401  (libtorch symbols for the module)
+    spec = importlib.util.spec_from_file_location("mmltk_ref", so[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod, None
+
+
+def _ref_synthetic(batch, res, seed, kmin=1, kmax=10, num_labels=80):
+    """Config-2 inputs with plain torch (same draw order as the framework's generator, so both arms
+    see the same images and boxes): N(0,1) images, K ~ U{kmin..kmax} boxes per image, centres
+    U(0.1, 0.9), w/h U(0.02, 0.4), labels U{0..num_labels-1}."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    imgs = torch.randn(batch, 3, res, res, generator=g)
+    boxes, labels, counts = [], [], []
+    for _ in range(batch):
+        k = int(torch.randint(kmin, kmax + 1, (1,), generator=g))
+        c = torch.rand(k, 2, generator=g) * 0.8 + 0.1
+        wh = torch.rand(k, 2, generator=g) * 0.38 + 0.02
+        boxes.append(torch.cat([c, wh], 1))
+        labels.append(torch.randint(0, num_labels, (k,), generator=g))
+        counts.append(k)
+    return imgs, torch.cat(boxes), torch.cat(labels), counts
+
+
+# The reference has no "base" preset; config 5's RF-DETR-Base is built from explicit fields
+# (560 px, patch 14 -> 40x40 tokens, 2 windows, 40x40 position table, 3 decoder layers).
+REF_SHAPES = {"rf-detr-base": dict(resolution=560, patch_size=14, num_windows=2, pos_size=40, dec_layers=3)}
+
+
 def reference_arm(args):
-    ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
-    why = ("rlewkowicz/mmltk is a CMake/libtorch C++20 project with no setup.py/pyproject (pip install fails: "
-           "'Neither setup.py nor pyproject.toml found'); its build also needs spdlog, ONNX, ONNX Runtime, "
-           "TensorRT and a CUDA 13.0 toolchain that this image does not have")
-    if not os.path.isdir(ref) or not os.listdir(ref):
+    mod, why = _load_reference()
+    if mod is None:
         print(json.dumps({"impl": "reference", "unavailable": why}))
         return 0
-    print(json.dumps({"impl": "reference", "unavailable": why}))
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    torch.manual_seed(0)
+    shape = REF_SHAPES.get(args.preset, {})
+    trainer = mod.RefTrainer(args.preset, args.batch, local, "selective", world_size=world, **shape)
+    res = trainer.resolution
+
+    def allreduce(tensors):
+        # train.cpp:1389-1410 (allreduce_coalesced of every gradient) and detection_ops.cpp:1501-1510
+        # (num_boxes): the same NCCL sums, issued as one coalesced group
+        with dist._coalescing_manager(async_ops=False):
+            for t in tensors:
+                dist.all_reduce(t)
+
+    reduce_fn = allreduce if world > 1 else None
+    nb = 4
+    host = []
+    for i in range(nb):
+        imgs, boxes, labels, counts = _ref_synthetic(args.batch, res, seed=1000 * rank + i, kmax=args.kmax)
+        # the loader's pixel format: float32 planar RGB in [0, 1] (pinned), normalised on the device
+        imgs01 = (imgs * torch.tensor([0.229, 0.224, 0.225])[:, None, None]
+                  + torch.tensor([0.485, 0.456, 0.406])[:, None, None]).contiguous()
+        host.append((imgs.pin_memory(), imgs01.pin_memory(), boxes.pin_memory(), labels.pin_memory(), counts))
+    dev_batches = [(h[0].to(dev), h[2].to(dev), h[3].to(dev), h[4]) for h in host]
+    pre = mod.RefPreprocessor(args.batch, res, res, local)
+    staged = torch.empty(args.batch, 3, res, res, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    for w in range(max(args.warmup, 3)):
+        x, b, l, c = dev_batches[w % nb]
+        trainer.step(x, b, l, c, reduce_fn)
+    barrier()
+
+    def timed(k, fn):
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        barrier()
+        start.record()
+        for s in range(k):
+            fn(s)
+        end.record()
+        barrier()
+        t = torch.tensor([start.elapsed_time(end)], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
+    losses = []
+
+    def dev_step(s):
+        x, b, l, c = dev_batches[s % nb]
+        losses.append(trainer.step(x, b, l, c, reduce_fn))
+
+    wall0 = time.time()
+    ms_dev = timed(args.steps, dev_step)
+    wall_dev = time.time() - wall0
+
+    def e2e_step(s):
+        _, x01, b, l, c = host[s % nb]
+        staged.copy_(x01, non_blocking=True)
+        x = pre.run(staged)
+        losses.append(trainer.step(x, b.to(dev, non_blocking=True), l.to(dev, non_blocking=True), c, reduce_fn))
+
+    wall1 = time.time()
+    ms_e2e = timed(args.steps, e2e_step)
+    wall_e2e = time.time() - wall1
+    clocks = sampler.stop(set(range(args.gpus))) if sampler else None
+    del trainer
+    torch.cuda.empty_cache()
+
+    infer = None
+    if rank == 0 and not args.no_infer:
+        infer = _ref_infer(mod, args, local, dev)
+    if world > 1:
+        barrier()
+    if rank == 0:
+        imgs_total = args.batch * args.steps * world
+        h2d = args.batch * 3 * res * res * 4 + sum(h[2].numel() * 4 + h[3].numel() * 8 for h in host) // nb
+        out = {
+            "impl": "reference", "metric": METRIC, "value": round(imgs_total / (ms_dev / 1e3), 2), "unit": "img/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_dev / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": ("synthetic: N(0,1) images (e2e: the same images as float32 [0,1] pinned host blobs, copied and "
+                     f"normalised by the reference's GpuBatchPreprocessor every step), K~U{{1..{args.kmax}}} boxes; "
+                     "random-init weights"),
+            "config": {"model": args.preset, "global_batch": args.batch * world, "seq_len": None, "resolution": res,
+                       "queries": None, "parallelism": f"dp{world}",
+                       "ddp": "nccl allreduce_coalesced after backward" if world > 1 else "none",
+                       "compile_mode": "selective (reference default)", "optimizer": "NativeAdamW fused + ModelEma",
+                       "l2": "not flushed: per-step working set (activations, several GB) >> 126 MB L2"},
+            "e2e": {"value": round(imgs_total / (ms_e2e / 1e3), 2), "unit": "img/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": 32, "ms_per_step": round(ms_e2e / args.steps, 3)},
+            "wall_s": {"value_region": round(wall_dev, 3), "e2e_region": round(wall_e2e, 3)},
+            "gpu_launches": None,
+            "infer_b1": infer,
+            "clocks": clocks,
+            "final_loss": losses[-1] if losses else None,
+            "reference": {"build": "baseline/build_reference.py (unmodified sources, torch.utils.cpp_extension)",
+                          "num_parameters": None},
+        }
+        print(json.dumps(out))
+    if world > 1:
+        dist.destroy_process_group()
     return 0
+
+
+def _ref_infer(mod, args, local, dev):
+    """Reference inference on config 5: RefPredictor (eval NativeRfDetrModel under bf16 autocast +
+    postprocess_output_batch_fixed_size), float32 [0,1] pinned input -> GpuBatchPreprocessor -> model
+    -> top-k -> results copied to pinned host memory, CUDA-event timed per call."""
+    import torch
+    shape = REF_SHAPES.get(args.infer_preset, {})
+    out = {"model": args.infer_preset, "dtype": "bf16", "num_select": args.infer_select}
+    for batch, iters in ((1, 200), (32, 30)):
+        p = mod.RefPredictor(args.infer_preset, batch, local, "selective", num_select=args.infer_select, **shape)
+        res = p.resolution
+        pre = mod.RefPreprocessor(batch, res, res, local)
+        x01 = torch.rand(batch, 3, res, res).pin_memory()
+        staged = torch.empty(batch, 3, res, res, device=dev)
+        host = None
+        times = []
+        for it in range(iters + 10):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record()
+            staged.copy_(x01, non_blocking=True)
+            r = p.run(pre.run(staged))
+            if host is None:
+                host = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in r]
+            for h, t in zip(host, r):
+                h.copy_(t, non_blocking=True)
+            b.record()
+            b.synchronize()
+            if it >= 10:
+                times.append(a.elapsed_time(b))
+        t = torch.tensor(times)
+        if batch == 1:
+            out.update({"resolution": res, "batch": 1, "p50_ms": round(float(t.median()), 4),
+                        "p99_ms": round(float(t.quantile(0.99)), 4), "mean_ms": round(float(t.mean()), 4)})
+        else:
+            out["b32"] = {"images_per_s": round(batch * 1e3 / float(t.mean()), 1),
+                          "p50_ms": round(float(t.median()), 4)}
+        del p, pre
+        torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -156,7 +358,7 @@ def main():
         else:
             from mmltk_b200.parallel.ddp import NcclGradSync
             sync = NcclGradSync()
-    T = 10
+    T = args.kmax
     engine = TrainEngine(model, opts, dev, grad_sync=sync, max_targets=T, steps_per_epoch=1000, total_steps=1000)
     engine.bind_static_inputs(args.batch, 3, cfg.resolution, cfg.resolution)
 
@@ -164,7 +366,7 @@ def main():
     nb = 4
     host_batches = []
     for i in range(nb):
-        imgs, tg = synthetic_batch(args.batch, cfg.resolution, seed=1000 * rank + i, kmax=10, slots=T,
+        imgs, tg = synthetic_batch(args.batch, cfg.resolution, seed=1000 * rank + i, kmax=args.kmax, slots=T,
                                    dtype=torch.bfloat16)
         imgs = imgs.pin_memory()
         tg.boxes = tg.boxes.pin_memory()
@@ -240,15 +442,23 @@ def main():
     if args.profile_launches:
         launches = count_launches(engine, dev_batches[0], args.steps)
 
-    # second half of the metric: batch-1 inference latency (same architecture, eval mode, CUDA-graph
-    # Predictor, pinned uint8 input -> preprocess -> model -> top-k post-process -> D2H), rank 0 only
+    # second half of the metric (config 5): RF-DETR-Base 560 inference, eval mode, CUDA-graph
+    # Predictor, pinned uint8 input -> preprocess -> model -> top-100 post-process -> D2H, rank 0 only
     infer = None
     if rank == 0 and not args.no_infer:
         from mmltk_b200.infer import Predictor
+        engine.release_graph()
+        engine = None                     # training buffers freed before the inference model is built
+        torch.cuda.empty_cache()
+        icfg = config_from_preset(args.infer_preset)
         torch.manual_seed(0)
-        pred = Predictor(RFDETR(cfg).eval(), device=dev)
-        infer = {"model": args.preset, "batch": 1, "resolution": cfg.resolution, "dtype": "bf16",
-                 **{k: (round(v, 4) if isinstance(v, float) else v) for k, v in pred.latency(200, 20, 1).items()}}
+        pred = Predictor(RFDETR(icfg).eval(), device=dev, num_select=args.infer_select)
+        b1 = pred.latency(200, 20, 1)
+        b32 = pred.latency(30, 5, 32)
+        infer = {"model": args.infer_preset, "batch": 1, "resolution": icfg.resolution, "dtype": "bf16",
+                 "num_select": args.infer_select,
+                 **{k: (round(v, 4) if isinstance(v, float) else v) for k, v in b1.items()},
+                 "b32": {"images_per_s": round(b32["images_per_s"], 1), "p50_ms": round(b32["p50_ms"], 4)}}
         pred.release()
         del pred
 
@@ -263,9 +473,9 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "img/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_dev / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": ("synthetic: value = N(0,1) images resident on the device; e2e = random uint8 PNG dataset "
-                     "(K~U{0..9} boxes) compiled to the native format and read through BatchLoader + GpuAugmenter; "
-                     "random-init weights"),
+            "data": (f"synthetic: value = N(0,1) images, K~U{{1..{args.kmax}}} boxes, resident on the device; e2e = "
+                     f"random uint8 PNG dataset (K~U{{1..{args.kmax}}} boxes) compiled to the native format and read through "
+                     "BatchLoader + GpuAugmenter; random-init weights"),
             "config": {"model": args.preset, "global_batch": args.batch * world, "seq_len": (cfg.resolution // cfg.patch_size) ** 2,
                        "resolution": cfg.resolution, "queries": cfg.num_queries * cfg.group_detr,
                        "parallelism": f"dp{world}", "ddp": (args.ddp if world > 1 else "none"),
@@ -281,7 +491,8 @@ def main():
         }
         print(json.dumps(out))
     if world > 1:
-        engine.release_graph()
+        if engine is not None:
+            engine.release_graph()
         dist.destroy_process_group()
     return 0
 
@@ -304,8 +515,8 @@ class E2EPipeline:
         root = tempfile.mkdtemp(prefix=f"mmltk_bench_r{rank}_")
         atexit.register(shutil.rmtree, root, True)     # the synthetic dataset is scratch
         write_synthetic_source(os.path.join(root, "src"), splits=("train",), images=images_per_rank,
-                               size=(res, res), classes=min(80, cfg.num_classes - 1), max_instances=slots - 1,
-                               seed=1000 + rank)
+                               size=(res, res), classes=min(80, cfg.num_classes - 1), max_instances=slots,
+                               min_instances=1, seed=1000 + rank)
         path = compile_split(os.path.join(root, "src"), os.path.join(root, "bin"), "train", res, res)["path"]
         # the host runtime a training run sets up: this rank's CPU shard, pinned loader / pool / lane
         from mmltk_b200.ops._ext import native

@@ -11,7 +11,7 @@
 //
 // The caller passes every input and output buffer.  The fp32 accumulators
 // the backward pass needs live in a fixed array inside this library
-// (kNoallocMaxValueElems + kNoallocMaxRefElems floats, 36 MiB), which every
+// (MMLTK_NOALLOC_MAX_VALUE_ELEMS + MMLTK_NOALLOC_MAX_REF_ELEMS floats, 36 MiB), which every
 // GPU that loads the library keeps until the process exits.
 //
 // Set-up: the first call on a device looks up the array's device address

@@ -29,22 +29,6 @@ NVCC_FLAGS = [
 CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-DNDEBUG"]
 
 
-def _cutlass_include():
-    """CUTLASS/CuTe headers vendored with flashinfer (used as headers only)."""
-    try:
-        import flashinfer  # noqa: F401
-        base = os.path.dirname(sys.modules["flashinfer"].__file__)
-    except Exception:
-        base = None
-    cands = []
-    if base:
-        cands.append(os.path.join(base, "data", "cutlass", "include"))
-    for c in cands:
-        if os.path.isdir(os.path.join(c, "cute")):
-            return c
-    return None
-
-
 def extensions():
     from torch.utils.cpp_extension import CppExtension, CUDAExtension
 
@@ -56,8 +40,7 @@ def extensions():
         CppExtension("mmltk_b200._native", host_src, include_dirs=inc + [os.path.join(ROOT, "csrc", "host")],
                      extra_compile_args={"cxx": CXX_FLAGS}, extra_link_args=["-lpthread", "-lz"]),
         CUDAExtension("mmltk_b200._kernels", kern_src, include_dirs=inc,
-                      extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
-                      libraries=["cuda"] if False else []),
+                      extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS}),
     ]
 
 

@@ -84,6 +84,9 @@ class SetCriterion:
         # fused CUDA path for the detection terms (the per-layer torch statement is the oracle)
         self.fused = os.environ.get("MMLTK_FUSED_LOSS", "1") != "0"
         self._match_full = None
+        # optional int32 device word [1] that collects the GPU assignment solver's status (the
+        # training engine points it at its per-step flags and raises when it is non-zero)
+        self.match_status: Optional[torch.Tensor] = None
 
     # ---------------------------------------------------------------- helpers
     def num_boxes(self, targets: Targets, groups: int) -> torch.Tensor:
@@ -196,7 +199,8 @@ class SetCriterion:
                 mcost = [mask_cost(layers[i], targets, cfg.mask_ce_loss_coef, cfg.mask_dice_loss_coef,
                                    cfg.mask_point_sample_ratio) for i in idx]
             mm = hungarian_match([layers[i]["pred_logits"] for i in idx], [layers[i]["pred_boxes"] for i in idx],
-                                 targets, g, cfg.set_cost_class, cfg.set_cost_bbox, cfg.set_cost_giou, mcost)
+                                 targets, g, cfg.set_cost_class, cfg.set_cost_bbox, cfg.set_cost_giou, mcost,
+                                 status_out=self.match_status)
             for j, i in enumerate(idx):
                 match[i] = mm[j]
             if len(by_q) == 1:

@@ -17,7 +17,7 @@ solver on the worker pool.
 """
 from __future__ import annotations
 
-from typing import List, Sequence
+from typing import List, Optional, Sequence
 
 import torch
 import torch.nn.functional as F
@@ -89,8 +89,13 @@ def mask_cost(layer: dict, targets: Targets, ce_coef: float, dice_coef: float, r
 
 
 def hungarian_match(logits: List[torch.Tensor], boxes: List[torch.Tensor], targets: Targets, groups: int,
-                    w_class: float = 2.0, w_bbox: float = 5.0, w_giou: float = 2.0, mask_costs=None) -> torch.Tensor:
-    """mask_costs: optional list (one per layer) of [B, Q, T] costs added before the assignment."""
+                    w_class: float = 2.0, w_bbox: float = 5.0, w_giou: float = 2.0, mask_costs=None,
+                    status_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """mask_costs: optional list (one per layer) of [B, Q, T] costs added before the assignment.
+
+    status_out: optional int32 device tensor [1]; the GPU solver's status word (non-zero when a
+    bounded augmenting-path search gave up and the assignment is partial) is OR-ed into it on the
+    device, so a caller can check it once per step without a host sync here."""
     with torch.no_grad():
         dev = logits[0].device
         if dev.type == "cuda":   # cost build + batched LSAP on the device (any target / query ratio)
@@ -99,7 +104,9 @@ def hungarian_match(logits: List[torch.Tensor], boxes: List[torch.Tensor], targe
                                   targets.boxes, targets.counts, w_class, w_bbox, w_giou, FOCAL_ALPHA)
             if mask_costs is not None:
                 cost += torch.stack(mask_costs).to(cost.dtype)
-            match, _status = k.lsap_batched(cost, targets.counts, groups)
+            match, status = k.lsap_batched(cost, targets.counts, groups)
+            if status_out is not None:
+                status_out.bitwise_or_(status)
             return match
         cost = matcher_cost_reference(logits, boxes, targets, w_class, w_bbox, w_giou)
         if mask_costs is not None:

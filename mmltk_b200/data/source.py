@@ -26,7 +26,7 @@ def _rle(mask: torch.Tensor) -> str:
 
 
 def write_synthetic_source(root: str, splits=("train", "val"), images: int = 8, size=(96, 80), classes: int = 3,
-                           max_instances: int = 4, seed: int = 0, masks: bool = True) -> str:
+                           max_instances: int = 4, seed: int = 0, masks: bool = True, min_instances: int = 0) -> str:
     g = torch.Generator().manual_seed(seed)
     w, h = size
     os.makedirs(root, exist_ok=True)
@@ -39,7 +39,7 @@ def write_synthetic_source(root: str, splits=("train", "val"), images: int = 8, 
         for k in range(1, images + 1):
             img = (torch.rand(h, w, 3, generator=g) * 255).to(torch.uint8)
             lines = []
-            for _ in range(int(torch.randint(0, max_instances + 1, (1,), generator=g))):
+            for _ in range(int(torch.randint(min_instances, max_instances + 1, (1,), generator=g))):
                 x1 = int(torch.randint(0, w - 12, (1,), generator=g))
                 y1 = int(torch.randint(0, h - 12, (1,), generator=g))
                 x2 = min(w, x1 + int(torch.randint(8, w // 2, (1,), generator=g)))

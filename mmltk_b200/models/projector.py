@@ -5,10 +5,16 @@ Reference (`src/rfdetr/layers/model.cpp:267-369,705-726`): single P4 level,
 ConvX = Conv(no bias) -> LayerNorm2d (eps 1e-6) -> SiLU; Bottleneck = two 3x3
 ConvX without a shortcut.
 
-The level list is configuration here: "P3" upsamples the taps x2 with a
-transposed conv before its C2f, "P5" downsamples /2 with a strided 3x3 ConvX,
-"P4" uses the taps as they are.  Features are channels-last [B, h, w, C]
-throughout (LayerNorm2d is then a plain last-dim LayerNorm and 1x1 convs are
+The level list is configuration here, laid out like upstream RF-DETR's
+multi-scale projector: every level resamples EACH backbone tap on its own
+(``stages_sampling[level][tap]``) and concatenates the results into that
+level's C2f.  "P3" (scale 2) is one 2x2 stride-2 transposed conv per tap
+(C -> C/2; the C2f then sees taps * C/2 channels), "P5" (scale 1/2) one
+stride-2 3x3 ConvX per tap (C -> C), "P4" (scale 1) the tap unchanged (an
+empty ``Sequential``, so a P4-only model has the reference's state-dict
+layout), "P6" (scale 1/4) a stride-2 max-pool of the previous level's output.
+Features are channels-last [B, h, w, C] throughout (LayerNorm2d is then a
+plain last-dim LayerNorm, 1x1 convs and the 2x2/stride-2 transposed convs are
 GEMMs); 3x3 convs run as cuDNN channels-last convolutions.
 """
 from __future__ import annotations
@@ -84,52 +90,59 @@ class ProjectorStage(nn.Sequential):
         return self[1].forward_nhwc(self[0].forward_nhwc(x))
 
 
-class Upsample2x(nn.Module):
-    def __init__(self, c: int):
-        super().__init__()
-        self.conv = nn.ConvTranspose2d(c, c // 2, kernel_size=2, stride=2)
-        self.bn = LayerNorm2d(c // 2)
+class TransposedConv2x(nn.ConvTranspose2d):
+    """2x2, stride-2 transposed conv on channels-last features.  Each input pixel writes its own
+    2x2 output patch, so it is one GEMM ``[B*h*w, C] x [C, 4*C']`` plus a pixel shuffle."""
 
-    def forward_nhwc(self, x):
-        y = F.conv_transpose2d(x.permute(0, 3, 1, 2), self.conv.weight.to(x.dtype), self.conv.bias.to(x.dtype),
-                               stride=2).permute(0, 2, 3, 1)
-        return F.gelu(self.bn.forward_nhwc(y))
+    def __init__(self, cin: int, cout: int):
+        super().__init__(cin, cout, kernel_size=2, stride=2)
+
+    def forward_nhwc(self, x: torch.Tensor) -> torch.Tensor:
+        B, h, w, C = x.shape
+        co = self.out_channels
+        wm = self.weight.to(x.dtype).permute(2, 3, 1, 0).reshape(4 * co, C)     # rows (dy, dx, co)
+        bias = self.bias.to(x.dtype).repeat(4)
+        y = ops.linear(x, wm, bias)                                               # [B, h, w, 4*co]
+        return y.view(B, h, w, 2, 2, co).permute(0, 1, 3, 2, 4, 5).reshape(B, 2 * h, 2 * w, co)
+
+
+def _sampling_layer(level: str, c: int) -> nn.Sequential:
+    if level == "P3":
+        return nn.Sequential(TransposedConv2x(c, c // 2))
+    if level == "P5":
+        return nn.Sequential(ConvX(c, c, 3, 2))
+    return nn.Sequential()      # P4: identity
+
+
+def _level_channels(level: str, c: int) -> int:
+    return c // 2 if level == "P3" else c
 
 
 class MultiScaleProjector(nn.Module):
     def __init__(self, in_channels: int, num_taps: int, out_channels: int, levels, blocks: int = 3):
         super().__init__()
         self.levels = tuple(levels)
-        cin = in_channels * num_taps
-        self.stages_sampling = nn.ModuleList()
-        self.stages = nn.ModuleList()
-        self.needs_sampling = any(l != "P4" for l in self.levels)
-        for lvl in self.levels:
-            if lvl == "P4":
-                samp, c = nn.Identity(), cin
-            elif lvl == "P3":
-                samp, c = Upsample2x(cin), cin // 2
-            elif lvl == "P5":
-                samp, c = ConvX(cin, cin, 3, 2), cin
-            else:  # P6
-                samp, c = nn.Sequential(ConvX(cin, cin, 3, 2), ConvX(cin, cin, 3, 2)), cin
-            self.stages_sampling.append(samp)
-            self.stages.append(ProjectorStage(C2f(c, out_channels, blocks), LayerNorm2d(out_channels)))
-        if not self.needs_sampling:
-            # keep the reference's state-dict layout (`projector.stages.0.*` only)
-            del self.stages_sampling
+        self.extra_pool = self.levels[-1] == "P6"
+        conv_levels = self.levels[:-1] if self.extra_pool else self.levels
+        if not conv_levels:
+            raise ValueError("the projector needs at least one of P3 / P4 / P5 before P6")
+        self.stages_sampling = nn.ModuleList(
+            nn.ModuleList(_sampling_layer(lvl, in_channels) for _ in range(num_taps)) for lvl in conv_levels)
+        self.stages = nn.ModuleList(
+            ProjectorStage(C2f(num_taps * _level_channels(lvl, in_channels), out_channels, blocks),
+                           LayerNorm2d(out_channels)) for lvl in conv_levels)
 
     def forward(self, taps: List[torch.Tensor]) -> List[torch.Tensor]:
-        x = torch.cat(taps, -1)
         outs = []
-        for i, lvl in enumerate(self.levels):
-            h = x
-            if self.needs_sampling:
-                samp = self.stages_sampling[i]
-                if isinstance(samp, nn.Sequential):
-                    for m in samp:
-                        h = m.forward_nhwc(h)
-                elif not isinstance(samp, nn.Identity):
-                    h = samp.forward_nhwc(h)
-            outs.append(self.stages[i].forward_nhwc(h))
+        for stage, sampling in zip(self.stages, self.stages_sampling):
+            fused = []
+            for tap, samp in zip(taps, sampling):
+                h = tap
+                for m in samp:
+                    h = m.forward_nhwc(h)
+                fused.append(h)
+            x = torch.cat(fused, -1) if len(fused) > 1 else fused[0]
+            outs.append(stage.forward_nhwc(x))
+        if self.extra_pool:
+            outs.append(outs[-1][:, ::2, ::2, :])      # max-pool with kernel 1, stride 2
         return outs

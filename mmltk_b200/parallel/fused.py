@@ -62,6 +62,7 @@ class FusedGradSync:
         self._handles: List[bytes] = []
         self._keep = []
         self._opened: List[int] = []
+        self.failed: Optional[str] = None
 
     # ---------------------------------------------------------------- buffers
     def alloc(self, numel: int, dtype) -> torch.Tensor:
@@ -118,6 +119,8 @@ class FusedGradSync:
         return t
 
     def step(self, engine) -> None:
+        if self.failed is not None:
+            raise RuntimeError(f"fused DDP gradient step is unusable after an earlier failure: {self.failed}")
         self.comm.rs(self.off, self.size, self.gshard, self.partials)
         self.comm.update(self.off, self.chunks, self.gshard, engine.master_shard, engine.m, engine.v, engine.ema_buf,
                          engine.group_hyper, engine.scalars, engine.flags)
@@ -129,9 +132,13 @@ class FusedGradSync:
         return self.ctrl[3:4]
 
     def check(self, code: int) -> None:
+        """Raise if the step's kernels reported a status.  A timed-out wait leaves the kernels'
+        arrival counters part-way through a step, so the sync cannot be used again: every later
+        ``step`` raises too (recover by restarting the ranks and resuming from a checkpoint)."""
         if code:
-            raise RuntimeError(f"fused DDP step failed on rank {self.rank}: {ERRORS.get(code, code)} "
-                               f"within the wait limit")
+            self.failed = (f"fused DDP step failed on rank {self.rank}: {ERRORS.get(code, code)} "
+                           f"within the wait limit")
+            raise RuntimeError(self.failed)
 
     # ---------------------------------------------------------------- state
     def gather_full(self, shard: torch.Tensor) -> torch.Tensor:

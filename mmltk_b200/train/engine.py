@@ -46,12 +46,14 @@ class StepResult:
 
 class PendingStep:
     """Handle of a step queued by ``TrainEngine.step_async``."""
-    __slots__ = ("engine", "rb", "event", "partial", "step", "_done")
+    __slots__ = ("engine", "rb", "event", "partial", "step", "_done", "_slot", "_gen")
 
     def __init__(self, engine, rb, event, partial: StepResult):
         self.engine, self.rb, self.event, self.partial = engine, rb, event, partial
         self.step = engine.step_count
         self._done = partial if rb is None else None
+        # which pinned readback slot holds this step's values, and that slot's use count then
+        self._slot, self._gen = (engine._rb_last if rb is not None else (None, None))
 
     def ready(self) -> bool:
         return self._done is not None or self.event.query()
@@ -59,6 +61,10 @@ class PendingStep:
     def result(self) -> StepResult:
         if self._done is None:
             self.event.synchronize()
+            if self.engine._rb_gen[self._slot] != self._gen:
+                raise RuntimeError(
+                    f"step {self.step}'s readback slot was reused by a later step: at most "
+                    f"{len(self.engine._readbacks) - 1} more steps may be queued before result() is called")
             self._done = self.engine._read_result(self.rb, self.partial.losses, self.step)
         return self._done
 
@@ -132,7 +138,10 @@ class TrainEngine:
         nsc = k.step_scalar_floats()
         self.scalars_host = torch.zeros(nsc, dtype=torch.float32).pin_memory()
         self.scalars = torch.zeros(nsc, dtype=torch.float32, device=self.device)
-        self.flags = torch.zeros(2, dtype=torch.int32, device=self.device)
+        # per-step status words: [0] non-finite gradients, [1] gradient norm (fp32 bits),
+        # [2] GPU assignment-solver status (non-zero: a bounded search gave up)
+        self.flags = torch.zeros(3, dtype=torch.int32, device=self.device)
+        self.criterion.match_status = self.flags[2:3]
         self.muon = None
         if self.opts.optimizer == "muon":
             # Muon runs eagerly on the master weights (fp32 views into the flat buffer)
@@ -161,7 +170,9 @@ class TrainEngine:
     def _alloc_readback(self) -> None:
         # a ring of pinned readback slots: a deferred step's values stay readable while up to
         # three more steps are queued behind it
-        self._readbacks = [torch.zeros(4, dtype=torch.float32).pin_memory() for _ in range(4)]
+        self._readbacks = [torch.zeros(5, dtype=torch.float32).pin_memory() for _ in range(4)]
+        self._rb_gen = [0] * len(self._readbacks)
+        self._rb_last = (0, 0)
         self._rb_turn = 0
         self.readback = self._readbacks[0]
 
@@ -299,21 +310,28 @@ class TrainEngine:
         return PendingStep(self, rb, ev, StepResult(None, r.losses, None, None))
 
     def _queue_readback(self, total) -> torch.Tensor:
-        rb = self._readbacks[self._rb_turn]
+        slot = self._rb_turn
+        rb = self._readbacks[slot]
+        self._rb_gen[slot] += 1
+        self._rb_last = (slot, self._rb_gen[slot])
         self._rb_turn = (self._rb_turn + 1) % len(self._readbacks)
         rb[0:1].copy_(total.reshape(1), non_blocking=True)
-        rb[1:3].copy_(self.flags.view(torch.float32), non_blocking=True)
+        rb[1:4].copy_(self.flags.view(torch.float32), non_blocking=True)
         sync_status = getattr(self.grad_sync, "status_tensor", None)
         if sync_status is not None:
-            rb[3:4].copy_(sync_status().view(torch.float32), non_blocking=True)
+            rb[4:5].copy_(sync_status().view(torch.float32), non_blocking=True)
         return rb
 
     def _read_result(self, rb: torch.Tensor, losses, step: int) -> StepResult:
         if getattr(self.grad_sync, "status_tensor", None) is not None:
-            self.grad_sync.check(self.flags_host_bits(rb[3]))
+            self.grad_sync.check(self.flags_host_bits(rb[4]))
         loss = float(rb[0])
         nonfinite = int(self.flags_host_bits(rb[1]))
         norm = float(rb[2])
+        match_status = int(self.flags_host_bits(rb[3]))
+        if match_status:
+            raise RuntimeError(f"GPU Hungarian matcher gave up on a bounded search at step {step} "
+                               f"(status {match_status}); the assignment would be partial")
         if nonfinite or not math.isfinite(loss):
             raise FloatingPointError(f"non-finite RF-DETR loss ({loss}) or gradients (norm {norm}) at step {step}")
         return StepResult(loss, losses, norm, nonfinite)

@@ -162,6 +162,32 @@ def test_large_vitb_p3p5_builds():
     assert o["pred_boxes"].shape == (1, 20, 4)
 
 
+def test_large_vitb_projector_layout_and_size():
+    """Config 4: each backbone tap is resampled on its own (upstream ``stages_sampling[level][tap]``
+    layout), which gives ~128 M parameters for ViT-B with P3 + P5."""
+    cfg = config_from_preset("rf-detr-large-vitb")
+    m = RFDETR(cfg)
+    n = sum(p.numel() for p in m.parameters())
+    assert abs(n - 128e6) / 128e6 < 0.05, n
+    sd = m.state_dict()
+    assert tuple(sd["backbone.0.projector.stages_sampling.0.3.0.weight"].shape) == (768, 384, 2, 2)
+    assert tuple(sd["backbone.0.projector.stages_sampling.1.3.0.conv.weight"].shape) == (768, 768, 3, 3)
+    assert tuple(sd["backbone.0.projector.stages.0.0.cv1.conv.weight"].shape)[1] == 4 * 384
+    assert tuple(sd["backbone.0.projector.stages.1.0.cv1.conv.weight"].shape)[1] == 4 * 768
+    # a P4-only model keeps the reference's layout: no sampling parameters at all
+    med = RFDETR(config_from_preset("rf-detr-medium")).state_dict()
+    assert not any("stages_sampling" in k for k in med)
+
+
+def test_transposed_conv_as_gemm_matches_conv_transpose2d():
+    from mmltk_b200.models.projector import TransposedConv2x
+    torch.manual_seed(0)
+    t = TransposedConv2x(12, 6)
+    x = torch.randn(2, 5, 7, 12)
+    ref = torch.nn.functional.conv_transpose2d(x.permute(0, 3, 1, 2), t.weight, t.bias, stride=2).permute(0, 2, 3, 1)
+    assert torch.allclose(t.forward_nhwc(x), ref, atol=1e-5, rtol=1e-5)
+
+
 def test_inference_encoder_path_matches_training_path():
     """Without autograd the ViT forms each LayerScale residual inside the next LayerNorm; the
     features must equal the autograd path's (random, non-trivial layer scales)."""

@@ -200,6 +200,90 @@ def test_cuda_losses_match_cpu_oracle(cuda_device):
         assert abs(a - b) / max(abs(a), 1e-3) < 0.1, (k, a, b)
 
 
+@pytest.mark.gpu
+def test_cuda_step_gradients_match_cpu_oracle(cuda_device, monkeypatch):
+    """The CUDA training step's flat bf16 gradient (fused linears, attention, MSDeformAttn, fused
+    losses, LayerNorm kernels, in-place accumulation) against autograd of the CPU fp32 oracle,
+    family by family: cosine >= 0.99 and norms within 5 %.  Both runs use the GPU matcher's
+    assignment, so near-tied costs cannot send the two runs to different targets."""
+    import mmltk_b200.criterion.losses as losses_mod
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-medium", group_detr=2, dec_layers=2, resolution=256,
+                             positional_encoding_size=16)
+    model = RFDETR(cfg).train()
+    cpu_model = copy.deepcopy(model)
+    imgs, tg = synthetic_batch(2, 256, seed=4, kmax=8, slots=8, dtype=torch.bfloat16)
+
+    real_match = losses_mod.hungarian_match
+    recorded = []
+
+    def record(*a, **kw):
+        recorded.append(real_match(*a, **kw))
+        return recorded[-1]
+
+    monkeypatch.setattr(losses_mod, "hungarian_match", record)
+    eng = TrainEngine(model, TrainOptions(cuda_graph=False, lr=0.0, lr_encoder=0.0), cuda_device, max_targets=8)
+    eng.bind_static_inputs(2, 3, 256, 256)
+    eng.step(imgs.to(cuda_device), tg.to(cuda_device))
+    gpu = {n: eng.flat.view(eng.flat.grad_buf, i).float().cpu().reshape(-1) for i, n in enumerate(eng.flat.names)}
+
+    replay = [m.cpu() for m in recorded]
+    monkeypatch.setattr(losses_mod, "hungarian_match", lambda *a, **kw: replay.pop(0))
+    crit = SetCriterion(cfg)
+    losses, _ = crit(cpu_model(imgs.float()), tg)
+    crit.weighted(losses).backward()
+    cpu = {n: p.grad.reshape(-1) for n, p in cpu_model.named_parameters() if p.grad is not None}
+
+    prefixes = {"encoder": "backbone.0.encoder", "projector": "backbone.0.projector",
+                "decoder": "transformer.decoder", "two-stage heads": "transformer.enc_"}
+
+    def family(name):
+        return next((f for f, q in prefixes.items() if name.startswith(q)), "heads")
+
+    checked = 0
+    for fam in list(prefixes) + ["heads"]:
+        names = [n for n in gpu if n in cpu and family(n) == fam]
+        if not names:
+            continue
+        a = torch.cat([gpu[n] for n in names])
+        b = torch.cat([cpu[n] for n in names])
+        if b.norm() == 0:
+            continue
+        cos = float(torch.nn.functional.cosine_similarity(a, b, dim=0))
+        ratio = float(a.norm() / b.norm())
+        assert cos >= 0.99 and abs(ratio - 1) <= 0.05, (fam, cos, ratio)
+        checked += 1
+    assert checked >= 4
+
+
+def test_matcher_status_word_raises():
+    """A non-zero GPU assignment-solver status in the step readback is an error, not a silent
+    partial match."""
+    eng = TrainEngine(RFDETR(config_from_preset("rf-detr-tiny-test", resolution=64)), TrainOptions(), "cpu",
+                      max_targets=4)
+    rb = torch.zeros(5)
+    rb[3:4] = torch.tensor([2], dtype=torch.int32).view(torch.float32)
+    with pytest.raises(RuntimeError, match="matcher"):
+        eng._read_result(rb, {}, 7)
+    rb[3:4] = torch.tensor([0], dtype=torch.int32).view(torch.float32)
+    assert eng._read_result(rb, {}, 7).loss == 0.0
+
+
+@pytest.mark.gpu
+def test_step_async_detects_reused_readback_slot(cuda_device):
+    """A pending step whose pinned readback slot was taken by a later step raises instead of
+    returning the later step's values."""
+    cfg = config_from_preset("rf-detr-tiny-test", resolution=64)
+    eng = TrainEngine(RFDETR(cfg), TrainOptions(cuda_graph=False), cuda_device, max_targets=4)
+    eng.bind_static_inputs(2, 3, 64, 64)
+    imgs, tg = synthetic_batch(2, 64, seed=1, kmax=4, slots=4, dtype=torch.bfloat16)
+    imgs, tg = imgs.to(cuda_device), tg.to(cuda_device)
+    pend = [eng.step_async(imgs, tg) for _ in range(len(eng._readbacks) + 1)]
+    with pytest.raises(RuntimeError, match="reused"):
+        pend[0].result()
+    assert math.isfinite(pend[-1].result().loss)
+
+
 def test_mask_matching_cost_prefers_the_right_mask():
     """The mask term of the matcher cost is lowest for the query whose mask logits agree with the target."""
     from mmltk_b200.criterion.matcher import mask_cost

@@ -80,3 +80,33 @@ def test_noalloc_rejects_oversized_problem(cuda_device):
     B, S, Lq, H, L, P, D = dims
     rc = _call(fn, 0, t, sh, st, (64, 100000, Lq, H, L, P, D), outs)  # 64*100000*8*16 > 8 Mi elements
     assert rc == -1
+
+
+def test_noalloc_rejects_unsupported_arguments(cuda_device):
+    """An unsupported head dim (24) or dtype code (2) returns MMLTK_NOALLOC_ERR_BAD_ARG (-2)."""
+    fn = _lib()
+    t, sh, st, dims = _inputs(torch.float32, cuda_device)
+    outs = [torch.empty_like(x) for x in t[1:]]
+    B, S, Lq, H, L, P, D = dims
+    assert _call(fn, 0, t, sh, st, (B, S, Lq, H, L, P, 24), outs) == -2
+    assert _call(fn, 2, t, sh, st, dims, outs) == -2
+
+
+def test_noalloc_on_a_side_stream(cuda_device):
+    """The entry point runs on the stream it is given: a call on a non-default stream matches
+    the regular op."""
+    from mmltk_b200.ops import kernels
+    fn = _lib()
+    t, sh, st, dims = _inputs(torch.float32, cuda_device, seed=3)
+    gout, value, ref, off, logits = t
+    expect = kernels().msda_bwd(gout, value, sh, st, ref, off, logits)
+    outs = [torch.full_like(x, float("nan")) for x in (value, ref, off, logits)]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        rc = _call(fn, 0, t, sh, st, dims, outs)
+    side.synchronize()
+    assert rc == 0
+    for got, exp in zip(outs, expect):
+        scale = max(1e-6, exp.float().abs().max().item())
+        assert (got.float() - exp.float()).abs().max().item() / scale < 1e-5
