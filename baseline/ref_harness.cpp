@@ -226,6 +226,9 @@ class RefTrainer {
     // place.  Returns the step loss read back to the host (the metric handoff's read-back).
     double step(const torch::Tensor& images, const torch::Tensor& boxes, const torch::Tensor& labels,
                 const std::vector<int64_t>& counts, const py::object& allreduce) {
+        // libtorch's autograd engine must not run under the GIL; the all-reduce callbacks take it back
+        const bool reduce = world_ > 1 && !allreduce.is_none();
+        py::gil_scoped_release nogil;
         c10::cuda::CUDAGuard guard(device_);
         const int64_t batch = images.size(0);
         R::PreparedTargets prepared = make_targets(boxes, labels, counts, batch);
@@ -236,7 +239,7 @@ class RefTrainer {
             R::AutocastGuard autocast(true, R::resolve_cuda_autocast_dtype());
             R::ModelOutputs outputs = model_->forward(R::NestedTensor{images, nested_mask_.narrow(0, 0, batch)});
             R::AllReduceTensorFn reduce_fn;
-            if (!allreduce.is_none()) {
+            if (reduce) {
                 reduce_fn = [&allreduce](torch::Tensor& value) {
                     py::gil_scoped_acquire gil;
                     py::list l;
@@ -245,7 +248,7 @@ class RefTrainer {
                 };
             }
             R::TensorMap loss_dict =
-                R::detection_loss_dict(outputs, prepared, det_, true, world_ > 1, reduce_fn);
+                R::detection_loss_dict(outputs, prepared, det_, true, reduce, reduce_fn);
             loss = R::weighted_detection_loss(loss_dict, det_, images.device());
             class_loss = loss_dict.count("loss_ce") ? loss_dict.at("loss_ce") : torch::zeros_like(loss);
             box_loss = loss_dict.count("loss_bbox") ? loss_dict.at("loss_bbox") : torch::zeros_like(loss);
@@ -265,17 +268,14 @@ class RefTrainer {
         // optimizer step (train.cpp:2295-2344)
         optimizer_->set_lrs(base_lrs_, 1.0);
         auto& params = optimizer_->parameters();
-        if (world_ > 1 && !allreduce.is_none()) {
-            py::list grads;
+        if (reduce) {
             std::vector<torch::Tensor> gs;
-            for (auto& p : params) {
-                if (p.grad().defined()) {
-                    grads.append(p.grad());
-                    gs.push_back(p.grad());
-                }
-            }
+            for (auto& p : params)
+                if (p.grad().defined()) gs.push_back(p.grad());
             {
                 py::gil_scoped_acquire gil;
+                py::list grads;
+                for (auto& g : gs) grads.append(g);
                 allreduce(grads);
             }
             for (auto& g : gs) g.mul_(1.0 / static_cast<double>(world_));
@@ -286,10 +286,7 @@ class RefTrainer {
         host_metrics_.copy_(metrics_, true);
         const auto stream = at::cuda::getCurrentCUDAStream(device_.index());
         TORCH_CHECK(cudaEventRecord(copy_done_, stream.stream()) == cudaSuccess);
-        {
-            py::gil_scoped_release nogil;
-            TORCH_CHECK(cudaEventSynchronize(copy_done_) == cudaSuccess);
-        }
+        TORCH_CHECK(cudaEventSynchronize(copy_done_) == cudaSuccess);
         const float* v = host_metrics_.data_ptr<float>();
         const double step_loss = v[3];
         const bool loss_finite = v[6] != 0.0f;
@@ -383,6 +380,7 @@ class RefPredictor {
 
     // images: [B,3,H,W] float32 normalised on the device.  Returns (scores, labels, boxes) on the device.
     std::vector<torch::Tensor> run(const torch::Tensor& images) {
+        py::gil_scoped_release nogil;
         c10::cuda::CUDAGuard guard(device_);
         torch::NoGradGuard no_grad;
         R::OutputTensors out;
@@ -431,6 +429,7 @@ std::vector<torch::Tensor> ref_msda_fwd_bwd(const torch::Tensor& value, const to
                                             const torch::Tensor& level_start, const torch::Tensor& loc,
                                             const torch::Tensor& attn, const torch::Tensor& grad_out,
                                             int64_t im2col_step) {
+    py::gil_scoped_release nogil;
     auto v = value.detach().requires_grad_(true);
     auto l = loc.detach().requires_grad_(true);
     auto a = attn.detach().requires_grad_(true);

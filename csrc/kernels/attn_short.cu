@@ -1,0 +1,761 @@
+// Short-sequence scaled dot-product attention on the 5th-generation tensor cores (tcgen05), forward
+// and backward, head dim 32 or 64, sequences of at most 384 tokens: the Group-DETR decoder's
+// self-attention (300 queries per group, head dim 32; reference `nn::MultiheadAttention`,
+// `src/rfdetr/layers/model.cpp:917,945`) and the windowed ViT layers (325 tokens per window, head
+// dim 64; reference `at::scaled_dot_product_attention`, `model.cpp:498`).
+//
+// One CTA per (sequence, head).  Because a whole sequence fits on chip, every score row is
+// complete before its softmax: S = Q.K^T for a 128-query tile spans all keys in tensor memory
+// (<= 384 fp32 columns), so the softmax is exact in two passes over the row (maximum, then
+// exponentials) with no running-maximum rescaling, and the backward pass accumulates dV, dK and
+// dQ on chip without atomics.
+//
+// Operands are read by TMA as 128-row x 64-column bf16 boxes with the 128-byte swizzle, straight
+// out of the projection outputs (each of q / k / v / dO has its own tensor map and first column,
+// head h at column col + h * D).  With D = 32 a box also carries the neighbouring head's columns;
+// the MMAs read only the first D.  Rows past the sequence are the next sequence's (or TMA's zero
+// fill) and are masked by index.
+//
+// Forward, warps 0-3 = softmax / epilogue (thread = query row = TMEM lane), warp 4 = TMA
+// producer + TMEM owner, warp 5 = MMA issuer.  Per 128-query tile t:
+//   S_t = Q_t.K^T  (M=128, N=keys, K=D)              TMEM columns [0, 384)
+//   P_t = exp2(S_t * scale * log2e - m)  -> bf16, K-major swizzled in shared memory
+//   O_t = P_t.V    (M=128, N=D, K=keys, V MN-major)  TMEM columns [384, 384 + D)
+// S_{t+1} is issued as soon as the softmax has read S_t, so it overlaps O_t and its epilogue.
+//
+// Backward, same roles; thread = key row for the transposed products.  For every (key tile kt,
+// query tile qt) block:
+//   S^T  = K_kt.Q_qt^T, dP^T = V_kt.dO_qt^T            TMEM [0, 128), [128, 256)
+//   P^T  = exp2(S^T * scale * log2e - lse2[q]),  dS^T = P^T * (dP^T - delta[q])  -> bf16 smem
+//   dV_kt += P^T.dO_qt,  dK_kt += dS^T.Q_qt            (dS^T K-major: rows = keys)
+//   dQ_qt += dS.K_kt                                   (the same dS^T tile read MN-major)
+// with delta[q] = sum_d dO[q, d] O[q, d] from a small pre-pass.  D = 32 keeps all three dQ tiles
+// in tensor memory; D = 64 (whose dQ tiles do not fit next to the rest) takes each block's dQ
+// part out of tensor memory and adds it into an fp32 row owned by the same thread (no atomics:
+// query row q is always thread q % 128).
+//
+// Every mbarrier wait is bounded; on timeout the kernel records a code in the status word, every
+// role leaves, and tensor memory is released.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+
+#include "common.cuh"
+#include "launch_api.h"
+#include "tcgen05.cuh"
+
+namespace mmltk {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kRows = 128;
+constexpr int kBox = kRows * 64 * 2;    // 16 KB: one 128-row x 64-column bf16 box
+constexpr int kMaxL = 384;
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// 16-byte chunk j (8 bf16) of row r of a K-major 128-byte-swizzled tile
+__device__ __forceinline__ void put16(unsigned char* tile, int r, int j, uint4 v) {
+    *reinterpret_cast<uint4*>(tile + r * 128 + ((j ^ (r & 7)) << 4)) = v;
+}
+
+struct __align__(8) FwdCtl {
+    uint64_t kv_full, q_full, q_empty, s_full, p_full, o_full, o_free;
+    uint32_t tmem_base;
+    int abort;
+};
+
+struct FwdArgs {
+    __nv_bfloat16* o;
+    int64_t ldo;
+    float* lse;        // [N, H, L] natural log, or null
+    int* status;
+    int L, H, qcol, kcol, vcol, ocol;
+    float scale_log2;
+};
+
+__host__ __device__ size_t fwd_smem_bytes(int L) {
+    const int T = (L + kRows - 1) / kRows;
+    const int SN = (L + 31) / 32 * 32;
+    const int NP = (SN + 63) / 64;
+    return 1024 + static_cast<size_t>(kBox) * (1 + 2 * T + NP);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_short_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                          const __grid_constant__ CUtensorMap tv, FwdArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    FwdCtl* ctl = reinterpret_cast<FwdCtl*>(smem_raw);
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + sizeof(FwdCtl) + 1023) & ~uintptr_t(1023));
+    const int L = a.L;
+    const int T = (L + kRows - 1) / kRows;     // 128-row tiles of queries (and keys)
+    const int SN = (L + 31) / 32 * 32;         // score columns computed / read
+    const int NP = (SN + 63) / 64;             // 64-key P tiles
+    const int KO = (L + 15) / 16 * 16;         // keys reduced by P.V
+    unsigned char* sQ = smem;
+    unsigned char* sK = sQ + kBox;
+    unsigned char* sV = sK + T * kBox;
+    unsigned char* sP = sV + T * kBox;
+    if (L > kMaxL || (sP + NP * kBox) - smem_raw > static_cast<ptrdiff_t>(fwd_smem_bytes(L))) {
+        if (threadIdx.x == 0) atomicCAS(a.status, 0, 8);
+        return;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x / a.H, h = blockIdx.x % a.H;
+    const int row0 = n * L;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&ctl->kv_full, 1);
+        mbar_init(&ctl->q_full, 1);
+        mbar_init(&ctl->q_empty, 1);
+        mbar_init(&ctl->s_full, 1);
+        mbar_init(&ctl->p_full, 4);
+        mbar_init(&ctl->o_full, 1);
+        mbar_init(&ctl->o_free, 4);
+        ctl->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&ctl->tmem_base)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+    const uint32_t tS = tmem, tO = tmem + kMaxL;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            mbar_expect_tx(&ctl->kv_full, 2 * T * kBox);
+            for (int t = 0; t < T; ++t) {
+                tma_load_2d(&tk, &ctl->kv_full, sK + t * kBox, a.kcol + h * D, row0 + t * kRows);
+                tma_load_2d(&tv, &ctl->kv_full, sV + t * kBox, a.vcol + h * D, row0 + t * kRows);
+            }
+            for (int t = 0; t < T; ++t) {
+                if (t > 0 && !mbar_wait(&ctl->q_empty, (t - 1) & 1, &ctl->abort)) {
+                    ctl->abort = 1;
+                    atomicCAS(a.status, 0, 1);
+                    break;
+                }
+                mbar_expect_tx(&ctl->q_full, kBox);
+                tma_load_2d(&tq, &ctl->q_full, sQ, a.qcol + h * D, row0 + t * kRows);
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_o = instr_desc(false, true, D);
+            const uint32_t q = smem_u32(sQ), k = smem_u32(sK), v = smem_u32(sV), p = smem_u32(sP);
+            auto issue_s = [&]() {
+                for (int c0 = 0; c0 < SN; c0 += 256) {
+                    const int nc = min(256, SN - c0);
+                    const uint32_t idesc_s = instr_desc(false, false, nc);
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; ++kk)
+                        tc_mma(tS + c0, operand_desc<false>(q, kk), smem_desc(k + c0 * 128 + kk * 32, 16, 1024),
+                               idesc_s, kk > 0);
+                }
+                tc_commit(&ctl->q_empty);
+                tc_commit(&ctl->s_full);
+            };
+            bool ok = mbar_wait(&ctl->kv_full, 0, &ctl->abort) && mbar_wait(&ctl->q_full, 0, &ctl->abort);
+            if (ok) {
+                tc_fence_after();
+                issue_s();
+            }
+            for (int t = 0; ok && t < T; ++t) {
+                ok = mbar_wait(&ctl->p_full, t & 1, &ctl->abort);   // P_t written, S_t read
+                if (!ok) break;
+                tc_fence_after();
+                if (t + 1 < T) {
+                    ok = mbar_wait(&ctl->q_full, (t + 1) & 1, &ctl->abort);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_s();
+                }
+                if (t > 0) {
+                    ok = mbar_wait(&ctl->o_free, (t - 1) & 1, &ctl->abort);   // O_{t-1} read out
+                    if (!ok) break;
+                    tc_fence_after();
+                }
+                for (int j = 0; j < KO / 16; ++j)
+                    tc_mma(tO, smem_desc(p + (j >> 2) * kBox + (j & 3) * 32, 16, 1024),
+                           smem_desc(v + j * 2048, 8192, 1024), idesc_o, j > 0);
+                tc_commit(&ctl->o_full);
+            }
+            if (!ok) {
+                ctl->abort = 1;
+                atomicCAS(a.status, 0, 2);
+            }
+        }
+    } else {
+        // softmax / epilogue warps: thread = query row r of the tile = TMEM lane r
+        const int r = threadIdx.x;
+        const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+        bool ok = true;
+        for (int t = 0; t < T; ++t) {
+            if (!mbar_wait(&ctl->s_full, t & 1, &ctl->abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float mx = -1e30f;
+            for (int c = 0; c < SN / 32; ++c) {
+                float sv[32];
+                tmem_ld32(tS + lane_off + 32 * c, sv);
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (32 * c + i < L) mx = fmaxf(mx, sv[i]);
+            }
+            const float m = mx * a.scale_log2;
+            float sum = 0.f;
+            for (int c = 0; c < SN / 32; ++c) {
+                float sv[32];
+                tmem_ld32(tS + lane_off + 32 * c, sv);
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int k0 = 32 * c + 2 * i;
+                    const float p0 = k0 < L ? ex2(sv[2 * i] * a.scale_log2 - m) : 0.f;
+                    const float p1 = k0 + 1 < L ? ex2(sv[2 * i + 1] * a.scale_log2 - m) : 0.f;
+                    sum += p0 + p1;
+                    w[i] = pack_bf16x2(p0, p1);
+                }
+                unsigned char* tile = sP + (c >> 1) * kBox;
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    put16(tile, r, 4 * (c & 1) + j, make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]));
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->p_full);
+            if (!mbar_wait(&ctl->o_full, t & 1, &ctl->abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float o[D];
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + lane_off + 32 * c, o + 32 * c);
+            const int qrow = t * kRows + r;
+            if (qrow < L) {
+                const float inv = 1.f / sum;
+                uint4* dst = reinterpret_cast<uint4*>(a.o + static_cast<int64_t>(row0 + qrow) * a.ldo + a.ocol + h * D);
+#pragma unroll
+                for (int j = 0; j < D / 8; ++j)
+                    dst[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
+                                        pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
+                                        pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
+                                        pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
+                if (a.lse) a.lse[(static_cast<int64_t>(n) * a.H + h) * L + qrow] = (m + __log2f(sum)) * 0.69314718055994531f;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->o_free);
+        }
+        if (!ok) {
+            ctl->abort = 1;
+            if (lane == 0) atomicCAS(a.status, 0, 3);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// ------------------------------------------------------------------------------------ backward
+
+struct __align__(8) BwdCtl {
+    uint64_t qdo_full, kv_full, kv_empty, sdp_full, pds_full, mma_done, dkv_full, dkv_free, dq_free;
+    uint32_t tmem_base;
+    int abort;
+};
+
+struct BwdArgs {
+    const float* lse;     // [N, H, L] natural log
+    const float* delta;   // [N, H, L]: sum_d dO * O
+    float* dq_acc;        // D = 64: fp32 [N * H, L, 64] scratch
+    __nv_bfloat16 *dq, *dk, *dv;
+    int64_t lddq, lddk, lddv;
+    int dqcol, dkcol, dvcol;
+    int* status;
+    int L, H, qcol, kcol, vcol, docol;
+    float scale_log2, scale;
+};
+
+__host__ __device__ size_t bwd_smem_bytes(int L) {
+    const int T = (L + kRows - 1) / kRows;
+    // Q and dO (all tiles), K and V (one tile), P^T and dS^T (two 64-query tiles each), lse / delta
+    return 1024 + static_cast<size_t>(kBox) * (2 * T + 2 + 4) + 2 * kMaxL * sizeof(float);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_short_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                          BwdArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    BwdCtl* ctl = reinterpret_cast<BwdCtl*>(smem_raw);
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + sizeof(BwdCtl) + 1023) & ~uintptr_t(1023));
+    const int L = a.L;
+    const int T = (L + kRows - 1) / kRows;
+    unsigned char* sQ = smem;
+    unsigned char* sDO = sQ + T * kBox;
+    unsigned char* sK = sDO + T * kBox;
+    unsigned char* sV = sK + kBox;
+    unsigned char* sPt = sV + kBox;          // [128 keys x 128 queries] as two 64-query tiles
+    unsigned char* sDSt = sPt + 2 * kBox;
+    float* s_lse2 = reinterpret_cast<float*>(sDSt + 2 * kBox);
+    float* s_delta = s_lse2 + kMaxL;
+    if (L > kMaxL ||
+        reinterpret_cast<unsigned char*>(s_delta + kMaxL) - smem_raw > static_cast<ptrdiff_t>(bwd_smem_bytes(L))) {
+        if (threadIdx.x == 0) atomicCAS(a.status, 0, 8);
+        return;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x / a.H, h = blockIdx.x % a.H;
+    const int row0 = n * L;
+    const int nblk = T * T;
+
+    // tensor memory: S^T, dP^T, dV, dK, then dQ (D = 32: one D-wide slot per query tile,
+    // accumulated over key tiles; D = 64: one slot reused by every block)
+    constexpr uint32_t cS = 0, cDP = 128, cDV = 256, cDK = 256 + D, cDQ = 256 + 2 * D;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&ctl->qdo_full, 1);
+        mbar_init(&ctl->kv_full, 1);
+        mbar_init(&ctl->kv_empty, 1);
+        mbar_init(&ctl->sdp_full, 1);
+        mbar_init(&ctl->pds_full, 4);
+        mbar_init(&ctl->mma_done, 1);
+        mbar_init(&ctl->dkv_full, 1);
+        mbar_init(&ctl->dkv_free, 4);
+        mbar_init(&ctl->dq_free, 4);
+        ctl->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&ctl->tmem_base)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            mbar_expect_tx(&ctl->qdo_full, 2 * T * kBox);
+            for (int t = 0; t < T; ++t) {
+                tma_load_2d(&tq, &ctl->qdo_full, sQ + t * kBox, a.qcol + h * D, row0 + t * kRows);
+                tma_load_2d(&tdo, &ctl->qdo_full, sDO + t * kBox, a.docol + h * D, row0 + t * kRows);
+            }
+            for (int kt = 0; kt < T; ++kt) {
+                if (kt > 0 && !mbar_wait(&ctl->kv_empty, (kt - 1) & 1, &ctl->abort)) {
+                    ctl->abort = 1;
+                    atomicCAS(a.status, 0, 1);
+                    break;
+                }
+                mbar_expect_tx(&ctl->kv_full, 2 * kBox);
+                tma_load_2d(&tk, &ctl->kv_full, sK, a.kcol + h * D, row0 + kt * kRows);
+                tma_load_2d(&tv, &ctl->kv_full, sV, a.vcol + h * D, row0 + kt * kRows);
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_t = instr_desc(false, false, kRows);   // S^T / dP^T
+            constexpr uint32_t idesc_kv = instr_desc(false, true, D);        // dV / dK
+            constexpr uint32_t idesc_q = instr_desc(true, true, D);          // dQ (dS read MN-major)
+            const uint32_t q = smem_u32(sQ), dob = smem_u32(sDO), k = smem_u32(sK), v = smem_u32(sV);
+            const uint32_t pt = smem_u32(sPt), dst = smem_u32(sDSt);
+            bool ok = mbar_wait(&ctl->qdo_full, 0, &ctl->abort);
+            for (int kt = 0; ok && kt < T; ++kt) {
+                ok = mbar_wait(&ctl->kv_full, kt & 1, &ctl->abort);
+                if (!ok) break;
+                tc_fence_after();
+                for (int qt = 0; qt < T; ++qt) {
+                    const int blk = kt * T + qt;
+                    const uint32_t qb = q + qt * kBox, db = dob + qt * kBox;
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; ++kk)
+                        tc_mma(tmem + cS, operand_desc<false>(k, kk), operand_desc<false>(qb, kk), idesc_t, kk > 0);
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; ++kk)
+                        tc_mma(tmem + cDP, operand_desc<false>(v, kk), operand_desc<false>(db, kk), idesc_t, kk > 0);
+                    tc_commit(&ctl->sdp_full);
+                    ok = mbar_wait(&ctl->pds_full, blk & 1, &ctl->abort);   // P^T, dS^T in smem; S^T, dP^T read
+                    if (!ok) break;
+                    if (qt == 0 && kt > 0) {
+                        ok = mbar_wait(&ctl->dkv_free, (kt - 1) & 1, &ctl->abort);   // dV / dK of kt-1 read out
+                        if (!ok) break;
+                    }
+                    if (D == 64 && blk > 0) {
+                        ok = mbar_wait(&ctl->dq_free, (blk - 1) & 1, &ctl->abort);   // previous dQ part read out
+                        if (!ok) break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int j = 0; j < kRows / 16; ++j) {
+                        const uint64_t ap = smem_desc(pt + (j >> 2) * kBox + (j & 3) * 32, 16, 1024);
+                        const uint64_t ad = smem_desc(dst + (j >> 2) * kBox + (j & 3) * 32, 16, 1024);
+                        tc_mma(tmem + cDV, ap, smem_desc(db + j * 2048, 8192, 1024), idesc_kv, (qt > 0 || j > 0));
+                        tc_mma(tmem + cDK, ad, smem_desc(qb + j * 2048, 8192, 1024), idesc_kv, (qt > 0 || j > 0));
+                    }
+                    const uint32_t dq_col = D == 32 ? cDQ + 32 * qt : cDQ;
+#pragma unroll
+                    for (int j = 0; j < kRows / 16; ++j)
+                        tc_mma(tmem + dq_col, smem_desc(dst + j * 2048, kBox, 1024),
+                               smem_desc(k + j * 2048, 8192, 1024), idesc_q, (D == 32 ? (kt > 0 || j > 0) : j > 0));
+                    tc_commit(&ctl->mma_done);
+                    if (qt == T - 1) {
+                        tc_commit(&ctl->dkv_full);
+                        tc_commit(&ctl->kv_empty);
+                    }
+                }
+            }
+            if (!ok) {
+                ctl->abort = 1;
+                atomicCAS(a.status, 0, 2);
+            }
+        }
+    } else {
+        const int r = threadIdx.x;
+        const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+        const float* lse = a.lse + (static_cast<int64_t>(n) * a.H + h) * L;
+        const float* delta = a.delta + (static_cast<int64_t>(n) * a.H + h) * L;
+        for (int i = r; i < kMaxL; i += kRows) {
+            s_lse2[i] = i < L ? lse[i] * kLog2e : __int_as_float(0x7f800000);   // +inf: P = 0 past the sequence
+            s_delta[i] = i < L ? delta[i] : 0.f;
+        }
+        named_sync_softmax();
+        float* dq_acc = a.dq_acc + (static_cast<int64_t>(n) * a.H + h) * L * 64;
+        bool ok = true;
+        for (int kt = 0; ok && kt < T; ++kt) {
+            const bool kvalid = kt * kRows + r < L;
+            for (int qt = 0; qt < T; ++qt) {
+                const int blk = kt * T + qt;
+                if (!mbar_wait(&ctl->sdp_full, blk & 1, &ctl->abort) ||
+                    (blk > 0 && !mbar_wait(&ctl->mma_done, (blk - 1) & 1, &ctl->abort))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const float* l2 = s_lse2 + qt * kRows;
+                const float* dl = s_delta + qt * kRows;
+#pragma unroll 1
+                for (int c = 0; c < kRows / 32; ++c) {
+                    float sv[32], dp[32];
+                    tmem_ld32(tmem + cS + lane_off + 32 * c, sv);
+                    tmem_ld32(tmem + cDP + lane_off + 32 * c, dp);
+                    uint32_t wp[16], wd[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int q0 = 32 * c + 2 * i;
+                        const float p0 = kvalid ? ex2(sv[2 * i] * a.scale_log2 - l2[q0]) : 0.f;
+                        const float p1 = kvalid ? ex2(sv[2 * i + 1] * a.scale_log2 - l2[q0 + 1]) : 0.f;
+                        wp[i] = pack_bf16x2(p0, p1);
+                        wd[i] = pack_bf16x2(p0 * (dp[2 * i] - dl[q0]), p1 * (dp[2 * i + 1] - dl[q0 + 1]));
+                    }
+                    unsigned char* tp = sPt + (c >> 1) * kBox;
+                    unsigned char* td = sDSt + (c >> 1) * kBox;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        put16(tp, r, 4 * (c & 1) + j, make_uint4(wp[4 * j], wp[4 * j + 1], wp[4 * j + 2], wp[4 * j + 3]));
+                        put16(td, r, 4 * (c & 1) + j, make_uint4(wd[4 * j], wd[4 * j + 1], wd[4 * j + 2], wd[4 * j + 3]));
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctl->pds_full);
+                if (D == 64) {
+                    // this block's dQ part: thread = query row qt*128 + r
+                    if (!mbar_wait(&ctl->mma_done, blk & 1, &ctl->abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    float part[D];
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) tmem_ld32(tmem + cDQ + lane_off + 32 * c, part + 32 * c);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ctl->dq_free);
+                    const int qrow = qt * kRows + r;
+                    if (qrow < L) {
+                        float4* acc = reinterpret_cast<float4*>(dq_acc + static_cast<int64_t>(qrow) * 64);
+#pragma unroll
+                        for (int j = 0; j < D / 4; ++j) {
+                            float4 x = make_float4(part[4 * j], part[4 * j + 1], part[4 * j + 2], part[4 * j + 3]);
+                            if (kt > 0) {
+                                const float4 y = acc[j];
+                                x.x += y.x;
+                                x.y += y.y;
+                                x.z += y.z;
+                                x.w += y.w;
+                            }
+                            acc[j] = x;
+                        }
+                    }
+                }
+            }
+            if (!ok) break;
+            // dV / dK of this key tile are complete: thread = key row
+            if (!mbar_wait(&ctl->dkv_full, kt & 1, &ctl->abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float dvr[D], dkr[D];
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                tmem_ld32(tmem + cDV + lane_off + 32 * c, dvr + 32 * c);
+                tmem_ld32(tmem + cDK + lane_off + 32 * c, dkr + 32 * c);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->dkv_free);
+            if (kvalid) {
+                const int64_t row = row0 + kt * kRows + r;
+                uint4* ov = reinterpret_cast<uint4*>(a.dv + row * a.lddv + a.dvcol + h * D);
+                uint4* ok_ = reinterpret_cast<uint4*>(a.dk + row * a.lddk + a.dkcol + h * D);
+                const float s = a.scale;
+#pragma unroll
+                for (int j = 0; j < D / 8; ++j) {
+                    ov[j] = make_uint4(pack_bf16x2(dvr[8 * j], dvr[8 * j + 1]), pack_bf16x2(dvr[8 * j + 2], dvr[8 * j + 3]),
+                                       pack_bf16x2(dvr[8 * j + 4], dvr[8 * j + 5]),
+                                       pack_bf16x2(dvr[8 * j + 6], dvr[8 * j + 7]));
+                    ok_[j] = make_uint4(pack_bf16x2(dkr[8 * j] * s, dkr[8 * j + 1] * s),
+                                        pack_bf16x2(dkr[8 * j + 2] * s, dkr[8 * j + 3] * s),
+                                        pack_bf16x2(dkr[8 * j + 4] * s, dkr[8 * j + 5] * s),
+                                        pack_bf16x2(dkr[8 * j + 6] * s, dkr[8 * j + 7] * s));
+                }
+            }
+        }
+        if (ok) {
+            // dQ: thread = query row qt*128 + r
+            if (D == 32 && !mbar_wait(&ctl->mma_done, (nblk - 1) & 1, &ctl->abort)) ok = false;
+            if (ok) {
+                tc_fence_after();
+                for (int qt = 0; qt < T; ++qt) {
+                    float dqr[D];
+                    if (D == 32) {
+                        tmem_ld32(tmem + cDQ + 32 * qt + lane_off, dqr);
+                    } else {
+                        const int qrow = qt * kRows + r;
+                        if (qrow < L) {
+                            const float4* acc = reinterpret_cast<const float4*>(dq_acc + static_cast<int64_t>(qrow) * 64);
+#pragma unroll
+                            for (int j = 0; j < D / 4; ++j) {
+                                const float4 y = acc[j];
+                                dqr[4 * j] = y.x;
+                                dqr[4 * j + 1] = y.y;
+                                dqr[4 * j + 2] = y.z;
+                                dqr[4 * j + 3] = y.w;
+                            }
+                        }
+                    }
+                    const int qrow = qt * kRows + r;
+                    if (qrow < L) {
+                        uint4* oq = reinterpret_cast<uint4*>(a.dq + static_cast<int64_t>(row0 + qrow) * a.lddq +
+                                                             a.dqcol + h * D);
+                        const float s = a.scale;
+#pragma unroll
+                        for (int j = 0; j < D / 8; ++j)
+                            oq[j] = make_uint4(pack_bf16x2(dqr[8 * j] * s, dqr[8 * j + 1] * s),
+                                               pack_bf16x2(dqr[8 * j + 2] * s, dqr[8 * j + 3] * s),
+                                               pack_bf16x2(dqr[8 * j + 4] * s, dqr[8 * j + 5] * s),
+                                               pack_bf16x2(dqr[8 * j + 6] * s, dqr[8 * j + 7] * s));
+                    }
+                }
+            }
+        }
+        if (!ok) {
+            ctl->abort = 1;
+            if (lane == 0) atomicCAS(a.status, 0, 3);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// delta[n, h, i] = sum_d dO[row, docol + h*D + d] * O[row, ocol + h*D + d], row = n*L + i
+template <int D>
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, int64_t lddo, int docol,
+                                  const __nv_bfloat16* __restrict__ o, int64_t ldo, int ocol, float* __restrict__ delta,
+                                  int N, int L, int H) {
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<int64_t>(N) * L * H) return;
+    const int h = static_cast<int>(idx % H);
+    const int64_t row = idx / H;
+    const __nv_bfloat16* a = dout + row * lddo + docol + h * D;
+    const __nv_bfloat16* b = o + row * ldo + ocol + h * D;
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < D; j += 8) {
+        float x[8], y[8];
+        load8(a + j, x);
+        load8(b + j, y);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s += x[i] * y[i];
+    }
+    const int n = static_cast<int>(row / L), i = static_cast<int>(row % L);
+    delta[(static_cast<int64_t>(n) * H + h) * L + i] = s;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 128-row x 64-column boxes of a row-major bf16 matrix [rows, cols] with row pitch ld (elements)
+cudaError_t make_map(CUtensorMap* tm, const void* base, int64_t cols, int64_t rows, int64_t ld) {
+    if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || ld % 8 != 0 || cols > ld) return cudaErrorInvalidValue;
+    auto fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+    cuuint32_t box[2] = {64, kRows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::fprintf(stderr, "attn_short: cuTensorMapEncodeTiled failed (%d)\n", static_cast<int>(r));
+        return cudaErrorInvalidValue;
+    }
+    return cudaSuccess;
+}
+
+template <typename K>
+cudaError_t set_smem(K kern, size_t bytes) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    return e;
+}
+
+}  // namespace
+
+bool attn_short_supported(int L, int D) { return L >= 1 && L <= kMaxL && (D == 32 || D == 64); }
+
+cudaError_t launch_attn_short_fwd(const AttnOperand& q, const AttnOperand& k, const AttnOperand& v, int nseq, int L,
+                                  int H, int D, void* o, int64_t ldo, int ocol, float* lse, float scale, int* status,
+                                  cudaStream_t st) {
+    if (nseq == 0 || L == 0) return cudaSuccess;
+    if (!attn_short_supported(L, D)) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(o) % 16 != 0 || ldo % 8 != 0 || ocol % 8 != 0) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);   // the driver-API encode needs a current context
+    if (e != cudaSuccess) return e;
+    const int64_t rows = static_cast<int64_t>(nseq) * L;
+    CUtensorMap mq, mk, mv;
+    if ((e = make_map(&mq, q.base, q.cols, rows, q.ld)) != cudaSuccess) return e;
+    if ((e = make_map(&mk, k.base, k.cols, rows, k.ld)) != cudaSuccess) return e;
+    if ((e = make_map(&mv, v.base, v.cols, rows, v.ld)) != cudaSuccess) return e;
+    FwdArgs a{static_cast<__nv_bfloat16*>(o), ldo, lse, status, L, H, q.col, k.col, v.col, ocol, scale * kLog2e};
+    const size_t smem = fwd_smem_bytes(kMaxL);   // one CTA per SM (the kernel takes all of tensor memory)
+    auto run = [&](auto kern) {
+        static bool set[64] = {};
+        if (!set[dev & 63]) {
+            cudaError_t es = set_smem(kern, smem);
+            if (es != cudaSuccess) return es;
+            set[dev & 63] = true;
+        }
+        kern<<<nseq * H, kThreads, smem, st>>>(mq, mk, mv, a);
+        return cudaGetLastError();
+    };
+    return D == 32 ? run(attn_short_fwd_kernel<32>) : run(attn_short_fwd_kernel<64>);
+}
+
+cudaError_t launch_attn_short_bwd(const AttnOperand& q, const AttnOperand& k, const AttnOperand& v,
+                                  const AttnOperand& dout, const void* o, int64_t ldo, int ocol, const float* lse,
+                                  float* delta, float* dq_acc, int nseq, int L, int H, int D, void* dq, int64_t lddq,
+                                  int dqcol, void* dk, int64_t lddk, int dkcol, void* dv, int64_t lddv, int dvcol,
+                                  float scale, int* status, cudaStream_t st) {
+    if (nseq == 0 || L == 0) return cudaSuccess;
+    if (!attn_short_supported(L, D)) return cudaErrorInvalidValue;
+    for (auto* p : {dq, dk, dv})
+        if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return cudaErrorInvalidValue;
+    if (lddq % 8 || lddk % 8 || lddv % 8 || dqcol % 8 || dkcol % 8 || dvcol % 8 || ldo % 8 || ocol % 8)
+        return cudaErrorInvalidValue;
+    if (D == 64 && dq_acc == nullptr) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return e;
+    const int64_t rows = static_cast<int64_t>(nseq) * L;
+    {
+        const int64_t n = rows * H;
+        const int threads = 256;
+        const unsigned blocks = static_cast<unsigned>((n + threads - 1) / threads);
+        if (D == 32)
+            attn_delta_kernel<32><<<blocks, threads, 0, st>>>(static_cast<const __nv_bfloat16*>(dout.base), dout.ld,
+                                                               dout.col, static_cast<const __nv_bfloat16*>(o), ldo, ocol,
+                                                               delta, nseq, L, H);
+        else
+            attn_delta_kernel<64><<<blocks, threads, 0, st>>>(static_cast<const __nv_bfloat16*>(dout.base), dout.ld,
+                                                               dout.col, static_cast<const __nv_bfloat16*>(o), ldo, ocol,
+                                                               delta, nseq, L, H);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    CUtensorMap mq, mk, mv, mdo;
+    if ((e = make_map(&mq, q.base, q.cols, rows, q.ld)) != cudaSuccess) return e;
+    if ((e = make_map(&mk, k.base, k.cols, rows, k.ld)) != cudaSuccess) return e;
+    if ((e = make_map(&mv, v.base, v.cols, rows, v.ld)) != cudaSuccess) return e;
+    if ((e = make_map(&mdo, dout.base, dout.cols, rows, dout.ld)) != cudaSuccess) return e;
+    BwdArgs a{lse,   delta, dq_acc, static_cast<__nv_bfloat16*>(dq), static_cast<__nv_bfloat16*>(dk),
+              static_cast<__nv_bfloat16*>(dv), lddq, lddk, lddv, dqcol, dkcol, dvcol, status, L, H, q.col, k.col,
+              v.col, dout.col, scale * kLog2e, scale};
+    const size_t smem = bwd_smem_bytes(kMaxL);
+    auto run = [&](auto kern) {
+        static bool set[64] = {};
+        if (!set[dev & 63]) {
+            cudaError_t es = set_smem(kern, smem);
+            if (es != cudaSuccess) return es;
+            set[dev & 63] = true;
+        }
+        kern<<<nseq * H, kThreads, smem, st>>>(mq, mk, mv, mdo, a);
+        return cudaGetLastError();
+    };
+    return D == 32 ? run(attn_short_bwd_kernel<32>) : run(attn_short_bwd_kernel<64>);
+}
+
+size_t attn_short_smem_bytes(bool backward) { return backward ? bwd_smem_bytes(kMaxL) : fwd_smem_bytes(kMaxL); }
+
+}  // namespace mmltk

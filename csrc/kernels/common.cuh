@@ -16,6 +16,46 @@
 
 namespace mmltk {
 
+// ---------------------------------------------------------------- debug bounds checks
+// Built with -DMMLTK_DEBUG_BOUNDS=1 (the `_kernels_dbg` variant, `python -m mmltk_b200.build
+// --debug-bounds`), MMLTK_DEBUG_CHECK(cond, code) records `code` in this translation unit's device
+// status word when a data-dependent index is out of range; the kernel itself keeps its release
+// behaviour (the index is clamped or the element skipped), so a bad input is reported instead of
+// trapping or reading out of bounds.  Each kernel file that checks declares
+// MMLTK_DEBUG_STATUS_TU(name) once; `debug_status()` (debug_status.cpp) reads and clears every
+// registered word.  Release builds compile the checks to nothing.
+#if defined(MMLTK_DEBUG_BOUNDS) && MMLTK_DEBUG_BOUNDS
+static __device__ unsigned int g_mmltk_debug_status = 0;
+__device__ __forceinline__ void debug_flag(unsigned code) { atomicCAS(&g_mmltk_debug_status, 0u, code); }
+#define MMLTK_DEBUG_CHECK(cond, code)            \
+    do {                                         \
+        if (!(cond)) ::mmltk::debug_flag(code);  \
+    } while (0)
+#define MMLTK_DEBUG_STATUS_TU(name)                                                         \
+    namespace {                                                                             \
+    unsigned debug_read_##name() {                                                          \
+        unsigned v = 0;                                                                     \
+        const unsigned zero = 0;                                                            \
+        if (cudaMemcpyFromSymbol(&v, g_mmltk_debug_status, sizeof(v)) != cudaSuccess) return 0u; \
+        if (v) cudaMemcpyToSymbol(g_mmltk_debug_status, &zero, sizeof(zero));               \
+        return v;                                                                           \
+    }                                                                                       \
+    const bool debug_registered_##name = ::mmltk::register_debug_reader(&debug_read_##name); \
+    }
+#else
+#define MMLTK_DEBUG_CHECK(cond, code) \
+    do {                              \
+    } while (0)
+#define MMLTK_DEBUG_STATUS_TU(name)
+#endif
+
+// debug status codes
+constexpr unsigned kDbgMatcherLabel = 0x101;      // matcher: target label outside [0, C)
+constexpr unsigned kDbgMatcherCount = 0x102;      // matcher: target count above the slot count T
+constexpr unsigned kDbgLossLabel = 0x201;         // matched losses: target label outside [0, C)
+constexpr unsigned kDbgLossQuery = 0x202;         // matched losses: matched query index outside [0, Q)
+constexpr unsigned kDbgMaskIndex = 0x301;         // packed-mask sampling: mask index outside the mask table
+
 __device__ __forceinline__ float to_f(float x) { return x; }
 __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }

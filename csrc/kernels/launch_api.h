@@ -42,6 +42,58 @@ int attn_fwd_tc_blocks_per_sm();   // resident CTAs per SM (registers, shared me
 // 2 (default): two CTAs per SM at 168 registers; 1: one CTA per SM, no register cap.
 void attn_fwd_tc_set_variant(int min_blocks);
 
+// Short-sequence attention (attn_short.cu): L <= 384, head dim 32 or 64, one CTA per (sequence, head).
+// Each operand is a row-major bf16 matrix [nseq * L rows, cols] with row pitch ld (elements); head h
+// of it starts at column col + h * D.  o / dq / dk / dv are written the same way (row pitch, first
+// column); lse [nseq, H, L] natural log (forward output, backward input); delta [nseq, H, L] fp32
+// scratch; dq_acc fp32 [nseq * H, L, 64] scratch (head dim 64 only).
+struct AttnOperand {
+    const void* base;
+    int64_t ld;
+    int64_t cols;
+    int col;
+};
+bool attn_short_supported(int L, int D);
+size_t attn_short_smem_bytes(bool backward);
+cudaError_t launch_attn_short_fwd(const AttnOperand& q, const AttnOperand& k, const AttnOperand& v, int nseq, int L,
+                                  int H, int D, void* o, int64_t ldo, int ocol, float* lse, float scale, int* status,
+                                  cudaStream_t st);
+cudaError_t launch_attn_short_bwd(const AttnOperand& q, const AttnOperand& k, const AttnOperand& v,
+                                  const AttnOperand& dout, const void* o, int64_t ldo, int ocol, const float* lse,
+                                  float* delta, float* dq_acc, int nseq, int L, int H, int D, void* dq, int64_t lddq,
+                                  int dqcol, void* dk, int64_t lddk, int dkcol, void* dv, int64_t lddv, int dvcol,
+                                  float scale, int* status, cudaStream_t st);
+
+// ---------------------------------------------------------------- debug bounds checks
+// A kernel file's reader of its debug status word (read and clear); see MMLTK_DEBUG_CHECK.
+using DebugReader = unsigned (*)();
+bool register_debug_reader(DebugReader reader);
+
+// ---------------------------------------------------------------- RGBA overlays (overlay.cu)
+// uint8 surfaces with a row pitch in bytes; rgba points at 4 host bytes (r, g, b, a)
+cudaError_t launch_overlay_detections(uint8_t* ov, int64_t pitch, int W, int H, const float* boxes,
+                                      const uint8_t* colors, const uint8_t* masks, int n, int thickness,
+                                      uint8_t mask_alpha, cudaStream_t st);
+cudaError_t launch_composite_rgba(uint8_t* dst, int64_t dpitch, int dst_channels, const uint8_t* src, int64_t spitch,
+                                  int W, int H, bool swap_rb, cudaStream_t st);
+cudaError_t launch_copy_rgb_to_rgba(const uint8_t* src, int64_t spitch, uint8_t* dst, int64_t dpitch, int W, int H,
+                                    bool swap_rb, uint8_t alpha, cudaStream_t st);
+cudaError_t launch_manual_mask(uint8_t* ov, int64_t pitch, int W, int H, int x0, int y0, int w, int h,
+                               const uint8_t* mask, const uint8_t* rgba, cudaStream_t st);
+cudaError_t launch_manual_mask_runs(uint8_t* ov, int64_t pitch, int W, int H, int x0, int y0, int w, int h,
+                                    const uint32_t* runs, int nruns, const uint8_t* rgba, cudaStream_t st);
+cudaError_t launch_box_outline(uint8_t* ov, int64_t pitch, int W, int H, int x1, int y1, int x2, int y2, int thickness,
+                               const uint8_t* rgba, cudaStream_t st);
+cudaError_t launch_selection_handles(uint8_t* ov, int64_t pitch, int W, int H, int x1, int y1, int x2, int y2,
+                                     int radius, const uint8_t* rgba, cudaStream_t st);
+// segments: edges [m, 2] point indices, or (edges == null) consecutive points, the last joined to the
+// first when nsegments == npts (a closed polyline)
+cudaError_t launch_segments(uint8_t* ov, int64_t pitch, int W, int H, const int* pts, int npts, const uint32_t* edges,
+                            int nsegments, int thickness, const uint8_t* rgba, cudaStream_t st);
+cudaError_t launch_points(uint8_t* ov, int64_t pitch, int W, int H, const int* pts, int npts, int radius,
+                          const uint8_t* rgba, cudaStream_t st);
+cudaError_t launch_label_colors(const int* labels, int n, uint8_t* rgb, cudaStream_t st);
+
 // ---------------------------------------------------------------- sine position embedding
 // pos [rows, n] fp32 (n = 2 or 4: x, y[, w, h]); out [rows, n * dim] bf16 in block order y, x[, w, h];
 // freq [dim / 2] fp32.  n * dim / 32 must be 8, 16 or 32 and divide dim.

@@ -108,6 +108,14 @@ __device__ __forceinline__ Elem load_elem(const MatchedLayers& L, int l, int i, 
     if (!e.valid) return e;
     const int b = i / GT, t = i % T;
     int64_t lab = labels[static_cast<int64_t>(b) * T + t];
+    MMLTK_DEBUG_CHECK(lab >= 0 && lab < C, kDbgLossLabel);
+#if defined(MMLTK_DEBUG_BOUNDS) && MMLTK_DEBUG_BOUNDS
+    if (q >= Q) {   // the debug build skips a matched query index past the predictions
+        debug_flag(kDbgLossQuery);
+        e.valid = false;
+        return e;
+    }
+#endif
     lab = lab < 0 ? 0 : (lab >= C ? C - 1 : lab);
     e.logit_off = (static_cast<int64_t>(b) * Q + q) * C + lab;
     e.box_off = (static_cast<int64_t>(b) * Q + q) * 4;
@@ -204,5 +212,7 @@ cudaError_t launch_matched_loss(bool backward, DType lt, DType bt, const Matched
 #undef MMLTK_ML
     return cudaGetLastError();
 }
+
+MMLTK_DEBUG_STATUS_TU(matched_loss)
 
 }  // namespace mmltk

@@ -54,10 +54,12 @@ __global__ void __launch_bounds__(128) matcher_cost_kernel(MatcherLayers lp, con
     const int tile = blockIdx.x % qtiles;
     const int b = (blockIdx.x / qtiles) % B;
     const int l = blockIdx.x / (qtiles * B);
+    MMLTK_DEBUG_CHECK(counts[b] <= T, kDbgMatcherCount);
     const int nt = min(counts[b], T);
     for (int i = threadIdx.x; i < nt * 4; i += blockDim.x) sbox[i] = tboxes[static_cast<int64_t>(b) * T * 4 + i];
     for (int i = threadIdx.x; i < nt; i += blockDim.x) {
         const int64_t lab = labels[static_cast<int64_t>(b) * T + i];
+        MMLTK_DEBUG_CHECK(lab >= 0 && lab < C, kDbgMatcherLabel);
         slab[i] = static_cast<int>(lab < 0 ? 0 : (lab >= C ? C - 1 : lab));  // labels are validated on the host
     }
     __syncthreads();
@@ -383,5 +385,7 @@ cudaError_t launch_lsap(const float* cost, const int32_t* counts, int32_t* match
     lsap_kernel<<<(problems + wpb - 1) / wpb, 32 * wpb, smem, st>>>(cost, counts, match, NL, B, G, Qg, T, status);
     return cudaGetLastError();
 }
+
+MMLTK_DEBUG_STATUS_TU(matcher)
 
 }  // namespace mmltk

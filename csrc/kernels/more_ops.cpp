@@ -211,6 +211,8 @@ void register_more_ops(pybind11::module& m) {
     register_loss_ops(m);
     register_image_ops(m);
     register_attn_ops(m);
+    register_overlay_ops(m);
+    register_debug_ops(m);
 }
 
 }  // namespace mmltk

@@ -19,5 +19,7 @@ void register_aug_ops(pybind11::module& m);
 void register_loss_ops(pybind11::module& m);
 void register_image_ops(pybind11::module& m);
 void register_attn_ops(pybind11::module& m);
+void register_overlay_ops(pybind11::module& m);
+void register_debug_ops(pybind11::module& m);
 
 }  // namespace mmltk

@@ -5,7 +5,13 @@
 * ``mmltk_b200/_kernels*.so`` from ``csrc/kernels`` for sm_100a only
   (``-gencode arch=compute_100a,code=sm_100a``; torch's own arch list is
   bypassed because the flag is given explicitly), and
-* ``mmltk_b200/_native*.so`` from ``csrc/host`` (plain C++17, no CUDA).
+* ``mmltk_b200/_native*.so`` from ``csrc/host`` (plain C++17, no CUDA);
+* with ``--debug-bounds``, also ``mmltk_b200/_kernels_dbg*.so``: the same kernels compiled with
+  ``-DMMLTK_DEBUG_BOUNDS=1``, whose index checks record an error code in a device status word
+  (``kernels().debug_status()``) instead of trapping; ``MMLTK_DEBUG_BOUNDS=1`` at run time loads
+  it in place of ``_kernels``;
+* with ``--host-sanitize address,undefined``, the host self-test (``csrc/host/selftest_main.cpp``
+  over the torch-free host sources) as an ASan / UBSan executable, ``build/host_selftest_san``.
 
 Both land next to the Python sources (``build_ext --inplace``) so a snapshot
 of the repository carries them to a GPU machine.  nvcc cross-compiles, so no
@@ -29,19 +35,27 @@ NVCC_FLAGS = [
 CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-DNDEBUG"]
 
 
-def extensions():
+DEBUG_FLAGS = ["-DMMLTK_DEBUG_BOUNDS=1"]
+
+
+def extensions(debug_bounds: bool = False):
     from torch.utils.cpp_extension import CppExtension, CUDAExtension
 
     kern_src = sorted(p for p in glob.glob(os.path.join("csrc", "kernels", "*.cu")) +
                       glob.glob(os.path.join("csrc", "kernels", "*.cpp")) if "noalloc" not in p)
-    host_src = sorted(glob.glob(os.path.join("csrc", "host", "*.cpp")))
+    host_src = sorted(p for p in glob.glob(os.path.join("csrc", "host", "*.cpp")) if "selftest" not in p)
     inc = [os.path.join(ROOT, "csrc", "include"), os.path.join(ROOT, "csrc", "kernels")]
-    return [
+    exts = [
         CppExtension("mmltk_b200._native", host_src, include_dirs=inc + [os.path.join(ROOT, "csrc", "host")],
                      extra_compile_args={"cxx": CXX_FLAGS}, extra_link_args=["-lpthread", "-lz"]),
         CUDAExtension("mmltk_b200._kernels", kern_src, include_dirs=inc,
                       extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS}),
     ]
+    if debug_bounds:
+        exts.append(CUDAExtension("mmltk_b200._kernels_dbg", kern_src, include_dirs=inc,
+                                  extra_compile_args={"cxx": CXX_FLAGS + DEBUG_FLAGS,
+                                                      "nvcc": NVCC_FLAGS + DEBUG_FLAGS}))
+    return exts
 
 
 NOALLOC_LIB = os.path.join(ROOT, "mmltk_b200", "libmmltk_noalloc.so")
@@ -70,7 +84,29 @@ def build_noalloc(verbose: bool = False) -> str:
     return NOALLOC_LIB
 
 
-def build(verbose: bool = False, jobs: int | None = None) -> None:
+HOST_SELFTEST_SOURCES = ("lsap.cpp", "worker_pool.cpp", "image_io.cpp", "selftest_main.cpp")
+
+
+def build_host_selftest(sanitize: str = "address,undefined", verbose: bool = False) -> str:
+    """ASan / UBSan build of the host self-test (the counterpart of the reference's Dev-build
+    sanitizer options, `cmake/mmltk_project_configuration.cmake:72-79`): torch-free host sources plus
+    ``csrc/host/selftest_main.cpp``, linked into ``build/host_selftest_san``.  Returns its path."""
+    import subprocess
+
+    out_dir = os.path.join(ROOT, "build")
+    os.makedirs(out_dir, exist_ok=True)
+    exe = os.path.join(out_dir, "host_selftest_san")
+    srcs = [os.path.join(ROOT, "csrc", "host", f) for f in HOST_SELFTEST_SOURCES]
+    cmd = ["g++", "-std=c++17", "-O1", "-g", "-fno-omit-frame-pointer", f"-fsanitize={sanitize}",
+           "-fno-sanitize-recover=undefined", "-I", os.path.join(ROOT, "csrc", "host"), *srcs, "-o", exe,
+           "-lpthread", "-lz"]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    return exe
+
+
+def build(verbose: bool = False, jobs: int | None = None, debug_bounds: bool = False) -> None:
     from setuptools import setup
     from torch.utils.cpp_extension import BuildExtension
 
@@ -81,7 +117,7 @@ def build(verbose: bool = False, jobs: int | None = None) -> None:
         args = ["build_ext", "--inplace"]
         if not verbose:
             args.insert(0, "-q")
-        setup(name="mmltk_b200_native", ext_modules=extensions(),
+        setup(name="mmltk_b200_native", ext_modules=extensions(debug_bounds),
               cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
               script_args=args)
     finally:
@@ -90,4 +126,9 @@ def build(verbose: bool = False, jobs: int | None = None) -> None:
 
 
 if __name__ == "__main__":
-    build(verbose="-v" in sys.argv)
+    if "--host-sanitize" in sys.argv:
+        i = sys.argv.index("--host-sanitize")
+        print(build_host_selftest(sys.argv[i + 1] if i + 1 < len(sys.argv) else "address,undefined",
+                                  verbose="-v" in sys.argv))
+    else:
+        build(verbose="-v" in sys.argv, debug_bounds="--debug-bounds" in sys.argv)

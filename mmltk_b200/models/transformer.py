@@ -132,6 +132,12 @@ class DecoderLayer(nn.Module):
         qk = ops.linear(tgt_pos if tgt_pos is not None else tgt + query_pos, w[:2 * d], b[:2 * d])  # [B, Q, 2d]
         v = ops.linear(tgt, w[2 * d:], b[2 * d:])              # [B, Q, d]
         Qg = Q // groups
+        qk2, v2 = qk.view(B * Q, 2 * d), v.view(B * Q, d)
+        if ops.short_attention_ok(Qg, Dh, qk2, v2):
+            # rows b*Q + g*Qg + i = sequence b*G + g: attention never crosses a group; q / k / v are
+            # read straight out of the projections and the gradients land in them
+            o = ops.short_attention(qk2, v2, (0, d, 0), B * groups, Qg, H, Dh).view(B, Q, d)
+            return ops.linear(o, self.self_attn.out_proj.weight, None), self.self_attn.out_proj.bias
         # [B, G, Qg, H, Dh] -> [B*G, H, Qg, Dh]: attention never crosses a group
         # split (not two slices): its backward is one concatenation instead of two
         # zero-filled full-width buffers, two copies and an add

@@ -1,7 +1,8 @@
 """Hot ops of the RF-DETR stack.  CUDA tensors run the in-tree sm_100a kernels;
 CPU tensors run the plain-PyTorch fp32 definitions that serve as test oracles."""
 from ._ext import has_kernels, has_native, kernels, native
-from .attention import attention, attention_reference, qkv_attention, qkv_attention_reference
+from .attention import (attention, attention_reference, qkv_attention, qkv_attention_reference, short_attention,
+                        short_attention_ok)
 from .linear import linear, linear_scale_residual, mlp_scale_residual
 from .msda import msda, msda_reference
 from .norm import add_layer_norm, layer_norm, layer_norm_with_residual, scaled_residual_layer_norm

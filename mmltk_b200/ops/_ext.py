@@ -8,6 +8,10 @@ Two shared objects are built in-tree by ``mmltk_b200.build``:
 
 CUDA tensors never fall back to a PyTorch implementation: if the kernel
 extension is missing on a machine with a GPU, ``kernels()`` raises.
+
+``MMLTK_DEBUG_BOUNDS=1`` makes ``kernels()`` load ``_kernels_dbg`` (the same kernels built
+with index checks that record an error code in a device status word, read by
+``kernels().debug_status()``; ``python -m mmltk_b200.build --debug-bounds``).
 """
 from __future__ import annotations
 
@@ -33,7 +37,7 @@ def _load(modname: str):
     except Exception as e:  # pragma: no cover - reported below
         err = e
     if mod is None:
-        cands = glob.glob(os.path.join(_PKG_DIR, f"{modname}*.so"))
+        cands = glob.glob(os.path.join(_PKG_DIR, f"{modname}.*so"))
         if cands:
             try:
                 spec = importlib.util.spec_from_file_location(full, cands[0])
@@ -47,9 +51,13 @@ def _load(modname: str):
     return _cache[modname]
 
 
+def kernel_module_name() -> str:
+    return "_kernels_dbg" if os.environ.get("MMLTK_DEBUG_BOUNDS", "0") == "1" else "_kernels"
+
+
 def kernels():
     """The CUDA kernel extension; raises if it is not built."""
-    mod, err = _load("_kernels")
+    mod, err = _load(kernel_module_name())
     if mod is None:
         raise RuntimeError(
             "mmltk_b200 CUDA kernels are not built (run `python -m mmltk_b200.build`); "
@@ -68,7 +76,7 @@ def native():
 
 
 def has_kernels() -> bool:
-    return _load("_kernels")[0] is not None
+    return _load(kernel_module_name())[0] is not None
 
 
 def has_native() -> bool:

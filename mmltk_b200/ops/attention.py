@@ -5,7 +5,13 @@
 Reference: `at::scaled_dot_product_attention` (`src/rfdetr/layers/model.cpp:498`) and
 `nn::MultiheadAttention` (`model.cpp:917`).
 
-CUDA runs cuDNN's sm100 flash attention (library kernel) forward and backward.
+Sequences of at most 384 tokens with head dim 32 or 64 -- the Group-DETR decoder's
+self-attention (300 queries per group, head dim 32) and the windowed ViT layers (325 tokens,
+head dim 64) -- run the framework's own tcgen05 kernels forward and backward
+(``short_attention``, ``attn_short.cu``: one CTA per (sequence, head), the whole score row in
+tensor memory, exact softmax, dV / dK / dQ accumulated on chip), reading q / k / v straight out
+of the projection outputs and writing the gradients straight into the projection gradients.
+Longer sequences (the ViT's global layers) run cuDNN's sm100 flash attention (library kernel).
 The framework's own tcgen05 forward (``attn_tc.cu``: q / k / v read by TMA straight
 out of the packed projection, S and P.V accumulated in tensor memory, online softmax
 in registers) is exact to the same tolerance but measured 1.3-2x slower than cuDNN on
@@ -28,9 +34,69 @@ import os
 import torch
 import torch.nn.functional as F
 
-__all__ = ["attention", "attention_reference", "qkv_attention", "qkv_attention_reference", "qkv_attention_tc"]
+__all__ = ["attention", "attention_reference", "qkv_attention", "qkv_attention_reference", "qkv_attention_tc",
+           "short_attention", "short_attention_ok"]
 
 _USE_TC = os.environ.get("MMLTK_ATTN_TC", "0") == "1"
+_USE_SHORT = os.environ.get("MMLTK_ATTN_SHORT", "1") != "0"
+SHORT_MAX_L = 384
+
+
+def _tma_ok(t: torch.Tensor) -> bool:
+    return (t.is_cuda and t.dtype == torch.bfloat16 and t.dim() == 2 and t.stride(1) == 1 and t.stride(0) % 8 == 0
+            and t.data_ptr() % 16 == 0)
+
+
+def short_attention_ok(L: int, D: int, *sources: torch.Tensor) -> bool:
+    """True when ``short_attention`` takes these operands (CUDA bf16 2-D sources, L <= 384,
+    head dim 32 or 64)."""
+    return _USE_SHORT and 1 <= L <= SHORT_MAX_L and D in (32, 64) and all(_tma_ok(t) for t in sources)
+
+
+class _ShortAttnFn(torch.autograd.Function):
+    """q / k from columns of ``a``, v from columns of ``b`` (or of ``a`` when b is None)."""
+
+    @staticmethod
+    def forward(ctx, a, b, cols, nseq, L, heads, D):
+        from ._ext import kernels
+        vs = a if b is None else b
+        o, lse = kernels().attn_short_fwd(a, cols[0], a, cols[1], vs, cols[2], nseq, L, heads, D)
+        ctx.save_for_backward(a, b, o, lse)
+        ctx.cfg = (cols, nseq, L, heads, D)
+        return o
+
+    @staticmethod
+    def backward(ctx, go):
+        from ._ext import kernels
+        a, b, o, lse = ctx.saved_tensors
+        cols, nseq, L, heads, D = ctx.cfg
+        go = go.contiguous()
+        width = heads * D
+        # the kernel writes every head's columns of dq / dk / dv; a source with other columns too
+        # gets zeros there
+        if b is None:
+            da = (torch.empty_like if a.shape[1] == 3 * width else torch.zeros_like)(a)
+            db, vdst = None, da
+        else:
+            da = (torch.empty_like if a.shape[1] == 2 * width else torch.zeros_like)(a)
+            db = (torch.empty_like if b.shape[1] == width else torch.zeros_like)(b)
+            vdst = db
+        vs = a if b is None else b
+        kernels().attn_short_bwd(a, cols[0], a, cols[1], vs, cols[2], o, go, lse, nseq, L, heads, D,
+                                 da, cols[0], da, cols[1], vdst, cols[2])
+        return da, db, None, None, None, None, None
+
+
+def short_attention(a: torch.Tensor, b, cols, nseq: int, L: int, heads: int, D: int) -> torch.Tensor:
+    """Softmax attention over ``nseq`` sequences of ``L`` tokens, on the tcgen05 short-sequence
+    kernels.  ``a`` [nseq * L, *] holds q (head h at column cols[0] + h * D) and k (cols[1] + h * D);
+    v is read from ``b`` at cols[2] + h * D, or from ``a`` when ``b`` is None.  Returns
+    o [nseq * L, heads * D] (token-major, heads side by side)."""
+    if torch.is_grad_enabled() and (a.requires_grad or (b is not None and b.requires_grad)):
+        return _ShortAttnFn.apply(a, b, tuple(cols), nseq, L, heads, D)
+    from ._ext import kernels
+    vs = a if b is None else b
+    return kernels().attn_short_fwd(a, cols[0], a, cols[1], vs, cols[2], nseq, L, heads, D)[0]
 
 
 def attention_reference(q, k, v):
@@ -92,6 +158,11 @@ def qkv_attention_tc(qkv: torch.Tensor, heads: int, want_lse: bool = False):
 
 def qkv_attention(qkv: torch.Tensor, heads: int) -> torch.Tensor:
     if qkv.is_cuda and qkv.dtype in (torch.bfloat16, torch.float16):
+        N, L, C3 = qkv.shape
+        D = C3 // (3 * heads)
+        if qkv.is_contiguous() and short_attention_ok(L, D, qkv.view(N * L, C3)):
+            C = C3 // 3
+            return short_attention(qkv.view(N * L, C3), None, (0, C, 2 * C), N, L, heads, D).view(N, L, C)
         if torch.is_grad_enabled() and qkv.requires_grad:
             return _QKVAttnFn.apply(qkv, heads)
         if _USE_TC and qkv.dtype == torch.bfloat16 and qkv.shape[-1] == 3 * 64 * heads:

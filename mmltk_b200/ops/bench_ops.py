@@ -147,9 +147,39 @@ def bench_msda(device="cuda", quick=False):
         return []
     t_ours = time_ms(ours, warmup=3, iters=5)
     t_base = time_ms(baseline, warmup=2, iters=3, reps=3)
-    return [{"op": "msda_fwd_bwd", "B": B, "S": S, "H": H, "D": D, "Lq": Lq, "levels": L, "points": P,
-             "ms_ours": round(t_ours, 3), "ms_fp32_grid_sample": round(t_base, 3),
-             "speedup": round(t_base / t_ours, 2)}]
+    row = {"op": "msda_fwd_bwd", "B": B, "S": S, "H": H, "D": D, "Lq": Lq, "levels": L, "points": P,
+           "ms_ours": round(t_ours, 3), "ms_fp32_grid_sample": round(t_base, 3), "speedup": round(t_base / t_ours, 2)}
+    mod = _reference_module()
+    if mod is not None:
+        # the reference's own K1 / K2 (ms_deform_attn_op.cpp: bf16 -> fp32 casts, im2col forward,
+        # col2im backward) on the same sampling locations and softmaxed weights
+        from .msda import _locations
+        with torch.no_grad():
+            loc = _locations(ref.float(), off.float()).bfloat16()
+            attn = torch.softmax(logits.float().view(B, Lq, H, L * P), -1).view(B, Lq, H, L, P).bfloat16()
+        spatial = torch.tensor(shapes, dtype=torch.int64, device=device)
+        starts = torch.tensor([0] + [h * w for h, w in shapes[:-1]], dtype=torch.int64, device=device).cumsum(0)
+
+        def reference():
+            mod.msda_fwd_bwd(value.detach(), spatial, starts, loc, attn, gout, 64)
+        row["ms_reference_k1k2"] = round(time_ms(reference, warmup=2, iters=5), 3)
+        row["speedup_vs_reference"] = round(row["ms_reference_k1k2"] / t_ours, 2)
+    return [row]
+
+
+def _reference_module():
+    """The reference build of bench.py's reference arm (baseline/_ref), or None when absent."""
+    import glob
+    import importlib.util
+    import os
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    so = sorted(glob.glob(os.path.join(root, "baseline", "_ref", "mmltk_ref*.so")))
+    if not so:
+        return None
+    spec = importlib.util.spec_from_file_location("mmltk_ref", so[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
 # (name, batch*windows or batch*groups, heads, length, head dim): RF-DETR-M batch 8

@@ -329,6 +329,12 @@ class TrainEngine:
         nonfinite = int(self.flags_host_bits(rb[1]))
         norm = float(rb[2])
         match_status = int(self.flags_host_bits(rb[3]))
+        if self.cuda and kernels().debug_build():
+            # debug-bounds build: the step's index checks (one read of the status words per step)
+            code = int(kernels().debug_status())
+            if code:
+                raise RuntimeError(f"debug bounds check failed at step {step}: code {code:#x} "
+                                   "(an input index outside its table; see MMLTK_DEBUG_CHECK codes)")
         if match_status:
             raise RuntimeError(f"GPU Hungarian matcher gave up on a bounded search at step {step} "
                                f"(status {match_status}); the assignment would be partial")

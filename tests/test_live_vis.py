@@ -119,3 +119,19 @@ def test_live_gpu_graph_path(tmp_path):
     st = run_live(SyntheticFrameSource(96, 64, frames=12, seed=2), an, out_dir=str(tmp_path), save_every=3)
     assert st.frames_analyzed >= 1 and st.latency_ms_p50 > 0
     p.release()
+
+
+def test_overlay_cpu_raster_rules():
+    """The CPU overlay rules the GPU kernels are tested against: a 1-pixel polyline is 8-connected
+    along its length, handles are 8 squares, a disc of radius r covers the lattice points within r."""
+    from mmltk_b200.infer import overlay as ovl
+    ov = torch.zeros(40, 40, 4, dtype=torch.uint8)
+    ovl.polyline(ov, torch.tensor([[2, 3], [35, 20]]), False, 1, (255, 0, 0))
+    cols = ov[..., 3].nonzero()[:, 1].unique()
+    assert cols.min().item() == 2 and cols.max().item() == 35 and len(cols) == 34
+    ov.zero_()
+    ovl.selection_handles(ov, [5, 5, 30, 30], 1, (0, 255, 0))
+    assert int((ov[..., 3] > 0).sum()) == 8 * 9
+    ov.zero_()
+    ovl.points(ov, torch.tensor([[20, 20]]), 3, (0, 0, 255))
+    assert int((ov[..., 3] > 0).sum()) == sum(1 for x in range(-3, 4) for y in range(-3, 4) if x * x + y * y <= 9)

@@ -103,3 +103,16 @@ def test_loader_accepts_cpu_placement(tmp_path):
     bl = BatchLoader(path, 2, shuffle=False, pixels="uint8", max_targets=4, cpus=[cpu0])
     got = [idx for _img, _t, idx in bl]
     assert sorted(sum(got, [])) == [0, 1, 2, 3]
+
+
+def test_host_selftest_under_asan_ubsan():
+    """The torch-free host runtime (LSAP, worker pool, PNG codec, resizers) built with
+    AddressSanitizer + UndefinedBehaviorSanitizer and run: any invalid access or UB aborts it."""
+    import shutil
+    import subprocess
+    if shutil.which("g++") is None:
+        pytest.skip("no host compiler")
+    from mmltk_b200.build import build_host_selftest
+    exe = build_host_selftest("address,undefined")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "host selftest ok" in r.stdout, r.stdout + r.stderr
