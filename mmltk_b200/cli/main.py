@@ -261,7 +261,8 @@ def train_options_from_args(a) -> "TrainOptions":
     if o.optimizer == "muon":
         log.warning("optimizer=muon: the fused AdamW step is not used; Muon runs in its eager form")
     if o.lanes and o.lanes > 1:
-        log.warning("--lanes %d: intra-GPU replicas are not used on B200; one larger graph-captured step is", o.lanes)
+        log.info("--lanes %d: each optimizer step sums the gradients of %d lane batches (x --grad-accum-steps), "
+                 "run back to back on one stream as graph replays instead of model replicas", o.lanes, o.lanes)
     return o
 
 

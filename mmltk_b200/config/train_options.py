@@ -113,6 +113,11 @@ class TrainOptions:
     cuda_graph: bool = True
     overrides: set = dataclasses.field(default_factory=set)
 
+    def micro_batches_per_step(self) -> int:
+        """Batches whose gradients make one optimizer step: grad_accum_steps x lanes (reference
+        `train.cpp:2459-2511`: a wave of ``lanes`` batches, every ``grad_accum_steps`` waves)."""
+        return max(1, int(self.grad_accum_steps)) * max(1, int(self.lanes))
+
     def validate(self) -> None:
         if self.optimizer not in RECIPES:
             raise ValueError(f"unknown optimizer {self.optimizer}")

@@ -98,9 +98,13 @@ class TrainEngine:
             self._init_cpu(named, assign)
         self.graph = None
         self._graph_warmup = 0
-        # gradient accumulation: micro-batches before one optimizer step (eager; the graph path needs 1)
-        self.accum = max(1, int(opts.grad_accum_steps))
+        # micro-batches per optimizer step: --grad-accum-steps x --lanes (the reference's lanes are
+        # that many batches whose gradients are summed before one step, each loss scaled by
+        # 1/(lanes * accum); here they run one after another on one stream, each a graph replay)
+        self.accum = opts.micro_batches_per_step()
         self._micro = 0
+        self._acc_graphs = {}      # "first" / "mid" / "last" micro-batch graphs (accumulation)
+        self._pool = None
 
     # ------------------------------------------------------------------ setup
     def _init_cpu(self, named, assign):
@@ -270,16 +274,29 @@ class TrainEngine:
         if images is not None:
             self.load_inputs(images, targets)
         if self.accum > 1:
-            # micro-batch: forward + backward into the flat gradient, optimizer on the last one
+            # micro-batch: forward + backward into the flat gradient, optimizer on the last one;
+            # after three eager optimizer steps each micro-batch kind is a graph replay
             first, last = self._micro == 0, self._micro == self.accum - 1
             self._micro = 0 if last else self._micro + 1
+            if last:
+                sc = self._host_scalars(self.step_count)
+                self.scalars_host[:len(sc)] = torch.tensor(sc)
+                self.scalars.copy_(self.scalars_host, non_blocking=True)
+            if (self.opts.cuda_graph and self._graph_warmup >= 3 and self.in_targets.masks is None
+                    and self.muon is None):
+                kind = "last" if last else ("first" if first else "mid")
+                g = self._acc_graphs.get(kind)
+                if g is None:
+                    g = self._capture_micro(first, last)
+                    self._acc_graphs[kind] = g
+                g[0].replay()
+                total, losses = g[1], g[2]
+            else:
+                total, losses = self._cuda_body(self.in_images, self.in_targets, first=first, last=last)
+                if last:
+                    self._graph_warmup += 1
             if not last:
-                total, losses = self._cuda_body(self.in_images, self.in_targets, first=first, last=False)
                 return StepResult(total, losses, None, None)
-            sc = self._host_scalars(self.step_count)
-            self.scalars_host[:len(sc)] = torch.tensor(sc)
-            self.scalars.copy_(self.scalars_host, non_blocking=True)
-            total, losses = self._cuda_body(self.in_images, self.in_targets, first=first, last=True)
             return self._finish(total, losses, sync)
         sc = self._host_scalars(self.step_count)
         self.scalars_host[:len(sc)] = torch.tensor(sc)
@@ -357,13 +374,17 @@ class TrainEngine:
         return int(x.view(torch.int32).item())
 
     def release_graph(self) -> None:
-        """Drop the captured graph (required before destroying a process group it uses)."""
-        if self.graph is not None:
+        """Drop the captured graphs (required before destroying a process group they use)."""
+        if self.graph is not None or self._acc_graphs:
             torch.cuda.synchronize()
+        if self.graph is not None:
             self.graph.reset()
             self.graph = None
             self.static_total = self.static_losses = None
             self._graph_warmup = 0
+        for g in self._acc_graphs.values():
+            g[0].reset()
+        self._acc_graphs = {}
 
     def _capture(self):
         stream = torch.cuda.current_stream()
@@ -372,6 +393,17 @@ class TrainEngine:
         with torch.cuda.graph(self.graph, stream=torch.cuda.Stream()):
             self.static_total, self.static_losses = self._cuda_body(self.in_images, self.in_targets)
         stream.wait_stream(stream)
+
+    def _capture_micro(self, first: bool, last: bool):
+        """One accumulation micro-batch kind as a graph.  The kinds never run concurrently, so they
+        share one memory pool: their activations reuse the same memory."""
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        g = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, pool=self._pool, stream=torch.cuda.Stream()):
+            total, losses = self._cuda_body(self.in_images, self.in_targets, first=first, last=last)
+        return g, total, losses
 
     def _cpu_step(self, images, targets) -> StepResult:
         o = self.opts

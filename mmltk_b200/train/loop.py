@@ -282,15 +282,16 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
                  opts.optimizer, ("fused-nvswitch" if opts.ddp_backend == "fused" and opts.optimizer == "adamw"
                                   else "nccl") if ctx.enabled else "single-gpu",
                  opts.cuda_graph and ctx.device.type == "cuda", ctx.world_size, opts.batch_size,
-                 opts.grad_accum_steps, opts.batch_size * opts.grad_accum_steps,
-                 opts.batch_size * opts.grad_accum_steps * ctx.world_size)
+                 opts.micro_batches_per_step(), opts.batch_size * opts.micro_batches_per_step(),
+                 opts.batch_size * opts.micro_batches_per_step() * ctx.world_size)
     loader = BatchLoader(opts.train_compiled, opts.batch_size, shuffle=True, seed=opts.seed, shard_rank=ctx.rank,
                          shard_count=ctx.world_size, drop_last=True, pixels="uint8", workers=max(1, rt.split["gather"]),
                          prefetch=max(2, opts.prefetch_factor), max_targets=1,
                          device=ctx.device if ctx.device.type == "cuda" else None,
                          cpus=rt.loader_cpus[:1] if ctx.device.type == "cuda" else None)
     batches = len(loader)
-    steps_per_epoch = batches // opts.grad_accum_steps
+    micro = opts.micro_batches_per_step()       # --grad-accum-steps x --lanes batches per optimizer step
+    steps_per_epoch = batches // micro
     if steps_per_epoch == 0:
         raise ValueError("the compiled train split is too small for one effective batch per rank; reduce "
                          "--batch-size, --grad-accum-steps or the world size")
@@ -348,7 +349,7 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
             if ctx.main and opts.print_freq > 0 and (b + 1) % opts.print_freq == 0:
                 el = time.monotonic() - t_epoch
                 log.info("epoch %d step %d/%d loss %.4f (mean %.4f) grad_norm %s %.1f img/s", epoch, b + 1,
-                         steps_per_epoch * opts.grad_accum_steps, float(r.loss), loss_sum / max(1, n_loss),
+                         steps_per_epoch * micro, float(r.loss), loss_sum / max(1, n_loss),
                          "-" if r.grad_norm is None else f"{r.grad_norm:.3f}",
                          (b + 1) * opts.batch_size * ctx.world_size / max(el, 1e-9))
             if progress is not None:
@@ -361,7 +362,7 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
 
         prev = None
         for b, (images, _plain, idx) in enumerate(loader):
-            if b >= steps_per_epoch * opts.grad_accum_steps:
+            if b >= steps_per_epoch * micro:
                 break
             st = augmenter.prepare(idx, loader.dataset.reader, epoch, seq)
             seq += 1
@@ -407,9 +408,9 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
         extra = _resume_extra(opts, engine, epoch, best_regular, best_ema)   # collective when sharded
         if ctx.main:
             save_native_checkpoint(paths["ckpt"], regular.state_dict(), meta, extra)
-            rec = {"epoch": epoch, "train_lanes": 1, "eval_lanes": 1,
-                   "effective_batch_per_rank": opts.batch_size * opts.grad_accum_steps,
-                   "effective_batch_global": opts.batch_size * opts.grad_accum_steps * ctx.world_size,
+            rec = {"epoch": epoch, "train_lanes": max(1, opts.lanes), "eval_lanes": 1,
+                   "effective_batch_per_rank": opts.batch_size * micro,
+                   "effective_batch_global": opts.batch_size * micro * ctx.world_size,
                    "train_loss": train_loss, "val_loss": val.get("loss"), "val": _summary_json(val),
                    "ema_val_loss": None if ema_val is None else ema_val.get("loss"),
                    "ema_val": _summary_json(ema_val)}
@@ -424,9 +425,9 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
     result = {"preset_name": cfg.preset_name, "output_dir": opts.output_dir, "checkpoint": paths["ckpt"],
               "best_checkpoint": best_path or paths["ckpt"], "best_is_ema": best_is_ema,
               "best_regular_metric": best_regular, "best_ema_metric": best_ema, "last_epoch": last_epoch,
-              "history_size": len(history), "train_lanes": 1, "eval_lanes": 1,
-              "effective_batch_per_rank": opts.batch_size * opts.grad_accum_steps,
-              "effective_batch_global": opts.batch_size * opts.grad_accum_steps * ctx.world_size,
+              "history_size": len(history), "train_lanes": max(1, opts.lanes), "eval_lanes": 1,
+              "effective_batch_per_rank": opts.batch_size * micro,
+              "effective_batch_global": opts.batch_size * micro * ctx.world_size,
               "gpu_augmentation": _augmentation_json(opts.augmentation), "test": {}}
     if opts.test_compiled:
         best = resolve_model(result["best_checkpoint"], preset=cfg.preset_name, num_classes=num_classes,

@@ -256,6 +256,55 @@ def test_cuda_step_gradients_match_cpu_oracle(cuda_device, monkeypatch):
     assert checked >= 4
 
 
+def test_lanes_are_accumulated_micro_batches():
+    """--lanes N keeps the reference's semantics: N lane batches' gradients summed per optimizer
+    step (times --grad-accum-steps), so it is the same step as accumulating N x accum batches."""
+    assert TrainOptions(lanes=2).micro_batches_per_step() == 2
+    assert TrainOptions(lanes=3, grad_accum_steps=2).micro_batches_per_step() == 6
+    assert TrainOptions(lanes=0).micro_batches_per_step() == 1
+    cfg = config_from_preset("rf-detr-tiny-test", resolution=64)
+    batches = [synthetic_batch(2, 64, seed=s, kmax=4, slots=4) for s in range(4)]
+    finals = []
+    for opts in (TrainOptions(lanes=2, lr=1e-3), TrainOptions(grad_accum_steps=2, lr=1e-3)):
+        torch.manual_seed(0)
+        eng = TrainEngine(RFDETR(cfg), opts, "cpu", max_targets=4)
+        for imgs, tg in batches:
+            eng.step(imgs, tg)
+        assert eng.step_count == 2
+        finals.append(torch.cat([p.detach().reshape(-1) for p in eng.params]))
+    assert torch.allclose(finals[0], finals[1], atol=1e-6)
+
+
+@pytest.mark.gpu
+def test_graph_accumulation_matches_eager(cuda_device):
+    """Gradient accumulation over 3 micro-batches as graph replays (first / middle / last kinds)
+    gives the optimizer the same gradient as the eager accumulation: equal gradient norms at every
+    step (zero learning rate, so the weights stay put and the batches alone set the norm)."""
+    cfg = config_from_preset("rf-detr-medium", group_detr=2, dec_layers=2, resolution=256,
+                             positional_encoding_size=16)
+    batches = []
+    for seed in range(3):
+        imgs, tg = synthetic_batch(2, 256, seed=seed, kmax=6, slots=6, dtype=torch.bfloat16)
+        batches.append((imgs.to(cuda_device), tg.to(cuda_device)))
+    norms = {}
+    for graph in (False, True):
+        torch.manual_seed(0)
+        eng = TrainEngine(RFDETR(cfg), TrainOptions(cuda_graph=graph, lr=0.0, lr_encoder=0.0, grad_accum_steps=3),
+                          cuda_device, max_targets=6)
+        eng.bind_static_inputs(2, 3, 256, 256)
+        out = []
+        for step in range(6):
+            for b in batches:
+                r = eng.step(*b)
+            out.append(r.grad_norm)
+        if graph:
+            assert set(eng._acc_graphs) == {"first", "mid", "last"}
+        eng.release_graph()
+        norms[graph] = out
+    for a, b in zip(norms[False], norms[True]):
+        assert abs(a - b) <= 2e-3 * abs(a), norms
+
+
 def test_matcher_status_word_raises():
     """A non-zero GPU assignment-solver status in the step readback is an error, not a silent
     partial match."""
