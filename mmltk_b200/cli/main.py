@@ -181,10 +181,14 @@ def build_parser() -> argparse.ArgumentParser:
     p = rf.add_parser("normalize-weights")
     p.add_argument("--input", "--weights", dest="input", required=True)
     p.add_argument("--output", required=True)
-    p = rf.add_parser("validate")
+    p = rf.add_parser("validate", help="native B200 predictor vs the export graph (fp32, CPU) on a compiled split")
     p.add_argument("--compiled")
     p.add_argument("--source")
     p.add_argument("--output", default=None)
+    p.add_argument("--max-dets", type=int, default=500)
+    p.add_argument("--limit", type=int, default=None, help="score only the first N images")
+    p.add_argument("--export-limit", type=int, default=16,
+                   help="images scored by the export backend (fp32 on the CPU); both backends use them")
     _add_model_inputs(p)
     _add_execution(p)
     p = rf.add_parser("live", help="headless live analysis of a frame source (synthetic: no capture device)")
@@ -365,6 +369,26 @@ def _evaluate(a) -> int:
     return 0
 
 
+def _validate(a) -> int:
+    from ..infer import resolve_model
+    from ..infer.validate import validate_compiled
+    if a.onnx or a.tensorrt or not a.weights and not a.preset:
+        raise Unavailable("validate compares ONNX Runtime and TensorRT in the reference; neither is installed "
+                          "in this environment -- pass --weights (or --preset) to compare the native B200 "
+                          "predictor with the export graph instead")
+    if not a.compiled:
+        raise SystemExit("validate requires --compiled (a compiled split; --source recompilation is not supported)")
+    model, info = resolve_model(a.weights, preset=a.preset, resolution=a.resolution or None)
+    rep = validate_compiled(model, a.compiled, ("native", "export"), max(1, a.batch_size), a.max_dets, a.limit,
+                            a.export_limit, workers=max(1, a.workers))
+    rep["model"] = info.get("preset_name")
+    print(json.dumps(rep, indent=1))
+    if a.output:
+        with open(a.output, "w") as f:
+            json.dump(rep, f, indent=1)
+    return 0
+
+
 def _export(a) -> int:
     from ..export import export_onnx
     from ..infer import resolve_model
@@ -474,8 +498,7 @@ def run(argv: Optional[List[str]] = None) -> int:
     if r == "build-engine":
         raise Unavailable("TensorRT is not installed in this environment; build-engine is unavailable")
     if r == "validate":
-        raise Unavailable("validate compares ONNX Runtime against TensorRT; neither is installed in this "
-                          "environment")
+        return _validate(a)
     if r == "latency":
         return _latency(a)
     if r == "live":

@@ -108,3 +108,30 @@ def test_graph_predictor_matches_eager(compiled32):
     assert lat["p50_ms"] > 0
     assert graph.latency(iters=5, warmup=1, batch=1, pin_cpus=False)["p50_ms"] > 0
     graph.release()
+
+
+def test_validate_native_vs_export_report(compiled32):
+    """validate: both backends scored on the same images with the reference's report keys; on
+    the CPU the native predictor runs the same fp32 statement as the export graph, so the two agree."""
+    from mmltk_b200.infer.validate import validate_compiled
+    torch.manual_seed(0)
+    model = build_model("rf-detr-tiny-test", num_classes=4)
+    rep = validate_compiled(model, compiled32, ("native", "export"), batch_size=2, limit=4, device="cpu")
+    assert rep["eval_order"] == ["native", "export"] and rep["images"] == 4
+    for name in ("native", "export"):
+        assert 0.0 <= rep[name]["bbox_ap"] <= 1.0 and rep[name]["img_per_s"] > 0
+    al = rep["alignment_probe"]
+    assert al["images_compared"] == 4
+    assert al["top1_score_abs_diff_max"] < 1e-4 and al["top1_box_abs_diff_px_max"] < 1e-2
+    assert abs(rep["delta_export_minus_native"]["bbox_ap"]) < 1e-9
+
+
+@pytest.mark.gpu
+def test_validate_gpu_predictor_against_export_graph(compiled32, cuda_device):
+    """The bf16 B200 predictor against the fp32 export graph: same images, close top-1 detections."""
+    from mmltk_b200.infer.validate import validate_compiled
+    torch.manual_seed(0)
+    model = build_model("rf-detr-tiny-test", num_classes=4)
+    rep = validate_compiled(model, compiled32, ("native", "export"), batch_size=1, limit=5, device=cuda_device)
+    assert rep["images"] == 5 and rep["alignment_probe"]["images_compared"] == 5
+    assert rep["alignment_probe"]["top1_score_abs_diff_mean"] < 0.05
