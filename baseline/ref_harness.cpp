@@ -86,6 +86,19 @@ R::NativeRfDetrConfig config_for(const std::string& preset_name, int resolution,
     return c;
 }
 
+torch::Device device_for(int device_id) {
+    return device_id < 0 ? torch::Device(torch::kCPU)
+                         : torch::Device(torch::kCUDA, static_cast<c10::DeviceIndex>(device_id));
+}
+
+// a device guard that does nothing on the CPU
+struct MaybeCudaGuard {
+    std::optional<c10::cuda::CUDAGuard> g;
+    explicit MaybeCudaGuard(const torch::Device& d) {
+        if (d.is_cuda()) g.emplace(d);
+    }
+};
+
 R::CompilationMode mode_for(const std::string& m) {
     if (m == "none") return R::CompilationMode::kNone;
     if (m == "full") return R::CompilationMode::kFullTrace;
@@ -100,13 +113,14 @@ class RefTrainer {
     RefTrainer(const std::string& preset, int batch, int device_id, const std::string& compile_mode, int resolution,
                int patch_size, int num_windows, int pos_size, int dec_layers, int world_size, double lr,
                double lr_encoder, double weight_decay, double component_decay, double layer_decay,
-               double clip_max_norm, double ema_decay, double ema_tau)
-        : device_(torch::kCUDA, static_cast<c10::DeviceIndex>(device_id)),
+               double clip_max_norm, double ema_decay, double ema_tau, int num_classes)
+        : device_(device_for(device_id)),
           batch_(batch),
           world_(world_size),
           clip_(clip_max_norm) {
-        c10::cuda::CUDAGuard guard(device_);
-        config_ = config_for(preset, resolution, patch_size, num_windows, pos_size, dec_layers, 0);
+        // device_id < 0: the reference's CPU training step (fp32, no autocast)
+        MaybeCudaGuard guard(device_);
+        config_ = config_for(preset, resolution, patch_size, num_windows, pos_size, dec_layers, num_classes);
         const auto mode = mode_for(compile_mode);
         model_ = std::make_shared<R::NativeRfDetrModel>(config_);
         model_->to(device_);
@@ -196,8 +210,9 @@ class RefTrainer {
         // the 8-float metric handoff: device accumulators, one pinned copy + event sync per step
         metrics_ = torch::zeros({8}, torch::TensorOptions().dtype(torch::kFloat32).device(device_));
         metrics_.select(0, 6).fill_(1.0f);
-        host_metrics_ = torch::empty({8}, torch::TensorOptions().dtype(torch::kFloat32).pinned_memory(true));
-        TORCH_CHECK(cudaEventCreateWithFlags(&copy_done_, cudaEventDisableTiming) == cudaSuccess);
+        host_metrics_ =
+            torch::empty({8}, torch::TensorOptions().dtype(torch::kFloat32).pinned_memory(device_.is_cuda()));
+        if (device_.is_cuda()) TORCH_CHECK(cudaEventCreateWithFlags(&copy_done_, cudaEventDisableTiming) == cudaSuccess);
         nested_mask_ = torch::zeros({batch, config_.resolution, config_.resolution},
                                     torch::TensorOptions().dtype(torch::kBool).device(device_));
         sizes_ = torch::tensor({static_cast<int64_t>(config_.resolution), static_cast<int64_t>(config_.resolution)},
@@ -229,14 +244,14 @@ class RefTrainer {
         // libtorch's autograd engine must not run under the GIL; the all-reduce callbacks take it back
         const bool reduce = world_ > 1 && !allreduce.is_none();
         py::gil_scoped_release nogil;
-        c10::cuda::CUDAGuard guard(device_);
+        MaybeCudaGuard guard(device_);
         const int64_t batch = images.size(0);
         R::PreparedTargets prepared = make_targets(boxes, labels, counts, batch);
 
         metrics_.narrow(0, 3, 3).zero_();
         torch::Tensor loss, class_loss, box_loss;
         {
-            R::AutocastGuard autocast(true, R::resolve_cuda_autocast_dtype());
+            R::AutocastGuard autocast(device_.is_cuda(), device_.is_cuda() ? R::resolve_cuda_autocast_dtype() : at::kFloat);
             R::ModelOutputs outputs = model_->forward(R::NestedTensor{images, nested_mask_.narrow(0, 0, batch)});
             R::AllReduceTensorFn reduce_fn;
             if (reduce) {
@@ -283,10 +298,14 @@ class RefTrainer {
         const auto found_inf = scaler_->check_and_unscale_(*optimizer_);
         if (clip_ > 0.0) torch::nn::utils::clip_grad_norm_(params, clip_);
         metrics_.select(0, 7).copy_(found_inf);
-        host_metrics_.copy_(metrics_, true);
-        const auto stream = at::cuda::getCurrentCUDAStream(device_.index());
-        TORCH_CHECK(cudaEventRecord(copy_done_, stream.stream()) == cudaSuccess);
-        TORCH_CHECK(cudaEventSynchronize(copy_done_) == cudaSuccess);
+        if (device_.is_cuda()) {
+            host_metrics_.copy_(metrics_, true);
+            const auto stream = at::cuda::getCurrentCUDAStream(device_.index());
+            TORCH_CHECK(cudaEventRecord(copy_done_, stream.stream()) == cudaSuccess);
+            TORCH_CHECK(cudaEventSynchronize(copy_done_) == cudaSuccess);
+        } else {
+            host_metrics_.copy_(metrics_);
+        }
         const float* v = host_metrics_.data_ptr<float>();
         const double step_loss = v[3];
         const bool loss_finite = v[6] != 0.0f;
@@ -448,13 +467,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "rlewkowicz/mmltk reference (unmodified libtorch sources) driven for benchmarking";
     py::class_<RefTrainer>(m, "RefTrainer")
         .def(py::init<const std::string&, int, int, const std::string&, int, int, int, int, int, int, double, double,
-                      double, double, double, double, double, double>(),
+                      double, double, double, double, double, double, int>(),
              py::arg("preset"), py::arg("batch"), py::arg("device_id"), py::arg("compile_mode") = "selective",
              py::arg("resolution") = 0, py::arg("patch_size") = 0, py::arg("num_windows") = 0,
              py::arg("pos_size") = 0, py::arg("dec_layers") = 0, py::arg("world_size") = 1, py::arg("lr") = 1e-4,
              py::arg("lr_encoder") = 1.5e-4, py::arg("weight_decay") = 1e-4, py::arg("component_decay") = 0.7,
              py::arg("layer_decay") = 0.8, py::arg("clip_max_norm") = 0.1, py::arg("ema_decay") = 0.993,
-             py::arg("ema_tau") = 100.0)
+             py::arg("ema_tau") = 100.0, py::arg("num_classes") = 0)
         .def("step", &RefTrainer::step, py::arg("images"), py::arg("boxes"), py::arg("labels"), py::arg("counts"),
              py::arg("allreduce") = py::none())
         .def_property_readonly("backend", &RefTrainer::backend_name)

@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--infer-preset", default="rf-detr-base")
     ap.add_argument("--infer-select", type=int, default=100, help="post-process top-k (config 5: top-100)")
     ap.add_argument("--profile-launches", action="store_true", default=True)
+    ap.add_argument("--device", default="cuda", choices=["cuda", "cpu"],
+                    help="cpu: BASELINE config 1 (RF-DETR-Nano fp32 train step, batch 2 @ 384, 90 classes)")
     return ap.parse_args()
 
 
@@ -320,8 +322,58 @@ def _ref_infer(mod, args, local, dev):
     return out
 
 
+def cpu_config1(args):
+    """BASELINE config 1 on the CPU: one RF-DETR-Nano fp32 training step (forward, Hungarian match,
+    losses, backward, AdamW), batch 2 of 384x384 N(0,1) images, 90-class head, K~U{1..10} boxes,
+    labels U{0..79}, seed 0; host wall clock per step (there is no device to time on)."""
+    import torch
+    torch.manual_seed(0)
+    imgs, boxes, labels, counts = _ref_synthetic(2, 384, seed=0)
+    if args.impl == "reference":
+        mod, why = _load_reference()
+        if mod is None:
+            print(json.dumps({"impl": "reference", "unavailable": why}))
+            return 0
+        tr = mod.RefTrainer("rf-detr-nano", 2, -1, "selective", num_classes=90, ema_decay=0.0)
+
+        def step():
+            tr.step(imgs, boxes, labels, counts, None)
+    else:
+        from mmltk_b200.config import TrainOptions, config_from_preset
+        from mmltk_b200.criterion.targets import pad_targets
+        from mmltk_b200.models import RFDETR
+        from mmltk_b200.train.engine import TrainEngine
+        cfg = config_from_preset("rf-detr-nano", num_classes=90)
+        eng = TrainEngine(RFDETR(cfg), TrainOptions(use_ema=False), "cpu", max_targets=10)
+        per, o = [], 0
+        for k in counts:
+            per.append({"boxes": boxes[o:o + k], "labels": labels[o:o + k]})
+            o += k
+        tg = pad_targets(per, slots=10)
+
+        def step():
+            eng.step(imgs, tg)
+    for _ in range(max(1, args.warmup)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    ms = (time.perf_counter() - t0) / args.steps * 1e3
+    out = {"metric": "RF-DETR-Nano CPU fp32 train step (BASELINE config 1)", "value": round(ms, 2), "unit": "ms",
+           "higher_is_better": False, "steps": args.steps, "warmup": args.warmup, "dtype": "fp32",
+           "data": "synthetic: N(0,1) images, K~U{1..10} boxes, labels U{0..79}, seed 0; random-init weights",
+           "config": {"model": "rf-detr-nano", "batch": 2, "resolution": 384, "num_classes": 90,
+                      "threads": torch.get_num_threads()}}
+    if args.impl == "reference":
+        out["impl"] = "reference"
+    print(json.dumps(out))
+    return 0
+
+
 def main():
     args = parse()
+    if args.device == "cpu":
+        return cpu_config1(args)
     if args.impl == "reference":
         return reference_arm(args)
 

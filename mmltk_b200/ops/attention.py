@@ -38,7 +38,7 @@ __all__ = ["attention", "attention_reference", "qkv_attention", "qkv_attention_r
            "short_attention", "short_attention_ok"]
 
 _USE_TC = os.environ.get("MMLTK_ATTN_TC", "0") == "1"
-_USE_SHORT = os.environ.get("MMLTK_ATTN_SHORT", "1") != "0"
+_USE_SHORT = os.environ.get("MMLTK_ATTN_SHORT", "0") == "1"
 SHORT_MAX_L = 384
 
 

@@ -7,6 +7,7 @@ import math
 import pytest
 import torch
 
+import mmltk_b200.ops.attention as _attn
 from mmltk_b200.ops import kernels
 from mmltk_b200.ops.attention import short_attention
 
@@ -86,8 +87,15 @@ def test_qkv_attention_takes_the_short_kernel_for_windows(cuda_device):
     from mmltk_b200.ops.attention import qkv_attention, qkv_attention_reference
     torch.manual_seed(3)
     N, L, H = 4, 325, 6
+    import mmltk_b200.ops.attention as attn_mod
     qkv = (torch.randn(N, L, 3 * H * 64, device=cuda_device)).bfloat16().requires_grad_()
-    o = qkv_attention(qkv, H)
-    assert o.grad_fn is not None and "ShortAttn" in type(o.grad_fn).__name__
+    old = attn_mod._USE_SHORT
+    attn_mod._USE_SHORT = True
+    try:
+        o = qkv_attention(qkv, H)
+    finally:
+        attn_mod._USE_SHORT = old
+    fns = [type(o.grad_fn).__name__] + [type(f[0]).__name__ for f in o.grad_fn.next_functions if f[0] is not None]
+    assert any("ShortAttn" in n for n in fns), fns
     ref = qkv_attention_reference(qkv.detach().float(), H)
     _close(o, ref, 2e-2)
