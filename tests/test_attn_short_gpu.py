@@ -7,7 +7,6 @@ import math
 import pytest
 import torch
 
-import mmltk_b200.ops.attention as _attn
 from mmltk_b200.ops import kernels
 from mmltk_b200.ops.attention import short_attention
 
