@@ -16,15 +16,16 @@
 // the MMAs read only the first D.  Rows past the sequence are the next sequence's (or TMA's zero
 // fill) and are masked by index.
 //
-// Forward, warps 0-3 = softmax / epilogue (thread = query row = TMEM lane), warp 4 = TMA
-// producer + TMEM owner, warp 5 = MMA issuer.  Per 128-query tile t:
+// Forward, warps 0-7 = softmax / epilogue (warp w: TMEM lane quadrant w % 4, so thread = query row,
+// and half w / 4 of the row's score columns; partial maxima and sums meet in shared memory),
+// warp 8 = TMA producer + TMEM owner, warp 9 = MMA issuer.  Per 128-query tile t:
 //   S_t = Q_t.K^T  (M=128, N=keys, K=D)              TMEM columns [0, 384)
 //   P_t = exp2(S_t * scale * log2e - m)  -> bf16, K-major swizzled in shared memory
 //   O_t = P_t.V    (M=128, N=D, K=keys, V MN-major)  TMEM columns [384, 384 + D)
 // S_{t+1} is issued as soon as the softmax has read S_t, so it overlaps O_t and its epilogue.
 //
-// Backward, same roles; thread = key row for the transposed products.  For every (key tile kt,
-// query tile qt) block:
+// Backward, same roles; thread = key row for the transposed products, the two halves taking the
+// block's two 64-query column tiles.  For every (key tile kt, query tile qt) block:
 //   S^T  = K_kt.Q_qt^T, dP^T = V_kt.dO_qt^T            TMEM [0, 128), [128, 256)
 //   P^T  = exp2(S^T * scale * log2e - lse2[q]),  dS^T = P^T * (dP^T - delta[q])  -> bf16 smem
 //   dV_kt += P^T.dO_qt,  dK_kt += dS^T.Q_qt            (dS^T K-major: rows = keys)
@@ -53,7 +54,10 @@ using namespace tc;
 constexpr int kRows = 128;
 constexpr int kBox = kRows * 64 * 2;    // 16 KB: one 128-row x 64-column bf16 box
 constexpr int kMaxL = 384;
-constexpr int kThreads = 192;
+constexpr int kSoftWarps = 8;           // two per TMEM lane quadrant; each takes half of a row's columns
+constexpr int kSoftThreads = 32 * kSoftWarps;
+constexpr int kProdWarp = kSoftWarps, kMmaWarp = kSoftWarps + 1;
+constexpr int kThreads = 32 * (kSoftWarps + 2);
 constexpr int kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -63,11 +67,29 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// named barrier of the softmax warps that also ANDs a flag across them, so that when one warp's
+// bounded wait gives up every softmax warp learns it at the same barrier and they leave together
+__device__ __forceinline__ bool soft_sync_and(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(ok ? 1u : 0u), "n"(kSoftThreads)
+        : "memory");
+    return r != 0;
+}
 
 // 16-byte chunk j (8 bf16) of row r of a K-major 128-byte-swizzled tile
 __device__ __forceinline__ void put16(unsigned char* tile, int r, int j, uint4 v) {
     *reinterpret_cast<uint4*>(tile + r * 128 + ((j ^ (r & 7)) << 4)) = v;
+}
+// 8 consecutive keys / queries starting at column k (a multiple of 8) of a P-style smem matrix made of
+// 64-column K-major tiles
+__device__ __forceinline__ void put8(unsigned char* mat, int r, int k, const uint32_t* w) {
+    put16(mat + (k >> 6) * kBox, r, (k & 63) >> 3, make_uint4(w[0], w[1], w[2], w[3]));
 }
 
 struct __align__(8) FwdCtl {
@@ -85,11 +107,13 @@ struct FwdArgs {
     float scale_log2;
 };
 
+// score columns computed per row: a multiple of 64, so that each half is whole 32-column loads
+__host__ __device__ __forceinline__ int fwd_score_cols(int L) { return (L + 63) / 64 * 64; }
+
 __host__ __device__ size_t fwd_smem_bytes(int L) {
     const int T = (L + kRows - 1) / kRows;
-    const int SN = (L + 31) / 32 * 32;
-    const int NP = (SN + 63) / 64;
-    return 1024 + static_cast<size_t>(kBox) * (1 + 2 * T + NP);
+    const int NP = fwd_score_cols(L) / 64;
+    return 1024 + static_cast<size_t>(kBox) * (1 + 2 * T + NP) + 4 * kRows * sizeof(float);
 }
 
 template <int D>
@@ -102,14 +126,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + sizeof(FwdCtl) + 1023) & ~uintptr_t(1023));
     const int L = a.L;
     const int T = (L + kRows - 1) / kRows;     // 128-row tiles of queries (and keys)
-    const int SN = (L + 31) / 32 * 32;         // score columns computed / read
-    const int NP = (SN + 63) / 64;             // 64-key P tiles
+    const int SN = fwd_score_cols(L);          // score columns computed / read
+    const int NP = SN / 64;                    // 64-key P tiles
     const int KO = (L + 15) / 16 * 16;         // keys reduced by P.V
     unsigned char* sQ = smem;
     unsigned char* sK = sQ + kBox;
     unsigned char* sV = sK + T * kBox;
     unsigned char* sP = sV + T * kBox;
-    if (L > kMaxL || (sP + NP * kBox) - smem_raw > static_cast<ptrdiff_t>(fwd_smem_bytes(L))) {
+    float* s_max = reinterpret_cast<float*>(sP + NP * kBox);   // [2][128] partial row maxima
+    float* s_sum = s_max + 2 * kRows;                          // [2][128] partial row sums
+    if (L > kMaxL ||
+        reinterpret_cast<unsigned char*>(s_sum + 2 * kRows) - smem_raw > static_cast<ptrdiff_t>(fwd_smem_bytes(L))) {
         if (threadIdx.x == 0) atomicCAS(a.status, 0, 8);
         return;
     }
@@ -122,14 +149,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&ctl->q_full, 1);
         mbar_init(&ctl->q_empty, 1);
         mbar_init(&ctl->s_full, 1);
-        mbar_init(&ctl->p_full, 4);
+        mbar_init(&ctl->p_full, kSoftWarps);
         mbar_init(&ctl->o_full, 1);
-        mbar_init(&ctl->o_free, 4);
+        mbar_init(&ctl->o_free, kSoftWarps);
         ctl->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (warp == 4) {
+    if (warp == kProdWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(&ctl->tmem_base)),
                      "r"(kTmemCols));
@@ -141,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = ctl->tmem_base;
     const uint32_t tS = tmem, tO = tmem + kMaxL;
 
-    if (warp == 4) {
+    if (warp == kProdWarp) {
         if (lane == 0) {
             mbar_expect_tx(&ctl->kv_full, 2 * T * kBox);
             for (int t = 0; t < T; ++t) {
@@ -158,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_2d(&tq, &ctl->q_full, sQ, a.qcol + h * D, row0 + t * kRows);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         if (lane == 0) {
             constexpr uint32_t idesc_o = instr_desc(false, true, D);
             const uint32_t q = smem_u32(sQ), k = smem_u32(sK), v = smem_u32(sV), p = smem_u32(sP);
@@ -205,66 +232,85 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // softmax / epilogue warps: thread = query row r of the tile = TMEM lane r
-        const int r = threadIdx.x;
-        const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+        // softmax / epilogue: warp w reads TMEM lane quadrant w % 4 (thread = query row r of the
+        // tile) and the half w / 4 of the row's score columns; partial maxima / sums meet in shared
+        // memory
+        const int quad = warp & 3, half = warp >> 2;
+        const int r = 32 * quad + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(32 * quad) << 16;
+        const int cn = SN / 2, c0 = half * cn;
         bool ok = true;
         for (int t = 0; t < T; ++t) {
-            if (!mbar_wait(&ctl->s_full, t & 1, &ctl->abort)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
+            ok = ok && mbar_wait(&ctl->s_full, t & 1, &ctl->abort);
             float mx = -1e30f;
-            for (int c = 0; c < SN / 32; ++c) {
-                float sv[32];
-                tmem_ld32(tS + lane_off + 32 * c, sv);
+            if (ok) {
+                tc_fence_after();
+                int c = c0;
+                for (; c + 64 <= c0 + cn; c += 64) {
+                    float sv[64];
+                    tmem_ld64(tS + lane_off + c, sv);
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (32 * c + i < L) mx = fmaxf(mx, sv[i]);
-            }
-            const float m = mx * a.scale_log2;
-            float sum = 0.f;
-            for (int c = 0; c < SN / 32; ++c) {
-                float sv[32];
-                tmem_ld32(tS + lane_off + 32 * c, sv);
-                uint32_t w[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int k0 = 32 * c + 2 * i;
-                    const float p0 = k0 < L ? ex2(sv[2 * i] * a.scale_log2 - m) : 0.f;
-                    const float p1 = k0 + 1 < L ? ex2(sv[2 * i + 1] * a.scale_log2 - m) : 0.f;
-                    sum += p0 + p1;
-                    w[i] = pack_bf16x2(p0, p1);
+                    for (int i = 0; i < 64; ++i)
+                        if (c + i < L) mx = fmaxf(mx, sv[i]);
                 }
-                unsigned char* tile = sP + (c >> 1) * kBox;
+                if (c < c0 + cn) {
+                    float sv[32];
+                    tmem_ld32(tS + lane_off + c, sv);
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    put16(tile, r, 4 * (c & 1) + j, make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]));
+                    for (int i = 0; i < 32; ++i)
+                        if (c + i < L) mx = fmaxf(mx, sv[i]);
+                }
             }
+            s_max[half * kRows + r] = mx;
+            ok = soft_sync_and(ok);
+            if (!ok) break;
+            const float m = fmaxf(s_max[r], s_max[kRows + r]) * a.scale_log2;
+            float sum = 0.f;
+            for (int c = c0; c < c0 + cn; c += 32) {
+                float sv[32];
+                tmem_ld32(tS + lane_off + c, sv);
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int k0 = c + 8 * g + 2 * i;
+                        const float p0 = k0 < L ? ex2(sv[8 * g + 2 * i] * a.scale_log2 - m) : 0.f;
+                        const float p1 = k0 + 1 < L ? ex2(sv[8 * g + 2 * i + 1] * a.scale_log2 - m) : 0.f;
+                        sum += p0 + p1;
+                        w[i] = pack_bf16x2(p0, p1);
+                    }
+                    put8(sP, r, c + 8 * g, w);
+                }
+            }
+            s_sum[half * kRows + r] = sum;
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc_fence_before();
+            soft_sync_and(true);
+            const float total = s_sum[r] + s_sum[kRows + r];
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctl->p_full);
-            if (!mbar_wait(&ctl->o_full, t & 1, &ctl->abort)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            float o[D];
+            ok = mbar_wait(&ctl->o_full, t & 1, &ctl->abort);
+            if (ok) {
+                tc_fence_after();
+                // this half's D / 2 output columns
+                float o[D / 2];
+                if (D == 32) tmem_ld16(tO + lane_off + half * 16, o);
+                else tmem_ld32(tO + lane_off + half * 32, o);
+                const int qrow = t * kRows + r;
+                if (qrow < L) {
+                    const float inv = 1.f / total;
+                    uint4* dst = reinterpret_cast<uint4*>(a.o + static_cast<int64_t>(row0 + qrow) * a.ldo + a.ocol +
+                                                          h * D + half * (D / 2));
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + lane_off + 32 * c, o + 32 * c);
-            const int qrow = t * kRows + r;
-            if (qrow < L) {
-                const float inv = 1.f / sum;
-                uint4* dst = reinterpret_cast<uint4*>(a.o + static_cast<int64_t>(row0 + qrow) * a.ldo + a.ocol + h * D);
-#pragma unroll
-                for (int j = 0; j < D / 8; ++j)
-                    dst[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
-                                        pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
-                                        pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
-                                        pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
-                if (a.lse) a.lse[(static_cast<int64_t>(n) * a.H + h) * L + qrow] = (m + __log2f(sum)) * 0.69314718055994531f;
+                    for (int j = 0; j < D / 16; ++j)
+                        dst[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
+                                            pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
+                                            pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
+                                            pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
+                    if (a.lse && half == 0)
+                        a.lse[(static_cast<int64_t>(n) * a.H + h) * L + qrow] = (m + __log2f(total)) * 0.69314718055994531f;
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -277,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == kProdWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
@@ -347,16 +393,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&ctl->kv_full, 1);
         mbar_init(&ctl->kv_empty, 1);
         mbar_init(&ctl->sdp_full, 1);
-        mbar_init(&ctl->pds_full, 4);
+        mbar_init(&ctl->pds_full, kSoftWarps);
         mbar_init(&ctl->mma_done, 1);
         mbar_init(&ctl->dkv_full, 1);
-        mbar_init(&ctl->dkv_free, 4);
-        mbar_init(&ctl->dq_free, 4);
+        mbar_init(&ctl->dkv_free, kSoftWarps);
+        mbar_init(&ctl->dq_free, kSoftWarps);
         ctl->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (warp == 4) {
+    if (warp == kProdWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(&ctl->tmem_base)),
                      "r"(kTmemCols));
@@ -367,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
 
-    if (warp == 4) {
+    if (warp == kProdWarp) {
         if (lane == 0) {
             mbar_expect_tx(&ctl->qdo_full, 2 * T * kBox);
             for (int t = 0; t < T; ++t) {
@@ -385,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_2d(&tv, &ctl->kv_full, sV, a.vcol + h * D, row0 + kt * kRows);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         if (lane == 0) {
             constexpr uint32_t idesc_t = instr_desc(false, false, kRows);   // S^T / dP^T
             constexpr uint32_t idesc_kv = instr_desc(false, true, D);        // dV / dK
@@ -443,15 +489,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        const int r = threadIdx.x;
-        const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+        // warp w: TMEM lane quadrant w % 4 (thread = key row r for the transposed products, query
+        // row r for dQ) and half w / 4: query columns [64 * half, +64) of each block, output columns
+        // [half * D / 2, +D / 2) of dV / dK / dQ
+        const int quad = warp & 3, half = warp >> 2;
+        const int r = 32 * quad + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(32 * quad) << 16;
         const float* lse = a.lse + (static_cast<int64_t>(n) * a.H + h) * L;
         const float* delta = a.delta + (static_cast<int64_t>(n) * a.H + h) * L;
-        for (int i = r; i < kMaxL; i += kRows) {
+        for (int i = threadIdx.x; i < kMaxL; i += kSoftThreads) {
             s_lse2[i] = i < L ? lse[i] * kLog2e : __int_as_float(0x7f800000);   // +inf: P = 0 past the sequence
             s_delta[i] = i < L ? delta[i] : 0.f;
         }
-        named_sync_softmax();
+        soft_sync_and(true);
         float* dq_acc = a.dq_acc + (static_cast<int64_t>(n) * a.H + h) * L * 64;
         bool ok = true;
         for (int kt = 0; ok && kt < T; ++kt) {
@@ -464,52 +514,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const float* l2 = s_lse2 + qt * kRows;
-                const float* dl = s_delta + qt * kRows;
-#pragma unroll 1
-                for (int c = 0; c < kRows / 32; ++c) {
-                    float sv[32], dp[32];
-                    tmem_ld32(tmem + cS + lane_off + 32 * c, sv);
-                    tmem_ld32(tmem + cDP + lane_off + 32 * c, dp);
-                    uint32_t wp[16], wd[16];
+                const int qc = 64 * half;                       // this half's query columns in the block
+                const float* l2 = s_lse2 + qt * kRows + qc;
+                const float* dl = s_delta + qt * kRows + qc;
+                float sv[64], dp[64];
+                tmem_ld64(tmem + cS + lane_off + qc, sv);
+                tmem_ld64(tmem + cDP + lane_off + qc, dp);
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int q0 = 32 * c + 2 * i;
-                        const float p0 = kvalid ? ex2(sv[2 * i] * a.scale_log2 - l2[q0]) : 0.f;
-                        const float p1 = kvalid ? ex2(sv[2 * i + 1] * a.scale_log2 - l2[q0 + 1]) : 0.f;
+                for (int g = 0; g < 8; ++g) {
+                    uint32_t wp[4], wd[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int c = 8 * g + 2 * i;
+                        const float p0 = kvalid ? ex2(sv[c] * a.scale_log2 - l2[c]) : 0.f;
+                        const float p1 = kvalid ? ex2(sv[c + 1] * a.scale_log2 - l2[c + 1]) : 0.f;
                         wp[i] = pack_bf16x2(p0, p1);
-                        wd[i] = pack_bf16x2(p0 * (dp[2 * i] - dl[q0]), p1 * (dp[2 * i + 1] - dl[q0 + 1]));
+                        wd[i] = pack_bf16x2(p0 * (dp[c] - dl[c]), p1 * (dp[c + 1] - dl[c + 1]));
                     }
-                    unsigned char* tp = sPt + (c >> 1) * kBox;
-                    unsigned char* td = sDSt + (c >> 1) * kBox;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        put16(tp, r, 4 * (c & 1) + j, make_uint4(wp[4 * j], wp[4 * j + 1], wp[4 * j + 2], wp[4 * j + 3]));
-                        put16(td, r, 4 * (c & 1) + j, make_uint4(wd[4 * j], wd[4 * j + 1], wd[4 * j + 2], wd[4 * j + 3]));
-                    }
+                    put16(sPt + half * kBox, r, g, make_uint4(wp[0], wp[1], wp[2], wp[3]));
+                    put16(sDSt + half * kBox, r, g, make_uint4(wd[0], wd[1], wd[2], wd[3]));
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&ctl->pds_full);
                 if (D == 64) {
-                    // this block's dQ part: thread = query row qt*128 + r
+                    // this block's dQ part: thread = query row qt*128 + r, columns [32 * half, +32)
                     if (!mbar_wait(&ctl->mma_done, blk & 1, &ctl->abort)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    float part[D];
-#pragma unroll
-                    for (int c = 0; c < D / 32; ++c) tmem_ld32(tmem + cDQ + lane_off + 32 * c, part + 32 * c);
+                    float part[32];
+                    tmem_ld32(tmem + cDQ + lane_off + 32 * half, part);
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&ctl->dq_free);
                     const int qrow = qt * kRows + r;
                     if (qrow < L) {
-                        float4* acc = reinterpret_cast<float4*>(dq_acc + static_cast<int64_t>(qrow) * 64);
+                        float4* acc = reinterpret_cast<float4*>(dq_acc + static_cast<int64_t>(qrow) * 64 + 32 * half);
 #pragma unroll
-                        for (int j = 0; j < D / 4; ++j) {
+                        for (int j = 0; j < 8; ++j) {
                             float4 x = make_float4(part[4 * j], part[4 * j + 1], part[4 * j + 2], part[4 * j + 3]);
                             if (kt > 0) {
                                 const float4 y = acc[j];
@@ -524,28 +569,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             if (!ok) break;
-            // dV / dK of this key tile are complete: thread = key row
+            // dV / dK of this key tile are complete: thread = key row, this half's output columns
             if (!mbar_wait(&ctl->dkv_full, kt & 1, &ctl->abort)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float dvr[D], dkr[D];
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-                tmem_ld32(tmem + cDV + lane_off + 32 * c, dvr + 32 * c);
-                tmem_ld32(tmem + cDK + lane_off + 32 * c, dkr + 32 * c);
+            float dvr[D / 2], dkr[D / 2];
+            if (D == 32) {
+                tmem_ld16(tmem + cDV + lane_off + 16 * half, dvr);
+                tmem_ld16(tmem + cDK + lane_off + 16 * half, dkr);
+            } else {
+                tmem_ld32(tmem + cDV + lane_off + 32 * half, dvr);
+                tmem_ld32(tmem + cDK + lane_off + 32 * half, dkr);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctl->dkv_free);
             if (kvalid) {
                 const int64_t row = row0 + kt * kRows + r;
-                uint4* ov = reinterpret_cast<uint4*>(a.dv + row * a.lddv + a.dvcol + h * D);
-                uint4* ok_ = reinterpret_cast<uint4*>(a.dk + row * a.lddk + a.dkcol + h * D);
+                uint4* ov = reinterpret_cast<uint4*>(a.dv + row * a.lddv + a.dvcol + h * D + half * (D / 2));
+                uint4* ok_ = reinterpret_cast<uint4*>(a.dk + row * a.lddk + a.dkcol + h * D + half * (D / 2));
                 const float s = a.scale;
 #pragma unroll
-                for (int j = 0; j < D / 8; ++j) {
+                for (int j = 0; j < D / 16; ++j) {
                     ov[j] = make_uint4(pack_bf16x2(dvr[8 * j], dvr[8 * j + 1]), pack_bf16x2(dvr[8 * j + 2], dvr[8 * j + 3]),
                                        pack_bf16x2(dvr[8 * j + 4], dvr[8 * j + 5]),
                                        pack_bf16x2(dvr[8 * j + 6], dvr[8 * j + 7]));
@@ -557,35 +604,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         if (ok) {
-            // dQ: thread = query row qt*128 + r
+            // dQ: thread = query row qt*128 + r, this half's output columns
             if (D == 32 && !mbar_wait(&ctl->mma_done, (nblk - 1) & 1, &ctl->abort)) ok = false;
             if (ok) {
                 tc_fence_after();
                 for (int qt = 0; qt < T; ++qt) {
-                    float dqr[D];
+                    float dqr[D / 2];
+                    const int qrow = qt * kRows + r;
                     if (D == 32) {
-                        tmem_ld32(tmem + cDQ + 32 * qt + lane_off, dqr);
-                    } else {
-                        const int qrow = qt * kRows + r;
-                        if (qrow < L) {
-                            const float4* acc = reinterpret_cast<const float4*>(dq_acc + static_cast<int64_t>(qrow) * 64);
+                        tmem_ld16(tmem + cDQ + 32 * qt + lane_off + 16 * half, dqr);
+                    } else if (qrow < L) {
+                        const float4* acc =
+                            reinterpret_cast<const float4*>(dq_acc + static_cast<int64_t>(qrow) * 64 + 32 * half);
 #pragma unroll
-                            for (int j = 0; j < D / 4; ++j) {
-                                const float4 y = acc[j];
-                                dqr[4 * j] = y.x;
-                                dqr[4 * j + 1] = y.y;
-                                dqr[4 * j + 2] = y.z;
-                                dqr[4 * j + 3] = y.w;
-                            }
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 y = acc[j];
+                            dqr[4 * j] = y.x;
+                            dqr[4 * j + 1] = y.y;
+                            dqr[4 * j + 2] = y.z;
+                            dqr[4 * j + 3] = y.w;
                         }
                     }
-                    const int qrow = qt * kRows + r;
                     if (qrow < L) {
                         uint4* oq = reinterpret_cast<uint4*>(a.dq + static_cast<int64_t>(row0 + qrow) * a.lddq +
-                                                             a.dqcol + h * D);
+                                                             a.dqcol + h * D + half * (D / 2));
                         const float s = a.scale;
 #pragma unroll
-                        for (int j = 0; j < D / 8; ++j)
+                        for (int j = 0; j < D / 16; ++j)
                             oq[j] = make_uint4(pack_bf16x2(dqr[8 * j] * s, dqr[8 * j + 1] * s),
                                                pack_bf16x2(dqr[8 * j + 2] * s, dqr[8 * j + 3] * s),
                                                pack_bf16x2(dqr[8 * j + 4] * s, dqr[8 * j + 5] * s),
@@ -601,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == kProdWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
@@ -662,12 +707,20 @@ cudaError_t make_map(CUtensorMap* tm, const void* base, int64_t cols, int64_t ro
     return cudaSuccess;
 }
 
-template <typename K>
-cudaError_t set_smem(K kern, size_t bytes) {
+// the shared-memory opt-in, once per (kernel, device): Tag makes every kernel its own instantiation
+// (the D = 32 and D = 64 kernels have the same function-pointer type, so the flags cannot be keyed
+// by that type alone)
+template <typename Tag, typename K>
+cudaError_t ensure_smem(K kern, size_t bytes, int dev) {
+    static bool set[64] = {};
+    if (set[dev & 63]) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e == cudaSuccess) set[dev & 63] = true;
     return e;
 }
+template <bool Bwd, int D>
+struct KernelTag {};
 
 }  // namespace
 
@@ -690,17 +743,14 @@ cudaError_t launch_attn_short_fwd(const AttnOperand& q, const AttnOperand& k, co
     if ((e = make_map(&mv, v.base, v.cols, rows, v.ld)) != cudaSuccess) return e;
     FwdArgs a{static_cast<__nv_bfloat16*>(o), ldo, lse, status, L, H, q.col, k.col, v.col, ocol, scale * kLog2e};
     const size_t smem = fwd_smem_bytes(kMaxL);   // one CTA per SM (the kernel takes all of tensor memory)
-    auto run = [&](auto kern) {
-        static bool set[64] = {};
-        if (!set[dev & 63]) {
-            cudaError_t es = set_smem(kern, smem);
-            if (es != cudaSuccess) return es;
-            set[dev & 63] = true;
-        }
-        kern<<<nseq * H, kThreads, smem, st>>>(mq, mk, mv, a);
-        return cudaGetLastError();
-    };
-    return D == 32 ? run(attn_short_fwd_kernel<32>) : run(attn_short_fwd_kernel<64>);
+    if (D == 32) {
+        if ((e = ensure_smem<KernelTag<false, 32>>(attn_short_fwd_kernel<32>, smem, dev)) != cudaSuccess) return e;
+        attn_short_fwd_kernel<32><<<nseq * H, kThreads, smem, st>>>(mq, mk, mv, a);
+    } else {
+        if ((e = ensure_smem<KernelTag<false, 64>>(attn_short_fwd_kernel<64>, smem, dev)) != cudaSuccess) return e;
+        attn_short_fwd_kernel<64><<<nseq * H, kThreads, smem, st>>>(mq, mk, mv, a);
+    }
+    return cudaGetLastError();
 }
 
 cudaError_t launch_attn_short_bwd(const AttnOperand& q, const AttnOperand& k, const AttnOperand& v,
@@ -743,17 +793,14 @@ cudaError_t launch_attn_short_bwd(const AttnOperand& q, const AttnOperand& k, co
               static_cast<__nv_bfloat16*>(dv), lddq, lddk, lddv, dqcol, dkcol, dvcol, status, L, H, q.col, k.col,
               v.col, dout.col, scale * kLog2e, scale};
     const size_t smem = bwd_smem_bytes(kMaxL);
-    auto run = [&](auto kern) {
-        static bool set[64] = {};
-        if (!set[dev & 63]) {
-            cudaError_t es = set_smem(kern, smem);
-            if (es != cudaSuccess) return es;
-            set[dev & 63] = true;
-        }
-        kern<<<nseq * H, kThreads, smem, st>>>(mq, mk, mv, mdo, a);
-        return cudaGetLastError();
-    };
-    return D == 32 ? run(attn_short_bwd_kernel<32>) : run(attn_short_bwd_kernel<64>);
+    if (D == 32) {
+        if ((e = ensure_smem<KernelTag<true, 32>>(attn_short_bwd_kernel<32>, smem, dev)) != cudaSuccess) return e;
+        attn_short_bwd_kernel<32><<<nseq * H, kThreads, smem, st>>>(mq, mk, mv, mdo, a);
+    } else {
+        if ((e = ensure_smem<KernelTag<true, 64>>(attn_short_bwd_kernel<64>, smem, dev)) != cudaSuccess) return e;
+        attn_short_bwd_kernel<64><<<nseq * H, kThreads, smem, st>>>(mq, mk, mv, mdo, a);
+    }
+    return cudaGetLastError();
 }
 
 size_t attn_short_smem_bytes(bool backward) { return backward ? bwd_smem_bytes(kMaxL) : fwd_smem_bytes(kMaxL); }

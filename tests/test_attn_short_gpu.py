@@ -86,7 +86,8 @@ def test_qkv_attention_takes_the_short_kernel_for_windows(cuda_device):
     from mmltk_b200.ops.attention import qkv_attention, qkv_attention_reference
     torch.manual_seed(3)
     N, L, H = 4, 325, 6
-    import mmltk_b200.ops.attention as attn_mod
+    import importlib
+    attn_mod = importlib.import_module("mmltk_b200.ops.attention")   # (the package re-exports a function of that name)
     qkv = (torch.randn(N, L, 3 * H * 64, device=cuda_device)).bfloat16().requires_grad_()
     old = attn_mod._USE_SHORT
     attn_mod._USE_SHORT = True
