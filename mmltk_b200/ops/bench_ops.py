@@ -219,6 +219,27 @@ def bench_attn(device="cuda", quick=False):
                 row[be.name.lower() + "_fwd_bwd_ms"] = round(time_ms(both, warmup=3, iters=10), 4)
             except RuntimeError as e:   # backend unavailable for this shape / arch
                 row[be.name.lower()] = f"unavailable: {str(e).splitlines()[0][:80]}"
+        if L <= 384 and D in (32, 64):
+            # the packed projection layout [N * L, 3 * H * D], forward and forward + backward as CUDA-graph
+            # replays: the framework's short-sequence tcgen05 kernels against cuDNN on strided views
+            from .attention import _split, short_attention
+            C = H * D
+            qkv = torch.randn(N * L, 3 * C, device=device, generator=g).bfloat16().requires_grad_()
+            gos = torch.randn(N * L, C, device=device, generator=g).bfloat16()
+
+            def cudnn_pk():
+                with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+                    return F.scaled_dot_product_attention(*_split(qkv.view(N, L, 3 * C), H))
+
+            def short_pk():
+                return short_attention(qkv, None, (0, C, 2 * C), N, L, H, D)
+
+            for tag, f in (("cudnn", cudnn_pk), ("short", short_pk)):
+                with torch.no_grad():
+                    row[f"packed_{tag}_fwd_ms"] = round(time_graph_ms(f), 4)
+                go_t = gos if tag == "short" else gos.view(N, L, H, D).transpose(1, 2)
+                row[f"packed_{tag}_fwd_bwd_ms"] = round(time_graph_ms(
+                    lambda: torch.autograd.grad(f(), (qkv,), go_t)), 4)
         if D == 64:
             # forward on the packed projection layout: the tcgen05 kernel vs cuDNN on strided views
             from .attention import _split, qkv_attention_tc
