@@ -103,7 +103,7 @@ std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::option
     g.epi = static_cast<int>(epi);
     torch::Tensor ws;
     if (epi == 0 && !want_aux && g.bias == nullptr && g.colacc == nullptr) {
-        const int splits = gemm_tc_splits(g.M, g.N, g.K);
+        const int splits = gemm_tc_splits(g.M, g.N, g.K, b_mn);
         if (splits > 1) {  // few output tiles, long reduction: split K, sum partials in fp32
             ws = torch::empty({M, N}, a.options().dtype(torch::kFloat32));
             g.ws = ws.data_ptr<float>();
@@ -132,6 +132,8 @@ void register_gemm_ops(pybind11::module& m) {
           py::arg("gamma") = py::none(), py::arg("colsum") = py::none(), py::arg("colsum_acc") = false);
     m.def("gemm_tc_status", &gemm_tc_status);
     m.def("gemm_tc_smem_bytes", &gemm_tc_smem_bytes);
+    m.def("gemm_tc_set_variant", &gemm_tc_set_variant, py::arg("variant"));
+    m.def("gemm_tc_variant", &gemm_tc_variant);
 }
 
 }  // namespace mmltk

@@ -20,6 +20,17 @@
 // or MN-major ([K, rows] row-major), so x.W^T, dY.W and dY^T.X all run without
 // materialising a transpose.  M/N/K tails: TMA zero fill + masked stores.
 //
+// Pair variant (gemm_tc2_kernel): a cluster of two CTAs on two SMs computes one
+// 256-row tile with tcgen05.mma.cta_group::2 (M = 256).  Each CTA loads its own
+// 128 rows of A and its own half of the tile's B columns; the MMA issued by the
+// even CTA reads both CTAs' shared memory, and each CTA's tensor memory receives
+// its 128 accumulator rows.  Per SM that halves the B operand traffic through
+// shared memory, which is what limits the single-CTA tiles.  Every CTA loads
+// only its own tiles; the odd CTA's loads complete on the even CTA's mbarriers
+// (the .cta_group::2 form of the tensor load), the MMA completion is committed
+// to the stage / accumulator barriers of both CTAs, and both epilogues arrive
+// on the even CTA's accumulator-free barrier.
+//
 // Every mbarrier wait is bounded; on timeout the kernel records an error code
 // in a status word and leaves (after releasing its TMEM) instead of spinning.
 #include <cudaTypedefs.h>
@@ -187,10 +198,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg,
 }
 
 struct Sched {
-    int m_tiles, n_tiles, splits, ktiles, kt_per_split, bn;
+    int m_tiles, n_tiles, splits, ktiles, kt_per_split, bn, rows;
     __device__ void unit(int u, int& m0, int& n0, int& kt0, int& kt1) const {
         const int tile = u / splits, s = u % splits;
-        m0 = (tile / n_tiles) * BM;
+        m0 = (tile / n_tiles) * rows;
         n0 = (tile % n_tiles) * bn;
         kt0 = s * kt_per_split;
         kt1 = min(ktiles, kt0 + kt_per_split);
@@ -359,6 +370,265 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     }
 }
 
+// ------------------------------------------------------------------ CTA-pair variant
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait on a barrier that receives arrivals from the other CTA of the pair
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+    for (long long i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 255) == 255 && *abort) return false;
+    }
+    return false;
+}
+// 2-D TMA tile load into this CTA's shared memory whose completion is counted on an mbarrier
+// of either CTA of the pair (given as a shared::cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster, void* dst, int c0,
+                                                 int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void tc_mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// arrive on an mbarrier (shared::cluster address, either CTA) once the pair's earlier MMAs are done
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
+
+constexpr int kPairRows = 256;                     // output rows of one pair tile (128 per CTA)
+
+template <int BN_>
+struct PairTile {
+    static constexpr int BN = BN_;                 // output columns of a pair tile (the MMA's N)
+    static constexpr int kBHalf = BN / 2;          // B rows (N) held by each CTA
+    static constexpr int kBTile = kBHalf * BK * 2;
+    static constexpr int kStageBytes = kATile + kBTile;
+    static constexpr int kStages =
+        (kSmemLimit - kStagingBytes - 2048) / kStageBytes < kMaxStages ? (kSmemLimit - kStagingBytes - 2048) / kStageBytes
+                                                                         : kMaxStages;
+    static constexpr int kAccCols = BN;
+    static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
+    static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + kStagingBytes + 1024 + 256;
+};
+
+// bytes one CTA's loads deliver for a stage (MN-major boxes past the extent are not loaded)
+template <bool A_MN, bool B_MN, int BN>
+__device__ __forceinline__ uint32_t pair_stage_bytes(const GemmArgs& g, int m_cta, int n_cta) {
+    using T = PairTile<BN>;
+    const int a_boxes = A_MN ? max(0, min(BM / 64, (g.M - m_cta + 63) / 64)) : 0;
+    const int b_boxes = B_MN ? max(0, min(T::kBHalf / 64, (g.N - n_cta + 63) / 64)) : 0;
+    return (A_MN ? a_boxes * 8192 : kATile) + (B_MN ? b_boxes * 8192 : T::kBTile);
+}
+
+template <bool A_MN, bool B_MN, int BN_>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g,
+                    Sched sch) {
+    using T = PairTile<BN_>;
+    constexpr int BN = T::BN, kStages = T::kStages, kBTile = T::kBTile, kAccCols = T::kAccCols, kBHalf = T::kBHalf;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* tilesA = smem;
+    unsigned char* tilesB = smem + kStages * kATile;
+    uint32_t* staging = reinterpret_cast<uint32_t*>(smem + kStages * (kATile + kBTile));
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(reinterpret_cast<unsigned char*>(staging) + kStagingBytes);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int units = sch.m_tiles * sch.n_tiles * sch.splits;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&ctl->full[s], 1);
+            mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->acc_full[b], 1);
+            mbar_init(&ctl->acc_empty[b], 2 * kEpiWarps);   // every epilogue warp of both CTAs
+        }
+        ctl->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0) {
+        // one warp of each CTA allocates together: both get the same columns
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&ctl->tmem_base)),
+                     "r"(T::kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();   // the peer's barriers are initialised before anything targets them
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;
+            for (int u = pair; u < units; u += npairs) {
+                int m0, n0, kt0, kt1;
+                sch.unit(u, m0, n0, kt0, kt1);
+                const int m_cta = m0 + static_cast<int>(rank) * BM;
+                const int n_cta = n0 + static_cast<int>(rank) * kBHalf;
+                const int a_boxes = A_MN ? max(0, min(BM / 64, (g.M - m_cta + 63) / 64)) : 1;
+                const int b_boxes = B_MN ? max(0, min(kBHalf / 64, (g.N - n_cta + 63) / 64)) : 1;
+                const uint32_t pair_bytes = pair_stage_bytes<A_MN, B_MN, BN>(g, m0, n0) +
+                                            pair_stage_bytes<A_MN, B_MN, BN>(g, m0 + BM, n0 + kBHalf);
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1;
+                    if (!mbar_wait(&ctl->empty[s], ph ^ 1, &ctl->abort)) {
+                        ctl->abort = 1;
+                        atomicCAS(g.status, 0, 1);
+                        goto producer_done;
+                    }
+                    // both CTAs' loads complete on the even CTA's barrier, which expects them all
+                    if (rank == 0) mbar_expect_tx(&ctl->full[s], pair_bytes);
+                    const uint32_t fullb = mapa_shared(smem_u32(&ctl->full[s]), 0);
+                    unsigned char* a = tilesA + s * kATile;
+                    unsigned char* b = tilesB + s * kBTile;
+                    const int k0 = kt * BK;
+                    if (A_MN) {
+                        for (int q = 0; q < a_boxes; ++q) tma_load_2d_pair(&tmA, fullb, a + q * 8192, m_cta + 64 * q, k0);
+                    } else {
+                        tma_load_2d_pair(&tmA, fullb, a, k0, m_cta);
+                    }
+                    if (B_MN) {
+                        for (int q = 0; q < b_boxes; ++q) tma_load_2d_pair(&tmB, fullb, b + q * 8192, n_cta + 64 * q, k0);
+                    } else {
+                        tma_load_2d_pair(&tmB, fullb, b, k0, n_cta);
+                    }
+                }
+            }
+        producer_done:;
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            const uint32_t idesc = instr_desc(A_MN, B_MN, BN, kPairRows);
+            int it = 0, local = 0;
+            for (int u = pair; u < units; u += npairs, ++local) {
+                int m0, n0, kt0, kt1;
+                sch.unit(u, m0, n0, kt0, kt1);
+                const int buf = local & 1;
+                const uint32_t acc_ph = (local >> 1) & 1;
+                if (!mbar_wait_cluster(&ctl->acc_empty[buf], acc_ph ^ 1, &ctl->abort)) {
+                    ctl->abort = 1;
+                    atomicCAS(g.status, 0, 2);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t acc = tmem + buf * kAccCols;
+                bool ok = true;
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1;
+                    if (!mbar_wait(&ctl->full[s], ph, &ctl->abort)) {
+                        ctl->abort = 1;
+                        atomicCAS(g.status, 0, 2);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(tilesA + s * kATile);
+                    const uint32_t b = smem_u32(tilesB + s * kBTile);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        tc_mma_pair(acc, operand_desc<A_MN>(a, kk), operand_desc<B_MN>(b, kk), idesc,
+                                    (kt > kt0 || kk > 0) ? 1u : 0u);
+                    // the stage is free in both CTAs once these MMAs are done
+                    tc_commit_pair(mapa_shared(smem_u32(&ctl->empty[s]), 0));
+                    tc_commit_pair(mapa_shared(smem_u32(&ctl->empty[s]), 1));
+                }
+                if (!ok) break;
+                tc_commit_pair(mapa_shared(smem_u32(&ctl->acc_full[buf]), 0));
+                tc_commit_pair(mapa_shared(smem_u32(&ctl->acc_full[buf]), 1));
+            }
+        }
+    } else {
+        // epilogue: this CTA's 128 rows of the pair tile (TMEM lanes), all BN columns; warp w reads
+        // lane quadrant w % 4 and half (w - 2) / 4 of the columns
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        uint32_t* stg = staging + (warp - 2) * kStageWords;
+        int local = 0;
+        for (int u = pair; u < units; u += npairs, ++local) {
+            int m0, n0, kt0, kt1;
+            sch.unit(u, m0, n0, kt0, kt1);
+            const int buf = local & 1;
+            const uint32_t acc_ph = (local >> 1) & 1;
+            if (!mbar_wait(&ctl->acc_full[buf], acc_ph, &ctl->abort)) {
+                if (lane == 0) atomicCAS(g.status, 0, 3);
+                ctl->abort = 1;
+                break;
+            }
+            tc_fence_after();
+            const int row0 = m0 + static_cast<int>(rank) * BM + 32 * q;
+            const uint32_t acc = tmem + buf * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
+            constexpr int kHalfCols = BN / 2;
+            for (int c = half * kHalfCols; c < (half + 1) * kHalfCols; c += 32) {
+                if (n0 + c >= g.N || row0 >= g.M) break;  // warp-uniform
+                const int ncols = min(min(32, (half + 1) * kHalfCols - c), g.N - n0 - c);
+                float v[32];
+                if (ncols > 16) {
+                    tmem_ld32(acc + c, v);
+                } else {
+                    tmem_ld16(acc + c, v);
+                }
+                epilogue_chunk(g, stg, lane, row0, n0 + c, ncols, v);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl->acc_empty[buf]), 0));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();   // no CTA leaves while the pair's MMAs may still read its shared memory
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(T::kTmemCols));
+    }
+}
+
 __global__ void ws_to_bf16_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ c, int64_t n) {
     for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x * 8) {
@@ -427,15 +697,68 @@ int pick_bn(int M, int N) {
 
 size_t gemm_tc_smem_bytes() { return Tile<256>::kSmemBytes; }
 
-int gemm_tc_splits(int M, int N, int K) {
-    const int bn = pick_bn(M, N);
-    const int tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-    const int ktiles = (K + BK - 1) / BK;
-    const int sms = num_sms();
-    if (tiles >= sms / 2 || ktiles < 8) return 1;
-    int s = std::min((sms + tiles - 1) / tiles, ktiles / 4);
-    return std::max(1, s);
+namespace {
+
+// 0: choose per shape, 1: single-CTA tiles only, 2: CTA-pair tiles whenever the shape allows
+int g_variant = 0;
+
+// Pair-tile width (MMA N) for an M x N output: useful columns x wave occupancy of the pairs.
+int pick_bn_pair(int M, int N) {
+    const int pairs = std::max(1, num_sms() / 2);
+    const int widths[2] = {256, 128};
+    const double tile_eff[2] = {1.0, 0.92};
+    int best = 256;
+    double best_score = -1.0;
+    for (int i = 0; i < 2; ++i) {
+        const int bn = widths[i];
+        const int tn = (N + bn - 1) / bn;
+        const double col_eff = static_cast<double>(N) / (static_cast<double>(tn) * bn);
+        const long long units = static_cast<long long>((M + kPairRows - 1) / kPairRows) * tn;
+        const long long waves = (units + pairs - 1) / pairs;
+        const double wave_eff = static_cast<double>(units) / static_cast<double>(waves * pairs);
+        const double score = col_eff * wave_eff * tile_eff[i];
+        if (score > best_score + 1e-9) {
+            best_score = score;
+            best = bn;
+        }
+    }
+    return best;
 }
+
+struct Plan {
+    bool pair;
+    int bn, splits;
+};
+
+// Variant, tile width and K splits for a product.  Pair tiles halve the per-SM shared-memory
+// operand traffic, so they are used whenever the output (or its K splits) still gives every
+// pair of SMs work; narrow outputs keep the single-CTA tiles.  MN-major B needs whole 64-column
+// boxes per CTA half, hence N % 128 == 0 for pair tiles.
+Plan plan_for(int M, int N, int K, bool b_mn, bool splittable) {
+    const int sms = num_sms();
+    const int ktiles = (K + BK - 1) / BK;
+    Plan p{false, pick_bn(M, N), 1};
+    const int bn2 = pick_bn_pair(M, N);
+    // per shape (variant 0) the single-CTA tiles are used until the pair tiles measure faster
+    const bool pair_ok = g_variant == 2 && (!b_mn || N % 128 == 0) && M > BM;
+    if (pair_ok) {
+        const int tiles2 = ((M + kPairRows - 1) / kPairRows) * ((N + bn2 - 1) / bn2);
+        int splits2 = 1;
+        if (splittable && tiles2 < sms / 4 && ktiles >= 8)
+            splits2 = std::max(1, std::min((sms / 2 + tiles2 - 1) / tiles2, ktiles / 4));
+        if (g_variant == 2 || tiles2 * splits2 >= sms / 2) return Plan{true, bn2, splits2};
+    }
+    const int tiles = ((M + BM - 1) / BM) * ((N + p.bn - 1) / p.bn);
+    if (splittable && tiles < sms / 2 && ktiles >= 8) p.splits = std::max(1, std::min((sms + tiles - 1) / tiles, ktiles / 4));
+    return p;
+}
+
+}  // namespace
+
+void gemm_tc_set_variant(int v) { g_variant = v; }
+int gemm_tc_variant() { return g_variant; }
+
+int gemm_tc_splits(int M, int N, int K, bool b_mn) { return plan_for(M, N, K, b_mn, true).splits; }
 
 cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t lda, int64_t ldb, cudaStream_t st) {
     GemmArgs g = g_in;
@@ -446,21 +769,25 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
     cudaError_t de = cudaGetDevice(&dev);
     if (de == cudaSuccess) de = cudaSetDevice(dev);
     if (de != cudaSuccess) return de;
-    const int bn = pick_bn(g.M, g.N);
+    const Plan plan = plan_for(g.M, g.N, g.K, b_mn, g.ws != nullptr);
+    const int bn = plan.bn;
+    const int rows = plan.pair ? kPairRows : BM;
+    const int b_rows = plan.pair ? bn / 2 : bn;     // B rows per CTA (K-major box height)
     CUtensorMap ta, tb;
     bool ok = a_mn ? make_map(&ta, g.A, g.M, g.K, lda, 64) : make_map(&ta, g.A, g.K, g.M, lda, BM);
-    ok = ok && (b_mn ? make_map(&tb, g.B, g.N, g.K, ldb, 64) : make_map(&tb, g.B, g.K, g.N, ldb, bn));
+    ok = ok && (b_mn ? make_map(&tb, g.B, g.N, g.K, ldb, 64) : make_map(&tb, g.B, g.K, g.N, ldb, b_rows));
     if (!ok) return cudaErrorInvalidValue;
     Sched sch;
     sch.bn = bn;
-    sch.m_tiles = (g.M + BM - 1) / BM;
+    sch.rows = rows;
+    sch.m_tiles = (g.M + rows - 1) / rows;
     sch.n_tiles = (g.N + bn - 1) / bn;
     sch.ktiles = (g.K + BK - 1) / BK;
     sch.splits = g.ws ? std::max(1, g.splits) : 1;
     sch.kt_per_split = (sch.ktiles + sch.splits - 1) / sch.splits;
     sch.splits = (sch.ktiles + sch.kt_per_split - 1) / sch.kt_per_split;
     const int units = sch.m_tiles * sch.n_tiles * sch.splits;
-    const int grid = std::min(units, num_sms());
+    const int grid = plan.pair ? 2 * std::min(units, std::max(1, num_sms() / 2)) : std::min(units, num_sms());
     cudaError_t e = cudaSuccess;
     if (g.ws) {
         e = cudaMemsetAsync(g.ws, 0, static_cast<size_t>(g.M) * g.ldc * sizeof(float), st);
@@ -483,9 +810,24 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
         else if (a_mn && b_mn) launch(gemm_tc_kernel<true, true, BNv>, smem);
         else launch(gemm_tc_kernel<true, false, BNv>, smem);
     };
-    if (bn == 256) by_major(std::integral_constant<int, 256>{});
-    else if (bn == 192) by_major(std::integral_constant<int, 192>{});
-    else by_major(std::integral_constant<int, 128>{});
+    auto by_major_pair = [&](auto bnc) {
+        constexpr int BNv = decltype(bnc)::value;
+        const size_t smem = PairTile<BNv>::kSmemBytes;
+        if (!a_mn && !b_mn) launch(gemm_tc2_kernel<false, false, BNv>, smem);
+        else if (!a_mn && b_mn) launch(gemm_tc2_kernel<false, true, BNv>, smem);
+        else if (a_mn && b_mn) launch(gemm_tc2_kernel<true, true, BNv>, smem);
+        else launch(gemm_tc2_kernel<true, false, BNv>, smem);
+    };
+    if (plan.pair) {
+        if (bn == 256) by_major_pair(std::integral_constant<int, 256>{});
+        else by_major_pair(std::integral_constant<int, 128>{});
+    } else if (bn == 256) {
+        by_major(std::integral_constant<int, 256>{});
+    } else if (bn == 192) {
+        by_major(std::integral_constant<int, 192>{});
+    } else {
+        by_major(std::integral_constant<int, 128>{});
+    }
     if (e != cudaSuccess || !g.ws) return e;
     const int64_t n = static_cast<int64_t>(g.M) * g.ldc;
     ws_to_bf16_kernel<<<std::min<int64_t>((n / 8 + 255) / 256, num_sms() * 8), 256, 0, st>>>(g.ws, g.C, n);

@@ -28,7 +28,10 @@ struct GemmArgs {
 
 size_t gemm_tc_smem_bytes();
 // K splits worth using for this shape (1 = none); only for plain products (no bias / epilogue).
-int gemm_tc_splits(int M, int N, int K);
+int gemm_tc_splits(int M, int N, int K, bool b_mn);
+// 0: single-CTA or CTA-pair tiles chosen per shape; 1: single-CTA only; 2: CTA pairs where allowed.
+void gemm_tc_set_variant(int v);
+int gemm_tc_variant();
 // a_mn: A stored [K, M] (else [M, K]); b_mn: B stored [K, N] (else [N, K]); lda/ldb: row pitch in elements.
 cudaError_t launch_gemm_tc(const GemmArgs& g, bool a_mn, bool b_mn, int64_t lda, int64_t ldb, cudaStream_t st);
 

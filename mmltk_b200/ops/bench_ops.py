@@ -107,12 +107,24 @@ def bench_gemm(device="cuda", only=None, quick=False):
                 ours()
             torch.cuda.synchronize()
             continue
-        t_ours, t_lib = time_ms(ours), time_ms(lib)
+        # device time from CUDA-graph replays, as in the training step (host launch cost excluded)
+        t_ours, t_lib = time_graph_ms(ours), time_graph_ms(lib)
         fl = 2.0 * M * N * K
-        rows.append({"shape": name, "M": M, "N": N, "K": K, "mode": mode, "ms_tc": round(t_ours, 4),
-                     "ms_cublas": round(t_lib, 4), "tflops_tc": round(fl / t_ours / 1e9, 1),
-                     "tflops_cublas": round(fl / t_lib / 1e9, 1), "speedup": round(t_lib / t_ours, 3),
-                     "rel_err": err, "status": k.gemm_tc_status(torch.cuda.current_device())})
+        row = {"shape": name, "M": M, "N": N, "K": K, "mode": mode, "ms_tc": round(t_ours, 4),
+               "ms_cublas": round(t_lib, 4), "tflops_tc": round(fl / t_ours / 1e9, 1),
+               "tflops_cublas": round(fl / t_lib / 1e9, 1), "speedup": round(t_lib / t_ours, 3),
+               "rel_err": err}
+        # the two tile variants forced: single-CTA 128-row tiles / CTA-pair 256-row tiles
+        for v in (1, 2):
+            k.gemm_tc_set_variant(v)
+            try:
+                e_v = ((ours()[0].float() - ref).abs().max() / ref.abs().max()).item()
+                t_v = time_graph_ms(ours)
+                row[f"ms_tc{v}"], row[f"tflops_tc{v}"], row[f"rel_err_tc{v}"] = round(t_v, 4), round(fl / t_v / 1e9, 1), e_v
+            finally:
+                k.gemm_tc_set_variant(0)
+        row["status"] = k.gemm_tc_status(torch.cuda.current_device())
+        rows.append(row)
     return rows
 
 
@@ -191,8 +203,18 @@ def bench_attn(device="cuda", quick=False):
     """Forward + backward of the step's attention shapes under each SDPA backend.  ``quick``:
     three launches of the tcgen05 forward on the ViT global shape, untimed (profiler runs)."""
     if quick:
-        from .attention import qkv_attention_tc
         g = torch.Generator(device=device).manual_seed(0)
+        if quick == "short":
+            # forward + backward of the short-sequence kernels on the decoder self-attention shape
+            from .attention import short_attention
+            N, H, L, D = 104, 8, 300, 32
+            qkv = torch.randn(N * L, 3 * H * D, device=device, generator=g).bfloat16().requires_grad_()
+            go = torch.randn(N * L, H * D, device=device, generator=g).bfloat16()
+            for _ in range(3):
+                torch.autograd.grad(short_attention(qkv, None, (0, H * D, 2 * H * D), N, L, H, D), (qkv,), go)
+            torch.cuda.synchronize()
+            return [{"op": "attention", "shape": "dec.self_attn", "quick": True}]
+        from .attention import qkv_attention_tc
         qkv = torch.randn(8, 1300, 3 * 384, device=device, generator=g).bfloat16()
         with torch.no_grad():
             for _ in range(3):
@@ -262,12 +284,18 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "msda", "attn"])
     ap.add_argument("--shape", default=None, help="run one GEMM shape (see GEMM_SHAPES)")
-    ap.add_argument("--quick", action="store_true", help="launch a few times without timing (profiler runs)")
+    ap.add_argument("--quick", nargs="?", const="default", default=None,
+                    help="launch a few times without timing (profiler runs); attn: '--quick short' runs the "
+                         "short-sequence kernels on the decoder shape")
+    ap.add_argument("--variant", type=int, default=0,
+                    help="gemm: 0 tile variant per shape, 1 single-CTA tiles, 2 CTA-pair tiles")
     args = ap.parse_args()
     if args.what == "gemm":
-        rows = bench_gemm(only=args.shape, quick=args.quick)
+        from ._ext import kernels
+        kernels().gemm_tc_set_variant(args.variant)
+        rows = bench_gemm(only=args.shape, quick=bool(args.quick))
     elif args.what == "msda":
-        rows = bench_msda(quick=args.quick)
+        rows = bench_msda(quick=bool(args.quick))
     else:
         rows = bench_attn(quick=args.quick)
     for r in rows:

@@ -252,6 +252,59 @@ def test_gemm_tc_all_operand_majors(cuda_device, a_mn, b_mn, M, N, K):
     assert err < 1e-2, err
 
 
+@pytest.fixture
+def pair_tiles():
+    """Force the CTA-pair (tcgen05.mma.cta_group::2) tiles for the test, then restore the choice."""
+    k = kernels()
+    old = k.gemm_tc_variant()
+    k.gemm_tc_set_variant(2)
+    yield k
+    k.gemm_tc_set_variant(old)
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K", [(1280, 384, 384), (1300, 1536, 200), (2048, 256, 3120), (384, 1152, 1536)])
+def test_gemm_tc_pair_tiles(cuda_device, pair_tiles, a_mn, b_mn, M, N, K):
+    """CTA-pair tiles (M = 256 per MMA, each CTA holding half of B) vs fp32 matmul, every operand
+    major, an M tail whose second CTA has no valid rows, K tails and a split-K shape."""
+    if (a_mn and M % 128) or (b_mn and N % 128):
+        pytest.skip("MN-major extents must be multiples of 128")
+    k = pair_tiles
+    g = torch.Generator().manual_seed(M + 7 * N + K)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, generator=g).to(torch.bfloat16)
+    ref = A.float() @ B.float().t()
+    a = (A.t().contiguous() if a_mn else A).to(cuda_device)
+    b = (B.t().contiguous() if b_mn else B).to(cuda_device)
+    for _ in range(2):   # the second call reuses the pair's barriers and tensor memory from a fresh launch
+        out = k.gemm_tc(a, b, None, a_mn, b_mn)[0]
+    torch.cuda.synchronize()
+    assert k.gemm_tc_status(0) == 0
+    err = (out.float().cpu() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, err
+
+
+@pytest.mark.parametrize("epi", ["gelu", "relu", "scale_residual"])
+def test_gemm_tc_pair_tiles_epilogues(cuda_device, pair_tiles, epi):
+    from mmltk_b200.ops.gemm import gemm_nt_epilogue
+    g = torch.Generator().manual_seed(5)
+    M, N, K = 333, 384, 384
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    B = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16)
+    bias = torch.randn(N, generator=g).to(torch.bfloat16)
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    gamma = torch.rand(N, generator=g).to(torch.bfloat16)
+    pre = A.float() @ B.float().t() + bias.float()
+    ref = {"gelu": torch.nn.functional.gelu(pre), "relu": torch.relu(pre),
+           "scale_residual": res.float() + gamma.float() * pre}[epi]
+    d = lambda t: t.to(cuda_device)
+    out, pre_d = gemm_nt_epilogue(d(A), d(B), d(bias), epi, d(res), d(gamma), force=True)
+    torch.cuda.synchronize()
+    assert pair_tiles.gemm_tc_status(0) == 0
+    assert (pre_d.float().cpu() - pre).abs().max().item() < 2e-2 * pre.abs().max().item()
+    assert (out.float().cpu() - ref).abs().max().item() < 2e-2 * ref.abs().max().item()
+
+
 @pytest.mark.parametrize("epi", ["gelu", "relu", "scale_residual"])
 def test_gemm_tc_fused_epilogues(cuda_device, epi):
     from mmltk_b200.ops.gemm import gemm_nt_epilogue
