@@ -329,6 +329,325 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ------------------------------------------------------------------------ forward, ping-pong form
+//
+// Two softmax warpgroups (warps 0-3, 4-7; thread = query row) each own a region of tensor memory
+// (S chunk: 128 columns, O: 64 columns) and a P buffer in shared memory, and work through the keys in
+// 128-key chunks with an online softmax: while one warpgroup exponentiates its chunk, the tensor core
+// computes the other's.  The running maximum is only moved (and O rescaled in tensor memory) when a
+// chunk's maximum exceeds it by more than 2^8, so rescaling is rare.  Head dim 32: one CTA takes two
+// heads of a sequence (the 64-column boxes of q / k / v hold both), warpgroup w head 2j + w, every
+// query tile; P.V runs with N = 64 (both heads' v columns) and each warpgroup keeps its half.  Head
+// dim 64: one CTA per (sequence, head), warpgroup w takes query tiles w, w + 2, ...
+namespace pp {
+constexpr int kWarps = 10;                  // 8 softmax (2 warpgroups), producer, MMA issuer
+constexpr int kThreadsPP = 32 * kWarps;
+constexpr int kProd = 8, kMma = 9;
+constexpr int kRegion = 256;                // tensor-memory columns per warpgroup: S [0, 128), O [128, 192)
+constexpr float kRescale = 8.f;             // log2 slack before the running maximum is moved
+}  // namespace pp
+
+struct __align__(8) Fwd2Ctl {
+    uint64_t kv_full, q_full[2], q_empty[2], s_full[2], p_full[2], o_full[2], o_free[2];
+    uint32_t tmem_base;
+    int abort;
+};
+
+__host__ __device__ constexpr size_t fwd2_smem_bytes() {
+    // K, V (3 boxes each), Q (2 buffers), P (2 warpgroups x 2 boxes of 64 keys), control block
+    return 1024 + static_cast<size_t>(kBox) * (3 + 3 + 2 + 4) + 256;
+}
+
+template <int D>
+__global__ void __launch_bounds__(pp::kThreadsPP, 1)
+    attn_short_fwd2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                           const __grid_constant__ CUtensorMap tv, FwdArgs a) {
+    using namespace pp;
+    constexpr bool kPair = D == 32;           // two heads per CTA
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    Fwd2Ctl* ctl = reinterpret_cast<Fwd2Ctl*>(smem_raw);
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + sizeof(Fwd2Ctl) + 1023) & ~uintptr_t(1023));
+    const int L = a.L;
+    const int T = (L + kRows - 1) / kRows;    // query tiles = key chunks
+    unsigned char* sK = smem;
+    unsigned char* sV = sK + 3 * kBox;
+    unsigned char* sQ = sV + 3 * kBox;        // 2 buffers
+    unsigned char* sP = sQ + 2 * kBox;        // 2 warpgroups x 2 boxes
+    if (L > kMaxL || sP + 4 * kBox - smem_raw > static_cast<ptrdiff_t>(fwd2_smem_bytes())) {
+        if (threadIdx.x == 0) atomicCAS(a.status, 0, 8);
+        return;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = kPair ? (a.H + 1) / 2 : a.H;     // CTAs per sequence
+    const int n = blockIdx.x / groups, g = blockIdx.x % groups;
+    const int row0 = n * L;
+    const int hcol = g * 64;                  // first column of this CTA's boxes within each source
+    // jobs (query tiles) of warpgroup w: pair form every tile, else tiles w, w + 2, ...
+    auto jobs = [&](int w) { return kPair ? (2 * g + w < a.H ? T : 0) : (T - w + 1) / 2; };
+    auto tile_of = [&](int w, int j) { return kPair ? j : w + 2 * j; };
+
+    if (threadIdx.x == 0) {
+        mbar_init(&ctl->kv_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&ctl->q_full[i], 1);
+            mbar_init(&ctl->q_empty[i], 1);
+            mbar_init(&ctl->s_full[i], 1);
+            mbar_init(&ctl->p_full[i], 4);
+            mbar_init(&ctl->o_full[i], 1);
+            mbar_init(&ctl->o_free[i], 4);
+        }
+        ctl->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == kProd) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&ctl->tmem_base)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == kProd) {
+        if (lane == 0) {
+            mbar_expect_tx(&ctl->kv_full, 2 * T * kBox);
+            for (int t = 0; t < T; ++t) {
+                tma_load_2d(&tk, &ctl->kv_full, sK + t * kBox, a.kcol + hcol, row0 + t * kRows);
+                tma_load_2d(&tv, &ctl->kv_full, sV + t * kBox, a.vcol + hcol, row0 + t * kRows);
+            }
+            bool ok = true;
+            if (kPair) {
+                for (int t = 0; ok && t < T; ++t) {
+                    const int b = t & 1;
+                    if (t >= 2 && !mbar_wait(&ctl->q_empty[b], ((t >> 1) - 1) & 1, &ctl->abort)) ok = false;
+                    if (!ok) break;
+                    mbar_expect_tx(&ctl->q_full[b], kBox);
+                    tma_load_2d(&tq, &ctl->q_full[b], sQ + b * kBox, a.qcol + hcol, row0 + t * kRows);
+                }
+            } else {
+                for (int j = 0; ok && 2 * j < T; ++j) {
+                    for (int w = 0; w < 2; ++w) {
+                        const int t = w + 2 * j;
+                        if (t >= T) break;
+                        if (j >= 1 && !mbar_wait(&ctl->q_empty[w], (j - 1) & 1, &ctl->abort)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(&ctl->q_full[w], kBox);
+                        tma_load_2d(&tq, &ctl->q_full[w], sQ + w * kBox, a.qcol + hcol, row0 + t * kRows);
+                    }
+                }
+            }
+            if (!ok) {
+                ctl->abort = 1;
+                atomicCAS(a.status, 0, 1);
+            }
+        }
+    } else if (warp == kMma) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = instr_desc(false, false, kRows);   // S chunk: N = 128 keys
+            constexpr uint32_t idesc_o = instr_desc(false, true, 64);       // O: N = 64 (a whole v box)
+            const uint32_t qb = smem_u32(sQ), kb = smem_u32(sK), vb = smem_u32(sV), pb = smem_u32(sP);
+            const int steps[2] = {jobs(0) * T, jobs(1) * T};
+            bool ok = mbar_wait(&ctl->kv_full, 0, &ctl->abort);
+            // S chunk of warpgroup w at step k (job k / T, key chunk k % T)
+            auto issue_s = [&](int w, int k) -> bool {
+                const int j = k / T, c = k % T;
+                const int qbuf = kPair ? (j & 1) : w;
+                if (c == 0) {
+                    const uint32_t qph = kPair ? ((j >> 1) & 1) : (j & 1);
+                    if (!mbar_wait(&ctl->q_full[qbuf], qph, &ctl->abort)) return false;
+                    tc_fence_after();
+                }
+                const int kk0 = kPair ? 2 * w : 0;   // head 2g + w: columns [32 w, 32 w + 32) of the box
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    tc_mma(tmem + w * kRegion, operand_desc<false>(qb + qbuf * kBox, kk0 + kk),
+                           operand_desc<false>(kb + c * kBox, kk0 + kk), idesc_s, kk > 0);
+                tc_commit(&ctl->s_full[w]);
+                if (c == T - 1 && (!kPair || w == 1 || jobs(1) == 0)) tc_commit(&ctl->q_empty[qbuf]);
+                return true;
+            };
+            for (int w = 0; ok && w < 2; ++w)
+                if (steps[w] > 0) ok = issue_s(w, 0);
+            for (int k = 0; ok; ++k) {
+                bool any = false;
+                for (int w = 0; ok && w < 2; ++w) {
+                    if (k >= steps[w]) continue;
+                    any = true;
+                    const int j = k / T, c = k % T;
+                    if (!mbar_wait(&ctl->p_full[w], k & 1, &ctl->abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (c == 0 && j > 0) {
+                        if (!mbar_wait(&ctl->o_free[w], (j - 1) & 1, &ctl->abort)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                    }
+                    const uint32_t p = pb + w * 2 * kBox;
+#pragma unroll
+                    for (int s16 = 0; s16 < kRows / 16; ++s16)
+                        tc_mma(tmem + w * kRegion + 128, smem_desc(p + (s16 >> 2) * kBox + (s16 & 3) * 32, 16, 1024),
+                               smem_desc(vb + c * kBox + s16 * 2048, 8192, 1024), idesc_o, (c > 0 || s16 > 0));
+                    if (c == T - 1) tc_commit(&ctl->o_full[w]);
+                    if (k + 1 < steps[w]) ok = issue_s(w, k + 1);
+                }
+                if (!any) break;
+            }
+            if (!ok) {
+                ctl->abort = 1;
+                atomicCAS(a.status, 0, 2);
+            }
+        }
+    } else {
+        // softmax warpgroup w = warp / 4: thread = query row r of the current tile (TMEM lane r)
+        const int w = warp >> 2, quad = warp & 3;
+        const int r = 32 * quad + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(32 * quad) << 16;
+        const uint32_t tS = tmem + w * kRegion + lane_off, tO = tS + 128;
+        const int h = kPair ? 2 * g + w : g;
+        const int ocol_t = kPair ? 32 * w : 0;   // this head's columns of the O accumulator
+        unsigned char* myP = sP + w * 2 * kBox;
+        const int J = jobs(w);
+        bool ok = true;
+        int k = 0;
+        for (int j = 0; ok && j < J; ++j) {
+            const int t = tile_of(w, j);
+            const bool live = t * kRows + 32 * quad < L;   // warp-uniform: any valid query row here
+            float m_used = -1e30f, l = 0.f;
+            for (int c = 0; c < T; ++c, ++k) {
+                if (!mbar_wait(&ctl->s_full[w], k & 1, &ctl->abort)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (live) {
+                    // 32 score columns in registers at a time: the row maximum over the chunk, then the
+                    // exponentials (the columns read again from tensor memory)
+                    const int kbase = c * kRows;
+                    float mc = -1e30f;
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float sv[32];
+                        tmem_ld32(tS + 32 * q4, sv);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (kbase + 32 * q4 + i < L) mc = fmaxf(mc, sv[i]);
+                        asm volatile("" : "+f"(mc));
+                    }
+                    const float m_new = mc * a.scale_log2;
+                    bool need = false;
+                    float alpha = 1.f;
+                    if (c == 0) {
+                        m_used = m_new;
+                    } else if (m_new > m_used + kRescale) {
+                        need = true;
+                        alpha = ex2(m_used - m_new);
+                        m_used = m_new;
+                        l *= alpha;
+                    }
+                    if (__any_sync(0xffffffffu, need)) {
+                        // O holds the chunks so far (their P.V are complete: S of this chunk was issued
+                        // after them); bring it to the new maximum before this chunk's P.V adds to it
+#pragma unroll
+                        for (int part = 0; part < D / 32; ++part) {
+                            float o[32];
+                            const uint32_t at = tO + ocol_t + 32 * part;
+                            tmem_ld32(at, o);
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                            tmem_st16(at, o);
+                            tmem_st16(at + 16, o + 16);
+                            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                        }
+                    }
+                    float sum = 0.f;
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float sv[32];
+                        tmem_ld32(tS + 32 * q4, sv);
+#pragma unroll
+                        for (int g8 = 0; g8 < 4; ++g8) {
+                            uint32_t wv[4];
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const int c0 = 8 * g8 + 2 * i;
+                                const int key = kbase + 32 * q4 + c0;
+                                const float p0 = key < L ? ex2(sv[c0] * a.scale_log2 - m_used) : 0.f;
+                                const float p1 = key + 1 < L ? ex2(sv[c0 + 1] * a.scale_log2 - m_used) : 0.f;
+                                sum += p0 + p1;
+                                wv[i] = pack_bf16x2(p0, p1);
+                            }
+                            put8(myP, r, 32 * q4 + 8 * g8, wv);
+                        }
+                        asm volatile("" : "+f"(sum)::"memory");
+                    }
+                    l += sum;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctl->p_full[w]);
+            }
+            if (!ok) break;
+            if (!mbar_wait(&ctl->o_full[w], j & 1, &ctl->abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float o[32];
+            if (D == 32) {
+                tmem_ld32(tO + ocol_t, o);
+            } else {
+                tmem_ld32(tO, o);
+            }
+            float o2[32];
+            if (D == 64) tmem_ld32(tO + 32, o2);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->o_free[w]);
+            const int qrow = t * kRows + r;
+            if (qrow < L) {
+                const float inv = 1.f / l;
+                uint4* dst = reinterpret_cast<uint4*>(a.o + static_cast<int64_t>(row0 + qrow) * a.ldo + a.ocol + h * D);
+#pragma unroll
+                for (int q8 = 0; q8 < 4; ++q8)
+                    dst[q8] = make_uint4(pack_bf16x2(o[8 * q8] * inv, o[8 * q8 + 1] * inv),
+                                         pack_bf16x2(o[8 * q8 + 2] * inv, o[8 * q8 + 3] * inv),
+                                         pack_bf16x2(o[8 * q8 + 4] * inv, o[8 * q8 + 5] * inv),
+                                         pack_bf16x2(o[8 * q8 + 6] * inv, o[8 * q8 + 7] * inv));
+                if (D == 64) {
+#pragma unroll
+                    for (int q8 = 0; q8 < 4; ++q8)
+                        dst[4 + q8] = make_uint4(pack_bf16x2(o2[8 * q8] * inv, o2[8 * q8 + 1] * inv),
+                                                 pack_bf16x2(o2[8 * q8 + 2] * inv, o2[8 * q8 + 3] * inv),
+                                                 pack_bf16x2(o2[8 * q8 + 4] * inv, o2[8 * q8 + 5] * inv),
+                                                 pack_bf16x2(o2[8 * q8 + 6] * inv, o2[8 * q8 + 7] * inv));
+                }
+                if (a.lse) a.lse[(static_cast<int64_t>(n) * a.H + h) * L + qrow] = (m_used + __log2f(l)) * 0.69314718055994531f;
+            }
+        }
+        if (!ok) {
+            ctl->abort = 1;
+            if (lane == 0) atomicCAS(a.status, 0, 3);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kProd) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
 // ------------------------------------------------------------------------------------ backward
 
 struct __align__(8) BwdCtl {
@@ -722,9 +1041,15 @@ cudaError_t ensure_smem(K kern, size_t bytes, int dev) {
 template <bool Bwd, int D>
 struct KernelTag {};
 
+// forward kernel: 1 = whole score row per (sequence, head), 2 = ping-pong warpgroups (default)
+int g_fwd_variant = 2;
+
 }  // namespace
 
 bool attn_short_supported(int L, int D) { return L >= 1 && L <= kMaxL && (D == 32 || D == 64); }
+
+void attn_short_set_fwd_variant(int v) { g_fwd_variant = v == 1 ? 1 : 2; }
+int attn_short_fwd_variant() { return g_fwd_variant; }
 
 cudaError_t launch_attn_short_fwd(const AttnOperand& q, const AttnOperand& k, const AttnOperand& v, int nseq, int L,
                                   int H, int D, void* o, int64_t ldo, int ocol, float* lse, float scale, int* status,
@@ -742,6 +1067,17 @@ cudaError_t launch_attn_short_fwd(const AttnOperand& q, const AttnOperand& k, co
     if ((e = make_map(&mk, k.base, k.cols, rows, k.ld)) != cudaSuccess) return e;
     if ((e = make_map(&mv, v.base, v.cols, rows, v.ld)) != cudaSuccess) return e;
     FwdArgs a{static_cast<__nv_bfloat16*>(o), ldo, lse, status, L, H, q.col, k.col, v.col, ocol, scale * kLog2e};
+    if (g_fwd_variant == 2) {
+        const size_t smem2 = fwd2_smem_bytes();
+        if (D == 32) {
+            if ((e = ensure_smem<KernelTag<false, 33>>(attn_short_fwd2_kernel<32>, smem2, dev)) != cudaSuccess) return e;
+            attn_short_fwd2_kernel<32><<<nseq * ((H + 1) / 2), pp::kThreadsPP, smem2, st>>>(mq, mk, mv, a);
+        } else {
+            if ((e = ensure_smem<KernelTag<false, 65>>(attn_short_fwd2_kernel<64>, smem2, dev)) != cudaSuccess) return e;
+            attn_short_fwd2_kernel<64><<<nseq * H, pp::kThreadsPP, smem2, st>>>(mq, mk, mv, a);
+        }
+        return cudaGetLastError();
+    }
     const size_t smem = fwd_smem_bytes(kMaxL);   // one CTA per SM (the kernel takes all of tensor memory)
     if (D == 32) {
         if ((e = ensure_smem<KernelTag<false, 32>>(attn_short_fwd_kernel<32>, smem, dev)) != cudaSuccess) return e;

@@ -6,8 +6,8 @@
 //
 // Every rank owns one contiguous shard of the flat parameter space.  Two
 // kernels per step, both reading and writing other GPUs' memory directly
-// (CUDA IPC mappings, 16-byte P2P loads and 8-byte P2P stores; no TMA and no
-// multicast):
+// (CUDA IPC mappings, 16-byte P2P loads and stores; no TMA, plain loads and
+// stores only):
 //
 //   ddp_rs_kernel      barrier "gradients ready" -> reduce-scatter: sum the
 //                      shard of every rank's bf16 gradient buffer in fp32
@@ -18,6 +18,10 @@
 //                      master shard -> EMA shard update -> all-gather: write
 //                      the new bf16 parameters into every rank's parameter
 //                      buffer -> barrier "parameters delivered".
+//
+// Between steps the same mappings carry a byte all-gather (evaluation match
+// records): each rank stages its payload in its own gradient buffer, and every
+// rank reads every peer's payload straight out of that peer's buffer.
 //
 // Flags carry a per-step epoch (incremented on the device at the end of the
 // update kernel), so the two kernels can be replayed from a CUDA graph
@@ -219,43 +223,50 @@ __global__ void __launch_bounds__(256) ddp_update_kernel(DdpPeers peers, DdpStat
         const GroupHyper gh = groups[cd.group];
         const float lr = gh.lr * sc->lr_scale;
         const float decay = 1.f - lr * gh.weight_decay;
-        for (int64_t i = cd.offset + 4 * threadIdx.x; i < cd.offset + cd.length; i += 4 * blockDim.x) {
-            float4 p = *reinterpret_cast<float4*>(master + i);
+        // 8 elements per thread: two float4 of every fp32 operand and one 16-byte store of the bf16
+        // parameters per peer (chunks start at multiples of 8; a chunk's last group may run into the
+        // parameter's zero padding, whose update keeps it zero)
+        for (int64_t i = cd.offset + 8 * threadIdx.x; i < cd.offset + cd.length; i += 8 * blockDim.x) {
+            float4 p[2] = {*reinterpret_cast<float4*>(master + i), *reinterpret_cast<float4*>(master + i + 4)};
             if (finite) {
                 // all operands loaded before use: one memory round trip per iteration
-                const float4 g4 = *reinterpret_cast<const float4*>(gshard + i);
-                float4 mm = *reinterpret_cast<float4*>(m + i);
-                float4 vv = *reinterpret_cast<float4*>(v + i);
-                float4 e = do_ema ? *reinterpret_cast<const float4*>(ema + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-                const float gv[4] = {g4.x * gs, g4.y * gs, g4.z * gs, g4.w * gs};
-                float* pp = &p.x;
-                float* mp = &mm.x;
-                float* vp = &vv.x;
+                float4 g4[2], mm[2], vv[2], e[2];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    mp[k] = b1 * mp[k] + (1.f - b1) * gv[k];
-                    vp[k] = b2 * vp[k] + (1.f - b2) * gv[k] * gv[k];
-                    const float denom = sqrtf(vp[k]) * inv_sqrt_bc2 + eps;
-                    pp[k] = pp[k] * decay - lr * inv_bc1 * mp[k] / denom;
+                for (int h = 0; h < 2; ++h) {
+                    g4[h] = *reinterpret_cast<const float4*>(gshard + i + 4 * h);
+                    mm[h] = *reinterpret_cast<float4*>(m + i + 4 * h);
+                    vv[h] = *reinterpret_cast<float4*>(v + i + 4 * h);
+                    e[h] = do_ema ? *reinterpret_cast<const float4*>(ema + i + 4 * h) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                *reinterpret_cast<float4*>(master + i) = p;
-                *reinterpret_cast<float4*>(m + i) = mm;
-                *reinterpret_cast<float4*>(v + i) = vv;
-                if (do_ema) {
-                    e.x = ema_d * e.x + (1.f - ema_d) * p.x;
-                    e.y = ema_d * e.y + (1.f - ema_d) * p.y;
-                    e.z = ema_d * e.z + (1.f - ema_d) * p.z;
-                    e.w = ema_d * e.w + (1.f - ema_d) * p.w;
-                    *reinterpret_cast<float4*>(ema + i) = e;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float gv[4] = {g4[h].x * gs, g4[h].y * gs, g4[h].z * gs, g4[h].w * gs};
+                    float* pp = &p[h].x;
+                    float* mp = &mm[h].x;
+                    float* vp = &vv[h].x;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        mp[k] = b1 * mp[k] + (1.f - b1) * gv[k];
+                        vp[k] = b2 * vp[k] + (1.f - b2) * gv[k] * gv[k];
+                        const float denom = sqrtf(vp[k]) * inv_sqrt_bc2 + eps;
+                        pp[k] = pp[k] * decay - lr * inv_bc1 * mp[k] / denom;
+                    }
+                    *reinterpret_cast<float4*>(master + i + 4 * h) = p[h];
+                    *reinterpret_cast<float4*>(m + i + 4 * h) = mm[h];
+                    *reinterpret_cast<float4*>(v + i + 4 * h) = vv[h];
+                    if (do_ema) {
+                        e[h].x = ema_d * e[h].x + (1.f - ema_d) * p[h].x;
+                        e[h].y = ema_d * e[h].y + (1.f - ema_d) * p[h].y;
+                        e[h].z = ema_d * e[h].z + (1.f - ema_d) * p[h].z;
+                        e[h].w = ema_d * e[h].w + (1.f - ema_d) * p[h].w;
+                        *reinterpret_cast<float4*>(ema + i + 4 * h) = e[h];
+                    }
                 }
             }
-            // all-gather: the same 8 bytes to every rank's parameter buffer
-            __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
-            uint2 raw;
-            raw.x = *reinterpret_cast<uint32_t*>(&lo);
-            raw.y = *reinterpret_cast<uint32_t*>(&hi);
-            for (int j = 0; j < world; ++j)
-                *reinterpret_cast<uint2*>(peers.param[j] + shard_off + i) = raw;
+            // all-gather: the same 16 bytes to every rank's parameter buffer
+            const uint4 raw = make_uint4(pack_bf16x2(p[0].x, p[0].y), pack_bf16x2(p[0].z, p[0].w),
+                                         pack_bf16x2(p[1].x, p[1].y), pack_bf16x2(p[1].z, p[1].w));
+            for (int j = 0; j < world; ++j) *reinterpret_cast<uint4*>(peers.param[j] + shard_off + i) = raw;
         }
     }
     // ---- completion: once every CTA's stores are out, tell every rank, wait for all
@@ -308,7 +319,59 @@ __global__ void small_allreduce_kernel(DdpPeers peers, DdpState st, float* __res
     if (threadIdx.x == 0) *st.small_epoch = epoch + 1;
 }
 
+// Gather barrier: tell every rank (slot `rank` of region `base`) that this rank reached it with the
+// current gather epoch, then wait for every rank's mark; `bump` advances the epoch afterwards.
+__global__ void gather_barrier_kernel(DdpPeers peers, DdpState st, int base, int bump) {
+    const uint32_t epoch = *st.gather_epoch;
+    const int world = peers.world, rank = peers.rank;
+    if (threadIdx.x < world) {
+        __threadfence_system();
+        st_release_u32(peers.flags[threadIdx.x] + base + rank, epoch);
+    }
+    __syncthreads();
+    if (threadIdx.x < world && !wait_u32(st.flags_local + base + threadIdx.x, epoch, st.spin_limit))
+        record_error(st.status, kErrTimeoutGather);
+    __syncthreads();
+    if (bump && threadIdx.x == 0) *st.gather_epoch = epoch + 1;
+}
+
+struct GatherPlan {
+    int64_t off16[kDdpMaxWorld], len16[kDdpMaxWorld];
+};
+
+// every peer's staged payload (the start of its gradient buffer), 16-byte P2P loads
+__global__ void __launch_bounds__(256) gather_copy_kernel(DdpPeers peers, uint4* __restrict__ out, GatherPlan plan) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int j = 0; j < peers.world; ++j) {
+        const uint4* src = reinterpret_cast<const uint4*>(peers.grad[j]);
+        uint4* dst = out + plan.off16[j];
+        for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < plan.len16[j]; i += stride)
+            dst[i] = ld_peer16(src + i);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_gather_bytes(const DdpPeers& peers, const DdpState& st, void* out, const int64_t* off16,
+                                const int64_t* len16, cudaStream_t s) {
+    if (peers.world < 1 || peers.world > kDdpMaxWorld || reinterpret_cast<uintptr_t>(out) % 16 != 0)
+        return cudaErrorInvalidValue;
+    GatherPlan plan{};
+    int64_t total = 0;
+    for (int j = 0; j < peers.world; ++j) {
+        plan.off16[j] = off16[j];
+        plan.len16[j] = len16[j];
+        total += len16[j];
+    }
+    gather_barrier_kernel<<<1, 32, 0, s>>>(peers, st, kFlagGather, 0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, num_sms() * 2)));
+    gather_copy_kernel<<<blocks, 256, 0, s>>>(peers, static_cast<uint4*>(out), plan);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    gather_barrier_kernel<<<1, 32, 0, s>>>(peers, st, kFlagGatherDone, 1);
+    return cudaGetLastError();
+}
 
 int ddp_rs_blocks() { return num_sms() * 2; }
 

@@ -18,13 +18,16 @@ constexpr int kFlagReady = 0;                       // [world] gradients ready (
 constexpr int kFlagDone = kFlagReady + kDdpMaxWorld;  // [world] parameters delivered (epoch)
 constexpr int kFlagSmall = kFlagDone + kDdpMaxWorld;  // [world] small all-reduce (epoch)
 constexpr int kFlagNorm = 64;                        // [world] u64 (epoch << 32 | sumsq bits), 8-byte aligned
-constexpr int kFlagWords = kFlagNorm + 2 * kDdpMaxWorld;
+constexpr int kFlagGather = kFlagNorm + 2 * kDdpMaxWorld;   // [world] byte all-gather: payload staged (epoch)
+constexpr int kFlagGatherDone = kFlagGather + kDdpMaxWorld;  // [world] byte all-gather: peers' payloads read
+constexpr int kFlagWords = kFlagGatherDone + kDdpMaxWorld;
 
 // Error codes written into DdpState::status.
 constexpr int kErrTimeoutReady = 1;
 constexpr int kErrTimeoutNorm = 2;
 constexpr int kErrTimeoutDone = 3;
 constexpr int kErrTimeoutSmall = 4;
+constexpr int kErrTimeoutGather = 5;
 
 // Pointers into every rank's peer-visible buffers (index = rank).
 struct DdpPeers {
@@ -42,6 +45,7 @@ struct DdpState {
     float* small_local;          // my small all-reduce slots [world * kSmallMax]
     uint32_t* epoch;             // step epoch (device), starts at 1
     uint32_t* small_epoch;       // small all-reduce epoch (device), starts at 1
+    uint32_t* gather_epoch;      // byte all-gather epoch (device), starts at 1
     unsigned int* ticket;        // zeroed grid ticket
     int* status;                 // 0 = ok, else kErrTimeout*
     long long spin_limit;        // polls before a wait gives up
@@ -54,5 +58,10 @@ cudaError_t launch_ddp_update(const DdpPeers& peers, const DdpState& st, int64_t
                               int nchunks, const float* gshard, float* master, float* m, float* v, float* ema,
                               const GroupHyper* groups, const StepScalars* sc, int* flags, cudaStream_t s);
 cudaError_t launch_small_allreduce(const DdpPeers& peers, const DdpState& st, float* data, int n, cudaStream_t s);
+// Byte all-gather between steps: every rank has staged its payload at the start of its own gradient
+// buffer; peer j's len16[j] 16-byte words land at out + off16[j].  Three launches: staged barrier,
+// peer-read copy, read-done barrier (after which every gradient buffer may be written again).
+cudaError_t launch_gather_bytes(const DdpPeers& peers, const DdpState& st, void* out, const int64_t* off16,
+                                const int64_t* len16, cudaStream_t s);
 
 }  // namespace mmltk

@@ -58,7 +58,7 @@ class DdpComm {
         TORCH_CHECK(static_cast<int64_t>(grad.size()) == world && static_cast<int64_t>(param.size()) == world &&
                         static_cast<int64_t>(flags.size()) == world && static_cast<int64_t>(small.size()) == world,
                     "DdpComm: one pointer per rank expected");
-        TORCH_CHECK(ctrl.scalar_type() == torch::kInt32 && ctrl.numel() >= 4 && ctrl.is_cuda(), "DdpComm: ctrl");
+        TORCH_CHECK(ctrl.scalar_type() == torch::kInt32 && ctrl.numel() >= 5 && ctrl.is_cuda(), "DdpComm: ctrl");
         std::memset(&peers_, 0, sizeof(peers_));
         for (int j = 0; j < world; ++j) {
             peers_.grad[j] = reinterpret_cast<const __nv_bfloat16*>(grad[j]);
@@ -75,6 +75,7 @@ class DdpComm {
         st_.small_epoch = reinterpret_cast<uint32_t*>(c + 1);
         st_.ticket = reinterpret_cast<unsigned int*>(c + 2);
         st_.status = c + 3;
+        st_.gather_epoch = reinterpret_cast<uint32_t*>(c + 4);
         st_.spin_limit = spin_limit;
     }
 
@@ -110,6 +111,19 @@ class DdpComm {
                    "small_allreduce");
     }
 
+    // Byte all-gather between steps (see launch_gather_bytes): this rank's payload must already be
+    // staged at the start of its gradient buffer; len16[j] 16-byte words of rank j land at out + off16[j].
+    void gather_bytes(torch::Tensor out, std::vector<int64_t> off16, std::vector<int64_t> len16) {
+        TORCH_CHECK(out.is_cuda() && out.is_contiguous(), "gather_bytes: contiguous CUDA output");
+        TORCH_CHECK(static_cast<int>(off16.size()) == peers_.world && static_cast<int>(len16.size()) == peers_.world,
+                    "gather_bytes: one offset and length per rank");
+        int64_t end = 0;
+        for (int j = 0; j < peers_.world; ++j) end = std::max(end, (off16[j] + len16[j]) * 16);
+        TORCH_CHECK(end <= out.numel() * out.element_size(), "gather_bytes: output too small");
+        check_cuda(launch_gather_bytes(peers_, st_, out.data_ptr(), off16.data(), len16.data(), cur_stream()),
+                   "gather_bytes");
+    }
+
    private:
     DdpPeers peers_;
     DdpState st_;
@@ -130,7 +144,8 @@ void register_ddp_ops(pybind11::module& m) {
                       int64_t, torch::Tensor, torch::Tensor, torch::Tensor, int64_t>())
         .def("rs", &DdpComm::rs)
         .def("update", &DdpComm::update)
-        .def("small_allreduce", &DdpComm::small_allreduce);
+        .def("small_allreduce", &DdpComm::small_allreduce)
+        .def("gather_bytes", &DdpComm::gather_bytes);
 }
 
 }  // namespace mmltk

@@ -31,15 +31,20 @@ class CocoEvaluator:
         self.ev.add_batch(list(int(i) for i in indices), scores, labels, boxes_xyxy,
                           masks if (self.masks and masks is not None) else None)
 
-    def reduce(self, group=None) -> None:
-        """All-gather every rank's match records (collective: every rank calls it)."""
+    def reduce(self, group=None, gather=None) -> None:
+        """All-gather every rank's match records (collective: every rank calls it).  ``gather``:
+        a tensor all-gather (``FusedGradSync.all_gather_tensor``: peer-memory reads over NVLink)
+        used instead of the process group's object all-gather."""
         import torch.distributed as dist
         if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
             return
         for mask in ([False, True] if self.masks else [False]):
             mine = self.ev.export_matches(mask)
-            parts = [None] * dist.get_world_size(group)
-            dist.all_gather_object(parts, mine, group=group)
+            if gather is not None:
+                parts = gather(mine)
+            else:
+                parts = [None] * dist.get_world_size(group)
+                dist.all_gather_object(parts, mine, group=group)
             rank = dist.get_rank(group)
             for r, t in enumerate(parts):
                 if r != rank and t.numel():

@@ -256,6 +256,12 @@ def bench_attn(device="cuda", quick=False):
             def short_pk():
                 return short_attention(qkv, None, (0, C, 2 * C), N, L, H, D)
 
+            from ._ext import kernels
+            for v in (1, 2):    # forward variants: whole score row per CTA / ping-pong warpgroups
+                kernels().attn_short_set_fwd_variant(v)
+                with torch.no_grad():
+                    row[f"packed_short_v{v}_fwd_ms"] = round(time_graph_ms(short_pk), 4)
+            kernels().attn_short_set_fwd_variant(2)
             for tag, f in (("cudnn", cudnn_pk), ("short", short_pk)):
                 with torch.no_grad():
                     row[f"packed_{tag}_fwd_ms"] = round(time_graph_ms(f), 4)

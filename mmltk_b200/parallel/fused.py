@@ -36,7 +36,8 @@ from ..ops._ext import kernels
 __all__ = ["FusedGradSync", "shard_chunks"]
 
 ERRORS = {1: "a peer never signalled 'gradients ready'", 2: "a peer never published its gradient norm",
-          3: "a peer never delivered its parameter shard", 4: "a peer never joined the small all-reduce"}
+          3: "a peer never delivered its parameter shard", 4: "a peer never joined the small all-reduce",
+          5: "a peer never joined the byte all-gather"}
 
 
 def shard_chunks(chunks: torch.Tensor, off: int, size: int) -> torch.Tensor:
@@ -92,8 +93,9 @@ class FusedGradSync:
                     self._opened.append(p)
                     ptrs[b][j] = p
         self.ctrl = torch.zeros(8, dtype=torch.int32, device=dev)
-        self.ctrl[0] = 1
-        self.ctrl[1] = 1
+        self.ctrl[0] = 1       # step epoch
+        self.ctrl[1] = 1       # small all-reduce epoch
+        self.ctrl[4] = 1       # byte all-gather epoch
         self.comm = k.DdpComm(ptrs[1], ptrs[0], ptrs[2], ptrs[3], self.rank, self.world_size,
                               flags.view(torch.int32), small.view(torch.float32), self.ctrl, self.spin_limit)
         # identical starting point on every rank
@@ -110,6 +112,7 @@ class FusedGradSync:
         self.gshard = torch.zeros(S, dtype=torch.float32, device=dev)
         self.partials = torch.zeros(k.ddp_rs_blocks(), dtype=torch.float32, device=dev)
         self.chunks = shard_chunks(engine.flat.chunk_table(), self.off, S).to(dev)
+        self._stage = engine.flat.grad_buf.view(torch.uint8)   # byte all-gather staging (between steps)
         dist.barrier(group=self.group)
 
     # ---------------------------------------------------------------- step
@@ -139,6 +142,45 @@ class FusedGradSync:
             self.failed = (f"fused DDP step failed on rank {self.rank}: {ERRORS.get(code, code)} "
                            f"within the wait limit")
             raise RuntimeError(self.failed)
+
+    def all_gather_tensor(self, t: torch.Tensor) -> List[torch.Tensor]:
+        """Every rank's ``t`` (same dtype and trailing shape on every rank, any first dimension),
+        in rank order, as CPU tensors.  Collective; runs between steps only: each rank stages its
+        bytes in its own gradient buffer and every rank reads every peer's bytes straight out of
+        that buffer over NVLink (16-byte loads), between two device-side barriers.  The next step
+        clears the gradient buffer before it accumulates into it."""
+        if self.failed is not None:
+            raise RuntimeError(f"fused DDP sync is unusable after an earlier failure: {self.failed}")
+        dev = self.device
+        tail = tuple(t.shape[1:])
+        raw = t.detach().contiguous().reshape(-1).view(torch.uint8)
+        # 16-byte header with the exact byte count, then the payload padded to 16 bytes
+        n = raw.numel()
+        n16 = 1 + (n + 15) // 16
+        if n16 >= (1 << 24):
+            raise ValueError(f"all_gather_tensor: {n} bytes is above the 256 MB limit of one gather")
+        if n16 * 16 > self._stage.numel():
+            raise ValueError(f"all_gather_tensor: {n} bytes do not fit the {self._stage.numel()}-byte staging buffer")
+        counts = torch.zeros(self.world_size, dtype=torch.float32, device=dev)
+        counts[self.rank] = float(n16)        # exact: below 2^24
+        self.comm.small_allreduce(counts)
+        head = torch.zeros(16, dtype=torch.uint8)
+        head[:8] = torch.tensor([n], dtype=torch.int64).view(torch.uint8)
+        self._stage[:16].copy_(head.to(dev, non_blocking=False))
+        if n:
+            self._stage[16:16 + n].copy_(raw.to(dev))
+        sizes = [int(c) for c in counts.cpu().tolist()]
+        offs = [sum(sizes[:j]) for j in range(self.world_size)]
+        out = torch.empty(sum(sizes) * 16, dtype=torch.uint8, device=dev)
+        self.comm.gather_bytes(out, offs, sizes)
+        host = out.cpu()
+        self.check(int(self.ctrl[3].item()))
+        parts = []
+        for j in range(self.world_size):
+            b = host[offs[j] * 16:(offs[j] + sizes[j]) * 16]
+            nb = int(b[:8].view(torch.int64).item())
+            parts.append(b[16:16 + nb].clone().view(t.dtype).reshape(-1, *tail))
+        return parts
 
     # ---------------------------------------------------------------- state
     def gather_full(self, shard: torch.Tensor) -> torch.Tensor:

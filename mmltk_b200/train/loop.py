@@ -136,7 +136,8 @@ def _check_resume(extra: Dict, opts: TrainOptions) -> None:
 
 
 def evaluate(model_fp32: torch.nn.Module, compiled: str, ctx: DistContext, batch_size: int, max_dets: int,
-             masks: bool, shard: bool = True, with_loss: bool = False, sample_png: Optional[str] = None) -> Dict:
+             masks: bool, shard: bool = True, with_loss: bool = False, sample_png: Optional[str] = None,
+             gather=None) -> Dict:
     """COCO AP of a model over a compiled split; each rank takes every world-th batch.
     ``sample_png``: the main rank also writes its first validation image with the predictions drawn
     on the GPU (reference: the eval sample image of `train.cpp:158-265`)."""
@@ -169,7 +170,7 @@ def evaluate(model_fp32: torch.nn.Module, compiled: str, ctx: DistContext, batch
             ev.add(ids, res["scores"], res["labels"], res["boxes"], res.get("masks"))
     pred.release()
     if shard and ctx.enabled:
-        ev.reduce()
+        ev.reduce(gather=gather)
     out = ev.summarize()
     if with_loss:
         out["loss"] = validation_loss(pred.model, compiled, ctx, batch_size, shard)
@@ -304,6 +305,8 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
         else:
             from ..parallel.ddp import NcclGradSync
             grad_sync = NcclGradSync()
+    # evaluation's match-record all-gather: over peer memory when the fused NVSwitch sync is in use
+    gather = getattr(grad_sync, "all_gather_tensor", None)
     engine = TrainEngine(model, opts, ctx.device, grad_sync, max_targets=slots, steps_per_epoch=steps_per_epoch,
                          total_steps=total_steps)
     if ctx.device.type == "cuda":
@@ -381,14 +384,15 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
         t_val = time.monotonic()
         val = evaluate(regular, opts.val_compiled, ctx, val_bs, opts.eval_max_dets, masks,
                        with_loss=opts.validation_loss,
-                       sample_png=os.path.join(opts.output_dir, "eval_samples", f"epoch_{epoch:04d}.png"))
+                       sample_png=os.path.join(opts.output_dir, "eval_samples", f"epoch_{epoch:04d}.png"),
+                       gather=gather)
         _validation_record(opts, paths, ctx, epoch, "regular", val, time.monotonic() - t_val)
         ema_val = None
         ema_model = engine.export_model("ema") if opts.use_ema else None
         if ema_model is not None:
             t_val = time.monotonic()
             ema_val = evaluate(ema_model, opts.val_compiled, ctx, val_bs, opts.eval_max_dets, masks,
-                               with_loss=opts.validation_loss)
+                               with_loss=opts.validation_loss, gather=gather)
             _validation_record(opts, paths, ctx, epoch, "ema", ema_val, time.monotonic() - t_val)
         if ctx.main:
             state = regular.state_dict()
@@ -432,7 +436,8 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
     if opts.test_compiled:
         best = resolve_model(result["best_checkpoint"], preset=cfg.preset_name, num_classes=num_classes,
                              strict=False)[0]
-        result["test"] = _summary_json(evaluate(best, opts.test_compiled, ctx, val_bs, opts.eval_max_dets, masks))
+        result["test"] = _summary_json(evaluate(best, opts.test_compiled, ctx, val_bs, opts.eval_max_dets, masks,
+                                                gather=gather))
     if ctx.main:
         with open(paths["results"], "w") as f:
             json.dump(result, f, indent=1)

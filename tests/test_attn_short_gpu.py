@@ -13,6 +13,17 @@ from mmltk_b200.ops.attention import short_attention
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, params=[2, 1], ids=["fwd-pingpong", "fwd-row"])
+def fwd_variant(request):
+    """Every test runs with both forward kernels: the ping-pong warpgroups over 128-key chunks
+    (default) and the whole-score-row kernel."""
+    k = kernels()
+    old = k.attn_short_fwd_variant()
+    k.attn_short_set_fwd_variant(request.param)
+    yield request.param
+    k.attn_short_set_fwd_variant(old)
+
+
 def _oracle(q, k, v, go):
     """q/k/v/go fp32 [N, H, L, D] leaves -> (o, lse, dq, dk, dv)."""
     q, k, v = (t.detach().clone().requires_grad_() for t in (q, k, v))
@@ -99,3 +110,25 @@ def test_qkv_attention_takes_the_short_kernel_for_windows(cuda_device):
     assert any("ShortAttn" in n for n in fns), fns
     ref = qkv_attention_reference(qkv.detach().float(), H)
     _close(o, ref, 2e-2)
+
+
+@pytest.mark.parametrize("D", [32, 64])
+def test_short_attention_running_max_moves(cuda_device, D):
+    """Keys of the last 128-key chunk score far above the first chunk's, so the online softmax of the
+    ping-pong kernel must move its running maximum and rescale the partial output in tensor memory."""
+    torch.manual_seed(4)
+    N, L, H = 2, 300, 2
+    C = H * D
+    qkv = torch.randn(N * L, 3 * C, device=cuda_device)
+    kv = qkv.view(N, L, 3 * C)
+    kv[:, 256:, C:2 * C] *= 6.0        # k rows of the third chunk
+    qkv = qkv.bfloat16().requires_grad_()
+    o = short_attention(qkv, None, (0, C, 2 * C), N, L, H, D)
+    go = torch.randn_like(o)
+    o.backward(go)
+    assert kernels().attn_tc_status(torch.cuda.current_device()) == 0
+    q_, k_, v_ = (_heads(qkv, c, N, L, H, D) for c in (0, C, 2 * C))
+    ro, _, dq, dk, dv = _oracle(q_, k_, v_, _heads(go, 0, N, L, H, D))
+    _close(o.view(N, L, H, D).transpose(1, 2), ro, 2e-2)
+    for c, ref in zip((0, C, 2 * C), (dq, dk, dv)):
+        _close(_heads(qkv.grad, c, N, L, H, D), ref, 4e-2)

@@ -111,6 +111,12 @@ def test_fused_wait_times_out_into_status(cuda_device):
     comm.small_allreduce(data)
     torch.cuda.synchronize()
     assert int(ctrl[3]) == 4
+    ctrl[3] = 0
+    ctrl[4] = 1
+    out = torch.zeros(64, dtype=torch.uint8, device=cuda_device)
+    comm.gather_bytes(out, [0, 1], [1, 1])
+    torch.cuda.synchronize()
+    assert int(ctrl[3]) == 5  # the peer never staged its payload for the byte all-gather
 
 
 def _oracle_update(master, m, v, ema, grad_sum, elem_lr, elem_wd, sc):
@@ -192,6 +198,26 @@ def _gpu_ddp_worker(rank, world, port, backend, q):
         report.append(dict(step=step, loss=loss, update=upd, master_err=((after[0] - om).abs()).max().item(),
                            master_rel=rel(after[0], om), m_rel=rel(after[1], omm), v_rel=rel(after[2], ov),
                            ema_err=(after[3] - oema).abs().max().item(), param_ulps=ulps, ranks_equal=same))
+    if fused:
+        # evaluation-style byte all-gather over the gradient buffers (between steps), then one more
+        # step that must still match the oracle (the step clears the staged bytes first)
+        mine = torch.arange((rank + 3) * 5, dtype=torch.float64).view(-1, 5) + 1000 * rank
+        parts = sync.all_gather_tensor(mine)
+        gathered_ok = len(parts) == world and all(
+            torch.equal(parts[j], torch.arange((j + 3) * 5, dtype=torch.float64).view(-1, 5) + 1000 * j)
+            for j in range(world))
+        empty_ok = all(p.shape == (0, 5) for p in sync.all_gather_tensor(torch.zeros(0, 5, dtype=torch.float64)))
+        before = state()
+        loss = eng.step(imgs, tg).loss
+        after = state()
+        grads = [torch.zeros_like(eng.flat.grad_buf) for _ in range(world)]
+        dist.all_gather(grads, eng.flat.grad_buf)
+        om, _, _, _ = _oracle_update(*before, sum(g.float() for g in grads), elem_lr, elem_wd,
+                                     eng.scalars.float().cpu())
+        report.append(dict(step=4, loss=loss, update=(om - before[0]).abs().max().item(),
+                           master_err=((after[0] - om).abs()).max().item(),
+                           master_rel=((after[0] - om).abs() / (om.abs() + 1e-6)).max().item(), m_rel=0.0,
+                           v_rel=0.0, ema_err=0.0, param_ulps=0, ranks_equal=gathered_ok and empty_ok))
     q.put((rank, report))
     eng.release_graph()
     if fused:
