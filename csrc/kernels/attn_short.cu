@@ -530,19 +530,25 @@ __global__ void __launch_bounds__(pp::kThreadsPP, 1)
                 }
                 tc_fence_after();
                 if (live) {
-                    // 32 score columns in registers at a time: the row maximum over the chunk, then the
-                    // exponentials (the columns read again from tensor memory)
+                    // the row maximum over the chunk: 64 columns per tensor-memory round trip, four
+                    // independent running maxima; columns past the sequence only in the last chunk
                     const int kbase = c * kRows;
-                    float mc = -1e30f;
+                    const bool full = kbase + kRows <= L;   // warp-uniform
+                    float mx[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        float sv[32];
-                        tmem_ld32(tS + 32 * q4, sv);
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        float sv[64];
+                        tmem_ld64(tS + 64 * h2, sv);
+                        if (!full) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (kbase + 32 * q4 + i < L) mc = fmaxf(mc, sv[i]);
-                        asm volatile("" : "+f"(mc));
+                            for (int i = 0; i < 64; ++i)
+                                if (kbase + 64 * h2 + i >= L) sv[i] = -1e30f;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 64; ++i) mx[i & 3] = fmaxf(mx[i & 3], sv[i]);
+                        asm volatile("" : "+f"(mx[0]), "+f"(mx[1]), "+f"(mx[2]), "+f"(mx[3]));
                     }
+                    const float mc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
                     const float m_new = mc * a.scale_log2;
                     bool need = false;
                     float alpha = 1.f;
@@ -569,27 +575,34 @@ __global__ void __launch_bounds__(pp::kThreadsPP, 1)
                             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                         }
                     }
-                    float sum = 0.f;
+                    // exponentials: 2^(s * scale * log2 e - m) with the columns past the sequence at
+                    // -inf (2^-inf = 0), four independent partial sums, bf16 P into shared memory
+                    float sm4[4] = {0.f, 0.f, 0.f, 0.f};
+                    const float sl = a.scale_log2, mneg = -m_used;
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        float sv[32];
-                        tmem_ld32(tS + 32 * q4, sv);
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        float sv[64];
+                        tmem_ld64(tS + 64 * h2, sv);
+                        if (!full) {
 #pragma unroll
-                        for (int g8 = 0; g8 < 4; ++g8) {
+                            for (int i = 0; i < 64; ++i)
+                                if (kbase + 64 * h2 + i >= L) sv[i] = -__int_as_float(0x7f800000);
+                        }
+#pragma unroll
+                        for (int g8 = 0; g8 < 8; ++g8) {
                             uint32_t wv[4];
 #pragma unroll
                             for (int i = 0; i < 4; ++i) {
-                                const int c0 = 8 * g8 + 2 * i;
-                                const int key = kbase + 32 * q4 + c0;
-                                const float p0 = key < L ? ex2(sv[c0] * a.scale_log2 - m_used) : 0.f;
-                                const float p1 = key + 1 < L ? ex2(sv[c0 + 1] * a.scale_log2 - m_used) : 0.f;
-                                sum += p0 + p1;
+                                const float p0 = ex2(fmaf(sv[8 * g8 + 2 * i], sl, mneg));
+                                const float p1 = ex2(fmaf(sv[8 * g8 + 2 * i + 1], sl, mneg));
+                                sm4[i] += p0 + p1;
                                 wv[i] = pack_bf16x2(p0, p1);
                             }
-                            put8(myP, r, 32 * q4 + 8 * g8, wv);
+                            put8(myP, r, 64 * h2 + 8 * g8, wv);
                         }
-                        asm volatile("" : "+f"(sum)::"memory");
+                        asm volatile("" : "+f"(sm4[0]), "+f"(sm4[1]), "+f"(sm4[2]), "+f"(sm4[3])::"memory");
                     }
+                    const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
                     l += sum;
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -834,24 +847,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const int qc = 64 * half;                       // this half's query columns in the block
-                const float* l2 = s_lse2 + qt * kRows + qc;
-                const float* dl = s_delta + qt * kRows + qc;
-                float sv[64], dp[64];
-                tmem_ld64(tmem + cS + lane_off + qc, sv);
-                tmem_ld64(tmem + cDP + lane_off + qc, dp);
+                // 16-byte broadcast reads of the per-query log-sum-exp / delta; 32 columns of S^T and
+                // dP^T per tensor-memory round trip; the exponential is computed for every key row and
+                // zeroed after (no predicated MUFU work)
+                const float4* l2v = reinterpret_cast<const float4*>(s_lse2 + qt * kRows + qc);
+                const float4* dlv = reinterpret_cast<const float4*>(s_delta + qt * kRows + qc);
+                const float sl = a.scale_log2;
+                const float keep = kvalid ? 1.f : 0.f;
 #pragma unroll
-                for (int g = 0; g < 8; ++g) {
-                    uint32_t wp[4], wd[4];
+                for (int piece = 0; piece < 2; ++piece) {
+                    float sv[32], dp[32];
+                    tmem_ld32x2(tmem + cS + lane_off + qc + 32 * piece, tmem + cDP + lane_off + qc + 32 * piece, sv, dp);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int c = 8 * g + 2 * i;
-                        const float p0 = kvalid ? ex2(sv[c] * a.scale_log2 - l2[c]) : 0.f;
-                        const float p1 = kvalid ? ex2(sv[c + 1] * a.scale_log2 - l2[c + 1]) : 0.f;
-                        wp[i] = pack_bf16x2(p0, p1);
-                        wd[i] = pack_bf16x2(p0 * (dp[c] - dl[c]), p1 * (dp[c + 1] - dl[c + 1]));
+                    for (int g = 0; g < 4; ++g) {
+                        uint32_t wp[4], wd[4];
+                        const float4 la = l2v[8 * piece + 2 * g], lb = l2v[8 * piece + 2 * g + 1];
+                        const float4 da = dlv[8 * piece + 2 * g], db = dlv[8 * piece + 2 * g + 1];
+                        const float lv[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+                        const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int c = 8 * g + 2 * i;
+                            const float p0 = keep * ex2(fmaf(sv[c], sl, -lv[2 * i]));
+                            const float p1 = keep * ex2(fmaf(sv[c + 1], sl, -lv[2 * i + 1]));
+                            wp[i] = pack_bf16x2(p0, p1);
+                            wd[i] = pack_bf16x2(p0 * (dp[c] - dv[2 * i]), p1 * (dp[c + 1] - dv[2 * i + 1]));
+                        }
+                        put16(sPt + half * kBox, r, 4 * piece + g, make_uint4(wp[0], wp[1], wp[2], wp[3]));
+                        put16(sDSt + half * kBox, r, 4 * piece + g, make_uint4(wd[0], wd[1], wd[2], wd[3]));
                     }
-                    put16(sPt + half * kBox, r, g, make_uint4(wp[0], wp[1], wp[2], wp[3]));
-                    put16(sDSt + half * kBox, r, g, make_uint4(wd[0], wd[1], wd[2], wd[3]));
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 tc_fence_before();

@@ -9,10 +9,14 @@
 // (CUDA IPC mappings, 16-byte P2P loads and stores; no TMA, plain loads and
 // stores only):
 //
-//   ddp_rs_kernel      barrier "gradients ready" -> reduce-scatter: sum the
-//                      shard of every rank's bf16 gradient buffer in fp32
-//                      (fixed rank order) into a local fp32 shard, plus the
-//                      shard's sum of squares, published to every peer;
+//   ddp_rs_kernel      per gradient bucket (launched on a side stream as the
+//                      backward pass completes the bucket): barrier "bucket
+//                      ready" -> reduce-scatter: sum this rank's slice of the
+//                      bucket over every rank's bf16 gradient buffer in fp32
+//                      (fixed rank order) into the local fp32 shard, plus the
+//                      slice's sum of squares;
+//   ddp_publish_kernel after the last bucket: the shard's sum of squares to
+//                      every peer;
 //   ddp_update_kernel  wait for every rank's sum of squares -> global L2 norm
 //                      of the averaged gradient -> clip -> AdamW on the fp32
 //                      master shard -> EMA shard update -> all-gather: write
@@ -98,42 +102,57 @@ __device__ bool last_cta(unsigned int* ticket) {
     return is_last;
 }
 
-__global__ void __launch_bounds__(256) ddp_rs_kernel(DdpPeers peers, DdpState st, int64_t shard_off, int64_t shard_len,
-                                                     float* __restrict__ gshard, float* __restrict__ partials) {
-    const uint32_t epoch = *st.epoch;
+// Reduce-scatter of one gradient bucket: this rank's slice [g_off, g_off + len) of the flat gradient,
+// summed over every rank's buffer in rank order (fp32), into gshard_at; per-CTA sums of squares into
+// partials_b.  Starts with the bucket's barrier: mark = epoch * 32 + bucket + 1 is published to every
+// rank and awaited from every rank (marks only grow within and across steps).
+__global__ void __launch_bounds__(256) ddp_rs_kernel(DdpPeers peers, DdpState st, int64_t g_off, int64_t len,
+                                                     float* __restrict__ gshard_at, float* __restrict__ partials_b,
+                                                     int bucket) {
+    const uint32_t mark = *st.epoch * 32u + static_cast<uint32_t>(bucket) + 1u;
     const int world = peers.world, rank = peers.rank;
-    // ---- barrier: my gradients are complete; wait for everybody's
+    // ---- barrier: my gradients of this bucket are complete; wait for everybody's
     if (blockIdx.x == 0 && threadIdx.x < world) {
         __threadfence_system();
-        st_release_u32(peers.flags[threadIdx.x] + kFlagReady + rank, epoch);
+        st_release_u32(peers.flags[threadIdx.x] + kFlagReady + rank, mark);
     }
     __shared__ int ok;
     if (threadIdx.x == 0) ok = 1;
     __syncthreads();
     if (threadIdx.x < world) {
-        if (!wait_u32(st.flags_local + kFlagReady + threadIdx.x, epoch, st.spin_limit)) {
+        if (!wait_u32(st.flags_local + kFlagReady + threadIdx.x, mark, st.spin_limit)) {
             record_error(st.status, kErrTimeoutReady);
             ok = 0;
         }
     }
     __syncthreads();
-    if (!ok) return;
-    // ---- reduce-scatter of this rank's shard, fp32 accumulation in rank order
+    if (!ok) {
+        if (threadIdx.x == 0) partials_b[blockIdx.x] = 0.f;
+        return;
+    }
+    // ---- reduce: every peer's 16 bytes loaded before any is added (all loads in flight at once)
     float ss = 0.f;
-    const int64_t nvec = shard_len / 8;
-    for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
-         v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        const int64_t e = shard_off + 8 * v;
-        for (int j = 0; j < world; ++j) {
-            float f[8];
-            bf16x8_to_f32(ld_peer16(peers.grad[j] + e), f);
+    const int64_t nvec = len / 8;
+    for (int64_t vi = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; vi < nvec;
+         vi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t e = g_off + 8 * vi;
+        uint4 raw[kDdpMaxWorld];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) acc[c] += f[c];
+        for (int j = 0; j < kDdpMaxWorld; ++j)
+            if (j < world) raw[j] = ld_peer16(peers.grad[j] + e);
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < kDdpMaxWorld; ++j) {
+            if (j < world) {
+                float f[8];
+                bf16x8_to_f32(raw[j], f);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc[c] += f[c];
+            }
         }
 #pragma unroll
         for (int c = 0; c < 8; ++c) ss += acc[c] * acc[c];
-        store8(gshard + 8 * v, acc);
+        store8(gshard_at + 8 * vi, acc);
     }
     __shared__ float red[8];
     ss = warp_sum(ss);
@@ -142,26 +161,28 @@ __global__ void __launch_bounds__(256) ddp_rs_kernel(DdpPeers peers, DdpState st
     if (threadIdx.x == 0) {
         float t = 0.f;
         for (int w = 0; w < (blockDim.x >> 5); ++w) t += red[w];
-        partials[blockIdx.x] = t;
-    }
-    // ---- the last CTA publishes the shard's sum of squares to every rank
-    if (last_cta(st.ticket)) {
-        if (threadIdx.x < 32) {
-            float t = 0.f;
-            for (int i = threadIdx.x; i < static_cast<int>(gridDim.x); i += 32) t += partials[i];
-            t = warp_sum(t);
-            if (threadIdx.x < world) {
-                const unsigned long long packed =
-                    (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(t);
-                st_release_u64(reinterpret_cast<unsigned long long*>(peers.flags[threadIdx.x] + kFlagNorm) + rank,
-                               packed);
-            }
-        }
+        partials_b[blockIdx.x] = t;
     }
 }
 
-__global__ void __launch_bounds__(256) ddp_update_kernel(DdpPeers peers, DdpState st, int64_t shard_off,
-                                                         const ChunkDesc* __restrict__ chunks, int nchunks,
+// After the last bucket: this rank's sum of squares (all buckets' partials, fixed order) published to
+// every rank as (epoch << 32 | bits).
+__global__ void ddp_publish_kernel(DdpPeers peers, DdpState st, const float* __restrict__ partials, int n) {
+    const uint32_t epoch = *st.epoch;
+    float t = 0.f;
+    for (int i = threadIdx.x; i < n; i += 32) t += partials[i];
+    t = warp_sum(t);
+    if (threadIdx.x < peers.world) {
+        const unsigned long long packed = (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(t);
+        __threadfence_system();
+        st_release_u64(reinterpret_cast<unsigned long long*>(peers.flags[threadIdx.x] + kFlagNorm) + peers.rank,
+                       packed);
+    }
+}
+
+__global__ void __launch_bounds__(256) ddp_update_kernel(DdpPeers peers, DdpState st,
+                                                         const ChunkDesc* __restrict__ chunks,
+                                                         const int64_t* __restrict__ gdelta, int nchunks,
                                                          const float* __restrict__ gshard,
                                                          float* __restrict__ master, float* __restrict__ m,
                                                          float* __restrict__ v, float* __restrict__ ema,
@@ -219,7 +240,8 @@ __global__ void __launch_bounds__(256) ddp_update_kernel(DdpPeers peers, DdpStat
     const bool do_ema = ema != nullptr && sc->ema_enabled != 0.f;
     // ---- sharded AdamW + EMA, then all-gather of the bf16 parameters
     for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
-        const ChunkDesc cd = chunks[c];  // offsets are shard-local
+        const ChunkDesc cd = chunks[c];  // offsets are shard-local; + gdelta[c] = flat offset
+        const int64_t to_flat = gdelta[c];
         const GroupHyper gh = groups[cd.group];
         const float lr = gh.lr * sc->lr_scale;
         const float decay = 1.f - lr * gh.weight_decay;
@@ -266,7 +288,7 @@ __global__ void __launch_bounds__(256) ddp_update_kernel(DdpPeers peers, DdpStat
             // all-gather: the same 16 bytes to every rank's parameter buffer
             const uint4 raw = make_uint4(pack_bf16x2(p[0].x, p[0].y), pack_bf16x2(p[0].z, p[0].w),
                                          pack_bf16x2(p[1].x, p[1].y), pack_bf16x2(p[1].z, p[1].w));
-            for (int j = 0; j < world; ++j) *reinterpret_cast<uint4*>(peers.param[j] + shard_off + i) = raw;
+            for (int j = 0; j < world; ++j) *reinterpret_cast<uint4*>(peers.param[j] + to_flat + i) = raw;
         }
     }
     // ---- completion: once every CTA's stores are out, tell every rank, wait for all
@@ -373,21 +395,29 @@ cudaError_t launch_gather_bytes(const DdpPeers& peers, const DdpState& st, void*
     return cudaGetLastError();
 }
 
-int ddp_rs_blocks() { return num_sms() * 2; }
+int ddp_rs_blocks(bool overlapped) { return overlapped ? 64 : num_sms() * 2; }
 
-cudaError_t launch_ddp_rs(const DdpPeers& peers, const DdpState& st, int64_t shard_off, int64_t shard_len,
-                          float* gshard, float* partials, cudaStream_t s) {
-    if (shard_len % 8 != 0 || peers.world < 1 || peers.world > kDdpMaxWorld) return cudaErrorInvalidValue;
-    ddp_rs_kernel<<<ddp_rs_blocks(), 256, 0, s>>>(peers, st, shard_off, shard_len, gshard, partials);
+cudaError_t launch_ddp_rs(const DdpPeers& peers, const DdpState& st, int64_t g_off, int64_t len, float* gshard_at,
+                          float* partials_b, int bucket, int blocks, cudaStream_t s) {
+    if (len % 8 != 0 || g_off % 8 != 0 || peers.world < 1 || peers.world > kDdpMaxWorld || bucket < 0 ||
+        bucket >= kDdpMaxBuckets || blocks < 1)
+        return cudaErrorInvalidValue;
+    ddp_rs_kernel<<<blocks, 256, 0, s>>>(peers, st, g_off, len, gshard_at, partials_b, bucket);
     return cudaGetLastError();
 }
 
-cudaError_t launch_ddp_update(const DdpPeers& peers, const DdpState& st, int64_t shard_off, const ChunkDesc* chunks,
+cudaError_t launch_ddp_publish(const DdpPeers& peers, const DdpState& st, const float* partials, int n,
+                               cudaStream_t s) {
+    ddp_publish_kernel<<<1, 32, 0, s>>>(peers, st, partials, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ddp_update(const DdpPeers& peers, const DdpState& st, const ChunkDesc* chunks, const int64_t* gdelta,
                               int nchunks, const float* gshard, float* master, float* m, float* v, float* ema,
                               const GroupHyper* groups, const StepScalars* sc, int* flags, cudaStream_t s) {
     const int blocks = std::max(1, std::min(nchunks, num_sms() * 4));
-    ddp_update_kernel<<<blocks, 256, 0, s>>>(peers, st, shard_off, chunks, nchunks, gshard, master, m, v, ema, groups,
-                                             sc, flags);
+    ddp_update_kernel<<<blocks, 256, 0, s>>>(peers, st, chunks, gdelta, nchunks, gshard, master, m, v, ema, groups, sc,
+                                             flags);
     return cudaGetLastError();
 }
 

@@ -12,9 +12,10 @@ namespace mmltk {
 
 constexpr int kDdpMaxWorld = 16;
 constexpr int kSmallMax = 16;  // floats per rank in the small all-reduce
+constexpr int kDdpMaxBuckets = 31;  // gradient buckets per step (barrier marks are epoch * 32 + bucket + 1)
 
 // Flag words (uint32) inside each rank's peer-visible flag buffer.
-constexpr int kFlagReady = 0;                       // [world] gradients ready (epoch)
+constexpr int kFlagReady = 0;                       // [world] gradient bucket ready (epoch * 32 + bucket + 1)
 constexpr int kFlagDone = kFlagReady + kDdpMaxWorld;  // [world] parameters delivered (epoch)
 constexpr int kFlagSmall = kFlagDone + kDdpMaxWorld;  // [world] small all-reduce (epoch)
 constexpr int kFlagNorm = 64;                        // [world] u64 (epoch << 32 | sumsq bits), 8-byte aligned
@@ -51,10 +52,15 @@ struct DdpState {
     long long spin_limit;        // polls before a wait gives up
 };
 
-int ddp_rs_blocks();
-cudaError_t launch_ddp_rs(const DdpPeers& peers, const DdpState& st, int64_t shard_off, int64_t shard_len,
-                          float* gshard, float* partials, cudaStream_t s);
-cudaError_t launch_ddp_update(const DdpPeers& peers, const DdpState& st, int64_t shard_off, const ChunkDesc* chunks,
+// CTAs of one bucket's reduce-scatter: few when it overlaps the backward pass on a side stream, two
+// waves when it runs alone after it.
+int ddp_rs_blocks(bool overlapped);
+cudaError_t launch_ddp_rs(const DdpPeers& peers, const DdpState& st, int64_t g_off, int64_t len, float* gshard_at,
+                          float* partials_b, int bucket, int blocks, cudaStream_t s);
+cudaError_t launch_ddp_publish(const DdpPeers& peers, const DdpState& st, const float* partials, int n,
+                               cudaStream_t s);
+// chunks: (shard-local offset, length, group); gdelta[c]: flat offset - shard-local offset of chunk c
+cudaError_t launch_ddp_update(const DdpPeers& peers, const DdpState& st, const ChunkDesc* chunks, const int64_t* gdelta,
                               int nchunks, const float* gshard, float* master, float* m, float* v, float* ema,
                               const GroupHyper* groups, const StepScalars* sc, int* flags, cudaStream_t s);
 cudaError_t launch_small_allreduce(const DdpPeers& peers, const DdpState& st, float* data, int n, cudaStream_t s);

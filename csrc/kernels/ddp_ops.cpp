@@ -79,21 +79,36 @@ class DdpComm {
         st_.spin_limit = spin_limit;
     }
 
-    void rs(int64_t off, int64_t len, torch::Tensor gshard, torch::Tensor partials) {
-        TORCH_CHECK(gshard.scalar_type() == torch::kFloat32 && gshard.numel() >= len, "ddp rs: gshard");
-        TORCH_CHECK(partials.numel() >= ddp_rs_blocks(), "ddp rs: partials");
-        check_cuda(launch_ddp_rs(peers_, st_, off, len, gshard.data_ptr<float>(), partials.data_ptr<float>(),
+    // reduce-scatter of bucket `bucket`: this rank's slice [g_off, g_off + len) of the flat gradient into
+    // gshard[l_off, l_off + len), per-CTA sums of squares into partials[p_off, p_off + blocks)
+    void rs(int64_t g_off, int64_t len, torch::Tensor gshard, int64_t l_off, torch::Tensor partials, int64_t p_off,
+            int64_t bucket, int64_t blocks) {
+        TORCH_CHECK(gshard.scalar_type() == torch::kFloat32 && l_off >= 0 && gshard.numel() >= l_off + len,
+                    "ddp rs: gshard");
+        TORCH_CHECK(partials.scalar_type() == torch::kFloat32 && p_off >= 0 && partials.numel() >= p_off + blocks,
+                    "ddp rs: partials");
+        check_cuda(launch_ddp_rs(peers_, st_, g_off, len, gshard.data_ptr<float>() + l_off,
+                                 partials.data_ptr<float>() + p_off, static_cast<int>(bucket), static_cast<int>(blocks),
                                  cur_stream()),
                    "ddp_rs");
     }
 
-    void update(int64_t off, torch::Tensor chunks, torch::Tensor gshard, torch::Tensor master, torch::Tensor m,
-                torch::Tensor v, c10::optional<torch::Tensor> ema, torch::Tensor groups, torch::Tensor scalars,
-                torch::Tensor flags) {
+    void publish(torch::Tensor partials, int64_t n) {
+        TORCH_CHECK(partials.scalar_type() == torch::kFloat32 && partials.numel() >= n, "ddp publish: partials");
+        check_cuda(launch_ddp_publish(peers_, st_, partials.data_ptr<float>(), static_cast<int>(n), cur_stream()),
+                   "ddp_publish");
+    }
+
+    void update(torch::Tensor chunks, torch::Tensor gdelta, torch::Tensor gshard, torch::Tensor master,
+                torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> ema, torch::Tensor groups,
+                torch::Tensor scalars, torch::Tensor flags) {
         TORCH_CHECK(chunks.scalar_type() == torch::kInt64 && chunks.is_cuda() && chunks.dim() == 2, "ddp: chunks");
+        TORCH_CHECK(gdelta.scalar_type() == torch::kInt64 && gdelta.is_cuda() && gdelta.numel() == chunks.size(0),
+                    "ddp: one flat-offset delta per chunk");
         TORCH_CHECK(scalars.numel() >= kStepScalarFloats, "ddp: scalars");
-        check_cuda(launch_ddp_update(peers_, st_, off, reinterpret_cast<const ChunkDesc*>(chunks.data_ptr<int64_t>()),
-                                     static_cast<int>(chunks.size(0)), gshard.data_ptr<float>(),
+        check_cuda(launch_ddp_update(peers_, st_, reinterpret_cast<const ChunkDesc*>(chunks.data_ptr<int64_t>()),
+                                     gdelta.data_ptr<int64_t>(), static_cast<int>(chunks.size(0)),
+                                     gshard.data_ptr<float>(),
                                      master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
                                      ema.has_value() ? ema->data_ptr<float>() : nullptr,
                                      reinterpret_cast<const GroupHyper*>(groups.data_ptr<float>()),
@@ -136,13 +151,15 @@ void register_ddp_ops(pybind11::module& m) {
     m.def("ipc_alloc", &ipc_alloc);
     m.def("ipc_open", &ipc_open);
     m.def("ipc_close", &ipc_close);
-    m.def("ddp_rs_blocks", &ddp_rs_blocks);
+    m.def("ddp_rs_blocks", &ddp_rs_blocks, py::arg("overlapped") = false);
+    m.def("ddp_max_buckets", [] { return kDdpMaxBuckets; });
     m.def("ddp_flag_words", [] { return kFlagWords; });
     m.def("ddp_small_floats", [] { return 2 * kDdpMaxWorld * kSmallMax; });
     py::class_<DdpComm>(m, "DdpComm")
         .def(py::init<std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t,
                       int64_t, torch::Tensor, torch::Tensor, torch::Tensor, int64_t>())
         .def("rs", &DdpComm::rs)
+        .def("publish", &DdpComm::publish)
         .def("update", &DdpComm::update)
         .def("small_allreduce", &DdpComm::small_allreduce)
         .def("gather_bytes", &DdpComm::gather_bytes);

@@ -122,6 +122,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 columns from each of two accumulators (e.g. S and dP) of this thread's row: four loads, one wait.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, float* a, float* b) {
+    uint32_t r[64];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(r[16 * c + 0]), "=r"(r[16 * c + 1]), "=r"(r[16 * c + 2]), "=r"(r[16 * c + 3]), "=r"(r[16 * c + 4]),
+              "=r"(r[16 * c + 5]), "=r"(r[16 * c + 6]), "=r"(r[16 * c + 7]), "=r"(r[16 * c + 8]), "=r"(r[16 * c + 9]),
+              "=r"(r[16 * c + 10]), "=r"(r[16 * c + 11]), "=r"(r[16 * c + 12]), "=r"(r[16 * c + 13]),
+              "=r"(r[16 * c + 14]), "=r"(r[16 * c + 15])
+            : "r"((c < 2 ? ta : tb) + 16 * (c & 1)));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        a[i] = __uint_as_float(r[i]);
+        b[i] = __uint_as_float(r[32 + i]);
+    }
+}
+
 // 64 consecutive accumulator columns of this thread's row: four loads, one wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
     uint32_t r[64];

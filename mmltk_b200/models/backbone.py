@@ -23,6 +23,8 @@ separate ``query``/``key``/``value`` tensors through state-dict hooks.
 """
 from __future__ import annotations
 
+import re
+
 import math
 import os
 from typing import List
@@ -229,6 +231,7 @@ class WindowedDinov2(nn.Module):
         self.encoder = Encoder(cfg)
         self.layernorm = nn.LayerNorm(cfg.vit_width, eps=1e-6)
         self.taps = tuple(cfg.out_feature_indexes)
+        self.grad_marks = None     # callable(i) run by GradMark's backward (data-parallel buckets)
 
     def forward(self, pixels: torch.Tensor) -> List[torch.Tensor]:
         """Returns the tapped feature maps, channels-last [B, h, w, C]."""
@@ -238,7 +241,10 @@ class WindowedDinov2(nn.Module):
         states = {}
         full_stages = set(self.taps)
         if torch.is_grad_enabled() or not _FUSED_RESIDUAL_INFERENCE:
+            marks = self.grad_marks if torch.is_grad_enabled() else None
             for i, layer in enumerate(self.encoder.layer):
+                if marks is not None:
+                    x = GradMark.apply(x, i, marks)
                 if i in full_stages:
                     states[i] = x
                 x = layer(x, i in full_stages)
@@ -268,6 +274,34 @@ class WindowedDinov2(nn.Module):
                 h = h.reshape(B, nw, nw, hpw, wpw, C).permute(0, 1, 3, 2, 4, 5)
             feats.append(h.reshape(B, hp, wp, C))
         return feats
+
+
+class GradMark(torch.autograd.Function):
+    """Identity whose backward calls ``cb(i)`` when the gradient reaches the input of ViT layer
+    ``i``: by then the backward pass has produced every gradient of layers i.. and of everything
+    after the backbone (the data-parallel sync starts reducing those while the pass goes on)."""
+
+    @staticmethod
+    def forward(ctx, x, i, cb):
+        ctx.i, ctx.cb = i, cb
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        ctx.cb(ctx.i)
+        return g, None, None
+
+
+def grad_stage(name: str) -> int:
+    """Backward-completion stage of a parameter (larger = complete earlier): 0 for the patch /
+    position embeddings, 1 + i for ViT layer i, a large value for everything after the ViT
+    (final encoder norm, projector, transformer, heads)."""
+    if ".encoder.embeddings." in name:
+        return 0
+    m = re.search(r"\.encoder\.layer\.(\d+)\.", name)
+    if m:
+        return 1 + int(m.group(1))
+    return 1 << 20
 
 
 class DinoV2Wrapper(nn.Module):

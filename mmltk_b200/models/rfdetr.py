@@ -94,6 +94,22 @@ class RFDETR(nn.Module):
             self.bbox_embed.layers[-1].weight.zero_()
             self.bbox_embed.layers[-1].bias.zero_()
 
+    # ------------------------------------------------------------------ data-parallel buckets
+    @staticmethod
+    def grad_stage(name: str) -> int:
+        """Backward-completion stage of a parameter (see ``backbone.grad_stage``)."""
+        from .backbone import grad_stage
+        return grad_stage(name)
+
+    def grad_mark_count(self) -> int:
+        """Number of gradient marks one backward pass raises (one per ViT layer input)."""
+        return len(self.backbone[0].encoder.encoder.encoder.layer)
+
+    def set_grad_marks(self, cb) -> None:
+        """``cb(i)`` is called during backward when the gradient reaches ViT layer i's input
+        (None: no marks)."""
+        self.backbone[0].encoder.encoder.grad_marks = cb
+
     # ------------------------------------------------------------------ forward
     def forward(self, pixels: torch.Tensor, include_masks: bool = True) -> Dict:
         cfg = self.cfg

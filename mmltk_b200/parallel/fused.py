@@ -1,17 +1,21 @@
 """Fused in-kernel data-parallel gradient step over NVSwitch peer memory.
 
-Per step (two kernels, replayed from the engine's CUDA graph):
+Per step (kernels replayed from the engine's CUDA graph):
 
-1. ``rs``: barrier on "gradients ready", then every rank reduces ITS shard of
-   the flat bf16 gradient buffer by reading that shard from every peer's buffer
-   over NVLink (16-byte P2P loads, fp32 accumulation in rank order) and
-   publishes the shard's sum of squares to every rank;
-2. ``update``: every rank combines the N sums of squares into the global norm
-   of the averaged gradient (same value on every rank), clips, runs AdamW on
-   its fp32 master shard (ZeRO-1: moments and master weights are sharded),
-   updates its EMA shard and writes the new bf16 parameters straight into
-   every peer's parameter buffer (P2P stores = all-gather), then waits until
-   every peer has delivered its shard.
+1. ``rs`` per gradient bucket: the flat gradient buffer is laid out in backward-completion order
+   (``FlatParams(stage=...)``), so each bucket is one contiguous range.  When the backward pass
+   reaches a ViT layer's input (``GradMark``), the bucket it completed is reduce-scattered on a
+   side stream while the pass goes on: a barrier on "bucket ready", then every rank sums ITS slice
+   of the bucket over every peer's buffer over NVLink (16-byte P2P loads, all peers' loads in
+   flight at once, fp32 accumulation in rank order) into its fp32 shard, plus the slice's sum of
+   squares.  The last bucket (patch / position embeddings and whatever no mark covered) runs after
+   the backward pass;
+2. ``publish``: the shard's sum of squares to every rank;
+3. ``update``: every rank combines the N sums of squares into the global norm of the averaged
+   gradient (same value on every rank), clips, runs AdamW on its fp32 master shard (ZeRO-1:
+   moments and master weights are sharded), updates its EMA shard and writes the new bf16
+   parameters straight into every peer's parameter buffer (16-byte P2P stores = all-gather),
+   then waits until every peer has delivered its shard.
 
 The reference instead all-reduces every fp32 gradient with NCCL after the
 whole backward and runs a replicated optimizer on every rank
@@ -26,14 +30,14 @@ arrives makes its peers' kernels return with a non-zero status that
 """
 from __future__ import annotations
 
-from typing import List, Optional
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
 
 from ..ops._ext import kernels
 
-__all__ = ["FusedGradSync", "shard_chunks"]
+__all__ = ["FusedGradSync", "shard_chunks", "plan_buckets", "rank_slices"]
 
 ERRORS = {1: "a peer never signalled 'gradients ready'", 2: "a peer never published its gradient norm",
           3: "a peer never delivered its parameter shard", 4: "a peer never joined the small all-reduce",
@@ -52,18 +56,54 @@ def shard_chunks(chunks: torch.Tensor, off: int, size: int) -> torch.Tensor:
     return torch.tensor(rows, dtype=torch.int64)
 
 
+def plan_buckets(total: int, mark_bounds: List[int], min_elems: int) -> List[Tuple[Optional[int], int, int]]:
+    """Buckets of a flat buffer laid out in backward-completion order (complete from the end).
+
+    ``mark_bounds[i]``: flat offset from which every gradient is complete when backward reaches
+    mark i (non-increasing in firing order, marks fire as i = len - 1 .. 0).  Returns
+    [(mark or None, start, end)] in firing order; consecutive marks are merged until a bucket
+    holds ``min_elems``; the last bucket (mark None) runs after the backward pass."""
+    out: List[Tuple[Optional[int], int, int]] = []
+    end = total
+    for i in range(len(mark_bounds) - 1, -1, -1):
+        b = mark_bounds[i]
+        if end - b >= min_elems and len(out) < 30:
+            out.append((i, b, end))
+            end = b
+    out.append((None, 0, end))
+    return [t for t in out if t[2] > t[1]] or [(None, 0, total)]
+
+
+def rank_slices(buckets: Sequence[Tuple[Optional[int], int, int]], world: int, rank: int) -> List[Tuple[int, int]]:
+    """This rank's [a, b) of every bucket: the bucket cut into ``world`` 64-element-aligned parts."""
+    out = []
+    for _, s0, s1 in buckets:
+        units = (s1 - s0) // 64
+        a = s0 + (units * rank // world) * 64
+        b = s0 + (units * (rank + 1) // world) * 64 if rank + 1 < world else s1
+        out.append((a, b))
+    return out
+
+
 class FusedGradSync:
-    def __init__(self, group=None, spin_limit: int = 1 << 26):
+    # the flat buffer is laid out by backward-completion stage (the engine asks the model for it)
+    bucketed = True
+
+    def __init__(self, group=None, spin_limit: int = 1 << 26, overlap: bool = True, min_bucket: int = 4 << 20):
         self.group = group
         self.world_size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.pad_multiple = self.world_size * 64
         self.spin_limit = int(spin_limit)
         self.device = torch.device("cuda", torch.cuda.current_device())
+        self.overlap = overlap
+        self.min_bucket = int(min_bucket)
         self._handles: List[bytes] = []
         self._keep = []
         self._opened: List[int] = []
         self.failed: Optional[str] = None
+        self._armed = False
+        self._next = 0
 
     # ---------------------------------------------------------------- buffers
     def alloc(self, numel: int, dtype) -> torch.Tensor:
@@ -101,18 +141,53 @@ class FusedGradSync:
         # identical starting point on every rank
         dist.broadcast(engine.flat.param_buf, 0, group=self.group)
         dist.broadcast(engine.master, 0, group=self.group)
-        P = engine.flat.total
-        S = P // self.world_size
-        self.off, self.size = self.rank * S, S
-        engine.master_shard = engine.master[self.off:self.off + S].clone()
+        flat = engine.flat
+        P = flat.total
+        # buckets: the backward pass completes the flat buffer from its end (stage order); mark i
+        # (ViT layer i's input) completes everything from the first parameter of layer i on
+        model = engine.model
+        marks = model.grad_mark_count() if (self.overlap and hasattr(model, "set_grad_marks")) else 0
+        bounds = []
+        for i in range(marks):
+            starts = [o for o, n in zip(flat.offsets, flat.names) if model.grad_stage(n) >= i + 1]
+            bounds.append(min(starts) if starts else P)
+        self.buckets = plan_buckets(P, bounds, self.min_bucket)
+        self.slices_of = [rank_slices(self.buckets, self.world_size, r) for r in range(self.world_size)]
+        self.slices = self.slices_of[self.rank]
+        self.local_off = []
+        S = 0
+        for a, b in self.slices:
+            self.local_off.append(S)
+            S += b - a
+        self.size = S
+        self.mark_bucket = {m: j for j, (m, _, _) in enumerate(self.buckets) if m is not None}
+        master = engine.master
+        engine.master_shard = torch.cat([master[a:b] for a, b in self.slices]).contiguous()
         engine.master = None  # the full fp32 copy is only kept as shards
         engine.m = torch.zeros(S, dtype=torch.float32, device=dev)
         engine.v = torch.zeros(S, dtype=torch.float32, device=dev)
         engine.ema_buf = engine.master_shard.clone() if engine.opts.use_ema else None
         self.gshard = torch.zeros(S, dtype=torch.float32, device=dev)
-        self.partials = torch.zeros(k.ddp_rs_blocks(), dtype=torch.float32, device=dev)
-        self.chunks = shard_chunks(engine.flat.chunk_table(), self.off, S).to(dev)
-        self._stage = engine.flat.grad_buf.view(torch.uint8)   # byte all-gather staging (between steps)
+        # reduce-scatter CTAs per bucket: few for the ones that overlap the backward pass
+        self.blocks = [k.ddp_rs_blocks(m is not None) for (m, _, _) in self.buckets]
+        self.p_off = [sum(self.blocks[:j]) for j in range(len(self.buckets))]
+        self.partials = torch.zeros(sum(self.blocks), dtype=torch.float32, device=dev)
+        table = flat.chunk_table()
+        rows, deltas = [], []
+        for (a, b), lo in zip(self.slices, self.local_off):
+            part = shard_chunks(table, a, b - a)
+            for o, n, g in part.tolist():
+                if n:
+                    rows.append((lo + o, n, g))
+                    deltas.append(a - lo)
+        if not rows:
+            rows, deltas = [(0, 0, 0)], [0]
+        self.chunks = torch.tensor(rows, dtype=torch.int64, device=dev)
+        self.gdelta = torch.tensor(deltas, dtype=torch.int64, device=dev)
+        self._stage = flat.grad_buf.view(torch.uint8)   # byte all-gather staging (between steps)
+        self.side = torch.cuda.Stream(dev)
+        if marks:
+            model.set_grad_marks(self._on_mark)
         dist.barrier(group=self.group)
 
     # ---------------------------------------------------------------- step
@@ -121,12 +196,41 @@ class FusedGradSync:
         self.comm.small_allreduce(t)
         return t
 
+    def arm(self) -> None:
+        """The next backward pass is the optimizer step's last: its marks launch the buckets."""
+        self._armed = True
+        self._next = 0
+
+    def _launch(self, j: int, stream) -> None:
+        a, b = self.slices[j]
+        with torch.cuda.stream(stream):
+            self.comm.rs(a, b - a, self.gshard, self.local_off[j], self.partials, self.p_off[j], j, self.blocks[j])
+
+    def _on_mark(self, i: int) -> None:
+        """Backward reached ViT layer i's input: reduce the bucket it completed on the side stream
+        (ordered after everything the main stream has issued so far)."""
+        j = self.mark_bucket.get(i)
+        if not self._armed or j is None or j != self._next:
+            return
+        cur = torch.cuda.current_stream(self.device)
+        self.side.wait_stream(cur)
+        self._launch(j, self.side)
+        self._next = j + 1
+
     def step(self, engine) -> None:
         if self.failed is not None:
             raise RuntimeError(f"fused DDP gradient step is unusable after an earlier failure: {self.failed}")
-        self.comm.rs(self.off, self.size, self.gshard, self.partials)
-        self.comm.update(self.off, self.chunks, self.gshard, engine.master_shard, engine.m, engine.v, engine.ema_buf,
-                         engine.group_hyper, engine.scalars, engine.flags)
+        cur = torch.cuda.current_stream(self.device)
+        launched = self._next if self._armed else 0
+        for j in range(launched, len(self.buckets)):      # the rest (at least the last bucket)
+            self._launch(j, cur)
+        if launched:
+            cur.wait_stream(self.side)
+        self._armed = False
+        self._next = 0
+        self.comm.publish(self.partials, self.partials.numel())
+        self.comm.update(self.chunks, self.gdelta, self.gshard, engine.master_shard, engine.m, engine.v,
+                         engine.ema_buf, engine.group_hyper, engine.scalars, engine.flags)
 
     def after_step(self, engine) -> None:
         pass
@@ -183,9 +287,25 @@ class FusedGradSync:
         return parts
 
     # ---------------------------------------------------------------- state
+    def shard_of(self, full: torch.Tensor) -> torch.Tensor:
+        """This rank's shard (its slice of every bucket, in bucket order) of a full flat vector."""
+        return torch.cat([full[a:b] for a, b in self.slices])
+
     def gather_full(self, shard: torch.Tensor) -> torch.Tensor:
-        out = torch.empty(shard.numel() * self.world_size, dtype=shard.dtype, device=shard.device)
-        dist.all_gather_into_tensor(out, shard.contiguous(), group=self.group)
+        """The full flat vector from every rank's shard (each rank holds its slice of every bucket)."""
+        sizes = [sum(b - a for a, b in sl) for sl in self.slices_of]
+        cap = max(sizes)
+        mine = torch.zeros(cap, dtype=shard.dtype, device=shard.device)
+        mine[:shard.numel()].copy_(shard)
+        allp = torch.empty(cap * self.world_size, dtype=shard.dtype, device=shard.device)
+        dist.all_gather_into_tensor(allp, mine, group=self.group)
+        total = max(b for sl in self.slices_of for _, b in sl)
+        out = torch.zeros(total, dtype=shard.dtype, device=shard.device)
+        for r, sl in enumerate(self.slices_of):
+            lo = r * cap
+            for a, b in sl:
+                out[a:b].copy_(allp[lo:lo + (b - a)])
+                lo += b - a
         return out
 
     def gather_ema(self, engine) -> Optional[torch.Tensor]:

@@ -130,7 +130,10 @@ class TrainEngine:
         self.model.to(self.device, torch.bfloat16)
         named_dev = [(n, p) for n, p in self.model.named_parameters() if p.requires_grad]
         alloc = getattr(self.grad_sync, "alloc", None) if self.grad_sync is not None else None
-        self.flat = FlatParams(named_dev, assign, self.device, torch.bfloat16, pad_to=pad, alloc=alloc)
+        # a bucketed gradient sync wants the flat layout in backward-completion order
+        stage = (getattr(self.model, "grad_stage", None)
+                 if getattr(self.grad_sync, "bucketed", False) and self.opts.optimizer != "muon" else None)
+        self.flat = FlatParams(named_dev, assign, self.device, torch.bfloat16, pad_to=pad, alloc=alloc, stage=stage)
         master = torch.zeros(self.flat.total, dtype=torch.float32, device=self.device)
         for i, n in enumerate(self.flat.names):
             o, c = self.flat.offsets[i], self.flat.numels[i]
@@ -201,6 +204,8 @@ class TrainEngine:
             self.flags.zero_()
             self.flat.zero_grad()
         total, losses = self._forward_loss(images, targets)
+        if last and self.muon is None and hasattr(self.grad_sync, "arm"):
+            self.grad_sync.arm()     # this backward's gradient marks start the bucket reduce-scatters
         (total / self.accum if self.accum > 1 else total).backward()
         if not last:
             return total.detach(), {k: v.detach() for k, v in losses.items()}
@@ -415,6 +420,8 @@ class TrainEngine:
         if first:
             self.optimizer.zero_grad(set_to_none=True)
         total, losses = self._forward_loss(images, targets)
+        if last and self.muon is None and hasattr(self.grad_sync, "arm"):
+            self.grad_sync.arm()     # this backward's gradient marks start the bucket reduce-scatters
         (total / self.accum if self.accum > 1 else total).backward()
         if not last:
             return StepResult(float(total.detach()),{k: v.detach() for k, v in losses.items()}, None, 0)
@@ -533,9 +540,8 @@ class TrainEngine:
             full_v[o:o + c] = e["exp_avg_sq"].reshape(-1)
         sharded = getattr(self, "master_shard", None) is not None and self.master is None
         if sharded:
-            off, size = self.grad_sync.off, self.grad_sync.size
-            self.m.copy_(full_m[off:off + size])
-            self.v.copy_(full_v[off:off + size])
+            self.m.copy_(self.grad_sync.shard_of(full_m))
+            self.v.copy_(self.grad_sync.shard_of(full_v))
         else:
             self.m.copy_(full_m)
             self.v.copy_(full_v)
@@ -559,6 +565,6 @@ class TrainEngine:
                 full[o:o + c] = state[n].reshape(-1).float()
         sharded = getattr(self, "master_shard", None) is not None and self.master is None
         if sharded:
-            self.ema_buf.copy_(full[self.grad_sync.off:self.grad_sync.off + self.grad_sync.size])
+            self.ema_buf.copy_(self.grad_sync.shard_of(full))
         else:
             self.ema_buf.copy_(full)

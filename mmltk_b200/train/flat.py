@@ -28,9 +28,14 @@ def _round(n: int, a: int = ALIGN) -> int:
 
 class FlatParams:
     def __init__(self, named_params: Sequence[Tuple[str, torch.nn.Parameter]], group_of: Sequence[int],
-                 device, dtype=torch.bfloat16, pad_to: int = 1, alloc=None):
-        # order parameters by group so every group is one contiguous range
-        order = sorted(range(len(named_params)), key=lambda i: (group_of[i], i))
+                 device, dtype=torch.bfloat16, pad_to: int = 1, alloc=None, stage=None):
+        # order parameters by group so every group is one contiguous range; with ``stage(name)``
+        # (backward-completion stage, larger = complete earlier) by stage first, so the gradients
+        # the backward pass completes together are one contiguous range (a data-parallel bucket)
+        if stage is None:
+            order = sorted(range(len(named_params)), key=lambda i: (group_of[i], i))
+        else:
+            order = sorted(range(len(named_params)), key=lambda i: (stage(named_params[i][0]), group_of[i], i))
         self.names: List[str] = []
         self.params: List[torch.nn.Parameter] = []
         self.offsets: List[int] = []

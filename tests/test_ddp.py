@@ -67,6 +67,41 @@ def _cpu_ddp_worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
+def test_bucket_plan_and_rank_slices_cover_each_element_once():
+    """Buckets of a backward-ordered flat buffer tile it exactly, fire from its end, and every
+    rank's 64-aligned slices of them tile each bucket exactly (any world size)."""
+    from mmltk_b200.parallel.fused import plan_buckets, rank_slices
+    total = 1000 * 64
+    bounds = [640 + 64 * 50 * i for i in range(12)]           # mark i completes [bounds[i], total)
+    buckets = plan_buckets(total, bounds, 64 * 120)
+    assert buckets[0][2] == total and buckets[-1][0] is None and buckets[-1][1] == 0
+    for (m0, a0, b0), (m1, a1, b1) in zip(buckets, buckets[1:]):
+        assert a0 == b1                                          # contiguous, firing towards the start
+        assert m1 is None or m1 < m0
+    for world in (1, 2, 3, 8):
+        cover = sorted(x for r in range(world) for x in rank_slices(buckets, world, r))
+        pos = 0
+        for a, b in cover:
+            assert a == pos and a % 64 == 0
+            pos = b
+        assert pos == total
+
+
+def test_flat_layout_follows_backward_stages():
+    """With a stage function the flat buffer holds later-completing (earlier) stages first, so the
+    gradients one ViT layer completes are contiguous."""
+    from mmltk_b200.config import config_from_preset
+    from mmltk_b200.models import RFDETR
+    from mmltk_b200.train.flat import FlatParams
+    m = RFDETR(config_from_preset("rf-detr-nano"))
+    named = [(n, p) for n, p in m.named_parameters()]
+    flat = FlatParams(named, [0] * len(named), "cpu", torch.float32, stage=m.grad_stage)
+    stages = [m.grad_stage(n) for n in flat.names]
+    assert stages == sorted(stages)
+    assert flat.offsets == sorted(flat.offsets)
+    assert m.grad_mark_count() == len(m.backbone[0].encoder.encoder.encoder.layer)
+
+
 def test_cpu_gloo_ddp_keeps_ranks_identical():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -100,12 +135,13 @@ def test_fused_wait_times_out_into_status(cuda_device):
                      [flags.data_ptr(), fake_flags.data_ptr()], [small.data_ptr(), fake_small.data_ptr()],
                      0, 2, flags.view(torch.int32), small.view(torch.float32), ctrl, 2000)
     gshard = torch.zeros(n // 2, device=cuda_device)
-    partials = torch.zeros(k.ddp_rs_blocks(), device=cuda_device)
-    comm.rs(0, n // 2, gshard, partials)
+    blocks = k.ddp_rs_blocks(True)
+    partials = torch.zeros(blocks, device=cuda_device)
+    comm.rs(0, n // 2, gshard, 0, partials, 0, 0, blocks)       # bucket 0 of step epoch 1
     torch.cuda.synchronize()
-    assert int(ctrl[3]) == 1  # timed out waiting for 'gradients ready'
-    # our own 'ready' flag was delivered to the fake peer
-    assert int(fake_flags.view(torch.int32)[0]) == 1
+    assert int(ctrl[3]) == 1  # timed out waiting for 'bucket ready'
+    # our own 'bucket ready' mark (epoch * 32 + bucket + 1) was delivered to the fake peer
+    assert int(fake_flags.view(torch.int32)[0]) == 33
     ctrl[3] = 0
     data = torch.ones(3, device=cuda_device)
     comm.small_allreduce(data)
