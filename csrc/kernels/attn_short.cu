@@ -493,8 +493,10 @@ __global__ void __launch_bounds__(pp::kThreadsPP, 1)
                         tc_fence_after();
                     }
                     const uint32_t p = pb + w * 2 * kBox;
-#pragma unroll
-                    for (int s16 = 0; s16 < kRows / 16; ++s16)
+                    // K slices of 16 keys that hold a key of the sequence (the last chunk's P is only
+                    // written that far)
+                    const int nks = min(kRows / 16, (L - c * kRows + 15) / 16);
+                    for (int s16 = 0; s16 < nks; ++s16)
                         tc_mma(tmem + w * kRegion + 128, smem_desc(p + (s16 >> 2) * kBox + (s16 & 3) * 32, 16, 1024),
                                smem_desc(vb + c * kBox + s16 * 2048, 8192, 1024), idesc_o, (c > 0 || s16 > 0));
                     if (c == T - 1) tc_commit(&ctl->o_full[w]);
@@ -537,6 +539,7 @@ __global__ void __launch_bounds__(pp::kThreadsPP, 1)
                     float mx[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
 #pragma unroll
                     for (int h2 = 0; h2 < 2; ++h2) {
+                        if (kbase + 64 * h2 >= L) break;   // no key of this half (warp-uniform)
                         float sv[64];
                         tmem_ld64(tS + 64 * h2, sv);
                         if (!full) {
@@ -581,6 +584,9 @@ __global__ void __launch_bounds__(pp::kThreadsPP, 1)
                     const float sl = a.scale_log2, mneg = -m_used;
 #pragma unroll
                     for (int h2 = 0; h2 < 2; ++h2) {
+                        // a half with no key is neither exponentiated nor read by P.V (its K slices
+                        // are not issued)
+                        if (kbase + 64 * h2 >= L) break;
                         float sv[64];
                         tmem_ld64(tS + 64 * h2, sv);
                         if (!full) {

@@ -2,7 +2,7 @@
 //
 //   * mbarriers with transaction counts and BOUNDED waits (a wait that gives up returns false,
 //     so a kernel can record an error and leave instead of spinning forever);
-//   * 2-D TMA tile loads (no multicast);
+//   * 2-D TMA tile loads, each CTA loading its own tiles;
 //   * tcgen05.mma kind::f16 (bf16 x bf16 -> fp32 in tensor memory), commit to an mbarrier,
 //     shared-memory matrix descriptors for 128-byte swizzled tiles, tcgen05.ld / st of 32 lanes.
 #pragma once

@@ -140,6 +140,7 @@ def build_parser() -> argparse.ArgumentParser:
     _add_compile(sub.add_parser("compile", help="compile a source dataset"))
     p = sub.add_parser("info", help="describe a compiled dataset")
     p.add_argument("path")
+    sub.add_parser("models", help="registered model families, capabilities and presets")
     p = sub.add_parser("bench", help="loader throughput of a compiled dataset")
     p.add_argument("path")
     p.add_argument("--batch-size", type=int, default=8)
@@ -319,9 +320,33 @@ def _bench(a) -> int:
 
 
 def _require_native_backend(a) -> None:
-    if getattr(a, "backend", "auto") in ("onnx", "tensorrt") or (not a.weights and (a.onnx or a.tensorrt)):
+    from ..models.registry import ModelArtifactRequest, default_registry
+    req = ModelArtifactRequest(weights_path=a.weights or "", onnx_path=getattr(a, "onnx", None) or "",
+                               tensorrt_path=getattr(a, "tensorrt", None) or "", preset_name=a.preset or "",
+                               resolution=a.resolution or 0)
+    try:
+        req.validate()
+    except ValueError as e:
+        raise SystemExit(str(e))
+    kind = req.selected_input_kind()
+    if getattr(a, "backend", "auto") in ("onnx", "tensorrt"):
+        kind = a.backend
+    module = default_registry().find_module("rfdetr")
+    caps = module.capabilities()
+    if (kind == "onnx" and not caps.supports_onnx) or (kind == "tensorrt" and not caps.supports_tensorrt):
         raise Unavailable("ONNX Runtime and TensorRT are not installed in this environment; "
                           "use --weights (the native B200 backend)")
+
+
+def _models() -> int:
+    """Registered model families, their capabilities and presets (JSON)."""
+    from dataclasses import asdict
+    from ..models.registry import default_registry
+    reg = default_registry()
+    print(json.dumps([{"module_id": m.module_id, "display_name": m.display_name,
+                       "capabilities": asdict(m.capabilities()),
+                       "presets": [asdict(p) for p in m.presets()]} for m in reg.modules()], indent=1))
+    return 0
 
 
 def _predictor(a):
@@ -477,6 +502,8 @@ def run(argv: Optional[List[str]] = None) -> int:
         return _info(a.path)
     if a.cmd == "bench":
         return _bench(a)
+    if a.cmd == "models":
+        return _models()
     r = a.rcmd
     if r == "compile":
         return _compile(a)

@@ -61,6 +61,8 @@ GEMM_SHAPES = [
     ("dec.ffn1.wgrad", 2048, 256, 31200, "tn"), ("dec.ffn2.dgrad", 31200, 2048, 256, "nn"),
     # the training forms: bias + GELU / ReLU epilogue that also stores the pre-activation
     ("vit.fc1.fwd.gelu_aux", 10400, 1536, 384, "nt_gelu"), ("dec.ffn1.fwd.relu_aux", 31200, 2048, 256, "nt_relu"),
+    # main-loop probe: one 128 x 256 tile per SM (one 256 x 256 pair tile per two SMs), a long reduction
+    ("probe.mainloop", 18944, 256, 8192, "nt"),
 ]
 
 
