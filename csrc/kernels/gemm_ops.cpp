@@ -2,6 +2,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <limits>
 #include <mutex>
 #include <vector>
 
@@ -119,6 +120,77 @@ std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::option
     return {C};
 }
 
+// Batched products through 2-D tensor maps (see GemmArgs): a / b are the whole operand matrices
+// (row-major, unit column stride); batch i reads them at tile coordinates shifted by
+// i * (a_bk, a_bm) and i * (b_bk, b_bn).  Returns C [batch, M, N] bf16, or for epi 7 the row
+// maxima of acc + bias as fp32 [2, batch, M] (one per half of the columns; take the larger).
+//   epi 0: acc + bias;  6: alpha * (acc + bias) + beta * res (res [batch, M, N]);  7: row max.
+std::vector<torch::Tensor> gemm_tc_batched(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> bias,
+                                           bool a_mn, bool b_mn, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                           int64_t a_bk, int64_t a_bm, int64_t b_bk, int64_t b_bn, int64_t epi,
+                                           double alpha, double beta, c10::optional<torch::Tensor> res) {
+    TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.dim() == 2 && b.dim() == 2, "gemm_tc_batched: 2-D CUDA tensors");
+    TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16, "gemm_tc_batched: bf16");
+    TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0 &&
+                    aligned16(a) && aligned16(b),
+                "gemm_tc_batched: row-major operands with 16-byte aligned rows");
+    TORCH_CHECK(batch >= 1 && M > 0 && N > 0 && K > 0 && N % 16 == 0, "gemm_tc_batched: bad sizes");
+    TORCH_CHECK(batch == 1 || K % 64 == 0, "gemm_tc_batched: K must be a multiple of 64 when batch > 1");
+    TORCH_CHECK(epi == 0 || epi == 6 || epi == 7, "gemm_tc_batched: epilogue 0, 6 or 7");
+    TORCH_CHECK(!a_mn || M % 128 == 0, "gemm_tc_batched: MN-major A needs M % 128 == 0");
+    TORCH_CHECK(!b_mn || N % 128 == 0, "gemm_tc_batched: MN-major B needs N % 128 == 0");
+    at::cuda::CUDAGuard guard(a.device());
+    GemmArgs g{};
+    g.A = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
+    g.B = reinterpret_cast<const __nv_bfloat16*>(b.data_ptr());
+    g.a_inner = a.size(1);
+    g.a_outer = a.size(0);
+    g.b_inner = b.size(1);
+    g.b_outer = b.size(0);
+    g.M = static_cast<int>(M);
+    g.N = static_cast<int>(N);
+    g.K = static_cast<int>(K);
+    g.ldc = N;
+    g.epi = static_cast<int>(epi);
+    g.batch = static_cast<int>(batch);
+    g.a_bk = static_cast<int>(a_bk);
+    g.a_bm = static_cast<int>(a_bm);
+    g.b_bk = static_cast<int>(b_bk);
+    g.b_bn = static_cast<int>(b_bn);
+    g.bs_c = M * N;
+    g.alpha = static_cast<float>(alpha);
+    g.beta = static_cast<float>(beta);
+    g.status = status_word(a.device()).data_ptr<int>();
+    torch::Tensor bias_c, res_c, C, rmax;
+    if (bias.has_value() && bias->defined()) {
+        bias_c = bias->contiguous();
+        TORCH_CHECK(bias_c.scalar_type() == torch::kBFloat16 && bias_c.numel() == batch * N,
+                    "gemm_tc_batched: bias bf16 [batch, N]");
+        if (!aligned16(bias_c)) bias_c = bias_c.clone();
+        g.bias = reinterpret_cast<const __nv_bfloat16*>(bias_c.data_ptr());
+        g.bs_bias = N;
+    }
+    if (epi == 6) {
+        TORCH_CHECK(res.has_value() && res->defined(), "gemm_tc_batched: epilogue 6 needs res");
+        res_c = res->contiguous();
+        TORCH_CHECK(res_c.scalar_type() == torch::kBFloat16 && res_c.numel() == batch * M * N && aligned16(res_c),
+                    "gemm_tc_batched: res bf16 [batch, M, N]");
+        g.res = reinterpret_cast<const __nv_bfloat16*>(res_c.data_ptr());
+    }
+    if (epi == 7) {
+        TORCH_CHECK(N <= 256, "gemm_tc_batched: the row maximum takes N <= 256");
+        rmax = torch::full({2, batch, M}, -std::numeric_limits<float>::infinity(),
+                           a.options().dtype(torch::kFloat32));
+        g.rmax = rmax.data_ptr<float>();
+        C = torch::empty({1}, a.options());
+    } else {
+        C = torch::empty({batch, M, N}, a.options());
+    }
+    g.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr());
+    check_cuda(launch_gemm_tc(g, a_mn, b_mn, a.stride(0), b.stride(0), cur_stream()), "gemm_tc_batched");
+    return {epi == 7 ? rmax : C};
+}
+
 int64_t gemm_tc_status(int64_t device) {
     auto& t = status_word(torch::Device(torch::kCUDA, static_cast<c10::DeviceIndex>(device)));
     return t.item<int>();
@@ -131,6 +203,10 @@ void register_gemm_ops(pybind11::module& m) {
           py::arg("b_mn") = false, py::arg("epi") = 0, py::arg("want_aux") = false, py::arg("res") = py::none(),
           py::arg("gamma") = py::none(), py::arg("colsum") = py::none(), py::arg("colsum_acc") = false);
     m.def("gemm_tc_status", &gemm_tc_status);
+    m.def("gemm_tc_batched", &gemm_tc_batched, py::arg("a"), py::arg("b"), py::arg("bias"), py::arg("a_mn"),
+          py::arg("b_mn"), py::arg("batch"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("a_bk"), py::arg("a_bm"),
+          py::arg("b_bk"), py::arg("b_bn"), py::arg("epi") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
+          py::arg("res") = py::none());
     m.def("gemm_tc_smem_bytes", &gemm_tc_smem_bytes);
     m.def("gemm_tc_set_variant", &gemm_tc_set_variant, py::arg("variant"));
     m.def("gemm_tc_variant", &gemm_tc_variant);

@@ -126,7 +126,7 @@ __device__ __forceinline__ void stage_load(uint32_t* stg, int lane, float* x, co
 
 // Epilogue of one warp's 32 rows x `ncols` (16 or 32) columns; lane = row.
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg, int lane, int row0, int col,
-                                               int ncols, float* v) {
+                                               int ncols, float* v, bool rmax_first = true) {
     const int rows_valid = min(32, g.M - row0);
     const int row = row0 + lane;
     if (g.ws) {  // split-K partial: fp32 vector atomics into the workspace
@@ -151,6 +151,19 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg,
         }
     }
     const int64_t base = static_cast<int64_t>(row0) * g.ldc + col;
+    if (g.epi == 7) {
+        // running row maximum over this warp's columns (the caller passes rmax already offset to
+        // this warp's half and batch; the first chunk of a half stores, later ones combine)
+        float m = -__int_as_float(0x7f800000);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i < ncols) m = fmaxf(m, v[i]);
+        if (row < g.M) {
+            float* dst = g.rmax + row;
+            *dst = (rmax_first ? m : fmaxf(*dst, m));
+        }
+        return;
+    }
     if (g.aux) stage_store(stg, lane, v, g.aux + base, g.ldc, rows_valid, ncols);  // pre-activation for backward
     if (g.epi == 1) {
 #pragma unroll
@@ -170,6 +183,11 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg,
                 for (int i = 0; i < 8; ++i) v[8 * j + i] = r[8 * j + i] + gm[i] * v[8 * j + i];
             }
         }
+    } else if (g.epi == 6) {
+        float r[32];
+        stage_load(stg, lane, r, g.res + base, g.ldc, rows_valid, ncols);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = g.alpha * v[i] + g.beta * r[i];
     } else if (g.epi == 4 || g.epi == 5) {
         // activation backward: the product is the gradient w.r.t. the activation output
         float p[32];
@@ -199,7 +217,9 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg,
 
 struct Sched {
     int m_tiles, n_tiles, splits, ktiles, kt_per_split, bn, rows;
+    __device__ int batch_of(int u) const { return u / (m_tiles * n_tiles * splits); }
     __device__ void unit(int u, int& m0, int& n0, int& kt0, int& kt1) const {
+        u %= m_tiles * n_tiles * splits;
         const int tile = u / splits, s = u % splits;
         m0 = (tile / n_tiles) * rows;
         n0 = (tile % n_tiles) * bn;
@@ -222,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     SmemCtl* ctl = reinterpret_cast<SmemCtl*>(reinterpret_cast<unsigned char*>(staging) + kStagingBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int units = sch.m_tiles * sch.n_tiles * sch.splits;
+    const int units = sch.m_tiles * sch.n_tiles * sch.splits * g.batch;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -259,6 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 const int a_boxes = A_MN ? min(BM / 64, (g.M - m0 + 63) / 64) : 1;
                 const int b_boxes = B_MN ? min(BN / 64, (g.N - n0 + 63) / 64) : 1;
                 const uint32_t bytes = (A_MN ? a_boxes * 8192 : kATile) + (B_MN ? b_boxes * 8192 : kBTile);
+                // batch bt: the operands' tile coordinates shifted by bt * (shift along K, along M / N)
+                const int bt = sch.batch_of(u);
+                const int ak = bt * g.a_bk, am = bt * g.a_bm, bk = bt * g.b_bk, bn_ = bt * g.b_bn;
                 for (int kt = kt0; kt < kt1; ++kt, ++it) {
                     const int s = it % kStages;
                     const uint32_t ph = (it / kStages) & 1;
@@ -272,14 +295,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                     unsigned char* b = tilesB + s * kBTile;
                     const int k0 = kt * BK;
                     if (A_MN) {
-                        for (int q = 0; q < a_boxes; ++q) tma_load_2d(&tmA, &ctl->full[s], a + q * 8192, m0 + 64 * q, k0);
+                        for (int q = 0; q < a_boxes; ++q)
+                            tma_load_2d(&tmA, &ctl->full[s], a + q * 8192, am + m0 + 64 * q, ak + k0);
                     } else {
-                        tma_load_2d(&tmA, &ctl->full[s], a, k0, m0);
+                        tma_load_2d(&tmA, &ctl->full[s], a, ak + k0, am + m0);
                     }
                     if (B_MN) {
-                        for (int q = 0; q < b_boxes; ++q) tma_load_2d(&tmB, &ctl->full[s], b + q * 8192, n0 + 64 * q, k0);
+                        for (int q = 0; q < b_boxes; ++q)
+                            tma_load_2d(&tmB, &ctl->full[s], b + q * 8192, bn_ + n0 + 64 * q, bk + k0);
                     } else {
-                        tma_load_2d(&tmB, &ctl->full[s], b, k0, n0);
+                        tma_load_2d(&tmB, &ctl->full[s], b, bk + k0, bn_ + n0);
                     }
                 }
             }
@@ -345,6 +370,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             const int row0 = m0 + 32 * q;
             const uint32_t acc = tmem + buf * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
             constexpr int kHalfCols = BN / 2;
+            // this unit's batch: outputs (and the epilogue's side inputs) at their batch offsets
+            GemmArgs gb = g;
+            const int bt = sch.batch_of(u);
+            if (bt) {
+                gb.C += bt * g.bs_c;
+                if (gb.aux) gb.aux += bt * g.bs_c;
+                if (gb.res) gb.res += bt * g.bs_c;
+                if (gb.bias) gb.bias += bt * g.bs_bias;
+            }
+            if (g.epi == 7) gb.rmax += (static_cast<int64_t>(half) * g.batch + bt) * g.M;
             for (int c = half * kHalfCols; c < (half + 1) * kHalfCols; c += 32) {
                 if (n0 + c >= g.N || row0 >= g.M) break;  // warp-uniform
                 const int ncols = min(min(32, (half + 1) * kHalfCols - c), g.N - n0 - c);
@@ -354,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 } else {
                     tmem_ld16(acc + c, v);
                 }
-                epilogue_chunk(g, stg, lane, row0, n0 + c, ncols, v);
+                epilogue_chunk(gb, stg, lane, row0, n0 + c, ncols, v, c == half * kHalfCols);
             }
             // accumulator buffer free again
             tc_fence_before();
@@ -473,7 +508,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-    const int units = sch.m_tiles * sch.n_tiles * sch.splits;
+    const int units = sch.m_tiles * sch.n_tiles * sch.splits;   // unbatched products only
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -769,13 +804,24 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
     cudaError_t de = cudaGetDevice(&dev);
     if (de == cudaSuccess) de = cudaSetDevice(dev);
     if (de != cudaSuccess) return de;
-    const Plan plan = plan_for(g.M, g.N, g.K, b_mn, g.ws != nullptr);
+    if (g.batch < 1) g.batch = 1;
+    if (g.batch > 1 && (g.K % BK != 0 || g.ws != nullptr)) return cudaErrorInvalidValue;
+    if (g.epi == 7 && (g.rmax == nullptr || g.N > 256)) return cudaErrorInvalidValue;
+    Plan plan = plan_for(g.M, g.N, g.K, b_mn, g.ws != nullptr);
+    if (g.batch > 1 || g.epi == 7) {
+        plan.pair = false;
+        plan.bn = pick_bn(g.M, g.N);
+    }
+    if (g.epi == 7) plan.bn = g.N <= 128 ? 128 : (g.N <= 192 ? 192 : 256);   // one column tile
     const int bn = plan.bn;
     const int rows = plan.pair ? kPairRows : BM;
     const int b_rows = plan.pair ? bn / 2 : bn;     // B rows per CTA (K-major box height)
     CUtensorMap ta, tb;
-    bool ok = a_mn ? make_map(&ta, g.A, g.M, g.K, lda, 64) : make_map(&ta, g.A, g.K, g.M, lda, BM);
-    ok = ok && (b_mn ? make_map(&tb, g.B, g.N, g.K, ldb, 64) : make_map(&tb, g.B, g.K, g.N, ldb, b_rows));
+    // batched products read every batch through one map over the whole operand matrix
+    const int64_t ai = g.a_inner ? g.a_inner : (a_mn ? g.M : g.K), ao = g.a_outer ? g.a_outer : (a_mn ? g.K : g.M);
+    const int64_t bi = g.b_inner ? g.b_inner : (b_mn ? g.N : g.K), bo = g.b_outer ? g.b_outer : (b_mn ? g.K : g.N);
+    bool ok = a_mn ? make_map(&ta, g.A, ai, ao, lda, 64) : make_map(&ta, g.A, ai, ao, lda, BM);
+    ok = ok && (b_mn ? make_map(&tb, g.B, bi, bo, ldb, 64) : make_map(&tb, g.B, bi, bo, ldb, b_rows));
     if (!ok) return cudaErrorInvalidValue;
     Sched sch;
     sch.bn = bn;
@@ -786,7 +832,7 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
     sch.splits = g.ws ? std::max(1, g.splits) : 1;
     sch.kt_per_split = (sch.ktiles + sch.splits - 1) / sch.splits;
     sch.splits = (sch.ktiles + sch.kt_per_split - 1) / sch.kt_per_split;
-    const int units = sch.m_tiles * sch.n_tiles * sch.splits;
+    const int units = sch.m_tiles * sch.n_tiles * sch.splits * g.batch;
     const int grid = plan.pair ? 2 * std::min(units, std::max(1, num_sms() / 2)) : std::min(units, num_sms());
     cudaError_t e = cudaSuccess;
     if (g.ws) {

@@ -23,7 +23,21 @@ struct GemmArgs {
     int64_t ldc;
     int epi;                    // 0 none, 1 GELU(erf), 2 ReLU, 3 res + gamma * (acc + bias),
                                 // 4 acc * GELU'(res), 5 acc * [res > 0]   (res = pre-activation, backward)
+                                // 6 alpha * (acc + bias) + beta * res,
+                                // 7 row maximum of acc + bias -> rmax (C is not written)
     float* colacc;              // optional fp32 [N]: += column sums of the stored (bf16-rounded) output
+    // Batched products: `batch` independent M x N x K products in one launch.  Batch b reads its
+    // operands through the same tensor maps with the tile coordinates shifted by b * (a_bk, a_bm)
+    // for A (along K, along M) and b * (b_bk, b_bn) for B, and writes C / aux / res at b * bs_c,
+    // bias at b * bs_bias.  K must be a multiple of 64 when batch > 1 (a K tail would read the
+    // next batch's operand).
+    int batch;
+    int a_bk, a_bm, b_bk, b_bn;
+    int64_t bs_c, bs_bias;
+    float alpha, beta;          // epi 6
+    float* rmax;                // epi 7: fp32 [2, batch, M], one partial maximum per half of the columns
+    // extents of the 2-D operand matrices the tensor maps cover (0: derived from M / N / K)
+    int64_t a_inner, a_outer, b_inner, b_outer;
 };
 
 size_t gemm_tc_smem_bytes();

@@ -440,7 +440,8 @@ class Transformer(nn.Module):
           folded into the class head: W' = W diag(gamma), b' = W beta + b;
         * class logits as a strided batched GEMM over the groups; the class dimension is
           padded to a multiple of 8 with zero weights and -inf bias, so the max over the
-          padded, contiguous rows equals the max over the real classes.
+          padded, contiguous rows equals the max over the real classes; on the GPU the GEMM's
+          epilogue reduces each row to its maximum (the logits are never stored).
         """
         B, S, C = out_mem.shape
         G = groups
@@ -461,9 +462,17 @@ class Transformer(nn.Module):
         if pad:
             w_f = F.pad(w_f, (0, 0, 0, pad))
             b_f = F.pad(b_f, (0, pad), value=float("-inf"))
-        x = hn.view(B * S, G, C).transpose(0, 1)                               # [G, B*S, C], row stride G*C
-        cls = torch.baddbmm(b_f.to(dt)[:, None, :], x, w_f.to(dt).transpose(1, 2))   # [G, B*S, K+pad]
-        best = cls.amax(-1).view(G, B, S)
+        if hn.is_cuda:
+            # one batched tcgen05 GEMM over the groups (group g's operand is columns [g*C, g*C + C) of
+            # the shared rows) whose epilogue keeps only each row's best logit: the [G, B*S, K] logits
+            # are never written.  Rounded to the compute dtype, like a max over rounded logits.
+            from ..ops.gemm import bmm_nt_rowmax
+            best = bmm_nt_rowmax(hn.view(B * S, G * C), w_f.to(dt).contiguous(), b_f.to(dt).contiguous(), C,
+                                 B * S).to(dt).view(G, B, S)
+        else:
+            x = hn.view(B * S, G, C).transpose(0, 1)                           # [G, B*S, C], row stride G*C
+            cls = torch.baddbmm(b_f.to(dt)[:, None, :], x, w_f.to(dt).transpose(1, 2))   # [G, B*S, K+pad]
+            best = cls.amax(-1).view(G, B, S)
         k = min(self.cfg.num_queries, S)
         return best.topk(k, dim=2)[1]
 

@@ -18,7 +18,8 @@ import torch
 
 from ._ext import kernels
 
-__all__ = ["gemm_nt", "gemm_nn", "gemm_tn", "gemm_nt_epilogue", "set_tc_gemm", "tc_gemm_enabled"]
+__all__ = ["gemm_nt", "gemm_nn", "gemm_tn", "gemm_nt_epilogue", "set_tc_gemm", "tc_gemm_enabled",
+           "bmm_nt", "bmm_nn_mn", "bmm_nt_rowmax"]
 
 # The fused-epilogue forward products always run on the tcgen05 kernel (that is
 # where fusing saves whole passes over memory); plain products (backward dgrad /
@@ -105,3 +106,54 @@ def gemm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 def gemm_tn_acc(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     """out += a^T b in one GEMM (beta = 1): weight gradients accumulated straight into .grad."""
     return out.addmm_(a.t(), b)
+
+
+# ---------------------------------------------------------------------------------------------
+# Batched products on the tcgen05 kernel: every batch reads the same 2-D tensor maps at shifted
+# tile coordinates, so stacked operands need no copies.  K must be a multiple of 64 (a K tail
+# would read the next batch's operand); other shapes run on the library's batched GEMM.
+
+def _bf16_rows(t):
+    return t.is_cuda and t.dtype == torch.bfloat16 and t.stride(-1) == 1 and _rowmajor(t)
+
+
+def bmm_nt(x: torch.Tensor, w: torch.Tensor, bias=None, alpha: float = 1.0, beta: float = 0.0, res=None):
+    """x [G, M, K] @ w[G, N, K]^T (+ bias [G, N]); with ``res``: alpha * (x w^T + bias) + beta * res."""
+    G, M, K = x.shape
+    N = w.shape[1]
+    if (tc_gemm_enabled() and K % 64 == 0 and N % 16 == 0 and x.is_contiguous() and w.is_contiguous()
+            and _bf16_rows(x.view(G * M, K)) and _bf16_rows(w.view(G * N, K))):
+        return kernels().gemm_tc_batched(x.view(G * M, K), w.view(G * N, K), bias, False, False, G, M, N, K,
+                                         0, M, 0, N, 6 if res is not None else 0, alpha, beta, res)[0]
+    y = torch.bmm(x, w.transpose(1, 2))
+    if bias is not None:
+        y = y + bias[:, None, :]
+    return y if res is None else alpha * y + beta * res
+
+
+def bmm_nn_mn(x: torch.Tensor, y: torch.Tensor, alpha: float = 1.0, beta: float = 0.0, res=None):
+    """x [G, M, K] @ y [G, K, N] (y read MN-major, no transpose); with ``res``: alpha * x y + beta * res."""
+    G, M, K = x.shape
+    N = y.shape[2]
+    if (tc_gemm_enabled() and K % 64 == 0 and N % 128 == 0 and x.is_contiguous() and y.is_contiguous()
+            and _bf16_rows(x.view(G * M, K)) and _bf16_rows(y.view(G * K, N))):
+        return kernels().gemm_tc_batched(x.view(G * M, K), y.view(G * K, N), None, False, True, G, M, N, K,
+                                         0, M, K, 0, 6 if res is not None else 0, alpha, beta, res)[0]
+    z = torch.bmm(x, y)
+    return z if res is None else alpha * z + beta * res
+
+
+def bmm_nt_rowmax(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, col_shift: int, rows: int):
+    """max over n of (A_g w_g^T + bias_g)[m, n] for every group g, without storing the products.
+
+    ``a`` [rows, G * col_shift]: group g's [rows, K] operand starts at column g * col_shift
+    (K = w.shape[2]); w [G, N, K], bias [G, N] (padding columns carry -inf bias).  Returns fp32
+    [G, rows].  Falls back to the library GEMM + max when the kernel does not take the shape."""
+    G, N, K = w.shape
+    if (tc_gemm_enabled() and K % 64 == 0 and N % 16 == 0 and N <= 256 and w.is_contiguous()
+            and _bf16_rows(a) and _bf16_rows(w.view(G * N, K))):
+        r = kernels().gemm_tc_batched(a, w.view(G * N, K), bias, False, False, G, rows, N, K,
+                                      col_shift, 0, 0, N, 7)[0]
+        return torch.maximum(r[0], r[1])
+    x = a.view(rows, G, col_shift)[..., :K].transpose(0, 1)
+    return torch.baddbmm(bias[:, None, :], x, w.transpose(1, 2)).amax(-1).float()

@@ -11,9 +11,13 @@ bf16 matrix normalised by its Frobenius norm (+1e-7), the wide orientation, a
 takes AdamW with betas (0.9, 0.95), eps 1e-10.
 
 B200 design: parameters with the same matrix shape are stacked and
-orthogonalised together with batched GEMMs (one ``bmm`` chain per shape class
-instead of one per parameter), which keeps the tensor cores busy on the many
-384x384 / 1536x384 ViT matrices.  State and updates are fp32 on the master
+orthogonalised together with batched GEMMs (one chain per shape class instead
+of one per parameter), which keeps the tensor cores busy on the many
+384x384 / 1536x384 ViT matrices.  On the GPU the chain runs on the framework's
+batched tcgen05 GEMM (``ops.gemm.bmm_nt`` / ``bmm_nn_mn``: every stacked matrix
+through one pair of tensor maps, the quintic's coefficients in the alpha / beta
+epilogue); shapes it does not take (a reduction that is not a multiple of 64)
+use the library's batched GEMM.  State and updates are fp32 on the master
 weights.  Eager only, like the reference.
 """
 from __future__ import annotations
@@ -51,7 +55,16 @@ def newton_schulz5(g: torch.Tensor, steps: int = NS_STEPS) -> torch.Tensor:
         x = x.transpose(-2, -1)
     x = x / (x.flatten(-2).norm(dim=-1)[..., None, None] + NORM_EPS)
     lead = x.shape[:-2]
-    x = x.reshape(-1, *x.shape[-2:])
+    x = x.reshape(-1, *x.shape[-2:]).contiguous()
+    if x.is_cuda:
+        # batched tcgen05 products (every matrix of the shape class in one launch), the polynomial's
+        # scaling and sums in their alpha / beta epilogues; G = X X^T is symmetric, so G.G = G G^T
+        from ..ops.gemm import bmm_nn_mn, bmm_nt
+        for _ in range(steps):
+            gram = bmm_nt(x, x)                                        # X X^T
+            poly = bmm_nt(gram, gram, alpha=c, beta=b, res=gram)       # c*G.G + b*G
+            x = bmm_nn_mn(poly, x, alpha=1.0, beta=a, res=x)           # P.X + a*X
+        steps = 0
     for _ in range(steps):
         # three GEMMs per step, the polynomial's scaling and sums in their alpha / beta epilogues
         gram = torch.bmm(x, x.transpose(-2, -1))

@@ -515,3 +515,80 @@ def test_scaled_residual_layer_norm_kernel(cuda_device, dtype):
     ref = torch.nn.functional.layer_norm(ref_s, (384,), w.to(dtype).float(), b.to(dtype).float(), 1e-6)
     tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
     assert _rel(s, ref_s) < tol and _rel(out, ref) < tol
+
+
+# ------------------------------------------------------------------ batched tcgen05 products
+
+def _rel(got, ref):
+    return ((got.float() - ref.float()).abs().max() / ref.float().abs().max().clamp_min(1e-6)).item()
+
+
+@pytest.mark.parametrize("G,M,N,K", [(3, 200, 256, 128), (5, 384, 384, 384), (2, 130, 96, 256)])
+def test_bmm_nt_batched_vs_fp32(cuda_device, G, M, N, K):
+    """Stacked products through shifted tile coordinates (M tails read the next batch's rows, which
+    only feed rows that are not stored), with bias and with the alpha / beta epilogue."""
+    from mmltk_b200.ops.gemm import bmm_nt
+    g = torch.Generator().manual_seed(G * 1000 + M)
+    x = torch.randn(G, M, K, generator=g).bfloat16()
+    w = (torch.randn(G, N, K, generator=g) * K ** -0.5).bfloat16()
+    bias = torch.randn(G, N, generator=g).bfloat16()
+    res = torch.randn(G, M, N, generator=g).bfloat16()
+    ref = x.float() @ w.float().transpose(1, 2) + bias.float()[:, None, :]
+    d = lambda t: t.to(cuda_device)
+    y = bmm_nt(d(x), d(w), d(bias))
+    y2 = bmm_nt(d(x), d(w), d(bias), alpha=0.7, beta=-1.3, res=d(res))
+    torch.cuda.synchronize()
+    assert kernels().gemm_tc_status(0) == 0
+    assert _rel(y.cpu(), ref) < 1e-2
+    assert _rel(y2.cpu(), 0.7 * ref - 1.3 * res.float()) < 1e-2
+
+
+def test_bmm_nn_mn_batched_vs_fp32(cuda_device):
+    from mmltk_b200.ops.gemm import bmm_nn_mn
+    g = torch.Generator().manual_seed(7)
+    G, M, K, N = 3, 200, 384, 384
+    x = torch.randn(G, M, K, generator=g).bfloat16()
+    y = (torch.randn(G, K, N, generator=g) * K ** -0.5).bfloat16()
+    res = torch.randn(G, M, N, generator=g).bfloat16()
+    d = lambda t: t.to(cuda_device)
+    z = bmm_nn_mn(d(x), d(y), alpha=1.0, beta=0.5, res=d(res))
+    torch.cuda.synchronize()
+    assert kernels().gemm_tc_status(0) == 0
+    assert _rel(z.cpu(), x.float() @ y.float() + 0.5 * res.float()) < 1e-2
+
+
+def test_bmm_nt_rowmax_vs_fp32(cuda_device):
+    """The selection pass's product: per group, columns [g*C, g*C + K) of shared rows against the
+    group's weights; only each row's best (bias-padded) logit leaves the kernel."""
+    from mmltk_b200.ops.gemm import bmm_nt_rowmax
+    g = torch.Generator().manual_seed(11)
+    rows, G, C, N = 333, 4, 256, 96
+    a = torch.randn(rows, G * C, generator=g).bfloat16()
+    w = (torch.randn(G, N, C, generator=g) * C ** -0.5).bfloat16()
+    bias = torch.randn(G, N, generator=g)
+    bias[:, 91:] = float("-inf")
+    bias = bias.bfloat16()
+    ref = torch.stack([(a[:, i * C:(i + 1) * C].float() @ w[i].float().t() + bias[i].float()).amax(-1)
+                       for i in range(G)])
+    d = lambda t: t.to(cuda_device)
+    got = bmm_nt_rowmax(d(a), d(w), d(bias), C, rows)
+    torch.cuda.synchronize()
+    assert kernels().gemm_tc_status(0) == 0
+    assert got.shape == (G, rows)
+    assert _rel(got.cpu(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("nb,r,c", [(6, 384, 384), (3, 384, 1536), (4, 64, 256)])
+def test_newton_schulz_gpu_matches_fp32(cuda_device, nb, r, c):
+    """Muon's quintic Newton-Schulz on the batched tcgen05 products vs the same iteration in fp32."""
+    from mmltk_b200.train.muon import NS_COEFFS, newton_schulz5
+    torch.manual_seed(nb + r)
+    gr = torch.randn(nb, r, c)
+    got = newton_schulz5(gr.to(cuda_device)).float().cpu()
+    a, b, cc = NS_COEFFS
+    x = gr / (gr.flatten(-2).norm(dim=-1)[..., None, None] + 1e-7)
+    for _ in range(5):
+        gm = x @ x.transpose(-2, -1)
+        x = a * x + (b * gm + cc * gm @ gm) @ x
+    err = ((got - x).norm() / x.norm()).item()
+    assert err < 5e-2, err
