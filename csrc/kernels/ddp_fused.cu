@@ -106,13 +106,14 @@ __device__ bool last_cta(unsigned int* ticket) {
 // summed over every rank's buffer in rank order (fp32), into gshard_at; per-CTA sums of squares into
 // partials_b.  Starts with the bucket's barrier: mark = epoch * 32 + bucket + 1 is published to every
 // rank and awaited from every rank (marks only grow within and across steps).
-__global__ void __launch_bounds__(256) ddp_rs_kernel(DdpPeers peers, DdpState st, int64_t g_off, int64_t len,
-                                                     float* __restrict__ gshard_at, float* __restrict__ partials_b,
-                                                     int bucket) {
+// The bucket barrier: publish mark = epoch * 32 + bucket + 1 to every rank, then wait (bounded) for
+// every rank's mark.  Run by every CTA of the reduce-scatter when it is alone on the GPU, or by a
+// one-CTA launch ahead of it when the reduce-scatter overlaps the backward pass (only 32 threads
+// spin then, instead of a whole grid holding SM slots the backward kernels need).
+__device__ bool bucket_barrier(const DdpPeers& peers, const DdpState& st, int bucket, bool publish) {
     const uint32_t mark = *st.epoch * 32u + static_cast<uint32_t>(bucket) + 1u;
     const int world = peers.world, rank = peers.rank;
-    // ---- barrier: my gradients of this bucket are complete; wait for everybody's
-    if (blockIdx.x == 0 && threadIdx.x < world) {
+    if (publish && threadIdx.x < world) {
         __threadfence_system();
         st_release_u32(peers.flags[threadIdx.x] + kFlagReady + rank, mark);
     }
@@ -126,7 +127,20 @@ __global__ void __launch_bounds__(256) ddp_rs_kernel(DdpPeers peers, DdpState st
         }
     }
     __syncthreads();
-    if (!ok) {
+    return ok != 0;
+}
+
+__global__ void ddp_bucket_barrier_kernel(DdpPeers peers, DdpState st, int bucket) {
+    bucket_barrier(peers, st, bucket, true);
+}
+
+__global__ void __launch_bounds__(256) ddp_rs_kernel(DdpPeers peers, DdpState st, int64_t g_off, int64_t len,
+                                                     float* __restrict__ gshard_at, float* __restrict__ partials_b,
+                                                     int bucket, int own_barrier) {
+    const int world = peers.world;
+    // ---- barrier: my gradients of this bucket are complete; wait for everybody's (here, or in the
+    // one-CTA launch before this one; a failed wait there left its code in the status word)
+    if (own_barrier && !bucket_barrier(peers, st, bucket, blockIdx.x == 0)) {
         if (threadIdx.x == 0) partials_b[blockIdx.x] = 0.f;
         return;
     }
@@ -402,7 +416,13 @@ cudaError_t launch_ddp_rs(const DdpPeers& peers, const DdpState& st, int64_t g_o
     if (len % 8 != 0 || g_off % 8 != 0 || peers.world < 1 || peers.world > kDdpMaxWorld || bucket < 0 ||
         bucket >= kDdpMaxBuckets || blocks < 1)
         return cudaErrorInvalidValue;
-    ddp_rs_kernel<<<blocks, 256, 0, s>>>(peers, st, g_off, len, gshard_at, partials_b, bucket);
+    const bool overlapped = blocks < num_sms();
+    if (overlapped) {
+        ddp_bucket_barrier_kernel<<<1, 32, 0, s>>>(peers, st, bucket);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    ddp_rs_kernel<<<blocks, 256, 0, s>>>(peers, st, g_off, len, gshard_at, partials_b, bucket, overlapped ? 0 : 1);
     return cudaGetLastError();
 }
 

@@ -36,6 +36,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "gemm_tc.h"
@@ -389,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 } else {
                     tmem_ld16(acc + c, v);
                 }
+                if (g.diag & 1) continue;
                 epilogue_chunk(gb, stg, lane, row0, n0 + c, ncols, v, c == half * kHalfCols);
             }
             // accumulator buffer free again
@@ -805,6 +807,13 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
     if (de == cudaSuccess) de = cudaSetDevice(dev);
     if (de != cudaSuccess) return de;
     if (g.batch < 1) g.batch = 1;
+    {
+        static const int diag = [] {
+            const char* e = std::getenv("MMLTK_GEMM_DIAG");
+            return e ? std::atoi(e) : 0;
+        }();
+        g.diag = diag;
+    }
     if (g.batch > 1 && (g.K % BK != 0 || g.ws != nullptr)) return cudaErrorInvalidValue;
     if (g.epi == 7 && (g.rmax == nullptr || g.N > 256)) return cudaErrorInvalidValue;
     Plan plan = plan_for(g.M, g.N, g.K, b_mn, g.ws != nullptr);

@@ -38,6 +38,9 @@ struct GemmArgs {
     float* rmax;                // epi 7: fp32 [2, batch, M], one partial maximum per half of the columns
     // extents of the 2-D operand matrices the tensor maps cover (0: derived from M / N / K)
     int64_t a_inner, a_outer, b_inner, b_outer;
+    // diagnostics (environment MMLTK_GEMM_DIAG): 1 = the epilogue reads the accumulator but stores
+    // nothing, which times the main loop and the tensor-memory hand-off alone
+    int diag;
 };
 
 size_t gemm_tc_smem_bytes();

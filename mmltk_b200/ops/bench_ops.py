@@ -4,6 +4,7 @@ library baseline of the same op, timed with CUDA events after warm-up.
     python -m mmltk_b200.ops.bench_ops gemm      # tcgen05 GEMM vs cuBLAS on the RF-DETR-M shapes
     python -m mmltk_b200.ops.bench_ops msda      # MSDeformAttn fwd+bwd vs fp32 reference path
     python -m mmltk_b200.ops.bench_ops attn      # attention fwd+bwd of the RF-DETR-M shapes per SDPA backend
+    python -m mmltk_b200.ops.bench_ops kernels   # LayerNorm, criterion (matcher + solver + losses), post-process
 
 Inputs are larger than L2 where the op allows; each timing is the median of
 several event-timed runs.
@@ -288,9 +289,72 @@ def bench_attn(device="cuda", quick=False):
     return rows
 
 
+def _criterion_case(device, B=8, groups=13, Qg=300, C=91, layers=4, kmax=10):
+    """Synthetic decoder outputs of RF-DETR-M training (main + aux layers + two-stage layer) and
+    targets: the criterion's matcher cost, assignment solver and matched / dense losses."""
+    from ..config import config_from_preset
+    from ..criterion import SetCriterion
+    from ..data.synthetic import synthetic_targets
+    cfg = config_from_preset("rf-detr-medium")
+    g = torch.Generator(device="cpu").manual_seed(0)
+    Q = groups * Qg
+
+    def layer():
+        lg = (torch.randn(B, Q, C, generator=g) * 2).to(device, torch.bfloat16).requires_grad_()
+        bx = torch.rand(B, Q, 4, generator=g).clamp(0.05, 0.95).to(device, torch.bfloat16).requires_grad_()
+        return {"pred_logits": lg, "pred_boxes": bx}
+
+    out = layer()
+    out["aux_outputs"] = [layer() for _ in range(layers - 1)]
+    out["enc_outputs"] = layer()
+    targets = synthetic_targets(B, g, 1, kmax, C - 1, kmax).to(device)
+    leaves = [l[k] for l in [out] + out["aux_outputs"] + [out["enc_outputs"]] for k in ("pred_logits", "pred_boxes")]
+    return SetCriterion(cfg), out, targets, leaves
+
+
+def bench_kernels(device="cuda", quick=False):
+    """Small-footprint launches of the step's memory-bound kernels (one op at a time, a few hundred MB
+    on the device): LayerNorm forward / backward on the ViT shape, the criterion (matcher cost + GPU
+    assignment solver + fused matched losses, forward and backward) on RF-DETR-M's training outputs,
+    and the top-k post-process.  ``quick``: three launches of each, untimed (profiler captures)."""
+    from .norm import layer_norm
+    from ..infer.postprocess import postprocess
+    g = torch.Generator(device=device).manual_seed(0)
+    x = torch.randn(10400, 384, device=device, generator=g).bfloat16().requires_grad_()
+    w = (1 + 0.1 * torch.randn(384, device=device, generator=g)).bfloat16().requires_grad_()
+    b = (0.1 * torch.randn(384, device=device, generator=g)).bfloat16().requires_grad_()
+    gy = torch.randn(10400, 384, device=device, generator=g).bfloat16()
+    crit, out, targets, leaves = _criterion_case(device)
+    logits = torch.randn(8, 300, 91, device=device, generator=g).bfloat16()
+    boxes = torch.rand(8, 300, 4, device=device, generator=g).bfloat16()
+
+    def ln():
+        torch.autograd.grad(layer_norm(x, w, b, 1e-6), (x, w, b), gy)
+
+    def crit_step():
+        losses, _ = crit(out, targets, training=True)
+        torch.autograd.grad(crit.weighted(losses), leaves)
+
+    def post():
+        postprocess({"pred_logits": logits, "pred_boxes": boxes}, 100, (560, 560), masks=False)
+
+    cases = [("layer_norm.fwd_bwd.vit-384", ln), ("criterion.fwd_bwd.rf-detr-m-b8", crit_step),
+             ("postprocess.topk100.b8", post)]
+    rows = []
+    for name, fn in cases:
+        if quick:
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            rows.append({"op": name, "quick": True})
+        else:
+            rows.append({"op": name, "ms": round(time_ms(fn, warmup=3, iters=10), 4)})
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "msda", "attn"])
+    ap.add_argument("what", choices=["gemm", "msda", "attn", "kernels"])
     ap.add_argument("--shape", default=None, help="run one GEMM shape (see GEMM_SHAPES)")
     ap.add_argument("--quick", nargs="?", const="default", default=None,
                     help="launch a few times without timing (profiler runs); attn: '--quick short' runs the "
@@ -304,6 +368,8 @@ def main():
         rows = bench_gemm(only=args.shape, quick=bool(args.quick))
     elif args.what == "msda":
         rows = bench_msda(quick=bool(args.quick))
+    elif args.what == "kernels":
+        rows = bench_kernels(quick=bool(args.quick))
     else:
         rows = bench_attn(quick=args.quick)
     for r in rows:

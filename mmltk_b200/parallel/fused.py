@@ -30,6 +30,7 @@ arrives makes its peers' kernels return with a non-zero status that
 """
 from __future__ import annotations
 
+import os
 from typing import List, Optional, Sequence, Tuple
 
 import torch
@@ -89,14 +90,17 @@ class FusedGradSync:
     # the flat buffer is laid out by backward-completion stage (the engine asks the model for it)
     bucketed = True
 
-    def __init__(self, group=None, spin_limit: int = 1 << 26, overlap: bool = True, min_bucket: int = 4 << 20):
+    def __init__(self, group=None, spin_limit: int = 1 << 26, overlap: Optional[bool] = None,
+                 min_bucket: int = 4 << 20):
         self.group = group
         self.world_size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.pad_multiple = self.world_size * 64
         self.spin_limit = int(spin_limit)
         self.device = torch.device("cuda", torch.cuda.current_device())
-        self.overlap = overlap
+        # reduce-scatter overlapped with the backward pass: off unless asked for (MMLTK_DDP_OVERLAP=1);
+        # on two B200s it measured slower than one reduce-scatter after the backward pass
+        self.overlap = (os.environ.get("MMLTK_DDP_OVERLAP", "0") == "1") if overlap is None else bool(overlap)
         self.min_bucket = int(min_bucket)
         self._handles: List[bytes] = []
         self._keep = []

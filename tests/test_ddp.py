@@ -226,13 +226,17 @@ def _gpu_ddp_worker(rank, world, port, backend, q):
         om, omm, ov, oema = _oracle_update(*before, gsum, elem_lr, elem_wd, sc)
         upd = (om - before[0]).abs().max().item()
         rel = lambda a, b: ((a - b).abs() / (b.abs() + 1e-6)).max().item()
+        # the master's error against the size of the numbers the update combined (a master value that
+        # the update nearly cancels is accurate to the ulp of its inputs, not of the small result)
+        mrel = lambda a, b, b0: ((a - b).abs() / (b.abs() + b0.abs() + 1e-6)).max().item()
         pb = eng.flat.param_buf
         ulps = (pb.view(torch.int16).int() - om.to(torch.bfloat16).view(torch.int16).int()).abs().max().item()
         others = [torch.zeros_like(pb) for _ in range(world)]
         dist.all_gather(others, pb)
         same = all(torch.equal(others[0], o) for o in others[1:])
         report.append(dict(step=step, loss=loss, update=upd, master_err=((after[0] - om).abs()).max().item(),
-                           master_rel=rel(after[0], om), m_rel=rel(after[1], omm), v_rel=rel(after[2], ov),
+                           master_rel=mrel(after[0], om, before[0]), m_rel=mrel(after[1], omm, before[1]),
+                           v_rel=rel(after[2], ov),
                            ema_err=(after[3] - oema).abs().max().item(), param_ulps=ulps, ranks_equal=same))
     if fused:
         # evaluation-style byte all-gather over the gradient buffers (between steps), then one more
@@ -252,7 +256,8 @@ def _gpu_ddp_worker(rank, world, port, backend, q):
                                      eng.scalars.float().cpu())
         report.append(dict(step=4, loss=loss, update=(om - before[0]).abs().max().item(),
                            master_err=((after[0] - om).abs()).max().item(),
-                           master_rel=((after[0] - om).abs() / (om.abs() + 1e-6)).max().item(), m_rel=0.0,
+                           master_rel=((after[0] - om).abs() / (om.abs() + before[0].abs() + 1e-6)).max().item(),
+                           m_rel=0.0,
                            v_rel=0.0, ema_err=0.0, param_ulps=0, ranks_equal=gathered_ok and empty_ok))
     q.put((rank, report))
     eng.release_graph()
