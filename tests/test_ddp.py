@@ -230,7 +230,9 @@ def _gpu_ddp_worker(rank, world, port, backend, q):
         # the update nearly cancels is accurate to the ulp of its inputs, not of the small result)
         mrel = lambda a, b, b0: ((a - b).abs() / (b.abs() + b0.abs() + 1e-6)).max().item()
         pb = eng.flat.param_buf
-        ulps = (pb.view(torch.int16).int() - om.to(torch.bfloat16).view(torch.int16).int()).abs().max().item()
+        # the bf16 parameters are the master rounded: within one bf16 ulp (2^-8 relative) at the scale
+        # of the numbers the update combined
+        ulps = ((pb.float() - om).abs() / (om.abs() + before[0].abs() + 1e-6)).max().item() * 256.0
         others = [torch.zeros_like(pb) for _ in range(world)]
         dist.all_gather(others, pb)
         same = all(torch.equal(others[0], o) for o in others[1:])
@@ -287,7 +289,9 @@ def _run_gpu_ddp(backend):
 def test_ddp_step_matches_fp32_oracle(backend):
     """Each step of either gradient path equals an fp32 oracle applied to the all-gathered bf16
     gradients and the state before the step (eager steps and a CUDA-graph replay): master / Adam
-    moments / EMA to 1e-5 relative, bf16 parameters to 1 ulp of the oracle's master, every rank
+    moments / EMA to 1e-5 relative, bf16 parameters to 1 ulp of the oracle's master (both at the scale
+    of the update's inputs, so that a value the update nearly cancels is not held to the ulp of the
+    small result), every rank
     identical.  The update itself is ~1e-3, so a step that changed nothing would fail."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -299,7 +303,7 @@ def test_ddp_step_matches_fp32_oracle(backend):
             assert r["master_rel"] < 1e-5 and r["master_err"] < 1e-3 * r["update"], r
             assert r["m_rel"] < 1e-4 and r["v_rel"] < 1e-4, r
             assert r["ema_err"] < 1e-5, r
-            assert r["param_ulps"] <= 1, r
+            assert r["param_ulps"] <= 1.0, r
             assert r["ranks_equal"], r
 
 
