@@ -355,6 +355,45 @@ __global__ void small_allreduce_kernel(DdpPeers peers, DdpState st, float* __res
     if (threadIdx.x == 0) *st.small_epoch = epoch + 1;
 }
 
+// Gradient all-reduce (optimizers that need every full gradient matrix, e.g. Muon): after the
+// bucket reduce-scatters, each rank writes its reduced slices, rounded to bf16, into every rank's
+// gradient buffer (16-byte P2P stores), then waits until every rank has delivered its slices and
+// advances the step epoch.  Slices are given as (flat offset, length, shard-local offset).
+struct SliceList {
+    int64_t g_off[kDdpMaxBuckets], len[kDdpMaxBuckets], l_off[kDdpMaxBuckets];
+    int n;
+};
+
+__global__ void __launch_bounds__(256) ddp_grad_allgather_kernel(DdpPeers peers, DdpState st, SliceList sl,
+                                                                 const float* __restrict__ gshard) {
+    const uint32_t epoch = *st.epoch;
+    const int world = peers.world, rank = peers.rank;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int b = 0; b < sl.n; ++b) {
+        const int64_t nvec = sl.len[b] / 8;
+        for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+            float f[8];
+            load8(gshard + sl.l_off[b] + 8 * v, f);
+            const uint4 raw = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                                         pack_bf16x2(f[6], f[7]));
+            for (int j = 0; j < world; ++j)
+                *reinterpret_cast<uint4*>(const_cast<__nv_bfloat16*>(peers.grad[j]) + sl.g_off[b] + 8 * v) = raw;
+        }
+    }
+    __threadfence_system();
+    if (last_cta(st.ticket)) {
+        __threadfence_system();
+        if (threadIdx.x < world) st_release_u32(peers.flags[threadIdx.x] + kFlagDone + rank, epoch);
+        __syncthreads();
+        if (threadIdx.x < world) {
+            if (!wait_u32(st.flags_local + kFlagDone + threadIdx.x, epoch, st.spin_limit))
+                record_error(st.status, kErrTimeoutDone);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) *st.epoch = epoch + 1;
+    }
+}
+
 // Gather barrier: tell every rank (slot `rank` of region `base`) that this rank reached it with the
 // current gather epoch, then wait for every rank's mark; `bump` advances the epoch afterwards.
 __global__ void gather_barrier_kernel(DdpPeers peers, DdpState st, int base, int bump) {
@@ -410,6 +449,25 @@ cudaError_t launch_gather_bytes(const DdpPeers& peers, const DdpState& st, void*
 }
 
 int ddp_rs_blocks(bool overlapped) { return overlapped ? 64 : num_sms() * 2; }
+
+cudaError_t launch_ddp_grad_allgather(const DdpPeers& peers, const DdpState& st, const int64_t* g_off,
+                                      const int64_t* len, const int64_t* l_off, int n, const float* gshard,
+                                      cudaStream_t s) {
+    if (n < 0 || n > kDdpMaxBuckets) return cudaErrorInvalidValue;
+    SliceList sl{};
+    sl.n = n;
+    int64_t total = 0;
+    for (int i = 0; i < n; ++i) {
+        if (g_off[i] % 8 || len[i] % 8 || l_off[i] % 8) return cudaErrorInvalidValue;
+        sl.g_off[i] = g_off[i];
+        sl.len[i] = len[i];
+        sl.l_off[i] = l_off[i];
+        total += len[i];
+    }
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total / 8 + 255) / 256, num_sms() * 4)));
+    ddp_grad_allgather_kernel<<<blocks, 256, 0, s>>>(peers, st, sl, gshard);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_ddp_rs(const DdpPeers& peers, const DdpState& st, int64_t g_off, int64_t len, float* gshard_at,
                           float* partials_b, int bucket, int blocks, cudaStream_t s) {

@@ -59,6 +59,12 @@ cudaError_t launch_ddp_rs(const DdpPeers& peers, const DdpState& st, int64_t g_o
                           float* partials_b, int bucket, int blocks, cudaStream_t s);
 cudaError_t launch_ddp_publish(const DdpPeers& peers, const DdpState& st, const float* partials, int n,
                                cudaStream_t s);
+// After the bucket reduce-scatters: every rank's reduced slices (bf16) into every rank's gradient
+// buffer, so each holds the summed gradient (an all-reduce); then the "delivered" barrier and the
+// epoch advance, as after the optimizer update.
+cudaError_t launch_ddp_grad_allgather(const DdpPeers& peers, const DdpState& st, const int64_t* g_off,
+                                      const int64_t* len, const int64_t* l_off, int n, const float* gshard,
+                                      cudaStream_t s);
 // chunks: (shard-local offset, length, group); gdelta[c]: flat offset - shard-local offset of chunk c
 cudaError_t launch_ddp_update(const DdpPeers& peers, const DdpState& st, const ChunkDesc* chunks, const int64_t* gdelta,
                               int nchunks, const float* gshard, float* master, float* m, float* v, float* ema,

@@ -93,6 +93,15 @@ class DdpComm {
                    "ddp_rs");
     }
 
+    void grad_allgather(std::vector<int64_t> g_off, std::vector<int64_t> len, std::vector<int64_t> l_off,
+                        torch::Tensor gshard) {
+        TORCH_CHECK(g_off.size() == len.size() && len.size() == l_off.size(), "grad_allgather: one entry per slice");
+        TORCH_CHECK(gshard.scalar_type() == torch::kFloat32 && gshard.is_cuda(), "grad_allgather: fp32 shard");
+        check_cuda(launch_ddp_grad_allgather(peers_, st_, g_off.data(), len.data(), l_off.data(),
+                                             static_cast<int>(g_off.size()), gshard.data_ptr<float>(), cur_stream()),
+                   "ddp_grad_allgather");
+    }
+
     void publish(torch::Tensor partials, int64_t n) {
         TORCH_CHECK(partials.scalar_type() == torch::kFloat32 && partials.numel() >= n, "ddp publish: partials");
         check_cuda(launch_ddp_publish(peers_, st_, partials.data_ptr<float>(), static_cast<int>(n), cur_stream()),
@@ -160,6 +169,7 @@ void register_ddp_ops(pybind11::module& m) {
                       int64_t, torch::Tensor, torch::Tensor, torch::Tensor, int64_t>())
         .def("rs", &DdpComm::rs)
         .def("publish", &DdpComm::publish)
+        .def("grad_allgather", &DdpComm::grad_allgather)
         .def("update", &DdpComm::update)
         .def("small_allreduce", &DdpComm::small_allreduce)
         .def("gather_bytes", &DdpComm::gather_bytes);

@@ -118,6 +118,39 @@ class FusedGradSync:
         return raw.view(dtype)[:numel]
 
     def setup(self, engine) -> None:
+        """Sharded mode: peer mappings, buckets, and ZeRO-1 shards of the master weights, Adam
+        moments and EMA (this rank's slice of every bucket)."""
+        dev = self.device
+        self._connect(engine)
+        # identical starting point on every rank
+        dist.broadcast(engine.flat.param_buf, 0, group=self.group)
+        dist.broadcast(engine.master, 0, group=self.group)
+        self._plan(engine)
+        flat = engine.flat
+        S = self.size
+        master = engine.master
+        engine.master_shard = torch.cat([master[a:b] for a, b in self.slices]).contiguous()
+        engine.master = None  # the full fp32 copy is only kept as shards
+        engine.m = torch.zeros(S, dtype=torch.float32, device=dev)
+        engine.v = torch.zeros(S, dtype=torch.float32, device=dev)
+        engine.ema_buf = engine.master_shard.clone() if engine.opts.use_ema else None
+        table = flat.chunk_table()
+        rows, deltas = [], []
+        for (a, b), lo in zip(self.slices, self.local_off):
+            part = shard_chunks(table, a, b - a)
+            for o, n, g in part.tolist():
+                if n:
+                    rows.append((lo + o, n, g))
+                    deltas.append(a - lo)
+        if not rows:
+            rows, deltas = [(0, 0, 0)], [0]
+        self.chunks = torch.tensor(rows, dtype=torch.int64, device=dev)
+        self.gdelta = torch.tensor(deltas, dtype=torch.int64, device=dev)
+        dist.barrier(group=self.group)
+
+    def _connect(self, engine) -> None:
+        """Exchange CUDA-IPC handles of the parameter / gradient / flag / small buffers and build the
+        kernels' peer tables."""
         k = kernels()
         dev = self.device
         flags, fh = k.ipc_alloc(k.ddp_flag_words() * 4, dev.index)
@@ -142,9 +175,32 @@ class FusedGradSync:
         self.ctrl[4] = 1       # byte all-gather epoch
         self.comm = k.DdpComm(ptrs[1], ptrs[0], ptrs[2], ptrs[3], self.rank, self.world_size,
                               flags.view(torch.int32), small.view(torch.float32), self.ctrl, self.spin_limit)
-        # identical starting point on every rank
+
+    def setup_replicated(self, engine) -> None:
+        """Gradient all-reduce only (optimizers that keep every full matrix, e.g. Muon): the same
+        peer mappings and bucket reduce-scatter, then each rank's reduced slices written back into
+        every rank's gradient buffer (``all_reduce_grads``); master weights stay replicated."""
+        self._connect(engine)
         dist.broadcast(engine.flat.param_buf, 0, group=self.group)
         dist.broadcast(engine.master, 0, group=self.group)
+        self._plan(engine)
+        dist.barrier(group=self.group)
+
+    def all_reduce_grads(self, engine) -> None:
+        """Sum of every rank's bf16 gradient buffer, left in every rank's buffer (fp32 accumulation in
+        rank order, rounded to bf16 once)."""
+        if self.failed is not None:
+            raise RuntimeError(f"fused DDP sync is unusable after an earlier failure: {self.failed}")
+        cur = torch.cuda.current_stream(self.device)
+        for j in range(len(self.buckets)):
+            self._launch(j, cur)
+        self.comm.grad_allgather([a for a, _ in self.slices], [b - a for a, b in self.slices], self.local_off,
+                                 self.gshard)
+
+    def _plan(self, engine) -> None:
+        """Buckets, this rank's slices of them, the fp32 shard and the reduction partials."""
+        k = kernels()
+        dev = self.device
         flat = engine.flat
         P = flat.total
         # buckets: the backward pass completes the flat buffer from its end (stage order); mark i
@@ -165,34 +221,15 @@ class FusedGradSync:
             S += b - a
         self.size = S
         self.mark_bucket = {m: j for j, (m, _, _) in enumerate(self.buckets) if m is not None}
-        master = engine.master
-        engine.master_shard = torch.cat([master[a:b] for a, b in self.slices]).contiguous()
-        engine.master = None  # the full fp32 copy is only kept as shards
-        engine.m = torch.zeros(S, dtype=torch.float32, device=dev)
-        engine.v = torch.zeros(S, dtype=torch.float32, device=dev)
-        engine.ema_buf = engine.master_shard.clone() if engine.opts.use_ema else None
         self.gshard = torch.zeros(S, dtype=torch.float32, device=dev)
         # reduce-scatter CTAs per bucket: few for the ones that overlap the backward pass
         self.blocks = [k.ddp_rs_blocks(m is not None) for (m, _, _) in self.buckets]
         self.p_off = [sum(self.blocks[:j]) for j in range(len(self.buckets))]
         self.partials = torch.zeros(sum(self.blocks), dtype=torch.float32, device=dev)
-        table = flat.chunk_table()
-        rows, deltas = [], []
-        for (a, b), lo in zip(self.slices, self.local_off):
-            part = shard_chunks(table, a, b - a)
-            for o, n, g in part.tolist():
-                if n:
-                    rows.append((lo + o, n, g))
-                    deltas.append(a - lo)
-        if not rows:
-            rows, deltas = [(0, 0, 0)], [0]
-        self.chunks = torch.tensor(rows, dtype=torch.int64, device=dev)
-        self.gdelta = torch.tensor(deltas, dtype=torch.int64, device=dev)
         self._stage = flat.grad_buf.view(torch.uint8)   # byte all-gather staging (between steps)
         self.side = torch.cuda.Stream(dev)
         if marks:
             model.set_grad_marks(self._on_mark)
-        dist.barrier(group=self.group)
 
     # ---------------------------------------------------------------- step
     def all_reduce_small(self, t: torch.Tensor) -> torch.Tensor:

@@ -153,8 +153,6 @@ class TrainEngine:
         if self.opts.optimizer == "muon":
             # Muon runs eagerly on the master weights (fp32 views into the flat buffer)
             from .muon import MuonAux
-            if self.grad_sync is not None and type(self.grad_sync).__name__ != "NcclGradSync":
-                raise ValueError("muon runs with the NCCL all-reduce gradient sync (--ddp-backend nccl)")
             shapes = dict((n, p.shape) for n, p in named_dev)
             self.muon = MuonAux(self.flat.names, [self.flat.view(master, i).view(shapes[n])
                                                   for i, n in enumerate(self.flat.names)],
@@ -164,6 +162,9 @@ class TrainEngine:
             self._alloc_readback()
             if self.grad_sync is not None:
                 self.grad_sync.muon_mode = True
+                if hasattr(self.grad_sync, "setup_replicated"):
+                    # the fused sync as a gradient all-reduce over peer memory (replicated Muon)
+                    self.grad_sync.setup_replicated(self)
             return
         if self.grad_sync is not None:
             self.grad_sync.setup(self)
@@ -225,7 +226,10 @@ class TrainEngine:
         o = self.opts
         g = self.flat.grad_buf
         if self.grad_sync is not None:
-            torch.distributed.all_reduce(g, group=self.grad_sync.group)
+            if hasattr(self.grad_sync, "all_reduce_grads"):
+                self.grad_sync.all_reduce_grads(self)      # in-kernel, over NVSwitch peer memory
+            else:
+                torch.distributed.all_reduce(g, group=self.grad_sync.group)
         gf = g.float()
         if self.world > 1:
             gf.div_(self.world)

@@ -299,7 +299,7 @@ def _train(opts: TrainOptions, ctx: DistContext, paths: Dict[str, str], progress
     total_steps = max(1, steps_per_epoch * opts.epochs)
     grad_sync = None
     if ctx.enabled:
-        if ctx.device.type == "cuda" and opts.ddp_backend == "fused" and opts.optimizer == "adamw":
+        if ctx.device.type == "cuda" and opts.ddp_backend == "fused":
             from ..parallel.fused import FusedGradSync
             grad_sync = FusedGradSync()
         else:

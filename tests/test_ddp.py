@@ -249,6 +249,20 @@ def _gpu_ddp_worker(rank, world, port, backend, q):
             torch.equal(parts[j], torch.arange((j + 3) * 5, dtype=torch.float64).view(-1, 5) + 1000 * j)
             for j in range(world))
         empty_ok = all(p.shape == (0, 5) for p in sync.all_gather_tensor(torch.zeros(0, 5, dtype=torch.float64)))
+        # the in-kernel gradient all-reduce (Muon's sync): every rank's buffer ends as the bf16 rounding
+        # of the fp32 sum in rank order, bit for bit
+        gen = torch.Generator(device="cuda").manual_seed(100 + rank)
+        mine_g = torch.randn(eng.flat.grad_buf.numel(), device="cuda", generator=gen).bfloat16()
+        every = [torch.zeros_like(mine_g) for _ in range(world)]
+        dist.all_gather(every, mine_g)
+        eng.flat.grad_buf.copy_(mine_g)
+        sync.all_reduce_grads(eng)
+        torch.cuda.synchronize()
+        expect = every[0].float()
+        for t in every[1:]:
+            expect = expect + t.float()
+        allreduce_ok = torch.equal(eng.flat.grad_buf, expect.bfloat16()) and int(sync.ctrl[3]) == 0
+        gathered_ok = gathered_ok and allreduce_ok
         before = state()
         loss = eng.step(imgs, tg).loss
         after = state()
