@@ -54,6 +54,10 @@ constexpr int kThreads = 320;                      // 2 producer/MMA warps + 8 e
 constexpr int kEpiWarps = 8;
 constexpr int kStageWords = 32 * 17;               // per-warp epilogue staging tile, padded rows
 constexpr int kStagingBytes = kEpiWarps * kStageWords * 4;
+// single-CTA kernel: two 32 x 32 bf16 tiles per epilogue warp, 64-byte rows in the TMA store's
+// 64-byte swizzle (the tensor store clips rows / columns past the output, so tails need no masks)
+constexpr int kTmaTileBytes = 32 * 64;
+constexpr int kTmaStagingBytes = kEpiWarps * 2 * kTmaTileBytes;
 constexpr int kMaxStages = 6;
 constexpr int kSmemLimit = 227 * 1024;
 
@@ -63,12 +67,12 @@ struct Tile {
     static constexpr int BN = BN_;
     static constexpr int kBTile = BN * BK * 2;
     static constexpr int kStageBytes = kATile + kBTile;
-    static constexpr int kStages =
-        (kSmemLimit - kStagingBytes - 2048) / kStageBytes < kMaxStages ? (kSmemLimit - kStagingBytes - 2048) / kStageBytes
-                                                                         : kMaxStages;
+    static constexpr int kStages = (kSmemLimit - kTmaStagingBytes - 2048) / kStageBytes < kMaxStages
+                                       ? (kSmemLimit - kTmaStagingBytes - 2048) / kStageBytes
+                                       : kMaxStages;
     static constexpr int kAccCols = BN;            // fp32 accumulator columns per buffer
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
-    static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + kStagingBytes + 1024 + 256;
+    static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + kTmaStagingBytes + 1024 + 256;
 };
 
 struct __align__(8) SmemCtl {
@@ -104,30 +108,66 @@ __device__ __forceinline__ void stage_store(uint32_t* stg, int lane, const float
     __syncwarp();
 }
 
-__device__ __forceinline__ void stage_load(uint32_t* stg, int lane, float* x, const __nv_bfloat16* base, int64_t ld,
-                                           int rows_valid, int ncols) {
-    const int seg = lane & 3;
+// This lane's row of a 32-row x `ncols` bf16 block (lane = row), straight from global memory: 16-byte
+// loads of the row's contiguous 64 bytes (the rows' sectors are read whole across the 4 loads).
+__device__ __forceinline__ void row_load(int lane, float* x, const __nv_bfloat16* base, int64_t ld, int rows_valid,
+                                        int ncols) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int r = 8 * i + (lane >> 2);
+    for (int j = 0; j < 4; ++j) {
         uint4 w = make_uint4(0, 0, 0, 0);
-        if (r < rows_valid && seg * 8 < ncols) w = *reinterpret_cast<const uint4*>(base + r * ld + seg * 8);
-        uint32_t* dst = stg + r * 17 + seg * 4;
-        dst[0] = w.x; dst[1] = w.y; dst[2] = w.z; dst[3] = w.w;
-    }
-    __syncwarp();
+        if (lane < rows_valid && 8 * j < ncols) w = *reinterpret_cast<const uint4*>(base + lane * ld + 8 * j);
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int w = 0; w < 16; ++w) {
-        const float2 t = unpack_bf16x2(stg[lane * 17 + w]);
-        x[2 * w] = t.x;
-        x[2 * w + 1] = t.y;
+        for (int i = 0; i < 4; ++i) {
+            const float2 t = unpack_bf16x2(u[i]);
+            x[8 * j + 2 * i] = t.x;
+            x[8 * j + 2 * i + 1] = t.y;
+        }
     }
+}
+
+// Where one epilogue warp's chunks go: the single-CTA kernel stores through 3-D tensor maps
+// (column, row, batch) from two rotating swizzled tiles; the CTA-pair kernel through the padded
+// staging tile and row-segment stores.
+struct EpiOut {
+    uint32_t* stg;
+    unsigned char* tbuf;                 // two kTmaTileBytes tiles, or null
+    const CUtensorMap* mapC;
+    const CUtensorMap* mapAux;
+    int bt;
+    int turn;
+};
+
+// Tensor store of this warp's 32 x 32 block (lane = row, x = 32 values) at (col, row0, batch bt).
+__device__ __forceinline__ void tma_store_tile(EpiOut& eo, const CUtensorMap* map, int lane, const float* x, int col,
+                                               int row0) {
+    unsigned char* buf = eo.tbuf + eo.turn * kTmaTileBytes;
+    // the store issued from this tile two chunks ago has finished reading it
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
     __syncwarp();
+    unsigned char* rowp = buf + lane * 64;
+    const int sw = (lane >> 1) & 3;     // 64-byte swizzle: 16-byte chunk c of row r at c ^ ((r >> 1) & 3)
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(rowp + ((c ^ sw) << 4)) =
+            make_uint4(pack_bf16x2(x[8 * c], x[8 * c + 1]), pack_bf16x2(x[8 * c + 2], x[8 * c + 3]),
+                       pack_bf16x2(x[8 * c + 4], x[8 * c + 5]), pack_bf16x2(x[8 * c + 6], x[8 * c + 7]));
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+        asm volatile(
+            "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+            "r"(smem_u32(buf)), "r"(col), "r"(row0), "r"(eo.bt)
+            : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    eo.turn ^= 1;
 }
 
 // Epilogue of one warp's 32 rows x `ncols` (16 or 32) columns; lane = row.
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg, int lane, int row0, int col,
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, EpiOut& eo, int lane, int row0, int col,
                                                int ncols, float* v, bool rmax_first = true) {
+    uint32_t* stg = eo.stg;
     const int rows_valid = min(32, g.M - row0);
     const int row = row0 + lane;
     if (g.ws) {  // split-K partial: fp32 vector atomics into the workspace
@@ -165,7 +205,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg,
         }
         return;
     }
-    if (g.aux) stage_store(stg, lane, v, g.aux + base, g.ldc, rows_valid, ncols);  // pre-activation for backward
+    if (g.aux) {   // pre-activation for backward
+        if (eo.tbuf) tma_store_tile(eo, eo.mapAux, lane, v, col, row0);
+        else stage_store(stg, lane, v, g.aux + base, g.ldc, rows_valid, ncols);
+    }
     if (g.epi == 1) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = gelu_f(v[i]);
@@ -174,7 +217,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg,
         for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.f);
     } else if (g.epi == 3) {
         float r[32];
-        stage_load(stg, lane, r, g.res + base, g.ldc, rows_valid, ncols);
+        row_load(lane, r, g.res + base, g.ldc, rows_valid, ncols);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             if (8 * j < ncols) {
@@ -186,13 +229,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg,
         }
     } else if (g.epi == 6) {
         float r[32];
-        stage_load(stg, lane, r, g.res + base, g.ldc, rows_valid, ncols);
+        row_load(lane, r, g.res + base, g.ldc, rows_valid, ncols);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = g.alpha * v[i] + g.beta * r[i];
     } else if (g.epi == 4 || g.epi == 5) {
         // activation backward: the product is the gradient w.r.t. the activation output
         float p[32];
-        stage_load(stg, lane, p, g.res + base, g.ldc, rows_valid, ncols);
+        row_load(lane, p, g.res + base, g.ldc, rows_valid, ncols);
         if (g.epi == 4) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= gelu_grad_f(p[i]);
@@ -201,14 +244,23 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t* stg,
             for (int i = 0; i < 32; ++i) v[i] = p[i] > 0.f ? v[i] : 0.f;
         }
     }
-    stage_store(stg, lane, v, g.C + base, g.ldc, rows_valid, ncols);
+    if (eo.tbuf) tma_store_tile(eo, eo.mapC, lane, v, col, row0);
+    else stage_store(stg, lane, v, g.C + base, g.ldc, rows_valid, ncols);
     if (g.colacc) {
-        // column sums of the stored tile (the staging buffer still holds it): lane = column
+        // column sums of the stored (bf16-rounded) tile, read back from the staging: lane = column
         if (lane < ncols) {
             float s = 0.f;
-            for (int r = 0; r < rows_valid; ++r) {
-                const float2 t = unpack_bf16x2(stg[r * 17 + (lane >> 1)]);
-                s += (lane & 1) ? t.y : t.x;
+            if (eo.tbuf) {
+                const unsigned char* buf = eo.tbuf + (eo.turn ^ 1) * kTmaTileBytes;   // the tile just stored
+                for (int r = 0; r < rows_valid; ++r) {
+                    const unsigned char* p = buf + r * 64 + ((((lane >> 3) ^ ((r >> 1) & 3))) << 4) + (lane & 7) * 2;
+                    s += __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(p));
+                }
+            } else {
+                for (int r = 0; r < rows_valid; ++r) {
+                    const float2 t = unpack_bf16x2(stg[r * 17 + (lane >> 1)]);
+                    s += (lane & 1) ? t.y : t.x;
+                }
             }
             atomicAdd(g.colacc + col + lane, s);
         }
@@ -231,7 +283,9 @@ struct Sched {
 
 template <bool A_MN, bool B_MN, int BN_>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                              const __grid_constant__ CUtensorMap tmB, GemmArgs g,
+                                                              const __grid_constant__ CUtensorMap tmB,
+                                                              const __grid_constant__ CUtensorMap tmC,
+                                                              const __grid_constant__ CUtensorMap tmAux, GemmArgs g,
                                                               Sched sch) {
     using T = Tile<BN_>;
     constexpr int BN = T::BN, kStages = T::kStages, kBTile = T::kBTile, kAccCols = T::kAccCols;
@@ -239,8 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* tilesA = smem;
     unsigned char* tilesB = smem + kStages * kATile;
-    uint32_t* staging = reinterpret_cast<uint32_t*>(smem + kStages * (kATile + kBTile));
-    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(reinterpret_cast<unsigned char*>(staging) + kStagingBytes);
+    unsigned char* tstage = smem + kStages * (kATile + kBTile);     // 1024-aligned TMA store tiles
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(tstage + kTmaStagingBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int units = sch.m_tiles * sch.n_tiles * sch.splits * g.batch;
@@ -355,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         // tile's rows) and half of the tile's columns, 32 columns per tcgen05.wait
         const int q = warp & 3;
         const int half = (warp - 2) >> 2;
-        uint32_t* stg = staging + (warp - 2) * kStageWords;
+        EpiOut eo{nullptr, tstage + (warp - 2) * 2 * kTmaTileBytes, &tmC, &tmAux, 0, 0};
         int local = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
             int m0, n0, kt0, kt1;
@@ -371,9 +425,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             const int row0 = m0 + 32 * q;
             const uint32_t acc = tmem + buf * kAccCols + (static_cast<uint32_t>(32 * q) << 16);
             constexpr int kHalfCols = BN / 2;
-            // this unit's batch: outputs (and the epilogue's side inputs) at their batch offsets
+            // this unit's batch: outputs (and the epilogue's side inputs) at their batch offsets; the
+            // tensor stores address the batch by their third coordinate
             GemmArgs gb = g;
             const int bt = sch.batch_of(u);
+            eo.bt = bt;
             if (bt) {
                 gb.C += bt * g.bs_c;
                 if (gb.aux) gb.aux += bt * g.bs_c;
@@ -391,13 +447,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                     tmem_ld16(acc + c, v);
                 }
                 if (g.diag & 1) continue;
-                epilogue_chunk(gb, stg, lane, row0, n0 + c, ncols, v, c == half * kHalfCols);
+                epilogue_chunk(gb, eo, lane, row0, n0 + c, ncols, v, c == half * kHalfCols);
             }
             // accumulator buffer free again
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctl->acc_empty[buf]);
         }
+        // every tensor store of this warp has completed before the CTA (and its shared memory) ends
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -625,7 +684,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // lane quadrant w % 4 and half (w - 2) / 4 of the columns
         const int q = warp & 3;
         const int half = (warp - 2) >> 2;
-        uint32_t* stg = staging + (warp - 2) * kStageWords;
+        EpiOut eo{staging + (warp - 2) * kStageWords, nullptr, nullptr, nullptr, 0, 0};
         int local = 0;
         for (int u = pair; u < units; u += npairs, ++local) {
             int m0, n0, kt0, kt1;
@@ -650,7 +709,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 } else {
                     tmem_ld16(acc + c, v);
                 }
-                epilogue_chunk(g, stg, lane, row0, n0 + c, ncols, v);
+                epilogue_chunk(g, eo, lane, row0, n0 + c, ncols, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -702,6 +761,27 @@ bool make_map(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, i
         std::fprintf(stderr, "gemm_tc: cuTensorMapEncodeTiled failed (%d): inner %lld outer %lld pitch %lld box %d\n",
                      static_cast<int>(r), static_cast<long long>(inner), static_cast<long long>(outer),
                      static_cast<long long>(pitch), box_rows);
+    return r == CUDA_SUCCESS;
+}
+
+// Output map for the epilogue's tensor stores: bf16 [batch, rows, cols] (row pitch `pitch`, batch
+// stride `bstride`, elements), 32 x 32 boxes, 64-byte swizzle; stores past the extents are clipped.
+bool make_store_map(CUtensorMap* map, const void* ptr, int64_t cols, int64_t rows, int64_t batch, int64_t pitch,
+                    int64_t bstride) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                          static_cast<cuuint64_t>(std::max<int64_t>(1, batch))};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(pitch * 2), static_cast<cuuint64_t>(bstride * 2)};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        std::fprintf(stderr, "gemm_tc: output tensor map failed (%d): cols %lld rows %lld batch %lld pitch %lld\n",
+                     static_cast<int>(r), static_cast<long long>(cols), static_cast<long long>(rows),
+                     static_cast<long long>(batch), static_cast<long long>(pitch));
     return r == CUDA_SUCCESS;
 }
 
@@ -848,6 +928,15 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
         e = cudaMemsetAsync(g.ws, 0, static_cast<size_t>(g.M) * g.ldc * sizeof(float), st);
         if (e != cudaSuccess) return e;
     }
+    // output tensor maps of the single-CTA kernel's epilogue (C, pre-activation): 32 x 32 boxes over
+    // [batch, M, N] (pitch ldc, batch stride bs_c), 64-byte swizzle
+    CUtensorMap tc_map{}, taux_map{};
+    if (!plan.pair && g.ws == nullptr && g.epi != 7) {
+        const int64_t bs = g.batch > 1 ? g.bs_c : static_cast<int64_t>(g.M) * g.ldc;
+        ok = make_store_map(&tc_map, g.C, g.N, g.M, g.batch, g.ldc, bs);
+        ok = ok && (g.aux == nullptr || make_store_map(&taux_map, g.aux, g.N, g.M, g.batch, g.ldc, bs));
+        if (!ok) return cudaErrorInvalidValue;
+    }
     auto launch = [&](auto kern, size_t smem) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) {
@@ -857,13 +946,22 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
         kern<<<grid, kThreads, smem, st>>>(ta, tb, g, sch);
         e = cudaGetLastError();
     };
+    auto launch1 = [&](auto kern, size_t smem) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) {
+            std::fprintf(stderr, "gemm_tc: cudaFuncSetAttribute(%zu bytes) failed: %s\n", smem, cudaGetErrorString(e));
+            return;
+        }
+        kern<<<grid, kThreads, smem, st>>>(ta, tb, tc_map, taux_map, g, sch);
+        e = cudaGetLastError();
+    };
     auto by_major = [&](auto bnc) {
         constexpr int BNv = decltype(bnc)::value;
         const size_t smem = Tile<BNv>::kSmemBytes;
-        if (!a_mn && !b_mn) launch(gemm_tc_kernel<false, false, BNv>, smem);
-        else if (!a_mn && b_mn) launch(gemm_tc_kernel<false, true, BNv>, smem);
-        else if (a_mn && b_mn) launch(gemm_tc_kernel<true, true, BNv>, smem);
-        else launch(gemm_tc_kernel<true, false, BNv>, smem);
+        if (!a_mn && !b_mn) launch1(gemm_tc_kernel<false, false, BNv>, smem);
+        else if (!a_mn && b_mn) launch1(gemm_tc_kernel<false, true, BNv>, smem);
+        else if (a_mn && b_mn) launch1(gemm_tc_kernel<true, true, BNv>, smem);
+        else launch1(gemm_tc_kernel<true, false, BNv>, smem);
     };
     auto by_major_pair = [&](auto bnc) {
         constexpr int BNv = decltype(bnc)::value;

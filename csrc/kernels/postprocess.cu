@@ -54,9 +54,17 @@ __global__ void __launch_bounds__(kThreads) topk_post_kernel(const LT* __restric
         for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix, mask = s_mask;
-        for (int64_t i = tid; i < N; i += kThreads) {
-            const uint32_t k = order_key(ld(x, i));
-            if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 0xffu], 1u);
+        // warp-aggregated counting: the logits of one image share a few leading digits, so most lanes
+        // of a warp hit the same bin; one shared atomic per distinct bin instead of one per lane
+        const int64_t span = (N + 31) / 32 * 32;    // every lane of a warp takes part in each round
+        for (int64_t i = tid; i < span; i += kThreads) {
+            uint32_t bin = 0xffffffffu;
+            if (i < N) {
+                const uint32_t k = order_key(ld(x, i));
+                if ((k & mask) == prefix) bin = (k >> shift) & 0xffu;
+            }
+            const uint32_t same = __match_any_sync(0xffffffffu, bin);
+            if (bin != 0xffffffffu && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
         }
         __syncthreads();
         if (tid == 0) {

@@ -317,6 +317,7 @@ def bench_kernels(device="cuda", quick=False):
     on the device): LayerNorm forward / backward on the ViT shape, the criterion (matcher cost + GPU
     assignment solver + fused matched losses, forward and backward) on RF-DETR-M's training outputs,
     and the top-k post-process.  ``quick``: three launches of each, untimed (profiler captures)."""
+    from ._ext import kernels
     from .norm import layer_norm
     from ..infer.postprocess import postprocess
     g = torch.Generator(device=device).manual_seed(0)
@@ -338,8 +339,22 @@ def bench_kernels(device="cuda", quick=False):
     def post():
         postprocess({"pred_logits": logits, "pred_boxes": boxes}, 100, (560, 560), masks=False)
 
+    # single-launch column reductions: the decoder FFN's ReLU backward with its bias gradient, and
+    # the ViT MLP's bias gradient (column sum of the 1536-wide gradient)
+    k = kernels()
+    g_relu = torch.randn(31200, 2048, device=device, generator=g).bfloat16()
+    pre_relu = torch.randn(31200, 2048, device=device, generator=g).bfloat16()
+    g_mlp = torch.randn(10400, 1536, device=device, generator=g).bfloat16()
+
+    def relu_bwd_bias():
+        k.act_bwd_bias(g_relu, pre_relu, 2)
+
+    def colsum():
+        k.colsum(g_mlp, torch.float32)
+
     cases = [("layer_norm.fwd_bwd.vit-384", ln), ("criterion.fwd_bwd.rf-detr-m-b8", crit_step),
-             ("postprocess.topk100.b8", post)]
+             ("postprocess.topk100.b8", post), ("colreduce.relu_bwd_bias.dec-ffn1-31200x2048", relu_bwd_bias),
+             ("colreduce.colsum.vit-mlp-10400x1536", colsum)]
     rows = []
     for name, fn in cases:
         if quick:
