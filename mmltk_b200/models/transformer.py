@@ -247,6 +247,30 @@ class GroupedLinear(nn.Module):
         return grouped_linear(x, self.weight[:groups], self.bias[:groups], act)
 
 
+class _GroupedLinearFn(torch.autograd.Function):
+    """y[g] = x[g] w[g]^T + b[g] for stacked x [G, R, din], w [G, dout, din], b [G, dout].
+    Forward and input gradient run as batched products on the tcgen05 kernel (``bmm_nt`` /
+    ``bmm_nn_mn``, library GEMM where the kernel does not take the shape); the weight gradient
+    reduces over the R rows of every group (not a multiple of 64 in general) on the library's
+    batched GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, w, b):
+        from ..ops.gemm import bmm_nt
+        ctx.save_for_backward(x, w)
+        return bmm_nt(x, w, b)
+
+    @staticmethod
+    def backward(ctx, gy):
+        from ..ops.gemm import bmm_nn_mn
+        x, w = ctx.saved_tensors
+        gy = gy.contiguous()
+        dx = bmm_nn_mn(gy, w) if ctx.needs_input_grad[0] else None
+        dw = torch.bmm(gy.transpose(1, 2), x) if ctx.needs_input_grad[1] else None
+        db = gy.sum(1) if ctx.needs_input_grad[2] else None
+        return dx, dw, db
+
+
 def grouped_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, act=None) -> torch.Tensor:
     """Per-group affine maps: x [G, B, N, din] or [B, N, din] (shared), w [G, dout, din], b [G, dout]."""
     w = w.to(x.dtype)
@@ -257,12 +281,18 @@ def grouped_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, act=None) 
         w = F.pad(w, (0, 0, 0, pad))
         b = F.pad(b, (0, pad))
     G = w.shape[0]
-    if x.dim() == 3:
+    shared = x.dim() == 3
+    if shared:
         B, N, C = x.shape
         x = x.unsqueeze(0).expand(G, B, N, C)
     _, B, N, C = x.shape
-    # batched GEMM with the bias folded in (beta = 1 on a broadcast bias)
-    y = torch.baddbmm(b[:, None, :], x.reshape(G, B * N, C), w.transpose(1, 2)).view(G, B, N, -1)
+    if x.is_cuda and x.dtype == torch.bfloat16 and not shared:
+        # batched tcgen05 products: forward and input gradient on the framework's kernel
+        y = _GroupedLinearFn.apply(x.reshape(G, B * N, C).contiguous(), w.contiguous(), b.contiguous())
+        y = y.view(G, B, N, -1)
+    else:
+        # batched GEMM with the bias folded in (beta = 1 on a broadcast bias)
+        y = torch.baddbmm(b[:, None, :], x.reshape(G, B * N, C), w.transpose(1, 2)).view(G, B, N, -1)
     if pad:
         y = y[..., :dout]
     if act == "relu":
