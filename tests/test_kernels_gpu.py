@@ -592,3 +592,26 @@ def test_newton_schulz_gpu_matches_fp32(cuda_device, nb, r, c):
         x = a * x + (b * gm + cc * gm @ gm) @ x
     err = ((got - x).norm() / x.norm()).item()
     assert err < 5e-2, err
+
+
+@pytest.mark.parametrize("dout", [256, 96, 4])
+def test_grouped_linear_gpu_vs_fp32(cuda_device, dout):
+    """The two-stage head's per-group linears (batched tcgen05 forward / input gradient, library
+    weight gradient) against fp32 autograd."""
+    from mmltk_b200.models.transformer import grouped_linear
+    g = torch.Generator().manual_seed(dout)
+    G, B, N, C = 13, 2, 150, 256
+    x = torch.randn(G, B, N, C, generator=g)
+    w = torch.randn(G, dout, C, generator=g) * C ** -0.5
+    b = torch.randn(G, dout, generator=g)
+    gy = torch.randn(G, B, N, dout, generator=g)
+    xr, wr, br = (t.clone().requires_grad_() for t in (x, w, b))
+    ref = torch.einsum("gbnc,gdc->gbnd", xr, wr) + br[:, None, None, :]
+    ref.backward(gy)
+    xd, wd, bd = (t.to(cuda_device).bfloat16().requires_grad_() for t in (x, w, b))
+    y = grouped_linear(xd, wd, bd)
+    y.backward(gy.to(cuda_device).bfloat16())
+    torch.cuda.synchronize()
+    assert kernels().gemm_tc_status(0) == 0
+    for got, want in ((y, ref), (xd.grad, xr.grad), (wd.grad, wr.grad), (bd.grad, br.grad)):
+        assert _rel(got.float().cpu(), want.detach()) < 2e-2
