@@ -159,8 +159,7 @@ class DecoderLayer(nn.Module):
         x, x_pos = ops.add_layer_norm(tgt, sa, self.norm1.weight, self.norm1.bias, 1e-5, pos=query_pos, rbias=sa_b)
         ca, ca_b = self.cross_attn(x_pos, ref, memory, shapes, padding_mask, defer_bias=True)
         x = ops.add_layer_norm(x, ca, self.norm2.weight, self.norm2.bias, 1e-5, rbias=ca_b)
-        h = ops.linear(x, self.linear1.weight, self.linear1.bias, act="relu")
-        h = ops.linear(h, self.linear2.weight, None)
+        h = ops.mlp_relu(x, self.linear1.weight, self.linear1.bias, self.linear2.weight)
         if want_pos:
             return ops.add_layer_norm(x, h, self.norm3.weight, self.norm3.bias, 1e-5, pos=query_pos,
                                       rbias=self.linear2.bias)

@@ -25,11 +25,13 @@ from ._ext import kernels
 from .gemm import _fits_nt, gemm_nn, gemm_nt, gemm_nt_epilogue, gemm_tn, gemm_tn_acc, tc_gemm_enabled
 from .gradacc import grad_target
 
-__all__ = ["linear", "linear_scale_residual", "mlp_scale_residual", "set_fused_linear"]
+__all__ = ["linear", "linear_scale_residual", "mlp_scale_residual", "mlp_relu", "set_fused_linear"]
 
 _ACTS = {None: 0, "none": 0, "gelu": 1, "relu": 2}
+_COLSUM_CAP = 16384   # widest output whose column sums the GEMM epilogue accumulates (its fp32 scratch)
 _state = {"enabled": os.environ.get("MMLTK_FUSED_LINEAR", "1") != "0",
-          "fused_mlp": os.environ.get("MMLTK_FUSED_MLP", "0") == "1"}
+          "fused_mlp": os.environ.get("MMLTK_FUSED_MLP", "0") == "1",
+          "fused_ffn": os.environ.get("MMLTK_FUSED_FFN", "1") != "0"}
 
 
 def set_fused_linear(flag: bool) -> None:
@@ -217,3 +219,51 @@ def mlp_scale_residual(x, w1, b1, w2, b2, gamma, res):
             return _MlpScaleResidual.apply(x, w1, b1, w2, b2, gamma, res)
     h = linear(x, w1, b1, act="gelu")
     return linear_scale_residual(h, w2, b2, gamma, res)
+
+
+class _MlpRelu(torch.autograd.Function):
+    """out = ReLU(x W1^T + b1) W2^T -- the decoder FFN (its output bias is added by the following
+    norm) as one autograd node.  Forward: the first product with the ReLU in the tcgen05 epilogue
+    (only h is stored: h > 0 <=> pre > 0).  Backward: the second layer's input-gradient GEMM applies
+    the ReLU mask of h in its epilogue and sums the first layer's bias gradient from the stored
+    tile (epilogue 5 + column sums), so the [tokens, 2048] gradient is written once and never
+    re-read for the activation backward."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2):
+        shp = x.shape
+        x2 = _2d(x, shp[-1])
+        h, _ = gemm_nt_epilogue(x2, w1, b1, "relu", want_pre=False, force=True)
+        out = gemm_nt(h, w2)
+        ctx.save_for_backward(x2, w1, h, w2)
+        ctx.params = (w1, b1, w2)
+        ctx.shp = shp
+        return out.view(*shp[:-1], w2.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, w1, h, w2 = ctx.saved_tensors
+        k = kernels()
+        wt1, bt1, wt2 = (grad_target(p) for p in ctx.params)
+        g = _2d(gy, w2.shape[0])
+        gw2 = gemm_tn(g, h) if wt2 is None else gemm_tn_acc(g, h, wt2)
+        gb1 = bt1 if bt1 is not None else torch.empty(w1.shape[0], device=g.device, dtype=w1.dtype)
+        # dh = g W2 with the ReLU mask and the bias-gradient column sums in the GEMM epilogue
+        g_pre1 = k.gemm_tc(g, w2, None, False, True, 5, False, h, None, gb1, bt1 is not None)[0]
+        gw1 = gemm_tn(g_pre1, x2) if wt1 is None else gemm_tn_acc(g_pre1, x2, wt1)
+        gx = gemm_nn(g_pre1, w1)
+        none_if = lambda t, v: None if t is not None else v
+        return gx.view(ctx.shp), none_if(wt1, gw1), none_if(bt1, gb1), none_if(wt2, gw2)
+
+
+def mlp_relu(x, w1, b1, w2):
+    """ReLU(x W1^T + b1) W2^T (no output bias), the decoder FFN; one fused autograd node on the
+    tcgen05 GEMM where the shapes fit (``MMLTK_FUSED_FFN=0``: two separate linears)."""
+    if (_state["fused_ffn"] and _ok(x, w1) and _ok(x, w2.new_empty(8, w2.shape[1])) and tc_gemm_enabled()
+            and w1.shape[0] % 128 == 0 and w1.shape[0] <= _COLSUM_CAP and torch.is_grad_enabled()):
+        x2 = x.reshape(-1, x.shape[-1])
+        if _fits_nt(x2 if x2.is_contiguous() else x2.contiguous(), w1):
+            return _MlpRelu.apply(x, w1, b1, w2)
+    h = linear(x, w1, b1, act="relu")
+    return linear(h, w2, None)
+

@@ -314,7 +314,9 @@ def test_ddp_step_matches_fp32_oracle(backend):
         for r in report:
             assert math.isfinite(r["loss"]), r
             assert r["update"] > 1e-4, r
-            assert r["master_rel"] < 1e-5 and r["master_err"] < 1e-3 * r["update"], r
+            # 3e-5: a master value near zero whose gradient is near zero takes an Adam step in the
+            # epsilon regime, where the kernel's flushed denormals and the CPU oracle's kept ones differ
+            assert r["master_rel"] < 3e-5 and r["master_err"] < 1e-3 * r["update"], r
             assert r["m_rel"] < 1e-4 and r["v_rel"] < 1e-4, r
             assert r["ema_err"] < 1e-5, r
             assert r["param_ulps"] <= 1.0, r
@@ -351,3 +353,57 @@ def test_worker_argv_rewrite():
     assert out[:4] == ["rfdetr", "train", "--epochs", "2"]
     assert out[out.index("--dist-rank") + 1] == "1" and out[out.index("--device-id") + 1] == "1"
     assert out.count("--workers") == 1 and out[out.index("--workers") + 1] == "4"
+
+
+def _muon_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    sys.path.insert(0, ROOT)
+    import datetime
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    from mmltk_b200.config import TrainOptions, config_from_preset
+    from mmltk_b200.data.synthetic import synthetic_batch
+    from mmltk_b200.models import RFDETR
+    from mmltk_b200.parallel.fused import FusedGradSync
+    from mmltk_b200.train.engine import TrainEngine
+    torch.manual_seed(0)
+    cfg = config_from_preset("rf-detr-medium", group_detr=2, dec_layers=2, resolution=256,
+                             positional_encoding_size=16)
+    sync = FusedGradSync()
+    eng = TrainEngine(RFDETR(cfg), TrainOptions(optimizer="muon", lr=1e-3, use_ema=True, cuda_graph=False), "cuda",
+                      grad_sync=sync, max_targets=6)
+    eng.bind_static_inputs(2, 3, 256, 256)
+    imgs, tg = synthetic_batch(2, 256, seed=20 + rank, kmax=6, slots=6, dtype=torch.bfloat16)
+    before = eng.flat.param_buf.clone()
+    losses = [eng.step(imgs.cuda(), tg.to("cuda")).loss for _ in range(3)]
+    pb = eng.flat.param_buf
+    others = [torch.zeros_like(pb) for _ in range(world)]
+    dist.all_gather(others, pb)
+    q.put((rank, dict(losses=losses, moved=(pb.float() - before.float()).abs().max().item(),
+                      same=all(torch.equal(others[0], o) for o in others[1:]), status=int(sync.ctrl[3]))))
+    sync.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_muon_with_fused_sync_keeps_ranks_identical():
+    """Muon (replicated master weights) with the in-kernel gradient all-reduce: three steps, every
+    rank's parameters identical and updated, finite losses, no wait gave up."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_muon_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=600) for _ in procs], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for _, r in res:
+        assert all(math.isfinite(x) for x in r["losses"]), r
+        assert r["moved"] > 1e-5 and r["same"] and r["status"] == 0, r

@@ -615,3 +615,27 @@ def test_grouped_linear_gpu_vs_fp32(cuda_device, dout):
     assert kernels().gemm_tc_status(0) == 0
     for got, want in ((y, ref), (xd.grad, xr.grad), (wd.grad, wr.grad), (bd.grad, br.grad)):
         assert _rel(got.float().cpu(), want.detach()) < 2e-2
+
+
+@pytest.mark.parametrize("M", [31200, 300])
+def test_mlp_relu_matches_fp32(cuda_device, M):
+    """The decoder FFN node (ReLU in the first product's epilogue; the ReLU mask and the first
+    bias's gradient in the second product's input-gradient epilogue) against fp32 autograd."""
+    g = torch.Generator().manual_seed(M)
+    K, H = 256, 2048
+    bf = lambda t: t.to(torch.bfloat16).float()
+    x = bf(torch.randn(M, K, generator=g))
+    w1, b1 = bf(torch.randn(H, K, generator=g) * K ** -0.5), bf(torch.randn(H, generator=g) * 0.1)
+    w2 = bf(torch.randn(K, H, generator=g) * H ** -0.5)
+    gy = bf(torch.randn(M, K, generator=g))
+    ins = [t.clone().requires_grad_() for t in (x, w1, b1, w2)]
+    yr = torch.nn.functional.linear(torch.relu(torch.nn.functional.linear(ins[0], ins[1], ins[2])), ins[3])
+    yr.backward(gy)
+    dins = [t.to(cuda_device, torch.bfloat16).requires_grad_() for t in (x, w1, b1, w2)]
+    yd = ops.mlp_relu(*dins)
+    yd.backward(gy.to(cuda_device, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert kernels().gemm_tc_status(0) == 0
+    assert _rel(yd.float().cpu(), yr) < 2e-2
+    for a, r in zip(dins, ins):
+        assert _rel(a.grad.float().cpu(), r.grad) < 3e-2
