@@ -52,10 +52,7 @@ constexpr int BM = 128, BK = 64;
 constexpr int kATile = BM * BK * 2;                // 16 KB
 constexpr int kThreads = 320;                      // 2 producer/MMA warps + 8 epilogue warps
 constexpr int kEpiWarps = 8;
-constexpr int kStageWords = 32 * 17;               // per-warp epilogue staging tile, padded rows
-constexpr int kStagingBytes = kEpiWarps * kStageWords * 4;
-// single-CTA kernel: two 32 x 32 bf16 tiles per epilogue warp, 64-byte rows in the TMA store's
-// 64-byte swizzle (the tensor store clips rows / columns past the output, so tails need no masks)
+// two 32 x 32 bf16 tiles per epilogue warp, 64-byte rows in the TMA store's 64-byte swizzle (the tensor store clips rows / columns past the output, so tails need no masks)
 constexpr int kTmaTileBytes = 32 * 64;
 constexpr int kTmaStagingBytes = kEpiWarps * 2 * kTmaTileBytes;
 constexpr int kMaxStages = 6;
@@ -87,27 +84,6 @@ struct __align__(8) SmemCtl {
 __device__ __forceinline__ float gelu_f(float x) { return gelu_fwd(x); }
 __device__ __forceinline__ float gelu_grad_f(float x) { return gelu_bwd(x); }
 
-// Warp-cooperative row-block copy through the padded staging tile (32 rows x 16
-// words, row stride 17 words: conflict-free when every lane writes its own row).
-// Each lane owns one row in registers; global memory is touched in 64-byte row
-// segments (8 rows per instruction) instead of one 16-byte piece per row.
-__device__ __forceinline__ void stage_store(uint32_t* stg, int lane, const float* x, __nv_bfloat16* base, int64_t ld,
-                                            int rows_valid, int ncols) {
-#pragma unroll
-    for (int w = 0; w < 16; ++w) stg[lane * 17 + w] = pack_bf16x2(x[2 * w], x[2 * w + 1]);
-    __syncwarp();
-    const int seg = lane & 3;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int r = 8 * i + (lane >> 2);
-        if (r < rows_valid && seg * 8 < ncols) {
-            const uint32_t* src = stg + r * 17 + seg * 4;
-            *reinterpret_cast<uint4*>(base + r * ld + seg * 8) = make_uint4(src[0], src[1], src[2], src[3]);
-        }
-    }
-    __syncwarp();
-}
-
 // This lane's row of a 32-row x `ncols` bf16 block (lane = row), straight from global memory: 16-byte
 // loads of the row's contiguous 64 bytes (the rows' sectors are read whole across the 4 loads).
 __device__ __forceinline__ void row_load(int lane, float* x, const __nv_bfloat16* base, int64_t ld, int rows_valid,
@@ -126,12 +102,10 @@ __device__ __forceinline__ void row_load(int lane, float* x, const __nv_bfloat16
     }
 }
 
-// Where one epilogue warp's chunks go: the single-CTA kernel stores through 3-D tensor maps
-// (column, row, batch) from two rotating swizzled tiles; the CTA-pair kernel through the padded
-// staging tile and row-segment stores.
+// Where one epilogue warp's chunks go: tensor stores through 3-D maps (column, row, batch) from two
+// rotating swizzled tiles of this warp.
 struct EpiOut {
-    uint32_t* stg;
-    unsigned char* tbuf;                 // two kTmaTileBytes tiles, or null
+    unsigned char* tbuf;                 // two kTmaTileBytes tiles
     const CUtensorMap* mapC;
     const CUtensorMap* mapAux;
     int bt;
@@ -167,7 +141,6 @@ __device__ __forceinline__ void tma_store_tile(EpiOut& eo, const CUtensorMap* ma
 // Epilogue of one warp's 32 rows x `ncols` (16 or 32) columns; lane = row.
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, EpiOut& eo, int lane, int row0, int col,
                                                int ncols, float* v, bool rmax_first = true) {
-    uint32_t* stg = eo.stg;
     const int rows_valid = min(32, g.M - row0);
     const int row = row0 + lane;
     if (g.ws) {  // split-K partial: fp32 vector atomics into the workspace
@@ -205,10 +178,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, EpiOut& eo, in
         }
         return;
     }
-    if (g.aux) {   // pre-activation for backward
-        if (eo.tbuf) tma_store_tile(eo, eo.mapAux, lane, v, col, row0);
-        else stage_store(stg, lane, v, g.aux + base, g.ldc, rows_valid, ncols);
-    }
+    if (g.aux) tma_store_tile(eo, eo.mapAux, lane, v, col, row0);   // pre-activation for backward
     if (g.epi == 1) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = gelu_f(v[i]);
@@ -244,23 +214,15 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, EpiOut& eo, in
             for (int i = 0; i < 32; ++i) v[i] = p[i] > 0.f ? v[i] : 0.f;
         }
     }
-    if (eo.tbuf) tma_store_tile(eo, eo.mapC, lane, v, col, row0);
-    else stage_store(stg, lane, v, g.C + base, g.ldc, rows_valid, ncols);
+    tma_store_tile(eo, eo.mapC, lane, v, col, row0);
     if (g.colacc) {
         // column sums of the stored (bf16-rounded) tile, read back from the staging: lane = column
         if (lane < ncols) {
             float s = 0.f;
-            if (eo.tbuf) {
-                const unsigned char* buf = eo.tbuf + (eo.turn ^ 1) * kTmaTileBytes;   // the tile just stored
-                for (int r = 0; r < rows_valid; ++r) {
-                    const unsigned char* p = buf + r * 64 + ((((lane >> 3) ^ ((r >> 1) & 3))) << 4) + (lane & 7) * 2;
-                    s += __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(p));
-                }
-            } else {
-                for (int r = 0; r < rows_valid; ++r) {
-                    const float2 t = unpack_bf16x2(stg[r * 17 + (lane >> 1)]);
-                    s += (lane & 1) ? t.y : t.x;
-                }
+            const unsigned char* buf = eo.tbuf + (eo.turn ^ 1) * kTmaTileBytes;   // the tile just stored
+            for (int r = 0; r < rows_valid; ++r) {
+                const unsigned char* p = buf + r * 64 + ((((lane >> 3) ^ ((r >> 1) & 3))) << 4) + (lane & 7) * 2;
+                s += __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(p));
             }
             atomicAdd(g.colacc + col + lane, s);
         }
@@ -409,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         // tile's rows) and half of the tile's columns, 32 columns per tcgen05.wait
         const int q = warp & 3;
         const int half = (warp - 2) >> 2;
-        EpiOut eo{nullptr, tstage + (warp - 2) * 2 * kTmaTileBytes, &tmC, &tmAux, 0, 0};
+        EpiOut eo{tstage + (warp - 2) * 2 * kTmaTileBytes, &tmC, &tmAux, 0, 0};
         int local = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
             int m0, n0, kt0, kt1;
@@ -536,12 +498,12 @@ struct PairTile {
     static constexpr int kBHalf = BN / 2;          // B rows (N) held by each CTA
     static constexpr int kBTile = kBHalf * BK * 2;
     static constexpr int kStageBytes = kATile + kBTile;
-    static constexpr int kStages =
-        (kSmemLimit - kStagingBytes - 2048) / kStageBytes < kMaxStages ? (kSmemLimit - kStagingBytes - 2048) / kStageBytes
-                                                                         : kMaxStages;
+    static constexpr int kStages = (kSmemLimit - kTmaStagingBytes - 2048) / kStageBytes < kMaxStages
+                                       ? (kSmemLimit - kTmaStagingBytes - 2048) / kStageBytes
+                                       : kMaxStages;
     static constexpr int kAccCols = BN;
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
-    static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + kStagingBytes + 1024 + 256;
+    static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + kTmaStagingBytes + 1024 + 256;
 };
 
 // bytes one CTA's loads deliver for a stage (MN-major boxes past the extent are not loaded)
@@ -555,7 +517,8 @@ __device__ __forceinline__ uint32_t pair_stage_bytes(const GemmArgs& g, int m_ct
 
 template <bool A_MN, bool B_MN, int BN_>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g,
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAux, GemmArgs g,
                     Sched sch) {
     using T = PairTile<BN_>;
     constexpr int BN = T::BN, kStages = T::kStages, kBTile = T::kBTile, kAccCols = T::kAccCols, kBHalf = T::kBHalf;
@@ -563,8 +526,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* tilesA = smem;
     unsigned char* tilesB = smem + kStages * kATile;
-    uint32_t* staging = reinterpret_cast<uint32_t*>(smem + kStages * (kATile + kBTile));
-    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(reinterpret_cast<unsigned char*>(staging) + kStagingBytes);
+    unsigned char* tstage = smem + kStages * (kATile + kBTile);     // 1024-aligned TMA store tiles
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(tstage + kTmaStagingBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -684,7 +647,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // lane quadrant w % 4 and half (w - 2) / 4 of the columns
         const int q = warp & 3;
         const int half = (warp - 2) >> 2;
-        EpiOut eo{staging + (warp - 2) * kStageWords, nullptr, nullptr, nullptr, 0, 0};
+        EpiOut eo{tstage + (warp - 2) * 2 * kTmaTileBytes, &tmC, &tmAux, 0, 0};
         int local = 0;
         for (int u = pair; u < units; u += npairs, ++local) {
             int m0, n0, kt0, kt1;
@@ -715,6 +678,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl->acc_empty[buf]), 0));
         }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -931,21 +896,12 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
     // output tensor maps of the single-CTA kernel's epilogue (C, pre-activation): 32 x 32 boxes over
     // [batch, M, N] (pitch ldc, batch stride bs_c), 64-byte swizzle
     CUtensorMap tc_map{}, taux_map{};
-    if (!plan.pair && g.ws == nullptr && g.epi != 7) {
+    if (g.ws == nullptr && g.epi != 7) {
         const int64_t bs = g.batch > 1 ? g.bs_c : static_cast<int64_t>(g.M) * g.ldc;
         ok = make_store_map(&tc_map, g.C, g.N, g.M, g.batch, g.ldc, bs);
         ok = ok && (g.aux == nullptr || make_store_map(&taux_map, g.aux, g.N, g.M, g.batch, g.ldc, bs));
         if (!ok) return cudaErrorInvalidValue;
     }
-    auto launch = [&](auto kern, size_t smem) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (e != cudaSuccess) {
-            std::fprintf(stderr, "gemm_tc: cudaFuncSetAttribute(%zu bytes) failed: %s\n", smem, cudaGetErrorString(e));
-            return;
-        }
-        kern<<<grid, kThreads, smem, st>>>(ta, tb, g, sch);
-        e = cudaGetLastError();
-    };
     auto launch1 = [&](auto kern, size_t smem) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) {
@@ -966,10 +922,10 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
     auto by_major_pair = [&](auto bnc) {
         constexpr int BNv = decltype(bnc)::value;
         const size_t smem = PairTile<BNv>::kSmemBytes;
-        if (!a_mn && !b_mn) launch(gemm_tc2_kernel<false, false, BNv>, smem);
-        else if (!a_mn && b_mn) launch(gemm_tc2_kernel<false, true, BNv>, smem);
-        else if (a_mn && b_mn) launch(gemm_tc2_kernel<true, true, BNv>, smem);
-        else launch(gemm_tc2_kernel<true, false, BNv>, smem);
+        if (!a_mn && !b_mn) launch1(gemm_tc2_kernel<false, false, BNv>, smem);
+        else if (!a_mn && b_mn) launch1(gemm_tc2_kernel<false, true, BNv>, smem);
+        else if (a_mn && b_mn) launch1(gemm_tc2_kernel<true, true, BNv>, smem);
+        else launch1(gemm_tc2_kernel<true, false, BNv>, smem);
     };
     if (plan.pair) {
         if (bn == 256) by_major_pair(std::integral_constant<int, 256>{});
