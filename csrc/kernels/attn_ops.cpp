@@ -114,6 +114,8 @@ void register_attn_ops(pybind11::module& m) {
     m.def("attn_short_smem_bytes", &attn_short_smem_bytes);
     m.def("attn_short_set_fwd_variant", &attn_short_set_fwd_variant, py::arg("variant"));
     m.def("attn_short_fwd_variant", &attn_short_fwd_variant);
+    m.def("attn_short_set_bwd_variant", &attn_short_set_bwd_variant, py::arg("variant"));
+    m.def("attn_short_bwd_variant", &attn_short_bwd_variant);
     m.def("attn_tc_blocks_per_sm", &attn_fwd_tc_blocks_per_sm);
     m.def("attn_tc_set_variant", &attn_fwd_tc_set_variant, py::arg("min_blocks"));
 }

@@ -1001,6 +1001,351 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------- backward, head dim 32, pipelined
+//
+// The head-dim-32 backward above runs each 128 x 128 block strictly in turn (S^T / dP^T products,
+// then the exponentials, then the dV / dK / dQ products), so the tensor core idles while the
+// softmax warps work and the other way round.  This kernel overlaps them:
+//   * work is cut into half-blocks of 128 keys x 64 queries; S^T / dP^T of half-block j + 1 are
+//     issued into the second of two tensor-memory buffers before the MMA warp waits for the
+//     softmax of half-block j, so the exponentials of j + 1 run while dV / dK of j are multiplied;
+//   * P^T half-tiles rotate through two shared-memory buffers and dS^T blocks (both halves, which
+//     the dQ product reads MN-major) through two, so the softmax never waits for the products of
+//     the half-block before;
+//   * dV / dK accumulate in one of two tensor-memory buffers per key tile, so the next key tile's
+//     products start before the previous one is read out;
+//   * Q / dO / K / V are 32-column boxes with the 64-byte swizzle (64-byte rows: exactly one head),
+//     half the bytes of the 64-column boxes the kernels above share with the neighbouring head;
+//   * a half-block whose 64 queries all lie past the sequence is skipped.
+// Tensor memory: S^T / dP^T buffers at [0, 256), dV / dK buffers at [256, 384), dQ of query tile
+// qt at 384 + 32 qt.
+namespace bw2 {
+constexpr int kTile = kRows * 32 * 2;       // 8 KB: 128 rows x 32 columns, 64-byte rows
+constexpr int kHalfQ = 64 * 64;             // byte offset of query row 64 in a kTile
+constexpr uint32_t cDKV = 256, cDQ = 384;
+}
+
+struct __align__(8) Bwd2Ctl {
+    uint64_t qdo_full, kv_full[2], kv_empty[2], sdp_full[2], soft_done[2], p_free[2], ds_free[2], dkv_full[2],
+        dkv_free[2], dq_done;
+    uint32_t tmem_base;
+    int abort;
+};
+
+__host__ __device__ constexpr size_t bwd2_smem_bytes() {
+    // control block, 1024 alignment, Q + dO (3 tiles each), K + V (two buffers each), P^T (two
+    // half-tiles), dS^T (two blocks of two half-tiles), log-sum-exp and delta rows
+    return 1024 + 1024 + static_cast<size_t>(bw2::kTile) * (6 + 4) + static_cast<size_t>(kBox) * (2 + 4) +
+           2 * kMaxL * sizeof(float);
+}
+
+// Shared-memory matrix descriptor, 64-byte swizzle (sm_100 layout type 4).
+__device__ __forceinline__ uint64_t smem_desc64(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3fff);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3fff) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3fff) << 32;
+    d |= 1ull << 46;
+    d |= 4ull << 61;
+    return d;
+}
+// 16-wide K slice kk of a K-major 64-byte-row tile (rows x 32 columns): 8-row groups 512 B apart
+__device__ __forceinline__ uint64_t kmajor64(uint32_t tile, int kk) { return smem_desc64(tile + kk * 32, 16, 512); }
+// 16-row K slice j of the same tile read MN-major (the 32 columns are the N side)
+__device__ __forceinline__ uint64_t mnmajor64(uint32_t tile, int j) { return smem_desc64(tile + j * 1024, 8192, 512); }
+
+// the number of 64-query halves of query tile qt that hold a query of the sequence
+__device__ __forceinline__ int bw2_halves(int qt, int T, int L) { return (qt == T - 1 && L - qt * kRows <= 64) ? 1 : 2; }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_short_bwd2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                           const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo, BwdArgs a) {
+    using namespace bw2;
+    constexpr int D = 32;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    Bwd2Ctl* ctl = reinterpret_cast<Bwd2Ctl*>(smem_raw);
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + sizeof(Bwd2Ctl) + 1023) & ~uintptr_t(1023));
+    const int L = a.L;
+    const int T = (L + kRows - 1) / kRows;
+    unsigned char* sQ = smem;
+    unsigned char* sDO = sQ + 3 * kTile;
+    unsigned char* sK = sDO + 3 * kTile;       // two buffers
+    unsigned char* sV = sK + 2 * kTile;        // two buffers
+    unsigned char* sP = sV + 2 * kTile;        // two 16 KB half-tiles [128 keys x 64 queries]
+    unsigned char* sDS = sP + 2 * kBox;        // two blocks of two half-tiles
+    float* s_lse2 = reinterpret_cast<float*>(sDS + 4 * kBox);
+    float* s_delta = s_lse2 + kMaxL;
+    if (L > kMaxL ||
+        reinterpret_cast<unsigned char*>(s_delta + kMaxL) - smem_raw > static_cast<ptrdiff_t>(bwd2_smem_bytes())) {
+        if (threadIdx.x == 0) atomicCAS(a.status, 0, 8);
+        return;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x / a.H, h = blockIdx.x % a.H;
+    const int row0 = n * L;
+    int J = 0;   // half-blocks: T key tiles x the valid halves of the T query tiles
+    for (int qt = 0; qt < T; ++qt) J += bw2_halves(qt, T, L);
+    J *= T;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&ctl->qdo_full, 1);
+        for (int x = 0; x < 2; ++x) {
+            mbar_init(&ctl->kv_full[x], 1);
+            mbar_init(&ctl->kv_empty[x], 1);
+            mbar_init(&ctl->sdp_full[x], 1);
+            mbar_init(&ctl->soft_done[x], kSoftWarps);
+            mbar_init(&ctl->p_free[x], 1);
+            mbar_init(&ctl->ds_free[x], 1);
+            mbar_init(&ctl->dkv_full[x], 1);
+            mbar_init(&ctl->dkv_free[x], kSoftWarps);
+        }
+        mbar_init(&ctl->dq_done, 1);
+        ctl->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == kProdWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&ctl->tmem_base)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == kProdWarp) {
+        if (lane == 0) {
+            mbar_expect_tx(&ctl->qdo_full, 2 * T * kTile);
+            for (int t = 0; t < T; ++t) {
+                tma_load_2d(&tq, &ctl->qdo_full, sQ + t * kTile, a.qcol + h * D, row0 + t * kRows);
+                tma_load_2d(&tdo, &ctl->qdo_full, sDO + t * kTile, a.docol + h * D, row0 + t * kRows);
+            }
+            for (int kt = 0; kt < T; ++kt) {
+                const int x = kt & 1;
+                if (kt >= 2 && !mbar_wait(&ctl->kv_empty[x], ((kt >> 1) - 1) & 1, &ctl->abort)) {
+                    ctl->abort = 1;
+                    atomicCAS(a.status, 0, 1);
+                    break;
+                }
+                mbar_expect_tx(&ctl->kv_full[x], 2 * kTile);
+                tma_load_2d(&tk, &ctl->kv_full[x], sK + x * kTile, a.kcol + h * D, row0 + kt * kRows);
+                tma_load_2d(&tv, &ctl->kv_full[x], sV + x * kTile, a.vcol + h * D, row0 + kt * kRows);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_sdp = instr_desc(false, false, 64);   // S^T / dP^T: 128 keys x 64 queries
+            constexpr uint32_t idesc_kv = instr_desc(false, true, D);      // dV / dK
+            constexpr uint32_t idesc_q = instr_desc(true, true, D);        // dQ (dS read MN-major)
+            const uint32_t q = smem_u32(sQ), dob = smem_u32(sDO), k = smem_u32(sK), v = smem_u32(sV);
+            const uint32_t pt = smem_u32(sP), dst = smem_u32(sDS);
+            auto issue_sdp = [&](int x, int kt, int qt, int hb) {
+                const uint32_t kb = k + (kt & 1) * kTile, vb = v + (kt & 1) * kTile;
+                const uint32_t qb = q + qt * kTile + hb * kHalfQ, db = dob + qt * kTile + hb * kHalfQ;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    tc_mma(tmem + 128 * x, kmajor64(kb, kk), kmajor64(qb, kk), idesc_sdp, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    tc_mma(tmem + 128 * x + 64, kmajor64(vb, kk), kmajor64(db, kk), idesc_sdp, kk > 0);
+                tc_commit(&ctl->sdp_full[x]);
+            };
+            bool ok = mbar_wait(&ctl->qdo_full, 0, &ctl->abort) && mbar_wait(&ctl->kv_full[0], 0, &ctl->abort);
+            if (ok) {
+                tc_fence_after();
+                issue_sdp(0, 0, 0, 0);
+            }
+            int kt = 0, qt = 0, hb = 0, blk = 0;
+            for (int j = 0; ok && j < J; ++j) {
+                int nkt = kt, nqt = qt, nhb = hb + 1;
+                if (nhb == bw2_halves(qt, T, L)) {
+                    nhb = 0;
+                    if (++nqt == T) {
+                        nqt = 0;
+                        ++nkt;
+                    }
+                }
+                if (j + 1 < J) {
+                    // the softmax of half-block j - 1 has read buffer (j + 1) & 1 (awaited last iteration)
+                    if (nkt != kt && !(ok = mbar_wait(&ctl->kv_full[nkt & 1], (nkt >> 1) & 1, &ctl->abort))) break;
+                    tc_fence_after();
+                    issue_sdp((j + 1) & 1, nkt, nqt, nhb);
+                }
+                if (!(ok = mbar_wait(&ctl->soft_done[j & 1], (j >> 1) & 1, &ctl->abort))) break;
+                tc_fence_after();
+                const bool first = qt == 0 && hb == 0;     // first half-block of this key tile
+                if (first && kt >= 2) {
+                    if (!(ok = mbar_wait(&ctl->dkv_free[kt & 1], ((kt >> 1) - 1) & 1, &ctl->abort))) break;
+                    tc_fence_after();
+                }
+                const uint32_t dv = tmem + cDKV + 64 * (kt & 1), dk = dv + 32;
+                const uint32_t pb = pt + (j & 1) * kBox, dsb = dst + (blk & 1) * 2 * kBox;
+                const uint32_t qb = q + qt * kTile + hb * kHalfQ, db = dob + qt * kTile + hb * kHalfQ;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+                    tc_mma(dv, smem_desc(pb + kk * 32, 16, 1024), mnmajor64(db, kk), idesc_kv, acc);
+                    tc_mma(dk, smem_desc(dsb + hb * kBox + kk * 32, 16, 1024), mnmajor64(qb, kk), idesc_kv, acc);
+                }
+                tc_commit(&ctl->p_free[j & 1]);
+                if (hb == bw2_halves(qt, T, L) - 1) {
+                    // dQ_qt += dS K_kt over the block's 128 keys (a skipped half only feeds query rows past
+                    // the sequence, which are never stored)
+                    const uint32_t kb = k + (kt & 1) * kTile;
+#pragma unroll
+                    for (int jj = 0; jj < kRows / 16; ++jj)
+                        tc_mma(tmem + cDQ + 32 * qt, smem_desc(dsb + jj * 2048, kBox, 1024), mnmajor64(kb, jj), idesc_q,
+                               (kt > 0 || jj > 0) ? 1u : 0u);
+                    tc_commit(&ctl->ds_free[blk & 1]);
+                    if (qt == T - 1) {
+                        tc_commit(&ctl->dkv_full[kt & 1]);
+                        tc_commit(&ctl->kv_empty[kt & 1]);
+                    }
+                    ++blk;
+                }
+                kt = nkt;
+                qt = nqt;
+                hb = nhb;
+            }
+            if (ok) tc_commit(&ctl->dq_done);
+            if (!ok) {
+                ctl->abort = 1;
+                atomicCAS(a.status, 0, 2);
+            }
+        }
+    } else {
+        // warp w: TMEM lane quadrant w % 4 (thread = key row r of the transposed products, query row r
+        // of dQ) and half w / 4: query columns [32 * half, +32) of each half-block, output columns
+        // [16 * half, +16) of dV / dK / dQ
+        const int quad = warp & 3, half = warp >> 2;
+        const int r = 32 * quad + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(32 * quad) << 16;
+        const float* lse = a.lse + (static_cast<int64_t>(n) * a.H + h) * L;
+        const float* delta = a.delta + (static_cast<int64_t>(n) * a.H + h) * L;
+        for (int i = threadIdx.x; i < kMaxL; i += kSoftThreads) {
+            s_lse2[i] = i < L ? lse[i] * kLog2e : __int_as_float(0x7f800000);   // +inf: P = 0 past the sequence
+            s_delta[i] = i < L ? delta[i] : 0.f;
+        }
+        soft_sync_and(true);
+        bool ok = true;
+        int kt = 0, qt = 0, hb = 0, blk = 0;
+        const float sl = a.scale_log2;
+        for (int j = 0; j < J; ++j) {
+            if (!mbar_wait(&ctl->sdp_full[j & 1], (j >> 1) & 1, &ctl->abort) ||
+                (j >= 2 && !mbar_wait(&ctl->p_free[j & 1], ((j >> 1) - 1) & 1, &ctl->abort)) ||
+                (hb == 0 && blk >= 2 && !mbar_wait(&ctl->ds_free[blk & 1], ((blk >> 1) - 1) & 1, &ctl->abort))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const float keep = kt * kRows + r < L ? 1.f : 0.f;
+            const int q0 = qt * kRows + hb * 64 + 32 * half;      // this thread's first query
+            const float4* l2v = reinterpret_cast<const float4*>(s_lse2 + q0);
+            const float4* dlv = reinterpret_cast<const float4*>(s_delta + q0);
+            float sv[32], dp[32];
+            tmem_ld32x2(tmem + 128 * (j & 1) + lane_off + 32 * half, tmem + 128 * (j & 1) + 64 + lane_off + 32 * half,
+                        sv, dp);
+            unsigned char* pbox = sP + (j & 1) * kBox;
+            unsigned char* dbox = sDS + (blk & 1) * 2 * kBox + hb * kBox;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                uint32_t wp[4], wd[4];
+                const float4 la = l2v[2 * g], lb = l2v[2 * g + 1];
+                const float4 da = dlv[2 * g], db = dlv[2 * g + 1];
+                const float lv[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+                const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int c = 8 * g + 2 * i;
+                    const float p0 = keep * ex2(fmaf(sv[c], sl, -lv[2 * i]));
+                    const float p1 = keep * ex2(fmaf(sv[c + 1], sl, -lv[2 * i + 1]));
+                    wp[i] = pack_bf16x2(p0, p1);
+                    wd[i] = pack_bf16x2(p0 * (dp[c] - dv[2 * i]), p1 * (dp[c + 1] - dv[2 * i + 1]));
+                }
+                put16(pbox, r, 4 * half + g, make_uint4(wp[0], wp[1], wp[2], wp[3]));
+                put16(dbox, r, 4 * half + g, make_uint4(wd[0], wd[1], wd[2], wd[3]));
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->soft_done[j & 1]);
+            const bool block_end = hb == bw2_halves(qt, T, L) - 1;
+            if (block_end && qt == T - 1) {
+                // dV / dK of key tile kt complete: thread = key row, this half's 16 output columns
+                if (!mbar_wait(&ctl->dkv_full[kt & 1], (kt >> 1) & 1, &ctl->abort)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                float dvr[16], dkr[16];
+                tmem_ld16(tmem + cDKV + 64 * (kt & 1) + lane_off + 16 * half, dvr);
+                tmem_ld16(tmem + cDKV + 64 * (kt & 1) + 32 + lane_off + 16 * half, dkr);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctl->dkv_free[kt & 1]);
+                if (kt * kRows + r < L) {
+                    const int64_t row = row0 + kt * kRows + r;
+                    uint4* ov = reinterpret_cast<uint4*>(a.dv + row * a.lddv + a.dvcol + h * D + half * 16);
+                    uint4* okp = reinterpret_cast<uint4*>(a.dk + row * a.lddk + a.dkcol + h * D + half * 16);
+                    const float sc = a.scale;
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        ov[i] = make_uint4(pack_bf16x2(dvr[8 * i], dvr[8 * i + 1]), pack_bf16x2(dvr[8 * i + 2], dvr[8 * i + 3]),
+                                           pack_bf16x2(dvr[8 * i + 4], dvr[8 * i + 5]),
+                                           pack_bf16x2(dvr[8 * i + 6], dvr[8 * i + 7]));
+                        okp[i] = make_uint4(pack_bf16x2(dkr[8 * i] * sc, dkr[8 * i + 1] * sc),
+                                            pack_bf16x2(dkr[8 * i + 2] * sc, dkr[8 * i + 3] * sc),
+                                            pack_bf16x2(dkr[8 * i + 4] * sc, dkr[8 * i + 5] * sc),
+                                            pack_bf16x2(dkr[8 * i + 6] * sc, dkr[8 * i + 7] * sc));
+                    }
+                }
+            }
+            if (block_end) ++blk;
+            if (++hb == bw2_halves(qt, T, L)) {
+                hb = 0;
+                if (++qt == T) {
+                    qt = 0;
+                    ++kt;
+                }
+            }
+        }
+        if (ok && mbar_wait(&ctl->dq_done, 0, &ctl->abort)) {
+            tc_fence_after();
+            for (int t = 0; t < T; ++t) {
+                float dqr[16];
+                tmem_ld16(tmem + cDQ + 32 * t + lane_off + 16 * half, dqr);
+                const int qrow = t * kRows + r;
+                if (qrow < L) {
+                    uint4* oq = reinterpret_cast<uint4*>(a.dq + static_cast<int64_t>(row0 + qrow) * a.lddq + a.dqcol +
+                                                         h * D + half * 16);
+                    const float sc = a.scale;
+#pragma unroll
+                    for (int i = 0; i < 2; ++i)
+                        oq[i] = make_uint4(pack_bf16x2(dqr[8 * i] * sc, dqr[8 * i + 1] * sc),
+                                           pack_bf16x2(dqr[8 * i + 2] * sc, dqr[8 * i + 3] * sc),
+                                           pack_bf16x2(dqr[8 * i + 4] * sc, dqr[8 * i + 5] * sc),
+                                           pack_bf16x2(dqr[8 * i + 6] * sc, dqr[8 * i + 7] * sc));
+                }
+            }
+        } else {
+            ok = false;
+        }
+        if (!ok) {
+            ctl->abort = 1;
+            if (lane == 0) atomicCAS(a.status, 0, 3);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kProdWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
 // delta[n, h, i] = sum_d dO[row, docol + h*D + d] * O[row, ocol + h*D + d], row = n*L + i
 template <int D>
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, int64_t lddo, int docol,
@@ -1056,6 +1401,25 @@ cudaError_t make_map(CUtensorMap* tm, const void* base, int64_t cols, int64_t ro
     return cudaSuccess;
 }
 
+// 128-row x 32-column boxes (one head-dim-32 head: 64-byte rows) with the 64-byte swizzle
+cudaError_t make_map32(CUtensorMap* tm, const void* base, int64_t cols, int64_t rows, int64_t ld) {
+    if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || ld % 8 != 0 || cols > ld) return cudaErrorInvalidValue;
+    auto fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+    cuuint32_t box[2] = {32, kRows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::fprintf(stderr, "attn_short: cuTensorMapEncodeTiled (32-column boxes) failed (%d)\n", static_cast<int>(r));
+        return cudaErrorInvalidValue;
+    }
+    return cudaSuccess;
+}
+
 // the shared-memory opt-in, once per (kernel, device): Tag makes every kernel its own instantiation
 // (the D = 32 and D = 64 kernels have the same function-pointer type, so the flags cannot be keyed
 // by that type alone)
@@ -1073,6 +1437,8 @@ struct KernelTag {};
 
 // forward kernel: 1 = whole score row per (sequence, head), 2 = ping-pong warpgroups (default)
 int g_fwd_variant = 2;
+// head-dim-32 backward kernel: 1 = one block at a time, 2 = pipelined half-blocks (default)
+int g_bwd_variant = 2;
 
 }  // namespace
 
@@ -1080,6 +1446,8 @@ bool attn_short_supported(int L, int D) { return L >= 1 && L <= kMaxL && (D == 3
 
 void attn_short_set_fwd_variant(int v) { g_fwd_variant = v == 1 ? 1 : 2; }
 int attn_short_fwd_variant() { return g_fwd_variant; }
+void attn_short_set_bwd_variant(int v) { g_bwd_variant = v == 1 ? 1 : 2; }
+int attn_short_bwd_variant() { return g_bwd_variant; }
 
 cudaError_t launch_attn_short_fwd(const AttnOperand& q, const AttnOperand& k, const AttnOperand& v, int nseq, int L,
                                   int H, int D, void* o, int64_t ldo, int ocol, float* lse, float scale, int* status,
@@ -1150,14 +1518,24 @@ cudaError_t launch_attn_short_bwd(const AttnOperand& q, const AttnOperand& k, co
                                                                delta, nseq, L, H);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
+    BwdArgs a{lse,   delta, dq_acc, static_cast<__nv_bfloat16*>(dq), static_cast<__nv_bfloat16*>(dk),
+              static_cast<__nv_bfloat16*>(dv), lddq, lddk, lddv, dqcol, dkcol, dvcol, status, L, H, q.col, k.col,
+              v.col, dout.col, scale * kLog2e, scale};
     CUtensorMap mq, mk, mv, mdo;
+    if (D == 32 && g_bwd_variant == 2) {
+        if ((e = make_map32(&mq, q.base, q.cols, rows, q.ld)) != cudaSuccess) return e;
+        if ((e = make_map32(&mk, k.base, k.cols, rows, k.ld)) != cudaSuccess) return e;
+        if ((e = make_map32(&mv, v.base, v.cols, rows, v.ld)) != cudaSuccess) return e;
+        if ((e = make_map32(&mdo, dout.base, dout.cols, rows, dout.ld)) != cudaSuccess) return e;
+        constexpr size_t smem2 = bwd2_smem_bytes();
+        if ((e = ensure_smem<KernelTag<true, 33>>(attn_short_bwd2_kernel, smem2, dev)) != cudaSuccess) return e;
+        attn_short_bwd2_kernel<<<nseq * H, kThreads, smem2, st>>>(mq, mk, mv, mdo, a);
+        return cudaGetLastError();
+    }
     if ((e = make_map(&mq, q.base, q.cols, rows, q.ld)) != cudaSuccess) return e;
     if ((e = make_map(&mk, k.base, k.cols, rows, k.ld)) != cudaSuccess) return e;
     if ((e = make_map(&mv, v.base, v.cols, rows, v.ld)) != cudaSuccess) return e;
     if ((e = make_map(&mdo, dout.base, dout.cols, rows, dout.ld)) != cudaSuccess) return e;
-    BwdArgs a{lse,   delta, dq_acc, static_cast<__nv_bfloat16*>(dq), static_cast<__nv_bfloat16*>(dk),
-              static_cast<__nv_bfloat16*>(dv), lddq, lddk, lddv, dqcol, dkcol, dvcol, status, L, H, q.col, k.col,
-              v.col, dout.col, scale * kLog2e, scale};
     const size_t smem = bwd_smem_bytes(kMaxL);
     if (D == 32) {
         if ((e = ensure_smem<KernelTag<true, 32>>(attn_short_bwd_kernel<32>, smem, dev)) != cudaSuccess) return e;

@@ -120,6 +120,51 @@ std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::option
     return {C};
 }
 
+// out += opA(a) opB(b): the product added into an existing bf16 [M, N] tensor (weight gradients
+// accumulated straight into the flat gradient buffer).  Split-K products sum their fp32 partials
+// and the conversion adds the old value; unsplit ones read it in the epilogue (alpha = beta = 1).
+void gemm_tc_acc(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, torch::Tensor out) {
+    TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.dim() == 2 && b.dim() == 2, "gemm_tc_acc: 2-D CUDA tensors expected");
+    TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16 &&
+                    out.scalar_type() == torch::kBFloat16,
+                "gemm_tc_acc: bf16 only");
+    TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm_tc_acc: operands must be row-major");
+    const int64_t M = a_mn ? a.size(1) : a.size(0);
+    const int64_t K = a_mn ? a.size(0) : a.size(1);
+    const int64_t N = b_mn ? b.size(1) : b.size(0);
+    TORCH_CHECK(K == (b_mn ? b.size(0) : b.size(1)), "gemm_tc_acc: reduction sizes differ");
+    TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0 && aligned16(a) && aligned16(b),
+                "gemm_tc_acc: rows must be 16-byte aligned");
+    TORCH_CHECK(N % 16 == 0 && (!a_mn || M % 128 == 0) && (!b_mn || N % 128 == 0) && M > 0 && K > 0,
+                "gemm_tc_acc: unsupported shape");
+    TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.size(0) == M && out.size(1) == N && aligned16(out),
+                "gemm_tc_acc: out must be a contiguous, 16-byte aligned bf16 [M, N] tensor");
+    at::cuda::CUDAGuard guard(a.device());
+    GemmArgs g{};
+    g.A = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
+    g.B = reinterpret_cast<const __nv_bfloat16*>(b.data_ptr());
+    g.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+    g.status = status_word(a.device()).data_ptr<int>();
+    g.M = static_cast<int>(M);
+    g.N = static_cast<int>(N);
+    g.K = static_cast<int>(K);
+    g.ldc = N;
+    torch::Tensor ws;
+    const int splits = gemm_tc_splits(g.M, g.N, g.K, b_mn);
+    if (splits > 1) {
+        ws = torch::empty({M, N}, a.options().dtype(torch::kFloat32));
+        g.ws = ws.data_ptr<float>();
+        g.splits = splits;
+        g.ws_acc = 1;
+    } else {
+        g.epi = 6;
+        g.alpha = 1.f;
+        g.beta = 1.f;
+        g.res = g.C;
+    }
+    check_cuda(launch_gemm_tc(g, a_mn, b_mn, a.stride(0), b.stride(0), cur_stream()), "gemm_tc_acc");
+}
+
 // Batched products through 2-D tensor maps (see GemmArgs): a / b are the whole operand matrices
 // (row-major, unit column stride); batch i reads them at tile coordinates shifted by
 // i * (a_bk, a_bm) and i * (b_bk, b_bn).  Returns C [batch, M, N] bf16, or for epi 7 the row
@@ -202,6 +247,8 @@ void register_gemm_ops(pybind11::module& m) {
     m.def("gemm_tc", &gemm_tc, py::arg("a"), py::arg("b"), py::arg("bias") = py::none(), py::arg("a_mn") = false,
           py::arg("b_mn") = false, py::arg("epi") = 0, py::arg("want_aux") = false, py::arg("res") = py::none(),
           py::arg("gamma") = py::none(), py::arg("colsum") = py::none(), py::arg("colsum_acc") = false);
+    m.def("gemm_tc_acc", &gemm_tc_acc, py::arg("a"), py::arg("b"), py::arg("a_mn"), py::arg("b_mn"),
+          py::arg("out"));
     m.def("gemm_tc_status", &gemm_tc_status);
     m.def("gemm_tc_batched", &gemm_tc_batched, py::arg("a"), py::arg("b"), py::arg("bias"), py::arg("a_mn"),
           py::arg("b_mn"), py::arg("batch"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("a_bk"), py::arg("a_bm"),

@@ -356,10 +356,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                     tc_fence_after();
                     const uint32_t a = smem_u32(tilesA + s * kATile);
                     const uint32_t b = smem_u32(tilesB + s * kBTile);
+                    if (!(g.diag & 2)) {
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        tc_mma(acc, operand_desc<A_MN>(a, kk), operand_desc<B_MN>(b, kk), idesc,
-                               (kt > kt0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            tc_mma(acc, operand_desc<A_MN>(a, kk), operand_desc<B_MN>(b, kk), idesc,
+                                   (kt > kt0 || kk > 0) ? 1u : 0u);
+                    }
                     tc_commit(&ctl->empty[s]);
                 }
                 if (!ok) break;
@@ -629,10 +631,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint32_t a = smem_u32(tilesA + s * kATile);
                     const uint32_t b = smem_u32(tilesB + s * kBTile);
+                    if (!(g.diag & 2)) {
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        tc_mma_pair(acc, operand_desc<A_MN>(a, kk), operand_desc<B_MN>(b, kk), idesc,
-                                    (kt > kt0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            tc_mma_pair(acc, operand_desc<A_MN>(a, kk), operand_desc<B_MN>(b, kk), idesc,
+                                        (kt > kt0 || kk > 0) ? 1u : 0u);
+                    }
                     // the stage is free in both CTAs once these MMAs are done
                     tc_commit_pair(mapa_shared(smem_u32(&ctl->empty[s]), 0));
                     tc_commit_pair(mapa_shared(smem_u32(&ctl->empty[s]), 1));
@@ -672,6 +676,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 } else {
                     tmem_ld16(acc + c, v);
                 }
+                if (g.diag & 1) continue;
                 epilogue_chunk(g, eo, lane, row0, n0 + c, ncols, v);
             }
             tc_fence_before();
@@ -690,11 +695,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
-__global__ void ws_to_bf16_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ c, int64_t n) {
+__global__ void ws_to_bf16_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ c, int64_t n, int acc) {
     for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x * 8) {
         float v[8];
         load8(ws + i, v);
+        if (acc) {
+            float o[8];
+            load8(c + i, o);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] += o[j];
+        }
         store8(c + i, v);
     }
 }
@@ -816,6 +827,26 @@ struct Plan {
 // operand traffic, so they are used whenever the output (or its K splits) still gives every
 // pair of SMs work; narrow outputs keep the single-CTA tiles.  MN-major B needs whole 64-column
 // boxes per CTA half, hence N % 128 == 0 for pair tiles.
+// K splits for `tiles` output tiles on `slots` persistent workers: the count (each split at least
+// four K tiles) whose units fill the last wave best, fewer splits on a tie (every split adds an fp32
+// partial tile of atomics).  E.g. 36 tiles on 148 SMs -> 4 splits (144 units, one wave), not 5
+// (180 units: a second, mostly idle wave).
+int best_splits(int tiles, int ktiles, int slots, double* eff_out) {
+    int best = 1;
+    double best_eff = -1.0;
+    for (int s = 1; s <= std::max(1, ktiles / 4); ++s) {
+        const long long units = static_cast<long long>(tiles) * s;
+        const long long waves = (units + slots - 1) / slots;
+        const double eff = static_cast<double>(units) / static_cast<double>(waves * slots) - 0.002 * s;
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best = s;
+        }
+    }
+    if (eff_out) *eff_out = best_eff;
+    return best;
+}
+
 Plan plan_for(int M, int N, int K, bool b_mn, bool splittable) {
     const int sms = num_sms();
     const int ktiles = (K + BK - 1) / BK;
@@ -826,12 +857,29 @@ Plan plan_for(int M, int N, int K, bool b_mn, bool splittable) {
     if (pair_ok) {
         const int tiles2 = ((M + kPairRows - 1) / kPairRows) * ((N + bn2 - 1) / bn2);
         int splits2 = 1;
-        if (splittable && tiles2 < sms / 4 && ktiles >= 8)
-            splits2 = std::max(1, std::min((sms / 2 + tiles2 - 1) / tiles2, ktiles / 4));
+        if (splittable && tiles2 < sms / 4 && ktiles >= 8) splits2 = best_splits(tiles2, ktiles, sms / 2, nullptr);
         if (g_variant == 2 || tiles2 * splits2 >= sms / 2) return Plan{true, bn2, splits2};
     }
     const int tiles = ((M + BM - 1) / BM) * ((N + p.bn - 1) / p.bn);
-    if (splittable && tiles < sms / 2 && ktiles >= 8) p.splits = std::max(1, std::min((sms + tiles - 1) / tiles, ktiles / 4));
+    if (splittable && tiles < sms / 2 && ktiles >= 8) {
+        // few output tiles, long reduction: tile width and split count together (wider tiles move
+        // fewer operand bytes per product, and a width that divides N wastes no columns)
+        const int widths[3] = {256, 192, 128};
+        const double tile_eff[3] = {1.0, 0.96, 0.88};
+        double best_score = -1.0;
+        for (int i = 0; i < 3; ++i) {
+            const int tn = (N + widths[i] - 1) / widths[i];
+            const double col_eff = static_cast<double>(N) / (static_cast<double>(tn) * widths[i]);
+            double eff = 0.0;
+            const int s = best_splits(((M + BM - 1) / BM) * tn, ktiles, sms, &eff);
+            const double score = col_eff * eff * tile_eff[i];
+            if (score > best_score + 1e-9) {
+                best_score = score;
+                p.bn = widths[i];
+                p.splits = s;
+            }
+        }
+    }
     return p;
 }
 
@@ -939,7 +987,7 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
     }
     if (e != cudaSuccess || !g.ws) return e;
     const int64_t n = static_cast<int64_t>(g.M) * g.ldc;
-    ws_to_bf16_kernel<<<std::min<int64_t>((n / 8 + 255) / 256, num_sms() * 8), 256, 0, st>>>(g.ws, g.C, n);
+    ws_to_bf16_kernel<<<std::min<int64_t>((n / 8 + 255) / 256, num_sms() * 8), 256, 0, st>>>(g.ws, g.C, n, g.ws_acc);
     return cudaGetLastError();
 }
 

@@ -19,6 +19,7 @@ struct GemmArgs {
     int* status;                // 0 ok, else a bounded wait gave up (1 producer, 2 MMA, 3 epilogue)
     float* ws;                  // split-K: fp32 [M, N] workspace (zeroed by the launcher); nullptr = no split
     int splits;                 // K splits when ws != nullptr
+    int ws_acc;                 // split-K: the conversion adds the existing C (C += product)
     int M, N, K;
     int64_t ldc;
     int epi;                    // 0 none, 1 GELU(erf), 2 ReLU, 3 res + gamma * (acc + bias),
@@ -38,8 +39,9 @@ struct GemmArgs {
     float* rmax;                // epi 7: fp32 [2, batch, M], one partial maximum per half of the columns
     // extents of the 2-D operand matrices the tensor maps cover (0: derived from M / N / K)
     int64_t a_inner, a_outer, b_inner, b_outer;
-    // diagnostics (environment MMLTK_GEMM_DIAG): 1 = the epilogue reads the accumulator but stores
-    // nothing, which times the main loop and the tensor-memory hand-off alone
+    // diagnostics (environment MMLTK_GEMM_DIAG, bit mask): 1 = the epilogue reads the accumulator but
+    // stores nothing, which times the main loop and the tensor-memory hand-off alone; 2 = the MMA warp
+    // commits every stage without issuing its MMAs, which times the loads and the epilogue alone
     int diag;
 };
 

@@ -58,6 +58,9 @@ bool attn_short_supported(int L, int D);
 // 2 = two ping-pong softmax warpgroups over 128-key chunks (online softmax)
 void attn_short_set_fwd_variant(int v);
 int attn_short_fwd_variant();
+// head-dim-32 backward kernel variant: 1 = one 128 x 128 block at a time, 2 = pipelined half-blocks
+void attn_short_set_bwd_variant(int v);
+int attn_short_bwd_variant();
 size_t attn_short_smem_bytes(bool backward);
 cudaError_t launch_attn_short_fwd(const AttnOperand& q, const AttnOperand& k, const AttnOperand& v, int nseq, int L,
                                   int H, int D, void* o, int64_t ldo, int ocol, float* lse, float scale, int* status,

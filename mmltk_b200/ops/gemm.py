@@ -105,6 +105,10 @@ def gemm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 
 def gemm_tn_acc(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     """out += a^T b in one GEMM (beta = 1): weight gradients accumulated straight into .grad."""
+    if (_state["all"] and tc_gemm_enabled() and a.shape[1] % 128 == 0 and b.shape[1] % 128 == 0 and _rowmajor(a)
+            and _rowmajor(b) and out.is_contiguous() and out.data_ptr() % 16 == 0):
+        kernels().gemm_tc_acc(a, b, True, True, out)
+        return out
     return out.addmm_(a.t(), b)
 
 

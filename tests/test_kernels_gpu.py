@@ -639,3 +639,24 @@ def test_mlp_relu_matches_fp32(cuda_device, M):
     assert _rel(yd.float().cpu(), yr) < 2e-2
     for a, r in zip(dins, ins):
         assert _rel(a.grad.float().cpu(), r.grad) < 3e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(1536, 384, 10400), (256, 2048, 31200), (384, 384, 1300)])
+def test_gemm_tc_weight_gradient_accumulates(cuda_device, M, N, K):
+    """out += a^T b (weight-gradient shapes: both operands MN-major, split K with the tile width and
+    split count chosen together; an unsplit shape accumulates in the epilogue) vs fp32."""
+    k = kernels()
+    g = torch.Generator().manual_seed(M + N + K)
+    a = torch.randn(K, M, generator=g).to(torch.bfloat16)
+    b = torch.randn(K, N, generator=g).to(torch.bfloat16)
+    out0 = torch.randn(M, N, generator=g).mul(8.0).to(torch.bfloat16)
+    ref = out0.float() + a.float().t() @ b.float()
+    out = out0.to(cuda_device)
+    k.gemm_tc_acc(a.to(cuda_device), b.to(cuda_device), True, True, out)
+    torch.cuda.synchronize()
+    assert k.gemm_tc_status(0) == 0
+    err = (out.float().cpu() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, err
+    plain = k.gemm_tc(a.to(cuda_device), b.to(cuda_device), None, True, True)[0]
+    ref0 = a.float().t() @ b.float()
+    assert (plain.float().cpu() - ref0).abs().max().item() < 1e-2 * ref0.abs().max().item()
