@@ -38,7 +38,9 @@ __all__ = ["attention", "attention_reference", "qkv_attention", "qkv_attention_r
            "short_attention", "short_attention_ok"]
 
 _USE_TC = os.environ.get("MMLTK_ATTN_TC", "0") == "1"
-_USE_SHORT = os.environ.get("MMLTK_ATTN_SHORT", "0") == "1"
+# "1": every sequence of at most 384 tokens on the short-sequence kernels; "d32": head dim 32 only
+# (the decoder's self-attention); "0": none
+_SHORT_MODE = os.environ.get("MMLTK_ATTN_SHORT", "0")
 SHORT_MAX_L = 384
 
 
@@ -50,7 +52,8 @@ def _tma_ok(t: torch.Tensor) -> bool:
 def short_attention_ok(L: int, D: int, *sources: torch.Tensor) -> bool:
     """True when ``short_attention`` takes these operands (CUDA bf16 2-D sources, L <= 384,
     head dim 32 or 64)."""
-    return _USE_SHORT and 1 <= L <= SHORT_MAX_L and D in (32, 64) and all(_tma_ok(t) for t in sources)
+    use = _SHORT_MODE == "1" or (_SHORT_MODE == "d32" and D == 32)
+    return use and 1 <= L <= SHORT_MAX_L and D in (32, 64) and all(_tma_ok(t) for t in sources)
 
 
 class _ShortAttnFn(torch.autograd.Function):

@@ -271,6 +271,13 @@ def bench_attn(device="cuda", quick=False):
                 go_t = gos if tag == "short" else gos.view(N, L, H, D).transpose(1, 2)
                 row[f"packed_{tag}_fwd_bwd_ms"] = round(time_graph_ms(
                     lambda: torch.autograd.grad(f(), (qkv,), go_t)), 4)
+            if D == 32:
+                # head-dim-32 backward kernels: one block at a time (1) / pipelined half-blocks (2)
+                for v in (1, 2):
+                    kernels().attn_short_set_bwd_variant(v)
+                    row[f"packed_short_bwd_v{v}_fwd_bwd_ms"] = round(time_graph_ms(
+                        lambda: torch.autograd.grad(short_pk(), (qkv,), gos)), 4)
+                kernels().attn_short_set_bwd_variant(2)
         if D == 64:
             # forward on the packed projection layout: the tcgen05 kernel vs cuDNN on strided views
             from .attention import _split, qkv_attention_tc

@@ -45,8 +45,19 @@ def _heads(m, col, N, L, H, D):
     return m[:, col:col + H * D].float().view(N, L, H, D).transpose(1, 2)
 
 
-@pytest.mark.parametrize("N,L,H", [(6, 300, 8), (3, 100, 8), (2, 129, 4), (2, 384, 8), (1, 17, 2)])
-def test_short_attention_split_d32(cuda_device, N, L, H):
+@pytest.fixture(params=[2, 1], ids=["bwd-pipelined", "bwd-blockwise"])
+def bwd_variant(request):
+    """Head-dim-32 tests run both backward kernels: pipelined half-blocks (default) and one block at
+    a time."""
+    k = kernels()
+    old = k.attn_short_bwd_variant()
+    k.attn_short_set_bwd_variant(request.param)
+    yield request.param
+    k.attn_short_set_bwd_variant(old)
+
+
+@pytest.mark.parametrize("N,L,H", [(6, 300, 8), (3, 100, 8), (2, 129, 4), (2, 384, 8), (1, 17, 2), (2, 200, 3)])
+def test_short_attention_split_d32(cuda_device, bwd_variant, N, L, H):
     torch.manual_seed(0)
     D = 32
     qk = (torch.randn(N * L, 2 * H * D, device=cuda_device) * 1.5).bfloat16().requires_grad_()
@@ -100,12 +111,12 @@ def test_qkv_attention_takes_the_short_kernel_for_windows(cuda_device):
     import importlib
     attn_mod = importlib.import_module("mmltk_b200.ops.attention")   # (the package re-exports a function of that name)
     qkv = (torch.randn(N, L, 3 * H * 64, device=cuda_device)).bfloat16().requires_grad_()
-    old = attn_mod._USE_SHORT
-    attn_mod._USE_SHORT = True
+    old = attn_mod._SHORT_MODE
+    attn_mod._SHORT_MODE = "1"
     try:
         o = qkv_attention(qkv, H)
     finally:
-        attn_mod._USE_SHORT = old
+        attn_mod._SHORT_MODE = old
     fns = [type(o.grad_fn).__name__] + [type(f[0]).__name__ for f in o.grad_fn.next_functions if f[0] is not None]
     assert any("ShortAttn" in n for n in fns), fns
     ref = qkv_attention_reference(qkv.detach().float(), H)
