@@ -28,7 +28,8 @@ bool aligned16(const torch::Tensor& t) { return reinterpret_cast<uintptr_t>(t.da
 // C = opA(a) opB(b) (+ bias) with an optional fused epilogue.
 //   a_mn=false: a is [M, K]; a_mn=true: a is [K, M].   b_mn=false: b is [N, K]; b_mn=true: b is [K, N].
 //   epi: 0 none, 1 GELU, 2 ReLU, 3 res + gamma * (acc + bias).  want_aux: also return acc + bias.
-//   epi 4 / 5 (activation backward: C = acc * GELU'(res) / acc * [res > 0]): res = pre-activation [M, N].
+//   epi 4 / 5 (activation backward: C = acc * GELU'(res) / acc * [res > 0]): res = pre-activation [M, N];
+//   epi 8: C = acc * res (res = a stored activation derivative [M, N]).
 //   colsum: optional [N] output that receives (or, colsum_acc, accumulates) the column sums of C.
 std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> bias, bool a_mn,
                                    bool b_mn, int64_t epi, bool want_aux, c10::optional<torch::Tensor> res,
@@ -77,14 +78,14 @@ std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::option
         g.res = reinterpret_cast<const __nv_bfloat16*>(res_c.data_ptr());
         g.gamma = reinterpret_cast<const __nv_bfloat16*>(gamma_c.data_ptr());
     }
-    if (epi == 4 || epi == 5) {
-        TORCH_CHECK(res.has_value() && res->defined(), "gemm_tc: epilogues 4/5 need the pre-activation (res)");
+    if (epi == 4 || epi == 5 || epi == 8) {
+        TORCH_CHECK(res.has_value() && res->defined(), "gemm_tc: epilogues 4/5/8 need the pre-activation (res)");
         res_c = res->contiguous();
         TORCH_CHECK(res_c.numel() == M * N && res_c.scalar_type() == torch::kBFloat16 && aligned16(res_c),
                     "gemm_tc: pre-activation must be bf16 [M, N]");
         g.res = reinterpret_cast<const __nv_bfloat16*>(res_c.data_ptr());
     }
-    TORCH_CHECK(epi >= 0 && epi <= 5, "gemm_tc: unknown epilogue");
+    TORCH_CHECK((epi >= 0 && epi <= 5) || epi == 8, "gemm_tc: unknown epilogue");
     torch::Tensor colsum_t;
     if (colsum.has_value() && colsum->defined()) {
         colsum_t = *colsum;

@@ -202,13 +202,16 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, EpiOut& eo, in
         row_load(lane, r, g.res + base, g.ldc, rows_valid, ncols);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = g.alpha * v[i] + g.beta * r[i];
-    } else if (g.epi == 4 || g.epi == 5) {
+    } else if (g.epi == 4 || g.epi == 5 || g.epi == 8) {
         // activation backward: the product is the gradient w.r.t. the activation output
         float p[32];
         row_load(lane, p, g.res + base, g.ldc, rows_valid, ncols);
         if (g.epi == 4) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= gelu_grad_f(p[i]);
+        } else if (g.epi == 8) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= p[i];     // res holds the stored derivative
         } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = p[i] > 0.f ? v[i] : 0.f;

@@ -24,6 +24,7 @@ struct GemmArgs {
     int64_t ldc;
     int epi;                    // 0 none, 1 GELU(erf), 2 ReLU, 3 res + gamma * (acc + bias),
                                 // 4 acc * GELU'(res), 5 acc * [res > 0]   (res = pre-activation, backward)
+                                // 8 acc * res (res = a stored activation derivative, backward)
                                 // 6 alpha * (acc + bias) + beta * res,
                                 // 7 row maximum of acc + bias -> rmax (C is not written)
     float* colacc;              // optional fp32 [N]: += column sums of the stored (bf16-rounded) output

@@ -103,8 +103,9 @@ class MSDeformAttn(nn.Module):
         if padding_mask is not None:
             value = value.masked_fill(padding_mask[..., None], 0.0)
         value = value.view(B, S, H, self.d_model // H)
-        off = ops.linear(query, self.sampling_offsets.weight, self.sampling_offsets.bias).view(B, Lq, H, L, P, 2)
-        logits = ops.linear(query, self.attention_weights.weight, self.attention_weights.bias).view(B, Lq, H, L * P)
+        off, logits = ops.linear_pair(query, self.sampling_offsets.weight, self.sampling_offsets.bias,
+                                      self.attention_weights.weight, self.attention_weights.bias)
+        off, logits = off.view(B, Lq, H, L, P, 2), logits.view(B, Lq, H, L * P)
         out = ops.msda(value, shapes, ref, off, logits)
         if defer_bias:
             return ops.linear(out.to(query.dtype), self.output_proj.weight, None), self.output_proj.bias

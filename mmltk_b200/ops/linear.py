@@ -25,7 +25,7 @@ from ._ext import kernels
 from .gemm import _fits_nt, gemm_nn, gemm_nt, gemm_nt_epilogue, gemm_tn, gemm_tn_acc, tc_gemm_enabled
 from .gradacc import grad_target
 
-__all__ = ["linear", "linear_scale_residual", "mlp_scale_residual", "mlp_relu", "set_fused_linear"]
+__all__ = ["linear", "linear_pair", "linear_scale_residual", "mlp_scale_residual", "mlp_relu", "set_fused_linear"]
 
 _ACTS = {None: 0, "none": 0, "gelu": 1, "relu": 2}
 _COLSUM_CAP = 16384   # widest output whose column sums the GEMM epilogue accumulates (its fp32 scratch)
@@ -159,6 +159,48 @@ def linear(x: torch.Tensor, w: torch.Tensor, b=None, act=None) -> torch.Tensor:
     return _act(F.linear(x, w.to(x.dtype), None if b is None else b.to(x.dtype)), _ACTS[act])
 
 
+class _LinearPair(torch.autograd.Function):
+    """(x W1^T + b1, x W2^T + b2): two linears that read the same input as one autograd node, so the
+    input gradient is g1 W1 + g2 W2 from two GEMMs, the second accumulating into the first (beta = 1),
+    instead of two GEMMs and a separate add of the two gradients."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2):
+        shp = x.shape
+        x2 = _2d(x, shp[-1])
+        y1, y2 = gemm_nt(x2, w1, b1), gemm_nt(x2, w2, b2)
+        ctx.save_for_backward(x2, w1, w2)
+        ctx.params = (w1, b1, w2, b2)
+        ctx.shp = shp
+        return y1.view(*shp[:-1], w1.shape[0]), y2.view(*shp[:-1], w2.shape[0])
+
+    @staticmethod
+    def backward(ctx, g1, g2):
+        x2, w1, w2 = ctx.saved_tensors
+        k = kernels()
+        outs = []
+        gx = None
+        for g, w, wp, bp in ((g1, w1, ctx.params[0], ctx.params[1]), (g2, w2, ctx.params[2], ctx.params[3])):
+            if g is None:
+                outs += [None, None]
+                continue
+            g = _2d(g, w.shape[0])
+            wt, bt = grad_target(wp), grad_target(bp)
+            gb = k.colsum(g, None, bt) if bp is not None else None
+            gw = gemm_tn(g, x2) if wt is None else gemm_tn_acc(g, x2, wt)
+            gx = gemm_nn(g, w) if gx is None else gx.addmm_(g, w)
+            outs += [None if wt is not None else gw, None if bt is not None else gb]
+        return (None if gx is None else gx.view(ctx.shp)), *outs
+
+
+def linear_pair(x, w1, b1, w2, b2):
+    """Two linears of the same input (the deformable attention's sampling offsets and attention
+    weights), one autograd node whose input gradient needs no separate add."""
+    if _ok(x, w1) and _ok(x, w2) and b1 is not None and b2 is not None and torch.is_grad_enabled():
+        return _LinearPair.apply(x, w1, b1, w2, b2)
+    return linear(x, w1, b1), linear(x, w2, b2)
+
+
 def linear_scale_residual(x, w, b, gamma, res):
     if _ok(x, w) and gamma.dtype == x.dtype:
         return _LinearScaleResidual.apply(x, w, b, gamma, res)
@@ -167,25 +209,27 @@ def linear_scale_residual(x, w, b, gamma, res):
 
 class _MlpScaleResidual(torch.autograd.Function):
     """y = res + gamma * (fc2(GELU(fc1(x)))) -- the ViT MLP sub-block as one autograd node, so that
-    the backward can fuse across the two layers: the fc2 input-gradient GEMM applies GELU' of the
-    saved fc1 pre-activation in its epilogue and accumulates the fc1 bias gradient from the same
-    tile (no separate activation-backward pass over the [tokens, 4C] gradient)."""
+    the backward can fuse across the two layers: the fc2 input-gradient GEMM multiplies by the
+    stored GELU'(fc1 pre-activation) in its epilogue and accumulates the fc1 bias gradient from the
+    same tile (no separate activation-backward pass over the [tokens, 4C] gradient).  Forward: fc1
+    GEMM, one GELU pass that also stores GELU'(pre) (no erf in the GEMM epilogue), fc2 with the
+    LayerScale + residual epilogue."""
 
     @staticmethod
     def forward(ctx, x, w1, b1, w2, b2, gamma, res):
         shp = x.shape
         x2 = _2d(x, shp[-1])
         r2 = _2d(res, w2.shape[0])
-        h, pre1 = gemm_nt_epilogue(x2, w1, b1, "gelu", force=True)
+        h, d1 = kernels().gelu_fwd_deriv(gemm_nt(x2, w1, b1))
         y, pre2 = gemm_nt_epilogue(h, w2, b2, "scale_residual", r2, gamma, force=True)
-        ctx.save_for_backward(x2, w1, pre1, h, w2, gamma, pre2)
+        ctx.save_for_backward(x2, w1, d1, h, w2, gamma, pre2)
         ctx.params = (w1, b1, w2, b2, gamma)
         ctx.shp = shp
         return y.view(*shp[:-1], w2.shape[0])
 
     @staticmethod
     def backward(ctx, gy):
-        x2, w1, pre1, h, w2, gamma, pre2 = ctx.saved_tensors
+        x2, w1, d1, h, w2, gamma, pre2 = ctx.saved_tensors
         k = kernels()
         wt1, bt1, wt2, bt2, gt = (grad_target(p) for p in ctx.params)
         g = _2d(gy, w2.shape[0])
@@ -196,8 +240,8 @@ class _MlpScaleResidual(torch.autograd.Function):
             gb2 = k.colsum(g_pre2, None, bt2)
         gw2 = gemm_tn(g_pre2, h) if wt2 is None else gemm_tn_acc(g_pre2, h, wt2)
         gb1 = bt1 if bt1 is not None else torch.empty(w1.shape[0], device=g.device, dtype=w1.dtype)
-        # fc2 input gradient, GELU backward and the fc1 bias gradient in one GEMM launch
-        g_pre1 = k.gemm_tc(g_pre2, w2, None, False, True, 4, False, pre1, None, gb1, bt1 is not None)[0]
+        # fc2 input gradient, GELU backward (x stored GELU') and the fc1 bias gradient in one GEMM launch
+        g_pre1 = k.gemm_tc(g_pre2, w2, None, False, True, 8, False, d1, None, gb1, bt1 is not None)[0]
         gw1 = gemm_tn(g_pre1, x2) if wt1 is None else gemm_tn_acc(g_pre1, x2, wt1)
         gx = gemm_nn(g_pre1, w1)
         none_if = lambda t, v: None if t is not None else v
@@ -206,12 +250,8 @@ class _MlpScaleResidual(torch.autograd.Function):
 
 
 def mlp_scale_residual(x, w1, b1, w2, b2, gamma, res):
-    """res + gamma * (GELU(x W1^T + b1) W2^T + b2).
-
-    The cross-layer fused backward is opt-in (``MMLTK_FUSED_MLP=1``): measured on B200 for the
-    RF-DETR-M ViT (10.4k tokens x 384 -> 1536) the GELU' epilogue leaves the tcgen05 GEMM
-    epilogue-bound (~75 us per layer) and the step ~0.1 ms slower than cuBLAS + the separate
-    single-pass activation/bias kernel."""
+    """res + gamma * (GELU(x W1^T + b1) W2^T + b2); the cross-layer fused backward with
+    ``MMLTK_FUSED_MLP=1``."""
     if (_state["fused_mlp"] and _ok(x, w1) and _ok(x, w2.new_empty(8, w2.shape[1])) and gamma.dtype == x.dtype
             and w1.shape[0] % 128 == 0 and tc_gemm_enabled()):
         x2 = x.reshape(-1, x.shape[-1])

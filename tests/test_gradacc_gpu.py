@@ -146,7 +146,16 @@ def test_fused_detection_losses_match_per_layer_statement(ia_bce):
 def test_mlp_block_fused_backward_matches_unfused():
     import importlib
     from mmltk_b200.ops.linear import linear, linear_scale_residual, mlp_scale_residual
-    importlib.import_module("mmltk_b200.ops.linear")._state["fused_mlp"] = True   # opt-in path under test
+    state = importlib.import_module("mmltk_b200.ops.linear")._state
+    old = state["fused_mlp"]
+    state["fused_mlp"] = True   # the path under test
+    try:
+        _mlp_block_fused_vs_unfused(linear, linear_scale_residual, mlp_scale_residual)
+    finally:
+        state["fused_mlp"] = old
+
+
+def _mlp_block_fused_vs_unfused(linear, linear_scale_residual, mlp_scale_residual):
     torch.manual_seed(0)
     C = 384
     x = (torch.randn(2, 650, C, device="cuda") * 0.5).bfloat16()

@@ -660,3 +660,24 @@ def test_gemm_tc_weight_gradient_accumulates(cuda_device, M, N, K):
     plain = k.gemm_tc(a.to(cuda_device), b.to(cuda_device), None, True, True)[0]
     ref0 = a.float().t() @ b.float()
     assert (plain.float().cpu() - ref0).abs().max().item() < 1e-2 * ref0.abs().max().item()
+
+
+def test_linear_pair_matches_fp32(cuda_device):
+    """Two linears of one input as one node (input gradient accumulated by the second GEMM) vs fp32."""
+    g = torch.Generator().manual_seed(11)
+    M, K, N1, N2 = 3900, 256, 256, 128
+    bf = lambda t: t.to(torch.bfloat16).float()
+    x = bf(torch.randn(M, K, generator=g))
+    w1, b1 = bf(torch.randn(N1, K, generator=g) * K ** -0.5), bf(torch.randn(N1, generator=g))
+    w2, b2 = bf(torch.randn(N2, K, generator=g) * K ** -0.5), bf(torch.randn(N2, generator=g))
+    g1, g2 = bf(torch.randn(M, N1, generator=g)), bf(torch.randn(M, N2, generator=g))
+    ins = [t.clone().requires_grad_() for t in (x, w1, b1, w2, b2)]
+    r1 = torch.nn.functional.linear(ins[0], ins[1], ins[2])
+    r2 = torch.nn.functional.linear(ins[0], ins[3], ins[4])
+    torch.autograd.backward((r1, r2), (g1, g2))
+    dins = [t.to(cuda_device, torch.bfloat16).requires_grad_() for t in (x, w1, b1, w2, b2)]
+    y1, y2 = ops.linear_pair(*dins)
+    torch.autograd.backward((y1, y2), (g1.to(cuda_device, torch.bfloat16), g2.to(cuda_device, torch.bfloat16)))
+    assert _rel(y1.float().cpu(), r1) < 2e-2 and _rel(y2.float().cpu(), r2) < 2e-2
+    for a, r in zip(dins, ins):
+        assert _rel(a.grad.float().cpu(), r.grad) < 3e-2
