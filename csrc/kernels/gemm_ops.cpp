@@ -166,6 +166,42 @@ void gemm_tc_acc(torch::Tensor a, torch::Tensor b, bool a_mn, bool b_mn, torch::
     check_cuda(launch_gemm_tc(g, a_mn, b_mn, a.stride(0), b.stride(0), cur_stream()), "gemm_tc_acc");
 }
 
+// 3 x 3 convolution, stride 1, zero padding 1, of a channels-last input x [B, H, W, C] with weights
+// w [N, 3, 3, C] (taps row-major, channel fastest) on the tcgen05 GEMM: each tile of `rows` image rows
+// is one product of [rows * W pixels, 9 C] x [9 C, N] whose A tiles are read straight from x (one
+// 4-D tensor load per tap and 64-channel chunk; the padding is the loads' zero fill).  Returns y
+// [B, H, W, N].  Needs C % 64 == 0, N % 16 == 0 and rows * W <= 128 for a row count dividing H.
+torch::Tensor conv3x3_tc(torch::Tensor x, torch::Tensor w) {
+    TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.dim() == 4 && w.dim() == 4, "conv3x3_tc: 4-D CUDA tensors expected");
+    TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && w.scalar_type() == torch::kBFloat16, "conv3x3_tc: bf16 only");
+    TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && aligned16(x) && aligned16(w),
+                "conv3x3_tc: contiguous, 16-byte aligned tensors expected");
+    const int64_t B = x.size(0), H = x.size(1), W = x.size(2), C = x.size(3), N = w.size(0);
+    TORCH_CHECK(w.size(1) == 3 && w.size(2) == 3 && w.size(3) == C, "conv3x3_tc: weights must be [N, 3, 3, C]");
+    TORCH_CHECK(C % 64 == 0 && N % 16 == 0 && B > 0 && H > 0 && W > 0, "conv3x3_tc: C % 64 and N % 16 required");
+    const int rows = conv3x3_tc_rows(static_cast<int>(H), static_cast<int>(W));
+    TORCH_CHECK(rows > 0, "conv3x3_tc: no row count r with r * W <= 128 divides H");
+    at::cuda::CUDAGuard guard(x.device());
+    auto y = torch::empty({B, H, W, N}, x.options());
+    GemmArgs g{};
+    g.A = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+    g.B = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+    g.C = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+    g.status = status_word(x.device()).data_ptr<int>();
+    g.M = static_cast<int>(rows * W);
+    g.N = static_cast<int>(N);
+    g.K = static_cast<int>(9 * C);
+    g.ldc = N;
+    g.batch = static_cast<int>(B * (H / rows));
+    g.bs_c = static_cast<int64_t>(rows) * W * N;
+    g.conv_w = static_cast<int>(W);
+    g.conv_rows = rows;
+    g.conv_groups = static_cast<int>(H / rows);
+    g.conv_c = static_cast<int>(C);
+    check_cuda(launch_gemm_tc(g, false, false, 9 * C, 9 * C, cur_stream()), "conv3x3_tc");
+    return y;
+}
+
 // Batched products through 2-D tensor maps (see GemmArgs): a / b are the whole operand matrices
 // (row-major, unit column stride); batch i reads them at tile coordinates shifted by
 // i * (a_bk, a_bm) and i * (b_bk, b_bn).  Returns C [batch, M, N] bf16, or for epi 7 the row
@@ -250,6 +286,8 @@ void register_gemm_ops(pybind11::module& m) {
           py::arg("gamma") = py::none(), py::arg("colsum") = py::none(), py::arg("colsum_acc") = false);
     m.def("gemm_tc_acc", &gemm_tc_acc, py::arg("a"), py::arg("b"), py::arg("a_mn"), py::arg("b_mn"),
           py::arg("out"));
+    m.def("conv3x3_tc", &conv3x3_tc, py::arg("x"), py::arg("w"));
+    m.def("conv3x3_tc_rows", &conv3x3_tc_rows, py::arg("H"), py::arg("W"));
     m.def("gemm_tc_status", &gemm_tc_status);
     m.def("gemm_tc_batched", &gemm_tc_batched, py::arg("a"), py::arg("b"), py::arg("bias"), py::arg("a_mn"),
           py::arg("b_mn"), py::arg("batch"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("a_bk"), py::arg("a_bm"),

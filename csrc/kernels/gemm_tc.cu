@@ -298,10 +298,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 // extent are skipped (they only feed output rows/columns that are masked)
                 const int a_boxes = A_MN ? min(BM / 64, (g.M - m0 + 63) / 64) : 1;
                 const int b_boxes = B_MN ? min(BN / 64, (g.N - n0 + 63) / 64) : 1;
-                const uint32_t bytes = (A_MN ? a_boxes * 8192 : kATile) + (B_MN ? b_boxes * 8192 : kBTile);
+                const uint32_t a_bytes = g.conv_w ? static_cast<uint32_t>(g.conv_w * g.conv_rows * 128)
+                                                  : (A_MN ? a_boxes * 8192 : kATile);
+                const uint32_t bytes = a_bytes + (B_MN ? b_boxes * 8192 : kBTile);
                 // batch bt: the operands' tile coordinates shifted by bt * (shift along K, along M / N)
                 const int bt = sch.batch_of(u);
                 const int ak = bt * g.a_bk, am = bt * g.a_bm, bk = bt * g.b_bk, bn_ = bt * g.b_bn;
+                // convolution tile bt: image and first output row
+                const int cimg = g.conv_w ? bt / g.conv_groups : 0;
+                const int cy0 = g.conv_w ? (bt % g.conv_groups) * g.conv_rows : 0;
+                const int cchunks = g.conv_w ? g.conv_c / BK : 1;
                 for (int kt = kt0; kt < kt1; ++kt, ++it) {
                     const int s = it % kStages;
                     const uint32_t ph = (it / kStages) & 1;
@@ -317,6 +323,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                     if (A_MN) {
                         for (int q = 0; q < a_boxes; ++q)
                             tma_load_2d(&tmA, &ctl->full[s], a + q * 8192, am + m0 + 64 * q, ak + k0);
+                    } else if (g.conv_w) {
+                        // tap (dy, dx) and channel chunk of this K tile; out-of-image pixels read as zero
+                        const int tap = kt / cchunks, c0 = (kt % cchunks) * BK;
+                        tma_load_4d(&tmA, &ctl->full[s], a, c0, tap % 3 - 1, cy0 + tap / 3 - 1, cimg);
                     } else {
                         tma_load_2d(&tmA, &ctl->full[s], a, ak + k0, am + m0);
                     }
@@ -743,6 +753,28 @@ bool make_map(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, i
     return r == CUDA_SUCCESS;
 }
 
+// Input map of the implicit-GEMM convolution: channels-last bf16 [images, H, W, C], box {64 channels,
+// W, rows, 1}, 128B swizzle (each pixel's 64 channels are one 128-byte row of the A tile), zero fill
+// outside the image.
+bool make_conv_map(CUtensorMap* map, const void* ptr, int64_t C, int64_t W, int64_t H, int64_t images, int rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                          static_cast<cuuint64_t>(images)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(C * 2), static_cast<cuuint64_t>(C * W * 2),
+                             static_cast<cuuint64_t>(C * W * H * 2)};
+    cuuint32_t box[4] = {64, static_cast<cuuint32_t>(W), static_cast<cuuint32_t>(rows), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        std::fprintf(stderr, "gemm_tc: convolution input map failed (%d): C %lld W %lld H %lld images %lld rows %d\n",
+                     static_cast<int>(r), static_cast<long long>(C), static_cast<long long>(W),
+                     static_cast<long long>(H), static_cast<long long>(images), rows);
+    return r == CUDA_SUCCESS;
+}
+
 // Output map for the epilogue's tensor stores: bf16 [batch, rows, cols] (row pitch `pitch`, batch
 // stride `bstride`, elements), 32 x 32 boxes, 64-byte swizzle; stores past the extents are clipped.
 bool make_store_map(CUtensorMap* map, const void* ptr, int64_t cols, int64_t rows, int64_t batch, int64_t pitch,
@@ -792,6 +824,12 @@ int pick_bn(int M, int N) {
 }
 
 size_t gemm_tc_smem_bytes() { return Tile<256>::kSmemBytes; }
+
+int conv3x3_tc_rows(int H, int W) {
+    for (int r = std::min(H, BM / std::max(1, W)); r >= 1; --r)
+        if (H % r == 0) return r;
+    return 0;
+}
 
 namespace {
 
@@ -925,7 +963,16 @@ cudaError_t launch_gemm_tc(const GemmArgs& g_in, bool a_mn, bool b_mn, int64_t l
     // batched products read every batch through one map over the whole operand matrix
     const int64_t ai = g.a_inner ? g.a_inner : (a_mn ? g.M : g.K), ao = g.a_outer ? g.a_outer : (a_mn ? g.K : g.M);
     const int64_t bi = g.b_inner ? g.b_inner : (b_mn ? g.N : g.K), bo = g.b_outer ? g.b_outer : (b_mn ? g.K : g.N);
-    bool ok = a_mn ? make_map(&ta, g.A, ai, ao, lda, 64) : make_map(&ta, g.A, ai, ao, lda, BM);
+    bool ok;
+    if (g.conv_w) {
+        if (a_mn || b_mn || g.conv_c % BK != 0 || g.K != 9 * g.conv_c || g.M != g.conv_w * g.conv_rows ||
+            g.M > BM || g.batch % g.conv_groups != 0 || g.ws != nullptr)
+            return cudaErrorInvalidValue;
+        ok = make_conv_map(&ta, g.A, g.conv_c, g.conv_w, static_cast<int64_t>(g.conv_groups) * g.conv_rows,
+                           g.batch / g.conv_groups, g.conv_rows);
+    } else {
+        ok = a_mn ? make_map(&ta, g.A, ai, ao, lda, 64) : make_map(&ta, g.A, ai, ao, lda, BM);
+    }
     ok = ok && (b_mn ? make_map(&tb, g.B, bi, bo, ldb, 64) : make_map(&tb, g.B, bi, bo, ldb, b_rows));
     if (!ok) return cudaErrorInvalidValue;
     Sched sch;

@@ -40,6 +40,13 @@ struct GemmArgs {
     float* rmax;                // epi 7: fp32 [2, batch, M], one partial maximum per half of the columns
     // extents of the 2-D operand matrices the tensor maps cover (0: derived from M / N / K)
     int64_t a_inner, a_outer, b_inner, b_outer;
+    // Implicit-GEMM 3 x 3 convolution (stride 1, zero padding 1) of a channels-last input [B, H, W, C]
+    // (conv_w > 0): the product is batched over tiles of conv_rows image rows (batch index =
+    // image * H / conv_rows + row group, M = conv_rows * W output pixels per tile), K = 9 taps x C
+    // ordered (tap, channel) with taps row-major over (dy, dx); the A tile of K tile kt is the
+    // input box at (channel chunk, x + dx - 1, y + dy - 1, image), loaded through a 4-D tensor map
+    // whose zero fill provides the padding.  B = weights [N, 9 * C].
+    int conv_w, conv_rows, conv_groups, conv_c;
     // diagnostics (environment MMLTK_GEMM_DIAG, bit mask): 1 = the epilogue reads the accumulator but
     // stores nothing, which times the main loop and the tensor-memory hand-off alone; 2 = the MMA warp
     // commits every stage without issuing its MMAs, which times the loads and the epilogue alone
@@ -47,6 +54,9 @@ struct GemmArgs {
 };
 
 size_t gemm_tc_smem_bytes();
+// Image rows per tile of the implicit-GEMM 3 x 3 convolution: the largest r with r * W <= 128 that
+// divides H (0 if none).
+int conv3x3_tc_rows(int H, int W);
 // K splits worth using for this shape (1 = none); only for plain products (no bias / epilogue).
 int gemm_tc_splits(int M, int N, int K, bool b_mn);
 // 0: single-CTA or CTA-pair tiles chosen per shape; 1: single-CTA only; 2: CTA pairs where allowed.

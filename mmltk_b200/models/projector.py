@@ -15,7 +15,8 @@ empty ``Sequential``, so a P4-only model has the reference's state-dict
 layout), "P6" (scale 1/4) a stride-2 max-pool of the previous level's output.
 Features are channels-last [B, h, w, C] throughout (LayerNorm2d is then a
 plain last-dim LayerNorm, 1x1 convs and the 2x2/stride-2 transposed convs are
-GEMMs); 3x3 convs run as cuDNN channels-last convolutions.
+GEMMs); 3x3 convs are cuDNN channels-last convolutions, or with ``MMLTK_TC_CONV=1`` the stride-1
+ones implicit GEMMs on the tcgen05 kernel (``ops.conv3x3``).
 """
 from __future__ import annotations
 
@@ -50,6 +51,8 @@ class ConvX(nn.Module):
         if self.k == 1 and self.s == 1:
             w = self.conv.weight.view(self.conv.weight.shape[0], -1)
             y = ops.linear(x, w)
+        elif self.k == 3 and self.s == 1:
+            y = ops.conv3x3(x, self.conv.weight)      # cuDNN, or the tcgen05 implicit GEMM (opt-in)
         else:
             xc = x.permute(0, 3, 1, 2)
             y = F.conv2d(xc, self.conv.weight.to(xc.dtype), None, self.s, self.k // 2).permute(0, 2, 3, 1)

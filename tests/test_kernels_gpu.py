@@ -681,3 +681,40 @@ def test_linear_pair_matches_fp32(cuda_device):
     assert _rel(y1.float().cpu(), r1) < 2e-2 and _rel(y2.float().cpu(), r2) < 2e-2
     for a, r in zip(dins, ins):
         assert _rel(a.grad.float().cpu(), r.grad) < 3e-2
+
+
+@pytest.mark.parametrize("B,H,W,C,N", [(8, 36, 36, 128, 128), (4, 40, 40, 64, 128), (48, 10, 7, 128, 64),
+                                       (32, 24, 24, 64, 64)])
+def test_conv3x3_implicit_gemm_matches_fp32(cuda_device, B, H, W, C, N):
+    """3x3 / stride 1 / padding 1 convolution of channels-last features on the tcgen05 kernel
+    (forward and input gradient as implicit GEMMs with zero-filled tap loads) vs fp32 autograd."""
+    import importlib
+    from mmltk_b200.ops.conv import conv3x3, conv3x3_ok
+    state = importlib.import_module("mmltk_b200.ops.conv")._state
+    old = state["enabled"]
+    state["enabled"] = True      # the tensor-core path is opt-in; test it explicitly
+    try:
+        _conv3x3_case(cuda_device, conv3x3, conv3x3_ok, B, H, W, C, N)
+    finally:
+        state["enabled"] = old
+
+
+def _conv3x3_case(cuda_device, conv3x3, conv3x3_ok, B, H, W, C, N):
+    g = torch.Generator().manual_seed(B * H + C)
+    bf = lambda t: t.to(torch.bfloat16).float()
+    x = bf(torch.randn(B, H, W, C, generator=g))
+    w = bf(torch.randn(N, C, 3, 3, generator=g) * (9 * C) ** -0.5)
+    gy = bf(torch.randn(B, H, W, N, generator=g))
+    xr, wr = x.clone().requires_grad_(), w.clone().requires_grad_()
+    yr = torch.nn.functional.conv2d(xr.permute(0, 3, 1, 2), wr, None, 1, 1).permute(0, 2, 3, 1)
+    yr.backward(gy)
+    xd = x.to(cuda_device, torch.bfloat16).requires_grad_()
+    wd = w.to(cuda_device, torch.bfloat16).requires_grad_()
+    assert conv3x3_ok(xd, wd)
+    yd = conv3x3(xd, wd)
+    yd.backward(gy.to(cuda_device, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert kernels().gemm_tc_status(0) == 0
+    assert _rel(yd.float().cpu(), yr) < 2e-2
+    assert _rel(xd.grad.float().cpu(), xr.grad) < 2e-2
+    assert _rel(wd.grad.float().cpu(), wr.grad) < 2e-2
