@@ -20,7 +20,12 @@ int num_sms();
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st,
                                  const void* res = nullptr, void* sum = nullptr, const void* pos = nullptr,
-                                 void* y2 = nullptr, const void* rbias = nullptr, const void* rscale = nullptr);
+                                 void* y2 = nullptr, const void* rbias = nullptr, const void* rscale = nullptr,
+                                 const int* ymap = nullptr, int64_t yld = 0, int64_t wgroup_rows = 0);
+// wgroup_rows > 0: the rows come in groups of that many and group g uses row g of w / b ([groups, C]).
+// ymap (optional, int32 [rows]): y row of input row r is ymap[r] (none when negative), row pitch yld --
+// a normalised row goes straight to its place in a differently laid out (e.g. un-windowed,
+// channel-concatenated) output.
 // One launch: gx, and gw / gb written (or added into, `accumulate`) by the last CTA.
 // gy2 (optional): a second output gradient added to gy (the y + pos output of the forward).
 // gres (optional): added to gx (the gradient x receives through a residual branch).
@@ -29,7 +34,11 @@ cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* 
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
                                  bool accumulate, cudaStream_t st, const void* gy2 = nullptr,
-                                 const void* gres = nullptr, void* gbias2 = nullptr, bool accumulate2 = false);
+                                 const void* gres = nullptr, void* gbias2 = nullptr, bool accumulate2 = false,
+                                 const int* gmap = nullptr, int64_t gld = 0, int64_t group_rows = 0);
+// group_rows > 0: per-group weights as in the forward; gw / gb are [groups, C].
+// gmap (optional, int32 [rows]): the gradient of input row r is gy row gmap[r] (zero when negative),
+// row pitch gld -- the backward of a forward with ymap.
 
 // ---------------------------------------------------------------- attention (tcgen05)
 // Softmax attention, head dim 64, from the packed projection qkv [nseq * L rows, >= 3 * H * 64]

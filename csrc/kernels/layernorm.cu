@@ -26,6 +26,9 @@ struct LnFwdExtra {
     T* y2;
     const W* rbias;
     const W* rscale;   // with res: normalise res + rscale * (x + rbias) (a LayerScale residual)
+    const int* ymap;   // y row of input row r (negative: not stored); null: row r
+    int64_t yld;       // y row pitch with ymap
+    int64_t wgroup_rows;   // > 0: rows come in groups of this many, group g normalised with w / b row g
 };
 
 template <typename T, typename W, int kMaxVec>
@@ -81,17 +84,21 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, co
             }
         }
         const float rstd = rsqrtf(warp_sum(q) / C + eps);
-        T* yr = y + r * C;
+        const int64_t orow = ex.ymap != nullptr ? ex.ymap[r] : r;
+        T* yr = y + orow * (ex.ymap != nullptr ? ex.yld : C);
+        const int64_t woff = ex.wgroup_rows > 0 ? (r / ex.wgroup_rows) * C : 0;
+        const W* __restrict__ wr = w + woff;
+        const W* __restrict__ br = b + woff;
 #pragma unroll
         for (int k = 0; k < kMaxVec; ++k) {
             const int i = lane + 32 * k;
-            if (i < nv) {
+            if (i < nv && orow >= 0) {
                 const int c0 = 4 * i;
                 float4 o;
-                o.x = (v[k].x - mean) * rstd * to_f(w[c0]) + to_f(b[c0]);
-                o.y = (v[k].y - mean) * rstd * to_f(w[c0 + 1]) + to_f(b[c0 + 1]);
-                o.z = (v[k].z - mean) * rstd * to_f(w[c0 + 2]) + to_f(b[c0 + 2]);
-                o.w = (v[k].w - mean) * rstd * to_f(w[c0 + 3]) + to_f(b[c0 + 3]);
+                o.x = (v[k].x - mean) * rstd * to_f(wr[c0]) + to_f(br[c0]);
+                o.y = (v[k].y - mean) * rstd * to_f(wr[c0 + 1]) + to_f(br[c0 + 1]);
+                o.z = (v[k].z - mean) * rstd * to_f(wr[c0 + 2]) + to_f(br[c0 + 2]);
+                o.w = (v[k].w - mean) * rstd * to_f(wr[c0 + 3]) + to_f(br[c0 + 3]);
                 store4(yr + c0, o);
                 if (ex.pos != nullptr) {   // second output y + pos (e.g. a query with its position embedding)
                     const float4 p4 = load4(ex.pos + r * C + c0);
@@ -113,6 +120,7 @@ template <>
 struct Raw4<__nv_bfloat16> {
     uint2 v;
     __device__ __forceinline__ void load(const __nv_bfloat16* p) { v = *reinterpret_cast<const uint2*>(p); }
+    __device__ __forceinline__ void zero() { v = make_uint2(0u, 0u); }
     __device__ __forceinline__ float4 widen() const {
         const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y);
         return make_float4(a.x, a.y, b.x, b.y);
@@ -122,6 +130,7 @@ template <>
 struct Raw4<float> {
     float4 v;
     __device__ __forceinline__ void load(const float* p) { v = *reinterpret_cast<const float4*>(p); }
+    __device__ __forceinline__ void zero() { v = make_float4(0.f, 0.f, 0.f, 0.f); }
     __device__ __forceinline__ float4 widen() const { return v; }
 };
 
@@ -187,12 +196,33 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                                                      W* __restrict__ gw, W* __restrict__ gb, int accumulate,
                                                      int64_t rows, int C, const T* __restrict__ gy2,
                                                      const T* __restrict__ gres, W* __restrict__ gbias2,
-                                                     int accumulate2) {
+                                                     int accumulate2, const int* __restrict__ gmap, int64_t gld,
+                                                     int64_t group_rows) {
     extern __shared__ float smem[];  // [warps][2][C]
+    // groups (group_rows > 0): blockIdx.y = group g, rows [g * group_rows, +group_rows), weight / bias
+    // row g, gradient accumulators, arrival counter and gw / gb row of that group
+    int64_t row_begin = 0;
+    if (group_rows > 0) {
+        const int g = blockIdx.y;
+        row_begin = g * group_rows;
+        rows = min(rows, row_begin + group_rows);
+        w += static_cast<int64_t>(g) * C;
+        gw += static_cast<int64_t>(g) * C;
+        gb += static_cast<int64_t>(g) * C;
+        acc_w += static_cast<int64_t>(g) * (kBias2 ? 3 : 2) * C;
+        acc_b += static_cast<int64_t>(g) * (kBias2 ? 3 : 2) * C;
+        counter += g;
+    }
+    // this row's output gradient: row gmap[r] of gy (pitch gld; none = zero) or row r
+    auto gy_row = [&](int64_t r) -> const T* {
+        if (gmap == nullptr) return gy + r * C;
+        const int g = gmap[r];
+        return g >= 0 ? gy + static_cast<int64_t>(g) * gld : nullptr;
+    };
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
     const int nwib = blockDim.x >> 5;
-    const int64_t warp = static_cast<int64_t>(blockIdx.x) * nwib + wib;
+    const int64_t warp = row_begin + static_cast<int64_t>(blockIdx.x) * nwib + wib;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * nwib;
     const int nv = C >> 2;
     float4 aw[kMaxVec], ab[kMaxVec], ad[kMaxVec];
@@ -211,12 +241,14 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
         if (r < rows) {
             nmean = mean_in[r];
             nrstd = rstd_in[r];
+            const T* gr0 = gy_row(r);
 #pragma unroll
             for (int k = 0; k < kMaxVec; ++k) {
                 const int i = lane + 32 * k;
                 if (i < nv) {
                     nx[k].load(x + r * C + 4 * i);
-                    ng[k].load(gy + r * C + 4 * i);
+                    if (gr0 != nullptr) ng[k].load(gr0 + 4 * i);
+                    else ng[k].zero();
                 }
             }
         }
@@ -236,12 +268,14 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
             if (rn < rows) {
                 nmean = mean_in[rn];
                 nrstd = rstd_in[rn];
+                const T* grn = gy_row(rn);
 #pragma unroll
                 for (int k = 0; k < kMaxVec; ++k) {
                     const int i = lane + 32 * k;
                     if (i < nv) {
                         nx[k].load(x + rn * C + 4 * i);
-                        ng[k].load(gy + rn * C + 4 * i);
+                        if (grn != nullptr) ng[k].load(grn + 4 * i);
+                        else ng[k].zero();
                     }
                 }
             }
@@ -252,12 +286,13 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
         // wide rows have no registers to spare for a second row
         for (int64_t r = warp; r < rows; r += nwarps) {
             float4 xv[kMaxVec], gv[kMaxVec];
+            const T* grr = gy_row(r);
 #pragma unroll
             for (int k = 0; k < kMaxVec; ++k) {
                 const int i = lane + 32 * k;
                 if (i < nv) {
                     xv[k] = load4(x + r * C + 4 * i);
-                    gv[k] = load4(gy + r * C + 4 * i);
+                    gv[k] = grr != nullptr ? load4(grr + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
                     if (gy2 != nullptr) {
                         const float4 g2 = load4(gy2 + r * C + 4 * i);
                         gv[k].x += g2.x; gv[k].y += g2.y; gv[k].z += g2.z; gv[k].w += g2.w;
@@ -344,9 +379,11 @@ void dispatch_vec(int C, F&& f) {
 
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st, const void* res,
-                                 void* sum, const void* pos, void* y2, const void* rbias, const void* rscale) {
+                                 void* sum, const void* pos, void* y2, const void* rbias, const void* rscale,
+                                 const int* ymap, int64_t yld, int64_t wgroup_rows) {
     if ((rbias != nullptr || rscale != nullptr) && res == nullptr) return cudaErrorInvalidValue;
     if ((res == nullptr) != (sum == nullptr) || (pos == nullptr) != (y2 == nullptr)) return cudaErrorInvalidValue;
+    if (ymap != nullptr && (pos != nullptr || yld < C || yld % 4 != 0)) return cudaErrorInvalidValue;
     if (rows == 0) return cudaSuccess;
     if (C % 4 != 0 || C > 4 * 32 * 12) return cudaErrorInvalidValue;
     const int threads = 256;
@@ -361,7 +398,7 @@ cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* 
                     static_cast<T*>(y), mean, rstd, rows, C, eps,
                     LnFwdExtra<T, Wt>{static_cast<const T*>(res), static_cast<T*>(sum), static_cast<const T*>(pos),
                                       static_cast<T*>(y2), static_cast<const Wt*>(rbias),
-                                      static_cast<const Wt*>(rscale)});
+                                      static_cast<const Wt*>(rscale), ymap, yld, wgroup_rows});
             });
             return cudaGetLastError();
         });
@@ -384,7 +421,12 @@ int ln_bwd_blocks(K kern, int threads, size_t smem, int64_t rows) {
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
                                  bool accumulate, cudaStream_t st, const void* gy2, const void* gres, void* gbias2,
-                                 bool accumulate2) {
+                                 bool accumulate2, const int* gmap, int64_t gld, int64_t group_rows) {
+    if (gmap != nullptr && (gy2 != nullptr || gld < C || gld % 4 != 0)) return cudaErrorInvalidValue;
+    const int64_t groups = group_rows > 0 ? (rows + group_rows - 1) / group_rows : 1;
+    if (group_rows > 0 && (rows % group_rows != 0 || groups > kMaxCounters || groups > 65535 ||
+                           groups * (gbias2 != nullptr ? 3 : 2) * C > kReduceAccFloats))
+        return cudaErrorInvalidValue;
     if (C % 4 != 0 || C > 4 * 32 * 12 || 3 * C > kReduceAccFloats) return cudaErrorInvalidValue;
     const ReduceScratch rs = reduce_scratch();
     if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
@@ -402,13 +444,16 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
                 if (smem >= 40 * 1024)
                     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
                 if (e != cudaSuccess) return;
-                const int blocks = ln_bwd_blocks(kern, threads, smem, rows);
-                kern<<<blocks, threads, smem, st>>>(static_cast<const T*>(gy), static_cast<const T*>(x),
+                // one resident wave over all groups
+                const int blocks = static_cast<int>(std::max<int64_t>(
+                    1, std::min<int64_t>(ln_bwd_blocks(kern, threads, smem, rows) / groups, (group_rows > 0 ? group_rows : rows) / 8 + 1)));
+                kern<<<dim3(blocks, static_cast<unsigned>(groups)), threads, smem, st>>>(static_cast<const T*>(gy), static_cast<const T*>(x),
                                                     static_cast<const Wt*>(w), mean, rstd, static_cast<T*>(gx), rs.acc,
                                                     rs.acc + C, rs.counters, static_cast<Wt*>(gw),
                                                     static_cast<Wt*>(gb), accumulate ? 1 : 0, rows, C,
                                                     static_cast<const T*>(gy2), static_cast<const T*>(gres),
-                                                    static_cast<Wt*>(gbias2), accumulate2 ? 1 : 0);
+                                                    static_cast<Wt*>(gbias2), accumulate2 ? 1 : 0, gmap, gld,
+                                                    group_rows);
             };
             dispatch_vec(C, [&](auto nvl) {
                 if (gbias2 != nullptr) run(nvl, std::true_type{});

@@ -137,6 +137,115 @@ std::vector<torch::Tensor> layernorm_bwd(torch::Tensor gy, torch::Tensor x, torc
     return {gx, gw, gb, gb2};
 }
 
+// LayerNorm whose row r lands in row ymap[r] (none when negative) of `out` [R, ld] at column `col`:
+// e.g. the backbone taps, normalised straight into their un-windowed place in the projector's
+// channel-concatenated input.  Returns {mean, rstd}.
+std::vector<torch::Tensor> layernorm_fwd_map(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps,
+                                             torch::Tensor ymap, torch::Tensor out, int64_t col) {
+    TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "layernorm_fwd_map: x must be contiguous [rows, C]");
+    const int64_t rows = x.size(0), C = x.size(1);
+    TORCH_CHECK(w.scalar_type() == b.scalar_type() && w.numel() == C && b.numel() == C,
+                "layernorm_fwd_map: weight/bias must match C and share a dtype");
+    TORCH_CHECK(ymap.is_cuda() && ymap.scalar_type() == torch::kInt32 && ymap.numel() == rows && ymap.is_contiguous(),
+                "layernorm_fwd_map: ymap must be a contiguous int32 [rows] CUDA tensor");
+    TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.stride(1) == 1 && out.scalar_type() == x.scalar_type() &&
+                    col >= 0 && col + C <= out.size(1) && col % 4 == 0 && out.stride(0) % 4 == 0,
+                "layernorm_fwd_map: out must be a row-major [R, >= col + C] tensor of the x dtype");
+    at::cuda::CUDAGuard guard(x.device());
+    auto opts = x.options().dtype(torch::kFloat32);
+    auto mean = torch::empty({rows}, opts);
+    auto rstd = torch::empty({rows}, opts);
+    auto wc = w.contiguous(), bc = b.contiguous();
+    void* y = static_cast<char*>(out.data_ptr()) + col * out.element_size();
+    check_cuda(launch_layernorm_fwd(dtype_of(x), dtype_of(w), x.data_ptr(), wc.data_ptr(), bc.data_ptr(), y,
+                                    mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, static_cast<int>(C),
+                                    static_cast<float>(eps), cur_stream(), nullptr, nullptr, nullptr, nullptr, nullptr,
+                                    nullptr, ymap.data_ptr<int>(), out.stride(0)),
+               "layernorm_fwd_map");
+    return {mean, rstd};
+}
+
+// Backward of layernorm_fwd_map: the output gradient of row r is row gmap[r] of g [R, ld] at column
+// `col` (zero when negative).  Returns {gx, gw, gb} (gw / gb added into gw_acc / gb_acc when given).
+std::vector<torch::Tensor> layernorm_bwd_map(torch::Tensor g, int64_t col, torch::Tensor gmap, torch::Tensor x,
+                                             torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
+                                             c10::optional<torch::Tensor> gw_acc, c10::optional<torch::Tensor> gb_acc) {
+    TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "layernorm_bwd_map: x must be contiguous [rows, C]");
+    const int64_t rows = x.size(0), C = x.size(1);
+    TORCH_CHECK(gmap.is_cuda() && gmap.scalar_type() == torch::kInt32 && gmap.numel() == rows && gmap.is_contiguous(),
+                "layernorm_bwd_map: gmap must be a contiguous int32 [rows] CUDA tensor");
+    TORCH_CHECK(g.is_cuda() && g.dim() == 2 && g.stride(1) == 1 && g.scalar_type() == x.scalar_type() && col >= 0 &&
+                    col + C <= g.size(1) && col % 4 == 0 && g.stride(0) % 4 == 0,
+                "layernorm_bwd_map: g must be a row-major [R, >= col + C] tensor of the x dtype");
+    at::cuda::CUDAGuard guard(x.device());
+    auto gx = torch::empty_like(x);
+    auto wc = w.contiguous();
+    const bool acc = gw_acc && gw_acc->defined() && gb_acc && gb_acc->defined();
+    if (acc)
+        TORCH_CHECK(gw_acc->is_contiguous() && gb_acc->is_contiguous() && gw_acc->numel() == C && gb_acc->numel() == C &&
+                        gw_acc->scalar_type() == w.scalar_type() && gb_acc->scalar_type() == w.scalar_type(),
+                    "layernorm_bwd_map: accumulation targets must be contiguous [C] of the weight dtype");
+    auto gw = acc ? *gw_acc : torch::empty_like(wc);
+    auto gb = acc ? *gb_acc : torch::empty_like(wc);
+    const void* gy = static_cast<const char*>(g.data_ptr()) + col * g.element_size();
+    check_cuda(launch_layernorm_bwd(dtype_of(x), dtype_of(w), gy, x.data_ptr(), wc.data_ptr(), mean.data_ptr<float>(),
+                                    rstd.data_ptr<float>(), gx.data_ptr(), gw.data_ptr(), gb.data_ptr(), rows,
+                                    static_cast<int>(C), acc, cur_stream(), nullptr, nullptr, nullptr, false,
+                                    gmap.data_ptr<int>(), g.stride(0)),
+               "layernorm_bwd_map");
+    return {gx, gw, gb};
+}
+
+// LayerNorm with one weight / bias row per group of rows: x [G * R, C] (group g = rows [g R, (g+1) R)),
+// w / b [G, C] -- the two-stage head's per-group encoder-output norms.  Returns {y, mean, rstd}.
+std::vector<torch::Tensor> layernorm_grouped_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps) {
+    TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "layernorm_grouped_fwd: x must be contiguous [rows, C]");
+    TORCH_CHECK(w.dim() == 2 && w.sizes() == b.sizes() && w.size(1) == x.size(1) && w.scalar_type() == b.scalar_type() &&
+                    x.size(0) % w.size(0) == 0,
+                "layernorm_grouped_fwd: weight / bias must be [G, C] with G dividing the rows");
+    at::cuda::CUDAGuard guard(x.device());
+    const int64_t rows = x.size(0);
+    auto y = torch::empty_like(x);
+    auto opts = x.options().dtype(torch::kFloat32);
+    auto mean = torch::empty({rows}, opts);
+    auto rstd = torch::empty({rows}, opts);
+    auto wc = w.contiguous(), bc = b.contiguous();
+    check_cuda(launch_layernorm_fwd(dtype_of(x), dtype_of(w), x.data_ptr(), wc.data_ptr(), bc.data_ptr(), y.data_ptr(),
+                                    mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, static_cast<int>(x.size(1)),
+                                    static_cast<float>(eps), cur_stream(), nullptr, nullptr, nullptr, nullptr, nullptr,
+                                    nullptr, nullptr, 0, rows / w.size(0)),
+               "layernorm_grouped_fwd");
+    return {y, mean, rstd};
+}
+
+// Backward of layernorm_grouped_fwd: {gx, gw [G, C], gb [G, C]} (added into gw_acc / gb_acc when given).
+std::vector<torch::Tensor> layernorm_grouped_bwd(torch::Tensor gy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
+                                                 torch::Tensor rstd, c10::optional<torch::Tensor> gw_acc,
+                                                 c10::optional<torch::Tensor> gb_acc) {
+    TORCH_CHECK(gy.sizes() == x.sizes() && gy.is_contiguous() && x.is_contiguous() && gy.scalar_type() == x.scalar_type(),
+                "layernorm_grouped_bwd: grad/x mismatch");
+    TORCH_CHECK(w.dim() == 2 && w.size(1) == x.size(1) && x.size(0) % w.size(0) == 0,
+                "layernorm_grouped_bwd: weight must be [G, C] with G dividing the rows");
+    at::cuda::CUDAGuard guard(x.device());
+    const int64_t rows = x.size(0);
+    auto gx = torch::empty_like(x);
+    auto wc = w.contiguous();
+    const bool acc = gw_acc && gw_acc->defined() && gb_acc && gb_acc->defined();
+    if (acc)
+        TORCH_CHECK(gw_acc->is_contiguous() && gb_acc->is_contiguous() && gw_acc->numel() == w.numel() &&
+                        gb_acc->numel() == w.numel() && gw_acc->scalar_type() == w.scalar_type() &&
+                        gb_acc->scalar_type() == w.scalar_type(),
+                    "layernorm_grouped_bwd: accumulation targets must be contiguous [G, C] of the weight dtype");
+    auto gw = acc ? *gw_acc : torch::empty_like(wc);
+    auto gb = acc ? *gb_acc : torch::empty_like(wc);
+    check_cuda(launch_layernorm_bwd(dtype_of(x), dtype_of(w), gy.data_ptr(), x.data_ptr(), wc.data_ptr(),
+                                    mean.data_ptr<float>(), rstd.data_ptr<float>(), gx.data_ptr(), gw.data_ptr(),
+                                    gb.data_ptr(), rows, static_cast<int>(x.size(1)), acc, cur_stream(), nullptr,
+                                    nullptr, nullptr, false, nullptr, 0, rows / w.size(0)),
+               "layernorm_grouped_bwd");
+    return {gx, gw, gb};
+}
+
 // ---------------------------------------------------------------- MSDeformAttn
 MsdaDims msda_dims(const torch::Tensor& value, const torch::Tensor& shapes, const torch::Tensor& starts,
                    const torch::Tensor& ref, const torch::Tensor& off, const torch::Tensor& logits) {
@@ -307,6 +416,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("layernorm_bwd", &mmltk::layernorm_bwd, py::arg("gy"), py::arg("x"), py::arg("w"), py::arg("mean"),
           py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none(), py::arg("gy2") = py::none(),
           py::arg("gres") = py::none(), py::arg("want_gbias2") = false, py::arg("gbias2_acc") = py::none());
+    m.def("layernorm_fwd_map", &mmltk::layernorm_fwd_map, py::arg("x"), py::arg("w"), py::arg("b"), py::arg("eps"),
+          py::arg("ymap"), py::arg("out"), py::arg("col"));
+    m.def("layernorm_bwd_map", &mmltk::layernorm_bwd_map, py::arg("g"), py::arg("col"), py::arg("gmap"), py::arg("x"),
+          py::arg("w"), py::arg("mean"), py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none());
+    m.def("layernorm_grouped_fwd", &mmltk::layernorm_grouped_fwd, py::arg("x"), py::arg("w"), py::arg("b"),
+          py::arg("eps"));
+    m.def("layernorm_grouped_bwd", &mmltk::layernorm_grouped_bwd, py::arg("gy"), py::arg("x"), py::arg("w"),
+          py::arg("mean"), py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none());
     m.def("msda_fwd", &mmltk::msda_fwd);
     m.def("msda_bwd", &mmltk::msda_bwd);
     m.def("matcher_cost", &mmltk::matcher_cost);

@@ -266,14 +266,10 @@ class WindowedDinov2(nn.Module):
         states[len(self.encoder.layer)] = x
         hp, wp = H // p, W // p
         hpw, wpw = hp // nw, wp // nw
-        feats = []
-        for s in self.taps:
-            h = ops.layer_norm(states[s], self.layernorm.weight, self.layernorm.bias, 1e-6)[:, 1:]
-            C = h.shape[-1]
-            if nw > 1:
-                h = h.reshape(B, nw, nw, hpw, wpw, C).permute(0, 1, 3, 2, 4, 5)
-            feats.append(h.reshape(B, hp, wp, C))
-        return feats
+        # final norm, cls drop and un-windowing of every tap in one mapped LayerNorm per tap, written
+        # side by side along the channels (the projector's concatenated input)
+        return ops.taps_layer_norm([states[s] for s in self.taps], self.layernorm.weight, self.layernorm.bias, 1e-6,
+                                   B, nw, hpw, wpw)
 
 
 class GradMark(torch.autograd.Function):

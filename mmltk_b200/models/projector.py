@@ -144,7 +144,7 @@ class MultiScaleProjector(nn.Module):
                 for m in samp:
                     h = m.forward_nhwc(h)
                 fused.append(h)
-            x = torch.cat(fused, -1) if len(fused) > 1 else fused[0]
+            x = ops.concat_channels(fused)     # no copy when the taps already sit side by side
             outs.append(stage.forward_nhwc(x))
         if self.extra_pool:
             outs.append(outs[-1][:, ::2, ::2, :])      # max-pool with kernel 1, stride 2

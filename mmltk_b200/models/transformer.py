@@ -324,9 +324,10 @@ class GroupedLayerNorm(nn.Module):
         self._register_load_state_dict_pre_hook(load_hook)
 
     def forward(self, x, groups):
-        # x [G, B, N, C]: normalise, then per-group affine
-        y = F.layer_norm(x, (x.shape[-1],), None, None, 1e-5)
-        return y * self.weight[:groups, None, None].to(y.dtype) + self.bias[:groups, None, None].to(y.dtype)
+        # x [G, B, N, C]: normalise with group g's affine (one kernel each way on the GPU)
+        if groups == self.groups:     # the parameters themselves (their gradients go straight to .grad)
+            return ops.grouped_layer_norm(x, self.weight, self.bias, 1e-5)
+        return ops.grouped_layer_norm(x, self.weight[:groups], self.bias[:groups], 1e-5)
 
 
 class GroupedMlp(nn.Module):
@@ -431,8 +432,10 @@ class Transformer(nn.Module):
             # enc_output + norm + box MLP on the k chosen rows gives the same values (and gradients)
             # as gathering them from the full pass, at k / S of the cost.
             S, C = out_mem.shape[1], out_mem.shape[2]
-            mem_in = out_mem.unsqueeze(0).expand(groups, B, S, C).gather(
-                2, topk[..., None].expand(-1, -1, -1, C))                              # [G, B, k, C]
+            # rows of the flattened [B*S, C] memory (its backward is one index_add into a [B*S, C]
+            # gradient, not a scatter into a group-expanded [G, B, S, C] buffer summed over groups)
+            rows = (torch.arange(B, device=topk.device, dtype=topk.dtype)[None, :, None] * S + topk).reshape(-1)
+            mem_in = out_mem.reshape(B * S, C).index_select(0, rows).view(groups, B, k, C)   # [G, B, k, C]
             mem_sel = self.enc_output_norm(self.enc_output(mem_in, groups), groups)    # [G, B, k, C]
             delta = self.enc_out_bbox_embed(mem_sel, groups)                            # [G, B, k, 4]
             props_sel = props.expand(B, -1, -1).unsqueeze(0).expand(groups, -1, -1, -1).gather(

@@ -6,6 +6,7 @@ from .attention import (attention, attention_reference, qkv_attention, qkv_atten
 from .conv import conv3x3, conv3x3_ok
 from .linear import linear, linear_pair, linear_scale_residual, mlp_relu, mlp_scale_residual
 from .msda import msda, msda_reference
-from .norm import add_layer_norm, layer_norm, layer_norm_with_residual, scaled_residual_layer_norm
+from .norm import (add_layer_norm, concat_channels, grouped_layer_norm, layer_norm, layer_norm_with_residual,
+                   scaled_residual_layer_norm, taps_layer_norm)
 from .posembed import sine_embed, sine_embed_reference
 from .losses import dense_focal_neg

@@ -15,7 +15,8 @@ import torch.nn.functional as F
 from ._ext import kernels
 from .gradacc import grad_target
 
-__all__ = ["scaled_residual_layer_norm", "layer_norm", "add_layer_norm", "layer_norm_with_residual"]
+__all__ = ["scaled_residual_layer_norm", "layer_norm", "add_layer_norm", "layer_norm_with_residual",
+           "taps_layer_norm", "concat_channels", "grouped_layer_norm"]
 
 
 class _LayerNormFn(torch.autograd.Function):
@@ -164,3 +165,149 @@ def layer_norm_with_residual(x: torch.Tensor, weight: torch.Tensor, bias: torch.
     if x.is_cuda and x.shape[-1] % 8 == 0 and x.dtype in (torch.bfloat16, torch.float32) and x.requires_grad:
         return _LayerNormResidualFn.apply(x, weight, bias, eps)
     return layer_norm(x, weight, bias, eps), x
+
+
+# ---------------------------------------------------------------------------------------------
+# Backbone taps: the final LayerNorm of every tapped stage, written straight into the projector's
+# input.  The stages are [windows, 1 + h*w tokens, C] in the windowed token order (a cls token per
+# window); the projector wants the image grid [B, hp, wp, taps * C], taps side by side along the
+# channels.  One mapped LayerNorm per tap writes each token row to its grid row (cls rows: nowhere)
+# at the tap's channel offset, so the slice / un-window permute / concatenation copies (and their
+# backward copies and zero fills) disappear; the backward reads each tap's gradient columns through
+# the same map.
+
+_TAP_MAPS = {}
+
+
+def _tap_row_map(device, B: int, nw: int, hpw: int, wpw: int) -> torch.Tensor:
+    """int32 [B * nw^2 * (1 + hpw*wpw)]: grid row (b, wy*hpw + iy, wx*wpw + ix) of each windowed token
+    row, -1 for the cls rows.  Built with device kernels (capture-safe) and cached per shape."""
+    key = (str(device), B, nw, hpw, wpw)
+    m = _TAP_MAPS.get(key)
+    if m is None:
+        L = 1 + hpw * wpw
+        r = torch.arange(B * nw * nw * L, device=device, dtype=torch.int64)
+        win, t = r // L, r % L
+        b, wy, wx = win // (nw * nw), (win % (nw * nw)) // nw, win % nw
+        tt = (t - 1).clamp(min=0)
+        iy, ix = tt // wpw, tt % wpw
+        hp, wp = nw * hpw, nw * wpw
+        grid = (b * hp + wy * hpw + iy) * wp + wx * wpw + ix
+        m = torch.where(t == 0, torch.full_like(grid, -1), grid).to(torch.int32)
+        _TAP_MAPS[key] = m
+    return m
+
+
+class _TapsNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, weight, bias, eps, ymap, grid, *states):
+        B, hp, wp = grid
+        T, C = len(states), states[0].shape[-1]
+        # allocated in its final shape (not returned as a view), so the channel slices handed out
+        # have it as their base and ``concat_channels`` can return it with its autograd history
+        out = torch.empty(B, hp, wp, T * C, device=states[0].device, dtype=states[0].dtype)
+        out2 = out.view(B * hp * wp, T * C)
+        xs, stats = [], []
+        for s, x in enumerate(states):
+            x2 = x.contiguous().view(-1, C)
+            mean, rstd = kernels().layernorm_fwd_map(x2, weight, bias, float(eps), ymap, out2, s * C)
+            xs.append(x2)
+            stats += [mean, rstd]
+        ctx.save_for_backward(weight, ymap, *xs, *stats)
+        ctx.T, ctx.C, ctx.shapes, ctx.params = T, C, [x.shape for x in states], (weight, bias)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        weight, ymap, *rest = ctx.saved_tensors
+        T, C = ctx.T, ctx.C
+        xs, stats = rest[:T], rest[T:]
+        g2 = g.contiguous().view(-1, T * C)
+        wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
+        gw = gb = None
+        gxs = []
+        k = kernels()
+        for s in range(T):
+            mean, rstd = stats[2 * s], stats[2 * s + 1]
+            if wt is not None and bt is not None:      # weight / bias gradients added straight into .grad
+                gx = k.layernorm_bwd_map(g2, s * C, ymap, xs[s], weight, mean, rstd, wt, bt)[0]
+            elif gw is None:
+                gx, gw, gb = k.layernorm_bwd_map(g2, s * C, ymap, xs[s], weight, mean, rstd)
+            else:                                       # the taps share the norm: accumulate
+                gx = k.layernorm_bwd_map(g2, s * C, ymap, xs[s], weight, mean, rstd, gw, gb)[0]
+            gxs.append(gx.view(ctx.shapes[s]))
+        return (None if wt is not None else gw, None if bt is not None else gb, None, None, None, *gxs)
+
+
+def taps_layer_norm(states, weight, bias, eps: float, B: int, nw: int, hpw: int, wpw: int):
+    """LayerNorm of every tapped stage [B * nw^2, 1 + hpw*wpw, C] (windowed token order) -> the
+    image-grid features [B, nw*hpw, nw*wpw, C] of each tap, as adjacent channel slices of one
+    [B, hp, wp, taps * C] tensor (``concat_channels`` of the list returns that tensor)."""
+    x0 = states[0]
+    C = x0.shape[-1]
+    if (x0.is_cuda and x0.dtype in (torch.bfloat16, torch.float32) and C % 8 == 0
+            and all(x.shape == x0.shape and x.dtype == x0.dtype for x in states)
+            and x0.shape[0] == B * nw * nw and x0.shape[1] == 1 + hpw * wpw and hasattr(kernels(), "layernorm_fwd_map")):
+        ymap = _tap_row_map(x0.device, B, nw, hpw, wpw)
+        cat = _TapsNormFn.apply(weight, bias, eps, ymap, (B, nw * hpw, nw * wpw), *states)
+        return [cat[..., s * C:(s + 1) * C] for s in range(len(states))]
+    feats = []
+    for x in states:
+        h = layer_norm(x, weight, bias, eps)[:, 1:]
+        if nw > 1:
+            h = h.reshape(B, nw, nw, hpw, wpw, C).permute(0, 1, 3, 2, 4, 5)
+        feats.append(h.reshape(B, nw * hpw, nw * wpw, C))
+    return feats
+
+
+def concat_channels(parts):
+    """torch.cat(parts, -1), except when the parts are, in order, the adjacent channel slices that
+    exactly cover one contiguous tensor (``taps_layer_norm``'s output): that tensor, with no copy."""
+    if len(parts) == 1:
+        return parts[0]
+    base = parts[0]._base
+    if base is not None and base.is_contiguous() and base.dim() == parts[0].dim():
+        off, width = base.storage_offset(), 0
+        ok = True
+        for p in parts:
+            if (p._base is not base or p.shape[:-1] != base.shape[:-1] or p.stride() != base.stride()
+                    or p.storage_offset() != off + width):
+                ok = False
+                break
+            width += p.shape[-1]
+        if ok and width == base.shape[-1]:
+            return base
+    return torch.cat(parts, -1)
+
+
+class _GroupedLayerNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        shape = x.shape
+        x2 = x.contiguous().view(-1, shape[-1])
+        y, mean, rstd = kernels().layernorm_grouped_fwd(x2, weight, bias, float(eps))
+        ctx.save_for_backward(x2, weight, mean, rstd)
+        ctx.shape, ctx.params = shape, (weight, bias)
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, weight, mean, rstd = ctx.saved_tensors
+        g2 = gy.contiguous().view(x2.shape)
+        wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
+        if wt is not None and bt is not None:
+            dx = kernels().layernorm_grouped_bwd(g2, x2, weight, mean, rstd, wt, bt)[0]
+            return dx.view(ctx.shape), None, None, None
+        dx, dw, db = kernels().layernorm_grouped_bwd(g2, x2, weight, mean, rstd)
+        return dx.view(ctx.shape), dw, db, None
+
+
+def grouped_layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float) -> torch.Tensor:
+    """x [G, ..., C] normalised over C with group g's affine weight[g], bias[g] (weight / bias [G, C])."""
+    G, C = weight.shape
+    if (x.is_cuda and x.dtype in (torch.bfloat16, torch.float32) and C % 8 == 0 and x.shape[0] == G
+            and weight.dtype == bias.dtype and hasattr(kernels(), "layernorm_grouped_fwd")):
+        return _GroupedLayerNormFn.apply(x, weight, bias, eps)
+    y = F.layer_norm(x, (C,), None, None, eps)
+    shape = (G,) + (1,) * (x.dim() - 2) + (C,)
+    return y * weight.view(shape).to(y.dtype) + bias.view(shape).to(y.dtype)

@@ -718,3 +718,56 @@ def _conv3x3_case(cuda_device, conv3x3, conv3x3_ok, B, H, W, C, N):
     assert _rel(yd.float().cpu(), yr) < 2e-2
     assert _rel(xd.grad.float().cpu(), xr.grad) < 2e-2
     assert _rel(wd.grad.float().cpu(), wr.grad) < 2e-2
+
+
+@pytest.mark.parametrize("B,nw,hpw,wpw,T", [(2, 2, 18, 18, 4), (3, 1, 5, 7, 2), (1, 2, 3, 4, 3)])
+def test_taps_layer_norm_matches_unfused(cuda_device, B, nw, hpw, wpw, T):
+    """The backbone taps' mapped LayerNorm (norm, cls drop, un-windowing and channel concatenation
+    in one kernel per tap) against LayerNorm + slice + permute + cat, forward and all gradients."""
+    from mmltk_b200.ops.norm import concat_channels, taps_layer_norm
+    g = torch.Generator().manual_seed(B * 100 + hpw)
+    C = 384
+    states = [torch.randn(B * nw * nw, 1 + hpw * wpw, C, generator=g) for _ in range(T)]
+    w, b = torch.randn(C, generator=g), torch.randn(C, generator=g)
+    gy = torch.randn(B, nw * hpw, nw * wpw, T * C, generator=g)
+    sr = [x.clone().requires_grad_() for x in states]
+    wr, br = w.clone().requires_grad_(), b.clone().requires_grad_()
+    feats = []
+    for x in sr:
+        h = torch.nn.functional.layer_norm(x, (C,), wr, br, 1e-6)[:, 1:]
+        h = h.reshape(B, nw, nw, hpw, wpw, C).permute(0, 1, 3, 2, 4, 5).reshape(B, nw * hpw, nw * wpw, C)
+        feats.append(h)
+    ref = torch.cat(feats, -1)
+    ref.backward(gy)
+    sd = [x.to(cuda_device, torch.bfloat16).requires_grad_() for x in states]
+    wd, bd = w.to(cuda_device).requires_grad_(), b.to(cuda_device).requires_grad_()
+    parts = taps_layer_norm(sd, wd, bd, 1e-6, B, nw, hpw, wpw)
+    out = concat_channels(parts)
+    assert out.data_ptr() == parts[0].data_ptr() and out.is_contiguous()    # no concatenation copy
+    out.backward(gy.to(cuda_device, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert _rel(out.float().cpu(), ref) < 2e-2
+    for a, r in zip(sd, sr):
+        assert _rel(a.grad.float().cpu(), r.grad) < 3e-2
+    assert _rel(wd.grad.float().cpu(), wr.grad) < 2e-2 and _rel(bd.grad.float().cpu(), br.grad) < 2e-2
+
+
+@pytest.mark.parametrize("G,R,C", [(13, 2400, 256), (3, 77, 128), (1, 5, 384)])
+def test_grouped_layer_norm_matches_fp32(cuda_device, G, R, C):
+    """LayerNorm with one affine row per group of rows (the per-group encoder-output norms) vs fp32."""
+    from mmltk_b200.ops.norm import grouped_layer_norm
+    g = torch.Generator().manual_seed(G * R)
+    x = torch.randn(G, R, C, generator=g)
+    w, b = torch.randn(G, C, generator=g), torch.randn(G, C, generator=g)
+    gy = torch.randn(G, R, C, generator=g)
+    xr, wr, br = (t.clone().requires_grad_() for t in (x, w, b))
+    ref = torch.nn.functional.layer_norm(xr, (C,), None, None, 1e-5) * wr[:, None] + br[:, None]
+    ref.backward(gy)
+    xd = x.to(cuda_device, torch.bfloat16).requires_grad_()
+    wd, bd = (t.to(cuda_device).requires_grad_() for t in (w, b))
+    y = grouped_layer_norm(xd, wd, bd, 1e-5)
+    y.backward(gy.to(cuda_device, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert _rel(y.float().cpu(), ref) < 2e-2
+    for a, r in ((xd, xr), (wd, wr), (bd, br)):
+        assert _rel(a.grad.float().cpu(), r.grad) < 2e-2
