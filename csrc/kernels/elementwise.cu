@@ -124,6 +124,18 @@ __global__ void __launch_bounds__(kColThreads, kColCtasPerSm) colreduce_kernel(c
                                                                    float* acc_buf, unsigned* counters,
                                                                    TO* __restrict__ out, int accumulate,
                                                                    TO* __restrict__ out2, int accumulate2) {
+    // groups (gridDim.z > 1): group g = blockIdx.z reduces its own M rows (x, pre and gout advanced by
+    // g * M rows) into its own accumulators, arrival counters and output row g (out / out2 [G, N])
+    if (gridDim.z > 1) {
+        const int64_t g = blockIdx.z;
+        x += g * M * N;
+        if (pre != nullptr) pre += g * M * N;
+        if (gout != nullptr) gout += g * M * N;
+        if (acc_buf != nullptr) acc_buf += g * (MODE == 3 ? 2 : 1) * static_cast<int64_t>(N);
+        counters += g * gridDim.y;
+        if (out != nullptr) out += g * N;
+        if (out2 != nullptr) out2 += g * N;
+    }
     __shared__ float red[kColThreads * 8];
     __shared__ unsigned s_last;
     const int tid = threadIdx.x, cl = tid & 31, rl = tid >> 5;
@@ -259,6 +271,25 @@ __global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, 
 }
 
 
+// out[rows[i]] += src[i] for every row i of src [n, C] (bf16; out zeroed by the caller): the backward of
+// a row gather whose rows may repeat.  One thread per 8 columns of a row, four packed bf16 pair
+// reductions into L2 (red.global.add.noftz.bf16x2).
+__global__ void index_add_rows_kernel(const __nv_bfloat16* __restrict__ src, const int64_t* __restrict__ rows,
+                                      __nv_bfloat16* __restrict__ out, int64_t n, int C) {
+    const int c8 = C / 8;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < n * c8;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t i = t / c8;
+        const int c = static_cast<int>(t % c8) * 8;
+        const uint4 v = *reinterpret_cast<const uint4*>(src + i * C + c);
+        __nv_bfloat16* dst = out + rows[i] * C + c;
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            asm volatile("red.global.add.noftz.bf16x2 [%0], %1;" ::"l"(dst + 2 * k), "r"(w[k]) : "memory");
+    }
+}
+
 // out (+)= acc, then acc = 0 (finishes a column sum accumulated by another kernel's atomics)
 template <typename TO>
 __global__ void colacc_finalize_kernel(float* acc, TO* out, int N, int accumulate) {
@@ -301,18 +332,22 @@ static int colsum_parts(int64_t M, int N, int mode) {
 
 static cudaError_t launch_colreduce(DType t, DType out_t, int mode, const void* x, const void* pre,
                                     const void* gamma, void* gout, int64_t M, int N, int act, void* out,
-                                    bool accumulate, cudaStream_t st, void* out2 = nullptr, bool accumulate2 = false) {
-    if (N % 8 != 0) return cudaErrorInvalidValue;
+                                    bool accumulate, cudaStream_t st, void* out2 = nullptr, bool accumulate2 = false,
+                                    int groups = 1) {
+    if (N % 8 != 0 || groups < 1 || groups > 65535) return cudaErrorInvalidValue;
     const int slabs = (N + kSlabCols - 1) / kSlabCols;
-    if (slabs > kMaxCounters || (out != nullptr && N > kReduceAccFloats)) return cudaErrorInvalidValue;
-    if (mode == 3 && (out2 == nullptr || out == nullptr || 2 * N > kReduceAccFloats)) return cudaErrorInvalidValue;
+    if (static_cast<int64_t>(slabs) * groups > kMaxCounters ||
+        (out != nullptr && static_cast<int64_t>(N) * groups > kReduceAccFloats))
+        return cudaErrorInvalidValue;
+    if (mode == 3 && (out2 == nullptr || out == nullptr || 2 * static_cast<int64_t>(N) * groups > kReduceAccFloats))
+        return cudaErrorInvalidValue;
     const ReduceScratch rs = reduce_scratch();
     if (rs.counters == nullptr) return cudaErrorMemoryAllocation;
     unsigned* counters = rs.counters;
     float* acc_buf = out != nullptr ? rs.acc : nullptr;   // null: no column sum wanted
-    const int parts = colsum_parts(M, N, mode);
+    const int parts = std::max(1, colsum_parts(M, N, mode) / groups);
     const int rows_per_cta = static_cast<int>((M + parts - 1) / parts);
-    const dim3 grid(parts, slabs);
+    const dim3 grid(parts, slabs, groups);
     return MMLTK_DISPATCH_DT(t, [&] {
         using T = scalar_t;
         return MMLTK_DISPATCH_DT(out_t, [&] {
@@ -342,9 +377,9 @@ static cudaError_t launch_colreduce(DType t, DType out_t, int mode, const void* 
 }
 
 cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const void* pre, const void* gamma,
-                          void* gout, int64_t M, int N, void* out, cudaStream_t st, bool accumulate) {
+                          void* gout, int64_t M, int N, void* out, cudaStream_t st, bool accumulate, int groups) {
     if (out == nullptr) return cudaErrorInvalidValue;
-    return launch_colreduce(t, out_t, mode, x, pre, gamma, gout, M, N, 0, out, accumulate, st);
+    return launch_colreduce(t, out_t, mode, x, pre, gamma, gout, M, N, 0, out, accumulate, st, nullptr, false, groups);
 }
 
 cudaError_t launch_scale_bias_bwd(DType t, DType out_t, const void* gy, const void* pre, const void* gamma, void* gpre,
@@ -366,6 +401,16 @@ cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bo
     });
 }
 
+
+cudaError_t launch_index_add_rows(const void* src, const int64_t* rows, void* out, int64_t n, int C, cudaStream_t st) {
+    if (C % 8 != 0) return cudaErrorInvalidValue;
+    if (n == 0) return cudaSuccess;
+    const int64_t work = n * (C / 8);
+    const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(num_sms()) * 16));
+    index_add_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), rows,
+                                                  static_cast<__nv_bfloat16*>(out), n, C);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_act_bwd(DType t, const void* gy, const void* pre, void* gx, int64_t n, int act, cudaStream_t st) {
     if (n % 8 != 0) return cudaErrorInvalidValue;

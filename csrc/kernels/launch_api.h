@@ -157,8 +157,10 @@ struct ReduceScratch {
     float* acc;
 };
 ReduceScratch reduce_scratch();
+// groups > 1: x is [groups, M, N] and out [groups, N] (one column sum per group).
 cudaError_t launch_colsum(DType t, DType out_t, int mode, const void* x, const void* pre, const void* gamma,
-                          void* gout, int64_t M, int N, void* out, cudaStream_t st, bool accumulate = false);
+                          void* gout, int64_t M, int N, void* out, cudaStream_t st, bool accumulate = false,
+                          int groups = 1);
 // LayerScale + bias backward in one pass: gpre = gy * gamma, ggamma (+)= colsum(gy * pre),
 // gbias (+)= colsum(gpre).  2 N <= kReduceAccFloats.
 cudaError_t launch_scale_bias_bwd(DType t, DType out_t, const void* gy, const void* pre, const void* gamma, void* gpre,
@@ -168,6 +170,8 @@ cudaError_t launch_scale_bias_bwd(DType t, DType out_t, const void* gy, const vo
 cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,
                                 int act, void* gb, bool accumulate, cudaStream_t st);
 // out (+)= acc; acc = 0 (acc: a column sum accumulated by atomics, e.g. in the GEMM epilogue)
+// out[rows[i], :] += src[i, :] (bf16 [n, C] -> [R, C], C % 8 == 0, out zeroed by the caller)
+cudaError_t launch_index_add_rows(const void* src, const int64_t* rows, void* out, int64_t n, int C, cudaStream_t st);
 cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bool accumulate, cudaStream_t st);
 // y = GELU(x), erf form; deriv (optional) = GELU'(x).  n % 8 == 0.
 cudaError_t launch_gelu_fwd(DType t, const void* x, void* y, int64_t n, cudaStream_t st, void* deriv = nullptr);

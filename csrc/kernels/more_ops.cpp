@@ -51,6 +51,36 @@ torch::Tensor reduce_target(const c10::optional<torch::Tensor>& acc, int64_t N, 
 }
 
 // sum over rows of a [M, N] tensor -> [N] in out_dtype, or added into `out`
+// [R, C] bf16 with row rows[i] += src[i] (rows may repeat): the backward of src = table.index_select(0, rows)
+torch::Tensor index_add_rows(torch::Tensor src, torch::Tensor rows, int64_t R) {
+    TORCH_CHECK(src.is_cuda() && src.dim() == 2 && src.is_contiguous() && src.scalar_type() == torch::kBFloat16,
+                "index_add_rows: src must be a contiguous bf16 [n, C] CUDA tensor");
+    TORCH_CHECK(rows.is_cuda() && rows.scalar_type() == torch::kInt64 && rows.is_contiguous() &&
+                    rows.numel() == src.size(0),
+                "index_add_rows: rows must be a contiguous int64 [n] CUDA tensor");
+    TORCH_CHECK(src.size(1) % 8 == 0, "index_add_rows: C % 8 == 0 required");
+    at::cuda::CUDAGuard guard(src.device());
+    auto out = torch::zeros({R, src.size(1)}, src.options());
+    check_cuda(launch_index_add_rows(src.data_ptr(), rows.data_ptr<int64_t>(), out.data_ptr(), src.size(0),
+                                     static_cast<int>(src.size(1)), cur_stream()),
+               "index_add_rows");
+    return out;
+}
+
+// x [G, M, N] -> [G, N] column sums per group (fp32 accumulation), one launch
+torch::Tensor colsum_grouped(torch::Tensor x, c10::optional<at::ScalarType> out_dtype) {
+    TORCH_CHECK(x.is_cuda() && x.dim() == 3 && x.is_contiguous(), "colsum_grouped: contiguous CUDA [G, M, N] expected");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && x.size(2) % 8 == 0,
+                "colsum_grouped: 16-byte aligned rows, N % 8 == 0");
+    at::cuda::CUDAGuard guard(x.device());
+    auto ot = out_dtype.has_value() ? *out_dtype : x.scalar_type();
+    auto o = torch::empty({x.size(0), x.size(2)}, x.options().dtype(ot));
+    check_cuda(launch_colsum(dtype_of(x), dtype_of(o), 0, x.data_ptr(), nullptr, nullptr, nullptr, x.size(1),
+                             static_cast<int>(x.size(2)), o.data_ptr(), cur_stream(), false, static_cast<int>(x.size(0))),
+               "colsum_grouped");
+    return o;
+}
+
 torch::Tensor colsum(torch::Tensor x, c10::optional<at::ScalarType> out_dtype, c10::optional<torch::Tensor> out) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 2, "colsum: CUDA [M,N] expected");
     at::cuda::CUDAGuard guard(x.device());
@@ -196,6 +226,8 @@ void register_more_ops(pybind11::module& m) {
     m.def("dense_focal_neg_fwd", &dense_focal_neg_fwd);
     m.def("dense_focal_neg_bwd", &dense_focal_neg_bwd);
     m.def("colsum", &colsum, py::arg("x"), py::arg("out_dtype") = py::none(), py::arg("out") = py::none());
+    m.def("index_add_rows", &index_add_rows, py::arg("src"), py::arg("rows"), py::arg("R"));
+    m.def("colsum_grouped", &colsum_grouped, py::arg("x"), py::arg("out_dtype") = py::none());
     m.def("scale_bwd", &scale_bwd, py::arg("gy"), py::arg("pre"), py::arg("gamma"),
           py::arg("gamma_grad") = py::none());
     m.def("scale_bias_bwd", &scale_bias_bwd, py::arg("gy"), py::arg("pre"), py::arg("gamma"),

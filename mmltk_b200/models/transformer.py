@@ -29,6 +29,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops
+from ..ops import kernels
 from ..config import RfDetrConfig
 
 
@@ -160,11 +161,9 @@ class DecoderLayer(nn.Module):
         x, x_pos = ops.add_layer_norm(tgt, sa, self.norm1.weight, self.norm1.bias, 1e-5, pos=query_pos, rbias=sa_b)
         ca, ca_b = self.cross_attn(x_pos, ref, memory, shapes, padding_mask, defer_bias=True)
         x = ops.add_layer_norm(x, ca, self.norm2.weight, self.norm2.bias, 1e-5, rbias=ca_b)
-        h = ops.mlp_relu(x, self.linear1.weight, self.linear1.bias, self.linear2.weight)
-        if want_pos:
-            return ops.add_layer_norm(x, h, self.norm3.weight, self.norm3.bias, 1e-5, pos=query_pos,
-                                      rbias=self.linear2.bias)
-        return ops.add_layer_norm(x, h, self.norm3.weight, self.norm3.bias, 1e-5, rbias=self.linear2.bias)
+        # FFN + residual + post-norm as one node (its backward needs no add of the two x gradients)
+        return ops.ffn_add_norm(x, self.linear1.weight, self.linear1.bias, self.linear2.weight, self.linear2.bias,
+                                self.norm3.weight, self.norm3.bias, 1e-5, pos=query_pos if want_pos else None)
 
 
 class Decoder(nn.Module):
@@ -267,7 +266,12 @@ class _GroupedLinearFn(torch.autograd.Function):
         gy = gy.contiguous()
         dx = bmm_nn_mn(gy, w) if ctx.needs_input_grad[0] else None
         dw = torch.bmm(gy.transpose(1, 2), x) if ctx.needs_input_grad[1] else None
-        db = gy.sum(1) if ctx.needs_input_grad[2] else None
+        db = None
+        if ctx.needs_input_grad[2]:
+            # per-group bias gradients in one column-reduction launch (fp32 accumulation)
+            k = kernels()
+            db = (k.colsum_grouped(gy) if gy.is_cuda and gy.shape[2] % 8 == 0 and hasattr(k, "colsum_grouped")
+                  else gy.sum(1))
         return dx, dw, db
 
 
@@ -435,7 +439,7 @@ class Transformer(nn.Module):
             # rows of the flattened [B*S, C] memory (its backward is one index_add into a [B*S, C]
             # gradient, not a scatter into a group-expanded [G, B, S, C] buffer summed over groups)
             rows = (torch.arange(B, device=topk.device, dtype=topk.dtype)[None, :, None] * S + topk).reshape(-1)
-            mem_in = out_mem.reshape(B * S, C).index_select(0, rows).view(groups, B, k, C)   # [G, B, k, C]
+            mem_in = ops.gather_rows(out_mem.reshape(B * S, C), rows).view(groups, B, k, C)   # [G, B, k, C]
             mem_sel = self.enc_output_norm(self.enc_output(mem_in, groups), groups)    # [G, B, k, C]
             delta = self.enc_out_bbox_embed(mem_sel, groups)                            # [G, B, k, 4]
             props_sel = props.expand(B, -1, -1).unsqueeze(0).expand(groups, -1, -1, -1).gather(

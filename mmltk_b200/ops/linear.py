@@ -25,7 +25,7 @@ from ._ext import kernels
 from .gemm import _fits_nt, gemm_nn, gemm_nt, gemm_nt_epilogue, gemm_tn, gemm_tn_acc, tc_gemm_enabled
 from .gradacc import grad_target
 
-__all__ = ["linear", "linear_pair", "linear_scale_residual", "mlp_scale_residual", "mlp_relu", "set_fused_linear"]
+__all__ = ["ffn_add_norm", "gather_rows", "linear", "linear_pair", "linear_scale_residual", "mlp_scale_residual", "mlp_relu", "set_fused_linear"]
 
 _ACTS = {None: 0, "none": 0, "gelu": 1, "relu": 2}
 _COLSUM_CAP = 16384   # widest output whose column sums the GEMM epilogue accumulates (its fp32 scratch)
@@ -307,3 +307,89 @@ def mlp_relu(x, w1, b1, w2):
     h = linear(x, w1, b1, act="relu")
     return linear(h, w2, None)
 
+
+
+class _GatherRows(torch.autograd.Function):
+    """table.index_select(0, rows) whose backward adds the rows' gradients back with packed bf16
+    reductions in one kernel (rows may repeat: the two-stage head's groups pick overlapping tokens)."""
+
+    @staticmethod
+    def forward(ctx, table, rows):
+        ctx.save_for_backward(rows)
+        ctx.R = table.shape[0]
+        return table.index_select(0, rows)
+
+    @staticmethod
+    def backward(ctx, g):
+        (rows,) = ctx.saved_tensors
+        return kernels().index_add_rows(g.contiguous(), rows, ctx.R), None
+
+
+def gather_rows(table: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
+    """table [R, C][rows] with a one-kernel backward on the GPU (bf16, C % 8 == 0)."""
+    if (table.is_cuda and table.dtype == torch.bfloat16 and table.shape[1] % 8 == 0 and rows.dtype == torch.int64
+            and hasattr(kernels(), "index_add_rows")):
+        return _GatherRows.apply(table, rows)
+    return table.index_select(0, rows)
+
+
+class _FfnAddNormFn(torch.autograd.Function):
+    """y = LN(x + ReLU(x W1^T + b1) W2^T + b2) [, y + pos]: the decoder's FFN sub-block and its
+    post-norm as one node.  The backward runs the norm first, then the FFN on the norm's input
+    gradient g, and forms the input gradient g + g_pre1 W1 in the last GEMM (beta = 1), so the two
+    gradients that reach x (residual and FFN) need no separate add."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2, nw, nb, pos, eps):
+        shp = x.shape
+        C = shp[-1]
+        x2 = _2d(x, C)
+        h, _ = gemm_nt_epilogue(x2, w1, b1, "relu", want_pre=False, force=True)
+        o = gemm_nt(h, w2)                                # b2 is added by the norm kernel
+        p2 = pos.contiguous().view(-1, C) if pos is not None else None
+        y, mean, rstd, s, y2 = kernels().layernorm_fwd(x2, nw, nb, float(eps), o, p2, b2.to(nw.dtype).contiguous())
+        ctx.save_for_backward(x2, w1, h, w2, s, nw, mean, rstd)
+        ctx.params = (w1, b1, w2, b2, nw, nb)
+        ctx.shp, ctx.has_pos = shp, pos is not None
+        if ctx.has_pos:
+            return y.view(shp), y2.view(shp)
+        return y.view(shp)
+
+    @staticmethod
+    def backward(ctx, gy, gy2=None):
+        x2, w1, h, w2, s, nw, mean, rstd = ctx.saved_tensors
+        k = kernels()
+        wt1, bt1, wt2, bt2, nwt, nbt = (grad_target(p) for p in ctx.params)
+        gy = gy.contiguous().view(s.shape) if gy is not None else torch.zeros_like(s)
+        g2 = gy2.contiguous().view(s.shape) if (ctx.has_pos and gy2 is not None) else None
+        acc_n = nwt is not None and nbt is not None
+        b2_ok = bt2 is not None and bt2.dtype == nw.dtype
+        g, dnw, dnb, db2 = k.layernorm_bwd(gy, s, nw, mean, rstd, nwt if acc_n else None, nbt if acc_n else None, g2,
+                                           None, True, bt2 if b2_ok else None)
+        # FFN backward on the norm's input gradient g
+        gw2 = gemm_tn(g, h) if wt2 is None else gemm_tn_acc(g, h, wt2)
+        gb1 = bt1 if bt1 is not None else torch.empty(w1.shape[0], device=g.device, dtype=w1.dtype)
+        g_pre1 = k.gemm_tc(g, w2, None, False, True, 5, False, h, None, gb1, bt1 is not None)[0]
+        gw1 = gemm_tn(g_pre1, x2) if wt1 is None else gemm_tn_acc(g_pre1, x2, wt1)
+        gx = torch.addmm(g, g_pre1, w1)                   # residual + FFN input gradients
+        none_if = lambda t, v: None if t is not None else v
+        db2_out = None if b2_ok else (db2.to(ctx.params[3].dtype) if db2 is not None else None)
+        gpos = g2.view(ctx.shp) if g2 is not None else None
+        return (gx.view(ctx.shp), none_if(wt1, gw1), none_if(bt1, gb1), none_if(wt2, gw2), db2_out,
+                None if acc_n else dnw, None if acc_n else dnb, gpos, None)
+
+
+def ffn_add_norm(x, w1, b1, w2, b2, nw, nb, eps: float, pos=None):
+    """LN(x + ReLU(x W1^T + b1) W2^T + b2) (and that + pos): the decoder's FFN block and post-norm,
+    one fused node on the GPU where the FFN takes the tensor-core path, else the separate ops."""
+    from .norm import add_layer_norm
+    C = x.shape[-1]
+    if (_state["fused_ffn"] and _ok(x, w1) and _ok(x, w2.new_empty(8, w2.shape[1])) and tc_gemm_enabled()
+            and w1.shape[0] % 128 == 0 and w1.shape[0] <= _COLSUM_CAP and torch.is_grad_enabled()
+            and C % 8 == 0 and (pos is None or (pos.dtype == x.dtype and pos.shape == x.shape))
+            and b2 is not None):
+        x2 = x.reshape(-1, C)
+        if _fits_nt(x2 if x2.is_contiguous() else x2.contiguous(), w1):
+            return _FfnAddNormFn.apply(x, w1, b1, w2, b2, nw, nb, pos, eps)
+    h = mlp_relu(x, w1, b1, w2)
+    return add_layer_norm(x, h, nw, nb, eps, pos=pos, rbias=b2)

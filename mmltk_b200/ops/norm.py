@@ -181,10 +181,12 @@ _TAP_MAPS = {}
 
 def _tap_row_map(device, B: int, nw: int, hpw: int, wpw: int) -> torch.Tensor:
     """int32 [B * nw^2 * (1 + hpw*wpw)]: grid row (b, wy*hpw + iy, wx*wpw + ix) of each windowed token
-    row, -1 for the cls rows.  Built with device kernels (capture-safe) and cached per shape."""
+    row, -1 for the cls rows.  Built with device kernels and cached per shape -- except while a CUDA
+    graph is being captured, when the kernels are only recorded (the map is then the graph's own)."""
     key = (str(device), B, nw, hpw, wpw)
     m = _TAP_MAPS.get(key)
     if m is None:
+        capturing = torch.cuda.is_current_stream_capturing()
         L = 1 + hpw * wpw
         r = torch.arange(B * nw * nw * L, device=device, dtype=torch.int64)
         win, t = r // L, r % L
@@ -194,7 +196,8 @@ def _tap_row_map(device, B: int, nw: int, hpw: int, wpw: int) -> torch.Tensor:
         hp, wp = nw * hpw, nw * wpw
         grid = (b * hp + wy * hpw + iy) * wp + wx * wpw + ix
         m = torch.where(t == 0, torch.full_like(grid, -1), grid).to(torch.int32)
-        _TAP_MAPS[key] = m
+        if not capturing:
+            _TAP_MAPS[key] = m
     return m
 
 

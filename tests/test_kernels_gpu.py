@@ -771,3 +771,69 @@ def test_grouped_layer_norm_matches_fp32(cuda_device, G, R, C):
     assert _rel(y.float().cpu(), ref) < 2e-2
     for a, r in ((xd, xr), (wd, wr), (bd, br)):
         assert _rel(a.grad.float().cpu(), r.grad) < 2e-2
+
+
+def test_gather_rows_backward_adds_repeated_rows(cuda_device):
+    """Row gather with repeated rows: the one-kernel backward (packed bf16 reductions) vs fp32."""
+    from mmltk_b200.ops.linear import gather_rows
+    g = torch.Generator().manual_seed(5)
+    R, C, n = 10368, 256, 31200
+    table = torch.randn(R, C, generator=g)
+    rows = torch.randint(0, R, (n,), generator=g)
+    gy = torch.randn(n, C, generator=g)
+    tr = table.clone().requires_grad_()
+    tr.index_select(0, rows).backward(gy)
+    td = table.to(cuda_device, torch.bfloat16).requires_grad_()
+    y = gather_rows(td, rows.to(cuda_device))
+    y.backward(gy.to(cuda_device, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert torch.equal(y.float().cpu(), table.to(torch.bfloat16).float()[rows])
+    assert _rel(td.grad.float().cpu(), tr.grad) < 2e-2
+
+
+@pytest.mark.parametrize("G,M,N", [(13, 2400, 256), (13, 2400, 96), (2, 7, 8)])
+def test_colsum_grouped(cuda_device, G, M, N):
+    """Per-group column sums in one launch vs fp32 sums."""
+    x = torch.randn(G, M, N, device=cuda_device).to(torch.bfloat16)
+    got = kernels().colsum_grouped(x, torch.float32)
+    ref = x.float().sum(1)
+    assert (got - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("with_pos", [False, True])
+def test_ffn_add_norm_matches_fp32(cuda_device, with_pos):
+    """The decoder's FFN + residual + post-norm node (input gradient accumulated by the last GEMM)
+    vs fp32 autograd, with and without the y + pos output."""
+    from mmltk_b200.ops.linear import ffn_add_norm
+    g = torch.Generator().manual_seed(7 + with_pos)
+    M, C, H = 3100, 256, 2048
+    bf = lambda t: t.to(torch.bfloat16).float()
+    x = bf(torch.randn(M, C, generator=g))
+    w1, b1 = bf(torch.randn(H, C, generator=g) * C ** -0.5), bf(torch.randn(H, generator=g) * 0.1)
+    w2, b2 = bf(torch.randn(C, H, generator=g) * H ** -0.5), bf(torch.randn(C, generator=g) * 0.1)
+    nw, nb = bf(torch.rand(C, generator=g) + 0.5), bf(torch.randn(C, generator=g) * 0.1)
+    pos = bf(torch.randn(M, C, generator=g))
+    gy, gy2 = bf(torch.randn(M, C, generator=g)), bf(torch.randn(M, C, generator=g))
+    ins = [t.clone().requires_grad_() for t in (x, w1, b1, w2, b2, nw, nb, pos)]
+    h = torch.relu(torch.nn.functional.linear(ins[0], ins[1], ins[2]))
+    yr = torch.nn.functional.layer_norm(ins[0] + torch.nn.functional.linear(h, ins[3], ins[4]), (C,), ins[5],
+                                        ins[6], 1e-5)
+    if with_pos:
+        torch.autograd.backward((yr, yr + ins[7]), (gy, gy2))
+    else:
+        yr.backward(gy)
+    d = [t.to(cuda_device, torch.bfloat16).requires_grad_() for t in (x, w1, b1, w2, b2, nw, nb, pos)]
+    out = ffn_add_norm(*d[:7], 1e-5, pos=d[7] if with_pos else None)
+    if with_pos:
+        torch.autograd.backward(out, (gy.to(cuda_device, torch.bfloat16), gy2.to(cuda_device, torch.bfloat16)))
+        y = out[0]
+    else:
+        out.backward(gy.to(cuda_device, torch.bfloat16))
+        y = out
+    torch.cuda.synchronize()
+    assert kernels().gemm_tc_status(0) == 0
+    assert _rel(y.float().cpu(), yr) < 2e-2
+    for a, r in zip(d[:7], ins[:7]):
+        assert _rel(a.grad.float().cpu(), r.grad) < 3e-2
+    if with_pos:
+        assert _rel(d[7].grad.float().cpu(), ins[7].grad) < 1e-2
