@@ -290,6 +290,37 @@ __global__ void index_add_rows_kernel(const __nv_bfloat16* __restrict__ src, con
     }
 }
 
+// Non-overlapping p x p patches of a planar image [B, Cin, H, W] as GEMM rows: out[(b, py, px), (c, ky, kx)]
+// (the patch-embedding convolution's im2col, with no copy of overlapping windows).  One thread per
+// 8-pixel run of a patch row: a 16-byte read of the image row and a 16-byte write of the output row.
+template <typename T>
+__global__ void patch_unfold_kernel(const T* __restrict__ img, T* __restrict__ out, int B, int Cin, int H, int W,
+                                    int p) {
+    const int hp = H / p, wp = W / p, runs = p / 8;
+    const int64_t total = static_cast<int64_t>(B) * hp * wp * Cin * p * runs;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t q = t;
+        const int run = static_cast<int>(q % runs);
+        q /= runs;
+        const int ky = static_cast<int>(q % p);
+        q /= p;
+        const int c = static_cast<int>(q % Cin);
+        q /= Cin;
+        const int64_t patch = q;                         // (b, py, px)
+        const int px = static_cast<int>(patch % wp), py = static_cast<int>((patch / wp) % hp);
+        const int b = static_cast<int>(patch / (static_cast<int64_t>(wp) * hp));
+        const T* src = img + ((static_cast<int64_t>(b) * Cin + c) * H + py * p + ky) * W + px * p + run * 8;
+        T* dst = out + patch * (static_cast<int64_t>(Cin) * p * p) + (c * p + ky) * p + run * 8;
+        if constexpr (sizeof(T) == 2) {
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        } else {
+            reinterpret_cast<float4*>(dst)[0] = reinterpret_cast<const float4*>(src)[0];
+            reinterpret_cast<float4*>(dst)[1] = reinterpret_cast<const float4*>(src)[1];
+        }
+    }
+}
+
 // out (+)= acc, then acc = 0 (finishes a column sum accumulated by another kernel's atomics)
 template <typename TO>
 __global__ void colacc_finalize_kernel(float* acc, TO* out, int N, int accumulate) {
@@ -401,6 +432,20 @@ cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bo
     });
 }
 
+
+cudaError_t launch_patch_unfold(DType t, const void* img, void* out, int B, int Cin, int H, int W, int p,
+                                cudaStream_t st) {
+    if (p % 8 != 0 || H % p != 0 || W % p != 0 || W % 8 != 0) return cudaErrorInvalidValue;
+    const int64_t total = static_cast<int64_t>(B) * (H / p) * (W / p) * Cin * p * (p / 8);
+    if (total == 0) return cudaSuccess;
+    const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(num_sms()) * 16));
+    return MMLTK_DISPATCH_DT(t, [&] {
+        using T = scalar_t;
+        patch_unfold_kernel<T><<<blocks, 256, 0, st>>>(static_cast<const T*>(img), static_cast<T*>(out), B, Cin, H, W,
+                                                        p);
+        return cudaGetLastError();
+    });
+}
 
 cudaError_t launch_index_add_rows(const void* src, const int64_t* rows, void* out, int64_t n, int C, cudaStream_t st) {
     if (C % 8 != 0) return cudaErrorInvalidValue;

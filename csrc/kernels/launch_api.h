@@ -170,6 +170,9 @@ cudaError_t launch_scale_bias_bwd(DType t, DType out_t, const void* gy, const vo
 cudaError_t launch_act_bwd_bias(DType t, DType out_t, const void* gy, const void* pre, void* gx, int64_t M, int N,
                                 int act, void* gb, bool accumulate, cudaStream_t st);
 // out (+)= acc; acc = 0 (acc: a column sum accumulated by atomics, e.g. in the GEMM epilogue)
+// planar image [B, Cin, H, W] -> patch rows [B * H/p * W/p, Cin * p * p] (p % 8 == 0, W % 8 == 0)
+cudaError_t launch_patch_unfold(DType t, const void* img, void* out, int B, int Cin, int H, int W, int p,
+                                cudaStream_t st);
 // out[rows[i], :] += src[i, :] (bf16 [n, C] -> [R, C], C % 8 == 0, out zeroed by the caller)
 cudaError_t launch_index_add_rows(const void* src, const int64_t* rows, void* out, int64_t n, int C, cudaStream_t st);
 cudaError_t launch_colacc_finalize(float* acc, DType out_t, void* out, int N, bool accumulate, cudaStream_t st);

@@ -67,6 +67,21 @@ torch::Tensor index_add_rows(torch::Tensor src, torch::Tensor rows, int64_t R) {
     return out;
 }
 
+// [B, Cin, H, W] -> [B * (H/p) * (W/p), Cin * p * p]: non-overlapping patches as GEMM rows
+torch::Tensor patch_unfold(torch::Tensor img, int64_t p) {
+    TORCH_CHECK(img.is_cuda() && img.dim() == 4 && img.is_contiguous(), "patch_unfold: contiguous CUDA [B, C, H, W]");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(img.data_ptr()) % 16 == 0, "patch_unfold: 16-byte aligned image");
+    const int64_t B = img.size(0), C = img.size(1), H = img.size(2), W = img.size(3);
+    TORCH_CHECK(p % 8 == 0 && H % p == 0 && W % p == 0, "patch_unfold: p % 8 == 0 and p dividing H, W");
+    at::cuda::CUDAGuard guard(img.device());
+    auto out = torch::empty({B * (H / p) * (W / p), C * p * p}, img.options());
+    check_cuda(launch_patch_unfold(dtype_of(img), img.data_ptr(), out.data_ptr(), static_cast<int>(B),
+                                   static_cast<int>(C), static_cast<int>(H), static_cast<int>(W), static_cast<int>(p),
+                                   cur_stream()),
+               "patch_unfold");
+    return out;
+}
+
 // x [G, M, N] -> [G, N] column sums per group (fp32 accumulation), one launch
 torch::Tensor colsum_grouped(torch::Tensor x, c10::optional<at::ScalarType> out_dtype) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 3 && x.is_contiguous(), "colsum_grouped: contiguous CUDA [G, M, N] expected");
@@ -228,6 +243,7 @@ void register_more_ops(pybind11::module& m) {
     m.def("colsum", &colsum, py::arg("x"), py::arg("out_dtype") = py::none(), py::arg("out") = py::none());
     m.def("index_add_rows", &index_add_rows, py::arg("src"), py::arg("rows"), py::arg("R"));
     m.def("colsum_grouped", &colsum_grouped, py::arg("x"), py::arg("out_dtype") = py::none());
+    m.def("patch_unfold", &patch_unfold, py::arg("img"), py::arg("p"));
     m.def("scale_bwd", &scale_bwd, py::arg("gy"), py::arg("pre"), py::arg("gamma"),
           py::arg("gamma_grad") = py::none());
     m.def("scale_bias_bwd", &scale_bias_bwd, py::arg("gy"), py::arg("pre"), py::arg("gamma"),

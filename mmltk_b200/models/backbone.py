@@ -51,8 +51,13 @@ class PatchEmbeddings(nn.Module):
         B, C, H, W = x.shape
         p = self.patch
         if x.is_cuda:
-            cols = x.view(B, C, H // p, p, W // p, p).permute(0, 2, 4, 1, 3, 5).reshape(B * (H // p) * (W // p),
-                                                                                        C * p * p)
+            k = ops.kernels()
+            if (p % 8 == 0 and W % 8 == 0 and not x.requires_grad and x.dtype in (torch.bfloat16, torch.float32)
+                    and hasattr(k, "patch_unfold")):
+                cols = k.patch_unfold(x.contiguous(), p)     # one pass, 16-byte runs (the pixels need no gradient)
+            else:
+                cols = x.view(B, C, H // p, p, W // p, p).permute(0, 2, 4, 1, 3, 5).reshape(
+                    B * (H // p) * (W // p), C * p * p)
             w = self.projection.weight.reshape(self.projection.weight.shape[0], -1)
             return ops.linear(cols.to(w.dtype), w, self.projection.bias).view(B, (H // p) * (W // p), -1)
         return self.projection(x.to(self.projection.weight.dtype)).flatten(2).transpose(1, 2)

@@ -280,8 +280,8 @@ def grouped_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, act=None) 
     w = w.to(x.dtype)
     b = b.to(x.dtype)
     dout = w.shape[1]
-    pad = (-dout) % 8 if (x.is_cuda and dout > 8) else 0
-    if pad:   # odd widths (91 classes) would put cuBLAS on its unaligned kernels
+    pad = (-dout) % 8 if x.is_cuda else 0
+    if pad:   # odd widths (91 classes, 4 box deltas) would put cuBLAS on its unaligned kernels
         w = F.pad(w, (0, 0, 0, pad))
         b = F.pad(b, (0, pad))
     G = w.shape[0]
@@ -421,7 +421,8 @@ class Transformer(nn.Module):
         cfg = self.cfg
         B = feats[0].shape[0]
         shapes = [(f.shape[1], f.shape[2]) for f in feats]
-        memory = torch.cat([f.reshape(B, -1, f.shape[-1]) for f in feats], 1)  # [B, S, C]
+        flat = [f.reshape(B, -1, f.shape[-1]) for f in feats]
+        memory = flat[0] if len(flat) == 1 else torch.cat(flat, 1)                 # [B, S, C]
         groups = max(1, cfg.group_detr) if training else 1
         out = {"shapes": shapes}
         refpoints = refpoint_embed.unsqueeze(0).expand(B, -1, -1)

@@ -148,10 +148,11 @@ def linear(x: torch.Tensor, w: torch.Tensor, b=None, act=None) -> torch.Tensor:
     if _ok(x, w):
         return _Linear.apply(x, w, b, _ACTS[act])
     n = w.shape[0]
-    if n % 8 and n > 8 and _ok(x, w.new_empty(8, w.shape[1])):
-        # Output widths that are not a multiple of 8 (the 91-class heads) make cuBLAS fall back to
-        # its 1-byte-aligned kernels, ~10x slower for the [B*Q, 91] logits and their weight gradient.
-        # Padding the weight rows to a multiple of 8 keeps every product on the aligned path.
+    if n % 8 and _ok(x, w.new_empty(8, w.shape[1])):
+        # Output widths that are not a multiple of 8 (the 91-class heads, the 4-wide box heads) make
+        # cuBLAS fall back to its 2-byte-aligned kernels, several times slower for the [B*Q, 91]
+        # logits, the [4 * B*Q, 4] box deltas and their weight gradients.  Padding the weight rows to
+        # a multiple of 8 keeps every product on the aligned path.
         pad = (-n) % 8
         wp = F.pad(w, (0, 0, 0, pad))
         bp = None if b is None else F.pad(b, (0, pad))
@@ -366,10 +367,11 @@ class _FfnAddNormFn(torch.autograd.Function):
         b2_ok = bt2 is not None and bt2.dtype == nw.dtype
         g, dnw, dnb, db2 = k.layernorm_bwd(gy, s, nw, mean, rstd, nwt if acc_n else None, nbt if acc_n else None, g2,
                                            None, True, bt2 if b2_ok else None)
-        # FFN backward on the norm's input gradient g
+        # FFN backward on the norm's input gradient g: the second layer's input gradient on the
+        # library GEMM, then one pass for the ReLU mask and the first bias's gradient (measured
+        # faster than the tcgen05 GEMM with both in its epilogue: that product is load-bound)
         gw2 = gemm_tn(g, h) if wt2 is None else gemm_tn_acc(g, h, wt2)
-        gb1 = bt1 if bt1 is not None else torch.empty(w1.shape[0], device=g.device, dtype=w1.dtype)
-        g_pre1 = k.gemm_tc(g, w2, None, False, True, 5, False, h, None, gb1, bt1 is not None)[0]
+        g_pre1, gb1 = k.act_bwd_bias(gemm_nn(g, w2), h, 2, bt1)
         gw1 = gemm_tn(g_pre1, x2) if wt1 is None else gemm_tn_acc(g_pre1, x2, wt1)
         gx = torch.addmm(g, g_pre1, w1)                   # residual + FFN input gradients
         none_if = lambda t, v: None if t is not None else v

@@ -837,3 +837,11 @@ def test_ffn_add_norm_matches_fp32(cuda_device, with_pos):
         assert _rel(a.grad.float().cpu(), r.grad) < 3e-2
     if with_pos:
         assert _rel(d[7].grad.float().cpu(), ins[7].grad) < 1e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("B,C,H,W,p", [(2, 3, 576, 576, 16), (1, 3, 560, 560, 8), (3, 2, 32, 48, 16)])
+def test_patch_unfold_matches_permute(cuda_device, dtype, B, C, H, W, p):
+    x = torch.randn(B, C, H, W, device=cuda_device).to(dtype)
+    ref = x.view(B, C, H // p, p, W // p, p).permute(0, 2, 4, 1, 3, 5).reshape(B * (H // p) * (W // p), C * p * p)
+    assert torch.equal(kernels().patch_unfold(x, p), ref)
