@@ -21,7 +21,8 @@ cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* 
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st,
                                  const void* res = nullptr, void* sum = nullptr, const void* pos = nullptr,
                                  void* y2 = nullptr, const void* rbias = nullptr, const void* rscale = nullptr,
-                                 const int* ymap = nullptr, int64_t yld = 0, int64_t wgroup_rows = 0);
+                                 const int* ymap = nullptr, int64_t yld = 0, int64_t wgroup_rows = 0, int act = 0);
+// act = 1: y = SiLU(normalised, affine row) (the backward recomputes the pre-activation from x).
 // wgroup_rows > 0: the rows come in groups of that many and group g uses row g of w / b ([groups, C]).
 // ymap (optional, int32 [rows]): y row of input row r is ymap[r] (none when negative), row pitch yld --
 // a normalised row goes straight to its place in a differently laid out (e.g. un-windowed,
@@ -35,7 +36,9 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
                                  bool accumulate, cudaStream_t st, const void* gy2 = nullptr,
                                  const void* gres = nullptr, void* gbias2 = nullptr, bool accumulate2 = false,
-                                 const int* gmap = nullptr, int64_t gld = 0, int64_t group_rows = 0);
+                                 const int* gmap = nullptr, int64_t gld = 0, int64_t group_rows = 0,
+                                 const void* bvec = nullptr, int act = 0);
+// act = 1: backward of a forward with SiLU; bvec = the norm's bias (to recompute the pre-activation).
 // group_rows > 0: per-group weights as in the forward; gw / gb are [groups, C].
 // gmap (optional, int32 [rows]): the gradient of input row r is gy row gmap[r] (zero when negative),
 // row pitch gld -- the backward of a forward with ymap.

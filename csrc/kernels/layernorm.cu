@@ -29,7 +29,15 @@ struct LnFwdExtra {
     const int* ymap;   // y row of input row r (negative: not stored); null: row r
     int64_t yld;       // y row pitch with ymap
     int64_t wgroup_rows;   // > 0: rows come in groups of this many, group g normalised with w / b row g
+    int act;               // 1: y = SiLU(normalised row), the channels-last ConvX's norm + activation
 };
+
+__device__ __forceinline__ float silu_f(float o) { return o / (1.f + __expf(-o)); }
+// d SiLU / d o = s (1 + o (1 - s)), s = sigmoid(o)
+__device__ __forceinline__ float silu_grad_f(float o) {
+    const float s = 1.f / (1.f + __expf(-o));
+    return s * (1.f + o * (1.f - s));
+}
 
 template <typename T, typename W, int kMaxVec>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, const W* __restrict__ w,
@@ -99,6 +107,7 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const T* __restrict__ x, co
                 o.y = (v[k].y - mean) * rstd * to_f(wr[c0 + 1]) + to_f(br[c0 + 1]);
                 o.z = (v[k].z - mean) * rstd * to_f(wr[c0 + 2]) + to_f(br[c0 + 2]);
                 o.w = (v[k].w - mean) * rstd * to_f(wr[c0 + 3]) + to_f(br[c0 + 3]);
+                if (ex.act == 1) o = make_float4(silu_f(o.x), silu_f(o.y), silu_f(o.z), silu_f(o.w));
                 store4(yr + c0, o);
                 if (ex.pos != nullptr) {   // second output y + pos (e.g. a query with its position embedding)
                     const float4 p4 = load4(ex.pos + r * C + c0);
@@ -139,7 +148,8 @@ template <typename T, typename W, int kMaxVec, bool kBias2>
 __device__ __forceinline__ void ln_bwd_row(float4 (&xh)[kMaxVec], float4 (&g)[kMaxVec], float mean, float rstd,
                                            const W* __restrict__ w, float4 (&aw)[kMaxVec], float4 (&ab)[kMaxVec],
                                            float4 (&ad)[kMaxVec], T* __restrict__ gxr, int lane,
-                                           int nv, int C, const T* __restrict__ gresr) {
+                                           int nv, int C, const T* __restrict__ gresr, const W* __restrict__ bvec,
+                                           int act) {
     // the residual gradient is loaded first so its latency hides behind the reductions below
     Raw4<T> gr[kMaxVec];
     if (gresr != nullptr) {
@@ -153,9 +163,16 @@ __device__ __forceinline__ void ln_bwd_row(float4 (&xh)[kMaxVec], float4 (&g)[kM
         const int i = lane + 32 * k;
         if (i < nv) {
             const int c0 = 4 * i;
-            const float4 xv = xh[k], gv = g[k];
+            const float4 xv = xh[k];
+            float4 gv = g[k];
             xh[k] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd,
                                 (xv.w - mean) * rstd);
+            if (act == 1) {   // the forward applied SiLU to the affine output: recompute it, chain its slope
+                gv.x *= silu_grad_f(xh[k].x * to_f(w[c0]) + to_f(bvec[c0]));
+                gv.y *= silu_grad_f(xh[k].y * to_f(w[c0 + 1]) + to_f(bvec[c0 + 1]));
+                gv.z *= silu_grad_f(xh[k].z * to_f(w[c0 + 2]) + to_f(bvec[c0 + 2]));
+                gv.w *= silu_grad_f(xh[k].w * to_f(w[c0 + 3]) + to_f(bvec[c0 + 3]));
+            }
             aw[k].x += gv.x * xh[k].x; aw[k].y += gv.y * xh[k].y;
             aw[k].z += gv.z * xh[k].z; aw[k].w += gv.w * xh[k].w;
             ab[k].x += gv.x; ab[k].y += gv.y; ab[k].z += gv.z; ab[k].w += gv.w;
@@ -197,7 +214,7 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                                                      int64_t rows, int C, const T* __restrict__ gy2,
                                                      const T* __restrict__ gres, W* __restrict__ gbias2,
                                                      int accumulate2, const int* __restrict__ gmap, int64_t gld,
-                                                     int64_t group_rows) {
+                                                     int64_t group_rows, const W* __restrict__ bvec, int act) {
     extern __shared__ float smem[];  // [warps][2][C]
     // groups (group_rows > 0): blockIdx.y = group g, rows [g * group_rows, +group_rows), weight / bias
     // row g, gradient accumulators, arrival counter and gw / gb row of that group
@@ -207,6 +224,7 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
         row_begin = g * group_rows;
         rows = min(rows, row_begin + group_rows);
         w += static_cast<int64_t>(g) * C;
+        if (bvec != nullptr) bvec += static_cast<int64_t>(g) * C;
         gw += static_cast<int64_t>(g) * C;
         gb += static_cast<int64_t>(g) * C;
         acc_w += static_cast<int64_t>(g) * (kBias2 ? 3 : 2) * C;
@@ -280,7 +298,7 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
                 }
             }
             ln_bwd_row<T, W, kMaxVec, kBias2>(xv, gv, mean, rstd, w, aw, ab, ad, gx + r * C, lane, nv, C,
-                                      gres != nullptr ? gres + r * C : nullptr);
+                                      gres != nullptr ? gres + r * C : nullptr, bvec, act);
         }
     } else {
         // wide rows have no registers to spare for a second row
@@ -301,7 +319,7 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const T* __restrict__ gy, c
             }
             ln_bwd_row<T, W, kMaxVec, kBias2>(xv, gv, mean_in[r], rstd_in[r], w, aw, ab, ad, gx + r * C, lane, nv,
                                               C,
-                                      gres != nullptr ? gres + r * C : nullptr);
+                                      gres != nullptr ? gres + r * C : nullptr, bvec, act);
         }
     }
     // CTA reduction of the per-lane column partials ([warps][nacc][C]: gamma, beta[, input])
@@ -380,7 +398,7 @@ void dispatch_vec(int C, F&& f) {
 cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* w, const void* b, void* y, float* mean,
                                  float* rstd, int64_t rows, int C, float eps, cudaStream_t st, const void* res,
                                  void* sum, const void* pos, void* y2, const void* rbias, const void* rscale,
-                                 const int* ymap, int64_t yld, int64_t wgroup_rows) {
+                                 const int* ymap, int64_t yld, int64_t wgroup_rows, int act) {
     if ((rbias != nullptr || rscale != nullptr) && res == nullptr) return cudaErrorInvalidValue;
     if ((res == nullptr) != (sum == nullptr) || (pos == nullptr) != (y2 == nullptr)) return cudaErrorInvalidValue;
     if (ymap != nullptr && (pos != nullptr || yld < C || yld % 4 != 0)) return cudaErrorInvalidValue;
@@ -398,7 +416,7 @@ cudaError_t launch_layernorm_fwd(DType xt, DType wt, const void* x, const void* 
                     static_cast<T*>(y), mean, rstd, rows, C, eps,
                     LnFwdExtra<T, Wt>{static_cast<const T*>(res), static_cast<T*>(sum), static_cast<const T*>(pos),
                                       static_cast<T*>(y2), static_cast<const Wt*>(rbias),
-                                      static_cast<const Wt*>(rscale), ymap, yld, wgroup_rows});
+                                      static_cast<const Wt*>(rscale), ymap, yld, wgroup_rows, act});
             });
             return cudaGetLastError();
         });
@@ -421,7 +439,9 @@ int ln_bwd_blocks(K kern, int threads, size_t smem, int64_t rows) {
 cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void* x, const void* w, const float* mean,
                                  const float* rstd, void* gx, void* gw, void* gb, int64_t rows, int C,
                                  bool accumulate, cudaStream_t st, const void* gy2, const void* gres, void* gbias2,
-                                 bool accumulate2, const int* gmap, int64_t gld, int64_t group_rows) {
+                                 bool accumulate2, const int* gmap, int64_t gld, int64_t group_rows, const void* bvec,
+                                 int act) {
+    if (act != 0 && bvec == nullptr) return cudaErrorInvalidValue;
     if (gmap != nullptr && (gy2 != nullptr || gld < C || gld % 4 != 0)) return cudaErrorInvalidValue;
     const int64_t groups = group_rows > 0 ? (rows + group_rows - 1) / group_rows : 1;
     if (group_rows > 0 && (rows % group_rows != 0 || groups > kMaxCounters || groups > 65535 ||
@@ -453,7 +473,7 @@ cudaError_t launch_layernorm_bwd(DType xt, DType wt, const void* gy, const void*
                                                     static_cast<Wt*>(gb), accumulate ? 1 : 0, rows, C,
                                                     static_cast<const T*>(gy2), static_cast<const T*>(gres),
                                                     static_cast<Wt*>(gbias2), accumulate2 ? 1 : 0, gmap, gld,
-                                                    group_rows);
+                                                    group_rows, static_cast<const Wt*>(bvec), act);
             };
             dispatch_vec(C, [&](auto nvl) {
                 if (gbias2 != nullptr) run(nvl, std::true_type{});

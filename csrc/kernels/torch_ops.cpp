@@ -246,6 +246,55 @@ std::vector<torch::Tensor> layernorm_grouped_bwd(torch::Tensor gy, torch::Tensor
     return {gx, gw, gb};
 }
 
+// y = SiLU(LN(x)) (act 1): the projector's ConvX norm + activation in one pass.  Returns {y, mean, rstd}.
+std::vector<torch::Tensor> layernorm_act_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps,
+                                             int64_t act) {
+    TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "layernorm_act_fwd: x must be contiguous [rows, C]");
+    TORCH_CHECK(w.scalar_type() == b.scalar_type() && w.numel() == x.size(1) && b.numel() == x.size(1),
+                "layernorm_act_fwd: weight/bias must match C and share a dtype");
+    TORCH_CHECK(act == 1, "layernorm_act_fwd: act 1 (SiLU) only");
+    at::cuda::CUDAGuard guard(x.device());
+    const int64_t rows = x.size(0);
+    auto y = torch::empty_like(x);
+    auto opts = x.options().dtype(torch::kFloat32);
+    auto mean = torch::empty({rows}, opts);
+    auto rstd = torch::empty({rows}, opts);
+    auto wc = w.contiguous(), bc = b.contiguous();
+    check_cuda(launch_layernorm_fwd(dtype_of(x), dtype_of(w), x.data_ptr(), wc.data_ptr(), bc.data_ptr(), y.data_ptr(),
+                                    mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, static_cast<int>(x.size(1)),
+                                    static_cast<float>(eps), cur_stream(), nullptr, nullptr, nullptr, nullptr, nullptr,
+                                    nullptr, nullptr, 0, 0, static_cast<int>(act)),
+               "layernorm_act_fwd");
+    return {y, mean, rstd};
+}
+
+// Backward of layernorm_act_fwd: {gx, gw, gb} (added into gw_acc / gb_acc when given).
+std::vector<torch::Tensor> layernorm_act_bwd(torch::Tensor gy, torch::Tensor x, torch::Tensor w, torch::Tensor b,
+                                             torch::Tensor mean, torch::Tensor rstd, int64_t act,
+                                             c10::optional<torch::Tensor> gw_acc, c10::optional<torch::Tensor> gb_acc) {
+    TORCH_CHECK(gy.sizes() == x.sizes() && gy.is_contiguous() && x.is_contiguous() && gy.scalar_type() == x.scalar_type(),
+                "layernorm_act_bwd: grad/x mismatch");
+    TORCH_CHECK(act == 1 && b.numel() == x.size(1) && b.scalar_type() == w.scalar_type(), "layernorm_act_bwd: bad args");
+    at::cuda::CUDAGuard guard(x.device());
+    const int64_t rows = x.size(0);
+    const int C = static_cast<int>(x.size(1));
+    auto gx = torch::empty_like(x);
+    auto wc = w.contiguous(), bc = b.contiguous();
+    const bool acc = gw_acc && gw_acc->defined() && gb_acc && gb_acc->defined();
+    if (acc)
+        TORCH_CHECK(gw_acc->is_contiguous() && gb_acc->is_contiguous() && gw_acc->numel() == C && gb_acc->numel() == C &&
+                        gw_acc->scalar_type() == w.scalar_type() && gb_acc->scalar_type() == w.scalar_type(),
+                    "layernorm_act_bwd: accumulation targets must be contiguous [C] of the weight dtype");
+    auto gw = acc ? *gw_acc : torch::empty_like(wc);
+    auto gb = acc ? *gb_acc : torch::empty_like(wc);
+    check_cuda(launch_layernorm_bwd(dtype_of(x), dtype_of(w), gy.data_ptr(), x.data_ptr(), wc.data_ptr(),
+                                    mean.data_ptr<float>(), rstd.data_ptr<float>(), gx.data_ptr(), gw.data_ptr(),
+                                    gb.data_ptr(), rows, C, acc, cur_stream(), nullptr, nullptr, nullptr, false, nullptr,
+                                    0, 0, bc.data_ptr(), static_cast<int>(act)),
+               "layernorm_act_bwd");
+    return {gx, gw, gb};
+}
+
 // ---------------------------------------------------------------- MSDeformAttn
 MsdaDims msda_dims(const torch::Tensor& value, const torch::Tensor& shapes, const torch::Tensor& starts,
                    const torch::Tensor& ref, const torch::Tensor& off, const torch::Tensor& logits) {
@@ -424,6 +473,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("eps"));
     m.def("layernorm_grouped_bwd", &mmltk::layernorm_grouped_bwd, py::arg("gy"), py::arg("x"), py::arg("w"),
           py::arg("mean"), py::arg("rstd"), py::arg("gw_acc") = py::none(), py::arg("gb_acc") = py::none());
+    m.def("layernorm_act_fwd", &mmltk::layernorm_act_fwd, py::arg("x"), py::arg("w"), py::arg("b"), py::arg("eps"),
+          py::arg("act"));
+    m.def("layernorm_act_bwd", &mmltk::layernorm_act_bwd, py::arg("gy"), py::arg("x"), py::arg("w"), py::arg("b"),
+          py::arg("mean"), py::arg("rstd"), py::arg("act"), py::arg("gw_acc") = py::none(),
+          py::arg("gb_acc") = py::none());
     m.def("msda_fwd", &mmltk::msda_fwd);
     m.def("msda_bwd", &mmltk::msda_bwd);
     m.def("matcher_cost", &mmltk::matcher_cost);

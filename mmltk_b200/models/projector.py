@@ -36,8 +36,8 @@ class LayerNorm2d(nn.Module):
         self.bias = nn.Parameter(torch.zeros(channels))
         self.eps = eps
 
-    def forward_nhwc(self, x: torch.Tensor) -> torch.Tensor:
-        return ops.layer_norm(x, self.weight, self.bias, self.eps)
+    def forward_nhwc(self, x: torch.Tensor, act: str = None) -> torch.Tensor:
+        return ops.layer_norm(x, self.weight, self.bias, self.eps, act=act)
 
 
 class ConvX(nn.Module):
@@ -56,8 +56,7 @@ class ConvX(nn.Module):
         else:
             xc = x.permute(0, 3, 1, 2)
             y = F.conv2d(xc, self.conv.weight.to(xc.dtype), None, self.s, self.k // 2).permute(0, 2, 3, 1)
-        y = self.bn.forward_nhwc(y)
-        return F.silu(y)
+        return self.bn.forward_nhwc(y, act="silu")      # norm + SiLU in one kernel on the GPU
 
 
 class Bottleneck(nn.Module):

@@ -42,10 +42,39 @@ class _LayerNormFn(torch.autograd.Function):
         return dx.view(ctx.shape), dw, db, None
 
 
-def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float) -> torch.Tensor:
+class _LayerNormSiluFn(torch.autograd.Function):
+    """SiLU(LN(x)) in one kernel each way; the backward recomputes the pre-activation from x."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        shape = x.shape
+        x2 = x.contiguous().view(-1, shape[-1])
+        y, mean, rstd = kernels().layernorm_act_fwd(x2, weight, bias, float(eps), 1)
+        ctx.save_for_backward(x2, weight, bias, mean, rstd)
+        ctx.shape, ctx.params = shape, (weight, bias)
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, weight, bias, mean, rstd = ctx.saved_tensors
+        g2 = gy.contiguous().view(x2.shape)
+        wt, bt = grad_target(ctx.params[0]), grad_target(ctx.params[1])
+        if wt is not None and bt is not None:
+            dx = kernels().layernorm_act_bwd(g2, x2, weight, bias, mean, rstd, 1, wt, bt)[0]
+            return dx.view(ctx.shape), None, None, None
+        dx, dw, db = kernels().layernorm_act_bwd(g2, x2, weight, bias, mean, rstd, 1)
+        return dx.view(ctx.shape), dw, db, None
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float, act: str = None) -> torch.Tensor:
+    """LayerNorm over the last dimension; ``act="silu"`` also applies SiLU (in the same kernel on the GPU)."""
     if x.is_cuda and x.shape[-1] % 8 == 0 and x.dtype in (torch.bfloat16, torch.float32):
-        return _LayerNormFn.apply(x, weight, bias, eps)
-    return F.layer_norm(x, (x.shape[-1],), weight.to(x.dtype), bias.to(x.dtype), eps)
+        if act is None:
+            return _LayerNormFn.apply(x, weight, bias, eps)
+        if act == "silu" and hasattr(kernels(), "layernorm_act_fwd") and weight.dtype == bias.dtype:
+            return _LayerNormSiluFn.apply(x, weight, bias, eps)
+    y = F.layer_norm(x, (x.shape[-1],), weight.to(x.dtype), bias.to(x.dtype), eps)
+    return F.silu(y) if act == "silu" else y
 
 
 class _AddLayerNormFn(torch.autograd.Function):

@@ -845,3 +845,23 @@ def test_patch_unfold_matches_permute(cuda_device, dtype, B, C, H, W, p):
     x = torch.randn(B, C, H, W, device=cuda_device).to(dtype)
     ref = x.view(B, C, H // p, p, W // p, p).permute(0, 2, 4, 1, 3, 5).reshape(B * (H // p) * (W // p), C * p * p)
     assert torch.equal(kernels().patch_unfold(x, p), ref)
+
+
+@pytest.mark.parametrize("C", [128, 256])
+def test_layer_norm_silu_matches_fp32(cuda_device, C):
+    """SiLU(LayerNorm(x)) in one kernel each way vs fp32 autograd."""
+    g = torch.Generator().manual_seed(C)
+    x = torch.randn(10368, C, generator=g)
+    w, b = torch.rand(C, generator=g) + 0.5, torch.randn(C, generator=g)
+    gy = torch.randn(10368, C, generator=g)
+    xr, wr, br = (t.clone().requires_grad_() for t in (x, w, b))
+    ref = torch.nn.functional.silu(torch.nn.functional.layer_norm(xr, (C,), wr, br, 1e-6))
+    ref.backward(gy)
+    xd = x.to(cuda_device, torch.bfloat16).requires_grad_()
+    wd, bd = (t.to(cuda_device).requires_grad_() for t in (w, b))
+    y = ops.layer_norm(xd, wd, bd, 1e-6, act="silu")
+    y.backward(gy.to(cuda_device, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert _rel(y.float().cpu(), ref) < 2e-2
+    for a, r in ((xd, xr), (wd, wr), (bd, br)):
+        assert _rel(a.grad.float().cpu(), r.grad) < 3e-2
