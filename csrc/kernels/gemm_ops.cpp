@@ -46,8 +46,9 @@ std::vector<torch::Tensor> gemm_tc(torch::Tensor a, torch::Tensor b, c10::option
     TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0 && aligned16(a) && aligned16(b),
                 "gemm_tc: rows must be 16-byte aligned");
     TORCH_CHECK(N % 16 == 0, "gemm_tc: N must be a multiple of 16");
-    TORCH_CHECK(!a_mn || M % 128 == 0, "gemm_tc: MN-major A needs M % 128 == 0");
-    TORCH_CHECK(!b_mn || N % 128 == 0, "gemm_tc: MN-major B needs N % 128 == 0");
+    // MN-major operands are read as 64-wide boxes (a box past the extent is skipped, a partial one
+    // zero-filled), so their extents only need the 16-byte row pitch checked above
+    TORCH_CHECK(!a_mn || M % 8 == 0, "gemm_tc: MN-major A needs M % 8 == 0");
     TORCH_CHECK(M > 0 && N > 0 && K > 0, "gemm_tc: empty problem");
     at::cuda::CUDAGuard guard(a.device());
     auto C = torch::empty({M, N}, a.options());
