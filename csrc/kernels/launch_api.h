@@ -240,6 +240,9 @@ cudaError_t launch_sample_packed(const uint64_t* bits, int n, int H, int W, cons
 // ---------------------------------------------------------------- detection post-process
 // logits [B,Q,C], boxes [B,Q,4] cxcywh (normalised); sizes [B,2] (h, w) fp32 or null (fixed_h/w).
 // K <= 1024.  Outputs: scores [B,K] f32, labels [B,K] i64, boxes [B,K,4] xyxy pixels, queries [B,K] i32.
+// idx [rows, K] (int64): indices of the K largest entries of each row of x [rows, N] (fp32 or bf16),
+// value descending, lowest index first on ties; K <= 1024.
+cudaError_t launch_row_topk(DType t, const void* x, int64_t rows, int64_t N, int K, int64_t* idx, cudaStream_t st);
 cudaError_t launch_topk_postprocess(DType lt, DType bt, const void* logits, const void* boxes, const float* sizes,
                                     int B, int Q, int C, int K, float fixed_h, float fixed_w, float* scores,
                                     int64_t* labels, float* out_boxes, int32_t* queries, cudaStream_t st);

@@ -82,6 +82,23 @@ torch::Tensor patch_unfold(torch::Tensor img, int64_t p) {
     return out;
 }
 
+// indices of the k largest entries of every row of x [..., N] (sorted, value descending)
+torch::Tensor row_topk(torch::Tensor x, int64_t k) {
+    TORCH_CHECK(x.is_cuda() && x.dim() >= 1 && x.is_contiguous() &&
+                    (x.scalar_type() == torch::kFloat32 || x.scalar_type() == torch::kBFloat16),
+                "row_topk: contiguous fp32 / bf16 CUDA tensor expected");
+    const int64_t N = x.size(-1);
+    TORCH_CHECK(k >= 1 && k <= N && k <= 1024, "row_topk: 1 <= k <= min(N, 1024)");
+    at::cuda::CUDAGuard guard(x.device());
+    auto sizes = x.sizes().vec();
+    sizes.back() = k;
+    auto idx = torch::empty(sizes, x.options().dtype(torch::kInt64));
+    check_cuda(launch_row_topk(dtype_of(x), x.data_ptr(), x.numel() / N, N, static_cast<int>(k), idx.data_ptr<int64_t>(),
+                               cur_stream()),
+               "row_topk");
+    return idx;
+}
+
 // x [G, M, N] -> [G, N] column sums per group (fp32 accumulation), one launch
 torch::Tensor colsum_grouped(torch::Tensor x, c10::optional<at::ScalarType> out_dtype) {
     TORCH_CHECK(x.is_cuda() && x.dim() == 3 && x.is_contiguous(), "colsum_grouped: contiguous CUDA [G, M, N] expected");
@@ -244,6 +261,7 @@ void register_more_ops(pybind11::module& m) {
     m.def("index_add_rows", &index_add_rows, py::arg("src"), py::arg("rows"), py::arg("R"));
     m.def("colsum_grouped", &colsum_grouped, py::arg("x"), py::arg("out_dtype") = py::none());
     m.def("patch_unfold", &patch_unfold, py::arg("img"), py::arg("p"));
+    m.def("row_topk", &row_topk, py::arg("x"), py::arg("k"));
     m.def("scale_bwd", &scale_bwd, py::arg("gy"), py::arg("pre"), py::arg("gamma"),
           py::arg("gamma_grad") = py::none());
     m.def("scale_bias_bwd", &scale_bias_bwd, py::arg("gy"), py::arg("pre"), py::arg("gamma"),

@@ -30,19 +30,14 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 template <typename T>
 __device__ __forceinline__ float ld(const T* p, int64_t i) { return to_f(p[i]); }
 
-template <typename LT, typename BT>
-__global__ void __launch_bounds__(kThreads) topk_post_kernel(const LT* __restrict__ logits, const BT* __restrict__ boxes,
-                                                             const float* __restrict__ sizes, int Q, int C, int K,
-                                                             float fixed_h, float fixed_w, float* __restrict__ scores,
-                                                             int64_t* __restrict__ labels, float* __restrict__ out_boxes,
-                                                             int32_t* __restrict__ queries) {
+// The K largest of x[0, N) into cand[0, K), sorted (value descending, index ascending), each entry the
+// order-preserving key in the high word and ~index in the low word; one CTA of kThreads threads.
+template <typename LT>
+__device__ void block_topk(const LT* __restrict__ x, int64_t N, int K, unsigned long long* cand) {
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_prefix, s_mask, s_need, s_count;
-    __shared__ unsigned long long cand[kMaxK];
     __shared__ uint32_t scan[kThreads];
-    const int b = blockIdx.x, tid = threadIdx.x;
-    const int64_t N = int64_t(Q) * C;
-    const LT* x = logits + int64_t(b) * N;
+    const int tid = threadIdx.x;
     if (tid == 0) {
         s_prefix = 0;
         s_mask = 0;
@@ -132,10 +127,27 @@ __global__ void __launch_bounds__(kThreads) topk_post_kernel(const LT* __restric
             __syncthreads();
         }
     }
+}
+
+__device__ __forceinline__ uint32_t cand_index(unsigned long long c) {
+    return 0xffffffffu - uint32_t(c & 0xffffffffull);
+}
+
+template <typename LT, typename BT>
+__global__ void __launch_bounds__(kThreads) topk_post_kernel(const LT* __restrict__ logits, const BT* __restrict__ boxes,
+                                                             const float* __restrict__ sizes, int Q, int C, int K,
+                                                             float fixed_h, float fixed_w, float* __restrict__ scores,
+                                                             int64_t* __restrict__ labels, float* __restrict__ out_boxes,
+                                                             int32_t* __restrict__ queries) {
+    __shared__ unsigned long long cand[kMaxK];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const int64_t N = int64_t(Q) * C;
+    const LT* x = logits + int64_t(b) * N;
+    block_topk(x, N, K, cand);
     // 4. epilogue
     const float H = sizes ? sizes[2 * b] : fixed_h, W = sizes ? sizes[2 * b + 1] : fixed_w;
     for (int r = tid; r < K; r += kThreads) {
-        const uint32_t idx = 0xffffffffu - uint32_t(cand[r] & 0xffffffffull);
+        const uint32_t idx = cand_index(cand[r]);
         const int q = int(idx / uint32_t(C)), c = int(idx % uint32_t(C));
         const float v = ld(x, idx);
         const int64_t o = int64_t(b) * K + r;
@@ -151,7 +163,30 @@ __global__ void __launch_bounds__(kThreads) topk_post_kernel(const LT* __restric
     }
 }
 
+// Indices of the K largest entries of every row of x [rows, N], sorted (value descending, index
+// ascending on ties): one CTA per row -- the two-stage head's per-group proposal selection.
+template <typename LT>
+__global__ void __launch_bounds__(kThreads) row_topk_kernel(const LT* __restrict__ x, int64_t N, int K,
+                                                            int64_t* __restrict__ idx) {
+    __shared__ unsigned long long cand[kMaxK];
+    block_topk(x + int64_t(blockIdx.x) * N, N, K, cand);
+    for (int r = threadIdx.x; r < K; r += kThreads) idx[int64_t(blockIdx.x) * K + r] = cand_index(cand[r]);
+}
+
 }  // namespace
+
+cudaError_t launch_row_topk(DType t, const void* x, int64_t rows, int64_t N, int K, int64_t* idx, cudaStream_t st) {
+    if (rows == 0 || K == 0) return cudaSuccess;
+    if (K > kMaxK || K > N || N >= (int64_t(1) << 31) || rows > 0x7fffffff) return cudaErrorInvalidValue;
+    if (t == DType::kBF16)
+        row_topk_kernel<__nv_bfloat16><<<static_cast<unsigned>(rows), kThreads, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(x), N, K, idx);
+    else if (t == DType::kF32)
+        row_topk_kernel<float><<<static_cast<unsigned>(rows), kThreads, 0, st>>>(static_cast<const float*>(x), N, K, idx);
+    else
+        return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
 
 cudaError_t launch_topk_postprocess(DType lt, DType bt, const void* logits, const void* boxes, const float* sizes,
                                     int B, int Q, int C, int K, float fixed_h, float fixed_w, float* scores,

@@ -512,6 +512,9 @@ class Transformer(nn.Module):
             cls = torch.baddbmm(b_f.to(dt)[:, None, :], x, w_f.to(dt).transpose(1, 2))   # [G, B*S, K+pad]
             best = cls.amax(-1).view(G, B, S)
         k = min(self.cfg.num_queries, S)
+        kern = kernels()
+        if best.is_cuda and k <= 1024 and hasattr(kern, "row_topk"):
+            return kern.row_topk(best.contiguous(), k)     # one CTA per (group, image) row, sorted like topk
         return best.topk(k, dim=2)[1]
 
     def encoder_class_logits(self, enc_memory: torch.Tensor, groups: int) -> torch.Tensor:

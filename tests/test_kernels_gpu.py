@@ -233,11 +233,13 @@ def test_colsum(cuda_device):
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
-@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 384), (10400 // 8, 256, 96), (384, 1152, 1536)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 384), (10400 // 8, 256, 96), (384, 1152, 1536),
+                                   (1304, 208, 200), (200, 1040, 328), (72, 48, 4200)])
 def test_gemm_tc_all_operand_majors(cuda_device, a_mn, b_mn, M, N, K):
-    """tcgen05 GEMM vs fp32 matmul for K-major / MN-major operands, with M and K tails."""
-    if (a_mn and M % 128) or (b_mn and N % 128):
-        pytest.skip("MN-major extents must be multiples of 128")
+    """tcgen05 GEMM vs fp32 matmul for K-major / MN-major operands, with M / N / K tails (MN-major
+    extents that are not multiples of the 64-wide boxes included; a split-K shape)."""
+    if a_mn and M % 8:
+        pytest.skip("an MN-major A needs 16-byte rows (M % 8 == 0)")
     k = kernels()
     g = torch.Generator().manual_seed(M + N + K)
     A = torch.randn(M, K, generator=g).to(torch.bfloat16)
@@ -865,3 +867,23 @@ def test_layer_norm_silu_matches_fp32(cuda_device, C):
     assert _rel(y.float().cpu(), ref) < 2e-2
     for a, r in ((xd, xr), (wd, wr), (bd, br)):
         assert _rel(a.grad.float().cpu(), r.grad) < 3e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape,k", [((13, 8, 1296), 300), ((3, 5000), 1024), ((2, 7), 7), ((4, 100), 1)])
+def test_row_topk_matches_torch(cuda_device, dtype, shape, k):
+    """Per-row top-k indices (radix select + sort in one CTA per row) against torch.topk; ties broken
+    by the lower index (checked on a row with repeated values)."""
+    g = torch.Generator().manual_seed(k)
+    x = torch.randn(*shape, generator=g).to(dtype)
+    x.view(-1, shape[-1])[0, : shape[-1] // 2] = 0.5                    # a block of equal values
+    xd = x.to(cuda_device)
+    got = kernels().row_topk(xd, k).cpu()
+    vals = x.float().gather(-1, got)
+    ref_vals = x.float().topk(k, dim=-1)[0]
+    assert torch.equal(vals, ref_vals)                                     # the same values, sorted
+    flat_x, flat_i = x.float().reshape(-1, shape[-1]), got.reshape(-1, k)
+    for r in range(flat_x.shape[0]):                                       # ties: ascending indices
+        v, i = flat_x[r][flat_i[r]], flat_i[r]
+        same = v[1:] == v[:-1]
+        assert bool((i[1:][same] > i[:-1][same]).all())
