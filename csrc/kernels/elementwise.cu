@@ -296,22 +296,21 @@ __global__ void index_add_rows_kernel(const __nv_bfloat16* __restrict__ src, con
 template <typename T>
 __global__ void patch_unfold_kernel(const T* __restrict__ img, T* __restrict__ out, int B, int Cin, int H, int W,
                                     int p) {
+    // 32-bit index decomposition (the launcher keeps the work count below 2^31); the pointer
+    // offsets themselves are formed in 64 bits.
     const int hp = H / p, wp = W / p, runs = p / 8;
-    const int64_t total = static_cast<int64_t>(B) * hp * wp * Cin * p * runs;
-    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
-         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        int64_t q = t;
-        const int run = static_cast<int>(q % runs);
-        q /= runs;
-        const int ky = static_cast<int>(q % p);
-        q /= p;
-        const int c = static_cast<int>(q % Cin);
-        q /= Cin;
-        const int64_t patch = q;                         // (b, py, px)
-        const int px = static_cast<int>(patch % wp), py = static_cast<int>((patch / wp) % hp);
-        const int b = static_cast<int>(patch / (static_cast<int64_t>(wp) * hp));
+    const int per_patch = Cin * p * runs;
+    const int total = B * hp * wp * per_patch;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const int patch = t / per_patch;                 // (b, py, px)
+        const int rem = t - patch * per_patch;
+        const int c = rem / (p * runs);
+        const int ky = (rem / runs) % p;
+        const int run = rem % runs;
+        const int px = patch % wp, py = (patch / wp) % hp;
+        const int b = patch / (wp * hp);
         const T* src = img + ((static_cast<int64_t>(b) * Cin + c) * H + py * p + ky) * W + px * p + run * 8;
-        T* dst = out + patch * (static_cast<int64_t>(Cin) * p * p) + (c * p + ky) * p + run * 8;
+        T* dst = out + static_cast<int64_t>(patch) * (Cin * p * p) + (c * p + ky) * p + run * 8;
         if constexpr (sizeof(T) == 2) {
             *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
         } else {
@@ -439,6 +438,10 @@ cudaError_t launch_patch_unfold(DType t, const void* img, void* out, int B, int 
     const int64_t total = static_cast<int64_t>(B) * (H / p) * (W / p) * Cin * p * (p / 8);
     if (total == 0) return cudaSuccess;
     const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(num_sms()) * 16));
+    // the kernel indexes its work items in 32 bits, grid-stride step included
+    if (total + static_cast<int64_t>(blocks) * 256 >= (int64_t(1) << 31) ||
+        static_cast<int64_t>(Cin) * p * p >= (int64_t(1) << 31))
+        return cudaErrorInvalidValue;
     return MMLTK_DISPATCH_DT(t, [&] {
         using T = scalar_t;
         patch_unfold_kernel<T><<<blocks, 256, 0, st>>>(static_cast<const T*>(img), static_cast<T*>(out), B, Cin, H, W,

@@ -512,9 +512,9 @@ class Transformer(nn.Module):
             cls = torch.baddbmm(b_f.to(dt)[:, None, :], x, w_f.to(dt).transpose(1, 2))   # [G, B*S, K+pad]
             best = cls.amax(-1).view(G, B, S)
         k = min(self.cfg.num_queries, S)
-        kern = kernels()
-        if best.is_cuda and k <= 1024 and hasattr(kern, "row_topk"):
-            return kern.row_topk(best.contiguous(), k)     # one CTA per (group, image) row, sorted like topk
+        # (the framework's row_topk kernel gives the same indices but measured 35 us against the
+        # library's 2 x 13.5 us for 104 rows of 1296: its per-row sort is barrier-bound at one CTA
+        # per row)
         return best.topk(k, dim=2)[1]
 
     def encoder_class_logits(self, enc_memory: torch.Tensor, groups: int) -> torch.Tensor:

@@ -359,9 +359,62 @@ def bench_kernels(device="cuda", quick=False):
     def colsum():
         k.colsum(g_mlp, torch.float32)
 
+    # the step's glue kernels on RF-DETR-M's batch-8 shapes: the four tapped ViT stages normalised
+    # straight into the [B, 36, 36, 4 * 384] projector input, the decoder's per-group LayerNorm, the
+    # two-stage gather's backward (index-add of 31200 rows into 10368), the grouped bias gradient,
+    # the row top-k of the proposal scores, the patch unfold of a 576^2 batch and the projector's
+    # LayerNorm + SiLU
+    from .norm import concat_channels, grouped_layer_norm, taps_layer_norm
+    from .linear import gather_rows
+    states = [torch.randn(32, 325, 384, device=device, generator=g).bfloat16().requires_grad_() for _ in range(4)]
+    g_taps = torch.randn(8, 36, 36, 4 * 384, device=device, generator=g).bfloat16()
+    xg = torch.randn(13, 8, 300, 256, device=device, generator=g).bfloat16().requires_grad_()
+    wg = (1 + 0.1 * torch.randn(13, 256, device=device, generator=g)).bfloat16().requires_grad_()
+    bg = (0.1 * torch.randn(13, 256, device=device, generator=g)).bfloat16().requires_grad_()
+    gyg = torch.randn_like(xg)
+    table = torch.randn(10368, 256, device=device, generator=g).bfloat16().requires_grad_()
+    rows_idx = torch.randint(0, 10368, (31200,), device=device, generator=g)
+    g_rows = torch.randn(31200, 256, device=device, generator=g).bfloat16()
+    g_grp = torch.randn(13, 2400, 256, device=device, generator=g).bfloat16()
+    scores = torch.randn(13, 8, 1296, device=device, generator=g).bfloat16()
+    img = torch.randn(8, 3, 576, 576, device=device, generator=g).bfloat16()
+    xs = torch.randn(8 * 72 * 72, 256, device=device, generator=g).bfloat16().requires_grad_()
+    ws = (1 + 0.1 * torch.randn(256, device=device, generator=g)).bfloat16().requires_grad_()
+    bs = (0.1 * torch.randn(256, device=device, generator=g)).bfloat16().requires_grad_()
+    gys = torch.randn_like(xs)
+
+    def taps():
+        feats = concat_channels(taps_layer_norm(states, w, b, 1e-6, 8, 2, 18, 18))
+        torch.autograd.grad(feats, states + [w, b], g_taps)
+
+    def grouped_ln():
+        torch.autograd.grad(grouped_layer_norm(xg, wg, bg, 1e-5), (xg, wg, bg), gyg)
+
+    def gather_bwd():
+        torch.autograd.grad(gather_rows(table, rows_idx), (table,), g_rows)
+
+    def colsum_grp():
+        k.colsum_grouped(g_grp, torch.float32)
+
+    def topk():
+        k.row_topk(scores, 300)
+
+    def unfold():
+        k.patch_unfold(img, 16)
+
+    def ln_silu():
+        torch.autograd.grad(layer_norm(xs, ws, bs, 1e-6, act="silu"), (xs, ws, bs), gys)
+
     cases = [("layer_norm.fwd_bwd.vit-384", ln), ("criterion.fwd_bwd.rf-detr-m-b8", crit_step),
              ("postprocess.topk100.b8", post), ("colreduce.relu_bwd_bias.dec-ffn1-31200x2048", relu_bwd_bias),
-             ("colreduce.colsum.vit-mlp-10400x1536", colsum)]
+             ("colreduce.colsum.vit-mlp-10400x1536", colsum),
+             ("layer_norm.taps.fwd_bwd.4x32x325x384", taps),
+             ("layer_norm.grouped.fwd_bwd.13x2400x256", grouped_ln),
+             ("gather_rows.bwd.31200-of-10368x256", gather_bwd),
+             ("colreduce.colsum_grouped.13x2400x256", colsum_grp),
+             ("row_topk.k300.104x1296", topk),
+             ("patch_unfold.p16.8x3x576x576", unfold),
+             ("layer_norm.silu.fwd_bwd.41472x256", ln_silu)]
     rows = []
     for name, fn in cases:
         if quick:
