@@ -6,6 +6,7 @@
   (``-gencode arch=compute_100a,code=sm_100a``; torch's own arch list is
   bypassed because the flag is given explicitly), and
 * ``mmltk_b200/_native*.so`` from ``csrc/host`` (plain C++17, no CUDA);
+* ``mmltk_b200/_sdpa_packed*.so`` from ``csrc/cudnn`` (host C++ on the cuDNN graph API);
 * with ``--debug-bounds``, also ``mmltk_b200/_kernels_dbg*.so``: the same kernels compiled with
   ``-DMMLTK_DEBUG_BOUNDS=1``, whose index checks record an error code in a device status word
   (``kernels().debug_status()``) instead of trapping; ``MMLTK_DEBUG_BOUNDS=1`` at run time loads
@@ -51,11 +52,50 @@ def extensions(debug_bounds: bool = False):
         CUDAExtension("mmltk_b200._kernels", kern_src, include_dirs=inc,
                       extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS}),
     ]
+    exts.append(_cudnn_extension(inc))
     if debug_bounds:
         exts.append(CUDAExtension("mmltk_b200._kernels_dbg", kern_src, include_dirs=inc,
                                   extra_compile_args={"cxx": CXX_FLAGS + DEBUG_FLAGS,
                                                       "nvcc": NVCC_FLAGS + DEBUG_FLAGS}))
     return exts
+
+
+def _cudnn_paths():
+    """(frontend include dir, cuDNN include dir, cuDNN library dir) of the cuDNN that torch loads."""
+    import site
+    for sp in site.getsitepackages():
+        fe = os.path.join(sp, "include")
+        cd = os.path.join(sp, "nvidia", "cudnn")
+        if os.path.exists(os.path.join(fe, "cudnn_frontend.h")) and os.path.isdir(cd):
+            return fe, os.path.join(cd, "include"), os.path.join(cd, "lib")
+    raise RuntimeError("cudnn_frontend.h / the nvidia-cudnn package not found in site-packages")
+
+
+def _cudnn_extension(inc):
+    """``mmltk_b200._sdpa_packed``: cuDNN SDPA backward into strided (packed) gradient views
+    (``csrc/cudnn/sdpa_packed.cpp``), linked against the libcudnn.so.9 that torch loads."""
+    from torch.utils.cpp_extension import CUDAExtension
+    fe_inc, cudnn_inc, cudnn_lib = _cudnn_paths()
+    # The image's g++ resolves -lstdc++ to the static archive (its shared-library link is dangling)
+    # and links shared objects with -Bsymbolic, so a library would run its stream / locale code on a
+    # private, never-initialised copy of libstdc++ (the cuDNN frontend formats numbers through
+    # std::ostream, and that crashed).  The process's shared libstdc++ is named explicitly; hidden
+    # visibility keeps the header-only frontend's symbols (libtorch carries its own copy) private.
+    return CUDAExtension("mmltk_b200._sdpa_packed", [os.path.join("csrc", "cudnn", "sdpa_packed.cpp")],
+                         include_dirs=inc + [fe_inc, cudnn_inc],
+                         extra_compile_args={"cxx": CXX_FLAGS + ["-fvisibility=hidden", "-fvisibility-inlines-hidden"],
+                                             "nvcc": NVCC_FLAGS},
+                         extra_link_args=[f"-L{cudnn_lib}", "-l:libcudnn.so.9", f"-Wl,-rpath,{cudnn_lib}",
+                                          "-Wl,--no-as-needed", _shared_libstdcxx(), "-Wl,--as-needed"])
+
+
+def _shared_libstdcxx() -> str:
+    """Path of the shared libstdc++ the Python process itself uses."""
+    for d in ("/usr/lib/x86_64-linux-gnu", "/usr/lib64", "/lib/x86_64-linux-gnu"):
+        p = os.path.join(d, "libstdc++.so.6")
+        if os.path.exists(p):
+            return p
+    raise RuntimeError("shared libstdc++.so.6 not found")
 
 
 NOALLOC_LIB = os.path.join(ROOT, "mmltk_b200", "libmmltk_noalloc.so")

@@ -122,24 +122,77 @@ def _split(qkv: torch.Tensor, heads: int):
     return [v5[:, :, i].transpose(1, 2) for i in range(3)]   # [N, H, L, D] strided views
 
 
+# cuDNN's SDPA backward through the framework's cuDNN-graph binding, writing dQ / dK / dV straight
+# into the packed [N, L, 3 * C] gradient (``MMLTK_SDPA_PACKED=0``: PyTorch's backward + a stack copy)
+_SDPA_PACKED = os.environ.get("MMLTK_SDPA_PACKED", "1") == "1"
+_sdpa_ext = []
+
+
+def _sdpa_packed():
+    """The ``_sdpa_packed`` extension, or None where it is switched off or not built."""
+    if not _SDPA_PACKED:
+        return None
+    if not _sdpa_ext:
+        from ._ext import _load
+        _sdpa_ext.append(_load("_sdpa_packed")[0])
+    return _sdpa_ext[0]
+
+
 class _QKVAttnFn(torch.autograd.Function):
+    """Self-attention over a packed projection qkv [N, L, 3 * C] -> [N, L, C] on cuDNN.
+
+    Forward: PyTorch's cuDNN SDPA on strided q / k / v views (its output and log-sum-exp are
+    saved).  Backward: the same cuDNN SDPA backward node, built through the cuDNN graph API with
+    the packed gradient's strides, so dQ / dK / dV land in their slices of d(qkv) with no copy
+    (PyTorch's own backward allocates three dense gradients, which then need a concatenation)."""
+
     @staticmethod
     def forward(ctx, qkv, heads):
         N, L, C3 = qkv.shape
         C = C3 // 3
+        ctx.shape = (N, L, heads, C // heads)
+        ext = _sdpa_packed()
+        if ext is not None:
+            q, k, v = _split(qkv, heads)
+            try:
+                res = torch.ops.aten._scaled_dot_product_cudnn_attention(q, k, v, None, True, 0.0, False, False)
+            except RuntimeError:
+                res = None
+            if res is not None:
+                o, lse = res[0], res[1]
+                ctx.save_for_backward(qkv, o, lse)
+                ctx.packed = True
+                return o.transpose(1, 2).reshape(N, L, C)
+        ctx.packed = False
         leaves = [t.detach().requires_grad_() for t in _split(qkv, heads)]
         with torch.enable_grad():
             o = F.scaled_dot_product_attention(*leaves)           # [N, H, L, D]
         ctx.leaves, ctx.o = leaves, o
-        ctx.shape = (N, L, heads, C // heads)
         return o.detach().transpose(1, 2).reshape(N, L, C)
 
     @staticmethod
     def backward(ctx, go):
         N, L, H, D = ctx.shape
         g = go.reshape(N, L, H, D).transpose(1, 2)
-        dq, dk, dv = torch.autograd.grad(ctx.o, ctx.leaves, g)
-        ctx.leaves = ctx.o = None
+        if ctx.packed:
+            qkv, o, lse = ctx.saved_tensors
+            ext = _sdpa_packed()
+            q, k, v = _split(qkv, H)
+            dqkv = torch.empty_like(qkv)
+            dq, dk, dv = _split(dqkv, H)
+            scale = 1.0 / math.sqrt(D)
+            if not torch.cuda.is_current_stream_capturing() or ext.has_plan(q, k, v, o, g, lse, dq, dk, dv, scale):
+                ext.sdpa_bwd(q, k, v, o, g, lse, dq, dk, dv, scale)
+                return dqkv, None
+            # first call of this shape inside a stream capture: no cuDNN plan is built while
+            # capturing; recompute the forward and take PyTorch's backward instead
+            leaves = [t.detach().requires_grad_() for t in (q, k, v)]
+            with torch.enable_grad():
+                o2 = F.scaled_dot_product_attention(*leaves)
+            dq, dk, dv = torch.autograd.grad(o2, leaves, g)
+        else:
+            dq, dk, dv = torch.autograd.grad(ctx.o, ctx.leaves, g)
+            ctx.leaves = ctx.o = None
         # [N, L, 3, H, D]: one concatenation of (usually contiguous) [N, L, H, D] gradients
         dqkv = torch.stack([dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2)], dim=2)
         return dqkv.view(N, L, 3 * H * D), None
