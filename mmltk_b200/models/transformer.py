@@ -140,7 +140,11 @@ class DecoderLayer(nn.Module):
             # read straight out of the projections and the gradients land in them
             o = ops.short_attention(qk2, v2, (0, d, 0), B * groups, Qg, H, Dh).view(B, Q, d)
             return ops.linear(o, self.self_attn.out_proj.weight, None), self.self_attn.out_proj.bias
-        # [B, G, Qg, H, Dh] -> [B*G, H, Qg, Dh]: attention never crosses a group
+        # [B, G, Qg, H, Dh] -> [B*G, H, Qg, Dh]: attention never crosses a group; on cuDNN with
+        # the backward writing straight into the two projections' gradients
+        o = ops.qk_split_attention(qk, v, B * groups, Qg, H)
+        if o is not None:
+            return ops.linear(o, self.self_attn.out_proj.weight, None), self.self_attn.out_proj.bias
         # split (not two slices): its backward is one concatenation instead of two
         # zero-filled full-width buffers, two copies and an add
         qh, kh = qk.split(d, dim=-1)

@@ -198,6 +198,65 @@ class _QKVAttnFn(torch.autograd.Function):
         return dqkv.view(N, L, 3 * H * D), None
 
 
+class _QKSplitAttnFn(torch.autograd.Function):
+    """Self-attention whose q / k come from one projection qk [..., 2 * C] (q | k) and v from
+    another [..., C]; rows are ``nseq`` sequences of ``L`` tokens.  cuDNN forward on strided views;
+    the cuDNN-graph backward writes dQ / dK into d(qk) and dV into d(v) in place (PyTorch's backward
+    would return dense dQ / dK that the split's backward then concatenates)."""
+
+    @staticmethod
+    def forward(ctx, qk, v, nseq, L, heads):
+        C = v.shape[-1]
+        D = C // heads
+        q, k, vv = _qk_views(qk, v, nseq, L, heads, D)
+        o, lse = torch.ops.aten._scaled_dot_product_cudnn_attention(q, k, vv, None, True, 0.0, False, False)[:2]
+        ctx.save_for_backward(qk, v, o, lse)
+        ctx.dims = (nseq, L, heads, D)
+        return o.transpose(1, 2).reshape(v.shape)
+
+    @staticmethod
+    def backward(ctx, go):
+        qk, v, o, lse = ctx.saved_tensors
+        nseq, L, H, D = ctx.dims
+        q, k, vv = _qk_views(qk, v, nseq, L, H, D)
+        g = go.reshape(nseq, L, H, D).transpose(1, 2)
+        dqk, dv = torch.empty_like(qk), torch.empty_like(v)
+        dq, dk, dvv = _qk_views(dqk, dv, nseq, L, H, D)
+        scale = 1.0 / math.sqrt(D)
+        ext = _sdpa_packed()
+        if not torch.cuda.is_current_stream_capturing() or ext.has_plan(q, k, vv, o, g, lse, dq, dk, dvv, scale):
+            ext.sdpa_bwd(q, k, vv, o, g, lse, dq, dk, dvv, scale)
+            return dqk, dv, None, None, None
+        # first call of this shape inside a stream capture (no cuDNN plan is built while capturing)
+        leaves = [t.detach().requires_grad_() for t in (q, k, vv)]
+        with torch.enable_grad():
+            o2 = F.scaled_dot_product_attention(*leaves)
+        gq, gk, gv = torch.autograd.grad(o2, leaves, g)
+        dq.copy_(gq)
+        dk.copy_(gk)
+        dvv.copy_(gv)
+        return dqk, dv, None, None, None
+
+
+def _qk_views(qk, v, nseq, L, H, D):
+    qk5 = qk.view(nseq, L, 2, H, D)
+    return (qk5[:, :, 0].transpose(1, 2), qk5[:, :, 1].transpose(1, 2),
+            v.view(nseq, L, H, D).transpose(1, 2))
+
+
+def qk_split_attention(qk: torch.Tensor, v: torch.Tensor, nseq: int, L: int, heads: int):
+    """Attention of ``nseq`` sequences of ``L`` rows each, q | k packed in ``qk`` [..., 2C] and v
+    [..., C] (contiguous); returns [..., C] in v's shape.  Training only: returns None without
+    autograd or where the cuDNN path does not apply (the caller keeps its own formulation)."""
+    if not (torch.is_grad_enabled() and (qk.requires_grad or v.requires_grad)):
+        return None                 # inference keeps the caller's forward-only formulation
+    if not (qk.is_cuda and qk.dtype in (torch.bfloat16, torch.float16) and v.dtype == qk.dtype
+            and qk.is_contiguous() and v.is_contiguous() and _sdpa_packed() is not None
+            and qk.shape[-1] == 2 * v.shape[-1] and v.shape[-1] % heads == 0):
+        return None
+    return _QKSplitAttnFn.apply(qk, v, nseq, L, heads)
+
+
 def qkv_attention_reference(qkv: torch.Tensor, heads: int) -> torch.Tensor:
     N, L, C3 = qkv.shape
     q, k, v = _split(qkv, heads)

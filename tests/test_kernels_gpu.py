@@ -916,3 +916,31 @@ def test_qkv_attention_packed_cudnn_backward(N, L, H):
     res = torch.ops.aten._scaled_dot_product_cudnn_attention(q, k, v, None, True, 0.0, False, False)
     g = go.reshape(N, L, H, D).transpose(1, 2)
     assert ext.has_plan(q, k, v, res[0], g, res[1], dq, dk, dv, 1.0 / D ** 0.5)
+
+
+@pytest.mark.gpu
+def test_qk_split_attention_packed_cudnn_backward():
+    """Decoder self-attention layout: q | k from one projection, v from another, 3 groups of 300
+    queries per image.  Output and both projections' gradients match the fp32 reference."""
+    import importlib
+    A = importlib.import_module("mmltk_b200.ops.attention")
+    assert A._sdpa_packed() is not None, "the _sdpa_packed extension is not built"
+    torch.manual_seed(0)
+    B, G, Qg, H, D = 2, 3, 300, 8, 32
+    d = H * D
+    for rep in range(2):
+        qk = (torch.randn(B, G * Qg, 2 * d, device="cuda") * 0.5).bfloat16().requires_grad_()
+        v = (torch.randn(B, G * Qg, d, device="cuda") * 0.5).bfloat16().requires_grad_()
+        o = A.qk_split_attention(qk, v, B * G, Qg, H)
+        assert o is not None and o.shape == v.shape
+        go = torch.randn_like(o)
+        o.backward(go)
+        qf, vf = qk.detach().float().requires_grad_(), v.detach().float().requires_grad_()
+        q = qf[..., :d].reshape(B * G, Qg, H, D).transpose(1, 2)
+        k = qf[..., d:].reshape(B * G, Qg, H, D).transpose(1, 2)
+        vv = vf.reshape(B * G, Qg, H, D).transpose(1, 2)
+        ref = A.attention_reference(q, k, vv).transpose(1, 2).reshape(B, G * Qg, d)
+        ref.backward(go.float())
+        assert torch.allclose(o.float(), ref, atol=2e-2, rtol=2e-2)
+        assert torch.allclose(qk.grad.float(), qf.grad, atol=3e-2, rtol=3e-2)
+        assert torch.allclose(v.grad.float(), vf.grad, atol=3e-2, rtol=3e-2)
