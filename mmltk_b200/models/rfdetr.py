@@ -117,8 +117,10 @@ class RFDETR(nn.Module):
         B, _, H, W = pixels.shape
         feats = self.backbone[0](pixels)  # channels-last per level
         nq = cfg.num_queries * max(1, cfg.group_detr) if training else cfg.num_queries
-        ref_w = self.refpoint_embed.weight[:nq]
-        qf_w = self.query_feat.weight[:nq]
+        # the full tables when every query is used (a full-range slice's backward zero-fills + copies)
+        ref_w, qf_w = self.refpoint_embed.weight, self.query_feat.weight
+        if nq != ref_w.shape[0]:
+            ref_w, qf_w = ref_w[:nq], qf_w[:nq]
         t = self.transformer(feats, ref_w, qf_w, training,
                              bbox_embed=None if cfg.lite_refpoint_refine else self.bbox_embed)
         hs = t["hs"]                      # [Ldec, B, Q, C]

@@ -131,8 +131,12 @@ class DecoderLayer(nn.Module):
         H = self.self_attn.num_heads
         Dh = d // H
         w, b = self.self_attn.in_proj_weight, self.self_attn.in_proj_bias
-        qk = ops.linear(tgt_pos if tgt_pos is not None else tgt + query_pos, w[:2 * d], b[:2 * d])  # [B, Q, 2d]
-        v = ops.linear(tgt, w[2 * d:], b[2 * d:])              # [B, Q, d]
+        # split (not slices): the weight / bias gradients are one concatenation each instead of
+        # zero-filled full-size buffers per slice, copies and an accumulation
+        w_qk, w_v = w.split([2 * d, d])
+        b_qk, b_v = b.split([2 * d, d])
+        qk = ops.linear(tgt_pos if tgt_pos is not None else tgt + query_pos, w_qk, b_qk)  # [B, Q, 2d]
+        v = ops.linear(tgt, w_v, b_v)                           # [B, Q, d]
         Qg = Q // groups
         qk2, v2 = qk.view(B * Q, 2 * d), v.view(B * Q, d)
         if ops.short_attention_ok(Qg, Dh, qk2, v2):
@@ -247,6 +251,8 @@ class GroupedLinear(nn.Module):
 
     def forward(self, x: torch.Tensor, groups: int, act=None) -> torch.Tensor:
         """x: [G', B, N, din] (one slice per group) or [B, N, din] (shared) -> [groups, B, N, dout]."""
+        if groups == self.weight.shape[0]:   # no slice: a full-range slice's backward still zero-fills + copies
+            return grouped_linear(x, self.weight, self.bias, act)
         return grouped_linear(x, self.weight[:groups], self.bias[:groups], act)
 
 
