@@ -59,8 +59,32 @@ def gen_sineembed_for_position(pos: torch.Tensor, dim: int = 128) -> torch.Tenso
     return ops.sine_embed(pos, dim)
 
 
+class _ReparamBoxesFn(torch.autograd.Function):
+    """reparam_boxes with its backward written out: two concatenated gradients instead of autograd's
+    zero-filled full-size buffer per slice of ``delta`` / ``base`` and the sums of their pieces."""
+
+    @staticmethod
+    def forward(ctx, delta, base):
+        dxy, dwh = delta[..., :2], delta[..., 2:]
+        bxy, bwh = base[..., :2], base[..., 2:]
+        e = dwh.exp()
+        ctx.save_for_backward(dxy, bwh, e)
+        return torch.cat([dxy * bwh + bxy, e * bwh], -1)
+
+    @staticmethod
+    def backward(ctx, g):
+        dxy, bwh, e = ctx.saved_tensors
+        gxy, gwh = g[..., :2], g[..., 2:]
+        gwh_e = gwh * e
+        gd = torch.cat([gxy * bwh, gwh_e * bwh], -1) if ctx.needs_input_grad[0] else None
+        gb = torch.cat([gxy, gxy * dxy + gwh_e], -1) if ctx.needs_input_grad[1] else None
+        return gd, gb
+
+
 def reparam_boxes(delta: torch.Tensor, base: torch.Tensor) -> torch.Tensor:
     """bbox reparameterisation: cxcy = d_xy * base_wh + base_xy, wh = exp(d_wh) * base_wh."""
+    if torch.is_grad_enabled() and (delta.requires_grad or base.requires_grad):
+        return _ReparamBoxesFn.apply(delta, base)
     cxcy = delta[..., :2] * base[..., 2:] + base[..., :2]
     wh = delta[..., 2:].exp() * base[..., 2:]
     return torch.cat([cxcy, wh], -1)

@@ -216,3 +216,24 @@ def test_scaled_residual_layer_norm_reference():
     out, s = scaled_residual_layer_norm(y, res, g, w, b, 1e-6)
     assert torch.allclose(s, res + g * y)
     assert torch.allclose(out, torch.nn.functional.layer_norm(res + g * y, (16,), w, b, 1e-6), atol=1e-6)
+
+
+def test_reparam_boxes_backward_matches_autograd():
+    """The written-out backward of the box reparameterisation equals autograd's (float64 gradcheck
+    plus a direct comparison against the slice-and-cat statement)."""
+    from mmltk_b200.models.transformer import _ReparamBoxesFn, reparam_boxes
+    torch.manual_seed(0)
+    d = (0.3 * torch.randn(2, 5, 4, dtype=torch.float64)).requires_grad_()
+    b = (0.2 + torch.rand(2, 5, 4, dtype=torch.float64)).requires_grad_()
+    assert torch.autograd.gradcheck(_ReparamBoxesFn.apply, (d, b))
+    g = torch.randn(2, 5, 4, dtype=torch.float64)
+    out = reparam_boxes(d, b)
+    gd, gb = torch.autograd.grad(out, (d, b), g)
+    ref = torch.cat([d[..., :2] * b[..., 2:] + b[..., :2], d[..., 2:].exp() * b[..., 2:]], -1)
+    rd, rb = torch.autograd.grad(ref, (d, b), g)
+    assert torch.allclose(out, ref) and torch.allclose(gd, rd) and torch.allclose(gb, rb)
+    bd = b.detach().requires_grad_()
+    gb_only = torch.autograd.grad(reparam_boxes(d.detach(), bd), bd, g)[0]
+    assert torch.allclose(gb_only, torch.autograd.grad(
+        torch.cat([d.detach()[..., :2] * bd[..., 2:] + bd[..., :2], d.detach()[..., 2:].exp() * bd[..., 2:]], -1),
+        bd, g)[0])
